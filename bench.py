@@ -1,0 +1,349 @@
+#!/usr/bin/env python
+"""MoE FFN tokens/s on B200 -- one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config mixtral] [--tokens 4096]
+
+A step is one forward of one MoE FFN layer (router -> top-k -> permute ->
+gate/up/SwiGLU -> down -> weighted combine) over `--tokens` tokens per GPU,
+through the library's C ABI (uaii_moe_ffn_forward).  Weights are the seeded
+synthetic GGUF layer of the chosen configuration (random-init, quantized by the
+library); activations are seeded N(0,1).  Under torchrun every rank runs its
+own replica of the layer on its own tokens (weak scaling, no data-path
+collective); the step time is the max over ranks.
+
+`value`: tokens/s with inputs resident in HBM.  `e2e`: the same metric through
+the same call with pinned HOST buffers, so every step includes the host->device
+copy of x and the device->host copy of y.  `--impl reference` times the
+reference's own CPU implementation (oracle/_ref, or the oracle restatement
+where that build is absent) on a bounded token sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+sys.path.insert(0, os.path.join(REPO, "universal-ai-inference_b200"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "MoE FFN tokens/s"
+UNIT = "tokens/s"
+WORKLOAD_NOTE = {
+    "mixtral": "Mixtral-8x7B-shaped MoE FFN layer (BASELINE configs[1]): d_model 4096, 8 experts, top-2 "
+               "renormalised, d_ff 14336, gate/up Q4_K, down Q6_K",
+    "cfg1_q4_0": "config 1 layer: d_model 1024, 8 experts, top-2, d_ff 2816, Q4_0",
+    "qwen2moe": "Qwen2-MoE-A2.7B-shaped layer: d_model 2048, 60 experts top-4 (no renorm), d_ff 1408, "
+                "shared d_ff 5632 with sigmoid gate, Q8_0, Zipf(1.1) routing",
+    "qwen3": "Qwen3-30B-A3B-shaped layer: d_model 2048, 128 experts top-8, d_ff 768, Q4_0",
+    "qwen3_hot": "Qwen3-30B-A3B-shaped layer with a 4x hot expert",
+}
+# DRAM bytes per launch of the dominant kernel from an ncu capture
+# (profiles/*.md gives the command and the raw figures); None until captured.
+NCU_TRAFFIC = {}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="mixtral")
+    ap.add_argument("--tokens", type=int, default=4096)
+    ap.add_argument("--path", type=int, default=0, help="0 auto, 1 CUDA-core GEMV, 2 tensor-core GEMM")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.out = os.path.join("/tmp", f"uaii_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.out, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.out):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.out) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        os.unlink(self.out)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ reference / CPU baseline
+
+def cpu_reference_run(cfg, lw, x_sample, steps: int, warmup: int):
+    """Time the reference CPU path on `x_sample` tokens: returns (tokens/s, cores, kind)."""
+    from oracle.oracle import Oracle, Reference, reference_available
+    threads = os.cpu_count() or 1
+    T = x_sample.shape[0]
+    if reference_available():
+        R = Reference()
+        kind = "reference"
+        # load-time dequant to f32 (excluded from timing), as the reference Session does
+        def deq(fmt, packed, rows, cols):
+            flat = packed.reshape(-1, packed.shape[-1])
+            return R.dequant(fmt, flat, rows, cols, flat.shape[1])
+        E, I, D = cfg.E, cfg.I, cfg.D
+        G = deq(cfg.gate_fmt, lw.gate, E * I, D).reshape(E, I, D)
+        U = deq(cfg.gate_fmt, lw.up, E * I, D).reshape(E, I, D)
+        Dn = deq(cfg.down_fmt, lw.down, E * D, I).reshape(E, D, I)
+
+        def step():
+            probs, _ = R.router(x_sample, lw.router_w)
+            return R.experts(x_sample, G, U, Dn, probs, cfg.top_k, threads)
+    else:
+        O = Oracle()
+        kind = "port"
+        threads = 1
+
+        def step():
+            _, probs, _ = O.router(x_sample, lw.router_w)
+            return O.experts_packed(x_sample, lw.gate, cfg.gate_fmt, lw.up, cfg.gate_fmt, lw.down, cfg.down_fmt,
+                                    probs, cfg.E, cfg.I, cfg.top_k, cfg.norm_topk)
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = time.perf_counter() - t0
+    return T * steps / dt, threads, kind
+
+
+def cpu_sample_tokens(cfg, T: int) -> int:
+    threads = os.cpu_count() or 1
+    # about 10-30 s of CPU work: the expert loop costs ~2*3*D*I*k flops per token, single-threaded per call
+    per_token_s = 2 * 3 * cfg.D * cfg.I * cfg.top_k / 1.5e9
+    n = int(min(4 * threads, max(threads, 20.0 / max(per_token_s, 1e-6))))
+    return max(1, min(T, n))
+
+
+# ------------------------------------------------------------------ main
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    from uaii_moe.synthetic import CONFIGS, algorithmic_bytes, flops, make_layer_weights, make_tokens
+    cfg = CONFIGS[args.config]
+    T = args.tokens
+    workload = f"{args.config}_T{T}"
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        lw = make_layer_weights(cfg)
+        n = cpu_sample_tokens(cfg, T)
+        xs = make_tokens(cfg, n, 0)
+        tps, cores, kind = cpu_reference_run(cfg, lw, xs, args.steps, args.warmup)
+        line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF layer)",
+                "config": {"workload": workload, "note": WORKLOAD_NOTE.get(args.config, ""),
+                           "tokens_per_step": n},
+                "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": kind,
+                                 "sample": f"{n} of {T} tokens per step, all experts dequantized to f32 "
+                                           f"before timing (reference load-time dequant)"},
+                "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    import uaii_moe as um
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    lw = make_layer_weights(cfg)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda() if a is not None else None
+    arrays = {"router_w": dev(lw.router_w), "gate": dev(lw.gate), "up": dev(lw.up), "down": dev(lw.down),
+              "shared": tuple(dev(a) for a in lw.shared) if lw.shared is not None else None}
+    L = lw.layer_struct(arrays)
+    x_host = torch.from_numpy(make_tokens(cfg, T, rank)).pin_memory()
+    y_host = torch.empty((T, cfg.D), dtype=torch.float32).pin_memory()
+    x = x_host.cuda()
+    y = torch.empty((T, cfg.D), dtype=torch.float32, device="cuda")
+    probs = torch.empty((T, cfg.E), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()  # inputs were written on the default stream
+    stream = torch.cuda.Stream()
+    be = um.Backend(local, stream.cuda_stream)
+    if args.path:
+        be.set_expert_path(args.path)
+
+    # routing statistics for the roofline (outside any timed region)
+    be.ffn(L, x, T, y, probs)
+    be.synchronize()
+    ids = torch.topk(probs, cfg.top_k, dim=1).indices
+    touched = int(torch.unique(ids).numel())
+
+    for _ in range(args.warmup):
+        be.ffn(L, x, T, y)
+    be.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        be.profile_enable(True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            be.ffn(L, x, T, y)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        phases, launches = be.profile_read()
+        be.profile_enable(False)
+    ms = ev0.elapsed_time(ev1)
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms = max_over_ranks(ms)
+    value = world * T * args.steps / (ms / 1e3)
+
+    e2e = None
+    if not args.no_e2e:
+        for _ in range(2):
+            be.ffn(L, x_host, T, y_host)
+        barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            be.ffn(L, x_host, T, y_host)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(ev0.elapsed_time(ev1))
+        e2e = {"value": world * T * args.steps / (e2e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": T * cfg.D * 4, "d2h_bytes_per_step": T * cfg.D * 4,
+               "ms_per_step": e2e_ms / args.steps}
+
+    # roofline of the dominant phase
+    peaks = load_peaks()
+    dom = max(("gateup", "down"), key=lambda p: phases[p][0])
+    dom_ms, dom_calls = phases[dom]
+    avg_s = dom_ms / max(dom_calls, 1) / 1e3
+    S = T * cfg.top_k
+    from uaii_moe import packed_nbytes
+    if dom == "gateup":
+        byts = touched * 2 * cfg.I * packed_nbytes(cfg.gate_fmt, cfg.D) + S * cfg.D * 4 + S * cfg.I * 4
+        fl = 2 * S * 2 * cfg.D * cfg.I
+    else:
+        byts = touched * cfg.D * packed_nbytes(cfg.down_fmt, cfg.I) + S * cfg.I * 4 + S * cfg.D * 4
+        fl = 2 * S * cfg.D * cfg.I
+    tokens_per_expert = S / max(touched, 1)
+    if tokens_per_expert < 64:
+        roof = {"bound": "hbm", "achieved": byts / avg_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s"}
+    else:
+        roof = {"bound": "tensor", "achieved": fl / avg_s / 1e12, "peak": peaks["bf16_tflops_sustained"],
+                "unit": "TFLOP/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = NCU_TRAFFIC.get((workload, dom))
+    roof["kernel"] = f"{dom} phase ({'CUDA-core GEMV' if args.path in (0, 1) else 'tensor-core GEMM'})"
+    roof["peak_src"] = f"{peaks['src']} ({'hbm_gbs' if roof['bound'] == 'hbm' else 'bf16_tflops_sustained'})"
+    roof["algorithmic_per_launch"] = byts if roof["bound"] == "hbm" else fl
+    roof["avg_launch_ms"] = avg_s * 1e3
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        n = cpu_sample_tokens(cfg, T)
+        xs = make_tokens(cfg, n, 0)
+        tps, cores, kind = cpu_reference_run(cfg, lw, xs, 1, 0)
+        cpu = {"value": tps, "unit": UNIT, "cores": cores, "kind": kind,
+               "sample": f"{n} of the {T} tokens, one pass (router + experts), f32 weights dequantized "
+                         f"before timing"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded random-init GGUF layer, N(0,1) activations)",
+                "config": {"workload": workload, "note": WORKLOAD_NOTE.get(args.config, ""),
+                           "tokens_per_gpu": T, "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                           "l2": "inputs larger than L2 (packed expert weights re-read every step)",
+                           "experts_touched": touched},
+                "e2e": e2e, "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu,
+                "clocks": clk.summary(),
+                "phases_ms_per_step": {p: v[0] / args.steps for p, v in phases.items()}}
+        print(json.dumps(line), flush=True)
+    be.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

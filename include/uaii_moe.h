@@ -1,0 +1,248 @@
+/*
+ * uaii_moe.h -- C ABI of the B200-native GGUF mixture-of-experts FFN path.
+ *
+ * This library is a drop-in device implementation of the MoE operators of UAII
+ * (arjun988/Universal-AI-Inference).  The reference runs these operators only
+ * on the host: its CUDA backend has no MoE kernel and falls back to
+ * kernels::dispatch_cpu (libs/uaii-backends/src/cuda_runtime_api.cpp:542-579,
+ * libs/uaii-backends/src/cuda_backend.cpp:166-207).  Each entry point below
+ * names the reference interface it replaces (paths are inside the reference
+ * project).  Signatures use plain pointers and sizes only.
+ *
+ * Residency.  Every data pointer may be host memory or device memory of the
+ * backend's device; the library tells them apart with cudaPointerGetAttributes,
+ * exactly like the reference's CudaBackend (cuda_runtime_api.cpp:586-601).
+ *   - Device pointers: work is queued on the backend's stream and the call
+ *     returns without waiting.
+ *   - Host pointers: inputs are copied in, outputs are copied back, and the
+ *     call returns after the copy back has completed (the reference's
+ *     host-staging behaviour, host_executable.cpp:169-233).
+ *   - Host-resident packed expert weights are uploaded once and cached on the
+ *     device, keyed by (host pointer, byte size); call
+ *     uaii_moe_release_weights() before reusing or freeing such a buffer.
+ *
+ * Errors.  Every int-returning function returns a uaii_moe_status; the message
+ * of the last failure on the calling thread is uaii_moe_last_error().
+ */
+#ifndef UAII_MOE_H_
+#define UAII_MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UAII_MOE_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define UAII_MOE_API __attribute__((visibility("default")))
+#else
+#define UAII_MOE_API
+#endif
+
+/* Status codes: the values of uaii::ErrorCode (include/uaii/core/error.hpp:12-22)
+ * and of uaii_status in the reference C ABI (include/uaii/c_api/uaii.h). */
+typedef enum uaii_moe_status {
+  UAII_MOE_OK = 0,
+  UAII_MOE_INVALID_ARGUMENT = 1,
+  UAII_MOE_NOT_FOUND = 2,
+  UAII_MOE_IO_ERROR = 3,
+  UAII_MOE_CONFIG_ERROR = 4,
+  UAII_MOE_PLUGIN_ERROR = 5,
+  UAII_MOE_ABI_MISMATCH = 6,
+  UAII_MOE_NOT_IMPLEMENTED = 7,
+  UAII_MOE_INTERNAL = 8
+} uaii_moe_status;
+
+/* Weight formats: the values of uaii::quant::QuantFormat
+ * (include/uaii/quant/formats.hpp:10-29).  GGUF blocks are byte-identical to
+ * the file format; rows are stored back to back (row pitch = packed bytes). */
+typedef enum uaii_moe_format {
+  UAII_MOE_F32 = 0,
+  UAII_MOE_F16 = 1,
+  UAII_MOE_Q4_0 = 7,
+  UAII_MOE_Q4_1 = 8,
+  UAII_MOE_Q5_0 = 9,
+  UAII_MOE_Q5_1 = 10,
+  UAII_MOE_Q8_0 = 11,
+  UAII_MOE_Q2_K = 12,
+  UAII_MOE_Q3_K = 13,
+  UAII_MOE_Q4_K = 14,
+  UAII_MOE_Q5_K = 15,
+  UAII_MOE_Q6_K = 16
+} uaii_moe_format;
+
+/* Element types: the values of uaii::DType (include/uaii/interfaces/types.hpp:14-25). */
+typedef enum uaii_moe_dtype {
+  UAII_MOE_DTYPE_UNKNOWN = 0,
+  UAII_MOE_DTYPE_F32 = 1,
+  UAII_MOE_DTYPE_F16 = 2
+} uaii_moe_dtype;
+
+/* A non-owning tensor view: the C form of kernels::TensorView
+ * (include/uaii/kernels/tensor_view.hpp:12-22).  Packed weights use
+ * dtype = UNKNOWN, quant_format = Q*, nbytes = packed bytes (session.cpp:342-357). */
+typedef struct uaii_moe_tensor {
+  int32_t dtype;
+  int32_t quant_format;
+  const int64_t* shape;
+  uint64_t rank;
+  void* data;
+  uint64_t nbytes;
+} uaii_moe_tensor;
+
+/* An operator attribute: the C form of ir::Attribute
+ * (include/uaii/ir/attribute.hpp:10-30).  type: 1 = Int (value in i),
+ * 2 = Float (value in f), 3 = Bool (value in i). */
+typedef struct uaii_moe_attr {
+  const char* key;
+  int32_t type;
+  int64_t i;
+  double f;
+} uaii_moe_attr;
+
+typedef struct uaii_moe_backend uaii_moe_backend;
+
+/* One MoE FFN layer (GGUF blk.N.ffn_* tensors, libs/uaii-loaders/src/gguf.cpp:1078-1128).
+ * gate/up experts are [n_experts, d_ff, d_model], down experts [n_experts, d_model, d_ff];
+ * the router weight ffn_gate_inp is f32 [n_experts, d_model].  The shared expert
+ * is optional (shared_d_ff = 0 for none); gate_inp_shexp is an optional f32
+ * [d_model] sigmoid gate of the shared expert (NULL = ungated, as in the reference). */
+typedef struct uaii_moe_layer {
+  int64_t d_model;
+  int64_t n_experts;
+  int64_t d_ff;
+  int32_t top_k;
+  int32_t norm_topk; /* 1 = renormalise the top-k weights (reference), 0 = raw probabilities */
+  const float* router_w;
+  const void* gate_exps;
+  int32_t gate_fmt;
+  const void* up_exps;
+  int32_t up_fmt;
+  const void* down_exps;
+  int32_t down_fmt;
+  int64_t shared_d_ff;
+  const void* gate_shexp;
+  int32_t gate_shexp_fmt;
+  const void* up_shexp;
+  int32_t up_shexp_fmt;
+  const void* down_shexp;
+  int32_t down_shexp_fmt;
+  const float* gate_inp_shexp;
+} uaii_moe_layer;
+
+/* ABI version of this library (UAII_MOE_ABI_VERSION). */
+UAII_MOE_API int uaii_moe_abi_version(void);
+
+/* Message of the last failure on this thread ("" if none).
+ * Replaces uaii_last_error (libs/uaii-capi/src/capi.cpp:17-44). */
+UAII_MOE_API const char* uaii_moe_last_error(void);
+
+/* Create a backend on CUDA device `device`; `stream` is a cudaStream_t or NULL
+ * for a backend-owned stream.  Replaces CudaBackend::initialize
+ * (libs/uaii-backends/src/cuda_backend.cpp:35-66) and native::cuda_init
+ * (libs/uaii-backends/src/cuda_runtime_api.cpp:376-428). */
+UAII_MOE_API int uaii_moe_backend_create(int device, void* stream, uaii_moe_backend** out);
+
+/* Free every device allocation of the backend (workspace, cached weights).
+ * Replaces CudaBackend::shutdown (cuda_backend.cpp:68-78). */
+UAII_MOE_API void uaii_moe_backend_destroy(uaii_moe_backend* b);
+
+/* Wait for all work queued by this backend.  Replaces IBackend::synchronize
+ * (include/uaii/interfaces/backend.hpp:74) / native::cuda_synchronize. */
+UAII_MOE_API int uaii_moe_synchronize(uaii_moe_backend* b);
+
+/* 1 if `op_name` runs natively on the device: "MoERouter", "MoEExpertsSwiGLU"
+ * and the fused "MoEFFN".  Replaces the native op table of
+ * native::cuda_dispatch (cuda_runtime_api.cpp:542-579). */
+UAII_MOE_API int uaii_moe_supports_op(const char* op_name);
+
+/* Execute one operator with TensorView-style arguments.  Replaces
+ * IBackend::dispatch (include/uaii/interfaces/backend.hpp:77-81) as implemented
+ * by CudaBackend::dispatch (cuda_backend.cpp:166-207); argument lists, arity
+ * checks and attributes follow kernels::dispatch_cpu
+ * (libs/uaii-kernels/src/dispatch.cpp:224-248):
+ *   MoERouter         inputs {x[T,D], gate[E,D]}                 outputs {probs[T,E], top_expert[T,1]}
+ *   MoEExpertsSwiGLU  inputs {x, gate_exps, up_exps, down_exps, probs}  outputs {y[T,D]}
+ *                     attrs num_experts (default 1), top_k (default 2), norm_topk (default 1)
+ *   MoEFFN            inputs {x, gate, gate_exps, up_exps, down_exps
+ *                            [, gate_shexp, up_shexp, down_shexp [, gate_inp_shexp]]}
+ *                     outputs {y[, probs]}; the two reference nodes fused.
+ * Unknown ops return UAII_MOE_NOT_IMPLEMENTED (the reference's signal to fall
+ * back to host staging). */
+UAII_MOE_API int uaii_moe_dispatch(uaii_moe_backend* b, const char* op_name, const char* op_version,
+                      const uaii_moe_tensor* inputs, size_t n_inputs, uaii_moe_tensor* outputs,
+                      size_t n_outputs, const uaii_moe_attr* attrs, size_t n_attrs);
+
+/* GGUF rows -> f32, bitwise equal to the reference for every finite value.
+ * `rows` rows of `cols` elements, stored back to back.  Replaces
+ * quant::dequant_gguf_row (include/uaii/quant/gguf_dequant.hpp:13-16) applied
+ * row by row. */
+UAII_MOE_API int uaii_moe_dequant_rows(uaii_moe_backend* b, int fmt, const void* packed, int64_t rows,
+                          int64_t cols, float* out);
+
+/* MoERouter: probs = softmax(x . gate^T), top_expert = first argmax as f32.
+ * Replaces kernels::moe_router_f32 (libs/uaii-kernels/src/transformer.cpp:446-481).
+ * `logits` may be NULL; when given it receives x . gate^T, bitwise equal to the
+ * reference GEMM (libs/uaii-kernels/src/gemm_ref.cpp:45-75). */
+UAII_MOE_API int uaii_moe_router_f32(uaii_moe_backend* b, const float* x, const float* gate_w, int64_t T,
+                        int64_t D, int64_t E, float* probs, float* top_expert, float* logits);
+
+/* MoEExpertsSwiGLU: y = sum over the top_k experts of w * down(silu(gate x) * up x).
+ * Replaces kernels::moe_experts_swiglu_f32 (transformer.cpp:522-612);
+ * norm_topk = 1 is the reference behaviour.  gate and up use the same format. */
+UAII_MOE_API int uaii_moe_experts_swiglu(uaii_moe_backend* b, const float* x, const void* gate_exps,
+                            int gate_fmt, const void* up_exps, int up_fmt,
+                            const void* down_exps, int down_fmt, const float* probs, int64_t T,
+                            int64_t D, int64_t E, int64_t I, int top_k, int norm_topk, float* y);
+
+/* The whole MoE FFN layer (router + experts [+ shared expert]) in one call:
+ * the MoERouter -> MoEExpertsSwiGLU node pair (and the shared-expert nodes) the
+ * reference GGUF loader emits per layer (libs/uaii-loaders/src/gguf.cpp:1078-1128).
+ * `probs` (T x n_experts) may be NULL. */
+UAII_MOE_API int uaii_moe_ffn_forward(uaii_moe_backend* b, const uaii_moe_layer* layer, const float* x,
+                         int64_t T, float* y, float* probs);
+
+/* Drop the cached device copy of a host weight buffer (no reference counterpart:
+ * the reference never uploads weights). */
+UAII_MOE_API int uaii_moe_release_weights(uaii_moe_backend* b, const void* host_ptr);
+
+/* Select the expert-product schedule: 0 = automatic, 1 = CUDA-core f32 GEMV,
+ * 2 = tensor-core grouped GEMM.  No reference counterpart. */
+UAII_MOE_API int uaii_moe_set_expert_path(uaii_moe_backend* b, int path);
+
+/* Device-side profile of the MoE phases, measured with CUDA events on the
+ * backend's stream.  Phases: 0 router, 1 routing (top-k, permutation, gather),
+ * 2 gate/up expert products + SwiGLU, 3 down expert products, 4 shared expert,
+ * 5 weighted combine.  Replaces the host wall-clock scopes the reference wraps
+ * around each dispatch (profiler::Profiler::Scope, libs/uaii-profiler/src/profiler.cpp:59,
+ * used at libs/uaii-runtime/src/session.cpp:1128-1130) with device time.
+ * uaii_moe_profile_enable resets the counters; uaii_moe_profile_read waits for
+ * the stream and returns the accumulated milliseconds and call counts per
+ * phase (arrays of UAII_MOE_N_PHASES) and the number of kernels this backend
+ * launched since the reset (counted whether or not timing is enabled). */
+#define UAII_MOE_N_PHASES 6
+UAII_MOE_API int uaii_moe_profile_enable(uaii_moe_backend* b, int enable);
+UAII_MOE_API int uaii_moe_profile_read(uaii_moe_backend* b, double* phase_ms, uint64_t* phase_calls,
+                                       uint64_t* kernel_launches);
+
+/* Bytes of one row of n elements in `fmt` (include/uaii/quant/formats.hpp:81-102). */
+UAII_MOE_API uint64_t uaii_moe_packed_nbytes(int fmt, int64_t n);
+
+/* Synthetic-input utilities (no reference counterpart: the reference has no
+ * GGUF block quantizer, libs/uaii-quant/src/codec.cpp:81-179).
+ * uaii_moe_quantize_rows: f32 rows -> GGUF blocks (Q4_0, Q8_0, Q4_K, Q6_K),
+ * round to nearest with per-block scales, deterministic.
+ * uaii_moe_fill_normal: out[i] = mean + std * N(0,1), a counter-based generator
+ * keyed by (seed, stream, i); identical on every host and thread count. */
+UAII_MOE_API int uaii_moe_quantize_rows(int fmt, const float* src, int64_t rows, int64_t cols, void* dst);
+UAII_MOE_API int uaii_moe_fill_normal(float* out, int64_t n, uint64_t seed, uint64_t stream, float mean,
+                         float std);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* UAII_MOE_H_ */

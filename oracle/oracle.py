@@ -1,0 +1,166 @@
+"""ctypes access to the CPU checkers -- TEST INFRASTRUCTURE ONLY.
+
+Imported by tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs,
+never by the product library.  Two checkers:
+
+* ``Oracle``: oracle/libmoe_oracle.so, the C restatement (moe_oracle.c) of
+  the reference path, pinned against the reference build and tests/golden/.
+* ``Reference``: oracle/_ref/libuaii_ref.so, the reference's own sources
+  compiled by oracle/Makefile; present when it was built (it is built where
+  the reference tree exists and travels with the repository as a binary).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "libmoe_oracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libuaii_ref.so")
+
+
+def _p(a):
+    if a is None:
+        return None
+    assert isinstance(a, np.ndarray) and a.flags["C_CONTIGUOUS"], "numpy C-contiguous arrays only"
+    return a.ctypes.data
+
+
+class Oracle:
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C {HERE} oracle`")
+        L = ctypes.CDLL(path)
+        sig = {
+            "uo_f16_to_f32": (c_float, [ctypes.c_uint16]),
+            "uo_packed_nbytes": (c_size_t, [c_int, c_int64]),
+            "uo_dequant_row": (c_int, [c_int, c_void_p, c_int64, c_void_p]),
+            "uo_dequant_rows": (c_int, [c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+            "uo_router_logits": (None, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+            "uo_softmax_rows": (None, [c_void_p, c_int64, c_int64, c_void_p]),
+            "uo_moe_router": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
+            "uo_topk_row": (None, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p]),
+            "uo_moe_experts_swiglu": (c_int, [c_void_p] * 5 + [c_int64] * 4 + [c_int, c_int, c_void_p, c_void_p, c_void_p]),
+            "uo_moe_experts_swiglu_packed": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int,
+                                                     c_void_p] + [c_int64] * 4 + [c_int, c_int, c_void_p, c_void_p,
+                                                                                  c_void_p]),
+            "uo_shared_expert_packed": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int,
+                                                c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+        }
+        for n, (r, a) in sig.items():
+            f = getattr(L, n)
+            f.restype, f.argtypes = r, a
+        self.L = L
+
+    def packed_nbytes(self, fmt, n):
+        return int(self.L.uo_packed_nbytes(fmt, n))
+
+    def dequant(self, fmt, packed: np.ndarray, rows: int, cols: int) -> np.ndarray:
+        out = np.empty((rows, cols), np.float32)
+        st = self.L.uo_dequant_rows(fmt, _p(packed), rows, cols, 0, _p(out))
+        if st != 0:
+            raise ValueError(f"oracle dequant status {st}")
+        return out
+
+    def router(self, x, w):
+        T, D = x.shape
+        E = w.shape[0]
+        lg = np.empty((T, E), np.float32)
+        pr = np.empty((T, E), np.float32)
+        top = np.empty((T, 1), np.float32)
+        assert self.L.uo_moe_router(_p(x), _p(w), T, D, E, _p(lg), _p(pr), _p(top)) == 0
+        return lg, pr, top
+
+    def topk(self, probs_row: np.ndarray, k: int, norm: int = 1):
+        ids = np.empty(k, np.int32)
+        w = np.empty(k, np.float32)
+        self.L.uo_topk_row(_p(probs_row), probs_row.shape[0], k, norm, _p(ids), _p(w))
+        return ids, w
+
+    def experts_f32(self, x, G, U, Dn, probs, top_k, norm=1):
+        T, D = x.shape
+        E, I, _ = G.shape
+        y = np.empty((T, D), np.float32)
+        ids = np.empty((T, max(1, min(top_k, E))), np.int32)
+        w = np.empty_like(ids, dtype=np.float32)
+        assert self.L.uo_moe_experts_swiglu(_p(x), _p(G), _p(U), _p(Dn), _p(probs), T, D, E, I, top_k, norm,
+                                            _p(y), _p(ids), _p(w)) == 0
+        return y, ids, w
+
+    def experts_packed(self, x, G, gf, U, uf, Dn, df, probs, E, I, top_k, norm=1):
+        T, D = x.shape
+        k = max(1, min(top_k, E))
+        y = np.empty((T, D), np.float32)
+        ids = np.empty((T, k), np.int32)
+        w = np.empty((T, k), np.float32)
+        assert self.L.uo_moe_experts_swiglu_packed(_p(x), _p(G), gf, _p(U), uf, _p(Dn), df, _p(probs), T, D, E,
+                                                   I, top_k, norm, _p(y), _p(ids), _p(w)) == 0
+        return y, ids, w
+
+    def shared_packed(self, x, G, gf, U, uf, Dn, df, wsg, Ish, y):
+        T, D = x.shape
+        assert self.L.uo_shared_expert_packed(_p(x), _p(G), gf, _p(U), uf, _p(Dn), df, _p(wsg), T, D, Ish,
+                                              _p(y)) == 0
+        return y
+
+
+class Reference:
+    """The reference's own compiled functions (oracle/_ref/libuaii_ref.so)."""
+
+    def __init__(self, path: str = REF_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C {HERE} ref` where the reference tree exists")
+        L = ctypes.CDLL(path)
+        sig = {
+            "uref_last_error": (c_char_p, []),
+            "uref_dequant_row": (c_int, [c_int, c_void_p, c_int64, c_void_p]),
+            "uref_moe_router": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
+            "uref_matmul_bt": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+            "uref_moe_experts_swiglu": (c_int, [c_void_p] * 5 + [c_int64] * 4 + [c_int, c_void_p]),
+            "uref_moe_experts_swiglu_mt": (c_int, [c_void_p] * 5 + [c_int64] * 4 + [c_int, c_void_p, c_int]),
+        }
+        for n, (r, a) in sig.items():
+            f = getattr(L, n)
+            f.restype, f.argtypes = r, a
+        self.L = L
+
+    def _chk(self, st):
+        if st != 0:
+            raise ValueError(f"reference status {st}: {self.L.uref_last_error().decode()}")
+
+    def dequant(self, fmt, packed: np.ndarray, rows: int, cols: int, pitch: int) -> np.ndarray:
+        out = np.empty((rows, cols), np.float32)
+        base = packed.ctypes.data
+        for r in range(rows):
+            self._chk(self.L.uref_dequant_row(fmt, base + r * pitch, cols, out.ctypes.data + r * cols * 4))
+        return out
+
+    def router(self, x, w):
+        T, D = x.shape
+        E = w.shape[0]
+        pr = np.empty((T, E), np.float32)
+        top = np.empty((T, 1), np.float32)
+        self._chk(self.L.uref_moe_router(_p(x), _p(w), T, D, E, _p(pr), _p(top)))
+        return pr, top
+
+    def logits(self, x, w):
+        T, D = x.shape
+        E = w.shape[0]
+        c = np.empty((T, E), np.float32)
+        self._chk(self.L.uref_matmul_bt(_p(x), _p(w), T, D, E, _p(c)))
+        return c
+
+    def experts(self, x, G, U, Dn, probs, top_k, threads: int = 1):
+        T, D = x.shape
+        E, I, _ = G.shape
+        y = np.empty((T, D), np.float32)
+        self._chk(self.L.uref_moe_experts_swiglu_mt(_p(x), _p(G), _p(U), _p(Dn), _p(probs), T, D, E, I, top_k,
+                                                    _p(y), threads))
+        return y
+
+
+def reference_available() -> bool:
+    return os.path.exists(REF_SO)

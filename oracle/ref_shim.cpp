@@ -1,0 +1,110 @@
+// ref_shim.cpp -- extern "C" entry points over the reference's OWN compiled code.
+//
+// TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
+// eleven unmodified source files of the reference (arjun988/Universal-AI-Inference)
+// into oracle/_ref/libuaii_ref.so.  Nothing here re-implements the reference:
+// each function only builds the reference's TensorView arguments and calls
+//   uaii::quant::dequant_gguf_row      (libs/uaii-quant/src/gguf_dequant.cpp:420-439)
+//   uaii::kernels::moe_router_f32      (libs/uaii-kernels/src/transformer.cpp:446-481)
+//   uaii::kernels::moe_experts_swiglu_f32 (libs/uaii-kernels/src/transformer.cpp:522-612)
+//   uaii::kernels::matmul_f32          (libs/uaii-kernels/src/matmul.cpp:22-56)
+// It is used by tests/ to pin oracle/moe_oracle.c, by tests/golden/make_golden.py
+// to produce fixtures, and by bench.py's reference arm as the timed CPU path.
+#include "uaii/kernels/kernels.hpp"
+#include "uaii/quant/gguf_dequant.hpp"
+
+#include <cstdint>
+#include <cstdlib>
+#include <string>
+#include <thread>
+#include <vector>
+
+using uaii::DType;
+using uaii::kernels::TensorView;
+
+namespace {
+
+TensorView f32_view(const float* p, const std::int64_t* shape, std::size_t rank) {
+  TensorView v;
+  v.dtype = DType::F32;
+  v.shape = shape;
+  v.rank = rank;
+  v.data = const_cast<float*>(p);
+  std::size_t n = 1;
+  for (std::size_t i = 0; i < rank; ++i) n *= static_cast<std::size_t>(shape[i]);
+  v.nbytes = n * sizeof(float);
+  return v;
+}
+
+thread_local std::string g_last;
+
+int status(const uaii::Error& e) {
+  g_last = e.message();
+  return static_cast<int>(e.code());
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* uref_last_error() { return g_last.c_str(); }
+
+int uref_dequant_row(int fmt, const std::uint8_t* packed, std::int64_t cols, float* out) {
+  return status(uaii::quant::dequant_gguf_row(static_cast<uaii::quant::QuantFormat>(fmt),
+                                              packed, cols, out));
+}
+
+int uref_moe_router(const float* x, const float* gate, std::int64_t T, std::int64_t D,
+                    std::int64_t E, float* probs, float* top) {
+  const std::int64_t sx[2] = {T, D}, sg[2] = {E, D}, sp[2] = {T, E}, st[2] = {T, 1};
+  TensorView vx = f32_view(x, sx, 2), vg = f32_view(gate, sg, 2);
+  TensorView vp = f32_view(probs, sp, 2), vt = f32_view(top, st, 2);
+  return status(uaii::kernels::moe_router_f32(vx, vg, &vp, &vt));
+}
+
+// Router logits through the reference GEMM (the path moe_router_f32 takes
+// before its softmax): logits[T,E] = x[T,D] . gate[E,D]^T.
+int uref_matmul_bt(const float* a, const float* b, std::int64_t M, std::int64_t K,
+                   std::int64_t N, float* c) {
+  const std::int64_t sa[2] = {M, K}, sb[2] = {N, K}, sc[2] = {M, N};
+  TensorView va = f32_view(a, sa, 2), vb = f32_view(b, sb, 2), vc = f32_view(c, sc, 2);
+  return status(uaii::kernels::matmul_f32(va, vb, &vc, false, true));
+}
+
+int uref_moe_experts_swiglu(const float* x, const float* G, const float* U, const float* Dn,
+                            const float* probs, std::int64_t T, std::int64_t D, std::int64_t E,
+                            std::int64_t I, int top_k, float* y) {
+  const std::int64_t sx[2] = {T, D}, sgu[3] = {E, I, D}, sd[3] = {E, D, I}, sp[2] = {T, E};
+  TensorView vx = f32_view(x, sx, 2), vg = f32_view(G, sgu, 3), vu = f32_view(U, sgu, 3);
+  TensorView vd = f32_view(Dn, sd, 3), vp = f32_view(probs, sp, 2), vy = f32_view(y, sx, 2);
+  return status(uaii::kernels::moe_experts_swiglu_f32(vx, vg, vu, vd, vp, &vy,
+                                                      static_cast<int>(E), top_k));
+}
+
+// Same call, with the token rows split across `threads` host threads.  Each
+// thread runs the unmodified reference function on its own contiguous token
+// range (the function is independent per token row), so the arithmetic per
+// token is exactly the reference's.  Used for the timed CPU baseline.
+int uref_moe_experts_swiglu_mt(const float* x, const float* G, const float* U,
+                               const float* Dn, const float* probs, std::int64_t T,
+                               std::int64_t D, std::int64_t E, std::int64_t I, int top_k,
+                               float* y, int threads) {
+  if (threads <= 1 || T <= 1) {
+    return uref_moe_experts_swiglu(x, G, U, Dn, probs, T, D, E, I, top_k, y);
+  }
+  if (threads > T) threads = static_cast<int>(T);
+  std::vector<int> rc(static_cast<std::size_t>(threads), 0);
+  std::vector<std::thread> pool;
+  for (int i = 0; i < threads; ++i) {
+    const std::int64_t t0 = T * i / threads, t1 = T * (i + 1) / threads;
+    pool.emplace_back([=, &rc]() {
+      rc[static_cast<std::size_t>(i)] = uref_moe_experts_swiglu(
+          x + t0 * D, G, U, Dn, probs + t0 * E, t1 - t0, D, E, I, top_k, y + t0 * D);
+    });
+  }
+  for (auto& th : pool) th.join();
+  for (int v : rc) if (v != 0) return v;
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,279 @@
+"""Device path against the oracle and the reference's golden vectors.
+
+Everything goes through the C ABI (libuaii_moe.so).  Bars:
+  * dequantized values, router logits and the top-expert id: bitwise;
+  * probabilities: within 4 ulp-scale relative error (the reference's expf
+    is not correctly rounded);
+  * layer outputs: max|y - y_ref| / max|y_ref| <= 2e-3 (REL_TOL).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+from golden.make_golden import (EXP_D, EXP_E, EXP_I, EXP_K, EXPERT_CASES, GGUF_FORMATS,  # noqa: E402
+                                expert_inputs)
+
+REL_TOL = 2e-3
+
+
+def rel_err(y, ref):
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+def bits_equal(a, b):
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    return bool(np.all((a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))))
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+# ---------------------------------------------------------------- dequant
+
+@pytest.mark.parametrize("fmt", GGUF_FORMATS)
+def test_dequant_bitexact_golden_device(backend, golden, fmt):
+    p = golden[f"dq_{fmt}_packed"]
+    out = torch.empty((p.shape[0], 512), dtype=torch.float32, device="cuda")
+    backend.dequant_rows(fmt, dev(p), p.shape[0], 512, out)
+    backend.synchronize()
+    assert bits_equal(out.cpu().numpy(), golden[f"dq_{fmt}_out"])
+
+
+@pytest.mark.parametrize("fmt", GGUF_FORMATS)
+def test_dequant_bitexact_random_host_staged(backend, oracle, um, fmt):
+    rng = np.random.default_rng(100 + fmt)
+    rows, cols = 96, 2048
+    p = rng.integers(0, 256, size=(rows, um.packed_nbytes(fmt, cols)), dtype=np.uint8)
+    out = np.empty((rows, cols), np.float32)
+    backend.dequant_rows(fmt, p, rows, cols, out)  # host in, host out
+    assert bits_equal(out, oracle.dequant(fmt, p, rows, cols))
+
+
+def test_dequant_reference_known_answer(backend, golden):
+    out = np.empty((1, 32), np.float32)
+    backend.dequant_rows(7, golden["kat_q4_0_packed"], 1, 32, out)
+    assert bits_equal(out, golden["kat_q4_0_out"])
+
+
+# ---------------------------------------------------------------- router
+
+def test_router_golden(backend, golden):
+    x, w = golden["router_x"], golden["router_w"]
+    T, D = x.shape
+    E = w.shape[0]
+    probs, top, logits = (np.empty((T, E), np.float32), np.empty((T, 1), np.float32),
+                          np.empty((T, E), np.float32))
+    backend.router(x, w, T, D, E, probs, top, logits)
+    assert bits_equal(logits, golden["router_logits"])
+    assert np.array_equal(top, golden["router_top"])
+    assert np.allclose(probs, golden["router_probs"], rtol=4e-7, atol=0)
+
+
+@pytest.mark.parametrize("T,D,E", [(1, 4096, 8), (32, 4096, 8), (4096, 4096, 8), (257, 2048, 60),
+                                   (1000, 2048, 128), (3, 100, 5)])
+def test_router_vs_oracle(backend, oracle, um, T, D, E):
+    x = um.fill_normal((T, D), 5, T)
+    w = um.fill_normal((E, D), 5, E + 99, 0.0, 0.02)
+    lg_ref, pr_ref, top_ref = oracle.router(x, w)
+    xd, wd = dev(x), dev(w)
+    probs = torch.empty((T, E), device="cuda")
+    top = torch.empty((T, 1), device="cuda")
+    logits = torch.empty((T, E), device="cuda")
+    backend.router(xd, wd, T, D, E, probs, top, logits)
+    backend.synchronize()
+    assert bits_equal(logits.cpu().numpy(), lg_ref)
+    assert np.allclose(probs.cpu().numpy(), pr_ref, rtol=4e-7, atol=0)
+    assert np.array_equal(top.cpu().numpy(), top_ref)
+
+
+def test_router_dispatch_arity_and_shapes(backend, um):
+    x = np.zeros((2, 64), np.float32)
+    w = np.zeros((4, 64), np.float32)
+    p = np.zeros((2, 4), np.float32)
+    with pytest.raises(um.UaiiMoeError) as e:
+        backend.dispatch("MoERouter", [um.f32_desc(x)], [um.f32_desc(p)])
+    assert e.value.status == 1 and "MoERouter expects" in e.value.message
+    with pytest.raises(um.UaiiMoeError) as e:
+        backend.dispatch("MoERouter", [um.f32_desc(x), um.f32_desc(w)],
+                         [um.f32_desc(p), um.f32_desc(np.zeros((2, 2), np.float32))])
+    assert "top_expert shape" in e.value.message
+    with pytest.raises(um.UaiiMoeError) as e:
+        backend.dispatch("Attention", [um.f32_desc(x)], [um.f32_desc(p)])
+    assert e.value.status == 7
+
+
+# ---------------------------------------------------------------- experts
+
+@pytest.mark.parametrize("name,gf,df", EXPERT_CASES)
+def test_experts_dispatch_golden(backend, golden, um, name, gf, df):
+    i = [c[0] for c in EXPERT_CASES].index(name)
+    x, w, G, U, Dn = expert_inputs(gf, df, 20 + i)
+    probs = golden[f"exp_{name}_probs"]
+    y = np.empty_like(x)
+    backend.dispatch("MoEExpertsSwiGLU",
+                     [um.f32_desc(x), um.packed_desc(G, gf, (EXP_E, EXP_I, EXP_D)),
+                      um.packed_desc(U, gf, (EXP_E, EXP_I, EXP_D)),
+                      um.packed_desc(Dn, df, (EXP_E, EXP_D, EXP_I)), um.f32_desc(probs)],
+                     [um.f32_desc(y)], {"num_experts": EXP_E, "top_k": EXP_K})
+    assert rel_err(y, golden[f"exp_{name}_y"]) <= REL_TOL
+
+
+@pytest.mark.parametrize("k", [1, 2, 3, 8])
+def test_experts_tie_order_golden(backend, golden, um, k):
+    x, G, U, Dn, p = (golden[n] for n in ("ties_x", "ties_G", "ties_U", "ties_D", "ties_probs"))
+    T, D = x.shape
+    E, I, _ = G.shape
+    y = np.empty_like(x)
+    backend.experts(x, G, um.F32, U, um.F32, Dn, um.F32, p, T, D, E, I, k, 1, y)
+    assert rel_err(y, golden[f"ties_y_k{k}"]) <= 1e-5
+
+
+def test_reference_smoke_demo_on_device(backend, golden, um):
+    """The reference's MoE smoke demo shapes (E=2, D=4, I=3) through dispatch."""
+    x, w = golden["smoke_x"], golden["smoke_w"]
+    probs, top = np.empty((1, 2), np.float32), np.empty((1, 1), np.float32)
+    backend.dispatch("MoERouter", [um.f32_desc(x), um.f32_desc(w)], [um.f32_desc(probs), um.f32_desc(top)],
+                     {"num_experts": 2})
+    assert abs(float(probs.sum()) - 1.0) <= 1e-3 and top[0, 0] in (0.0, 1.0)
+    assert np.array_equal(top, golden["smoke_top"])
+    y = np.empty((1, 4), np.float32)
+    backend.dispatch("MoEExpertsSwiGLU",
+                     [um.f32_desc(x), um.f32_desc(golden["smoke_G"]), um.f32_desc(golden["smoke_U"]),
+                      um.f32_desc(golden["smoke_D"]), um.f32_desc(golden["smoke_probs"])],
+                     [um.f32_desc(y)], {"num_experts": 2, "top_k": 2})
+    assert rel_err(y, golden["smoke_y"]) <= 1e-5
+
+
+def layer_case(um, gf, df, T, D, E, I, k, seed, norm=1):
+    x = um.fill_normal((T, D), seed, 1)
+    w = um.fill_normal((E, D), seed, 2, 0.0, 0.02)
+    G = um.quantize_rows(gf, um.fill_normal((E * I, D), seed, 3, 0.0, 0.02)).reshape(E, I, -1)
+    U = um.quantize_rows(gf, um.fill_normal((E * I, D), seed, 4, 0.0, 0.02)).reshape(E, I, -1)
+    Dn = um.quantize_rows(df, um.fill_normal((E * D, I), seed, 5, 0.0, 0.02)).reshape(E, D, -1)
+    return x, w, G, U, Dn
+
+
+@pytest.mark.parametrize("gf,df,T,D,E,I,k,norm", [
+    (7, 7, 64, 1024, 8, 2816, 2, 1),        # config 1 shapes
+    (14, 16, 5, 1024, 8, 512, 2, 1),        # Mixtral formats, reduced width
+    (11, 11, 40, 512, 12, 384, 4, 0),       # Qwen2 formats, no renormalisation
+    (7, 7, 50, 512, 32, 256, 8, 1),         # Qwen3 formats
+    (7, 7, 1, 256, 4, 256, 4, 1),           # k == E
+    (8, 10, 9, 256, 6, 256, 3, 1),          # Q4_1 gate/up, Q5_1 down
+    (12, 15, 7, 256, 4, 512, 2, 1),         # Q2_K gate/up, Q5_K down
+    (13, 9, 7, 512, 4, 256, 2, 1),          # Q3_K gate/up, Q5_0 down
+])
+def test_ffn_vs_oracle(backend, oracle, um, gf, df, T, D, E, I, k, norm):
+    if gf in (8, 12, 13):  # formats without a quantizer: random bytes with tame scales
+        rng = np.random.default_rng(T * 31 + D)
+        x = um.fill_normal((T, D), 4, 1)
+        w = um.fill_normal((E, D), 4, 2, 0.0, 0.02)
+        G, U, Dn = (random_blocks(um, rng, f, rows, cols) for f, rows, cols in
+                    ((gf, E * I, D), (gf, E * I, D), (df, E * D, I)))
+    else:
+        x, w, G, U, Dn = layer_case(um, gf, df, T, D, E, I, k, 40 + T)
+    _, pr, _ = oracle.router(x, w)
+    y_ref, ids_ref, _ = oracle.experts_packed(x, G, gf, U, gf, Dn, df, pr, E, I, k, norm)
+    L = um.make_layer(D, E, I, k, norm, w, G, gf, U, gf, Dn, df)
+    y = np.empty_like(x)
+    probs = np.empty((T, E), np.float32)
+    backend.ffn(L, x, T, y, probs)
+    assert np.allclose(probs, pr, rtol=4e-7, atol=0)
+    assert rel_err(y, y_ref) <= REL_TOL
+
+
+def random_blocks(um, rng, fmt, rows, cols):
+    """Random GGUF rows whose f16 scales are set to small finite values."""
+    from golden.make_golden import D_OFFSET
+    qk, bb = um.BLOCK[fmt]
+    p = rng.integers(0, 256, size=(rows, cols // qk, bb), dtype=np.uint8)
+    scale = np.float16(0.002).view(np.uint16)
+    offs = [D_OFFSET[fmt]]
+    if fmt in (8, 10, 12, 14, 15):  # a second f16 (min / dmin) follows or precedes d
+        offs.append(D_OFFSET[fmt] + 2)
+    for o in offs:
+        p[:, :, o] = scale & 0xFF
+        p[:, :, o + 1] = scale >> 8
+    return p.reshape(rows, -1)
+
+
+def test_ffn_shared_expert_sigmoid_gate(backend, oracle, um):
+    T, D, E, I, Ish, k = 16, 512, 8, 256, 768, 4
+    x, w, G, U, Dn = layer_case(um, 11, 11, T, D, E, I, k, 77)
+    Gs = um.quantize_rows(11, um.fill_normal((Ish, D), 77, 6, 0.0, 0.02))
+    Us = um.quantize_rows(11, um.fill_normal((Ish, D), 77, 7, 0.0, 0.02))
+    Ds = um.quantize_rows(11, um.fill_normal((D, Ish), 77, 8, 0.0, 0.02))
+    gi = um.fill_normal((D,), 77, 9, 0.0, 0.02)
+    _, pr, _ = oracle.router(x, w)
+    for gate in (None, gi):
+        y_ref, _, _ = oracle.experts_packed(x, G, 11, U, 11, Dn, 11, pr, E, I, k, 0)
+        oracle.shared_packed(x, Gs, 11, Us, 11, Ds, 11, gate, Ish, y_ref)
+        L = um.make_layer(D, E, I, k, 0, w, G, 11, U, 11, Dn, 11, shared=(Ish, Gs, 11, Us, 11, Ds, 11, gate))
+        y = np.empty_like(x)
+        backend.ffn(L, x, T, y)
+        assert rel_err(y, y_ref) <= REL_TOL
+
+
+def test_ffn_device_and_host_agree_and_deterministic(backend, um):
+    T, D, E, I, k = 33, 512, 8, 512, 2
+    x, w, G, U, Dn = layer_case(um, 14, 16, T, D, E, I, k, 5)
+    L = um.make_layer(D, E, I, k, 1, w, G, 14, U, 14, Dn, 16)
+    y_host = np.empty_like(x)
+    backend.ffn(L, x, T, y_host)
+    xd, wd, Gd, Ud, Dd = (dev(a) for a in (x, w, G, U, Dn))
+    Ld = um.make_layer(D, E, I, k, 1, wd, Gd, 14, Ud, 14, Dd, 16)
+    outs = []
+    for _ in range(2):
+        y = torch.empty((T, D), device="cuda")
+        backend.ffn(Ld, xd, T, y)
+        backend.synchronize()
+        outs.append(y.cpu().numpy())
+    assert bits_equal(outs[0], outs[1])
+    assert bits_equal(outs[0], y_host)
+
+
+def test_ffn_token_permutation_equivariance(backend, um):
+    T, D, E, I, k = 24, 256, 8, 256, 2
+    x, w, G, U, Dn = layer_case(um, 7, 7, T, D, E, I, k, 8)
+    L = um.make_layer(D, E, I, k, 1, w, G, 7, U, 7, Dn, 7)
+    y = np.empty_like(x)
+    backend.ffn(L, x, T, y)
+    perm = np.random.default_rng(0).permutation(T)
+    xp = np.ascontiguousarray(x[perm])
+    yp = np.empty_like(x)
+    backend.ffn(L, xp, T, yp)
+    assert bits_equal(yp, y[perm])
+
+
+def test_zero_tokens_is_a_no_op(backend, um):
+    D, E, I = 256, 4, 256
+    x, w, G, U, Dn = layer_case(um, 7, 7, 1, D, E, I, 2, 9)
+    L = um.make_layer(D, E, I, 2, 1, w, G, 7, U, 7, Dn, 7)
+    y = np.full((1, D), 7.0, np.float32)
+    backend.ffn(L, x, 0, y)
+    assert (y == 7.0).all()
+
+
+def test_bad_arguments_are_reported(backend, um):
+    D, E, I = 256, 4, 256
+    x, w, G, U, Dn = layer_case(um, 7, 7, 2, D, E, I, 2, 9)
+    y = np.empty_like(x)
+    with pytest.raises(um.UaiiMoeError) as e:  # gate/up formats differ
+        backend.ffn(um.make_layer(D, E, I, 2, 1, w, G, 7, U, 11, Dn, 7), x, 2, y)
+    assert e.value.status == 7
+    with pytest.raises(um.UaiiMoeError) as e:  # K-quant row length must be a multiple of 256
+        backend.ffn(um.make_layer(D, E, 96, 2, 1, w, G, 14, U, 14, Dn, 7), x, 2, y)
+    assert e.value.status == 1
+    with pytest.raises(um.UaiiMoeError) as e:  # wrong num_experts attribute
+        backend.dispatch("MoEExpertsSwiGLU",
+                         [um.f32_desc(x), um.packed_desc(G, 7, (E, I, D)), um.packed_desc(U, 7, (E, I, D)),
+                          um.packed_desc(Dn, 7, (E, D, I)), um.f32_desc(np.zeros((2, E), np.float32))],
+                         [um.f32_desc(y)], {"num_experts": E + 1, "top_k": 2})
+    assert "shape mismatch" in e.value.message

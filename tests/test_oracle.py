@@ -1,0 +1,154 @@
+"""The CPU oracle (oracle/moe_oracle.c) pinned to the reference.
+
+Two anchors: the committed golden vectors (tests/golden/golden.npz, produced by
+the reference's own compiled functions) and, where oracle/_ref exists, the
+reference build itself on fresh seeded inputs.  Bitwise equality is required
+for dequantized values, router logits/probabilities/argmax and the expert
+layer (the oracle repeats the reference's f32 operation order exactly).
+"""
+import numpy as np
+import pytest
+
+from golden.make_golden import (D_OFFSET, EXP_D, EXP_E, EXP_I, EXP_K, EXPERT_CASES, GGUF_FORMATS,
+                                expert_inputs, q4_0_kat_block, sha)
+
+
+def bits_equal(a, b):
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    same = a.view(np.uint32) == b.view(np.uint32)
+    return bool(np.all(same | (np.isnan(a) & np.isnan(b))))
+
+
+@pytest.mark.parametrize("fmt", GGUF_FORMATS)
+def test_dequant_matches_golden(oracle, golden, fmt):
+    p = golden[f"dq_{fmt}_packed"]
+    out = oracle.dequant(fmt, p, p.shape[0], 512)
+    assert bits_equal(out, golden[f"dq_{fmt}_out"])
+
+
+def test_golden_has_special_scales(golden, um):
+    # the fixtures really contain subnormal, inf and NaN block scales
+    for fmt in GGUF_FORMATS:
+        p = golden[f"dq_{fmt}_packed"]
+        o = D_OFFSET[fmt]
+        assert int(p[0, o]) | (int(p[0, o + 1]) << 8) == 0x0001
+        assert int(p[1, o]) | (int(p[1, o + 1]) << 8) == 0x7C00
+        out = golden[f"dq_{fmt}_out"]
+        assert np.isnan(out).any() and np.isinf(out).any()
+
+
+def test_reference_q4_0_known_answer(oracle, golden):
+    # the reference's quant test block: d = 0.5, low nibble (j+1)%8, high (j+4)%8
+    blk = q4_0_kat_block()
+    assert np.array_equal(blk, golden["kat_q4_0_packed"])
+    expected = np.array([((j + 1) % 8 - 8) * 0.5 for j in range(16)] +
+                        [((j + 4) % 8 - 8) * 0.5 for j in range(16)], np.float32)
+    out = oracle.dequant(7, blk, 1, 32)[0]
+    assert bits_equal(out, expected)
+    assert bits_equal(out, golden["kat_q4_0_out"][0])
+
+
+def test_router_matches_golden(oracle, golden):
+    lg, pr, top = oracle.router(golden["router_x"], golden["router_w"])
+    assert bits_equal(lg, golden["router_logits"])
+    assert bits_equal(pr, golden["router_probs"])
+    assert np.array_equal(top, golden["router_top"])
+
+
+@pytest.mark.parametrize("name,gf,df", EXPERT_CASES)
+def test_experts_match_golden(oracle, golden, um, name, gf, df):
+    i = [c[0] for c in EXPERT_CASES].index(name)
+    x, w, G, U, Dn = expert_inputs(gf, df, 20 + i)
+    assert np.array_equal(sha(x, w, G, U, Dn), golden[f"exp_{name}_sha"]), \
+        "synthetic inputs changed: regenerate tests/golden with make_golden.py"
+    _, pr, _ = oracle.router(x, w)
+    assert bits_equal(pr, golden[f"exp_{name}_probs"])
+    y, _, _ = oracle.experts_packed(x, G, gf, U, gf, Dn, df, pr, EXP_E, EXP_I, EXP_K)
+    assert bits_equal(y, golden[f"exp_{name}_y"])
+
+
+@pytest.mark.parametrize("k", [1, 2, 3, 8])
+def test_tie_order_matches_golden(oracle, golden, k):
+    y, _, _ = oracle.experts_f32(golden["ties_x"], golden["ties_G"], golden["ties_U"], golden["ties_D"],
+                                 golden["ties_probs"], k)
+    assert bits_equal(y, golden[f"ties_y_k{k}"])
+
+
+def test_reference_moe_smoke_demo(oracle, golden):
+    """The reference's only MoE test (demos_phase4.cpp:186-282): probs sum to 1,
+    the top id is 0 or 1, y has 4 values -- plus exact golden values."""
+    lg, pr, top = oracle.router(golden["smoke_x"], golden["smoke_w"])
+    assert abs(float(pr.sum()) - 1.0) <= 1e-3
+    assert top[0, 0] in (0.0, 1.0)
+    assert bits_equal(pr, golden["smoke_probs"]) and np.array_equal(top, golden["smoke_top"])
+    y, _, _ = oracle.experts_f32(golden["smoke_x"], golden["smoke_G"], golden["smoke_U"], golden["smoke_D"], pr, 2)
+    assert y.shape == (1, 4)
+    assert bits_equal(y, golden["smoke_y"])
+
+
+def test_topk_renorm_and_raw(oracle):
+    p = np.array([0.1, 0.4, 0.2, 0.3], np.float32)
+    ids, w = oracle.topk(p, 2, 1)
+    assert list(ids) == [1, 3]
+    assert np.allclose(w, [0.4 / 0.7, 0.3 / 0.7])
+    ids, w = oracle.topk(p, 2, 0)
+    assert np.array_equal(w, np.array([0.4, 0.3], np.float32))
+    # all-zero mass falls back to 1 (transformer.cpp:574)
+    ids, w = oracle.topk(np.zeros(4, np.float32), 2, 1)
+    assert np.array_equal(w, np.zeros(2, np.float32))
+
+
+# ---- against the reference build itself (skipped where oracle/_ref is absent)
+
+@pytest.mark.parametrize("fmt", GGUF_FORMATS)
+def test_dequant_vs_reference_random(oracle, reference, fmt):
+    rng = np.random.default_rng(5 + fmt)
+    cols = 1024
+    pitch = oracle.packed_nbytes(fmt, cols)
+    p = rng.integers(0, 256, size=(32, pitch), dtype=np.uint8)
+    assert bits_equal(oracle.dequant(fmt, p, 32, cols), reference.dequant(fmt, p, 32, cols, pitch))
+
+
+@pytest.mark.parametrize("T,D,E", [(1, 64, 2), (33, 100, 8), (64, 2048, 60), (7, 4096, 128)])
+def test_router_vs_reference(oracle, reference, um, T, D, E):
+    x = um.fill_normal((T, D), 3, T)
+    w = um.fill_normal((E, D), 3, E + 1000, 0.0, 0.02)
+    lg, pr, top = oracle.router(x, w)
+    pr2, top2 = reference.router(x, w)
+    assert bits_equal(lg, reference.logits(x, w))
+    assert bits_equal(pr, pr2)
+    assert np.array_equal(top, top2)
+
+
+def test_tie_order_vs_reference_exhaustive(oracle, reference):
+    """The restated std::partial_sort procedure on thousands of tie-heavy rows."""
+    rng = np.random.default_rng(11)
+    D, I = 32, 16
+    for E in (2, 3, 5, 8, 16, 60, 128):
+        G = rng.standard_normal((E, I, D)).astype(np.float32)
+        U = rng.standard_normal((E, I, D)).astype(np.float32)
+        Dn = rng.standard_normal((E, D, I)).astype(np.float32)
+        x = rng.standard_normal((64, D)).astype(np.float32)
+        vals = np.array([0.05, 0.1, 0.2, 0.3], np.float32)
+        p = rng.choice(vals, size=(64, E)).astype(np.float32)
+        for k in sorted({1, 2, 3, 4, 8, E}):
+            if k > E:
+                continue
+            y, _, _ = oracle.experts_f32(x, G, U, Dn, p, k)
+            assert bits_equal(y, reference.experts(x, G, U, Dn, p, k)), (E, k)
+
+
+def test_packed_experts_vs_reference_q4k_q6k(oracle, reference, um):
+    T, D, I, E, k = 6, 512, 256, 8, 2
+    x = um.fill_normal((T, D), 9, 1)
+    w = um.fill_normal((E, D), 9, 2, 0.0, 0.02)
+    G = um.quantize_rows(um.Q4_K, um.fill_normal((E * I, D), 9, 3, 0.0, 0.02))
+    U = um.quantize_rows(um.Q4_K, um.fill_normal((E * I, D), 9, 4, 0.0, 0.02))
+    Dn = um.quantize_rows(um.Q6_K, um.fill_normal((E * D, I), 9, 5, 0.0, 0.02))
+    _, pr, _ = oracle.router(x, w)
+    y, _, _ = oracle.experts_packed(x, G, um.Q4_K, U, um.Q4_K, Dn, um.Q6_K, pr, E, I, k)
+    Gf = oracle.dequant(um.Q4_K, G, E * I, D).reshape(E, I, D)
+    Uf = oracle.dequant(um.Q4_K, U, E * I, D).reshape(E, I, D)
+    Df = oracle.dequant(um.Q6_K, Dn, E * D, I).reshape(E, D, I)
+    assert bits_equal(y, reference.experts(x, Gf, Uf, Df, pr, k))

@@ -1,0 +1,801 @@
+// backend.cpp -- the MoE operators of UAII on a B200, behind the reference's
+// operator seam (IBackend::dispatch, include/uaii/interfaces/backend.hpp:77-81),
+// and the extern "C" shim declared in include/uaii_moe.h.
+//
+// Residency follows the reference CUDA backend: a pointer is device memory when
+// cudaPointerGetAttributes says so (libs/uaii-backends/src/cuda_runtime_api.cpp:586-601).
+// Host activations are staged through a backend-owned workspace and host
+// outputs are copied back before the call returns (the reference's host
+// staging, libs/uaii-backends/src/host_executable.cpp:169-233).  Host expert
+// weights are uploaded once and cached, keyed by (pointer, bytes); the cache is
+// backend-owned and freed in shutdown() like the reference's device_allocs_
+// (libs/uaii-backends/src/cuda_backend.cpp:68-78).
+#include "backend.hpp"
+
+#include <cstring>
+#include <string>
+
+#include "../../include/uaii_moe.h"
+#include "gguf_format.hpp"
+
+namespace uaii_b200 {
+
+bool is_device_ptr(const void* p) noexcept {
+  if (p == nullptr) return false;
+  cudaPointerAttributes attr{};
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  return attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
+}
+
+// CUDA errors map to Internal with the CUDA message
+// (libs/uaii-backends/src/cuda_runtime_api.cpp:30-36).
+Error cuda_status(cudaError_t st, const char* what) {
+  if (st == cudaSuccess) return Error::success();
+  return Error::make(ErrorCode::Internal, std::string("CUDA ") + what + ": " + cudaGetErrorString(st));
+}
+
+#define UAII_TRY(expr)                   \
+  do {                                   \
+    Error _e = (expr);                   \
+    if (!_e.ok()) return _e;             \
+  } while (0)
+#define UAII_CUDA(expr, what) UAII_TRY(cuda_status((expr), what))
+
+namespace {
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t v) { return (v + kAlign - 1) & ~(kAlign - 1); }
+
+bool fmt_supported(int f) { return f == kF32 || f == kF16 || fmt_is_gguf(f); }
+
+uint64_t row_bytes(int fmt, int64_t cols) {
+  if (fmt == kF32) return (uint64_t)cols * 4;
+  if (fmt == kF16) return (uint64_t)cols * 2;
+  return (uint64_t)fmt_row_bytes(fmt, cols);
+}
+
+Error check_cols(const char* what, int fmt, int64_t cols) {
+  if (!fmt_supported(fmt))
+    return Error::make(ErrorCode::NotImplemented, std::string(what) + ": unsupported weight format");
+  const int qk = fmt_block_elems(fmt);  // 1 for dense rows: any length
+  if (cols % qk != 0)
+    return Error::make(ErrorCode::InvalidArgument,
+                       std::string(what) + ": row length " + std::to_string(cols) +
+                           " is not a multiple of " + std::to_string(qk));
+  return Error::success();
+}
+
+}  // namespace
+
+Error MoeCudaBackend::initialize(int device, cudaStream_t stream) {
+  int count = 0;
+  UAII_CUDA(cudaGetDeviceCount(&count), "GetDeviceCount");
+  if (device < 0 || device >= count)
+    return Error::make(ErrorCode::InvalidArgument, "no CUDA device " + std::to_string(device));
+  UAII_CUDA(cudaSetDevice(device), "SetDevice");
+  cudaDeviceProp prop{};
+  UAII_CUDA(cudaGetDeviceProperties(&prop, device), "GetDeviceProperties");
+  if (prop.major != 10)
+    return Error::make(ErrorCode::NotImplemented,
+                       std::string("device ") + prop.name + " is not sm_100 (this build targets B200 only)");
+  device_ = device;
+  if (stream == nullptr) {
+    UAII_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "StreamCreate");
+    own_stream_ = true;
+  } else {
+    stream_ = stream;
+    own_stream_ = false;
+  }
+  return Error::success();
+}
+
+void MoeCudaBackend::shutdown() noexcept {
+  if (device_ < 0) return;
+  (void)cudaSetDevice(device_);
+  if (stream_) (void)cudaStreamSynchronize(stream_);
+  for (auto& kv : weights_) (void)cudaFree(kv.second);
+  weights_.clear();
+  for (auto& m : marks_) { (void)cudaEventDestroy(m.start); (void)cudaEventDestroy(m.stop); }
+  marks_.clear();
+  for (auto e : event_pool_) (void)cudaEventDestroy(e);
+  event_pool_.clear();
+  if (ws_) (void)cudaFree(ws_);
+  ws_ = nullptr;
+  ws_cap_ = ws_used_ = 0;
+  if (own_stream_ && stream_) (void)cudaStreamDestroy(stream_);
+  stream_ = nullptr;
+  device_ = -1;
+}
+
+Error MoeCudaBackend::synchronize() {
+  return cuda_status(cudaStreamSynchronize(stream_), "StreamSynchronize");
+}
+
+Error MoeCudaBackend::reserve(size_t bytes) {
+  ws_used_ = 0;
+  if (bytes <= ws_cap_) return Error::success();
+  UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+  if (ws_) UAII_CUDA(cudaFree(ws_), "Free");
+  ws_ = nullptr;
+  ws_cap_ = 0;
+  const size_t cap = align_up(bytes + bytes / 4);
+  UAII_CUDA(cudaMalloc(&ws_, cap), "Malloc(workspace)");
+  ws_cap_ = cap;
+  return Error::success();
+}
+
+void* MoeCudaBackend::carve(size_t bytes) {
+  void* p = ws_ + ws_used_;
+  ws_used_ += align_up(bytes);
+  return p;
+}
+
+cudaEvent_t pool_event(std::vector<cudaEvent_t>& pool) {
+  if (!pool.empty()) {
+    cudaEvent_t e = pool.back();
+    pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+void MoeCudaBackend::phase_begin(int phase) {
+  if (!profiling_) return;
+  open_phase_ = phase;
+  open_start_ = pool_event(event_pool_);
+  if (open_start_) (void)cudaEventRecord(open_start_, stream_);
+}
+
+void MoeCudaBackend::phase_end() {
+  if (!profiling_ || open_phase_ < 0 || !open_start_) return;
+  cudaEvent_t stop = pool_event(event_pool_);
+  if (stop) {
+    (void)cudaEventRecord(stop, stream_);
+    marks_.push_back(PhaseMark{open_phase_, open_start_, stop});
+  }
+  open_phase_ = -1;
+  open_start_ = nullptr;
+}
+
+Error MoeCudaBackend::profile_enable(bool on) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+  for (auto& m : marks_) { event_pool_.push_back(m.start); event_pool_.push_back(m.stop); }
+  marks_.clear();
+  for (int i = 0; i < kPhases; ++i) { phase_ms_[i] = 0.0; phase_calls_[i] = 0; }
+  launches_ = 0;
+  profiling_ = on;
+  return Error::success();
+}
+
+Error MoeCudaBackend::profile_read(double* ms, uint64_t* calls, uint64_t* launches) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+  for (auto& m : marks_) {
+    float t = 0.f;
+    UAII_CUDA(cudaEventElapsedTime(&t, m.start, m.stop), "EventElapsedTime");
+    phase_ms_[m.phase] += t;
+    phase_calls_[m.phase] += 1;
+    event_pool_.push_back(m.start);
+    event_pool_.push_back(m.stop);
+  }
+  marks_.clear();
+  for (int i = 0; i < kPhases; ++i) {
+    if (ms) ms[i] = phase_ms_[i];
+    if (calls) calls[i] = phase_calls_[i];
+  }
+  if (launches) *launches = launches_;
+  return Error::success();
+}
+
+Error MoeCudaBackend::stage_weight(const void* p, size_t bytes, const void** dev) {
+  if (p == nullptr) return Error::make(ErrorCode::InvalidArgument, "null weight pointer");
+  if (is_device_ptr(p)) {
+    *dev = p;
+    return Error::success();
+  }
+  auto key = std::make_pair(p, bytes);
+  auto it = weights_.find(key);
+  if (it != weights_.end()) {
+    *dev = it->second;
+    return Error::success();
+  }
+  void* d = nullptr;
+  UAII_CUDA(cudaMalloc(&d, align_up(bytes)), "Malloc(weights)");
+  cudaError_t st = cudaMemcpy(d, p, bytes, cudaMemcpyHostToDevice);
+  if (st != cudaSuccess) {
+    (void)cudaFree(d);
+    return cuda_status(st, "Memcpy(weights)");
+  }
+  weights_[key] = d;
+  *dev = d;
+  return Error::success();
+}
+
+Error MoeCudaBackend::release_weights(const void* host_ptr) {
+  std::lock_guard<std::mutex> lk(mu_);
+  bool found = false;
+  for (auto it = weights_.begin(); it != weights_.end();) {
+    if (it->first.first == host_ptr) {
+      UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+      (void)cudaFree(it->second);
+      it = weights_.erase(it);
+      found = true;
+    } else {
+      ++it;
+    }
+  }
+  return found ? Error::success()
+               : Error::make(ErrorCode::NotFound, "pointer has no cached device copy");
+}
+
+Error MoeCudaBackend::stage_input(const void* p, size_t bytes, void* scratch, const void** dev,
+                                  bool* was_host) {
+  if (p == nullptr) return Error::make(ErrorCode::InvalidArgument, "null input pointer");
+  if (is_device_ptr(p)) {
+    *dev = p;
+    *was_host = false;
+    return Error::success();
+  }
+  UAII_CUDA(cudaMemcpyAsync(scratch, p, bytes, cudaMemcpyHostToDevice, stream_), "MemcpyAsync(H2D)");
+  *dev = scratch;
+  *was_host = true;
+  return Error::success();
+}
+
+Error MoeCudaBackend::dequant_rows(int fmt, const void* packed, int64_t rows, int64_t cols,
+                                   float* out) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaSetDevice(device_), "SetDevice");
+  if (rows < 0 || cols <= 0) return Error::make(ErrorCode::InvalidArgument, "dequant: bad shape");
+  UAII_TRY(check_cols("dequant", fmt, cols));
+  if (!fmt_is_gguf(fmt) && cols % 32 != 0)
+    return Error::make(ErrorCode::InvalidArgument, "dequant: dense rows must be a multiple of 32");
+  const size_t in_bytes = (size_t)rows * row_bytes(fmt, cols);
+  const size_t out_bytes = sizeof(float) * (size_t)rows * (size_t)cols;
+  UAII_TRY(reserve(align_up(in_bytes) + align_up(out_bytes)));
+  void* in_scratch = carve(in_bytes);
+  float* out_scratch = static_cast<float*>(carve(out_bytes));
+  const void* in_dev = nullptr;
+  bool in_host = false;
+  UAII_TRY(stage_input(packed, in_bytes, in_scratch, &in_dev, &in_host));
+  const bool out_host = !is_device_ptr(out);
+  float* o = out_host ? out_scratch : out;
+  UAII_CUDA(launch_dequant_rows_f32(fmt, in_dev, rows, cols, (int64_t)row_bytes(fmt, cols), o, stream_),
+            "dequant_rows");
+  count_launches(rows > 0 ? 1 : 0);
+  if (out_host) {
+    UAII_CUDA(cudaMemcpyAsync(out, o, out_bytes, cudaMemcpyDeviceToHost, stream_), "MemcpyAsync(D2H)");
+    UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+  }
+  return Error::success();
+}
+
+Error MoeCudaBackend::router(const float* x, const float* gate_w, int64_t T, int64_t D,
+                             int64_t E, float* probs, float* top, float* logits) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaSetDevice(device_), "SetDevice");
+  if (T < 0 || D <= 0 || E <= 0) return Error::make(ErrorCode::InvalidArgument, "moe router ranks");
+  if (!probs || !top) return Error::make(ErrorCode::InvalidArgument, "moe router outs");
+  const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E),
+               tb = sizeof(float) * (size_t)T;
+  UAII_TRY(reserve(align_up(xb) + 3 * align_up(pb) + align_up(tb) + 4 * kAlign));
+  void* xs = carve(xb);
+  float* ls = static_cast<float*>(carve(pb));
+  float* ps = static_cast<float*>(carve(pb));
+  float* ts = static_cast<float*>(carve(tb));
+  const void* xd = nullptr;
+  const void* wd = nullptr;
+  bool xh = false;
+  if (T == 0) return Error::success();
+  UAII_TRY(stage_input(x, xb, xs, &xd, &xh));
+  UAII_TRY(stage_weight(gate_w, sizeof(float) * (size_t)(E * D), &wd));
+  const bool ph = !is_device_ptr(probs), th = !is_device_ptr(top);
+  const bool lh = logits != nullptr && !is_device_ptr(logits);
+  float* lo = (logits && !lh) ? logits : ls;
+  float* po = ph ? ps : probs;
+  float* to = th ? ts : top;
+  phase_begin(kRouter);
+  UAII_CUDA(launch_router(static_cast<const float*>(xd), static_cast<const float*>(wd), T, D, E,
+                          lo, po, to, stream_),
+            "router");
+  phase_end();
+  count_launches(2);
+  bool any_host = false;
+  if (ph) { UAII_CUDA(cudaMemcpyAsync(probs, po, pb, cudaMemcpyDeviceToHost, stream_), "D2H"); any_host = true; }
+  if (th) { UAII_CUDA(cudaMemcpyAsync(top, to, tb, cudaMemcpyDeviceToHost, stream_), "D2H"); any_host = true; }
+  if (lh) { UAII_CUDA(cudaMemcpyAsync(logits, lo, pb, cudaMemcpyDeviceToHost, stream_), "D2H"); any_host = true; }
+  if (any_host) UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+  return Error::success();
+}
+
+// Routing + expert products + combine for device-resident x.
+// `scores` rank the experts; `probs_for_w` supplies the weights (may equal scores).
+Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const float* probs_for_w,
+                                  const LayerArgs& L, int64_t T, float* yd) {
+  const int64_t D = L.D, E = L.E, I = L.I;
+  const int k = L.top_k;
+  const int64_t S = T * k;
+  RouteBuffers rb{};
+  rb.topk_ids = static_cast<int32_t*>(carve(sizeof(int32_t) * S));
+  rb.topk_w = static_cast<float*>(carve(sizeof(float) * S));
+  rb.mask = static_cast<uint8_t*>(carve((size_t)(E * T)));
+  rb.slot_local = static_cast<int32_t*>(carve(sizeof(int32_t) * S));
+  rb.slot_of = static_cast<int32_t*>(carve(sizeof(int32_t) * S));
+  rb.token_of = static_cast<int32_t*>(carve(sizeof(int32_t) * S));
+  rb.counts = static_cast<int32_t*>(carve(sizeof(int32_t) * E));
+  rb.offsets = static_cast<int32_t*>(carve(sizeof(int32_t) * (E + 1)));
+  float* xp = static_cast<float*>(carve(sizeof(float) * S * D));
+  float* h = static_cast<float*>(carve(sizeof(float) * S * I));
+  float* out = static_cast<float*>(carve(sizeof(float) * S * D));
+
+  phase_begin(kRoute);
+  UAII_CUDA(launch_route_topk(scores, probs_for_w, T, E, k, L.norm_topk, rb, stream_), "route_topk");
+  UAII_CUDA(launch_route_scan(T, E, k, rb, stream_), "route_scan");
+  UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, xp, nullptr, stream_), "route_gather");
+  phase_end();
+  count_launches(3);
+
+  const void *gd = nullptr, *ud = nullptr, *dd = nullptr;
+  UAII_TRY(stage_weight(L.gate.data, (size_t)(E * I) * row_bytes(L.gate.fmt, D), &gd));
+  UAII_TRY(stage_weight(L.up.data, (size_t)(E * I) * row_bytes(L.up.fmt, D), &ud));
+  UAII_TRY(stage_weight(L.down.data, (size_t)(E * D) * row_bytes(L.down.fmt, I), &dd));
+  phase_begin(kGateUp);
+  UAII_CUDA(launch_gateup_simt(L.gate.fmt, gd, L.up.fmt, ud, E, I, D, (int64_t)row_bytes(L.gate.fmt, D),
+                               (int64_t)row_bytes(L.up.fmt, D), xp, rb.offsets, rb.counts, h, stream_),
+            "gateup");
+  phase_end();
+  phase_begin(kDown);
+  UAII_CUDA(launch_down_simt(L.down.fmt, dd, E, D, I, (int64_t)row_bytes(L.down.fmt, I), h, rb.offsets,
+                             rb.counts, out, stream_),
+            "down");
+  phase_end();
+  count_launches(2);
+
+  float* sh_out = nullptr;
+  float* sh_gate = nullptr;
+  if (L.I_sh > 0) {
+    const int64_t Is = L.I_sh;
+    int32_t* sh_route = static_cast<int32_t*>(carve(sizeof(int32_t) * 4));
+    float* sh_h = static_cast<float*>(carve(sizeof(float) * T * Is));
+    sh_out = static_cast<float*>(carve(sizeof(float) * T * D));
+    const void *sg = nullptr, *su = nullptr, *sd = nullptr;
+    UAII_TRY(stage_weight(L.gate_sh.data, (size_t)Is * row_bytes(L.gate_sh.fmt, D), &sg));
+    UAII_TRY(stage_weight(L.up_sh.data, (size_t)Is * row_bytes(L.up_sh.fmt, D), &su));
+    UAII_TRY(stage_weight(L.down_sh.data, (size_t)D * row_bytes(L.down_sh.fmt, Is), &sd));
+    phase_begin(kShared);
+    UAII_CUDA(launch_identity_route(sh_route, T, stream_), "identity_route");
+    UAII_CUDA(launch_gateup_simt(L.gate_sh.fmt, sg, L.up_sh.fmt, su, 1, Is, D,
+                                 (int64_t)row_bytes(L.gate_sh.fmt, D), (int64_t)row_bytes(L.up_sh.fmt, D),
+                                 xd, sh_route, sh_route + 2, sh_h, stream_),
+              "shared_gateup");
+    UAII_CUDA(launch_down_simt(L.down_sh.fmt, sd, 1, D, Is, (int64_t)row_bytes(L.down_sh.fmt, Is), sh_h,
+                               sh_route, sh_route + 2, sh_out, stream_),
+              "shared_down");
+    if (L.gate_inp_sh) {
+      const void* gw = nullptr;
+      UAII_TRY(stage_weight(L.gate_inp_sh, sizeof(float) * (size_t)D, &gw));
+      sh_gate = static_cast<float*>(carve(sizeof(float) * T));
+      UAII_CUDA(launch_shared_gate(xd, static_cast<const float*>(gw), T, D, sh_gate, stream_), "shared_gate");
+      count_launches(1);
+    }
+    phase_end();
+    count_launches(3);
+  }
+  phase_begin(kCombine);
+  UAII_CUDA(launch_combine(out, D, T, D, k, rb, sh_out, sh_gate, yd, stream_), "combine");
+  phase_end();
+  count_launches(1);
+  return Error::success();
+}
+
+namespace {
+
+size_t experts_ws_bytes(const LayerArgs& L, int64_t T) {
+  const int64_t S = T * L.top_k;
+  size_t b = 0;
+  b += 6 * align_up(sizeof(int32_t) * S) + align_up((size_t)(L.E * T));
+  b += 2 * align_up(sizeof(int32_t) * (L.E + 1));
+  b += 2 * align_up(sizeof(float) * S * L.D) + align_up(sizeof(float) * S * L.I);
+  if (L.I_sh > 0)
+    b += kAlign + align_up(sizeof(float) * T * L.I_sh) + 2 * align_up(sizeof(float) * T * L.D);
+  return b + 16 * kAlign;
+}
+
+Error check_layer(const LayerArgs& L) {
+  if (L.D <= 0 || L.E <= 0 || L.I <= 0)
+    return Error::make(ErrorCode::InvalidArgument, "moe swiglu shape mismatch");
+  if (L.E > 1024) return Error::make(ErrorCode::NotImplemented, "more than 1024 experts");
+  if (L.top_k > 32) return Error::make(ErrorCode::NotImplemented, "top_k above 32");
+  if (L.gate.fmt != L.up.fmt)
+    return Error::make(ErrorCode::NotImplemented, "gate and up experts must share one format");
+  UAII_TRY(check_cols("gate_exps", L.gate.fmt, L.D));
+  UAII_TRY(check_cols("up_exps", L.up.fmt, L.D));
+  UAII_TRY(check_cols("down_exps", L.down.fmt, L.I));
+  if (L.I_sh > 0) {
+    if (L.gate_sh.fmt != L.up_sh.fmt)
+      return Error::make(ErrorCode::NotImplemented, "shared gate and up must share one format");
+    UAII_TRY(check_cols("gate_shexp", L.gate_sh.fmt, L.D));
+    UAII_TRY(check_cols("up_shexp", L.up_sh.fmt, L.D));
+    UAII_TRY(check_cols("down_shexp", L.down_sh.fmt, L.I_sh));
+  }
+  return Error::success();
+}
+
+}  // namespace
+
+Error MoeCudaBackend::experts(const float* x, const ExpertWeights& g, const ExpertWeights& u,
+                              const ExpertWeights& d, const float* probs, int64_t T, int64_t D,
+                              int64_t E, int64_t I, int top_k, int norm_topk, float* y) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaSetDevice(device_), "SetDevice");
+  LayerArgs L;
+  L.D = D; L.E = E; L.I = I;
+  // transformer.cpp:562-563: k = top_k > 0 ? top_k : 1, clamped to E
+  int k = top_k > 0 ? top_k : 1;
+  if (k > E) k = (int)E;
+  L.top_k = k;
+  L.norm_topk = norm_topk;
+  L.gate = g; L.up = u; L.down = d;
+  UAII_TRY(check_layer(L));
+  if (T < 0 || !x || !probs || !y) return Error::make(ErrorCode::InvalidArgument, "moe swiglu args");
+  if (T == 0) return Error::success();
+  const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E);
+  UAII_TRY(reserve(experts_ws_bytes(L, T) + 2 * align_up(xb) + align_up(pb)));
+  void* xs = carve(xb);
+  void* ps = carve(pb);
+  float* ys = static_cast<float*>(carve(xb));
+  const void *xd = nullptr, *pd = nullptr;
+  bool xh = false, ph = false;
+  UAII_TRY(stage_input(x, xb, xs, &xd, &xh));
+  UAII_TRY(stage_input(probs, pb, ps, &pd, &ph));
+  const bool yh = !is_device_ptr(y);
+  float* yo = yh ? ys : y;
+  UAII_TRY(run_experts(static_cast<const float*>(xd), static_cast<const float*>(pd),
+                       static_cast<const float*>(pd), L, T, yo));
+  if (yh) {
+    UAII_CUDA(cudaMemcpyAsync(y, yo, xb, cudaMemcpyDeviceToHost, stream_), "MemcpyAsync(D2H)");
+    UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+  }
+  return Error::success();
+}
+
+Error MoeCudaBackend::ffn(const LayerArgs& Lin, const float* x, int64_t T, float* y, float* probs) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaSetDevice(device_), "SetDevice");
+  LayerArgs L = Lin;
+  int k = L.top_k > 0 ? L.top_k : 1;
+  if (k > L.E) k = (int)L.E;
+  L.top_k = k;
+  UAII_TRY(check_layer(L));
+  if (!L.router_w || !x || !y) return Error::make(ErrorCode::InvalidArgument, "moe ffn args");
+  if (T < 0) return Error::make(ErrorCode::InvalidArgument, "moe ffn: negative token count");
+  if (T == 0) return Error::success();
+  const int64_t D = L.D, E = L.E;
+  const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E);
+  UAII_TRY(reserve(experts_ws_bytes(L, T) + 2 * align_up(xb) + 2 * align_up(pb)));
+  void* xs = carve(xb);
+  float* ys = static_cast<float*>(carve(xb));
+  float* logits = static_cast<float*>(carve(pb));
+  float* ps = static_cast<float*>(carve(pb));
+  const void *xd = nullptr, *wd = nullptr;
+  bool xh = false;
+  UAII_TRY(stage_input(x, xb, xs, &xd, &xh));
+  UAII_TRY(stage_weight(L.router_w, sizeof(float) * (size_t)(E * D), &wd));
+  const bool ph = probs != nullptr && !is_device_ptr(probs);
+  float* po = (probs && !ph) ? probs : ps;
+  phase_begin(kRouter);
+  UAII_CUDA(launch_router(static_cast<const float*>(xd), static_cast<const float*>(wd), T, D, E, logits,
+                          po, nullptr, stream_),
+            "router");
+  phase_end();
+  count_launches(2);
+  const bool yh = !is_device_ptr(y);
+  float* yo = yh ? ys : y;
+  // Rank on the exact logits (same order as the probabilities), weight with probs.
+  UAII_TRY(run_experts(static_cast<const float*>(xd), logits, po, L, T, yo));
+  bool any_host = false;
+  if (yh) { UAII_CUDA(cudaMemcpyAsync(y, yo, xb, cudaMemcpyDeviceToHost, stream_), "D2H"); any_host = true; }
+  if (ph) { UAII_CUDA(cudaMemcpyAsync(probs, po, pb, cudaMemcpyDeviceToHost, stream_), "D2H"); any_host = true; }
+  if (any_host) UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+  return Error::success();
+}
+
+// ---------------------------------------------------------------------------
+// IBackend::dispatch seam.  Arity checks, attribute names and defaults follow
+// kernels::dispatch_cpu (libs/uaii-kernels/src/dispatch.cpp:224-248); shape
+// checks follow moe_router_f32 / moe_experts_swiglu_f32 (transformer.cpp:446-560).
+namespace {
+
+int64_t attr_int(const std::vector<Attribute>& attrs, const char* key, int64_t def) {
+  for (const auto& a : attrs)
+    if (a.key == key && (a.type == AttrType::Int || a.type == AttrType::Bool)) return a.i;
+  return def;
+}
+
+Error weight_fmt(const TensorView& t, int* fmt) {
+  if (fmt_is_gguf(t.quant_format)) { *fmt = t.quant_format; return Error::success(); }
+  if (t.dtype == DType::F32) { *fmt = kF32; return Error::success(); }
+  if (t.dtype == DType::F16) { *fmt = kF16; return Error::success(); }
+  return Error::make(ErrorCode::NotImplemented, "unsupported expert weight type");
+}
+
+Error expert_view(const TensorView& t, const char* name, int64_t E, int64_t rows, int64_t cols,
+                  ExpertWeights* w) {
+  if (t.rank != 3 || t.dim(0) != E || t.dim(1) != rows || t.dim(2) != cols)
+    return Error::make(ErrorCode::InvalidArgument, std::string("moe swiglu shape mismatch (") + name + ")");
+  UAII_TRY(weight_fmt(t, &w->fmt));
+  const uint64_t need = (uint64_t)(E * rows) * row_bytes(w->fmt, cols);
+  if (t.nbytes != 0 && t.nbytes < need)
+    return Error::make(ErrorCode::InvalidArgument, std::string(name) + ": buffer smaller than its shape");
+  w->data = t.data;
+  w->rows = rows;
+  w->cols = cols;
+  return Error::success();
+}
+
+Error f32_2d(const TensorView& t, const char* name) {
+  if (t.dtype != DType::F32 || t.rank != 2 || t.data == nullptr)
+    return Error::make(ErrorCode::InvalidArgument, std::string(name) + " must be rank-2 f32 with data");
+  return Error::success();
+}
+
+}  // namespace
+
+Error MoeCudaBackend::dispatch(const std::string& op_name, const std::string& /*op_version*/,
+                               const std::vector<TensorView>& inputs,
+                               std::vector<TensorView>* outputs,
+                               const std::vector<Attribute>& attrs) {
+  if (outputs == nullptr || outputs->empty())
+    return Error::make(ErrorCode::InvalidArgument, "dispatch outputs empty");
+  if (op_name == "MoERouter") {
+    if (inputs.size() != 2 || outputs->size() < 2)
+      return Error::make(ErrorCode::InvalidArgument, "MoERouter expects x,gate -> probs,top_expert");
+    const TensorView &x = inputs[0], &g = inputs[1];
+    TensorView &p = (*outputs)[0], &t = (*outputs)[1];
+    if (x.rank != 2 || g.rank != 2) return Error::make(ErrorCode::InvalidArgument, "moe router ranks");
+    UAII_TRY(f32_2d(x, "x"));
+    UAII_TRY(f32_2d(g, "gate"));
+    const int64_t T = x.dim(0), D = x.dim(1), E = g.dim(0);
+    if (g.dim(1) != D) return Error::make(ErrorCode::InvalidArgument, "matmul shape mismatch");
+    if (p.rank != 2 || p.dim(0) != T || p.dim(1) != E)
+      return Error::make(ErrorCode::InvalidArgument, "matmul output shape mismatch");
+    if (t.rank != 2 || t.dim(0) != T || t.dim(1) != 1)
+      return Error::make(ErrorCode::InvalidArgument, "top_expert shape");
+    return router(static_cast<const float*>(x.data), static_cast<const float*>(g.data), T, D, E,
+                  static_cast<float*>(p.data), static_cast<float*>(t.data), nullptr);
+  }
+  if (op_name == "MoEExpertsSwiGLU") {
+    if (inputs.size() != 5 || outputs->size() != 1)
+      return Error::make(ErrorCode::InvalidArgument, "MoEExpertsSwiGLU expects x,gate,up,down,probs");
+    const TensorView& x = inputs[0];
+    const TensorView& p = inputs[4];
+    TensorView& y = (*outputs)[0];
+    if (x.rank != 2 || y.rank != 2 || inputs[1].rank != 3 || inputs[2].rank != 3 ||
+        inputs[3].rank != 3 || p.rank != 2)
+      return Error::make(ErrorCode::InvalidArgument,
+                         "moe swiglu expects x[B,D], gate/up[E,I,D], down[E,D,I], probs[B,E]");
+    const int64_t T = x.dim(0), D = x.dim(1), E = inputs[1].dim(0), I = inputs[1].dim(1);
+    const int64_t num_experts = attr_int(attrs, "num_experts", 1);
+    if (E != num_experts || p.dim(0) != T || p.dim(1) != E || y.dim(0) != T || y.dim(1) != D)
+      return Error::make(ErrorCode::InvalidArgument, "moe swiglu shape mismatch");
+    ExpertWeights g, u, d;
+    UAII_TRY(expert_view(inputs[1], "gate_exps", E, I, D, &g));
+    UAII_TRY(expert_view(inputs[2], "up_exps", E, I, D, &u));
+    UAII_TRY(expert_view(inputs[3], "down_exps", E, D, I, &d));
+    UAII_TRY(f32_2d(x, "x"));
+    UAII_TRY(f32_2d(p, "probs"));
+    return experts(static_cast<const float*>(x.data), g, u, d, static_cast<const float*>(p.data), T, D,
+                   E, I, (int)attr_int(attrs, "top_k", 2), (int)attr_int(attrs, "norm_topk", 1),
+                   static_cast<float*>(y.data));
+  }
+  if (op_name == "MoEFFN") {
+    if ((inputs.size() != 5 && inputs.size() != 8 && inputs.size() != 9) || outputs->empty() ||
+        outputs->size() > 2)
+      return Error::make(ErrorCode::InvalidArgument,
+                         "MoEFFN expects x,gate,gate_exps,up_exps,down_exps[,shexp x3[,gate_inp_shexp]]");
+    const TensorView& x = inputs[0];
+    UAII_TRY(f32_2d(x, "x"));
+    UAII_TRY(f32_2d(inputs[1], "gate"));
+    const int64_t T = x.dim(0), D = x.dim(1), E = inputs[1].dim(0);
+    if (inputs[2].rank != 3) return Error::make(ErrorCode::InvalidArgument, "gate_exps must be rank 3");
+    const int64_t I = inputs[2].dim(1);
+    LayerArgs L;
+    L.D = D; L.E = E; L.I = I;
+    L.top_k = (int)attr_int(attrs, "top_k", 2);
+    L.norm_topk = (int)attr_int(attrs, "norm_topk", 1);
+    L.router_w = static_cast<const float*>(inputs[1].data);
+    if (inputs[1].dim(1) != D) return Error::make(ErrorCode::InvalidArgument, "router shape mismatch");
+    UAII_TRY(expert_view(inputs[2], "gate_exps", E, I, D, &L.gate));
+    UAII_TRY(expert_view(inputs[3], "up_exps", E, I, D, &L.up));
+    UAII_TRY(expert_view(inputs[4], "down_exps", E, D, I, &L.down));
+    if (inputs.size() >= 8) {
+      if (inputs[5].rank != 2) return Error::make(ErrorCode::InvalidArgument, "gate_shexp must be rank 2");
+      L.I_sh = inputs[5].dim(0);
+      const int64_t one = 1;
+      TensorView v;
+      for (int j = 0; j < 3; ++j) {
+        v = inputs[5 + j];
+        const int64_t shp[3] = {one, v.dim(0), v.dim(1)};
+        v.shape = shp;
+        v.rank = 3;
+        ExpertWeights* dst = j == 0 ? &L.gate_sh : j == 1 ? &L.up_sh : &L.down_sh;
+        const int64_t rows = j == 2 ? D : L.I_sh, cols = j == 2 ? L.I_sh : D;
+        UAII_TRY(expert_view(v, j == 0 ? "gate_shexp" : j == 1 ? "up_shexp" : "down_shexp", 1, rows, cols, dst));
+      }
+      if (inputs.size() == 9) L.gate_inp_sh = static_cast<const float*>(inputs[8].data);
+    }
+    TensorView& y = (*outputs)[0];
+    if (y.rank != 2 || y.dim(0) != T || y.dim(1) != D)
+      return Error::make(ErrorCode::InvalidArgument, "MoEFFN output shape mismatch");
+    float* probs = outputs->size() == 2 ? static_cast<float*>((*outputs)[1].data) : nullptr;
+    return ffn(L, static_cast<const float*>(x.data), T, static_cast<float*>(y.data), probs);
+  }
+  return Error::make(ErrorCode::NotImplemented, "CUDA native op not implemented: " + op_name);
+}
+
+}  // namespace uaii_b200
+
+// ---------------------------------------------------------------------------
+// extern "C" shim (include/uaii_moe.h)
+using namespace uaii_b200;
+
+struct uaii_moe_backend {
+  MoeCudaBackend impl;
+};
+
+namespace {
+thread_local std::string g_last_error;
+
+int report(const Error& e) {
+  g_last_error = e.ok() ? std::string() : e.message();
+  return static_cast<int>(e.code());
+}
+
+int no_backend() { return report(Error::make(ErrorCode::InvalidArgument, "null backend")); }
+
+TensorView to_view(const uaii_moe_tensor& t) {
+  TensorView v;
+  v.dtype = static_cast<DType>(t.dtype);
+  v.quant_format = t.quant_format;
+  v.shape = t.shape;
+  v.rank = (size_t)t.rank;
+  v.data = t.data;
+  v.nbytes = (size_t)t.nbytes;
+  return v;
+}
+}  // namespace
+
+extern "C" {
+
+int uaii_moe_abi_version(void) { return UAII_MOE_ABI_VERSION; }
+
+const char* uaii_moe_last_error(void) { return g_last_error.c_str(); }
+
+int uaii_moe_backend_create(int device, void* stream, uaii_moe_backend** out) {
+  if (out == nullptr) return report(Error::make(ErrorCode::InvalidArgument, "null out"));
+  *out = nullptr;
+  auto* b = new uaii_moe_backend();
+  Error e = b->impl.initialize(device, static_cast<cudaStream_t>(stream));
+  if (!e.ok()) {
+    delete b;
+    return report(e);
+  }
+  *out = b;
+  return report(Error::success());
+}
+
+void uaii_moe_backend_destroy(uaii_moe_backend* b) { delete b; }
+
+int uaii_moe_synchronize(uaii_moe_backend* b) {
+  if (!b) return no_backend();
+  return report(b->impl.synchronize());
+}
+
+int uaii_moe_supports_op(const char* op) {
+  if (!op) return 0;
+  const std::string s(op);
+  return (s == "MoERouter" || s == "MoEExpertsSwiGLU" || s == "MoEFFN") ? 1 : 0;
+}
+
+int uaii_moe_dispatch(uaii_moe_backend* b, const char* op_name, const char* op_version,
+                      const uaii_moe_tensor* inputs, size_t n_inputs, uaii_moe_tensor* outputs,
+                      size_t n_outputs, const uaii_moe_attr* attrs, size_t n_attrs) {
+  if (!b) return no_backend();
+  if (!op_name || (n_inputs && !inputs) || (n_outputs && !outputs) || (n_attrs && !attrs))
+    return report(Error::make(ErrorCode::InvalidArgument, "dispatch: null argument"));
+  std::vector<TensorView> in, out;
+  for (size_t i = 0; i < n_inputs; ++i) in.push_back(to_view(inputs[i]));
+  for (size_t i = 0; i < n_outputs; ++i) out.push_back(to_view(outputs[i]));
+  std::vector<Attribute> at;
+  for (size_t i = 0; i < n_attrs; ++i) {
+    Attribute a;
+    a.key = attrs[i].key ? attrs[i].key : "";
+    a.type = static_cast<AttrType>(attrs[i].type);
+    a.i = attrs[i].i;
+    a.f = attrs[i].f;
+    at.push_back(a);
+  }
+  return report(b->impl.dispatch(op_name, op_version ? op_version : "1", in, &out, at));
+}
+
+int uaii_moe_dequant_rows(uaii_moe_backend* b, int fmt, const void* packed, int64_t rows,
+                          int64_t cols, float* out) {
+  if (!b) return no_backend();
+  if (!packed || !out) return report(Error::make(ErrorCode::InvalidArgument, "dequant_gguf_row null"));
+  return report(b->impl.dequant_rows(fmt, packed, rows, cols, out));
+}
+
+int uaii_moe_router_f32(uaii_moe_backend* b, const float* x, const float* gate_w, int64_t T,
+                        int64_t D, int64_t E, float* probs, float* top_expert, float* logits) {
+  if (!b) return no_backend();
+  if (!x || !gate_w) return report(Error::make(ErrorCode::InvalidArgument, "moe router inputs"));
+  return report(b->impl.router(x, gate_w, T, D, E, probs, top_expert, logits));
+}
+
+int uaii_moe_experts_swiglu(uaii_moe_backend* b, const float* x, const void* gate_exps,
+                            int gate_fmt, const void* up_exps, int up_fmt,
+                            const void* down_exps, int down_fmt, const float* probs, int64_t T,
+                            int64_t D, int64_t E, int64_t I, int top_k, int norm_topk, float* y) {
+  if (!b) return no_backend();
+  ExpertWeights g{gate_exps, gate_fmt, I, D}, u{up_exps, up_fmt, I, D}, d{down_exps, down_fmt, D, I};
+  if (!gate_exps || !up_exps || !down_exps)
+    return report(Error::make(ErrorCode::InvalidArgument, "moe swiglu weights"));
+  return report(b->impl.experts(x, g, u, d, probs, T, D, E, I, top_k, norm_topk, y));
+}
+
+int uaii_moe_ffn_forward(uaii_moe_backend* b, const uaii_moe_layer* l, const float* x, int64_t T,
+                         float* y, float* probs) {
+  if (!b) return no_backend();
+  if (!l) return report(Error::make(ErrorCode::InvalidArgument, "null layer"));
+  LayerArgs L;
+  L.D = l->d_model; L.E = l->n_experts; L.I = l->d_ff;
+  L.top_k = l->top_k;
+  L.norm_topk = l->norm_topk;
+  L.router_w = l->router_w;
+  L.gate = ExpertWeights{l->gate_exps, l->gate_fmt, L.I, L.D};
+  L.up = ExpertWeights{l->up_exps, l->up_fmt, L.I, L.D};
+  L.down = ExpertWeights{l->down_exps, l->down_fmt, L.D, L.I};
+  if (!l->gate_exps || !l->up_exps || !l->down_exps)
+    return report(Error::make(ErrorCode::InvalidArgument, "moe ffn: null expert weights"));
+  if (l->shared_d_ff > 0) {
+    if (!l->gate_shexp || !l->up_shexp || !l->down_shexp)
+      return report(Error::make(ErrorCode::InvalidArgument, "moe ffn: null shared-expert weights"));
+    L.I_sh = l->shared_d_ff;
+    L.gate_sh = ExpertWeights{l->gate_shexp, l->gate_shexp_fmt, L.I_sh, L.D};
+    L.up_sh = ExpertWeights{l->up_shexp, l->up_shexp_fmt, L.I_sh, L.D};
+    L.down_sh = ExpertWeights{l->down_shexp, l->down_shexp_fmt, L.D, L.I_sh};
+    L.gate_inp_sh = l->gate_inp_shexp;
+  }
+  return report(b->impl.ffn(L, x, T, y, probs));
+}
+
+int uaii_moe_release_weights(uaii_moe_backend* b, const void* host_ptr) {
+  if (!b) return no_backend();
+  return report(b->impl.release_weights(host_ptr));
+}
+
+int uaii_moe_profile_enable(uaii_moe_backend* b, int enable) {
+  if (!b) return no_backend();
+  return report(b->impl.profile_enable(enable != 0));
+}
+
+int uaii_moe_profile_read(uaii_moe_backend* b, double* phase_ms, uint64_t* phase_calls,
+                          uint64_t* kernel_launches) {
+  if (!b) return no_backend();
+  return report(b->impl.profile_read(phase_ms, phase_calls, kernel_launches));
+}
+
+int uaii_moe_set_expert_path(uaii_moe_backend* b, int path) {
+  if (!b) return no_backend();
+  if (path < 0 || path > 2) return report(Error::make(ErrorCode::InvalidArgument, "path must be 0, 1 or 2"));
+  b->impl.set_expert_path(path);
+  return report(Error::success());
+}
+
+}  // extern "C"

@@ -1,0 +1,154 @@
+// backend.hpp -- C++17 host side of the B200 MoE backend.
+//
+// The types mirror the reference's operator interface so that the backend reads
+// like a native op of UAII's CUDA backend:
+//   ErrorCode / Error  <- uaii::ErrorCode, uaii::Error (include/uaii/core/error.hpp:12-51)
+//   TensorView         <- kernels::TensorView (include/uaii/kernels/tensor_view.hpp:12-50)
+//   Attribute          <- ir::Attribute (include/uaii/ir/attribute.hpp:10-30), scalar kinds
+//   MoeCudaBackend::dispatch <- IBackend::dispatch (include/uaii/interfaces/backend.hpp:77-81)
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "kernels.hpp"
+
+namespace uaii_b200 {
+
+enum class ErrorCode {
+  Ok = 0, InvalidArgument = 1, NotFound = 2, IoError = 3, ConfigError = 4,
+  PluginError = 5, AbiMismatch = 6, NotImplemented = 7, Internal = 8,
+};
+
+class Error {
+ public:
+  Error() = default;
+  Error(ErrorCode c, std::string m) : code_(c), message_(std::move(m)) {}
+  static Error success() { return Error{}; }
+  static Error make(ErrorCode c, std::string m) { return Error{c, std::move(m)}; }
+  bool ok() const noexcept { return code_ == ErrorCode::Ok; }
+  ErrorCode code() const noexcept { return code_; }
+  const std::string& message() const noexcept { return message_; }
+
+ private:
+  ErrorCode code_ = ErrorCode::Ok;
+  std::string message_;
+};
+
+// uaii::DType values (include/uaii/interfaces/types.hpp:14-25)
+enum class DType { Unknown = 0, F32 = 1, F16 = 2, BF16 = 3 };
+
+struct TensorView {
+  DType dtype = DType::Unknown;
+  int quant_format = 0;  // uaii::quant::QuantFormat value
+  const int64_t* shape = nullptr;
+  size_t rank = 0;
+  void* data = nullptr;
+  size_t nbytes = 0;
+  int64_t dim(size_t i) const { return i < rank ? shape[i] : 1; }
+};
+
+enum class AttrType { String = 0, Int = 1, Float = 2, Bool = 3 };
+struct Attribute {
+  std::string key;
+  AttrType type = AttrType::Int;
+  int64_t i = 0;
+  double f = 0.0;
+};
+
+// Expert weights of one projection: [E, rows, cols] in `fmt`.
+struct ExpertWeights {
+  const void* data = nullptr;
+  int fmt = 0;
+  int64_t rows = 0, cols = 0;
+};
+
+struct LayerArgs {
+  int64_t D = 0, E = 0, I = 0;
+  int top_k = 2;
+  int norm_topk = 1;
+  const float* router_w = nullptr;  // [E, D] f32
+  ExpertWeights gate, up, down;
+  int64_t I_sh = 0;                 // shared expert width, 0 = none
+  ExpertWeights gate_sh, up_sh, down_sh;
+  const float* gate_inp_sh = nullptr;  // [D] f32 or null
+};
+
+class MoeCudaBackend {
+ public:
+  ~MoeCudaBackend() { shutdown(); }
+  Error initialize(int device, cudaStream_t stream);
+  void shutdown() noexcept;
+  Error synchronize();
+
+  Error dispatch(const std::string& op_name, const std::string& op_version,
+                 const std::vector<TensorView>& inputs, std::vector<TensorView>* outputs,
+                 const std::vector<Attribute>& attrs);
+
+  Error dequant_rows(int fmt, const void* packed, int64_t rows, int64_t cols, float* out);
+  Error router(const float* x, const float* gate_w, int64_t T, int64_t D, int64_t E,
+               float* probs, float* top, float* logits);
+  Error experts(const float* x, const ExpertWeights& g, const ExpertWeights& u,
+                const ExpertWeights& d, const float* probs, int64_t T, int64_t D, int64_t E,
+                int64_t I, int top_k, int norm_topk, float* y);
+  Error ffn(const LayerArgs& L, const float* x, int64_t T, float* y, float* probs);
+
+  Error release_weights(const void* host_ptr);
+  Error profile_enable(bool on);
+  Error profile_read(double* ms, uint64_t* calls, uint64_t* launches);
+  void set_expert_path(int p) { path_ = p; }
+  cudaStream_t stream() const { return stream_; }
+  int device() const { return device_; }
+
+ private:
+  struct Staged {  // an argument resolved to device memory
+    const void* dev = nullptr;
+    bool host = false;
+  };
+  Error stage_weight(const void* p, size_t bytes, const void** dev);
+  Error stage_input(const void* p, size_t bytes, void* scratch, const void** dev, bool* was_host);
+  Error reserve(size_t bytes);
+  void* carve(size_t bytes);
+  Error run_experts(const float* x_dev, const float* scores, const float* probs_for_w,
+                    const LayerArgs& L, int64_t T, float* y_dev);
+
+  // phase timing: events recorded around each phase while profiling is on
+  static constexpr int kPhases = 6;
+  enum Phase { kRouter = 0, kRoute = 1, kGateUp = 2, kDown = 3, kShared = 4, kCombine = 5 };
+  struct PhaseMark {
+    int phase;
+    cudaEvent_t start, stop;
+  };
+  void phase_begin(int phase);
+  void phase_end();
+  void count_launches(uint64_t n) { launches_ += n; }
+  bool profiling_ = false;
+  std::vector<PhaseMark> marks_;
+  std::vector<cudaEvent_t> event_pool_;
+  int open_phase_ = -1;
+  cudaEvent_t open_start_ = nullptr;
+  double phase_ms_[kPhases] = {};
+  uint64_t phase_calls_[kPhases] = {};
+  uint64_t launches_ = 0;
+
+  int device_ = -1;
+  cudaStream_t stream_ = nullptr;
+  bool own_stream_ = false;
+  int path_ = 0;
+  char* ws_ = nullptr;
+  size_t ws_cap_ = 0;
+  size_t ws_used_ = 0;
+  std::map<std::pair<const void*, size_t>, void*> weights_;
+  std::mutex mu_;
+};
+
+bool is_device_ptr(const void* p) noexcept;
+Error cuda_status(cudaError_t st, const char* what);
+
+}  // namespace uaii_b200

@@ -1,0 +1,65 @@
+// kernels.hpp -- launch wrappers for the device kernels of the MoE FFN path.
+// Plain pointers, sizes and a stream; every function returns a cudaError_t.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace uaii_b200 {
+
+// ---- dequant.cu: exact GGUF rows -> f32 (parity kernel for dequant_gguf_row)
+cudaError_t launch_dequant_rows_f32(int fmt, const void* packed, int64_t rows, int64_t cols,
+                                    int64_t row_pitch, float* out, cudaStream_t st);
+
+// ---- router.cu: logits in the reference GEMM order, softmax, argmax
+// probs/top may be null when only logits are wanted; logits may be null.
+cudaError_t launch_router(const float* x, const float* w, int64_t T, int64_t D, int64_t E,
+                          float* logits, float* probs, float* top, cudaStream_t st);
+
+// ---- route.cu: top-k selection, stable permutation, gather, combine
+struct RouteBuffers {
+  int32_t* topk_ids;    // [T*k]
+  float* topk_w;        // [T*k]
+  uint8_t* mask;        // [E*T] rank+1 of token t in expert e's selection, 0 if absent
+  int32_t* slot_local;  // [T*k] position of (t,r) inside its expert's list
+  int32_t* slot_of;     // [T*k] global slot of (t,r)
+  int32_t* token_of;    // [T*k] token of each slot
+  int32_t* counts;      // [E]
+  int32_t* offsets;     // [E+1]
+};
+// `scores` [T,E] rank the experts in the order of the reference's
+// std::partial_sort (value descending, ties as the reference orders them); the
+// routing weights are taken from `probs` [T,E] (which may be the same array).
+cudaError_t launch_route_topk(const float* scores, const float* probs, int64_t T, int64_t E,
+                              int k, int norm_topk, const RouteBuffers& rb, cudaStream_t st);
+// offsets = {0, T}, counts = {T} in buf[0..2]: one expert that owns every token.
+cudaError_t launch_identity_route(int32_t* buf, int64_t T, cudaStream_t st);
+cudaError_t launch_route_scan(int64_t T, int64_t E, int k, const RouteBuffers& rb,
+                              cudaStream_t st);
+// Gathers x rows into expert-contiguous slots: xp_f32 and/or xp_f16 (either may be null).
+cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E, int k,
+                                const RouteBuffers& rb, float* xp_f32, void* xp_f16,
+                                cudaStream_t st);
+// y[t] = sum_r w[t,r] * out[slot_of[t,r]] (rank order, from 0), then
+// y[t] += gate[t] * shared_out[t] when shared_out is given (gate may be null = 1).
+cudaError_t launch_combine(const float* out, int64_t out_ld, int64_t T, int64_t D, int k,
+                           const RouteBuffers& rb, const float* shared_out,
+                           const float* shared_gate, float* y, cudaStream_t st);
+// x rows -> f16 copy (shared-expert operand in token order)
+cudaError_t launch_to_f16(const float* x, int64_t n, void* out, cudaStream_t st);
+// gate[t] = sigmoid(x[t] . w) with the reference GEMM summation order
+cudaError_t launch_shared_gate(const float* x, const float* w, int64_t T, int64_t D,
+                               float* gate, cudaStream_t st);
+
+// ---- experts_simt.cu: CUDA-core grouped GEMV (f32 end to end)
+// Gate/up for every (expert, slot): h[slot, i] = silu(x.G[e,i]) * (x.U[e,i]).
+cudaError_t launch_gateup_simt(int gfmt, const void* G, int ufmt, const void* U, int64_t E,
+                               int64_t I, int64_t D, int64_t g_pitch, int64_t u_pitch,
+                               const float* xp, const int32_t* offsets, const int32_t* counts,
+                               float* h, cudaStream_t st);
+// Down for every (expert, slot): out[slot, o] = h[slot] . Dn[e, o].
+cudaError_t launch_down_simt(int dfmt, const void* Dn, int64_t E, int64_t D, int64_t I,
+                             int64_t d_pitch, const float* h, const int32_t* offsets,
+                             const int32_t* counts, float* out, cudaStream_t st);
+
+}  // namespace uaii_b200

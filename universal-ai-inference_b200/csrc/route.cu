@@ -1,0 +1,296 @@
+// route.cu -- token routing for the MoE FFN: top-k selection with renormalised
+// weights, a stable token -> expert permutation, the gather of activation rows
+// into expert-contiguous slots, and the weighted combine back to token order.
+//
+// Reference semantics (kernels::moe_experts_swiglu_f32,
+// libs/uaii-kernels/src/transformer.cpp:564-609):
+//   * experts ranked by probability descending with the reference's
+//     std::partial_sort procedure (ties included, see route_topk_kernel);
+//   * mass = sum of the k selected probabilities in rank order (1 if not > 0),
+//     w = p / mass  (norm_topk = 1, the reference behaviour; 0 keeps w = p);
+//   * y = 0, then y += w * expert_out in rank order.
+// The permutation is deterministic: inside each expert, slots follow token
+// order, so every run produces the same slot layout.
+#include <cuda_fp16.h>
+
+#include "kernels.hpp"
+
+namespace uaii_b200 {
+namespace {
+
+// The reference ranks experts with std::partial_sort over (prob, index) pairs
+// and the comparator a.prob > b.prob (transformer.cpp:564-570).  Equal
+// probabilities are ordered by the procedure of the reference's standard
+// library (GNU libstdc++): a binary heap over the first k pairs, each later
+// pair replacing the root only when strictly greater, then a heap sort.  The
+// same procedure is restated in the CPU oracle and pinned there against the
+// reference build on tie-heavy inputs, so selection and order match the
+// reference exactly, ties included.
+struct Pair {
+  float p;
+  int e;
+};
+__device__ __forceinline__ bool before(const Pair& a, const Pair& b) { return a.p > b.p; }
+
+__device__ void push_heap(Pair* h, int hole, int top, Pair v) {
+  int parent = (hole - 1) / 2;
+  while (hole > top && before(h[parent], v)) {
+    h[hole] = h[parent];
+    hole = parent;
+    parent = (hole - 1) / 2;
+  }
+  h[hole] = v;
+}
+
+__device__ void adjust_heap(Pair* h, int hole, int len, Pair v) {
+  const int top = hole;
+  int child = hole;
+  while (child < (len - 1) / 2) {
+    child = 2 * (child + 1);
+    if (before(h[child], h[child - 1])) child--;
+    h[hole] = h[child];
+    hole = child;
+  }
+  if ((len & 1) == 0 && child == (len - 2) / 2) {
+    child = 2 * (child + 1);
+    h[hole] = h[child - 1];
+    hole = child - 1;
+  }
+  push_heap(h, hole, top, v);
+}
+
+// One thread per token.  k <= 32.
+__global__ void route_topk_kernel(const float* __restrict__ scores, const float* __restrict__ probs,
+                                  int64_t T, int64_t E, int k, int norm_topk, RouteBuffers rb) {
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  const float* row = scores + t * E;
+  Pair h[32];
+  for (int i = 0; i < k; ++i) h[i] = Pair{row[i], i};
+  if (k >= 2)
+    for (int parent = (k - 2) / 2;; --parent) {
+      adjust_heap(h, parent, k, h[parent]);
+      if (parent == 0) break;
+    }
+  for (int64_t i = k; i < E; ++i) {
+    const Pair v{row[i], (int)i};
+    if (before(v, h[0])) adjust_heap(h, 0, k, v);  // the displaced root leaves the selection
+  }
+  for (int last = k; last > 1;) {
+    --last;
+    const Pair v = h[last];
+    h[last] = h[0];
+    adjust_heap(h, 0, last, v);
+  }
+  float ps[32];
+  for (int r = 0; r < k; ++r) ps[r] = (probs == scores) ? h[r].p : probs[t * E + h[r].e];
+  float mass = 0.0f;
+  for (int r = 0; r < k; ++r) mass = __fadd_rn(mass, ps[r]);
+  if (!(mass > 0.0f)) mass = 1.0f;
+  for (int r = 0; r < k; ++r) {
+    rb.topk_ids[t * k + r] = h[r].e;
+    rb.topk_w[t * k + r] = norm_topk ? __fdiv_rn(ps[r], mass) : ps[r];
+    rb.mask[(int64_t)h[r].e * T + t] = (uint8_t)(r + 1);
+  }
+}
+
+// One block per expert: stable exclusive scan of its token mask.
+__global__ void __launch_bounds__(1024) route_scan_kernel(int64_t T, int k, RouteBuffers rb) {
+  __shared__ int warp_tot[32];
+  const int e = blockIdx.x;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const uint8_t* m = rb.mask + (int64_t)e * T;
+  int running = 0;
+  for (int64_t base = 0; base < T; base += 1024) {
+    const int64_t t = base + threadIdx.x;
+    const int mv = (t < T) ? m[t] : 0;
+    const unsigned bal = __ballot_sync(0xffffffffu, mv != 0);
+    const int in_warp = __popc(bal & ((1u << lane) - 1u));
+    if (lane == 0) warp_tot[wid] = __popc(bal);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = warp_tot[w];
+      before += (w < wid) ? c : 0;
+      total += c;
+    }
+    if (mv != 0) rb.slot_local[t * k + (mv - 1)] = running + before + in_warp;
+    running += total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) rb.counts[e] = running;
+}
+
+// Offsets by a block-wide exclusive scan of counts; then one warp per (t, r).
+__global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int64_t D,
+                                    int64_t E, int k, RouteBuffers rb, float* xp32,
+                                    __half* xp16) {
+  extern __shared__ int offs[];  // [E+1]
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int64_t e = 0; e < E; ++e) { offs[e] = run; run += rb.counts[e]; }
+    offs[E] = run;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0)
+    for (int64_t e = threadIdx.x; e <= E; e += blockDim.x) rb.offsets[e] = offs[e];
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t npairs = T * k;
+  for (int64_t p = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; p < npairs; p += nw) {
+    const int64_t t = p / k;
+    const int e = rb.topk_ids[p];
+    const int slot = offs[e] + rb.slot_local[p];
+    if (lane == 0) { rb.slot_of[p] = slot; rb.token_of[slot] = (int32_t)t; }
+    if (D % 4 != 0) {  // odd widths: element by element
+      for (int64_t i = lane; i < D; i += 32) {
+        const float v = x[t * D + i];
+        if (xp32) xp32[(int64_t)slot * D + i] = v;
+        if (xp16) xp16[(int64_t)slot * D + i] = __float2half_rn(v);
+      }
+      continue;
+    }
+    const float4* src = reinterpret_cast<const float4*>(x + t * D);
+    for (int64_t i = lane; i < D / 4; i += 32) {
+      const float4 v = src[i];
+      if (xp32) reinterpret_cast<float4*>(xp32 + (int64_t)slot * D)[i] = v;
+      if (xp16) {
+        __half2* d2 = reinterpret_cast<__half2*>(xp16 + (int64_t)slot * D) + 2 * i;
+        d2[0] = __floats2half2_rn(v.x, v.y);
+        d2[1] = __floats2half2_rn(v.z, v.w);
+      }
+    }
+  }
+}
+
+__global__ void combine_kernel(const float* __restrict__ out, int64_t ld, int64_t T, int64_t D,
+                               int k, RouteBuffers rb, const float* __restrict__ sh,
+                               const float* __restrict__ gate, float* __restrict__ y) {
+  const int64_t d4 = D / 4;
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= T * d4) return;
+  const int64_t t = i / d4, c = i - t * d4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int r = 0; r < k; ++r) {
+    const int slot = rb.slot_of[t * k + r];
+    const float w = rb.topk_w[t * k + r];
+    const float4 o = reinterpret_cast<const float4*>(out + (int64_t)slot * ld)[c];
+    acc.x = __fadd_rn(acc.x, __fmul_rn(w, o.x));
+    acc.y = __fadd_rn(acc.y, __fmul_rn(w, o.y));
+    acc.z = __fadd_rn(acc.z, __fmul_rn(w, o.z));
+    acc.w = __fadd_rn(acc.w, __fmul_rn(w, o.w));
+  }
+  if (sh) {
+    const float g = gate ? gate[t] : 1.0f;
+    const float4 s = reinterpret_cast<const float4*>(sh + t * D)[c];
+    acc.x = __fadd_rn(acc.x, __fmul_rn(g, s.x));
+    acc.y = __fadd_rn(acc.y, __fmul_rn(g, s.y));
+    acc.z = __fadd_rn(acc.z, __fmul_rn(g, s.z));
+    acc.w = __fadd_rn(acc.w, __fmul_rn(g, s.w));
+  }
+  reinterpret_cast<float4*>(y + t * D)[c] = acc;
+}
+
+__global__ void combine1_kernel(const float* __restrict__ out, int64_t ld, int64_t T, int64_t D,
+                                int k, RouteBuffers rb, const float* __restrict__ sh,
+                                const float* __restrict__ gate, float* __restrict__ y) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= T * D) return;
+  const int64_t t = i / D, c = i - t * D;
+  float acc = 0.f;
+  for (int r = 0; r < k; ++r)
+    acc = __fadd_rn(acc, __fmul_rn(rb.topk_w[t * k + r], out[(int64_t)rb.slot_of[t * k + r] * ld + c]));
+  if (sh) acc = __fadd_rn(acc, __fmul_rn(gate ? gate[t] : 1.0f, sh[t * D + c]));
+  y[i] = acc;
+}
+
+__global__ void to_f16_kernel(const float* __restrict__ x, int64_t n, __half* __restrict__ o) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i < n) o[i] = __float2half_rn(x[i]);
+}
+
+// gate[t] = 1 / (1 + exp(-(x[t] . w))), one warp per token.
+__global__ void shared_gate_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                   int64_t T, int64_t D, float* __restrict__ gate) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (t >= T) return;
+  float s = 0.f;
+  for (int64_t d = lane; d < D; d += 32) s += x[t * D + d] * w[d];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) gate[t] = 1.0f / (1.0f + expf(-s));
+}
+
+__global__ void identity_route_kernel(int32_t* buf, int64_t T) {
+  buf[0] = 0;
+  buf[1] = (int32_t)T;
+  buf[2] = (int32_t)T;
+}
+
+}  // namespace
+
+cudaError_t launch_identity_route(int32_t* buf, int64_t T, cudaStream_t st) {
+  identity_route_kernel<<<1, 1, 0, st>>>(buf, T);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_route_topk(const float* scores, const float* probs, int64_t T, int64_t E,
+                              int k, int norm_topk, const RouteBuffers& rb, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  if (E > 1024 || k < 1 || k > 32 || k > E) return cudaErrorInvalidValue;
+  cudaError_t err = cudaMemsetAsync(rb.mask, 0, (size_t)(E * T), st);
+  if (err != cudaSuccess) return err;
+  route_topk_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(scores, probs, T, E, k, norm_topk,
+                                                                 rb);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_route_scan(int64_t T, int64_t E, int k, const RouteBuffers& rb,
+                              cudaStream_t st) {
+  if (T == 0) return cudaMemsetAsync(rb.counts, 0, sizeof(int32_t) * (size_t)E, st);
+  route_scan_kernel<<<(unsigned)E, 1024, 0, st>>>(T, k, rb);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E, int k,
+                                const RouteBuffers& rb, float* xp_f32, void* xp_f16,
+                                cudaStream_t st) {
+  int64_t blocks = (T * k + 7) / 8;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (blocks < 1) blocks = 1;
+  const size_t smem = sizeof(int) * (size_t)(E + 1);
+  route_gather_kernel<<<(unsigned)blocks, 256, smem, st>>>(x, T, D, E, k, rb, xp_f32,
+                                                           static_cast<__half*>(xp_f16));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const float* out, int64_t out_ld, int64_t T, int64_t D, int k,
+                           const RouteBuffers& rb, const float* shared_out,
+                           const float* shared_gate, float* y, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  if (D % 4 != 0 || out_ld % 4 != 0) {
+    combine1_kernel<<<(unsigned)((T * D + 255) / 256), 256, 0, st>>>(out, out_ld, T, D, k, rb, shared_out,
+                                                                     shared_gate, y);
+    return cudaGetLastError();
+  }
+  const int64_t n = T * (D / 4);
+  combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(out, out_ld, T, D, k, rb,
+                                                              shared_out, shared_gate, y);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_to_f16(const float* x, int64_t n, void* out, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  to_f16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, n, static_cast<__half*>(out));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_shared_gate(const float* x, const float* w, int64_t T, int64_t D, float* gate,
+                               cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  shared_gate_kernel<<<(unsigned)((T * 32 + 255) / 256), 256, 0, st>>>(x, w, T, D, gate);
+  return cudaGetLastError();
+}
+
+}  // namespace uaii_b200

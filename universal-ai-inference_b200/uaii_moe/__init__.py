@@ -1,0 +1,261 @@
+"""ctypes binding of libuaii_moe.so (the C ABI in include/uaii_moe.h).
+
+This is the binding a maintainer of the reference's Python SDK would add beside
+its own ctypes fallback (bindings/python/uaii/__init__.py in the reference):
+every call goes straight to the C ABI, and array arguments may be torch tensors
+(host or CUDA) or numpy arrays.  There is no Python compute path: if the shared
+library is missing, importing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_double, c_float, c_int, c_int32, c_int64, c_size_t, c_uint64, c_void_p
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(_HERE), "libuaii_moe.so")
+
+# uaii::quant::QuantFormat values (include/uaii/quant/formats.hpp:10-29)
+F32, F16 = 0, 1
+Q4_0, Q4_1, Q5_0, Q5_1, Q8_0 = 7, 8, 9, 10, 11
+Q2_K, Q3_K, Q4_K, Q5_K, Q6_K = 12, 13, 14, 15, 16
+FORMAT_NAMES = {F32: "f32", F16: "f16", Q4_0: "q4_0", Q4_1: "q4_1", Q5_0: "q5_0", Q5_1: "q5_1",
+                Q8_0: "q8_0", Q2_K: "q2_k", Q3_K: "q3_k", Q4_K: "q4_k", Q5_K: "q5_k", Q6_K: "q6_k"}
+BLOCK = {F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q5_0: (32, 22), Q5_1: (32, 24),
+         Q8_0: (32, 34), Q2_K: (256, 84), Q3_K: (256, 110), Q4_K: (256, 144), Q5_K: (256, 176),
+         Q6_K: (256, 210)}
+
+OK = 0
+STATUS_NAMES = {0: "Ok", 1: "InvalidArgument", 2: "NotFound", 3: "IoError", 4: "ConfigError",
+                5: "PluginError", 6: "AbiMismatch", 7: "NotImplemented", 8: "Internal"}
+
+DTYPE_UNKNOWN, DTYPE_F32, DTYPE_F16 = 0, 1, 2
+ATTR_INT, ATTR_FLOAT, ATTR_BOOL = 1, 2, 3
+
+
+class UaiiMoeError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+        self.message = message
+
+
+class Tensor(ctypes.Structure):
+    _fields_ = [("dtype", c_int32), ("quant_format", c_int32), ("shape", POINTER(c_int64)),
+                ("rank", c_uint64), ("data", c_void_p), ("nbytes", c_uint64)]
+
+
+class Attr(ctypes.Structure):
+    _fields_ = [("key", c_char_p), ("type", c_int32), ("i", c_int64), ("f", c_double)]
+
+
+class Layer(ctypes.Structure):
+    _fields_ = [("d_model", c_int64), ("n_experts", c_int64), ("d_ff", c_int64), ("top_k", c_int32),
+                ("norm_topk", c_int32), ("router_w", c_void_p), ("gate_exps", c_void_p),
+                ("gate_fmt", c_int32), ("up_exps", c_void_p), ("up_fmt", c_int32),
+                ("down_exps", c_void_p), ("down_fmt", c_int32), ("shared_d_ff", c_int64),
+                ("gate_shexp", c_void_p), ("gate_shexp_fmt", c_int32), ("up_shexp", c_void_p),
+                ("up_shexp_fmt", c_int32), ("down_shexp", c_void_p), ("down_shexp_fmt", c_int32),
+                ("gate_inp_shexp", c_void_p)]
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is not built; run `make -C {os.path.dirname(LIB_PATH)}` "
+                          "(or __graft_entry__.build())")
+    lib = ctypes.CDLL(LIB_PATH)
+    sig = {
+        "uaii_moe_abi_version": (c_int, []),
+        "uaii_moe_last_error": (c_char_p, []),
+        "uaii_moe_backend_create": (c_int, [c_int, c_void_p, POINTER(c_void_p)]),
+        "uaii_moe_backend_destroy": (None, [c_void_p]),
+        "uaii_moe_synchronize": (c_int, [c_void_p]),
+        "uaii_moe_supports_op": (c_int, [c_char_p]),
+        "uaii_moe_dispatch": (c_int, [c_void_p, c_char_p, c_char_p, POINTER(Tensor), c_size_t,
+                                      POINTER(Tensor), c_size_t, POINTER(Attr), c_size_t]),
+        "uaii_moe_dequant_rows": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_int64, c_void_p]),
+        "uaii_moe_router_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                        c_void_p, c_void_p, c_void_p]),
+        "uaii_moe_experts_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int,
+                                            c_void_p, c_int, c_void_p, c_int64, c_int64, c_int64,
+                                            c_int64, c_int, c_int, c_void_p]),
+        "uaii_moe_ffn_forward": (c_int, [c_void_p, POINTER(Layer), c_void_p, c_int64, c_void_p, c_void_p]),
+        "uaii_moe_release_weights": (c_int, [c_void_p, c_void_p]),
+        "uaii_moe_set_expert_path": (c_int, [c_void_p, c_int]),
+        "uaii_moe_profile_enable": (c_int, [c_void_p, c_int]),
+        "uaii_moe_profile_read": (c_int, [c_void_p, POINTER(c_double), POINTER(c_uint64), POINTER(c_uint64)]),
+        "uaii_moe_packed_nbytes": (c_uint64, [c_int, c_int64]),
+        "uaii_moe_quantize_rows": (c_int, [c_int, c_void_p, c_int64, c_int64, c_void_p]),
+        "uaii_moe_fill_normal": (c_int, [c_void_p, c_int64, c_uint64, c_uint64, c_float, c_float]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+EXPORTED = ("uaii_moe_abi_version", "uaii_moe_last_error", "uaii_moe_backend_create",
+            "uaii_moe_backend_destroy", "uaii_moe_synchronize", "uaii_moe_supports_op",
+            "uaii_moe_dispatch", "uaii_moe_dequant_rows", "uaii_moe_router_f32",
+            "uaii_moe_experts_swiglu", "uaii_moe_ffn_forward", "uaii_moe_release_weights",
+            "uaii_moe_set_expert_path", "uaii_moe_profile_enable", "uaii_moe_profile_read",
+            "uaii_moe_packed_nbytes", "uaii_moe_quantize_rows",
+            "uaii_moe_fill_normal")
+
+
+def _check(status: int):
+    if status != OK:
+        raise UaiiMoeError(status, lib.uaii_moe_last_error().decode())
+
+
+def ptr(a) -> int | None:
+    """Address of a torch tensor, numpy array or raw int; None stays None."""
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return a
+    if isinstance(a, np.ndarray):
+        if not a.flags["C_CONTIGUOUS"]:
+            raise ValueError("numpy array must be C-contiguous")
+        return a.ctypes.data
+    if hasattr(a, "data_ptr"):
+        if not a.is_contiguous():
+            raise ValueError("tensor must be contiguous")
+        return a.data_ptr()
+    raise TypeError(f"cannot take the address of {type(a)}")
+
+
+def packed_nbytes(fmt: int, n: int) -> int:
+    return int(lib.uaii_moe_packed_nbytes(fmt, n))
+
+
+def quantize_rows(fmt: int, src: np.ndarray) -> np.ndarray:
+    """f32 [rows, cols] -> GGUF bytes [rows, packed_nbytes(fmt, cols)] (uint8)."""
+    src = np.ascontiguousarray(src, dtype=np.float32)
+    cols = src.shape[-1]
+    rows = src.size // cols
+    out = np.empty(src.shape[:-1] + (packed_nbytes(fmt, cols),), dtype=np.uint8)
+    _check(lib.uaii_moe_quantize_rows(fmt, src.ctypes.data, rows, cols, out.ctypes.data))
+    return out
+
+
+def fill_normal(shape, seed: int, stream: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+    out = np.empty(shape, dtype=np.float32)
+    _check(lib.uaii_moe_fill_normal(out.ctypes.data, out.size, seed, stream, mean, std))
+    return out
+
+
+class Backend:
+    """One device, one stream, a workspace and a weight cache (uaii_moe_backend)."""
+
+    def __init__(self, device: int = 0, stream: int | None = None):
+        h = c_void_p()
+        _check(lib.uaii_moe_backend_create(device, stream, ctypes.byref(h)))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            lib.uaii_moe_backend_destroy(self._h)
+            self._h = c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def synchronize(self):
+        _check(lib.uaii_moe_synchronize(self._h))
+
+    def set_expert_path(self, path: int):
+        _check(lib.uaii_moe_set_expert_path(self._h, path))
+
+    PHASES = ("router", "route", "gateup", "down", "shared", "combine")
+
+    def profile_enable(self, on: bool = True):
+        _check(lib.uaii_moe_profile_enable(self._h, int(on)))
+
+    def profile_read(self):
+        """{phase: (total_ms, calls)}, kernel launches since profile_enable."""
+        ms = (c_double * 6)()
+        calls = (c_uint64 * 6)()
+        n = c_uint64()
+        _check(lib.uaii_moe_profile_read(self._h, ms, calls, ctypes.byref(n)))
+        return {p: (ms[i], int(calls[i])) for i, p in enumerate(self.PHASES)}, int(n.value)
+
+    @property
+    def handle(self):
+        return self._h
+
+    def release_weights(self, host_array):
+        _check(lib.uaii_moe_release_weights(self._h, ptr(host_array)))
+
+    def dequant_rows(self, fmt: int, packed, rows: int, cols: int, out):
+        _check(lib.uaii_moe_dequant_rows(self._h, fmt, ptr(packed), rows, cols, ptr(out)))
+
+    def router(self, x, gate_w, T: int, D: int, E: int, probs, top, logits=None):
+        _check(lib.uaii_moe_router_f32(self._h, ptr(x), ptr(gate_w), T, D, E, ptr(probs), ptr(top),
+                                       ptr(logits)))
+
+    def experts(self, x, gate, gfmt, up, ufmt, down, dfmt, probs, T, D, E, I, top_k, norm_topk, y):
+        _check(lib.uaii_moe_experts_swiglu(self._h, ptr(x), ptr(gate), gfmt, ptr(up), ufmt, ptr(down),
+                                           dfmt, ptr(probs), T, D, E, I, top_k, norm_topk, ptr(y)))
+
+    def ffn(self, layer: Layer, x, T: int, y, probs=None):
+        _check(lib.uaii_moe_ffn_forward(self._h, ctypes.byref(layer), ptr(x), T, ptr(y), ptr(probs)))
+
+    def dispatch(self, op_name: str, inputs, outputs, attrs: dict | None = None, op_version="1"):
+        """inputs/outputs: lists of tensor_desc(...) tuples; attrs: {key: int|float|bool}."""
+        keep = []
+        def mk(descs):
+            arr = (Tensor * max(1, len(descs)))()
+            for i, (dtype, qfmt, shape, data, nbytes) in enumerate(descs):
+                shp = (c_int64 * len(shape))(*shape)
+                keep.append(shp)
+                arr[i] = Tensor(dtype, qfmt, ctypes.cast(shp, POINTER(c_int64)), len(shape), ptr(data), nbytes)
+            return arr
+        ins, outs = mk(inputs), mk(outputs)
+        attrs = attrs or {}
+        at = (Attr * max(1, len(attrs)))()
+        for i, (k, v) in enumerate(attrs.items()):
+            if isinstance(v, bool):
+                at[i] = Attr(k.encode(), ATTR_BOOL, int(v), 0.0)
+            elif isinstance(v, int):
+                at[i] = Attr(k.encode(), ATTR_INT, v, 0.0)
+            else:
+                at[i] = Attr(k.encode(), ATTR_FLOAT, 0, float(v))
+        _check(lib.uaii_moe_dispatch(self._h, op_name.encode(), op_version.encode(), ins, len(inputs),
+                                     outs, len(outputs), at, len(attrs)))
+
+
+def f32_desc(a, shape=None):
+    shape = tuple(shape if shape is not None else a.shape)
+    n = int(np.prod(shape)) if shape else 0
+    return (DTYPE_F32, F32, shape, a, 4 * n)
+
+
+def packed_desc(a, fmt: int, shape):
+    """Packed GGUF expert tensor [E, rows, cols] (dtype Unknown, quant_format = fmt)."""
+    rows = int(np.prod(shape[:-1]))
+    return (DTYPE_UNKNOWN, fmt, tuple(shape), a, rows * packed_nbytes(fmt, shape[-1]))
+
+
+def make_layer(D, E, I, top_k, norm_topk, router_w, gate, gfmt, up, ufmt, down, dfmt,
+               shared=None) -> Layer:
+    """shared: None or (I_sh, gate_sh, gfmt, up_sh, ufmt, down_sh, dfmt, gate_inp_or_None)."""
+    L = Layer()
+    L.d_model, L.n_experts, L.d_ff, L.top_k, L.norm_topk = D, E, I, top_k, norm_topk
+    L.router_w, L.gate_exps, L.gate_fmt = ptr(router_w), ptr(gate), gfmt
+    L.up_exps, L.up_fmt, L.down_exps, L.down_fmt = ptr(up), ufmt, ptr(down), dfmt
+    if shared is not None:
+        I_sh, g, gf, u, uf, d, df, gi = shared
+        L.shared_d_ff = I_sh
+        L.gate_shexp, L.gate_shexp_fmt = ptr(g), gf
+        L.up_shexp, L.up_shexp_fmt = ptr(u), uf
+        L.down_shexp, L.down_shexp_fmt = ptr(d), df
+        L.gate_inp_shexp = ptr(gi)
+    return L
