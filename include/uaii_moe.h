@@ -17,9 +17,12 @@
  *   - Host pointers: inputs are copied in, outputs are copied back, and the
  *     call returns after the copy back has completed (the reference's
  *     host-staging behaviour, host_executable.cpp:169-233).
- *   - Host-resident packed expert weights are uploaded once and cached on the
- *     device, keyed by (host pointer, byte size); call
- *     uaii_moe_release_weights() before reusing or freeing such a buffer.
+ *   - Host-resident weights are copied to the device on every call, unless
+ *     the buffer was registered with uaii_moe_register_weights(): a
+ *     registered buffer is uploaded once and its device copy is reused until
+ *     uaii_moe_release_weights().  (Caching unregistered host buffers by
+ *     address is unsafe: a freed buffer's address can come back holding
+ *     different weights.)
  *
  * Errors.  Every int-returning function returns a uaii_moe_status; the message
  * of the last failure on the calling thread is uaii_moe_last_error().
@@ -205,8 +208,14 @@ UAII_MOE_API int uaii_moe_experts_swiglu(uaii_moe_backend* b, const float* x, co
 UAII_MOE_API int uaii_moe_ffn_forward(uaii_moe_backend* b, const uaii_moe_layer* layer, const float* x,
                          int64_t T, float* y, float* probs);
 
-/* Drop the cached device copy of a host weight buffer (no reference counterpart:
- * the reference never uploads weights). */
+/* Upload a host weight buffer once and reuse the device copy whenever a call
+ * passes the same (pointer, bytes); the caller keeps the host buffer unchanged
+ * until uaii_moe_release_weights().  No reference counterpart: the reference
+ * never uploads weights (its Session keeps them in host memory,
+ * libs/uaii-runtime/src/session.cpp:259-367). */
+UAII_MOE_API int uaii_moe_register_weights(uaii_moe_backend* b, const void* host_ptr, uint64_t bytes);
+
+/* Drop the device copy of a registered host weight buffer. */
 UAII_MOE_API int uaii_moe_release_weights(uaii_moe_backend* b, const void* host_ptr);
 
 /* Select the expert-product schedule: 0 = automatic, 1 = CUDA-core f32 GEMV,

@@ -277,3 +277,28 @@ def test_bad_arguments_are_reported(backend, um):
                           um.packed_desc(Dn, 7, (E, D, I)), um.f32_desc(np.zeros((2, E), np.float32))],
                          [um.f32_desc(y)], {"num_experts": E + 1, "top_k": 2})
     assert "shape mismatch" in e.value.message
+
+
+def test_registered_weights_are_reused_and_released(backend, um):
+    T, D, E, I, k = 4, 256, 4, 256, 2
+    x, w, G, U, Dn = layer_case(um, 7, 7, T, D, E, I, k, 12)
+    L = um.make_layer(D, E, I, k, 1, w, G, 7, U, 7, Dn, 7)
+    y0 = np.empty_like(x)
+    backend.ffn(L, x, T, y0)  # unregistered: staged per call
+    for a in (w, G, U, Dn):
+        backend.register_weights(a)
+    y1 = np.empty_like(x)
+    backend.ffn(L, x, T, y1)
+    assert bits_equal(y0, y1)
+    G[...] = 0  # registered buffers are not re-read: the cached copy is used
+    y2 = np.empty_like(x)
+    backend.ffn(L, x, T, y2)
+    assert bits_equal(y0, y2)
+    for a in (w, G, U, Dn):
+        backend.release_weights(a)
+    with pytest.raises(um.UaiiMoeError) as e:
+        backend.release_weights(G)
+    assert e.value.status == 2
+    y3 = np.empty_like(x)
+    backend.ffn(L, x, T, y3)  # unregistered again: zero gate weights now take effect
+    assert not bits_equal(y0, y3)

@@ -6,10 +6,10 @@
 // cudaPointerGetAttributes says so (libs/uaii-backends/src/cuda_runtime_api.cpp:586-601).
 // Host activations are staged through a backend-owned workspace and host
 // outputs are copied back before the call returns (the reference's host
-// staging, libs/uaii-backends/src/host_executable.cpp:169-233).  Host expert
-// weights are uploaded once and cached, keyed by (pointer, bytes); the cache is
-// backend-owned and freed in shutdown() like the reference's device_allocs_
-// (libs/uaii-backends/src/cuda_backend.cpp:68-78).
+// staging, libs/uaii-backends/src/host_executable.cpp:169-233).  Host weights
+// are staged per call unless registered; registered buffers are uploaded once
+// into a backend-owned cache that shutdown() frees, like the reference's
+// device_allocs_ (libs/uaii-backends/src/cuda_backend.cpp:68-78).
 #include "backend.hpp"
 
 #include <cstring>
@@ -193,18 +193,36 @@ Error MoeCudaBackend::profile_read(double* ms, uint64_t* calls, uint64_t* launch
   return Error::success();
 }
 
+size_t MoeCudaBackend::weight_stage_bytes(const void* p, size_t bytes) const {
+  if (p == nullptr || is_device_ptr(p)) return 0;
+  if (weights_.count(std::make_pair(p, bytes))) return 0;
+  return align_up(bytes);
+}
+
 Error MoeCudaBackend::stage_weight(const void* p, size_t bytes, const void** dev) {
   if (p == nullptr) return Error::make(ErrorCode::InvalidArgument, "null weight pointer");
   if (is_device_ptr(p)) {
     *dev = p;
     return Error::success();
   }
-  auto key = std::make_pair(p, bytes);
-  auto it = weights_.find(key);
+  auto it = weights_.find(std::make_pair(p, bytes));
   if (it != weights_.end()) {
     *dev = it->second;
     return Error::success();
   }
+  void* scratch = carve(bytes);
+  UAII_CUDA(cudaMemcpyAsync(scratch, p, bytes, cudaMemcpyHostToDevice, stream_), "MemcpyAsync(weights)");
+  *dev = scratch;
+  return Error::success();
+}
+
+Error MoeCudaBackend::register_weights(const void* p, size_t bytes) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaSetDevice(device_), "SetDevice");
+  if (p == nullptr || bytes == 0) return Error::make(ErrorCode::InvalidArgument, "register_weights: empty buffer");
+  if (is_device_ptr(p)) return Error::make(ErrorCode::InvalidArgument, "register_weights: pointer is device memory");
+  auto key = std::make_pair(p, bytes);
+  if (weights_.count(key)) return Error::success();
   void* d = nullptr;
   UAII_CUDA(cudaMalloc(&d, align_up(bytes)), "Malloc(weights)");
   cudaError_t st = cudaMemcpy(d, p, bytes, cudaMemcpyHostToDevice);
@@ -213,7 +231,6 @@ Error MoeCudaBackend::stage_weight(const void* p, size_t bytes, const void** dev
     return cuda_status(st, "Memcpy(weights)");
   }
   weights_[key] = d;
-  *dev = d;
   return Error::success();
 }
 
@@ -284,7 +301,8 @@ Error MoeCudaBackend::router(const float* x, const float* gate_w, int64_t T, int
   if (!probs || !top) return Error::make(ErrorCode::InvalidArgument, "moe router outs");
   const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E),
                tb = sizeof(float) * (size_t)T;
-  UAII_TRY(reserve(align_up(xb) + 3 * align_up(pb) + align_up(tb) + 4 * kAlign));
+  UAII_TRY(reserve(align_up(xb) + 3 * align_up(pb) + align_up(tb) + 4 * kAlign +
+                   weight_stage_bytes(gate_w, sizeof(float) * (size_t)(E * D))));
   void* xs = carve(xb);
   float* ls = static_cast<float*>(carve(pb));
   float* ps = static_cast<float*>(carve(pb));
@@ -429,6 +447,24 @@ Error check_layer(const LayerArgs& L) {
 
 }  // namespace
 
+namespace {
+size_t expert_bytes(const ExpertWeights& w, int64_t E) { return (size_t)(E * w.rows) * row_bytes(w.fmt, w.cols); }
+}  // namespace
+
+size_t MoeCudaBackend::layer_stage_bytes(const LayerArgs& L) const {
+  size_t b = weight_stage_bytes(L.gate.data, expert_bytes(L.gate, L.E)) +
+             weight_stage_bytes(L.up.data, expert_bytes(L.up, L.E)) +
+             weight_stage_bytes(L.down.data, expert_bytes(L.down, L.E));
+  if (L.router_w) b += weight_stage_bytes(L.router_w, sizeof(float) * (size_t)(L.E * L.D));
+  if (L.I_sh > 0) {
+    b += weight_stage_bytes(L.gate_sh.data, expert_bytes(L.gate_sh, 1)) +
+         weight_stage_bytes(L.up_sh.data, expert_bytes(L.up_sh, 1)) +
+         weight_stage_bytes(L.down_sh.data, expert_bytes(L.down_sh, 1));
+    if (L.gate_inp_sh) b += weight_stage_bytes(L.gate_inp_sh, sizeof(float) * (size_t)L.D);
+  }
+  return b;
+}
+
 Error MoeCudaBackend::experts(const float* x, const ExpertWeights& g, const ExpertWeights& u,
                               const ExpertWeights& d, const float* probs, int64_t T, int64_t D,
                               int64_t E, int64_t I, int top_k, int norm_topk, float* y) {
@@ -446,7 +482,7 @@ Error MoeCudaBackend::experts(const float* x, const ExpertWeights& g, const Expe
   if (T < 0 || !x || !probs || !y) return Error::make(ErrorCode::InvalidArgument, "moe swiglu args");
   if (T == 0) return Error::success();
   const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E);
-  UAII_TRY(reserve(experts_ws_bytes(L, T) + 2 * align_up(xb) + align_up(pb)));
+  UAII_TRY(reserve(experts_ws_bytes(L, T) + 2 * align_up(xb) + align_up(pb) + layer_stage_bytes(L)));
   void* xs = carve(xb);
   void* ps = carve(pb);
   float* ys = static_cast<float*>(carve(xb));
@@ -478,7 +514,7 @@ Error MoeCudaBackend::ffn(const LayerArgs& Lin, const float* x, int64_t T, float
   if (T == 0) return Error::success();
   const int64_t D = L.D, E = L.E;
   const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E);
-  UAII_TRY(reserve(experts_ws_bytes(L, T) + 2 * align_up(xb) + 2 * align_up(pb)));
+  UAII_TRY(reserve(experts_ws_bytes(L, T) + 2 * align_up(xb) + 2 * align_up(pb) + layer_stage_bytes(L)));
   void* xs = carve(xb);
   float* ys = static_cast<float*>(carve(xb));
   float* logits = static_cast<float*>(carve(pb));
@@ -773,6 +809,11 @@ int uaii_moe_ffn_forward(uaii_moe_backend* b, const uaii_moe_layer* l, const flo
     L.gate_inp_sh = l->gate_inp_shexp;
   }
   return report(b->impl.ffn(L, x, T, y, probs));
+}
+
+int uaii_moe_register_weights(uaii_moe_backend* b, const void* host_ptr, uint64_t bytes) {
+  if (!b) return no_backend();
+  return report(b->impl.register_weights(host_ptr, (size_t)bytes));
 }
 
 int uaii_moe_release_weights(uaii_moe_backend* b, const void* host_ptr) {

@@ -99,6 +99,7 @@ class MoeCudaBackend {
                 int64_t I, int top_k, int norm_topk, float* y);
   Error ffn(const LayerArgs& L, const float* x, int64_t T, float* y, float* probs);
 
+  Error register_weights(const void* host_ptr, size_t bytes);
   Error release_weights(const void* host_ptr);
   Error profile_enable(bool on);
   Error profile_read(double* ms, uint64_t* calls, uint64_t* launches);
@@ -111,7 +112,11 @@ class MoeCudaBackend {
     const void* dev = nullptr;
     bool host = false;
   };
+  // Device address of a weight: device pointers as they are, registered host
+  // buffers from the cache, other host buffers copied into the workspace.
   Error stage_weight(const void* p, size_t bytes, const void** dev);
+  size_t weight_stage_bytes(const void* p, size_t bytes) const;
+  size_t layer_stage_bytes(const LayerArgs& L) const;
   Error stage_input(const void* p, size_t bytes, void* scratch, const void** dev, bool* was_host);
   Error reserve(size_t bytes);
   void* carve(size_t bytes);

@@ -82,6 +82,7 @@ def _load():
                                             c_void_p, c_int, c_void_p, c_int64, c_int64, c_int64,
                                             c_int64, c_int, c_int, c_void_p]),
         "uaii_moe_ffn_forward": (c_int, [c_void_p, POINTER(Layer), c_void_p, c_int64, c_void_p, c_void_p]),
+        "uaii_moe_register_weights": (c_int, [c_void_p, c_void_p, c_uint64]),
         "uaii_moe_release_weights": (c_int, [c_void_p, c_void_p]),
         "uaii_moe_set_expert_path": (c_int, [c_void_p, c_int]),
         "uaii_moe_profile_enable": (c_int, [c_void_p, c_int]),
@@ -101,7 +102,8 @@ lib = _load()
 EXPORTED = ("uaii_moe_abi_version", "uaii_moe_last_error", "uaii_moe_backend_create",
             "uaii_moe_backend_destroy", "uaii_moe_synchronize", "uaii_moe_supports_op",
             "uaii_moe_dispatch", "uaii_moe_dequant_rows", "uaii_moe_router_f32",
-            "uaii_moe_experts_swiglu", "uaii_moe_ffn_forward", "uaii_moe_release_weights",
+            "uaii_moe_experts_swiglu", "uaii_moe_ffn_forward", "uaii_moe_register_weights",
+            "uaii_moe_release_weights",
             "uaii_moe_set_expert_path", "uaii_moe_profile_enable", "uaii_moe_profile_read",
             "uaii_moe_packed_nbytes", "uaii_moe_quantize_rows",
             "uaii_moe_fill_normal")
@@ -190,6 +192,9 @@ class Backend:
     @property
     def handle(self):
         return self._h
+
+    def register_weights(self, host_array):
+        _check(lib.uaii_moe_register_weights(self._h, ptr(host_array), host_array.nbytes))
 
     def release_weights(self, host_array):
         _check(lib.uaii_moe_release_weights(self._h, ptr(host_array)))
