@@ -269,7 +269,7 @@ def test_bad_arguments_are_reported(backend, um):
         backend.ffn(um.make_layer(D, E, I, 2, 1, w, G, 7, U, 11, Dn, 7), x, 2, y)
     assert e.value.status == 7
     with pytest.raises(um.UaiiMoeError) as e:  # K-quant row length must be a multiple of 256
-        backend.ffn(um.make_layer(D, E, 96, 2, 1, w, G, 14, U, 14, Dn, 7), x, 2, y)
+        backend.ffn(um.make_layer(D, E, 96, 2, 1, w, G, 7, U, 7, Dn, 16), x, 2, y)
     assert e.value.status == 1
     with pytest.raises(um.UaiiMoeError) as e:  # wrong num_experts attribute
         backend.dispatch("MoEExpertsSwiGLU",
@@ -302,3 +302,64 @@ def test_registered_weights_are_reused_and_released(backend, um):
     y3 = np.empty_like(x)
     backend.ffn(L, x, T, y3)  # unregistered again: zero gate weights now take effect
     assert not bits_equal(y0, y3)
+
+
+# ---------------------------------------------------------------- tensor-core path
+
+@pytest.mark.parametrize("gf,df,T,D,E,I,k", [
+    (7, 7, 1, 1024, 8, 2816, 2),       # config 1 shapes, decode (slot tile 16, split-K down)
+    (7, 7, 64, 1024, 8, 2816, 2),      # config 1 shapes, 64 tokens
+    (14, 16, 1, 1024, 8, 2048, 2),     # Mixtral formats (Q4_K / Q6_K), decode
+    (14, 16, 32, 1024, 8, 2048, 2),    # Mixtral formats, 32 tokens
+    (14, 16, 700, 512, 4, 2048, 2),    # Mixtral formats, slot tile 256
+    (11, 11, 100, 512, 8, 512, 4),     # Q8_0, slot tile 64
+    (7, 7, 200, 2048, 16, 768, 8),     # Qwen3 formats, slot tile 128
+    (7, 7, 3, 256, 4, 256, 4),         # k == E, tiny
+])
+def test_tensor_core_path_vs_oracle(backend, oracle, um, gf, df, T, D, E, I, k):
+    x, w, G, U, Dn = layer_case(um, gf, df, T, D, E, I, k, 60 + T)
+    _, pr, _ = oracle.router(x, w)
+    y_ref, _, _ = oracle.experts_packed(x, G, gf, U, gf, Dn, df, pr, E, I, k, 1)
+    L = um.make_layer(D, E, I, k, 1, w, G, gf, U, gf, Dn, df)
+    y = np.empty_like(x)
+    backend.set_expert_path(2)
+    try:
+        backend.ffn(L, x, T, y)
+    finally:
+        backend.set_expert_path(0)
+    assert rel_err(y, y_ref) <= REL_TOL
+
+
+def test_tensor_core_path_refuses_unaligned_pitch(backend, um):
+    # Q6_K rows of 256 elements are 210 bytes: not a 16-byte pitch for TMA
+    D, E, I = 256, 4, 256
+    x, w, G, U, Dn = layer_case(um, 14, 16, 2, D, E, I, 2, 3)
+    y = np.empty_like(x)
+    backend.set_expert_path(2)
+    try:
+        with pytest.raises(um.UaiiMoeError) as e:
+            backend.ffn(um.make_layer(D, E, I, 2, 1, w, G, 14, U, 14, Dn, 16), x, 2, y)
+        assert e.value.status == 7
+    finally:
+        backend.set_expert_path(0)
+    backend.ffn(um.make_layer(D, E, I, 2, 1, w, G, 14, U, 14, Dn, 16), x, 2, y)  # automatic: CUDA cores
+
+
+def test_tensor_core_shared_expert(backend, oracle, um):
+    T, D, E, I, Ish, k = 48, 512, 8, 256, 1024, 4
+    x, w, G, U, Dn = layer_case(um, 11, 11, T, D, E, I, k, 78)
+    Gs = um.quantize_rows(11, um.fill_normal((Ish, D), 78, 6, 0.0, 0.02))
+    Us = um.quantize_rows(11, um.fill_normal((Ish, D), 78, 7, 0.0, 0.02))
+    Ds = um.quantize_rows(11, um.fill_normal((D, Ish), 78, 8, 0.0, 0.02))
+    gi = um.fill_normal((D,), 78, 9, 0.0, 0.02)
+    _, pr, _ = oracle.router(x, w)
+    y_ref, _, _ = oracle.experts_packed(x, G, 11, U, 11, Dn, 11, pr, E, I, k, 0)
+    oracle.shared_packed(x, Gs, 11, Us, 11, Ds, 11, gi, Ish, y_ref)
+    L = um.make_layer(D, E, I, k, 0, w, G, 11, U, 11, Dn, 11, shared=(Ish, Gs, 11, Us, 11, Ds, 11, gi))
+    y = np.empty_like(x)
+    backend.set_expert_path(2)
+    try:
+        backend.ffn(L, x, T, y)
+    finally:
+        backend.set_expert_path(0)
+    assert rel_err(y, y_ref) <= REL_TOL

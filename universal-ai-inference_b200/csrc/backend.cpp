@@ -82,6 +82,8 @@ Error MoeCudaBackend::initialize(int device, cudaStream_t stream) {
     return Error::make(ErrorCode::NotImplemented,
                        std::string("device ") + prop.name + " is not sm_100 (this build targets B200 only)");
   device_ = device;
+  UAII_CUDA(cudaMalloc(&dev_err_, sizeof(int)), "Malloc(error flag)");
+  UAII_CUDA(cudaMemset(dev_err_, 0, sizeof(int)), "Memset(error flag)");
   if (stream == nullptr) {
     UAII_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "StreamCreate");
     own_stream_ = true;
@@ -105,13 +107,30 @@ void MoeCudaBackend::shutdown() noexcept {
   if (ws_) (void)cudaFree(ws_);
   ws_ = nullptr;
   ws_cap_ = ws_used_ = 0;
+  if (dev_err_) (void)cudaFree(dev_err_);
+  dev_err_ = nullptr;
   if (own_stream_ && stream_) (void)cudaStreamDestroy(stream_);
   stream_ = nullptr;
   device_ = -1;
 }
 
 Error MoeCudaBackend::synchronize() {
-  return cuda_status(cudaStreamSynchronize(stream_), "StreamSynchronize");
+  std::lock_guard<std::mutex> lk(mu_);
+  return sync_and_check();
+}
+
+// Wait for the stream and report a device-side failure recorded by a kernel
+// (a bounded wait that ran out); the flag is cleared once reported.
+Error MoeCudaBackend::sync_and_check() {
+  UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+  int code = 0;
+  UAII_CUDA(cudaMemcpy(&code, dev_err_, sizeof(int), cudaMemcpyDeviceToHost), "Memcpy(error flag)");
+  if (code != 0) {
+    (void)cudaMemset(dev_err_, 0, sizeof(int));
+    return Error::make(ErrorCode::Internal,
+                       "tensor-core expert kernel gave up waiting (code " + std::to_string(code) + ")");
+  }
+  return Error::success();
 }
 
 Error MoeCudaBackend::reserve(size_t bytes) {
@@ -332,13 +351,48 @@ Error MoeCudaBackend::router(const float* x, const float* gate_w, int64_t T, int
   return Error::success();
 }
 
+// Which expert-product schedule a layer call uses, and its tile shape.
+ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T) const {
+  ExpertPlan p;
+  const int64_t S = T * L.top_k;
+  const bool umma_ok = umma_shapes_supported(L.gate.fmt, L.down.fmt, L.D, L.I);
+  p.umma = path_ != 1 && umma_ok;
+  p.umma_refused = path_ == 2 && !umma_ok;
+  const int sms = 148;
+  auto pick_bn = [](double tpe) { return tpe <= 16 ? 16 : tpe <= 32 ? 32 : tpe <= 64 ? 64 : tpe <= 128 ? 128 : 256; };
+  auto pick_splits = [&](int64_t tiles, int kchunks) {
+    int64_t sp = tiles > 0 ? (2 * sms + tiles - 1) / tiles : 1;
+    if (sp > 16) sp = 16;
+    if (sp > kchunks) sp = kchunks;
+    return (int)(sp < 1 ? 1 : sp);
+  };
+  const int64_t active = S < L.E ? S : L.E;
+  const double tpe = active > 0 ? (double)S / (double)active : 1.0;
+  p.bn = pick_bn(tpe);
+  if (p.umma) {
+    const int64_t n_tiles = (int64_t)((tpe + p.bn - 1) / p.bn);
+    p.splits = pick_splits(active * n_tiles * (L.D / 128), umma_kchunks(L.down.fmt, L.I));
+  }
+  if (L.I_sh > 0) {
+    p.sh_umma = p.umma && umma_shapes_supported(L.gate_sh.fmt, L.down_sh.fmt, L.D, L.I_sh);
+    p.sh_bn = pick_bn((double)T);
+    if (p.sh_umma)
+      p.sh_splits = pick_splits(((T + p.sh_bn - 1) / p.sh_bn) * (L.D / 128), umma_kchunks(L.down_sh.fmt, L.I_sh));
+  }
+  return p;
+}
+
 // Routing + expert products + combine for device-resident x.
 // `scores` rank the experts; `probs_for_w` supplies the weights (may equal scores).
 Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const float* probs_for_w,
-                                  const LayerArgs& L, int64_t T, float* yd) {
+                                  const LayerArgs& L, const ExpertPlan& P, int64_t T, float* yd) {
   const int64_t D = L.D, E = L.E, I = L.I;
   const int k = L.top_k;
   const int64_t S = T * k;
+  if (P.umma_refused)
+    return Error::make(ErrorCode::NotImplemented,
+                       "tensor-core path needs Q4_0/Q8_0/Q4_K/Q6_K weights, d_ff % 64 == 0, d_model % 128 == 0 "
+                       "and 16-byte row pitches");
   RouteBuffers rb{};
   rb.topk_ids = static_cast<int32_t*>(carve(sizeof(int32_t) * S));
   rb.topk_w = static_cast<float*>(carve(sizeof(float) * S));
@@ -348,53 +402,94 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
   rb.token_of = static_cast<int32_t*>(carve(sizeof(int32_t) * S));
   rb.counts = static_cast<int32_t*>(carve(sizeof(int32_t) * E));
   rb.offsets = static_cast<int32_t*>(carve(sizeof(int32_t) * (E + 1)));
-  float* xp = static_cast<float*>(carve(sizeof(float) * S * D));
-  float* h = static_cast<float*>(carve(sizeof(float) * S * I));
-  float* out = static_cast<float*>(carve(sizeof(float) * S * D));
-
-  phase_begin(kRoute);
-  UAII_CUDA(launch_route_topk(scores, probs_for_w, T, E, k, L.norm_topk, rb, stream_), "route_topk");
-  UAII_CUDA(launch_route_scan(T, E, k, rb, stream_), "route_scan");
-  UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, xp, nullptr, stream_), "route_gather");
-  phase_end();
-  count_launches(3);
+  int32_t* tile_base = static_cast<int32_t*>(carve(sizeof(int32_t) * (E + 1)));
 
   const void *gd = nullptr, *ud = nullptr, *dd = nullptr;
   UAII_TRY(stage_weight(L.gate.data, (size_t)(E * I) * row_bytes(L.gate.fmt, D), &gd));
   UAII_TRY(stage_weight(L.up.data, (size_t)(E * I) * row_bytes(L.up.fmt, D), &ud));
   UAII_TRY(stage_weight(L.down.data, (size_t)(E * D) * row_bytes(L.down.fmt, I), &dd));
-  phase_begin(kGateUp);
-  UAII_CUDA(launch_gateup_simt(L.gate.fmt, gd, L.up.fmt, ud, E, I, D, (int64_t)row_bytes(L.gate.fmt, D),
-                               (int64_t)row_bytes(L.up.fmt, D), xp, rb.offsets, rb.counts, h, stream_),
-            "gateup");
-  phase_end();
-  phase_begin(kDown);
-  UAII_CUDA(launch_down_simt(L.down.fmt, dd, E, D, I, (int64_t)row_bytes(L.down.fmt, I), h, rb.offsets,
-                             rb.counts, out, stream_),
-            "down");
-  phase_end();
-  count_launches(2);
+
+  float* out = nullptr;
+  int splits = 1;
+  phase_begin(kRoute);
+  UAII_CUDA(launch_route_topk(scores, probs_for_w, T, E, k, L.norm_topk, rb, stream_), "route_topk");
+  UAII_CUDA(launch_route_scan(T, E, k, rb, stream_), "route_scan");
+  if (P.umma) {
+    void* xp16 = carve(2 * (size_t)(S * D));
+    void* h16 = carve(2 * (size_t)(S * I));
+    splits = P.splits;
+    out = static_cast<float*>(carve(sizeof(float) * (size_t)(splits * S * D)));
+    UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, nullptr, xp16, stream_), "route_gather");
+    phase_end();
+    count_launches(3);
+    phase_begin(kGateUp);
+    UAII_CUDA(launch_gateup_umma(L.gate.fmt, gd, ud, E, I, D, xp16, S, rb.counts, rb.offsets, tile_base, P.bn, h16,
+                                 dev_err_, stream_),
+              "gateup(tensor cores)");
+    phase_end();
+    phase_begin(kDown);
+    UAII_CUDA(launch_down_umma(L.down.fmt, dd, E, D, I, h16, S, rb.counts, rb.offsets, tile_base, P.bn, splits, out,
+                               dev_err_, stream_),
+              "down(tensor cores)");
+    phase_end();
+    count_launches(4);
+  } else {
+    float* xp = static_cast<float*>(carve(sizeof(float) * S * D));
+    float* h = static_cast<float*>(carve(sizeof(float) * S * I));
+    out = static_cast<float*>(carve(sizeof(float) * S * D));
+    UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, xp, nullptr, stream_), "route_gather");
+    phase_end();
+    count_launches(3);
+    phase_begin(kGateUp);
+    UAII_CUDA(launch_gateup_simt(L.gate.fmt, gd, L.up.fmt, ud, E, I, D, (int64_t)row_bytes(L.gate.fmt, D),
+                                 (int64_t)row_bytes(L.up.fmt, D), xp, rb.offsets, rb.counts, h, stream_),
+              "gateup");
+    phase_end();
+    phase_begin(kDown);
+    UAII_CUDA(launch_down_simt(L.down.fmt, dd, E, D, I, (int64_t)row_bytes(L.down.fmt, I), h, rb.offsets,
+                               rb.counts, out, stream_),
+              "down");
+    phase_end();
+    count_launches(2);
+  }
 
   float* sh_out = nullptr;
   float* sh_gate = nullptr;
+  int sh_splits = 1;
   if (L.I_sh > 0) {
     const int64_t Is = L.I_sh;
     int32_t* sh_route = static_cast<int32_t*>(carve(sizeof(int32_t) * 4));
-    float* sh_h = static_cast<float*>(carve(sizeof(float) * T * Is));
-    sh_out = static_cast<float*>(carve(sizeof(float) * T * D));
+    int32_t* sh_tiles = static_cast<int32_t*>(carve(sizeof(int32_t) * 2));
     const void *sg = nullptr, *su = nullptr, *sd = nullptr;
     UAII_TRY(stage_weight(L.gate_sh.data, (size_t)Is * row_bytes(L.gate_sh.fmt, D), &sg));
     UAII_TRY(stage_weight(L.up_sh.data, (size_t)Is * row_bytes(L.up_sh.fmt, D), &su));
     UAII_TRY(stage_weight(L.down_sh.data, (size_t)D * row_bytes(L.down_sh.fmt, Is), &sd));
     phase_begin(kShared);
     UAII_CUDA(launch_identity_route(sh_route, T, stream_), "identity_route");
-    UAII_CUDA(launch_gateup_simt(L.gate_sh.fmt, sg, L.up_sh.fmt, su, 1, Is, D,
-                                 (int64_t)row_bytes(L.gate_sh.fmt, D), (int64_t)row_bytes(L.up_sh.fmt, D),
-                                 xd, sh_route, sh_route + 2, sh_h, stream_),
-              "shared_gateup");
-    UAII_CUDA(launch_down_simt(L.down_sh.fmt, sd, 1, D, Is, (int64_t)row_bytes(L.down_sh.fmt, Is), sh_h,
-                               sh_route, sh_route + 2, sh_out, stream_),
-              "shared_down");
+    if (P.sh_umma) {
+      void* x16 = carve(2 * (size_t)(T * D));
+      void* sh_h16 = carve(2 * (size_t)(T * Is));
+      sh_splits = P.sh_splits;
+      sh_out = static_cast<float*>(carve(sizeof(float) * (size_t)(sh_splits * T * D)));
+      UAII_CUDA(launch_to_f16(xd, T * D, x16, stream_), "shared_to_f16");
+      UAII_CUDA(launch_gateup_umma(L.gate_sh.fmt, sg, su, 1, Is, D, x16, T, sh_route + 2, sh_route, sh_tiles,
+                                   P.sh_bn, sh_h16, dev_err_, stream_),
+                "shared_gateup(tensor cores)");
+      UAII_CUDA(launch_down_umma(L.down_sh.fmt, sd, 1, D, Is, sh_h16, T, sh_route + 2, sh_route, sh_tiles, P.sh_bn,
+                                 sh_splits, sh_out, dev_err_, stream_),
+                "shared_down(tensor cores)");
+      count_launches(6);
+    } else {
+      float* sh_h = static_cast<float*>(carve(sizeof(float) * T * Is));
+      sh_out = static_cast<float*>(carve(sizeof(float) * T * D));
+      UAII_CUDA(launch_gateup_simt(L.gate_sh.fmt, sg, L.up_sh.fmt, su, 1, Is, D, (int64_t)row_bytes(L.gate_sh.fmt, D),
+                                   (int64_t)row_bytes(L.up_sh.fmt, D), xd, sh_route, sh_route + 2, sh_h, stream_),
+                "shared_gateup");
+      UAII_CUDA(launch_down_simt(L.down_sh.fmt, sd, 1, D, Is, (int64_t)row_bytes(L.down_sh.fmt, Is), sh_h, sh_route,
+                                 sh_route + 2, sh_out, stream_),
+                "shared_down");
+      count_launches(3);
+    }
     if (L.gate_inp_sh) {
       const void* gw = nullptr;
       UAII_TRY(stage_weight(L.gate_inp_sh, sizeof(float) * (size_t)D, &gw));
@@ -403,10 +498,10 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
       count_launches(1);
     }
     phase_end();
-    count_launches(3);
   }
   phase_begin(kCombine);
-  UAII_CUDA(launch_combine(out, D, T, D, k, rb, sh_out, sh_gate, yd, stream_), "combine");
+  UAII_CUDA(launch_combine(out, D, splits, S * D, T, D, k, rb, sh_out, sh_splits, T * D, sh_gate, yd, stream_),
+            "combine");
   phase_end();
   count_launches(1);
   return Error::success();
@@ -414,14 +509,24 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
 
 namespace {
 
-size_t experts_ws_bytes(const LayerArgs& L, int64_t T) {
+size_t experts_ws_bytes(const LayerArgs& L, int64_t T, const ExpertPlan& P) {
   const int64_t S = T * L.top_k;
   size_t b = 0;
-  b += 6 * align_up(sizeof(int32_t) * S) + align_up((size_t)(L.E * T));
-  b += 2 * align_up(sizeof(int32_t) * (L.E + 1));
-  b += 2 * align_up(sizeof(float) * S * L.D) + align_up(sizeof(float) * S * L.I);
-  if (L.I_sh > 0)
-    b += kAlign + align_up(sizeof(float) * T * L.I_sh) + 2 * align_up(sizeof(float) * T * L.D);
+  b += 5 * align_up(sizeof(int32_t) * S) + align_up((size_t)(L.E * T));
+  b += 3 * align_up(sizeof(int32_t) * (L.E + 1));
+  if (P.umma)
+    b += align_up(2 * (size_t)(S * L.D)) + align_up(2 * (size_t)(S * L.I)) +
+         align_up(sizeof(float) * (size_t)(P.splits * S * L.D));
+  else
+    b += 2 * align_up(sizeof(float) * S * L.D) + align_up(sizeof(float) * S * L.I);
+  if (L.I_sh > 0) {
+    b += 2 * kAlign + align_up(sizeof(float) * T);
+    if (P.sh_umma)
+      b += align_up(2 * (size_t)(T * L.D)) + align_up(2 * (size_t)(T * L.I_sh)) +
+           align_up(sizeof(float) * (size_t)(P.sh_splits * T * L.D));
+    else
+      b += align_up(sizeof(float) * T * L.I_sh) + align_up(sizeof(float) * T * L.D);
+  }
   return b + 16 * kAlign;
 }
 
@@ -482,7 +587,8 @@ Error MoeCudaBackend::experts(const float* x, const ExpertWeights& g, const Expe
   if (T < 0 || !x || !probs || !y) return Error::make(ErrorCode::InvalidArgument, "moe swiglu args");
   if (T == 0) return Error::success();
   const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E);
-  UAII_TRY(reserve(experts_ws_bytes(L, T) + 2 * align_up(xb) + align_up(pb) + layer_stage_bytes(L)));
+  const ExpertPlan P = plan_experts(L, T);
+  UAII_TRY(reserve(experts_ws_bytes(L, T, P) + 2 * align_up(xb) + align_up(pb) + layer_stage_bytes(L)));
   void* xs = carve(xb);
   void* ps = carve(pb);
   float* ys = static_cast<float*>(carve(xb));
@@ -493,10 +599,10 @@ Error MoeCudaBackend::experts(const float* x, const ExpertWeights& g, const Expe
   const bool yh = !is_device_ptr(y);
   float* yo = yh ? ys : y;
   UAII_TRY(run_experts(static_cast<const float*>(xd), static_cast<const float*>(pd),
-                       static_cast<const float*>(pd), L, T, yo));
+                       static_cast<const float*>(pd), L, P, T, yo));
   if (yh) {
     UAII_CUDA(cudaMemcpyAsync(y, yo, xb, cudaMemcpyDeviceToHost, stream_), "MemcpyAsync(D2H)");
-    UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+    UAII_TRY(sync_and_check());
   }
   return Error::success();
 }
@@ -514,7 +620,8 @@ Error MoeCudaBackend::ffn(const LayerArgs& Lin, const float* x, int64_t T, float
   if (T == 0) return Error::success();
   const int64_t D = L.D, E = L.E;
   const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E);
-  UAII_TRY(reserve(experts_ws_bytes(L, T) + 2 * align_up(xb) + 2 * align_up(pb) + layer_stage_bytes(L)));
+  const ExpertPlan P = plan_experts(L, T);
+  UAII_TRY(reserve(experts_ws_bytes(L, T, P) + 2 * align_up(xb) + 2 * align_up(pb) + layer_stage_bytes(L)));
   void* xs = carve(xb);
   float* ys = static_cast<float*>(carve(xb));
   float* logits = static_cast<float*>(carve(pb));
@@ -534,11 +641,11 @@ Error MoeCudaBackend::ffn(const LayerArgs& Lin, const float* x, int64_t T, float
   const bool yh = !is_device_ptr(y);
   float* yo = yh ? ys : y;
   // Rank on the exact logits (same order as the probabilities), weight with probs.
-  UAII_TRY(run_experts(static_cast<const float*>(xd), logits, po, L, T, yo));
+  UAII_TRY(run_experts(static_cast<const float*>(xd), logits, po, L, P, T, yo));
   bool any_host = false;
   if (yh) { UAII_CUDA(cudaMemcpyAsync(y, yo, xb, cudaMemcpyDeviceToHost, stream_), "D2H"); any_host = true; }
   if (ph) { UAII_CUDA(cudaMemcpyAsync(probs, po, pb, cudaMemcpyDeviceToHost, stream_), "D2H"); any_host = true; }
-  if (any_host) UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+  if (any_host) UAII_TRY(sync_and_check());
   return Error::success();
 }
 

@@ -80,6 +80,15 @@ struct LayerArgs {
   const float* gate_inp_sh = nullptr;  // [D] f32 or null
 };
 
+struct ExpertPlan {
+  bool umma = false;   // tensor-core grouped GEMM (else CUDA-core GEMV)
+  bool umma_refused = false;  // tensor cores forced but the layer does not qualify
+  int bn = 16;         // slots per tile (MMA N)
+  int splits = 1;      // K splits of the down projection
+  bool sh_umma = false;
+  int sh_bn = 16, sh_splits = 1;
+};
+
 class MoeCudaBackend {
  public:
   ~MoeCudaBackend() { shutdown(); }
@@ -120,8 +129,10 @@ class MoeCudaBackend {
   Error stage_input(const void* p, size_t bytes, void* scratch, const void** dev, bool* was_host);
   Error reserve(size_t bytes);
   void* carve(size_t bytes);
+  ExpertPlan plan_experts(const LayerArgs& L, int64_t T) const;
   Error run_experts(const float* x_dev, const float* scores, const float* probs_for_w,
-                    const LayerArgs& L, int64_t T, float* y_dev);
+                    const LayerArgs& L, const ExpertPlan& P, int64_t T, float* y_dev);
+  Error sync_and_check();
 
   // phase timing: events recorded around each phase while profiling is on
   static constexpr int kPhases = 6;
@@ -146,6 +157,7 @@ class MoeCudaBackend {
   cudaStream_t stream_ = nullptr;
   bool own_stream_ = false;
   int path_ = 0;
+  int* dev_err_ = nullptr;
   char* ws_ = nullptr;
   size_t ws_cap_ = 0;
   size_t ws_used_ = 0;

@@ -1,0 +1,674 @@
+// experts_umma.cu -- grouped expert GEMM on the 5th-generation tensor cores.
+//
+// One launch computes every (expert, weight-row tile, slot tile[, K split]) of
+// one projection:  C[row, slot] = sum_k W_e[row, k] * X[slot, k]  with the
+// weight rows as the MMA M dimension (128) and the expert's routed slots as N
+// (16..256), so a decode step with one token per expert still fills the
+// M = 128 tensor-core tile.
+//
+// Per CTA (persistent, one per SM, 6 warps):
+//   warp 0   TMA producer: packed GGUF weight windows (2-D uint8 tensor map,
+//            row pitch = packed row bytes, window start rounded down to 16 B)
+//            and f16 activation tiles (SWIZZLE_128B) into shared-memory rings;
+//   warp 1   TMEM allocation and the single MMA-issuing thread
+//            (tcgen05.mma kind::f16, A and B from shared memory, D in TMEM);
+//   warps 2-5 dequantize the packed window of their row into the f16 A tile
+//            (K-major, SWIZZLE_128B canonical layout), then run the epilogue
+//            from TMEM: SwiGLU for gate/up (rows 0-63 gate, 64-127 up of the
+//            same 64 features) writing h in f16, or f32 partial sums for down.
+// The weights are never repacked: blocks stay byte-identical to GGUF.  Each
+// dequantized operand is the GGUF value in f16: Q4_0 and Q8_0 exactly
+// fp16(round(d*q)); K-quants scale by fp16(d*sc), fp16(dmin*m).
+//
+// Every mbarrier wait is bounded: on timeout the CTA records an error code in
+// *err, waits (bounded) for its own copies and MMAs in flight, frees TMEM and
+// exits.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include "gguf_blocks.cuh"
+#include "kernels.hpp"
+#include "umma.cuh"
+
+namespace uaii_b200 {
+namespace {
+
+using namespace umma;
+
+// K chunk per packed-window load: one K-quant super-block (256) or two
+// 32-element blocks (64).  kBytes = packed bytes of one chunk of one row.
+template <int F> struct Fmt;
+template <> struct Fmt<kQ4_0> { static constexpr int kChunk = 64, kAtoms = 1, kBytes = 36; };
+template <> struct Fmt<kQ8_0> { static constexpr int kChunk = 64, kAtoms = 1, kBytes = 68; };
+template <> struct Fmt<kQ4_K> { static constexpr int kChunk = 256, kAtoms = 4, kBytes = 144; };
+template <> struct Fmt<kQ6_K> { static constexpr int kChunk = 256, kAtoms = 4, kBytes = 210; };
+
+// Bytes of the 16-byte-aligned window that holds any chunk of a row.
+__host__ __device__ constexpr int window_bytes(int bytes) {
+  int w = 0;
+  for (int c = 0; c < 16; ++c) {
+    const int x = ((((c * bytes) & 15) + bytes) + 15) & ~15;
+    w = x > w ? x : w;
+  }
+  return w;
+}
+
+constexpr int kThreads = 192;
+constexpr int kAtomBytes = 128 * 128;  // 128 rows x 64 f16
+
+enum : int { kErrTimeoutProducer = 1, kErrTimeoutMma = 2, kErrTimeoutDequant = 3, kErrTimeoutEpilogue = 4 };
+
+struct Args {
+  const int32_t* counts;
+  const int32_t* offsets;
+  const int32_t* tile_base;  // [E+1]
+  int E, m_tiles, splits, kchunks, rows_per_expert, gateup;
+  __half* h_out;  // gate/up: [S, out_ld] f16
+  float* out;     // down: [splits][S][out_ld] f32
+  int64_t out_ld, split_stride;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t ld32_a2(const uint8_t* p) {  // p is 2-byte aligned
+  const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
+  return (uint32_t)q[0] | ((uint32_t)q[1] << 16);
+}
+__device__ __forceinline__ __half2 as_h2(uint32_t v) {
+  __half2 h;
+  memcpy(&h, &v, 4);
+  return h;
+}
+__device__ __forceinline__ uint32_t as_u32(__half2 h) {
+  uint32_t v;
+  memcpy(&v, &h, 4);
+  return v;
+}
+// bytes (0,1) and (2,3) of w spread to the two halves of a 32-bit word
+__device__ __forceinline__ uint32_t spread01(uint32_t w) { return __byte_perm(w, 0, 0x4140); }
+__device__ __forceinline__ uint32_t spread23(uint32_t w) { return __byte_perm(w, 0, 0x4342); }
+// small integers v (< 1024) in each 16-bit half -> f16 (1024 + v)
+__device__ __forceinline__ __half2 magic(uint32_t v) { return as_h2(v | 0x64006400u); }
+
+// Dequantize 64 elements (one MMA K atom) of one row into eight 16-byte
+// chunks of 8 f16 each.  `blk` points at the row's chunk inside the window.
+template <int F>
+__device__ __forceinline__ void dequant_atom(const uint8_t* blk, int atom, uint4 (&o)[8]);
+
+template <>
+__device__ __forceinline__ void dequant_atom<kQ4_0>(const uint8_t* blk, int, uint4 (&o)[8]) {
+  const __half2 bias = __float2half2_rn(1032.f);  // 1024 + 8
+#pragma unroll
+  for (int b = 0; b < 2; ++b) {
+    const uint8_t* bb = blk + 18 * b;
+    const __half dh = __ushort_as_half((unsigned short)ld_u16(bb));
+    const __half2 d = __halves2half2(dh, dh);
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = ld32_a2(bb + 2 + 4 * i);
+#pragma unroll
+    for (int hi = 0; hi < 2; ++hi) {
+#pragma unroll
+      for (int half8 = 0; half8 < 2; ++half8) {
+        uint32_t r[4];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const uint32_t ww = w[2 * half8 + j];
+          const uint32_t a = hi ? (spread01(ww) >> 4) : spread01(ww);
+          const uint32_t c = hi ? (spread23(ww) >> 4) : spread23(ww);
+          r[2 * j] = as_u32(__hmul2(__hsub2(magic(a & 0x000F000Fu), bias), d));
+          r[2 * j + 1] = as_u32(__hmul2(__hsub2(magic(c & 0x000F000Fu), bias), d));
+        }
+        o[4 * b + 2 * hi + half8] = make_uint4(r[0], r[1], r[2], r[3]);
+      }
+    }
+  }
+}
+
+template <>
+__device__ __forceinline__ void dequant_atom<kQ8_0>(const uint8_t* blk, int, uint4 (&o)[8]) {
+  const __half2 bias = __float2half2_rn(1152.f);  // 1024 + 128
+#pragma unroll
+  for (int b = 0; b < 2; ++b) {
+    const uint8_t* bb = blk + 34 * b;
+    const __half dh = __ushort_as_half((unsigned short)ld_u16(bb));
+    const __half2 d = __halves2half2(dh, dh);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t r[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t ww = ld32_a2(bb + 2 + 8 * c + 4 * j) ^ 0x80808080u;  // int8 -> q + 128
+        r[2 * j] = as_u32(__hmul2(__hsub2(magic(spread01(ww)), bias), d));
+        r[2 * j + 1] = as_u32(__hmul2(__hsub2(magic(spread23(ww)), bias), d));
+      }
+      o[4 * b + c] = make_uint4(r[0], r[1], r[2], r[3]);
+    }
+  }
+}
+
+template <>
+__device__ __forceinline__ void dequant_atom<kQ4_K>(const uint8_t* blk, int atom, uint4 (&o)[8]) {
+  const float d = f16_bits_to_f32(ld_u16(blk));
+  const float dmin = f16_bits_to_f32(ld_u16(blk + 2));
+  int sc0, m0, sc1, m1;
+  k4_scale_min(2 * atom, blk + 4, sc0, m0);
+  k4_scale_min(2 * atom + 1, blk + 4, sc1, m1);
+  const __half2 d0 = __float2half2_rn(d * (float)sc0), n0 = __float2half2_rn(-(dmin * (float)m0));
+  const __half2 d1 = __float2half2_rn(d * (float)sc1), n1 = __float2half2_rn(-(dmin * (float)m1));
+  const __half2 k1024 = __float2half2_rn(1024.f);
+  const uint4* q = reinterpret_cast<const uint4*>(blk + 16 + 32 * atom);
+  const uint4 qa = q[0], qb = q[1];
+  const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+  for (int hi = 0; hi < 2; ++hi) {
+    const __half2 dd = hi ? d1 : d0, nn = hi ? n1 : n0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t r[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t ww = w[2 * c + j];
+        const uint32_t a = hi ? (spread01(ww) >> 4) : spread01(ww);
+        const uint32_t b = hi ? (spread23(ww) >> 4) : spread23(ww);
+        r[2 * j] = as_u32(__hfma2(__hsub2(magic(a & 0x000F000Fu), k1024), dd, nn));
+        r[2 * j + 1] = as_u32(__hfma2(__hsub2(magic(b & 0x000F000Fu), k1024), dd, nn));
+      }
+      o[4 * hi + c] = make_uint4(r[0], r[1], r[2], r[3]);
+    }
+  }
+}
+
+template <>
+__device__ __forceinline__ void dequant_atom<kQ6_K>(const uint8_t* blk, int atom, uint4 (&o)[8]) {
+  const int n = atom >> 1, hiq = atom & 1;
+  const uint8_t* ql = blk + 64 * n;
+  const uint8_t* qh = blk + 128 + 32 * n;
+  const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * n);
+  const float d = f16_bits_to_f32(ld_u16(blk + 208));
+  const __half2 bias = __float2half2_rn(1056.f);  // 1024 + 32
+  const int ns = hiq ? 4 : 0;
+#pragma unroll
+  for (int qq = 0; qq < 2; ++qq) {
+    const int qt = 2 * hiq + qq;
+    const __half2 s_lo = __float2half2_rn(d * (float)sc[2 * qt]);
+    const __half2 s_hi = __float2half2_rn(d * (float)sc[2 * qt + 1]);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t r[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t lw = ld32_a2(ql + 32 * qq + 8 * c + 4 * j);
+        const uint32_t hw = ld32_a2(qh + 8 * c + 4 * j);
+        const uint32_t q6 = ((lw >> ns) & 0x0F0F0F0Fu) | (((hw >> (2 * qt)) & 0x03030303u) << 4);
+        const __half2 s = c < 2 ? s_lo : s_hi;
+        r[2 * j] = as_u32(__hmul2(__hsub2(magic(spread01(q6)), bias), s));
+        r[2 * j + 1] = as_u32(__hmul2(__hsub2(magic(spread23(q6)), bias), s));
+      }
+      o[4 * qq + c] = make_uint4(r[0], r[1], r[2], r[3]);
+    }
+  }
+}
+
+struct Tile {
+  int e, m_tile, n_tile, split;
+};
+
+__device__ __forceinline__ Tile decode_tile(const Args& a, int tile, int bn) {
+  int lo = 0, hi = a.E;  // largest e with tile_base[e] <= tile (always a non-empty expert)
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(a.tile_base + mid) <= tile) lo = mid; else hi = mid;
+  }
+  Tile t;
+  t.e = lo;
+  int local = tile - __ldg(a.tile_base + lo);
+  t.split = local % a.splits;
+  local /= a.splits;
+  const int nt = (__ldg(a.counts + lo) + bn - 1) / bn;
+  t.n_tile = local % nt;
+  t.m_tile = local / nt;
+  return t;
+}
+
+// Wait with abort: false when another role aborted or the clock budget ran out.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort = 1;
+      atomicExch(err, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+template <int F, int BN, int A_ST, int B_ST, int P_ST>
+struct Cfg {
+  static constexpr int kWB = window_bytes(Fmt<F>::kBytes);
+  static constexpr int kPStage = 128 * kWB;
+  static constexpr int kBStage = BN * 128;
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kOffA + A_ST * kAtomBytes;
+  static constexpr int kOffP = kOffB + B_ST * kBStage;
+  static constexpr int kOffX = kOffP + P_ST * kPStage;       // 64 x 17 f32 exchange tile
+  static constexpr int kOffBar = kOffX + 64 * 17 * 4;
+  static constexpr int kNumBars = 2 * (P_ST + A_ST + B_ST) + 4 + 1;
+  static constexpr int kSmem = kOffBar + kNumBars * 8 + 16 + 1024;  // + alignment slack
+  static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+};
+
+template <int F, int BN, int A_ST, int B_ST, int P_ST>
+__global__ void __launch_bounds__(kThreads, 1)
+    expert_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
+                       const __grid_constant__ CUtensorMap tm_x, const Args args) {
+  using C = Cfg<F, BN, A_ST, B_ST, P_ST>;
+  constexpr int kAtoms = Fmt<F>::kAtoms;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem + C::kOffA;
+  uint8_t* sB = smem + C::kOffB;
+  uint8_t* sP = smem + C::kOffP;
+  float* sX = reinterpret_cast<float*>(smem + C::kOffX);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* pk_full = bars;
+  uint64_t* pk_empty = pk_full + P_ST;
+  uint64_t* a_full = pk_empty + P_ST;
+  uint64_t* a_empty = a_full + A_ST;
+  uint64_t* b_full = a_empty + A_ST;
+  uint64_t* b_empty = b_full + B_ST;
+  uint64_t* acc_full = b_empty + B_ST;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* x_full = acc_empty + 1;
+  uint64_t* x_empty = x_full + 1;
+  uint64_t* mma_done = x_empty + 1;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < P_ST; ++i) { mbar_init(pk_full + i, 1); mbar_init(pk_empty + i, 128); }
+    for (int i = 0; i < A_ST; ++i) { mbar_init(a_full + i, 128); mbar_init(a_empty + i, 1); }
+    for (int i = 0; i < B_ST; ++i) { mbar_init(b_full + i, 1); mbar_init(b_empty + i, 1); }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 128);
+    mbar_init(x_full, 64);
+    mbar_init(x_empty, 64);
+    mbar_init(mma_done, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_w0);
+    prefetch_tmap(&tm_w1);
+    prefetch_tmap(&tm_x);
+  }
+  if (warp == 1) tmem_alloc(s_tmem, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  const int total = __ldg(args.tile_base + args.E);
+  int* err = args.err;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t pi = 0, bi = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const Tile t = decode_tile(args, tile, BN);
+        const int row0 = t.e * args.rows_per_expert + t.m_tile * (args.gateup ? 64 : 128);
+        const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
+        const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
+        for (int c = c0; c < c1 && ok; ++c) {
+          const int ps = pi % P_ST;
+          if (!(ok = wait_bar(pk_empty + ps, ((pi / P_ST) & 1) ^ 1, s_abort, err, kErrTimeoutProducer))) break;
+          mbar_arrive_expect_tx(pk_full + ps, C::kPStage);
+          const int x = (c * Fmt<F>::kBytes) & ~15;
+          uint8_t* dst = sP + ps * C::kPStage;
+          if (args.gateup) {
+            tma_load_2d(dst, &tm_w0, pk_full + ps, x, row0);
+            tma_load_2d(dst + 64 * C::kWB, &tm_w1, pk_full + ps, x, row0);
+          } else {
+            tma_load_2d(dst, &tm_w0, pk_full + ps, x, row0);
+            tma_load_2d(dst + 64 * C::kWB, &tm_w0, pk_full + ps, x, row0 + 64);
+          }
+          ++pi;
+          for (int at = 0; at < kAtoms && ok; ++at) {
+            const int bs = bi % B_ST;
+            if (!(ok = wait_bar(b_empty + bs, ((bi / B_ST) & 1) ^ 1, s_abort, err, kErrTimeoutProducer))) break;
+            mbar_arrive_expect_tx(b_full + bs, C::kBStage);
+            tma_load_2d(sB + bs * C::kBStage, &tm_x, b_full + bs, c * Fmt<F>::kChunk + at * 64, slot0);
+            ++bi;
+          }
+        }
+      }
+      // never leave with copies in flight: wait (bounded) for the last load of every stage
+      for (uint32_t j = (pi > (uint32_t)P_ST ? pi - P_ST : 0); j < pi; ++j)
+        (void)mbar_wait(pk_full + j % P_ST, (j / P_ST) & 1);
+      for (uint32_t j = (bi > (uint32_t)B_ST ? bi - B_ST : 0); j < bi; ++j)
+        (void)mbar_wait(b_full + j % B_ST, (j / B_ST) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, BN);
+      uint32_t ai = 0, bi = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
+        const Tile t = decode_tile(args, tile, BN);
+        const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
+        if (!(ok = wait_bar(acc_empty, (it & 1) ^ 1, s_abort, err, kErrTimeoutMma))) break;
+        tc_fence_after();
+        uint32_t acc = 0;
+        for (int c = c0; c < c1 && ok; ++c) {
+          for (int at = 0; at < kAtoms; ++at) {
+            const int as = ai % A_ST, bs = bi % B_ST;
+            if (!(ok = wait_bar(a_full + as, (ai / A_ST) & 1, s_abort, err, kErrTimeoutMma))) break;
+            if (!(ok = wait_bar(b_full + bs, (bi / B_ST) & 1, s_abort, err, kErrTimeoutMma))) break;
+            tc_fence_after();
+            const uint64_t ad = sw128_desc(smem_u32(sA + as * kAtomBytes));
+            const uint64_t bd = sw128_desc(smem_u32(sB + bs * C::kBStage));
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              mma_f16(tmem, ad + 2 * ks, bd + 2 * ks, idesc, acc);
+              acc = 1;
+            }
+            mma_commit(a_empty + as);
+            mma_commit(b_empty + bs);
+            ++ai;
+            ++bi;
+          }
+        }
+        if (ok) mma_commit(acc_full);
+      }
+      // the tensor core must be idle before TMEM is freed
+      mma_commit(mma_done);
+      (void)mbar_wait(mma_done, 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ dequant + epilogue (128 threads)
+    const int q = warp & 3;            // TMEM lane quarter this warp may access
+    const int row = 32 * q + lane;     // A-tile row == accumulator lane
+    uint32_t pi = 0, ai = 0, it = 0, xi = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
+      const Tile t = decode_tile(args, tile, BN);
+      const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
+      for (int c = c0; c < c1 && ok; ++c) {
+        const int ps = pi % P_ST;
+        if (!(ok = wait_bar(pk_full + ps, (pi / P_ST) & 1, s_abort, err, kErrTimeoutDequant))) break;
+        const uint8_t* blk = sP + ps * C::kPStage + row * C::kWB + ((c * Fmt<F>::kBytes) & 15);
+        for (int at = 0; at < kAtoms && ok; ++at) {
+          const int as = ai % A_ST;
+          if (!(ok = wait_bar(a_empty + as, ((ai / A_ST) & 1) ^ 1, s_abort, err, kErrTimeoutDequant))) break;
+          uint4 o[8];
+          dequant_atom<F>(blk, at, o);
+          uint8_t* arow = sA + as * kAtomBytes + row * 128;
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) *reinterpret_cast<uint4*>(arow + ((cc ^ (row & 7)) << 4)) = o[cc];
+          fence_proxy_async_smem();
+          mbar_arrive(a_full + as);
+          ++ai;
+        }
+        mbar_arrive(pk_empty + ps);
+        ++pi;
+      }
+      if (!ok) break;
+      // ---- epilogue
+      if (!(ok = wait_bar(acc_full, it & 1, s_abort, err, kErrTimeoutEpilogue))) break;
+      tc_fence_after();
+      const int n_valid = min(BN, __ldg(args.counts + t.e) - t.n_tile * BN);
+      const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
+      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
+      if (args.gateup) {
+        const int i0 = t.m_tile * 64;
+        for (int cb = 0; cb < BN / 16 && ok; ++cb) {
+          uint32_t r[16];
+          tmem_ld16(taddr + cb * 16, r);
+          tmem_ld_wait();
+          if (q >= 2) {  // up rows: hand the values to the gate thread of the same feature
+            if (!(ok = wait_bar(x_empty, (xi & 1) ^ 1, s_abort, err, kErrTimeoutEpilogue))) break;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) sX[(row - 64) * 17 + j] = __uint_as_float(r[j]);
+            mbar_arrive(x_full);
+          } else {
+            if (!(ok = wait_bar(x_full, xi & 1, s_abort, err, kErrTimeoutEpilogue))) break;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int n = cb * 16 + j;
+              const float g = __uint_as_float(r[j]);
+              const float u = sX[row * 17 + j];
+              const float sig = 1.0f / (1.0f + __expf(-g));
+              if (n < n_valid)
+                args.h_out[(int64_t)(slot0 + n) * args.out_ld + i0 + row] = __float2half_rn((g * sig) * u);
+            }
+            mbar_arrive(x_empty);
+          }
+          ++xi;
+        }
+      } else {
+        const int o0 = t.m_tile * 128;
+        float* out = args.out + (int64_t)t.split * args.split_stride;
+        for (int cb = 0; cb < BN / 16; ++cb) {
+          uint32_t r[16];
+          tmem_ld16(taddr + cb * 16, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int n = cb * 16 + j;
+            if (n < n_valid) out[(int64_t)(slot0 + n) * args.out_ld + o0 + row] = __uint_as_float(r[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+__global__ void tile_table_kernel(const int32_t* counts, int E, int bn, int m_tiles, int splits,
+                                  int32_t* tile_base) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int run = 0;
+  for (int e = 0; e < E; ++e) {
+    tile_base[e] = run;
+    run += ((counts[e] + bn - 1) / bn) * m_tiles * splits;
+  }
+  tile_base[E] = run;
+}
+
+// ---- host side ----------------------------------------------------------
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                 CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                 CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static EncodeTiled fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  }
+  return fn;
+}
+
+// packed weights: [rows_total, pitch] bytes, box = window x 64 rows
+bool make_weight_map(CUtensorMap* m, const void* base, int64_t pitch, int64_t rows_total, int window) {
+  EncodeTiled enc = encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)pitch, (cuuint64_t)rows_total};
+  const cuuint64_t strides[1] = {(cuuint64_t)pitch};
+  const cuuint32_t box[2] = {(cuuint32_t)window, 64};
+  const cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// f16 activations: [rows, K], box = 64 x bn, SWIZZLE_128B
+bool make_act_map(CUtensorMap* m, const void* base, int64_t K, int64_t rows, int bn) {
+  EncodeTiled enc = encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
+  const cuuint32_t box[2] = {64, (cuuint32_t)bn};
+  const cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int F, int BN, int A_ST, int B_ST, int P_ST>
+cudaError_t run_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x, const Args& a,
+                     cudaStream_t st) {
+  using C = Cfg<F, BN, A_ST, B_ST, P_ST>;
+  static_assert(C::kSmem <= 227 * 1024, "shared memory budget");
+  auto kern = expert_gemm_kernel<F, BN, A_ST, B_ST, P_ST>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  kern<<<num_sms(), kThreads, C::kSmem, st>>>(w0, w1, x, a);
+  return cudaGetLastError();
+}
+
+template <int F>
+cudaError_t dispatch_bn(int bn, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
+                        const Args& a, cudaStream_t st) {
+  switch (bn) {
+    case 16: return run_gemm<F, 16, 4, 4, 4>(w0, w1, x, a, st);
+    case 32: return run_gemm<F, 32, 4, 4, 4>(w0, w1, x, a, st);
+    case 64: return run_gemm<F, 64, 4, 4, 3>(w0, w1, x, a, st);
+    case 128: return run_gemm<F, 128, 4, 4, 2>(w0, w1, x, a, st);
+    case 256: return run_gemm<F, 256, 3, 3, 2>(w0, w1, x, a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+int chunk_elems(int fmt) {
+  switch (fmt) {
+    case kQ4_0: return Fmt<kQ4_0>::kChunk;
+    case kQ8_0: return Fmt<kQ8_0>::kChunk;
+    case kQ4_K: return Fmt<kQ4_K>::kChunk;
+    case kQ6_K: return Fmt<kQ6_K>::kChunk;
+    default: return 0;
+  }
+}
+int chunk_bytes(int fmt) {
+  switch (fmt) {
+    case kQ4_0: return Fmt<kQ4_0>::kBytes;
+    case kQ8_0: return Fmt<kQ8_0>::kBytes;
+    case kQ4_K: return Fmt<kQ4_K>::kBytes;
+    case kQ6_K: return Fmt<kQ6_K>::kBytes;
+    default: return 0;
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+cudaError_t launch_common(int fmt, bool gateup, const void* W0, const void* W1, int64_t E, int64_t rows,
+                          int64_t K, const void* act16, int64_t S_rows, const int32_t* counts,
+                          const int32_t* offsets, int32_t* tile_base, int bn, int splits, void* h16,
+                          float* out, int64_t out_ld, int64_t split_stride, int* err, cudaStream_t st) {
+  const int ce = chunk_elems(fmt);
+  if (!ce || K % ce != 0) return cudaErrorNotSupported;
+  const int64_t pitch = fmt_row_bytes(fmt, K);
+  const int m_rows = gateup ? 64 : 128;
+  if (rows % m_rows != 0 || pitch % 16 != 0) return cudaErrorNotSupported;
+  if (!aligned16(W0) || !aligned16(W1) || !aligned16(act16) || K % 8 != 0) return cudaErrorNotSupported;
+  const int kchunks = (int)(K / ce);
+  if (splits < 1) splits = 1;
+  if (splits > kchunks) splits = kchunks;
+  const int window = window_bytes(chunk_bytes(fmt));
+  CUtensorMap m0, m1, mx;
+  if (!make_weight_map(&m0, W0, pitch, E * rows, window) || !make_weight_map(&m1, W1, pitch, E * rows, window) ||
+      !make_act_map(&mx, act16, K, S_rows, bn))
+    return cudaErrorNotSupported;
+  const int m_tiles = (int)(rows / m_rows);
+  tile_table_kernel<<<1, 32, 0, st>>>(counts, (int)E, bn, m_tiles, splits, tile_base);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  Args a{};
+  a.counts = counts;
+  a.offsets = offsets;
+  a.tile_base = tile_base;
+  a.E = (int)E;
+  a.m_tiles = m_tiles;
+  a.splits = splits;
+  a.kchunks = kchunks;
+  a.rows_per_expert = (int)rows;
+  a.gateup = gateup ? 1 : 0;
+  a.h_out = static_cast<__half*>(h16);
+  a.out = out;
+  a.out_ld = out_ld;
+  a.split_stride = split_stride;
+  a.err = err;
+  switch (fmt) {
+    case kQ4_0: return dispatch_bn<kQ4_0>(bn, m0, m1, mx, a, st);
+    case kQ8_0: return dispatch_bn<kQ8_0>(bn, m0, m1, mx, a, st);
+    case kQ4_K: return dispatch_bn<kQ4_K>(bn, m0, m1, mx, a, st);
+    case kQ6_K: return dispatch_bn<kQ6_K>(bn, m0, m1, mx, a, st);
+    default: return cudaErrorNotSupported;
+  }
+}
+
+}  // namespace
+
+bool umma_format_supported(int fmt) { return chunk_elems(fmt) != 0; }
+
+bool umma_shapes_supported(int gfmt, int dfmt, int64_t D, int64_t I) {
+  if (!umma_format_supported(gfmt) || !umma_format_supported(dfmt)) return false;
+  if (D % chunk_elems(gfmt) || I % chunk_elems(dfmt) || I % 64 || D % 128) return false;
+  return fmt_row_bytes(gfmt, D) % 16 == 0 && fmt_row_bytes(dfmt, I) % 16 == 0 && D % 8 == 0 && I % 8 == 0;
+}
+
+cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t E, int64_t I, int64_t D,
+                               const void* xp16, int64_t S_rows, const int32_t* counts, const int32_t* offsets,
+                               int32_t* tile_base, int bn, void* h16, int* err, cudaStream_t st) {
+  return launch_common(fmt, true, G, U, E, I, D, xp16, S_rows, counts, offsets, tile_base, bn, 1, h16, nullptr,
+                       I, 0, err, st);
+}
+
+cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t E, int64_t D, int64_t I, const void* h16,
+                             int64_t S_rows, const int32_t* counts, const int32_t* offsets, int32_t* tile_base,
+                             int bn, int splits, float* out, int* err, cudaStream_t st) {
+  return launch_common(fmt, false, Dn, Dn, E, D, I, h16, S_rows, counts, offsets, tile_base, bn, splits, nullptr,
+                       out, D, S_rows * D, err, st);
+}
+
+int umma_kchunks(int fmt, int64_t K) {
+  const int ce = chunk_elems(fmt);
+  return ce ? (int)(K / ce) : 0;
+}
+
+}  // namespace uaii_b200

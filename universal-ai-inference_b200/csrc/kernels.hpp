@@ -42,8 +42,11 @@ cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E,
                                 cudaStream_t st);
 // y[t] = sum_r w[t,r] * out[slot_of[t,r]] (rank order, from 0), then
 // y[t] += gate[t] * shared_out[t] when shared_out is given (gate may be null = 1).
-cudaError_t launch_combine(const float* out, int64_t out_ld, int64_t T, int64_t D, int k,
-                           const RouteBuffers& rb, const float* shared_out,
+// `out` (and `shared_out`) may hold `splits` partial planes `split_stride`
+// elements apart; the planes are added in order before weighting.
+cudaError_t launch_combine(const float* out, int64_t out_ld, int splits, int64_t split_stride,
+                           int64_t T, int64_t D, int k, const RouteBuffers& rb,
+                           const float* shared_out, int sh_splits, int64_t sh_split_stride,
                            const float* shared_gate, float* y, cudaStream_t st);
 // x rows -> f16 copy (shared-expert operand in token order)
 cudaError_t launch_to_f16(const float* x, int64_t n, void* out, cudaStream_t st);
@@ -61,5 +64,21 @@ cudaError_t launch_gateup_simt(int gfmt, const void* G, int ufmt, const void* U,
 cudaError_t launch_down_simt(int dfmt, const void* Dn, int64_t E, int64_t D, int64_t I,
                              int64_t d_pitch, const float* h, const int32_t* offsets,
                              const int32_t* counts, float* out, cudaStream_t st);
+
+// ---- experts_umma.cu: tensor-core grouped GEMM (tcgen05 + TMEM + TMA)
+bool umma_format_supported(int fmt);
+// whole-layer check: formats, K chunking, 16-byte row pitches, tile multiples
+bool umma_shapes_supported(int gate_fmt, int down_fmt, int64_t D, int64_t I);
+int umma_kchunks(int fmt, int64_t K);
+// h16[slot, i] = silu(x.G[e,i]) * (x.U[e,i]) in f16; x is xp16 [S_rows, D] f16.
+// tile_base: scratch of E+1 ints.  *err receives a nonzero code if a wait timed out.
+cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t E, int64_t I, int64_t D,
+                               const void* xp16, int64_t S_rows, const int32_t* counts,
+                               const int32_t* offsets, int32_t* tile_base, int bn, void* h16, int* err,
+                               cudaStream_t st);
+// out[split][slot, o] = partial of h16[slot] . Dn[e, o] over the split's K range (f32).
+cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t E, int64_t D, int64_t I, const void* h16,
+                             int64_t S_rows, const int32_t* counts, const int32_t* offsets,
+                             int32_t* tile_base, int bn, int splits, float* out, int* err, cudaStream_t st);
 
 }  // namespace uaii_b200

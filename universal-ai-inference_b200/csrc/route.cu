@@ -163,9 +163,22 @@ __global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int6
   }
 }
 
-__global__ void combine_kernel(const float* __restrict__ out, int64_t ld, int64_t T, int64_t D,
-                               int k, RouteBuffers rb, const float* __restrict__ sh,
-                               const float* __restrict__ gate, float* __restrict__ y) {
+__device__ __forceinline__ float4 sum_planes(const float* base, int64_t off4, int splits, int64_t stride) {
+  float4 o = reinterpret_cast<const float4*>(base)[off4];
+  for (int s = 1; s < splits; ++s) {
+    const float4 p = reinterpret_cast<const float4*>(base + s * stride)[off4];
+    o.x = __fadd_rn(o.x, p.x);
+    o.y = __fadd_rn(o.y, p.y);
+    o.z = __fadd_rn(o.z, p.z);
+    o.w = __fadd_rn(o.w, p.w);
+  }
+  return o;
+}
+
+__global__ void combine_kernel(const float* __restrict__ out, int64_t ld, int splits, int64_t stride,
+                               int64_t T, int64_t D, int k, RouteBuffers rb, const float* __restrict__ sh,
+                               int sh_splits, int64_t sh_stride, const float* __restrict__ gate,
+                               float* __restrict__ y) {
   const int64_t d4 = D / 4;
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= T * d4) return;
@@ -174,7 +187,7 @@ __global__ void combine_kernel(const float* __restrict__ out, int64_t ld, int64_
   for (int r = 0; r < k; ++r) {
     const int slot = rb.slot_of[t * k + r];
     const float w = rb.topk_w[t * k + r];
-    const float4 o = reinterpret_cast<const float4*>(out + (int64_t)slot * ld)[c];
+    const float4 o = sum_planes(out, ((int64_t)slot * ld) / 4 + c, splits, stride);
     acc.x = __fadd_rn(acc.x, __fmul_rn(w, o.x));
     acc.y = __fadd_rn(acc.y, __fmul_rn(w, o.y));
     acc.z = __fadd_rn(acc.z, __fmul_rn(w, o.z));
@@ -182,7 +195,7 @@ __global__ void combine_kernel(const float* __restrict__ out, int64_t ld, int64_
   }
   if (sh) {
     const float g = gate ? gate[t] : 1.0f;
-    const float4 s = reinterpret_cast<const float4*>(sh + t * D)[c];
+    const float4 s = sum_planes(sh, t * d4 + c, sh_splits, sh_stride);
     acc.x = __fadd_rn(acc.x, __fmul_rn(g, s.x));
     acc.y = __fadd_rn(acc.y, __fmul_rn(g, s.y));
     acc.z = __fadd_rn(acc.z, __fmul_rn(g, s.z));
@@ -191,16 +204,25 @@ __global__ void combine_kernel(const float* __restrict__ out, int64_t ld, int64_
   reinterpret_cast<float4*>(y + t * D)[c] = acc;
 }
 
-__global__ void combine1_kernel(const float* __restrict__ out, int64_t ld, int64_t T, int64_t D,
-                                int k, RouteBuffers rb, const float* __restrict__ sh,
-                                const float* __restrict__ gate, float* __restrict__ y) {
+__global__ void combine1_kernel(const float* __restrict__ out, int64_t ld, int splits, int64_t stride,
+                                int64_t T, int64_t D, int k, RouteBuffers rb, const float* __restrict__ sh,
+                                int sh_splits, int64_t sh_stride, const float* __restrict__ gate,
+                                float* __restrict__ y) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= T * D) return;
   const int64_t t = i / D, c = i - t * D;
   float acc = 0.f;
-  for (int r = 0; r < k; ++r)
-    acc = __fadd_rn(acc, __fmul_rn(rb.topk_w[t * k + r], out[(int64_t)rb.slot_of[t * k + r] * ld + c]));
-  if (sh) acc = __fadd_rn(acc, __fmul_rn(gate ? gate[t] : 1.0f, sh[t * D + c]));
+  for (int r = 0; r < k; ++r) {
+    const int64_t at = (int64_t)rb.slot_of[t * k + r] * ld + c;
+    float o = out[at];
+    for (int s = 1; s < splits; ++s) o = __fadd_rn(o, out[at + s * stride]);
+    acc = __fadd_rn(acc, __fmul_rn(rb.topk_w[t * k + r], o));
+  }
+  if (sh) {
+    float o = sh[t * D + c];
+    for (int s = 1; s < sh_splits; ++s) o = __fadd_rn(o, sh[t * D + c + s * sh_stride]);
+    acc = __fadd_rn(acc, __fmul_rn(gate ? gate[t] : 1.0f, o));
+  }
   y[i] = acc;
 }
 
@@ -265,18 +287,23 @@ cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E,
   return cudaGetLastError();
 }
 
-cudaError_t launch_combine(const float* out, int64_t out_ld, int64_t T, int64_t D, int k,
-                           const RouteBuffers& rb, const float* shared_out,
+cudaError_t launch_combine(const float* out, int64_t out_ld, int splits, int64_t split_stride,
+                           int64_t T, int64_t D, int k, const RouteBuffers& rb,
+                           const float* shared_out, int sh_splits, int64_t sh_split_stride,
                            const float* shared_gate, float* y, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  if (D % 4 != 0 || out_ld % 4 != 0) {
-    combine1_kernel<<<(unsigned)((T * D + 255) / 256), 256, 0, st>>>(out, out_ld, T, D, k, rb, shared_out,
+  if (splits < 1) splits = 1;
+  if (sh_splits < 1) sh_splits = 1;
+  if (D % 4 != 0 || out_ld % 4 != 0 || split_stride % 4 != 0 || sh_split_stride % 4 != 0) {
+    combine1_kernel<<<(unsigned)((T * D + 255) / 256), 256, 0, st>>>(out, out_ld, splits, split_stride, T, D, k,
+                                                                     rb, shared_out, sh_splits, sh_split_stride,
                                                                      shared_gate, y);
     return cudaGetLastError();
   }
   const int64_t n = T * (D / 4);
-  combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(out, out_ld, T, D, k, rb,
-                                                              shared_out, shared_gate, y);
+  combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(out, out_ld, splits, split_stride, T, D, k, rb,
+                                                              shared_out, sh_splits, sh_split_stride,
+                                                              shared_gate, y);
   return cudaGetLastError();
 }
 
