@@ -6,16 +6,19 @@
 // (16..256), so a decode step with one token per expert still fills the
 // M = 128 tensor-core tile.
 //
-// Per CTA (persistent, one per SM, 6 warps):
+// Per CTA (persistent, one per SM, 10 warps):
 //   warp 0   TMA producer: packed GGUF weight windows (2-D uint8 tensor map,
 //            row pitch = packed row bytes, window start rounded down to 16 B)
 //            and f16 activation tiles (SWIZZLE_128B) into shared-memory rings;
 //   warp 1   TMEM allocation and the single MMA-issuing thread
 //            (tcgen05.mma kind::f16, A and B from shared memory, D in TMEM);
-//   warps 2-5 dequantize the packed window of their row into the f16 A tile
-//            (K-major, SWIZZLE_128B canonical layout), then run the epilogue
-//            from TMEM: SwiGLU for gate/up (rows 0-63 gate, 64-127 up of the
-//            same 64 features) writing h in f16, or f32 partial sums for down.
+//   warps 2-9 dequantize the packed window into the f16 A tile (K-major,
+//            SWIZZLE_128B canonical layout; two warps per 32 rows, each half of
+//            the 64-element K atom), then run the epilogue from TMEM, each
+//            warp group on half of the slot columns: SwiGLU for gate/up (rows
+//            0-63 gate, 64-127 up of the same 64 features) writing h in f16,
+//            or f32 partial sums for down.  Consumer barriers take one elected
+//            arrival per warp.
 // The weights are never repacked: blocks stay byte-identical to GGUF.  Each
 // dequantized operand is the GGUF value in f16: Q4_0 and Q8_0 exactly
 // fp16(round(d*q)); K-quants scale by fp16(d*sc), fp16(dmin*m).
@@ -43,17 +46,21 @@ template <> struct Fmt<kQ8_0> { static constexpr int kChunk = 64, kAtoms = 1, kB
 template <> struct Fmt<kQ4_K> { static constexpr int kChunk = 256, kAtoms = 4, kBytes = 144; };
 template <> struct Fmt<kQ6_K> { static constexpr int kChunk = 256, kAtoms = 4, kBytes = 210; };
 
-// Bytes of the 16-byte-aligned window that holds any chunk of a row.
+// Bytes of the 16-byte-aligned window that holds any chunk of a row, rounded
+// up to an odd number of 16-byte units: rows of the packed stage then start in
+// different 16-byte bank groups, so eight lanes reading eight rows with 16-byte
+// loads never collide.
 __host__ __device__ constexpr int window_bytes(int bytes) {
   int w = 0;
   for (int c = 0; c < 16; ++c) {
     const int x = ((((c * bytes) & 15) + bytes) + 15) & ~15;
     w = x > w ? x : w;
   }
-  return w;
+  return ((w / 16) & 1) ? w : w + 16;
 }
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 352;  // warp 0 weight TMA, warp 1 MMA, warps 2-9 dequant + epilogue, warp 10 activation TMA
+constexpr int kDqWarps = 8;
 constexpr int kAtomBytes = 128 * 128;  // 128 rows x 64 f16
 
 enum : int { kErrTimeoutProducer = 1, kErrTimeoutMma = 2, kErrTimeoutDequant = 3, kErrTimeoutEpilogue = 4 };
@@ -69,10 +76,6 @@ struct Args {
   int* err;
 };
 
-__device__ __forceinline__ uint32_t ld32_a2(const uint8_t* p) {  // p is 2-byte aligned
-  const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
-  return (uint32_t)q[0] | ((uint32_t)q[1] << 16);
-}
 __device__ __forceinline__ __half2 as_h2(uint32_t v) {
   __half2 h;
   memcpy(&h, &v, 4);
@@ -89,122 +92,193 @@ __device__ __forceinline__ uint32_t spread23(uint32_t w) { return __byte_perm(w,
 // small integers v (< 1024) in each 16-bit half -> f16 (1024 + v)
 __device__ __forceinline__ __half2 magic(uint32_t v) { return as_h2(v | 0x64006400u); }
 
-// Dequantize 64 elements (one MMA K atom) of one row into eight 16-byte
-// chunks of 8 f16 each.  `blk` points at the row's chunk inside the window.
-template <int F>
-__device__ __forceinline__ void dequant_atom(const uint8_t* blk, int atom, uint4 (&o)[8]);
-
-template <>
-__device__ __forceinline__ void dequant_atom<kQ4_0>(const uint8_t* blk, int, uint4 (&o)[8]) {
-  const __half2 bias = __float2half2_rn(1032.f);  // 1024 + 8
+// NW consecutive 32-bit words starting at byte (16*q + OFF) of a 16-byte
+// aligned row, read with 16-byte shared-memory loads; OFF (0..15) is a
+// compile-time constant, q a runtime 16-byte index.
+template <int OFF, int NW>
+__device__ __forceinline__ void load_words(const uint8_t* row16, int q, uint32_t (&w)[NW]) {
+  constexpr int kChunks = (OFF + 4 * NW + 15) / 16 + ((OFF % 4) ? 1 : 0);
+  uint32_t u[4 * kChunks];
+  const uint4* src = reinterpret_cast<const uint4*>(row16) + q;
 #pragma unroll
-  for (int b = 0; b < 2; ++b) {
-    const uint8_t* bb = blk + 18 * b;
-    const __half dh = __ushort_as_half((unsigned short)ld_u16(bb));
-    const __half2 d = __halves2half2(dh, dh);
-    uint32_t w[4];
+  for (int i = 0; i < kChunks; ++i) {
+    const uint4 v = src[i];
+    u[4 * i] = v.x; u[4 * i + 1] = v.y; u[4 * i + 2] = v.z; u[4 * i + 3] = v.w;
+  }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) w[i] = ld32_a2(bb + 2 + 4 * i);
-#pragma unroll
-    for (int hi = 0; hi < 2; ++hi) {
-#pragma unroll
-      for (int half8 = 0; half8 < 2; ++half8) {
-        uint32_t r[4];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const uint32_t ww = w[2 * half8 + j];
-          const uint32_t a = hi ? (spread01(ww) >> 4) : spread01(ww);
-          const uint32_t c = hi ? (spread23(ww) >> 4) : spread23(ww);
-          r[2 * j] = as_u32(__hmul2(__hsub2(magic(a & 0x000F000Fu), bias), d));
-          r[2 * j + 1] = as_u32(__hmul2(__hsub2(magic(c & 0x000F000Fu), bias), d));
-        }
-        o[4 * b + 2 * hi + half8] = make_uint4(r[0], r[1], r[2], r[3]);
-      }
-    }
+  for (int j = 0; j < NW; ++j) {
+    constexpr int kShift = 8 * (OFF % 4);
+    const int k = OFF / 4 + j;
+    if constexpr (kShift == 0) w[j] = u[k];
+    else w[j] = __funnelshift_r(u[k], u[k + 1], kShift);
   }
 }
 
-template <>
-__device__ __forceinline__ void dequant_atom<kQ8_0>(const uint8_t* blk, int, uint4 (&o)[8]) {
-  const __half2 bias = __float2half2_rn(1152.f);  // 1024 + 128
+// Dequantize half of one MMA K atom (32 of its 64 elements) of one row into
+// four 16-byte chunks of 8 f16: half h holds chunks 4h..4h+3 of the atom.
+// `row` is the row's window (16-byte aligned); OFF is the byte offset of the
+// chunk inside it, (c * chunk bytes) % 16, a compile-time constant.
+template <int F, int OFF>
+__device__ __forceinline__ void dequant_half(const uint8_t* row, int atom, int h, uint4 (&o)[4]);
+
+// Q4_0: the half is block h (18 bytes at OFF + 18h); low nibbles -> elements
+// 0..15, high nibbles -> 16..31; value (q - 8) * d.
+template <int OFF, int H>
+__device__ __forceinline__ void q4_0_block(const uint8_t* row, uint4 (&o)[4]) {
+  constexpr int kB = OFF + 18 * H;  // block start; d at kB, qs at kB + 2
+  uint32_t w[5];
+  load_words<kB % 16, 5>(row, kB / 16, w);  // bytes kB .. kB+19
+  const uint32_t dbits = w[0] & 0xFFFFu;
+  const __half dh = __ushort_as_half((unsigned short)dbits);
+  const __half2 d = __halves2half2(dh, dh);
+  const __half2 bias = __float2half2_rn(1032.f);  // 1024 + 8
+  uint32_t q[4];  // qs bytes 0..15
 #pragma unroll
-  for (int b = 0; b < 2; ++b) {
-    const uint8_t* bb = blk + 34 * b;
-    const __half dh = __ushort_as_half((unsigned short)ld_u16(bb));
-    const __half2 d = __halves2half2(dh, dh);
+  for (int i = 0; i < 4; ++i) q[i] = __funnelshift_r(w[i], w[i + 1], 16);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+  for (int hi = 0; hi < 2; ++hi) {
+#pragma unroll
+    for (int half8 = 0; half8 < 2; ++half8) {
       uint32_t r[4];
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        const uint32_t ww = ld32_a2(bb + 2 + 8 * c + 4 * j) ^ 0x80808080u;  // int8 -> q + 128
-        r[2 * j] = as_u32(__hmul2(__hsub2(magic(spread01(ww)), bias), d));
-        r[2 * j + 1] = as_u32(__hmul2(__hsub2(magic(spread23(ww)), bias), d));
+        const uint32_t ww = q[2 * half8 + j];
+        const uint32_t a = hi ? (spread01(ww) >> 4) : spread01(ww);
+        const uint32_t c = hi ? (spread23(ww) >> 4) : spread23(ww);
+        r[2 * j] = as_u32(__hmul2(__hsub2(magic(a & 0x000F000Fu), bias), d));
+        r[2 * j + 1] = as_u32(__hmul2(__hsub2(magic(c & 0x000F000Fu), bias), d));
       }
-      o[4 * b + c] = make_uint4(r[0], r[1], r[2], r[3]);
+      o[2 * hi + half8] = make_uint4(r[0], r[1], r[2], r[3]);
     }
   }
 }
-
 template <>
-__device__ __forceinline__ void dequant_atom<kQ4_K>(const uint8_t* blk, int atom, uint4 (&o)[8]) {
-  const float d = f16_bits_to_f32(ld_u16(blk));
-  const float dmin = f16_bits_to_f32(ld_u16(blk + 2));
-  int sc0, m0, sc1, m1;
-  k4_scale_min(2 * atom, blk + 4, sc0, m0);
-  k4_scale_min(2 * atom + 1, blk + 4, sc1, m1);
-  const __half2 d0 = __float2half2_rn(d * (float)sc0), n0 = __float2half2_rn(-(dmin * (float)m0));
-  const __half2 d1 = __float2half2_rn(d * (float)sc1), n1 = __float2half2_rn(-(dmin * (float)m1));
+__device__ __forceinline__ void dequant_half<kQ4_0, 0>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q4_0_block<0, 1>(r, o) : q4_0_block<0, 0>(r, o); }
+template <>
+__device__ __forceinline__ void dequant_half<kQ4_0, 4>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q4_0_block<4, 1>(r, o) : q4_0_block<4, 0>(r, o); }
+template <>
+__device__ __forceinline__ void dequant_half<kQ4_0, 8>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q4_0_block<8, 1>(r, o) : q4_0_block<8, 0>(r, o); }
+template <>
+__device__ __forceinline__ void dequant_half<kQ4_0, 12>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q4_0_block<12, 1>(r, o) : q4_0_block<12, 0>(r, o); }
+
+// Q8_0: the half is block h (34 bytes at OFF + 34h); value q * d.
+template <int OFF, int H>
+__device__ __forceinline__ void q8_0_block(const uint8_t* row, uint4 (&o)[4]) {
+  constexpr int kB = OFF + 34 * H;
+  uint32_t w[9];
+  load_words<kB % 16, 9>(row, kB / 16, w);  // bytes kB .. kB+35
+  const __half dh = __ushort_as_half((unsigned short)(w[0] & 0xFFFFu));
+  const __half2 d = __halves2half2(dh, dh);
+  const __half2 bias = __float2half2_rn(1152.f);  // 1024 + 128
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t ww = __funnelshift_r(w[2 * c + j], w[2 * c + j + 1], 16) ^ 0x80808080u;  // q + 128
+      r[2 * j] = as_u32(__hmul2(__hsub2(magic(spread01(ww)), bias), d));
+      r[2 * j + 1] = as_u32(__hmul2(__hsub2(magic(spread23(ww)), bias), d));
+    }
+    o[c] = make_uint4(r[0], r[1], r[2], r[3]);
+  }
+}
+template <>
+__device__ __forceinline__ void dequant_half<kQ8_0, 0>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q8_0_block<0, 1>(r, o) : q8_0_block<0, 0>(r, o); }
+template <>
+__device__ __forceinline__ void dequant_half<kQ8_0, 4>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q8_0_block<4, 1>(r, o) : q8_0_block<4, 0>(r, o); }
+template <>
+__device__ __forceinline__ void dequant_half<kQ8_0, 8>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q8_0_block<8, 1>(r, o) : q8_0_block<8, 0>(r, o); }
+template <>
+__device__ __forceinline__ void dequant_half<kQ8_0, 12>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q8_0_block<12, 1>(r, o) : q8_0_block<12, 0>(r, o); }
+
+// Q4_K (always 16-byte aligned: 144-byte super-blocks): half h of atom `atom`
+// is sub-block 2*atom + h, the low (h = 0) or high (h = 1) nibbles of qs[32*atom ..].
+template <>
+__device__ __forceinline__ void dequant_half<kQ4_K, 0>(const uint8_t* blk, int atom, int h, uint4 (&o)[4]) {
+  const uint4 hdr = *reinterpret_cast<const uint4*>(blk);  // d, dmin, scales[12]
+  const float d = f16_bits_to_f32(hdr.x & 0xFFFFu);
+  const float dmin = f16_bits_to_f32(hdr.x >> 16);
+  // 6-bit (scale, min) pair j of the 12 scale bytes held in hdr.y/z/w
+  // (the get_scale_min_k4 bit layout, read from registers)
+  const int j = 2 * atom + h, sh = 8 * (j & 3);
+  const uint32_t y = hdr.y >> sh, z = hdr.z >> sh, w4 = hdr.w >> sh;
+  const int sc = j < 4 ? (int)(y & 63u) : (int)((w4 & 15u) | (((y >> 6) & 3u) << 4));
+  const int m = j < 4 ? (int)(z & 63u) : (int)(((w4 >> 4) & 15u) | (((z >> 6) & 3u) << 4));
+  const __half2 dd = __float2half2_rn(d * (float)sc), nn = __float2half2_rn(-(dmin * (float)m));
   const __half2 k1024 = __float2half2_rn(1024.f);
   const uint4* q = reinterpret_cast<const uint4*>(blk + 16 + 32 * atom);
   const uint4 qa = q[0], qb = q[1];
   const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-  for (int hi = 0; hi < 2; ++hi) {
-    const __half2 dd = hi ? d1 : d0, nn = hi ? n1 : n0;
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t r[4];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const uint32_t ww = w[2 * c + j];
-        const uint32_t a = hi ? (spread01(ww) >> 4) : spread01(ww);
-        const uint32_t b = hi ? (spread23(ww) >> 4) : spread23(ww);
-        r[2 * j] = as_u32(__hfma2(__hsub2(magic(a & 0x000F000Fu), k1024), dd, nn));
-        r[2 * j + 1] = as_u32(__hfma2(__hsub2(magic(b & 0x000F000Fu), k1024), dd, nn));
-      }
-      o[4 * hi + c] = make_uint4(r[0], r[1], r[2], r[3]);
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t ww = w[2 * c + j];
+      const uint32_t a = h ? (spread01(ww) >> 4) : spread01(ww);
+      const uint32_t b = h ? (spread23(ww) >> 4) : spread23(ww);
+      r[2 * j] = as_u32(__hfma2(__hsub2(magic(a & 0x000F000Fu), k1024), dd, nn));
+      r[2 * j + 1] = as_u32(__hfma2(__hsub2(magic(b & 0x000F000Fu), k1024), dd, nn));
     }
+    o[c] = make_uint4(r[0], r[1], r[2], r[3]);
   }
 }
 
-template <>
-__device__ __forceinline__ void dequant_atom<kQ6_K>(const uint8_t* blk, int atom, uint4 (&o)[8]) {
+// Q6_K (super-block at even offset OFF): the atom covers quarters
+// 2*(atom&1) and 2*(atom&1)+1 of half (atom>>1); h picks the quarter.
+template <int OFF>
+__device__ __forceinline__ void q6_k_half(const uint8_t* row, int atom, int h, uint4 (&o)[4]) {
   const int n = atom >> 1, hiq = atom & 1;
-  const uint8_t* ql = blk + 64 * n;
-  const uint8_t* qh = blk + 128 + 32 * n;
-  const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * n);
-  const float d = f16_bits_to_f32(ld_u16(blk + 208));
+  const int qt = 2 * hiq + h;
+  uint32_t lw[8], hw[8];
+  load_words<OFF, 8>(row, 4 * n + 2 * h, lw);  // ql[64n + 32h .. +31]
+  load_words<OFF, 8>(row, 8 + 2 * n, hw);      // qh[32n .. +31]
+  const int8_t* sc = reinterpret_cast<const int8_t*>(row + OFF + 192 + 8 * n);
+  const float d = f16_bits_to_f32(ld_u16(row + OFF + 208));
   const __half2 bias = __float2half2_rn(1056.f);  // 1024 + 32
   const int ns = hiq ? 4 : 0;
+  const __half2 s_lo = __float2half2_rn(d * (float)sc[2 * qt]);
+  const __half2 s_hi = __float2half2_rn(d * (float)sc[2 * qt + 1]);
 #pragma unroll
-  for (int qq = 0; qq < 2; ++qq) {
-    const int qt = 2 * hiq + qq;
-    const __half2 s_lo = __float2half2_rn(d * (float)sc[2 * qt]);
-    const __half2 s_hi = __float2half2_rn(d * (float)sc[2 * qt + 1]);
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t r[4];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const uint32_t lw = ld32_a2(ql + 32 * qq + 8 * c + 4 * j);
-        const uint32_t hw = ld32_a2(qh + 8 * c + 4 * j);
-        const uint32_t q6 = ((lw >> ns) & 0x0F0F0F0Fu) | (((hw >> (2 * qt)) & 0x03030303u) << 4);
-        const __half2 s = c < 2 ? s_lo : s_hi;
-        r[2 * j] = as_u32(__hmul2(__hsub2(magic(spread01(q6)), bias), s));
-        r[2 * j + 1] = as_u32(__hmul2(__hsub2(magic(spread23(q6)), bias), s));
-      }
-      o[4 * qq + c] = make_uint4(r[0], r[1], r[2], r[3]);
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t q6 = ((lw[2 * c + j] >> ns) & 0x0F0F0F0Fu) | (((hw[2 * c + j] >> (2 * qt)) & 0x03030303u) << 4);
+      const __half2 s = c < 2 ? s_lo : s_hi;
+      r[2 * j] = as_u32(__hmul2(__hsub2(magic(spread01(q6)), bias), s));
+      r[2 * j + 1] = as_u32(__hmul2(__hsub2(magic(spread23(q6)), bias), s));
+    }
+    o[c] = make_uint4(r[0], r[1], r[2], r[3]);
+  }
+}
+#define UAII_Q6K_OFF(O) \
+  template <> __device__ __forceinline__ void dequant_half<kQ6_K, O>(const uint8_t* r, int a, int h, uint4 (&o)[4]) { q6_k_half<O>(r, a, h, o); }
+UAII_Q6K_OFF(0) UAII_Q6K_OFF(2) UAII_Q6K_OFF(4) UAII_Q6K_OFF(6) UAII_Q6K_OFF(8) UAII_Q6K_OFF(10) UAII_Q6K_OFF(12) UAII_Q6K_OFF(14)
+#undef UAII_Q6K_OFF
+
+// Runtime (warp-uniform) chunk offset -> the specialised decoder.
+template <int F>
+__device__ __forceinline__ void dequant_half_at(const uint8_t* row, int off, int atom, int h, uint4 (&o)[4]) {
+  if constexpr (F == kQ4_K) {
+    dequant_half<kQ4_K, 0>(row, atom, h, o);
+  } else if constexpr (F == kQ6_K) {
+    switch (off) {
+      case 0: dequant_half<F, 0>(row, atom, h, o); break;
+      case 2: dequant_half<F, 2>(row, atom, h, o); break;
+      case 4: dequant_half<F, 4>(row, atom, h, o); break;
+      case 6: dequant_half<F, 6>(row, atom, h, o); break;
+      case 8: dequant_half<F, 8>(row, atom, h, o); break;
+      case 10: dequant_half<F, 10>(row, atom, h, o); break;
+      case 12: dequant_half<F, 12>(row, atom, h, o); break;
+      default: dequant_half<F, 14>(row, atom, h, o); break;
+    }
+  } else {  // Q4_0, Q8_0: chunk offsets are multiples of 4
+    switch (off) {
+      case 0: dequant_half<F, 0>(row, atom, h, o); break;
+      case 4: dequant_half<F, 4>(row, atom, h, o); break;
+      case 8: dequant_half<F, 8>(row, atom, h, o); break;
+      default: dequant_half<F, 12>(row, atom, h, o); break;
     }
   }
 }
@@ -253,9 +327,9 @@ struct Cfg {
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + A_ST * kAtomBytes;
   static constexpr int kOffP = kOffB + B_ST * kBStage;
-  static constexpr int kOffX = kOffP + P_ST * kPStage;       // 64 x 17 f32 exchange tile
-  static constexpr int kOffBar = kOffX + 64 * 17 * 4;
-  static constexpr int kNumBars = 2 * (P_ST + A_ST + B_ST) + 4 + 1;
+  static constexpr int kOffX = kOffP + P_ST * kPStage;       // 2 x (64 x 9) f32 exchange tiles
+  static constexpr int kOffBar = kOffX + 2 * 64 * 9 * 4;
+  static constexpr int kNumBars = 2 * (P_ST + A_ST + B_ST) + 6 + 1;
   static constexpr int kSmem = kOffBar + kNumBars * 8 + 16 + 1024;  // + alignment slack
   static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
 };
@@ -281,21 +355,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* b_empty = b_full + B_ST;
   uint64_t* acc_full = b_empty + B_ST;
   uint64_t* acc_empty = acc_full + 1;
-  uint64_t* x_full = acc_empty + 1;
-  uint64_t* x_empty = x_full + 1;
-  uint64_t* mma_done = x_empty + 1;
+  uint64_t* x_full = acc_empty + 1;   // [2], one per epilogue column group
+  uint64_t* x_empty = x_full + 2;     // [2]
+  uint64_t* mma_done = x_empty + 2;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < P_ST; ++i) { mbar_init(pk_full + i, 1); mbar_init(pk_empty + i, 128); }
-    for (int i = 0; i < A_ST; ++i) { mbar_init(a_full + i, 128); mbar_init(a_empty + i, 1); }
+    // consumer-side barriers count one elected lane per dequant warp
+    for (int i = 0; i < P_ST; ++i) { mbar_init(pk_full + i, 1); mbar_init(pk_empty + i, kDqWarps); }
+    for (int i = 0; i < A_ST; ++i) { mbar_init(a_full + i, kDqWarps); mbar_init(a_empty + i, 1); }
     for (int i = 0; i < B_ST; ++i) { mbar_init(b_full + i, 1); mbar_init(b_empty + i, 1); }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 128);
-    mbar_init(x_full, 64);
-    mbar_init(x_empty, 64);
+    mbar_init(acc_empty, kDqWarps);
+    for (int g = 0; g < 2; ++g) { mbar_init(x_full + g, 2); mbar_init(x_empty + g, 2); }
     mbar_init(mma_done, 1);
     *s_abort = 0;
     fence_barrier_init();
@@ -314,14 +388,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* err = args.err;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ weight TMA producer
     if (lane == 0) {
-      uint32_t pi = 0, bi = 0;
+      uint32_t pi = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
         const Tile t = decode_tile(args, tile, BN);
         const int row0 = t.e * args.rows_per_expert + t.m_tile * (args.gateup ? 64 : 128);
-        const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
         const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
         for (int c = c0; c < c1 && ok; ++c) {
           const int ps = pi % P_ST;
@@ -337,6 +410,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(dst + 64 * C::kWB, &tm_w0, pk_full + ps, x, row0 + 64);
           }
           ++pi;
+        }
+      }
+      // never leave with copies in flight: wait (bounded) for the last load of every stage
+      for (uint32_t j = (pi > (uint32_t)P_ST ? pi - P_ST : 0); j < pi; ++j)
+        (void)mbar_wait(pk_full + j % P_ST, (j / P_ST) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 10) {
+    // ------------------------------------------------------------ activation TMA producer
+    if (lane == 0) {
+      uint32_t bi = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const Tile t = decode_tile(args, tile, BN);
+        const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
+        const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
+        for (int c = c0; c < c1 && ok; ++c) {
           for (int at = 0; at < kAtoms && ok; ++at) {
             const int bs = bi % B_ST;
             if (!(ok = wait_bar(b_empty + bs, ((bi / B_ST) & 1) ^ 1, s_abort, err, kErrTimeoutProducer))) break;
@@ -346,9 +436,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // never leave with copies in flight: wait (bounded) for the last load of every stage
-      for (uint32_t j = (pi > (uint32_t)P_ST ? pi - P_ST : 0); j < pi; ++j)
-        (void)mbar_wait(pk_full + j % P_ST, (j / P_ST) & 1);
       for (uint32_t j = (bi > (uint32_t)B_ST ? bi - B_ST : 0); j < bi; ++j)
         (void)mbar_wait(b_full + j % B_ST, (j / B_ST) & 1);
     }
@@ -391,10 +478,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       (void)mbar_wait(mma_done, 0);
     }
     __syncwarp();
-  } else {
-    // ------------------------------------------------------------ dequant + epilogue (128 threads)
+  } else if (warp >= 2 && warp < 10) {
+    // ------------------------------------------------------------ dequant + epilogue (256 threads)
     const int q = warp & 3;            // TMEM lane quarter this warp may access
     const int row = 32 * q + lane;     // A-tile row == accumulator lane
+    const int grp = (warp - 2) >> 2;   // 0: warps 2-5, 1: warps 6-9 (each row has one of each)
     uint32_t pi = 0, ai = 0, it = 0, xi = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
@@ -403,71 +491,80 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = c0; c < c1 && ok; ++c) {
         const int ps = pi % P_ST;
         if (!(ok = wait_bar(pk_full + ps, (pi / P_ST) & 1, s_abort, err, kErrTimeoutDequant))) break;
-        const uint8_t* blk = sP + ps * C::kPStage + row * C::kWB + ((c * Fmt<F>::kBytes) & 15);
+        const uint8_t* rowp = sP + ps * C::kPStage + row * C::kWB;
+        const int off = (c * Fmt<F>::kBytes) & 15;
         for (int at = 0; at < kAtoms && ok; ++at) {
           const int as = ai % A_ST;
           if (!(ok = wait_bar(a_empty + as, ((ai / A_ST) & 1) ^ 1, s_abort, err, kErrTimeoutDequant))) break;
-          uint4 o[8];
-          dequant_atom<F>(blk, at, o);
+          uint4 o[4];
+          dequant_half_at<F>(rowp, off, at, grp, o);
           uint8_t* arow = sA + as * kAtomBytes + row * 128;
 #pragma unroll
-          for (int cc = 0; cc < 8; ++cc) *reinterpret_cast<uint4*>(arow + ((cc ^ (row & 7)) << 4)) = o[cc];
+          for (int cc = 0; cc < 4; ++cc)
+            *reinterpret_cast<uint4*>(arow + (((4 * grp + cc) ^ (row & 7)) << 4)) = o[cc];
           fence_proxy_async_smem();
-          mbar_arrive(a_full + as);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(a_full + as);
           ++ai;
         }
-        mbar_arrive(pk_empty + ps);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pk_empty + ps);
         ++pi;
       }
       if (!ok) break;
-      // ---- epilogue
+      // ---- epilogue: group `grp` owns accumulator columns [grp*BN/2, (grp+1)*BN/2)
       if (!(ok = wait_bar(acc_full, it & 1, s_abort, err, kErrTimeoutEpilogue))) break;
       tc_fence_after();
       const int n_valid = min(BN, __ldg(args.counts + t.e) - t.n_tile * BN);
       const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
       const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
+      constexpr int kHalf = BN / 2;
       if (args.gateup) {
         const int i0 = t.m_tile * 64;
-        for (int cb = 0; cb < BN / 16 && ok; ++cb) {
-          uint32_t r[16];
-          tmem_ld16(taddr + cb * 16, r);
+        float* xb = sX + grp * 64 * 9;
+        for (int cb = grp * kHalf; cb < (grp + 1) * kHalf && ok; cb += 8) {
+          uint32_t r[8];
+          tmem_ld8(taddr + cb, r);
           tmem_ld_wait();
-          if (q >= 2) {  // up rows: hand the values to the gate thread of the same feature
-            if (!(ok = wait_bar(x_empty, (xi & 1) ^ 1, s_abort, err, kErrTimeoutEpilogue))) break;
+          if (q >= 2) {  // up rows: hand the values to the gate warp of the same features
+            if (!(ok = wait_bar(x_empty + grp, (xi & 1) ^ 1, s_abort, err, kErrTimeoutEpilogue))) break;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) sX[(row - 64) * 17 + j] = __uint_as_float(r[j]);
-            mbar_arrive(x_full);
+            for (int j = 0; j < 8; ++j) xb[(row - 64) * 9 + j] = __uint_as_float(r[j]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(x_full + grp);
           } else {
-            if (!(ok = wait_bar(x_full, xi & 1, s_abort, err, kErrTimeoutEpilogue))) break;
+            if (!(ok = wait_bar(x_full + grp, xi & 1, s_abort, err, kErrTimeoutEpilogue))) break;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int n = cb * 16 + j;
+            for (int j = 0; j < 8; ++j) {
+              const int n = cb + j;
               const float g = __uint_as_float(r[j]);
-              const float u = sX[row * 17 + j];
+              const float u = xb[row * 9 + j];
               const float sig = 1.0f / (1.0f + __expf(-g));
               if (n < n_valid)
                 args.h_out[(int64_t)(slot0 + n) * args.out_ld + i0 + row] = __float2half_rn((g * sig) * u);
             }
-            mbar_arrive(x_empty);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(x_empty + grp);
           }
           ++xi;
         }
       } else {
         const int o0 = t.m_tile * 128;
         float* out = args.out + (int64_t)t.split * args.split_stride;
-        for (int cb = 0; cb < BN / 16; ++cb) {
-          uint32_t r[16];
-          tmem_ld16(taddr + cb * 16, r);
+        for (int cb = grp * kHalf; cb < (grp + 1) * kHalf; cb += 8) {
+          uint32_t r[8];
+          tmem_ld8(taddr + cb, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int n = cb * 16 + j;
+          for (int j = 0; j < 8; ++j) {
+            const int n = cb + j;
             if (n < n_valid) out[(int64_t)(slot0 + n) * args.out_ld + o0 + row] = __uint_as_float(r[j]);
           }
         }
       }
       tc_fence_before();
-      mbar_arrive(acc_empty);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
     }
   }
   __syncthreads();
@@ -566,8 +663,8 @@ template <int F>
 cudaError_t dispatch_bn(int bn, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
                         const Args& a, cudaStream_t st) {
   switch (bn) {
-    case 16: return run_gemm<F, 16, 4, 4, 4>(w0, w1, x, a, st);
-    case 32: return run_gemm<F, 32, 4, 4, 4>(w0, w1, x, a, st);
+    case 16: return run_gemm<F, 16, 4, 8, 4>(w0, w1, x, a, st);
+    case 32: return run_gemm<F, 32, 4, 8, 4>(w0, w1, x, a, st);
     case 64: return run_gemm<F, 64, 4, 4, 3>(w0, w1, x, a, st);
     case 128: return run_gemm<F, 128, 4, 4, 2>(w0, w1, x, a, st);
     case 256: return run_gemm<F, 256, 3, 3, 2>(w0, w1, x, a, st);
