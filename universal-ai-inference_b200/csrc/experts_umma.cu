@@ -86,11 +86,6 @@ __device__ __forceinline__ uint32_t as_u32(__half2 h) {
   memcpy(&v, &h, 4);
   return v;
 }
-// bytes (0,1) and (2,3) of w spread to the two halves of a 32-bit word
-__device__ __forceinline__ uint32_t spread01(uint32_t w) { return __byte_perm(w, 0, 0x4140); }
-__device__ __forceinline__ uint32_t spread23(uint32_t w) { return __byte_perm(w, 0, 0x4342); }
-// small integers v (< 1024) in each 16-bit half -> f16 (1024 + v)
-__device__ __forceinline__ __half2 magic(uint32_t v) { return as_h2(v | 0x64006400u); }
 
 // NW consecutive 32-bit words starting at byte (16*q + OFF) of a 16-byte
 // aligned row, read with 16-byte shared-memory loads; OFF (0..15) is a
@@ -114,54 +109,62 @@ __device__ __forceinline__ void load_words(const uint8_t* row16, int q, uint32_t
   }
 }
 
-// Dequantize half of one MMA K atom (32 of its 64 elements) of one row into
-// four 16-byte chunks of 8 f16: half h holds chunks 4h..4h+3 of the atom.
-// `row` is the row's window (16-byte aligned); OFF is the byte offset of the
-// chunk inside it, (c * chunk bytes) % 16, a compile-time constant.
-template <int F, int OFF>
-__device__ __forceinline__ void dequant_half(const uint8_t* row, int atom, int h, uint4 (&o)[4]);
+// Operand K order.  Inside every group of four consecutive K elements the
+// tensor-core operands store elements in the order [0, 2, 1, 3] (both the
+// weight tile built here and the activation rows written by the gather and
+// the gate/up epilogue), which leaves every dot product unchanged and lets a
+// 32-bit word of packed bytes unpack with one shift and one LOP3 per pair.
+// the masked values (< 1024) of both 16-bit halves as f16 (1024 + v)
+__device__ __forceinline__ uint32_t lo_pairs(uint32_t w, uint32_t mask) { return (w & mask) | 0x64006400u; }
 
-// Q4_0: the half is block h (18 bytes at OFF + 18h); low nibbles -> elements
-// 0..15, high nibbles -> 16..31; value (q - 8) * d.
+// 8 elements (two words of four 4-bit values at bit offset s) -> one 16-byte chunk
+__device__ __forceinline__ uint4 nib_chunk(uint32_t w0, uint32_t w1, int s, __half2 bias, __half2 d, __half2 nm,
+                                          bool fma) {
+  const uint32_t a[4] = {lo_pairs(w0 >> s, 0x000F000Fu), lo_pairs(w0 >> (s + 8), 0x000F000Fu),
+                         lo_pairs(w1 >> s, 0x000F000Fu), lo_pairs(w1 >> (s + 8), 0x000F000Fu)};
+  uint32_t r[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 q = __hsub2(as_h2(a[i]), bias);
+    r[i] = as_u32(fma ? __hfma2(q, d, nm) : __hmul2(q, d));
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+// 8 elements from two words of four byte values -> one 16-byte chunk
+__device__ __forceinline__ uint4 byte_chunk(uint32_t w0, uint32_t w1, __half2 bias, __half2 d) {
+  const uint32_t a[4] = {lo_pairs(w0, 0x00FF00FFu), lo_pairs(w0 >> 8, 0x00FF00FFu), lo_pairs(w1, 0x00FF00FFu),
+                         lo_pairs(w1 >> 8, 0x00FF00FFu)};
+  uint32_t r[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) r[i] = as_u32(__hmul2(__hsub2(as_h2(a[i]), bias), d));
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+// Q4_0 / Q8_0: one thread makes half of the 64-element atom (block h of the
+// two blocks in the chunk): four 16-byte chunks, chunks 4h..4h+3 of the atom.
+template <int F, int OFF>
+__device__ __forceinline__ void dequant_half(const uint8_t* row, int h, uint4 (&o)[4]);
+
+// Q4_0 block: {f16 d; u8 qs[16]}, low nibbles -> elements 0..15, high -> 16..31, (q - 8) * d
 template <int OFF, int H>
 __device__ __forceinline__ void q4_0_block(const uint8_t* row, uint4 (&o)[4]) {
-  constexpr int kB = OFF + 18 * H;  // block start; d at kB, qs at kB + 2
+  constexpr int kB = OFF + 18 * H;
   uint32_t w[5];
   load_words<kB % 16, 5>(row, kB / 16, w);  // bytes kB .. kB+19
-  const uint32_t dbits = w[0] & 0xFFFFu;
-  const __half dh = __ushort_as_half((unsigned short)dbits);
+  const __half dh = __ushort_as_half((unsigned short)(w[0] & 0xFFFFu));
   const __half2 d = __halves2half2(dh, dh);
   const __half2 bias = __float2half2_rn(1032.f);  // 1024 + 8
   uint32_t q[4];  // qs bytes 0..15
 #pragma unroll
   for (int i = 0; i < 4; ++i) q[i] = __funnelshift_r(w[i], w[i + 1], 16);
-#pragma unroll
-  for (int hi = 0; hi < 2; ++hi) {
-#pragma unroll
-    for (int half8 = 0; half8 < 2; ++half8) {
-      uint32_t r[4];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const uint32_t ww = q[2 * half8 + j];
-        const uint32_t a = hi ? (spread01(ww) >> 4) : spread01(ww);
-        const uint32_t c = hi ? (spread23(ww) >> 4) : spread23(ww);
-        r[2 * j] = as_u32(__hmul2(__hsub2(magic(a & 0x000F000Fu), bias), d));
-        r[2 * j + 1] = as_u32(__hmul2(__hsub2(magic(c & 0x000F000Fu), bias), d));
-      }
-      o[2 * hi + half8] = make_uint4(r[0], r[1], r[2], r[3]);
-    }
-  }
+  o[0] = nib_chunk(q[0], q[1], 0, bias, d, d, false);
+  o[1] = nib_chunk(q[2], q[3], 0, bias, d, d, false);
+  o[2] = nib_chunk(q[0], q[1], 4, bias, d, d, false);
+  o[3] = nib_chunk(q[2], q[3], 4, bias, d, d, false);
 }
-template <>
-__device__ __forceinline__ void dequant_half<kQ4_0, 0>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q4_0_block<0, 1>(r, o) : q4_0_block<0, 0>(r, o); }
-template <>
-__device__ __forceinline__ void dequant_half<kQ4_0, 4>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q4_0_block<4, 1>(r, o) : q4_0_block<4, 0>(r, o); }
-template <>
-__device__ __forceinline__ void dequant_half<kQ4_0, 8>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q4_0_block<8, 1>(r, o) : q4_0_block<8, 0>(r, o); }
-template <>
-__device__ __forceinline__ void dequant_half<kQ4_0, 12>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q4_0_block<12, 1>(r, o) : q4_0_block<12, 0>(r, o); }
 
-// Q8_0: the half is block h (34 bytes at OFF + 34h); value q * d.
+// Q8_0 block: {f16 d; i8 qs[32]}, q * d
 template <int OFF, int H>
 __device__ __forceinline__ void q8_0_block(const uint8_t* row, uint4 (&o)[4]) {
   constexpr int kB = OFF + 34 * H;
@@ -170,118 +173,114 @@ __device__ __forceinline__ void q8_0_block(const uint8_t* row, uint4 (&o)[4]) {
   const __half dh = __ushort_as_half((unsigned short)(w[0] & 0xFFFFu));
   const __half2 d = __halves2half2(dh, dh);
   const __half2 bias = __float2half2_rn(1152.f);  // 1024 + 128
+  uint32_t q[8];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t r[4];
+  for (int i = 0; i < 8; ++i) q[i] = __funnelshift_r(w[i], w[i + 1], 16) ^ 0x80808080u;  // int8 -> q + 128
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t ww = __funnelshift_r(w[2 * c + j], w[2 * c + j + 1], 16) ^ 0x80808080u;  // q + 128
-      r[2 * j] = as_u32(__hmul2(__hsub2(magic(spread01(ww)), bias), d));
-      r[2 * j + 1] = as_u32(__hmul2(__hsub2(magic(spread23(ww)), bias), d));
-    }
-    o[c] = make_uint4(r[0], r[1], r[2], r[3]);
-  }
+  for (int c = 0; c < 4; ++c) o[c] = byte_chunk(q[2 * c], q[2 * c + 1], bias, d);
 }
-template <>
-__device__ __forceinline__ void dequant_half<kQ8_0, 0>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q8_0_block<0, 1>(r, o) : q8_0_block<0, 0>(r, o); }
-template <>
-__device__ __forceinline__ void dequant_half<kQ8_0, 4>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q8_0_block<4, 1>(r, o) : q8_0_block<4, 0>(r, o); }
-template <>
-__device__ __forceinline__ void dequant_half<kQ8_0, 8>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q8_0_block<8, 1>(r, o) : q8_0_block<8, 0>(r, o); }
-template <>
-__device__ __forceinline__ void dequant_half<kQ8_0, 12>(const uint8_t* r, int, int h, uint4 (&o)[4]) { h ? q8_0_block<12, 1>(r, o) : q8_0_block<12, 0>(r, o); }
 
-// Q4_K (always 16-byte aligned: 144-byte super-blocks): half h of atom `atom`
-// is sub-block 2*atom + h, the low (h = 0) or high (h = 1) nibbles of qs[32*atom ..].
-template <>
-__device__ __forceinline__ void dequant_half<kQ4_K, 0>(const uint8_t* blk, int atom, int h, uint4 (&o)[4]) {
+#define UAII_HALF_OFF(F, FN, O)                                                                    \
+  template <>                                                                                       \
+  __device__ __forceinline__ void dequant_half<F, O>(const uint8_t* r, int h, uint4(&o)[4]) {       \
+    h ? FN<O, 1>(r, o) : FN<O, 0>(r, o);                                                            \
+  }
+UAII_HALF_OFF(kQ4_0, q4_0_block, 0) UAII_HALF_OFF(kQ4_0, q4_0_block, 4)
+UAII_HALF_OFF(kQ4_0, q4_0_block, 8) UAII_HALF_OFF(kQ4_0, q4_0_block, 12)
+UAII_HALF_OFF(kQ8_0, q8_0_block, 0) UAII_HALF_OFF(kQ8_0, q8_0_block, 4)
+UAII_HALF_OFF(kQ8_0, q8_0_block, 8) UAII_HALF_OFF(kQ8_0, q8_0_block, 12)
+#undef UAII_HALF_OFF
+
+// K-quants: one thread makes whole 64-element atoms of one super-block; the
+// super-block header is decoded once per chunk into a Header.
+struct Q4KHeader {
+  uint32_t y, z, w;  // the 12 scale bytes
+  float d, dmin;
+};
+__device__ __forceinline__ Q4KHeader q4_k_header(const uint8_t* blk) {
   const uint4 hdr = *reinterpret_cast<const uint4*>(blk);  // d, dmin, scales[12]
-  const float d = f16_bits_to_f32(hdr.x & 0xFFFFu);
-  const float dmin = f16_bits_to_f32(hdr.x >> 16);
-  // 6-bit (scale, min) pair j of the 12 scale bytes held in hdr.y/z/w
-  // (the get_scale_min_k4 bit layout, read from registers)
-  const int j = 2 * atom + h, sh = 8 * (j & 3);
-  const uint32_t y = hdr.y >> sh, z = hdr.z >> sh, w4 = hdr.w >> sh;
+  return Q4KHeader{hdr.y, hdr.z, hdr.w, f16_bits_to_f32(hdr.x & 0xFFFFu), f16_bits_to_f32(hdr.x >> 16)};
+}
+// (scale, min) pair j with the get_scale_min_k4 bit layout, from registers
+__device__ __forceinline__ void q4_k_pair(const Q4KHeader& H, int j, __half2& d, __half2& nm) {
+  const int sh = 8 * (j & 3);
+  const uint32_t y = H.y >> sh, z = H.z >> sh, w4 = H.w >> sh;
   const int sc = j < 4 ? (int)(y & 63u) : (int)((w4 & 15u) | (((y >> 6) & 3u) << 4));
   const int m = j < 4 ? (int)(z & 63u) : (int)(((w4 >> 4) & 15u) | (((z >> 6) & 3u) << 4));
-  const __half2 dd = __float2half2_rn(d * (float)sc), nn = __float2half2_rn(-(dmin * (float)m));
-  const __half2 k1024 = __float2half2_rn(1024.f);
-  const uint4* q = reinterpret_cast<const uint4*>(blk + 16 + 32 * atom);
-  const uint4 qa = q[0], qb = q[1];
+  d = __float2half2_rn(H.d * (float)sc);
+  nm = __float2half2_rn(-(H.dmin * (float)m));
+}
+// atom `at` = qs[32*at .. +31]: low nibbles -> sub-block 2at, high -> 2at+1
+__device__ __forceinline__ void q4_k_atom(const uint8_t* blk, const Q4KHeader& H, int at, uint4 (&o)[8]) {
+  __half2 d0, n0, d1, n1;
+  q4_k_pair(H, 2 * at, d0, n0);
+  q4_k_pair(H, 2 * at + 1, d1, n1);
+  const __half2 bias = __float2half2_rn(1024.f);
+  const uint4* qp = reinterpret_cast<const uint4*>(blk + 16 + 32 * at);
+  const uint4 qa = qp[0], qb = qp[1];
   const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    uint32_t r[4];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t ww = w[2 * c + j];
-      const uint32_t a = h ? (spread01(ww) >> 4) : spread01(ww);
-      const uint32_t b = h ? (spread23(ww) >> 4) : spread23(ww);
-      r[2 * j] = as_u32(__hfma2(__hsub2(magic(a & 0x000F000Fu), k1024), dd, nn));
-      r[2 * j + 1] = as_u32(__hfma2(__hsub2(magic(b & 0x000F000Fu), k1024), dd, nn));
-    }
-    o[c] = make_uint4(r[0], r[1], r[2], r[3]);
+    o[c] = nib_chunk(w[2 * c], w[2 * c + 1], 0, bias, d0, n0, true);
+    o[4 + c] = nib_chunk(w[2 * c], w[2 * c + 1], 4, bias, d1, n1, true);
   }
 }
 
-// Q6_K (super-block at even offset OFF): the atom covers quarters
-// 2*(atom&1) and 2*(atom&1)+1 of half (atom>>1); h picks the quarter.
+// Q6_K super-block at even offset OFF: atom `at` covers quarters 2*(at&1) and
+// 2*(at&1)+1 of half (at>>1)
 template <int OFF>
-__device__ __forceinline__ void q6_k_half(const uint8_t* row, int atom, int h, uint4 (&o)[4]) {
-  const int n = atom >> 1, hiq = atom & 1;
-  const int qt = 2 * hiq + h;
-  uint32_t lw[8], hw[8];
-  load_words<OFF, 8>(row, 4 * n + 2 * h, lw);  // ql[64n + 32h .. +31]
-  load_words<OFF, 8>(row, 8 + 2 * n, hw);      // qh[32n .. +31]
-  const int8_t* sc = reinterpret_cast<const int8_t*>(row + OFF + 192 + 8 * n);
-  const float d = f16_bits_to_f32(ld_u16(row + OFF + 208));
-  const __half2 bias = __float2half2_rn(1056.f);  // 1024 + 32
+__device__ __forceinline__ void q6_k_atom(const uint8_t* row, float d, int at, uint4 (&o)[8]) {
+  const int n = at >> 1, hiq = at & 1;
   const int ns = hiq ? 4 : 0;
-  const __half2 s_lo = __float2half2_rn(d * (float)sc[2 * qt]);
-  const __half2 s_hi = __float2half2_rn(d * (float)sc[2 * qt + 1]);
+  uint32_t hw[8];
+  load_words<OFF, 8>(row, 8 + 2 * n, hw);  // qh[32n .. +31]
+  const int8_t* sc = reinterpret_cast<const int8_t*>(row + OFF + 192 + 8 * n);
+  const __half2 bias = __float2half2_rn(1056.f);  // 1024 + 32
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t r[4];
+  for (int qq = 0; qq < 2; ++qq) {
+    const int qt = 2 * hiq + qq;
+    uint32_t lw[8];
+    load_words<OFF, 8>(row, 4 * n + 2 * qq, lw);  // ql[64n + 32qq .. +31]
+    const __half2 s_lo = __float2half2_rn(d * (float)sc[2 * qt]);
+    const __half2 s_hi = __float2half2_rn(d * (float)sc[2 * qt + 1]);
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t q6 = ((lw[2 * c + j] >> ns) & 0x0F0F0F0Fu) | (((hw[2 * c + j] >> (2 * qt)) & 0x03030303u) << 4);
-      const __half2 s = c < 2 ? s_lo : s_hi;
-      r[2 * j] = as_u32(__hmul2(__hsub2(magic(spread01(q6)), bias), s));
-      r[2 * j + 1] = as_u32(__hmul2(__hsub2(magic(spread23(q6)), bias), s));
+    for (int c = 0; c < 4; ++c) {
+      uint32_t q6[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        q6[j] = ((lw[2 * c + j] >> ns) & 0x0F0F0F0Fu) | (((hw[2 * c + j] >> (2 * qt)) & 0x03030303u) << 4);
+      o[4 * qq + c] = byte_chunk(q6[0], q6[1], bias, c < 2 ? s_lo : s_hi);
     }
-    o[c] = make_uint4(r[0], r[1], r[2], r[3]);
   }
 }
-#define UAII_Q6K_OFF(O) \
-  template <> __device__ __forceinline__ void dequant_half<kQ6_K, O>(const uint8_t* r, int a, int h, uint4 (&o)[4]) { q6_k_half<O>(r, a, h, o); }
-UAII_Q6K_OFF(0) UAII_Q6K_OFF(2) UAII_Q6K_OFF(4) UAII_Q6K_OFF(6) UAII_Q6K_OFF(8) UAII_Q6K_OFF(10) UAII_Q6K_OFF(12) UAII_Q6K_OFF(14)
-#undef UAII_Q6K_OFF
 
-// Runtime (warp-uniform) chunk offset -> the specialised decoder.
+// Runtime (warp-uniform) chunk offset -> the specialised half decoder (Q4_0, Q8_0).
 template <int F>
-__device__ __forceinline__ void dequant_half_at(const uint8_t* row, int off, int atom, int h, uint4 (&o)[4]) {
-  if constexpr (F == kQ4_K) {
-    dequant_half<kQ4_K, 0>(row, atom, h, o);
-  } else if constexpr (F == kQ6_K) {
-    switch (off) {
-      case 0: dequant_half<F, 0>(row, atom, h, o); break;
-      case 2: dequant_half<F, 2>(row, atom, h, o); break;
-      case 4: dequant_half<F, 4>(row, atom, h, o); break;
-      case 6: dequant_half<F, 6>(row, atom, h, o); break;
-      case 8: dequant_half<F, 8>(row, atom, h, o); break;
-      case 10: dequant_half<F, 10>(row, atom, h, o); break;
-      case 12: dequant_half<F, 12>(row, atom, h, o); break;
-      default: dequant_half<F, 14>(row, atom, h, o); break;
-    }
-  } else {  // Q4_0, Q8_0: chunk offsets are multiples of 4
-    switch (off) {
-      case 0: dequant_half<F, 0>(row, atom, h, o); break;
-      case 4: dequant_half<F, 4>(row, atom, h, o); break;
-      case 8: dequant_half<F, 8>(row, atom, h, o); break;
-      default: dequant_half<F, 12>(row, atom, h, o); break;
-    }
+__device__ __forceinline__ void dequant_half_at(const uint8_t* row, int off, int h, uint4 (&o)[4]) {
+  switch (off) {
+    case 0: dequant_half<F, 0>(row, h, o); break;
+    case 4: dequant_half<F, 4>(row, h, o); break;
+    case 8: dequant_half<F, 8>(row, h, o); break;
+    default: dequant_half<F, 12>(row, h, o); break;
   }
 }
+
+template <int F>
+__device__ __forceinline__ void q6_k_atom_at(const uint8_t* row, int off, float d, int at, uint4 (&o)[8]) {
+  switch (off) {
+    case 0: q6_k_atom<0>(row, d, at, o); break;
+    case 2: q6_k_atom<2>(row, d, at, o); break;
+    case 4: q6_k_atom<4>(row, d, at, o); break;
+    case 6: q6_k_atom<6>(row, d, at, o); break;
+    case 8: q6_k_atom<8>(row, d, at, o); break;
+    case 10: q6_k_atom<10>(row, d, at, o); break;
+    case 12: q6_k_atom<12>(row, d, at, o); break;
+    default: q6_k_atom<14>(row, d, at, o); break;
+  }
+}
+
+// position of K element i in the operand order [0, 2, 1, 3] of every group of four
+__device__ __forceinline__ int k_perm(int i) { return (i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1); }
 
 struct Tile {
   int e, m_tile, n_tile, split;
@@ -304,8 +303,39 @@ __device__ __forceinline__ Tile decode_tile(const Args& a, int tile, int bn) {
   return t;
 }
 
+#ifdef UAII_UMMA_STATS
+// Diagnostic build only: cycles spent in each wait site, accumulated per
+// thread and added to these grid-wide totals once at kernel exit.
+__device__ unsigned long long g_wait_cycles[16];
+__device__ unsigned long long g_wait_count[16];
+struct WaitStats {
+  unsigned long long cyc[12];
+  unsigned int cnt[12];
+};
+#define UAII_WS_PARAM , WaitStats* ws
+#define UAII_WS_ARG , &wstats
+#else
+#define UAII_WS_PARAM
+#define UAII_WS_ARG
+#endif
+
 // Wait with abort: false when another role aborted or the clock budget ran out.
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
+// `site` identifies the wait for the diagnostic build.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code,
+                                         int site UAII_WS_PARAM) {
+#ifdef UAII_UMMA_STATS
+  struct Acc {
+    WaitStats* ws;
+    long long ts;
+    int site;
+    __device__ ~Acc() {
+      ws->cyc[site] += (unsigned long long)(clock64() - ts);
+      ws->cnt[site] += 1;
+    }
+  } acc{ws, clock64(), site};
+#else
+  (void)site;
+#endif
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
@@ -327,9 +357,8 @@ struct Cfg {
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + A_ST * kAtomBytes;
   static constexpr int kOffP = kOffB + B_ST * kBStage;
-  static constexpr int kOffX = kOffP + P_ST * kPStage;       // 2 x (64 x 9) f32 exchange tiles
-  static constexpr int kOffBar = kOffX + 2 * 64 * 9 * 4;
-  static constexpr int kNumBars = 2 * (P_ST + A_ST + B_ST) + 6 + 1;
+  static constexpr int kOffBar = kOffP + P_ST * kPStage;
+  static constexpr int kNumBars = 2 * (P_ST + A_ST + B_ST) + 2 + 1;
   static constexpr int kSmem = kOffBar + kNumBars * 8 + 16 + 1024;  // + alignment slack
   static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
 };
@@ -345,7 +374,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sA = smem + C::kOffA;
   uint8_t* sB = smem + C::kOffB;
   uint8_t* sP = smem + C::kOffP;
-  float* sX = reinterpret_cast<float*>(smem + C::kOffX);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   uint64_t* pk_full = bars;
   uint64_t* pk_empty = pk_full + P_ST;
@@ -355,21 +383,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* b_empty = b_full + B_ST;
   uint64_t* acc_full = b_empty + B_ST;
   uint64_t* acc_empty = acc_full + 1;
-  uint64_t* x_full = acc_empty + 1;   // [2], one per epilogue column group
-  uint64_t* x_empty = x_full + 2;     // [2]
-  uint64_t* mma_done = x_empty + 2;
+  uint64_t* mma_done = acc_empty + 1;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#ifdef UAII_UMMA_STATS
+  WaitStats wstats{};
+  const long long t_kernel = clock64();
+#endif
   if (threadIdx.x == 0) {
     // consumer-side barriers count one elected lane per dequant warp
     for (int i = 0; i < P_ST; ++i) { mbar_init(pk_full + i, 1); mbar_init(pk_empty + i, kDqWarps); }
-    for (int i = 0; i < A_ST; ++i) { mbar_init(a_full + i, kDqWarps); mbar_init(a_empty + i, 1); }
+    // K-quant atoms are written whole by one warp group (4 warps), 32-element-block
+    // atoms in halves by both groups (8 warps)
+    for (int i = 0; i < A_ST; ++i) { mbar_init(a_full + i, kAtoms == 4 ? 4 : kDqWarps); mbar_init(a_empty + i, 1); }
     for (int i = 0; i < B_ST; ++i) { mbar_init(b_full + i, 1); mbar_init(b_empty + i, 1); }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, kDqWarps);
-    for (int g = 0; g < 2; ++g) { mbar_init(x_full + g, 2); mbar_init(x_empty + g, 2); }
     mbar_init(mma_done, 1);
     *s_abort = 0;
     fence_barrier_init();
@@ -398,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
         for (int c = c0; c < c1 && ok; ++c) {
           const int ps = pi % P_ST;
-          if (!(ok = wait_bar(pk_empty + ps, ((pi / P_ST) & 1) ^ 1, s_abort, err, kErrTimeoutProducer))) break;
+          if (!(ok = wait_bar(pk_empty + ps, ((pi / P_ST) & 1) ^ 1, s_abort, err, kErrTimeoutProducer, 0 UAII_WS_ARG))) break;
           mbar_arrive_expect_tx(pk_full + ps, C::kPStage);
           const int x = (c * Fmt<F>::kBytes) & ~15;
           uint8_t* dst = sP + ps * C::kPStage;
@@ -429,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = c0; c < c1 && ok; ++c) {
           for (int at = 0; at < kAtoms && ok; ++at) {
             const int bs = bi % B_ST;
-            if (!(ok = wait_bar(b_empty + bs, ((bi / B_ST) & 1) ^ 1, s_abort, err, kErrTimeoutProducer))) break;
+            if (!(ok = wait_bar(b_empty + bs, ((bi / B_ST) & 1) ^ 1, s_abort, err, kErrTimeoutProducer, 1 UAII_WS_ARG))) break;
             mbar_arrive_expect_tx(b_full + bs, C::kBStage);
             tma_load_2d(sB + bs * C::kBStage, &tm_x, b_full + bs, c * Fmt<F>::kChunk + at * 64, slot0);
             ++bi;
@@ -449,14 +480,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
         const Tile t = decode_tile(args, tile, BN);
         const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
-        if (!(ok = wait_bar(acc_empty, (it & 1) ^ 1, s_abort, err, kErrTimeoutMma))) break;
+        if (!(ok = wait_bar(acc_empty, (it & 1) ^ 1, s_abort, err, kErrTimeoutMma, 2 UAII_WS_ARG))) break;
         tc_fence_after();
         uint32_t acc = 0;
         for (int c = c0; c < c1 && ok; ++c) {
           for (int at = 0; at < kAtoms; ++at) {
             const int as = ai % A_ST, bs = bi % B_ST;
-            if (!(ok = wait_bar(a_full + as, (ai / A_ST) & 1, s_abort, err, kErrTimeoutMma))) break;
-            if (!(ok = wait_bar(b_full + bs, (bi / B_ST) & 1, s_abort, err, kErrTimeoutMma))) break;
+            if (!(ok = wait_bar(a_full + as, (ai / A_ST) & 1, s_abort, err, kErrTimeoutMma, 3 UAII_WS_ARG))) break;
+            if (!(ok = wait_bar(b_full + bs, (bi / B_ST) & 1, s_abort, err, kErrTimeoutMma, 4 UAII_WS_ARG))) break;
             tc_fence_after();
             const uint64_t ad = sw128_desc(smem_u32(sA + as * kAtomBytes));
             const uint64_t bd = sw128_desc(smem_u32(sB + bs * C::kBStage));
@@ -483,21 +514,66 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;            // TMEM lane quarter this warp may access
     const int row = 32 * q + lane;     // A-tile row == accumulator lane
     const int grp = (warp - 2) >> 2;   // 0: warps 2-5, 1: warps 6-9 (each row has one of each)
-    uint32_t pi = 0, ai = 0, it = 0, xi = 0;
+    // Gate/up tiles hold 64 features: in every 32-row block (one TMEM lane
+    // quarter) lanes 0-15 are gate rows and lanes 16-31 the up rows of the same
+    // 16 features, so the SwiGLU epilogue pairs them with one lane shuffle.
+    // The packed stage keeps the TMA layout: gate rows 0-63, up rows 64-127.
+    const int src_row = args.gateup ? (lane < 16 ? 16 * q + lane : 64 + 16 * q + (lane - 16)) : row;
+    uint32_t pi = 0, ai = 0, it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
       const Tile t = decode_tile(args, tile, BN);
       const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
       for (int c = c0; c < c1 && ok; ++c) {
         const int ps = pi % P_ST;
-        if (!(ok = wait_bar(pk_full + ps, (pi / P_ST) & 1, s_abort, err, kErrTimeoutDequant))) break;
-        const uint8_t* rowp = sP + ps * C::kPStage + row * C::kWB;
+        if (!(ok = wait_bar(pk_full + ps, (pi / P_ST) & 1, s_abort, err, kErrTimeoutDequant, 5 UAII_WS_ARG))) break;
+        const uint8_t* rowp = sP + ps * C::kPStage + src_row * C::kWB;
         const int off = (c * Fmt<F>::kBytes) & 15;
-        for (int at = 0; at < kAtoms && ok; ++at) {
+        if constexpr (kAtoms == 4) {
+          // this warp group makes atoms grp and grp + 2 of the super-block
+          Q4KHeader h4{};
+          float d6 = 0.f;
+          if constexpr (F == kQ4_K) h4 = q4_k_header(rowp);
+          else d6 = f16_bits_to_f32(ld_u16(rowp + off + 208));
+          for (int k = 0; k < 2 && ok; ++k) {
+            const int at = grp + 2 * k;
+            const uint32_t aidx = ai + at;
+            const int as = aidx % A_ST;
+            if (!(ok = wait_bar(a_empty + as, ((aidx / A_ST) & 1) ^ 1, s_abort, err, kErrTimeoutDequant, 6 UAII_WS_ARG)))
+              break;
+            uint4 o[8];
+#ifdef UAII_UMMA_STATS
+            const long long tq = clock64();
+#endif
+            if constexpr (F == kQ4_K) q4_k_atom(rowp, h4, at, o);
+            else q6_k_atom_at<F>(rowp, off, d6, at, o);
+#ifdef UAII_UMMA_STATS
+            asm volatile("" ::"r"(o[0].x), "r"(o[3].y), "r"(o[5].z), "r"(o[7].w));
+            wstats.cyc[10] += (unsigned long long)(clock64() - tq);
+            wstats.cnt[10] += 1;
+#endif
+            uint8_t* arow = sA + as * kAtomBytes + row * 128;
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) *reinterpret_cast<uint4*>(arow + ((cc ^ (row & 7)) << 4)) = o[cc];
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(a_full + as);
+          }
+          ai += kAtoms;
+        } else {
           const int as = ai % A_ST;
-          if (!(ok = wait_bar(a_empty + as, ((ai / A_ST) & 1) ^ 1, s_abort, err, kErrTimeoutDequant))) break;
+          if (!(ok = wait_bar(a_empty + as, ((ai / A_ST) & 1) ^ 1, s_abort, err, kErrTimeoutDequant, 6 UAII_WS_ARG)))
+            break;
           uint4 o[4];
-          dequant_half_at<F>(rowp, off, at, grp, o);
+#ifdef UAII_UMMA_STATS
+          const long long tq = clock64();
+#endif
+          dequant_half_at<F>(rowp, off, grp, o);
+#ifdef UAII_UMMA_STATS
+          asm volatile("" ::"r"(o[0].x), "r"(o[1].y), "r"(o[2].z), "r"(o[3].w));
+          wstats.cyc[10] += (unsigned long long)(clock64() - tq);
+          wstats.cnt[10] += 1;
+#endif
           uint8_t* arow = sA + as * kAtomBytes + row * 128;
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc)
@@ -513,40 +589,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       // ---- epilogue: group `grp` owns accumulator columns [grp*BN/2, (grp+1)*BN/2)
-      if (!(ok = wait_bar(acc_full, it & 1, s_abort, err, kErrTimeoutEpilogue))) break;
+      if (!(ok = wait_bar(acc_full, it & 1, s_abort, err, kErrTimeoutEpilogue, 7 UAII_WS_ARG))) break;
       tc_fence_after();
       const int n_valid = min(BN, __ldg(args.counts + t.e) - t.n_tile * BN);
       const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
       const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
       constexpr int kHalf = BN / 2;
       if (args.gateup) {
-        const int i0 = t.m_tile * 64;
-        float* xb = sX + grp * 64 * 9;
-        for (int cb = grp * kHalf; cb < (grp + 1) * kHalf && ok; cb += 8) {
+        // lane l < 16 holds gate, lane l + 16 up of feature i0 + 16q + (l & 15); each
+        // column pair (n, n+1) is split: the gate lane finishes n, the up lane n + 1
+        const int feat = k_perm(t.m_tile * 64 + 16 * q + (lane & 15));
+        const bool gate_lane = lane < 16;
+        for (int cb = grp * kHalf; cb < (grp + 1) * kHalf; cb += 8) {
           uint32_t r[8];
           tmem_ld8(taddr + cb, r);
           tmem_ld_wait();
-          if (q >= 2) {  // up rows: hand the values to the gate warp of the same features
-            if (!(ok = wait_bar(x_empty + grp, (xi & 1) ^ 1, s_abort, err, kErrTimeoutEpilogue))) break;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) xb[(row - 64) * 9 + j] = __uint_as_float(r[j]);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(x_full + grp);
-          } else {
-            if (!(ok = wait_bar(x_full + grp, xi & 1, s_abort, err, kErrTimeoutEpilogue))) break;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int n = cb + j;
-              const float g = __uint_as_float(r[j]);
-              const float u = xb[row * 9 + j];
-              const float sig = 1.0f / (1.0f + __expf(-g));
-              if (n < n_valid)
-                args.h_out[(int64_t)(slot0 + n) * args.out_ld + i0 + row] = __float2half_rn((g * sig) * u);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(x_empty + grp);
+          for (int j = 0; j < 8; j += 2) {
+            const float mine0 = __uint_as_float(r[j]), mine1 = __uint_as_float(r[j + 1]);
+            const float other = __shfl_xor_sync(0xffffffffu, gate_lane ? mine1 : mine0, 16);
+            const float g = gate_lane ? mine0 : other;  // column n (gate lane) or n + 1 (up lane)
+            const float u = gate_lane ? other : mine1;
+            const int n = cb + j + (gate_lane ? 0 : 1);
+            const float sig = 1.0f / (1.0f + __expf(-g));
+            if (n < n_valid) args.h_out[(int64_t)(slot0 + n) * args.out_ld + feat] = __float2half_rn((g * sig) * u);
           }
-          ++xi;
         }
       } else {
         const int o0 = t.m_tile * 128;
@@ -567,6 +634,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(acc_empty);
     }
   }
+#ifdef UAII_UMMA_STATS
+  wstats.cyc[11] = (unsigned long long)(clock64() - t_kernel);
+  wstats.cnt[11] = 1;
+  for (int i = 0; i < 12; ++i)
+    if (wstats.cnt[i]) {
+      atomicAdd(&g_wait_cycles[i], wstats.cyc[i]);
+      atomicAdd(&g_wait_count[i], (unsigned long long)wstats.cnt[i]);
+    }
+
+#endif
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -740,6 +817,22 @@ cudaError_t launch_common(int fmt, bool gateup, const void* W0, const void* W1, 
 }
 
 }  // namespace
+
+#ifdef UAII_UMMA_STATS
+extern "C" __attribute__((visibility("default"))) int uaii_moe_debug_wait_stats(unsigned long long* cycles,
+                                                                                unsigned long long* counts,
+                                                                                int reset) {
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(cycles, g_wait_cycles, sizeof(g_wait_cycles));
+  cudaMemcpyFromSymbol(counts, g_wait_count, sizeof(g_wait_count));
+  if (reset) {
+    unsigned long long z[16] = {};
+    cudaMemcpyToSymbol(g_wait_cycles, z, sizeof(z));
+    cudaMemcpyToSymbol(g_wait_count, z, sizeof(z));
+  }
+  return 0;
+}
+#endif
 
 bool umma_format_supported(int fmt) { return chunk_elems(fmt) != 0; }
 

@@ -37,6 +37,8 @@ cudaError_t launch_identity_route(int32_t* buf, int64_t T, cudaStream_t st);
 cudaError_t launch_route_scan(int64_t T, int64_t E, int k, const RouteBuffers& rb,
                               cudaStream_t st);
 // Gathers x rows into expert-contiguous slots: xp_f32 and/or xp_f16 (either may be null).
+// xp_f16 rows are in the tensor-core operand order: elements [0, 2, 1, 3] of
+// every group of four (the expert GEMM builds its weight tiles the same way).
 cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E, int k,
                                 const RouteBuffers& rb, float* xp_f32, void* xp_f16,
                                 cudaStream_t st);
@@ -48,7 +50,7 @@ cudaError_t launch_combine(const float* out, int64_t out_ld, int splits, int64_t
                            int64_t T, int64_t D, int k, const RouteBuffers& rb,
                            const float* shared_out, int sh_splits, int64_t sh_split_stride,
                            const float* shared_gate, float* y, cudaStream_t st);
-// x rows -> f16 copy (shared-expert operand in token order)
+// x rows -> f16 copy (shared-expert operand in token order, tensor-core operand K order)
 cudaError_t launch_to_f16(const float* x, int64_t n, void* out, cudaStream_t st);
 // gate[t] = sigmoid(x[t] . w) with the reference GEMM summation order
 cudaError_t launch_shared_gate(const float* x, const float* w, int64_t T, int64_t D,

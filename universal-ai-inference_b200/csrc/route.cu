@@ -146,7 +146,7 @@ __global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int6
       for (int64_t i = lane; i < D; i += 32) {
         const float v = x[t * D + i];
         if (xp32) xp32[(int64_t)slot * D + i] = v;
-        if (xp16) xp16[(int64_t)slot * D + i] = __float2half_rn(v);
+        if (xp16) xp16[(int64_t)slot * D + ((i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1))] = __float2half_rn(v);
       }
       continue;
     }
@@ -154,10 +154,10 @@ __global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int6
     for (int64_t i = lane; i < D / 4; i += 32) {
       const float4 v = src[i];
       if (xp32) reinterpret_cast<float4*>(xp32 + (int64_t)slot * D)[i] = v;
-      if (xp16) {
+      if (xp16) {  // tensor-core operand order: [0, 2, 1, 3] inside each group of four
         __half2* d2 = reinterpret_cast<__half2*>(xp16 + (int64_t)slot * D) + 2 * i;
-        d2[0] = __floats2half2_rn(v.x, v.y);
-        d2[1] = __floats2half2_rn(v.z, v.w);
+        d2[0] = __floats2half2_rn(v.x, v.z);
+        d2[1] = __floats2half2_rn(v.y, v.w);
       }
     }
   }
@@ -226,9 +226,11 @@ __global__ void combine1_kernel(const float* __restrict__ out, int64_t ld, int s
   y[i] = acc;
 }
 
+// f16 copy in the tensor-core operand order ([0, 2, 1, 3] inside each group of
+// four consecutive elements; n is a multiple of 4)
 __global__ void to_f16_kernel(const float* __restrict__ x, int64_t n, __half* __restrict__ o) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i < n) o[i] = __float2half_rn(x[i]);
+  if (i < n) o[(i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1)] = __float2half_rn(x[i]);
 }
 
 // gate[t] = 1 / (1 + exp(-(x[t] . w))), one warp per token.

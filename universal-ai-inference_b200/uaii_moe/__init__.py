@@ -15,7 +15,7 @@ from ctypes import POINTER, c_char_p, c_double, c_float, c_int, c_int32, c_int64
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(os.path.dirname(_HERE), "libuaii_moe.so")
+LIB_PATH = os.environ.get("UAII_MOE_LIB") or os.path.join(os.path.dirname(_HERE), "libuaii_moe.so")
 
 # uaii::quant::QuantFormat values (include/uaii/quant/formats.hpp:10-29)
 F32, F16 = 0, 1
