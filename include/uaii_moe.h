@@ -215,6 +215,23 @@ UAII_MOE_API int uaii_moe_ffn_forward(uaii_moe_backend* b, const uaii_moe_layer*
  * libs/uaii-runtime/src/session.cpp:259-367). */
 UAII_MOE_API int uaii_moe_register_weights(uaii_moe_backend* b, const void* host_ptr, uint64_t bytes);
 
+/* The whole MoE FFN layer, like uaii_moe_ffn_forward, for callers that cannot
+ * allocate device memory (engines that pre-reserve HBM for their own pools,
+ * runtimes that own every allocation, decode loops that must not be stalled by
+ * the device-wide synchronization of cudaMalloc/cudaFree).  It allocates
+ * nothing: its scratch is one fixed 32 MiB array compiled into the library,
+ * held by every GPU that loads it until the process exits.  x, y, probs and all
+ * weights must be device memory of `device`; work runs on `stream` (a
+ * cudaStream_t, NULL for the default stream) and the call returns after it has
+ * finished.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress), so make it before any stream capture.  A call that
+ * needs more than 32 MiB of scratch returns UAII_MOE_INVALID_ARGUMENT.  All
+ * calls share the array; calls are serialized inside one process because
+ * overlapping GPU work on it would race.  No reference counterpart: the
+ * reference runs this operator only on the host. */
+UAII_MOE_API int uaii_moe_ffn_forward_noalloc(int device, void* stream, const uaii_moe_layer* layer,
+                                              const float* x, int64_t T, float* y, float* probs);
+
 /* Drop the device copy of a registered host weight buffer. */
 UAII_MOE_API int uaii_moe_release_weights(uaii_moe_backend* b, const void* host_ptr);
 

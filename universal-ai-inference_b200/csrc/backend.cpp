@@ -94,8 +94,32 @@ Error MoeCudaBackend::initialize(int device, cudaStream_t stream) {
   return Error::success();
 }
 
+Error MoeCudaBackend::attach_external(int device, cudaStream_t stream, void* scratch, size_t bytes) {
+  if (scratch == nullptr || bytes < 2 * kAlign)
+    return Error::make(ErrorCode::InvalidArgument, "external scratch too small");
+  UAII_CUDA(cudaSetDevice(device), "SetDevice");
+  device_ = device;
+  stream_ = stream;
+  own_stream_ = false;
+  external_ = true;
+  dev_err_ = static_cast<int*>(scratch);  // first 256 bytes: the error flag
+  ws_ = static_cast<char*>(scratch) + kAlign;
+  ws_cap_ = bytes - kAlign;
+  ws_used_ = 0;
+  return cuda_status(cudaMemsetAsync(dev_err_, 0, sizeof(int), stream_), "MemsetAsync(error flag)");
+}
+
 void MoeCudaBackend::shutdown() noexcept {
   if (device_ < 0) return;
+  if (external_) {  // nothing here is ours to free
+    if (stream_) (void)cudaStreamSynchronize(stream_);
+    ws_ = nullptr;
+    dev_err_ = nullptr;
+    ws_cap_ = ws_used_ = 0;
+    stream_ = nullptr;
+    device_ = -1;
+    return;
+  }
   (void)cudaSetDevice(device_);
   if (stream_) (void)cudaStreamSynchronize(stream_);
   for (auto& kv : weights_) (void)cudaFree(kv.second);
@@ -136,6 +160,10 @@ Error MoeCudaBackend::sync_and_check() {
 Error MoeCudaBackend::reserve(size_t bytes) {
   ws_used_ = 0;
   if (bytes <= ws_cap_) return Error::success();
+  if (external_)
+    return Error::make(ErrorCode::InvalidArgument, "call needs " + std::to_string(bytes) +
+                                                       " bytes of scratch; the fixed scratch holds " +
+                                                       std::to_string(ws_cap_));
   UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
   if (ws_) UAII_CUDA(cudaFree(ws_), "Free");
   ws_ = nullptr;
@@ -784,6 +812,27 @@ Error MoeCudaBackend::dispatch(const std::string& op_name, const std::string& /*
 
 }  // namespace uaii_b200
 
+bool uaii_b200::layer_args_from_c(const uaii_moe_layer* l, LayerArgs* out) {
+  LayerArgs& L = *out;
+  L.D = l->d_model; L.E = l->n_experts; L.I = l->d_ff;
+  L.top_k = l->top_k;
+  L.norm_topk = l->norm_topk;
+  L.router_w = l->router_w;
+  L.gate = ExpertWeights{l->gate_exps, l->gate_fmt, L.I, L.D};
+  L.up = ExpertWeights{l->up_exps, l->up_fmt, L.I, L.D};
+  L.down = ExpertWeights{l->down_exps, l->down_fmt, L.D, L.I};
+  if (!l->gate_exps || !l->up_exps || !l->down_exps) return false;
+  if (l->shared_d_ff > 0) {
+    if (!l->gate_shexp || !l->up_shexp || !l->down_shexp) return false;
+    L.I_sh = l->shared_d_ff;
+    L.gate_sh = ExpertWeights{l->gate_shexp, l->gate_shexp_fmt, L.I_sh, L.D};
+    L.up_sh = ExpertWeights{l->up_shexp, l->up_shexp_fmt, L.I_sh, L.D};
+    L.down_sh = ExpertWeights{l->down_shexp, l->down_shexp_fmt, L.D, L.I_sh};
+    L.gate_inp_sh = l->gate_inp_shexp;
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------------------
 // extern "C" shim (include/uaii_moe.h)
 using namespace uaii_b200;
@@ -794,11 +843,15 @@ struct uaii_moe_backend {
 
 namespace {
 thread_local std::string g_last_error;
+}  // namespace
 
-int report(const Error& e) {
+int uaii_b200::report_status(const Error& e) {
   g_last_error = e.ok() ? std::string() : e.message();
   return static_cast<int>(e.code());
 }
+
+namespace {
+int report(const Error& e) { return report_status(e); }
 
 int no_backend() { return report(Error::make(ErrorCode::InvalidArgument, "null backend")); }
 
@@ -897,24 +950,8 @@ int uaii_moe_ffn_forward(uaii_moe_backend* b, const uaii_moe_layer* l, const flo
   if (!b) return no_backend();
   if (!l) return report(Error::make(ErrorCode::InvalidArgument, "null layer"));
   LayerArgs L;
-  L.D = l->d_model; L.E = l->n_experts; L.I = l->d_ff;
-  L.top_k = l->top_k;
-  L.norm_topk = l->norm_topk;
-  L.router_w = l->router_w;
-  L.gate = ExpertWeights{l->gate_exps, l->gate_fmt, L.I, L.D};
-  L.up = ExpertWeights{l->up_exps, l->up_fmt, L.I, L.D};
-  L.down = ExpertWeights{l->down_exps, l->down_fmt, L.D, L.I};
-  if (!l->gate_exps || !l->up_exps || !l->down_exps)
+  if (!layer_args_from_c(l, &L))
     return report(Error::make(ErrorCode::InvalidArgument, "moe ffn: null expert weights"));
-  if (l->shared_d_ff > 0) {
-    if (!l->gate_shexp || !l->up_shexp || !l->down_shexp)
-      return report(Error::make(ErrorCode::InvalidArgument, "moe ffn: null shared-expert weights"));
-    L.I_sh = l->shared_d_ff;
-    L.gate_sh = ExpertWeights{l->gate_shexp, l->gate_shexp_fmt, L.I_sh, L.D};
-    L.up_sh = ExpertWeights{l->up_shexp, l->up_shexp_fmt, L.I_sh, L.D};
-    L.down_sh = ExpertWeights{l->down_shexp, l->down_shexp_fmt, L.D, L.I_sh};
-    L.gate_inp_sh = l->gate_inp_shexp;
-  }
   return report(b->impl.ffn(L, x, T, y, probs));
 }
 

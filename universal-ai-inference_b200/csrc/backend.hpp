@@ -19,6 +19,8 @@
 
 #include "kernels.hpp"
 
+struct uaii_moe_layer;
+
 namespace uaii_b200 {
 
 enum class ErrorCode {
@@ -93,6 +95,10 @@ class MoeCudaBackend {
  public:
   ~MoeCudaBackend() { shutdown(); }
   Error initialize(int device, cudaStream_t stream);
+  // Use caller-owned device memory as workspace and error flag, on the caller's
+  // stream: nothing is allocated and shutdown() frees nothing.  Weights and
+  // activations must then be device pointers.
+  Error attach_external(int device, cudaStream_t stream, void* scratch, size_t bytes);
   void shutdown() noexcept;
   Error synchronize();
 
@@ -134,6 +140,14 @@ class MoeCudaBackend {
                     const LayerArgs& L, const ExpertPlan& P, int64_t T, float* y_dev);
   Error sync_and_check();
 
+ public:
+  Error sync_and_check_public() {
+    std::lock_guard<std::mutex> lk(mu_);
+    return sync_and_check();
+  }
+
+ private:
+
   // phase timing: events recorded around each phase while profiling is on
   static constexpr int kPhases = 6;
   enum Phase { kRouter = 0, kRoute = 1, kGateUp = 2, kDown = 3, kShared = 4, kCombine = 5 };
@@ -158,6 +172,7 @@ class MoeCudaBackend {
   bool own_stream_ = false;
   int path_ = 0;
   int* dev_err_ = nullptr;
+  bool external_ = false;  // workspace and error flag belong to the caller
   char* ws_ = nullptr;
   size_t ws_cap_ = 0;
   size_t ws_used_ = 0;
@@ -166,6 +181,11 @@ class MoeCudaBackend {
 };
 
 bool is_device_ptr(const void* p) noexcept;
+// The C ABI layer description (include/uaii_moe.h) as LayerArgs; false if a
+// required expert weight pointer is null.
+bool layer_args_from_c(const struct uaii_moe_layer* l, LayerArgs* out);
+// Record `e` as this thread's last error (uaii_moe_last_error) and return its status code.
+int report_status(const Error& e);
 Error cuda_status(cudaError_t st, const char* what);
 
 }  // namespace uaii_b200

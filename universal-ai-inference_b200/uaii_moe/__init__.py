@@ -82,6 +82,8 @@ def _load():
                                             c_void_p, c_int, c_void_p, c_int64, c_int64, c_int64,
                                             c_int64, c_int, c_int, c_void_p]),
         "uaii_moe_ffn_forward": (c_int, [c_void_p, POINTER(Layer), c_void_p, c_int64, c_void_p, c_void_p]),
+        "uaii_moe_ffn_forward_noalloc": (c_int, [c_int, c_void_p, POINTER(Layer), c_void_p, c_int64, c_void_p,
+                                                 c_void_p]),
         "uaii_moe_register_weights": (c_int, [c_void_p, c_void_p, c_uint64]),
         "uaii_moe_release_weights": (c_int, [c_void_p, c_void_p]),
         "uaii_moe_set_expert_path": (c_int, [c_void_p, c_int]),
@@ -102,7 +104,8 @@ lib = _load()
 EXPORTED = ("uaii_moe_abi_version", "uaii_moe_last_error", "uaii_moe_backend_create",
             "uaii_moe_backend_destroy", "uaii_moe_synchronize", "uaii_moe_supports_op",
             "uaii_moe_dispatch", "uaii_moe_dequant_rows", "uaii_moe_router_f32",
-            "uaii_moe_experts_swiglu", "uaii_moe_ffn_forward", "uaii_moe_register_weights",
+            "uaii_moe_experts_swiglu", "uaii_moe_ffn_forward", "uaii_moe_ffn_forward_noalloc",
+            "uaii_moe_register_weights",
             "uaii_moe_release_weights",
             "uaii_moe_set_expert_path", "uaii_moe_profile_enable", "uaii_moe_profile_read",
             "uaii_moe_packed_nbytes", "uaii_moe_quantize_rows",
@@ -235,6 +238,12 @@ class Backend:
                 at[i] = Attr(k.encode(), ATTR_FLOAT, 0, float(v))
         _check(lib.uaii_moe_dispatch(self._h, op_name.encode(), op_version.encode(), ins, len(inputs),
                                      outs, len(outputs), at, len(attrs)))
+
+
+def ffn_forward_noalloc(device: int, stream, layer: Layer, x, T: int, y, probs=None):
+    """uaii_moe_ffn_forward_noalloc: the layer forward without any device allocation
+    (fixed scratch inside the library; all arrays must be on the device)."""
+    _check(lib.uaii_moe_ffn_forward_noalloc(device, stream, ctypes.byref(layer), ptr(x), T, ptr(y), ptr(probs)))
 
 
 def f32_desc(a, shape=None):
