@@ -6,19 +6,19 @@
 // (16..256), so a decode step with one token per expert still fills the
 // M = 128 tensor-core tile.
 //
-// Per CTA (persistent, one per SM, 10 warps):
-//   warp 0   TMA producer: packed GGUF weight windows (2-D uint8 tensor map,
-//            row pitch = packed row bytes, window start rounded down to 16 B)
-//            and f16 activation tiles (SWIZZLE_128B) into shared-memory rings;
+// Per CTA (persistent, one per SM, 19 warps):
+//   warp 0   TMA producer of packed GGUF weight windows (2-D uint8 tensor map,
+//            row pitch = packed row bytes, window start rounded down to 16 B);
 //   warp 1   TMEM allocation and the single MMA-issuing thread
 //            (tcgen05.mma kind::f16, A and B from shared memory, D in TMEM);
-//   warps 2-9 dequantize the packed window into the f16 A tile (K-major,
-//            SWIZZLE_128B canonical layout; two warps per 32 rows, each half of
-//            the 64-element K atom), then run the epilogue from TMEM, each
-//            warp group on half of the slot columns: SwiGLU for gate/up (rows
-//            0-63 gate, 64-127 up of the same 64 features) writing h in f16,
+//   warps 2-17 (four groups of four warps, each group covering all 128 rows)
+//            dequantize the packed window into f16 A tiles (K-major,
+//            SWIZZLE_128B canonical layout), one whole 64-element K atom per
+//            group at a time, then run the epilogue from TMEM, each group on a
+//            quarter of the slot columns: SwiGLU for gate/up writing h in f16,
 //            or f32 partial sums for down.  Consumer barriers take one elected
-//            arrival per warp.
+//            arrival per warp;
+//   warp 18  TMA producer of the f16 activation tiles (SWIZZLE_128B).
 // The weights are never repacked: blocks stay byte-identical to GGUF.  Each
 // dequantized operand is the GGUF value in f16: Q4_0 and Q8_0 exactly
 // fp16(round(d*q)); K-quants scale by fp16(d*sc), fp16(dmin*m).
@@ -59,8 +59,10 @@ __host__ __device__ constexpr int window_bytes(int bytes) {
   return ((w / 16) & 1) ? w : w + 16;
 }
 
-constexpr int kThreads = 352;  // warp 0 weight TMA, warp 1 MMA, warps 2-9 dequant + epilogue, warp 10 activation TMA
-constexpr int kDqWarps = 8;
+constexpr int kGroups = 4;                // dequant warp groups (4 warps = 128 rows each)
+constexpr int kDqWarps = 4 * kGroups;     // warps 2 .. 2+kDqWarps-1
+constexpr int kBWarp = 2 + kDqWarps;      // activation TMA producer warp
+constexpr int kThreads = 32 * (kBWarp + 1);
 constexpr int kAtomBytes = 128 * 128;  // 128 rows x 64 f16
 
 enum : int { kErrTimeoutProducer = 1, kErrTimeoutMma = 2, kErrTimeoutDequant = 3, kErrTimeoutEpilogue = 4 };
@@ -113,128 +115,111 @@ __device__ __forceinline__ void load_words(const uint8_t* row16, int q, uint32_t
 // tensor-core operands store elements in the order [0, 2, 1, 3] (both the
 // weight tile built here and the activation rows written by the gather and
 // the gate/up epilogue), which leaves every dot product unchanged and lets a
-// 32-bit word of packed bytes unpack with one shift and one LOP3 per pair.
-// the masked values (< 1024) of both 16-bit halves as f16 (1024 + v)
-__device__ __forceinline__ uint32_t lo_pairs(uint32_t w, uint32_t mask) { return (w & mask) | 0x64006400u; }
+// 32-bit word of packed bytes unpack with masks only: for a word w and
+// w8 = w >> 8, (w & 0x000F000F) holds the low nibbles of bytes (0, 2), (w8 & ...)
+// those of bytes (1, 3), and (w & 0x00F000F0) the high nibbles times 16.
+// OR-ing 0x6400 into a 16-bit half gives the f16 value 1024 + v exactly.
+constexpr uint32_t kMagic = 0x64006400u;
+__device__ __forceinline__ __half2 magic_pair(uint32_t w, uint32_t mask) { return as_h2((w & mask) | kMagic); }
 
-// 8 elements (two words of four 4-bit values at bit offset s) -> one 16-byte chunk
-__device__ __forceinline__ uint4 nib_chunk(uint32_t w0, uint32_t w1, int s, __half2 bias, __half2 d, __half2 nm,
-                                          bool fma) {
-  const uint32_t a[4] = {lo_pairs(w0 >> s, 0x000F000Fu), lo_pairs(w0 >> (s + 8), 0x000F000Fu),
-                         lo_pairs(w1 >> s, 0x000F000Fu), lo_pairs(w1 >> (s + 8), 0x000F000Fu)};
-  uint32_t r[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __half2 q = __hsub2(as_h2(a[i]), bias);
-    r[i] = as_u32(fma ? __hfma2(q, d, nm) : __hmul2(q, d));
-  }
-  return make_uint4(r[0], r[1], r[2], r[3]);
-}
+// An atom is 64 K elements = 32 words of two f16; word 4c + j belongs to the
+// 16-byte chunk c (elements 8c .. 8c+7).
+using AtomWords = uint32_t[32];
 
-// 8 elements from two words of four byte values -> one 16-byte chunk
-__device__ __forceinline__ uint4 byte_chunk(uint32_t w0, uint32_t w1, __half2 bias, __half2 d) {
-  const uint32_t a[4] = {lo_pairs(w0, 0x00FF00FFu), lo_pairs(w0 >> 8, 0x00FF00FFu), lo_pairs(w1, 0x00FF00FFu),
-                         lo_pairs(w1 >> 8, 0x00FF00FFu)};
-  uint32_t r[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) r[i] = as_u32(__hmul2(__hsub2(as_h2(a[i]), bias), d));
-  return make_uint4(r[0], r[1], r[2], r[3]);
-}
-
-// Q4_0 / Q8_0: one thread makes half of the 64-element atom (block h of the
-// two blocks in the chunk): four 16-byte chunks, chunks 4h..4h+3 of the atom.
-template <int F, int OFF>
-__device__ __forceinline__ void dequant_half(const uint8_t* row, int h, uint4 (&o)[4]);
-
-// Q4_0 block: {f16 d; u8 qs[16]}, low nibbles -> elements 0..15, high -> 16..31, (q - 8) * d
+// Q4_0: one 32-element block {f16 d; u8 qs[16]}: low nibbles -> elements 0..15,
+// high -> 16..31, value (q - 8) * d; writes words 16h .. 16h+15 of the atom.
 template <int OFF, int H>
-__device__ __forceinline__ void q4_0_block(const uint8_t* row, uint4 (&o)[4]) {
+__device__ __forceinline__ void q4_0_block(const uint8_t* row, uint32_t* out) {
   constexpr int kB = OFF + 18 * H;
   uint32_t w[5];
   load_words<kB % 16, 5>(row, kB / 16, w);  // bytes kB .. kB+19
   const __half dh = __ushort_as_half((unsigned short)(w[0] & 0xFFFFu));
   const __half2 d = __halves2half2(dh, dh);
-  const __half2 bias = __float2half2_rn(1032.f);  // 1024 + 8
-  uint32_t q[4];  // qs bytes 0..15
+  const __half2 lo_bias = __float2half2_rn(1032.f);  // 1024 + 8
+  const __half2 k16 = __float2half2_rn(0.0625f), hi_bias = __float2half2_rn(-72.f);  // (1024 + 16q)/16 - 72 = q - 8
 #pragma unroll
-  for (int i = 0; i < 4; ++i) q[i] = __funnelshift_r(w[i], w[i + 1], 16);
-  o[0] = nib_chunk(q[0], q[1], 0, bias, d, d, false);
-  o[1] = nib_chunk(q[2], q[3], 0, bias, d, d, false);
-  o[2] = nib_chunk(q[0], q[1], 4, bias, d, d, false);
-  o[3] = nib_chunk(q[2], q[3], 4, bias, d, d, false);
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t q = __funnelshift_r(w[i], w[i + 1], 16), q8 = q >> 8;  // qs bytes 4i .. 4i+3
+    uint32_t* lo = out + 16 * H + 4 * (i >> 1) + 2 * (i & 1);
+    uint32_t* hi = lo + 8;
+    lo[0] = as_u32(__hmul2(__hsub2(magic_pair(q, 0x000F000Fu), lo_bias), d));
+    lo[1] = as_u32(__hmul2(__hsub2(magic_pair(q8, 0x000F000Fu), lo_bias), d));
+    hi[0] = as_u32(__hmul2(__hfma2(magic_pair(q, 0x00F000F0u), k16, hi_bias), d));
+    hi[1] = as_u32(__hmul2(__hfma2(magic_pair(q8, 0x00F000F0u), k16, hi_bias), d));
+  }
 }
 
-// Q8_0 block: {f16 d; i8 qs[32]}, q * d
+// Q8_0: one 32-element block {f16 d; i8 qs[32]}: value q * d; words 16h .. 16h+15.
 template <int OFF, int H>
-__device__ __forceinline__ void q8_0_block(const uint8_t* row, uint4 (&o)[4]) {
+__device__ __forceinline__ void q8_0_block(const uint8_t* row, uint32_t* out) {
   constexpr int kB = OFF + 34 * H;
   uint32_t w[9];
   load_words<kB % 16, 9>(row, kB / 16, w);  // bytes kB .. kB+35
   const __half dh = __ushort_as_half((unsigned short)(w[0] & 0xFFFFu));
   const __half2 d = __halves2half2(dh, dh);
   const __half2 bias = __float2half2_rn(1152.f);  // 1024 + 128
-  uint32_t q[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) q[i] = __funnelshift_r(w[i], w[i + 1], 16) ^ 0x80808080u;  // int8 -> q + 128
-#pragma unroll
-  for (int c = 0; c < 4; ++c) o[c] = byte_chunk(q[2 * c], q[2 * c + 1], bias, d);
-}
-
-#define UAII_HALF_OFF(F, FN, O)                                                                    \
-  template <>                                                                                       \
-  __device__ __forceinline__ void dequant_half<F, O>(const uint8_t* r, int h, uint4(&o)[4]) {       \
-    h ? FN<O, 1>(r, o) : FN<O, 0>(r, o);                                                            \
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t q = __funnelshift_r(w[i], w[i + 1], 16) ^ 0x80808080u;  // int8 -> q + 128
+    out[16 * H + 2 * i] = as_u32(__hmul2(__hsub2(magic_pair(q, 0x00FF00FFu), bias), d));
+    out[16 * H + 2 * i + 1] = as_u32(__hmul2(__hsub2(magic_pair(q >> 8, 0x00FF00FFu), bias), d));
   }
-UAII_HALF_OFF(kQ4_0, q4_0_block, 0) UAII_HALF_OFF(kQ4_0, q4_0_block, 4)
-UAII_HALF_OFF(kQ4_0, q4_0_block, 8) UAII_HALF_OFF(kQ4_0, q4_0_block, 12)
-UAII_HALF_OFF(kQ8_0, q8_0_block, 0) UAII_HALF_OFF(kQ8_0, q8_0_block, 4)
-UAII_HALF_OFF(kQ8_0, q8_0_block, 8) UAII_HALF_OFF(kQ8_0, q8_0_block, 12)
-#undef UAII_HALF_OFF
+}
 
-// K-quants: one thread makes whole 64-element atoms of one super-block; the
-// super-block header is decoded once per chunk into a Header.
-struct Q4KHeader {
-  uint32_t y, z, w;  // the 12 scale bytes
-  float d, dmin;
-};
-__device__ __forceinline__ Q4KHeader q4_k_header(const uint8_t* blk) {
+template <int F, int OFF>
+__device__ __forceinline__ void dequant_block32_atom(const uint8_t* row, uint32_t* out) {
+  if constexpr (F == kQ4_0) {
+    q4_0_block<OFF, 0>(row, out);
+    q4_0_block<OFF, 1>(row, out);
+  } else {
+    q8_0_block<OFF, 0>(row, out);
+    q8_0_block<OFF, 1>(row, out);
+  }
+}
+
+// K-quants: the super-block header is decoded per atom from one 16-byte load.
+__device__ __forceinline__ float f16f(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)bits)); }
+
+// Q4_K atom `at` = qs[32*at .. +31]: low nibbles -> sub-block 2at (words 0..15),
+// high nibbles -> sub-block 2at+1 (words 16..31); value d*sc*q - dmin*m
+__device__ __forceinline__ void q4_k_atom(const uint8_t* blk, int at, uint32_t* out) {
   const uint4 hdr = *reinterpret_cast<const uint4*>(blk);  // d, dmin, scales[12]
-  return Q4KHeader{hdr.y, hdr.z, hdr.w, f16_bits_to_f32(hdr.x & 0xFFFFu), f16_bits_to_f32(hdr.x >> 16)};
-}
-// (scale, min) pair j with the get_scale_min_k4 bit layout, from registers
-__device__ __forceinline__ void q4_k_pair(const Q4KHeader& H, int j, __half2& d, __half2& nm) {
-  const int sh = 8 * (j & 3);
-  const uint32_t y = H.y >> sh, z = H.z >> sh, w4 = H.w >> sh;
-  const int sc = j < 4 ? (int)(y & 63u) : (int)((w4 & 15u) | (((y >> 6) & 3u) << 4));
-  const int m = j < 4 ? (int)(z & 63u) : (int)(((w4 >> 4) & 15u) | (((z >> 6) & 3u) << 4));
-  d = __float2half2_rn(H.d * (float)sc);
-  nm = __float2half2_rn(-(H.dmin * (float)m));
-}
-// atom `at` = qs[32*at .. +31]: low nibbles -> sub-block 2at, high -> 2at+1
-__device__ __forceinline__ void q4_k_atom(const uint8_t* blk, const Q4KHeader& H, int at, uint4 (&o)[8]) {
-  __half2 d0, n0, d1, n1;
-  q4_k_pair(H, 2 * at, d0, n0);
-  q4_k_pair(H, 2 * at + 1, d1, n1);
-  const __half2 bias = __float2half2_rn(1024.f);
+  const float d = f16f(hdr.x & 0xFFFFu), dmin = f16f(hdr.x >> 16);
+  __half2 dd[2], nm[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {  // (scale, min) pair j with the get_scale_min_k4 bit layout
+    const int j = 2 * at + h, sh = 8 * (j & 3);
+    const uint32_t y = hdr.y >> sh, z = hdr.z >> sh, w4 = hdr.w >> sh;
+    const int sc = j < 4 ? (int)(y & 63u) : (int)((w4 & 15u) | (((y >> 6) & 3u) << 4));
+    const int m = j < 4 ? (int)(z & 63u) : (int)(((w4 >> 4) & 15u) | (((z >> 6) & 3u) << 4));
+    dd[h] = __float2half2_rn(d * (float)sc);
+    nm[h] = __float2half2_rn(-(dmin * (float)m));
+  }
+  const __half2 k1024 = __float2half2_rn(1024.f);
+  const __half2 k16 = __float2half2_rn(0.0625f), km64 = __float2half2_rn(-64.f);  // (1024 + 16q)/16 - 64 = q
   const uint4* qp = reinterpret_cast<const uint4*>(blk + 16 + 32 * at);
   const uint4 qa = qp[0], qb = qp[1];
   const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    o[c] = nib_chunk(w[2 * c], w[2 * c + 1], 0, bias, d0, n0, true);
-    o[4 + c] = nib_chunk(w[2 * c], w[2 * c + 1], 4, bias, d1, n1, true);
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t q = w[i], q8 = q >> 8;
+    out[2 * i] = as_u32(__hfma2(__hsub2(magic_pair(q, 0x000F000Fu), k1024), dd[0], nm[0]));
+    out[2 * i + 1] = as_u32(__hfma2(__hsub2(magic_pair(q8, 0x000F000Fu), k1024), dd[0], nm[0]));
+    out[16 + 2 * i] = as_u32(__hfma2(__hfma2(magic_pair(q, 0x00F000F0u), k16, km64), dd[1], nm[1]));
+    out[16 + 2 * i + 1] = as_u32(__hfma2(__hfma2(magic_pair(q8, 0x00F000F0u), k16, km64), dd[1], nm[1]));
   }
 }
 
 // Q6_K super-block at even offset OFF: atom `at` covers quarters 2*(at&1) and
-// 2*(at&1)+1 of half (at>>1)
+// 2*(at&1)+1 of half (at>>1); value d*sc*(q - 32)
 template <int OFF>
-__device__ __forceinline__ void q6_k_atom(const uint8_t* row, float d, int at, uint4 (&o)[8]) {
+__device__ __forceinline__ void q6_k_atom(const uint8_t* row, int at, uint32_t* out) {
   const int n = at >> 1, hiq = at & 1;
   const int ns = hiq ? 4 : 0;
   uint32_t hw[8];
   load_words<OFF, 8>(row, 8 + 2 * n, hw);  // qh[32n .. +31]
   const int8_t* sc = reinterpret_cast<const int8_t*>(row + OFF + 192 + 8 * n);
+  const float d = f16f(ld_u16(row + OFF + 208));
   const __half2 bias = __float2half2_rn(1056.f);  // 1024 + 32
 #pragma unroll
   for (int qq = 0; qq < 2; ++qq) {
@@ -244,38 +229,38 @@ __device__ __forceinline__ void q6_k_atom(const uint8_t* row, float d, int at, u
     const __half2 s_lo = __float2half2_rn(d * (float)sc[2 * qt]);
     const __half2 s_hi = __float2half2_rn(d * (float)sc[2 * qt + 1]);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t q6[2];
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-        q6[j] = ((lw[2 * c + j] >> ns) & 0x0F0F0F0Fu) | (((hw[2 * c + j] >> (2 * qt)) & 0x03030303u) << 4);
-      o[4 * qq + c] = byte_chunk(q6[0], q6[1], bias, c < 2 ? s_lo : s_hi);
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t q6 = ((lw[i] >> ns) & 0x0F0F0F0Fu) | (((hw[i] >> (2 * qt)) & 0x03030303u) << 4);
+      const __half2 s = i < 4 ? s_lo : s_hi;
+      out[16 * qq + 2 * i] = as_u32(__hmul2(__hsub2(magic_pair(q6, 0x00FF00FFu), bias), s));
+      out[16 * qq + 2 * i + 1] = as_u32(__hmul2(__hsub2(magic_pair(q6 >> 8, 0x00FF00FFu), bias), s));
     }
   }
 }
 
-// Runtime (warp-uniform) chunk offset -> the specialised half decoder (Q4_0, Q8_0).
+// Runtime (warp-uniform) chunk offset -> the specialised decoder.
 template <int F>
-__device__ __forceinline__ void dequant_half_at(const uint8_t* row, int off, int h, uint4 (&o)[4]) {
-  switch (off) {
-    case 0: dequant_half<F, 0>(row, h, o); break;
-    case 4: dequant_half<F, 4>(row, h, o); break;
-    case 8: dequant_half<F, 8>(row, h, o); break;
-    default: dequant_half<F, 12>(row, h, o); break;
-  }
-}
-
-template <int F>
-__device__ __forceinline__ void q6_k_atom_at(const uint8_t* row, int off, float d, int at, uint4 (&o)[8]) {
-  switch (off) {
-    case 0: q6_k_atom<0>(row, d, at, o); break;
-    case 2: q6_k_atom<2>(row, d, at, o); break;
-    case 4: q6_k_atom<4>(row, d, at, o); break;
-    case 6: q6_k_atom<6>(row, d, at, o); break;
-    case 8: q6_k_atom<8>(row, d, at, o); break;
-    case 10: q6_k_atom<10>(row, d, at, o); break;
-    case 12: q6_k_atom<12>(row, d, at, o); break;
-    default: q6_k_atom<14>(row, d, at, o); break;
+__device__ __forceinline__ void dequant_atom(const uint8_t* row, int off, int at, uint32_t* out) {
+  if constexpr (F == kQ4_K) {
+    q4_k_atom(row, at, out);
+  } else if constexpr (F == kQ6_K) {
+    switch (off) {
+      case 0: q6_k_atom<0>(row, at, out); break;
+      case 2: q6_k_atom<2>(row, at, out); break;
+      case 4: q6_k_atom<4>(row, at, out); break;
+      case 6: q6_k_atom<6>(row, at, out); break;
+      case 8: q6_k_atom<8>(row, at, out); break;
+      case 10: q6_k_atom<10>(row, at, out); break;
+      case 12: q6_k_atom<12>(row, at, out); break;
+      default: q6_k_atom<14>(row, at, out); break;
+    }
+  } else {  // Q4_0, Q8_0: chunk offsets are multiples of 4
+    switch (off) {
+      case 0: dequant_block32_atom<F, 0>(row, out); break;
+      case 4: dequant_block32_atom<F, 4>(row, out); break;
+      case 8: dequant_block32_atom<F, 8>(row, out); break;
+      default: dequant_block32_atom<F, 12>(row, out); break;
+    }
   }
 }
 
@@ -351,16 +336,25 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
 
 template <int F, int BN, int A_ST, int B_ST, int P_ST>
 struct Cfg {
+  // Slot tiles up to 128 wide keep the A ring in TMEM (32 columns per atom
+  // stage, next to the two accumulators); 256-wide tiles need all 512 columns
+  // for the accumulators and keep A in shared memory.
+  static constexpr bool kTmemA = BN <= 128;
   static constexpr int kWB = window_bytes(Fmt<F>::kBytes);
   static constexpr int kPStage = 128 * kWB;
   static constexpr int kBStage = BN * 128;
   static constexpr int kOffA = 0;
-  static constexpr int kOffB = kOffA + A_ST * kAtomBytes;
+  static constexpr int kOffB = kOffA + (kTmemA ? 0 : A_ST * kAtomBytes);
   static constexpr int kOffP = kOffB + B_ST * kBStage;
   static constexpr int kOffBar = kOffP + P_ST * kPStage;
-  static constexpr int kNumBars = 2 * (P_ST + A_ST + B_ST) + 2 + 1;
+  static constexpr int kNumBars = 2 * (P_ST + A_ST + B_ST) + 4 + 1;
   static constexpr int kSmem = kOffBar + kNumBars * 8 + 16 + 1024;  // + alignment slack
-  static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+  static constexpr uint32_t kAccCols = BN < 32 ? 32 : BN;  // one accumulator
+  static constexpr uint32_t kACol0 = 2 * kAccCols;          // first A column (TMEM A)
+  static constexpr uint32_t kUsedCols = kACol0 + (kTmemA ? A_ST * 32 : 0);
+  static constexpr uint32_t kTmemCols = kUsedCols <= 32 ? 32 : kUsedCols <= 64 ? 64 : kUsedCols <= 128 ? 128
+                                      : kUsedCols <= 256 ? 256 : 512;
+  static_assert(kUsedCols <= 512, "tensor memory budget");
 };
 
 template <int F, int BN, int A_ST, int B_ST, int P_ST>
@@ -381,9 +375,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* a_empty = a_full + A_ST;
   uint64_t* b_full = a_empty + A_ST;
   uint64_t* b_empty = b_full + B_ST;
-  uint64_t* acc_full = b_empty + B_ST;
-  uint64_t* acc_empty = acc_full + 1;
-  uint64_t* mma_done = acc_empty + 1;
+  uint64_t* acc_full = b_empty + B_ST;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* mma_done = acc_empty + 2;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
@@ -394,13 +388,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
   if (threadIdx.x == 0) {
     // consumer-side barriers count one elected lane per dequant warp
-    for (int i = 0; i < P_ST; ++i) { mbar_init(pk_full + i, 1); mbar_init(pk_empty + i, kDqWarps); }
-    // K-quant atoms are written whole by one warp group (4 warps), 32-element-block
-    // atoms in halves by both groups (8 warps)
-    for (int i = 0; i < A_ST; ++i) { mbar_init(a_full + i, kAtoms == 4 ? 4 : kDqWarps); mbar_init(a_empty + i, 1); }
+    // a K-quant chunk is read by every group (one atom each); a 32-element-block
+    // chunk (one atom) by one group
+    for (int i = 0; i < P_ST; ++i) { mbar_init(pk_full + i, 1); mbar_init(pk_empty + i, kAtoms == 4 ? kDqWarps : 4); }
+    static_assert(kAtoms == 4 || P_ST % kGroups == 0, "32-element-block windows: stages owned per group");
+    static_assert(A_ST % kGroups == 0, "A stages owned per group");
+    // every atom is written whole by one warp group (4 warps)
+    for (int i = 0; i < A_ST; ++i) { mbar_init(a_full + i, 4); mbar_init(a_empty + i, 1); }
     for (int i = 0; i < B_ST; ++i) { mbar_init(b_full + i, 1); mbar_init(b_empty + i, 1); }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, kDqWarps);
+    for (int b = 0; b < 2; ++b) { mbar_init(acc_full + b, 1); mbar_init(acc_empty + b, kDqWarps); }
     mbar_init(mma_done, 1);
     *s_abort = 0;
     fence_barrier_init();
@@ -448,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         (void)mbar_wait(pk_full + j % P_ST, (j / P_ST) & 1);
     }
     __syncwarp();
-  } else if (warp == 10) {
+  } else if (warp == kBWarp) {
     // ------------------------------------------------------------ activation TMA producer
     if (lane == 0) {
       uint32_t bi = 0;
@@ -480,8 +476,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
         const Tile t = decode_tile(args, tile, BN);
         const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
-        if (!(ok = wait_bar(acc_empty, (it & 1) ^ 1, s_abort, err, kErrTimeoutMma, 2 UAII_WS_ARG))) break;
+        const uint32_t ab = it & 1;  // accumulator buffer of this tile
+        if (!(ok = wait_bar(acc_empty + ab, ((it >> 1) & 1) ^ 1, s_abort, err, kErrTimeoutMma, 2 UAII_WS_ARG))) break;
         tc_fence_after();
+        const uint32_t dacc = tmem + ab * C::kAccCols;
         uint32_t acc = 0;
         for (int c = c0; c < c1 && ok; ++c) {
           for (int at = 0; at < kAtoms; ++at) {
@@ -489,12 +487,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!(ok = wait_bar(a_full + as, (ai / A_ST) & 1, s_abort, err, kErrTimeoutMma, 3 UAII_WS_ARG))) break;
             if (!(ok = wait_bar(b_full + bs, (bi / B_ST) & 1, s_abort, err, kErrTimeoutMma, 4 UAII_WS_ARG))) break;
             tc_fence_after();
-            const uint64_t ad = sw128_desc(smem_u32(sA + as * kAtomBytes));
             const uint64_t bd = sw128_desc(smem_u32(sB + bs * C::kBStage));
+            if constexpr (C::kTmemA) {
+              const uint32_t at_col = tmem + C::kACol0 + as * 32;  // 8 columns per 16 K elements
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-              mma_f16(tmem, ad + 2 * ks, bd + 2 * ks, idesc, acc);
-              acc = 1;
+              for (int ks = 0; ks < 4; ++ks) {
+                mma_f16_ts(dacc, at_col + 8 * ks, bd + 2 * ks, idesc, acc);
+                acc = 1;
+              }
+            } else {
+              const uint64_t ad = sw128_desc(smem_u32(sA + as * kAtomBytes));
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks) {
+                mma_f16(dacc, ad + 2 * ks, bd + 2 * ks, idesc, acc);
+                acc = 1;
+              }
             }
             mma_commit(a_empty + as);
             mma_commit(b_empty + bs);
@@ -502,18 +509,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++bi;
           }
         }
-        if (ok) mma_commit(acc_full);
+        if (ok) mma_commit(acc_full + ab);
       }
       // the tensor core must be idle before TMEM is freed
       mma_commit(mma_done);
       (void)mbar_wait(mma_done, 0);
     }
     __syncwarp();
-  } else if (warp >= 2 && warp < 10) {
-    // ------------------------------------------------------------ dequant + epilogue (256 threads)
+  } else if (warp >= 2 && warp < kBWarp) {
+    // ------------------------------------------------------------ dequant + epilogue (kDqWarps warps)
     const int q = warp & 3;            // TMEM lane quarter this warp may access
     const int row = 32 * q + lane;     // A-tile row == accumulator lane
-    const int grp = (warp - 2) >> 2;   // 0: warps 2-5, 1: warps 6-9 (each row has one of each)
+    const int grp = (warp - 2) >> 2;   // warp group 0..kGroups-1; each group covers all 128 rows
     // Gate/up tiles hold 64 features: in every 32-row block (one TMEM lane
     // quarter) lanes 0-15 are gate rows and lanes 16-31 the up rows of the same
     // 16 features, so the SwiGLU epilogue pairs them with one lane shuffle.
@@ -521,91 +528,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int src_row = args.gateup ? (lane < 16 ? 16 * q + lane : 64 + 16 * q + (lane - 16)) : row;
     uint32_t pi = 0, ai = 0, it = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
-      const Tile t = decode_tile(args, tile, BN);
-      const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
-      for (int c = c0; c < c1 && ok; ++c) {
-        const int ps = pi % P_ST;
-        if (!(ok = wait_bar(pk_full + ps, (pi / P_ST) & 1, s_abort, err, kErrTimeoutDequant, 5 UAII_WS_ARG))) break;
-        const uint8_t* rowp = sP + ps * C::kPStage + src_row * C::kWB;
-        const int off = (c * Fmt<F>::kBytes) & 15;
-        if constexpr (kAtoms == 4) {
-          // this warp group makes atoms grp and grp + 2 of the super-block
-          Q4KHeader h4{};
-          float d6 = 0.f;
-          if constexpr (F == kQ4_K) h4 = q4_k_header(rowp);
-          else d6 = f16_bits_to_f32(ld_u16(rowp + off + 208));
-          for (int k = 0; k < 2 && ok; ++k) {
-            const int at = grp + 2 * k;
-            const uint32_t aidx = ai + at;
-            const int as = aidx % A_ST;
-            if (!(ok = wait_bar(a_empty + as, ((aidx / A_ST) & 1) ^ 1, s_abort, err, kErrTimeoutDequant, 6 UAII_WS_ARG)))
-              break;
-            uint4 o[8];
-#ifdef UAII_UMMA_STATS
-            const long long tq = clock64();
-#endif
-            if constexpr (F == kQ4_K) q4_k_atom(rowp, h4, at, o);
-            else q6_k_atom_at<F>(rowp, off, d6, at, o);
-#ifdef UAII_UMMA_STATS
-            asm volatile("" ::"r"(o[0].x), "r"(o[3].y), "r"(o[5].z), "r"(o[7].w));
-            wstats.cyc[10] += (unsigned long long)(clock64() - tq);
-            wstats.cnt[10] += 1;
-#endif
-            uint8_t* arow = sA + as * kAtomBytes + row * 128;
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) *reinterpret_cast<uint4*>(arow + ((cc ^ (row & 7)) << 4)) = o[cc];
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(a_full + as);
-          }
-          ai += kAtoms;
-        } else {
-          const int as = ai % A_ST;
-          if (!(ok = wait_bar(a_empty + as, ((ai / A_ST) & 1) ^ 1, s_abort, err, kErrTimeoutDequant, 6 UAII_WS_ARG)))
-            break;
-          uint4 o[4];
-#ifdef UAII_UMMA_STATS
-          const long long tq = clock64();
-#endif
-          dequant_half_at<F>(rowp, off, grp, o);
-#ifdef UAII_UMMA_STATS
-          asm volatile("" ::"r"(o[0].x), "r"(o[1].y), "r"(o[2].z), "r"(o[3].w));
-          wstats.cyc[10] += (unsigned long long)(clock64() - tq);
-          wstats.cnt[10] += 1;
-#endif
-          uint8_t* arow = sA + as * kAtomBytes + row * 128;
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc)
-            *reinterpret_cast<uint4*>(arow + (((4 * grp + cc) ^ (row & 7)) << 4)) = o[cc];
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(a_full + as);
-          ++ai;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(pk_empty + ps);
-        ++pi;
-      }
-      if (!ok) break;
-      // ---- epilogue: group `grp` owns accumulator columns [grp*BN/2, (grp+1)*BN/2)
-      if (!(ok = wait_bar(acc_full, it & 1, s_abort, err, kErrTimeoutEpilogue, 7 UAII_WS_ARG))) break;
+    // Epilogue of tile number `e_it` (accumulator buffer e_it & 1), run after the
+    // next tile's dequantization has been issued so that the tensor core keeps
+    // working while the accumulator is drained.
+    auto epilogue = [&](const Tile& t, uint32_t e_it) -> bool {
+      // group `grp` owns accumulator columns [grp*BN/kGroups, (grp+1)*BN/kGroups)
+      if (!wait_bar(acc_full + (e_it & 1), (e_it >> 1) & 1, s_abort, err, kErrTimeoutEpilogue, 7 UAII_WS_ARG))
+        return false;
       tc_fence_after();
       const int n_valid = min(BN, __ldg(args.counts + t.e) - t.n_tile * BN);
       const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
-      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
-      constexpr int kHalf = BN / 2;
+      const uint32_t taddr = tmem + (e_it & 1) * C::kAccCols + ((uint32_t)(32 * q) << 16);
+      constexpr int kCols = BN / kGroups;          // columns per group (>= 4)
+      constexpr int kW = kCols >= 8 ? 8 : 4;       // columns per TMEM load
       if (args.gateup) {
         // lane l < 16 holds gate, lane l + 16 up of feature i0 + 16q + (l & 15); each
         // column pair (n, n+1) is split: the gate lane finishes n, the up lane n + 1
         const int feat = k_perm(t.m_tile * 64 + 16 * q + (lane & 15));
         const bool gate_lane = lane < 16;
-        for (int cb = grp * kHalf; cb < (grp + 1) * kHalf; cb += 8) {
+        for (int cb = grp * kCols; cb < (grp + 1) * kCols; cb += kW) {
           uint32_t r[8];
-          tmem_ld8(taddr + cb, r);
+          if constexpr (kW == 8) tmem_ld8(taddr + cb, r);
+          else tmem_ld4(taddr + cb, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 8; j += 2) {
+          for (int j = 0; j < kW; j += 2) {
             const float mine0 = __uint_as_float(r[j]), mine1 = __uint_as_float(r[j + 1]);
             const float other = __shfl_xor_sync(0xffffffffu, gate_lane ? mine1 : mine0, 16);
             const float g = gate_lane ? mine0 : other;  // column n (gate lane) or n + 1 (up lane)
@@ -618,12 +565,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         const int o0 = t.m_tile * 128;
         float* out = args.out + (int64_t)t.split * args.split_stride;
-        for (int cb = grp * kHalf; cb < (grp + 1) * kHalf; cb += 8) {
+        for (int cb = grp * kCols; cb < (grp + 1) * kCols; cb += kW) {
           uint32_t r[8];
-          tmem_ld8(taddr + cb, r);
+          if constexpr (kW == 8) tmem_ld8(taddr + cb, r);
+          else tmem_ld4(taddr + cb, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
+          for (int j = 0; j < kW; ++j) {
             const int n = cb + j;
             if (n < n_valid) out[(int64_t)(slot0 + n) * args.out_ld + o0 + row] = __uint_as_float(r[j]);
           }
@@ -631,8 +579,62 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
+      if (lane == 0) mbar_arrive(acc_empty + (e_it & 1));
+      return true;
+    };
+    Tile prev{};
+    bool have_prev = false;
+    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
+      const Tile t = decode_tile(args, tile, BN);
+      const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
+      for (int c = c0; c < c1 && ok; ++c, ++pi) {
+        const int ps = pi % P_ST;
+        // K-quants: group g makes atom g of every super-block.  32-element blocks:
+        // the chunk is one atom, made by group (chunk counter % kGroups).
+        const int at = kAtoms == 4 ? grp : 0;
+        const uint32_t aidx = kAtoms == 4 ? ai + grp : ai;
+        ai += kAtoms;
+        if (kAtoms == 1 && (int)(pi % kGroups) != grp) continue;
+        if (!(ok = wait_bar(pk_full + ps, (pi / P_ST) & 1, s_abort, err, kErrTimeoutDequant, 5 UAII_WS_ARG))) break;
+        const uint8_t* rowp = sP + ps * C::kPStage + src_row * C::kWB;
+        const int off = (c * Fmt<F>::kBytes) & 15;
+        const int as = aidx % A_ST;
+        if (!(ok = wait_bar(a_empty + as, ((aidx / A_ST) & 1) ^ 1, s_abort, err, kErrTimeoutDequant, 6 UAII_WS_ARG)))
+          break;
+        uint32_t o[32];
+#ifdef UAII_UMMA_STATS
+        const long long tq = clock64();
+#endif
+        dequant_atom<F>(rowp, off, at, o);
+#ifdef UAII_UMMA_STATS
+        asm volatile("" ::"r"(o[0]), "r"(o[13]), "r"(o[22]), "r"(o[31]));
+        wstats.cyc[10] += (unsigned long long)(clock64() - tq);
+        wstats.cnt[10] += 1;
+#endif
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pk_empty + ps);  // the window has been read
+        if constexpr (C::kTmemA) {
+          tc_fence_after();  // after the MMA that last read this stage (a_empty)
+          tmem_st32(tmem + C::kACol0 + as * 32 + ((uint32_t)(32 * q) << 16), o);
+          tmem_st_wait();
+          tc_fence_before();
+        } else {
+          uint8_t* arow = sA + as * kAtomBytes + row * 128;
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc)
+            *reinterpret_cast<uint4*>(arow + ((cc ^ (row & 7)) << 4)) =
+                make_uint4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]);
+          fence_proxy_async_smem();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(a_full + as);
+      }
+      if (!ok) break;
+      if (have_prev && !(ok = epilogue(prev, it - 1))) break;
+      prev = t;
+      have_prev = true;
     }
+    if (ok && have_prev) (void)epilogue(prev, it - 1);
   }
 #ifdef UAII_UMMA_STATS
   wstats.cyc[11] = (unsigned long long)(clock64() - t_kernel);
@@ -736,15 +738,50 @@ cudaError_t run_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtenso
   return cudaGetLastError();
 }
 
+// Ring depths per (format, slot tile).  Every ring that one warp group can run
+// ahead on has a depth that is a multiple of kGroups, so each stage is always
+// filled (A tiles) or consumed (32-element-block packed windows) by the same
+// group and no waiter is ever more than one barrier phase ahead.  Packed
+// stages: deeper at decode widths (HBM latency); activation stages; then as
+// many A stages (4 or 8) as the shared-memory budget leaves.
+template <int F, int BN>
+struct Stages {
+  static constexpr bool kTmemA = BN <= 128;
+  static constexpr int kWB = window_bytes(Fmt<F>::kBytes);
+  static constexpr int kBudget = 224 * 1024;  // stage bytes; barriers and alignment slack come on top
+  static constexpr bool kBlock32 = Fmt<F>::kAtoms == 1;
+  static constexpr int B0 = BN <= 16 ? 8 : 4;
+  // TMEM A: 8 A stages in tensor memory, shared memory goes to the weight ring
+  static constexpr int P_fit = (kBudget - B0 * BN * 128) / (128 * kWB);
+  static constexpr int P_t = P_fit > 8 ? 8 : P_fit;
+  static constexpr int P_tmem = kBlock32 ? (P_t >= 8 ? 8 : 4) : P_t;
+  // shared-memory A (256-wide tiles)
+  static constexpr int P_smem = kBlock32 ? 4 : 2;
+  static constexpr int kP = P_smem * 128 * kWB;
+  static constexpr int B_smem = (kP + B0 * BN * 128 + 4 * kAtomBytes <= kBudget) ? B0 : 3;
+  static constexpr int A_fit = (kBudget - kP - B_smem * BN * 128) / kAtomBytes;
+  static constexpr int P = kTmemA ? P_tmem : P_smem;
+  static constexpr int B = kTmemA ? B0 : B_smem;
+  static constexpr int A = kTmemA ? 8 : (A_fit >= 8 ? 8 : 4);
+  static_assert(kTmemA ? P >= 2 : A_fit >= 4, "shared-memory budget");
+};
+
+template <int F, int BN>
+cudaError_t run_cfg(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x, const Args& a,
+                    cudaStream_t st) {
+  using S = Stages<F, BN>;
+  return run_gemm<F, BN, S::A, S::B, S::P>(w0, w1, x, a, st);
+}
+
 template <int F>
 cudaError_t dispatch_bn(int bn, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
                         const Args& a, cudaStream_t st) {
   switch (bn) {
-    case 16: return run_gemm<F, 16, 4, 8, 4>(w0, w1, x, a, st);
-    case 32: return run_gemm<F, 32, 4, 8, 4>(w0, w1, x, a, st);
-    case 64: return run_gemm<F, 64, 4, 4, 3>(w0, w1, x, a, st);
-    case 128: return run_gemm<F, 128, 4, 4, 2>(w0, w1, x, a, st);
-    case 256: return run_gemm<F, 256, 3, 3, 2>(w0, w1, x, a, st);
+    case 16: return run_cfg<F, 16>(w0, w1, x, a, st);
+    case 32: return run_cfg<F, 32>(w0, w1, x, a, st);
+    case 64: return run_cfg<F, 64>(w0, w1, x, a, st);
+    case 128: return run_cfg<F, 128>(w0, w1, x, a, st);
+    case 256: return run_cfg<F, 256>(w0, w1, x, a, st);
     default: return cudaErrorInvalidValue;
   }
 }
