@@ -3,21 +3,27 @@
 // One launch computes every (expert, weight-row tile, slot tile[, K split]) of
 // one projection:  C[row, slot] = sum_k W_e[row, k] * X[slot, k]  with the
 // weight rows as the MMA M dimension (128) and the expert's routed slots as N
-// (16..256), so a decode step with one token per expert still fills the
+// (16..128), so a decode step with one token per expert still fills the
 // M = 128 tensor-core tile.
+//
+// The K loop runs in quads of 256 elements (one K-quant super-block, eight
+// 32-element blocks): one packed-window stage, one activation stage and one
+// A stage per quad, so the single MMA-issuing thread waits on two barriers and
+// commits once per 16 MMAs.  Narrow MMAs are bound by how fast one thread can
+// issue them, and every barrier wait on that thread's path costs as much as
+// several MMAs.
 //
 // Per CTA (persistent, one per SM, 19 warps):
 //   warp 0   TMA producer of packed GGUF weight windows (2-D uint8 tensor map,
 //            row pitch = packed row bytes, window start rounded down to 16 B);
-//   warp 1   TMEM allocation and the single MMA-issuing thread
-//            (tcgen05.mma kind::f16, A and B from shared memory, D in TMEM);
+//   warp 1   TMEM allocation and the MMA-issuing thread (tcgen05.mma kind::f16,
+//            A from tensor memory, B from shared memory, D in tensor memory);
 //   warps 2-17 (four groups of four warps, each group covering all 128 rows)
-//            dequantize the packed window into f16 A tiles (K-major,
-//            SWIZZLE_128B canonical layout), one whole 64-element K atom per
-//            group at a time, then run the epilogue from TMEM, each group on a
-//            quarter of the slot columns: SwiGLU for gate/up writing h in f16,
-//            or f32 partial sums for down.  Consumer barriers take one elected
-//            arrival per warp;
+//            dequantize: group g turns 64-element atom g of every quad into f16
+//            and stores it into the quad's A stage in tensor memory; then they
+//            run the epilogue from TMEM, each group on a quarter of the slot
+//            columns: SwiGLU for gate/up writing h in f16, or f32 partial sums
+//            for down.  Consumer barriers take one elected arrival per warp;
 //   warp 18  TMA producer of the f16 activation tiles (SWIZZLE_128B).
 // The weights are never repacked: blocks stay byte-identical to GGUF.  Each
 // dequantized operand is the GGUF value in f16: Q4_0 and Q8_0 exactly
@@ -38,32 +44,26 @@ namespace {
 
 using namespace umma;
 
-// K chunk per packed-window load: one K-quant super-block (256) or two
-// 32-element blocks (64).  kBytes = packed bytes of one chunk of one row.
-template <int F> struct Fmt;
-template <> struct Fmt<kQ4_0> { static constexpr int kChunk = 64, kAtoms = 1, kBytes = 36; };
-template <> struct Fmt<kQ8_0> { static constexpr int kChunk = 64, kAtoms = 1, kBytes = 68; };
-template <> struct Fmt<kQ4_K> { static constexpr int kChunk = 256, kAtoms = 4, kBytes = 144; };
-template <> struct Fmt<kQ6_K> { static constexpr int kChunk = 256, kAtoms = 4, kBytes = 210; };
+constexpr int kQuadK = 256;  // K elements per quad = 4 atoms of 64
 
-// Bytes of the 16-byte-aligned window that holds any chunk of a row, rounded
-// up to an odd number of 16-byte units: rows of the packed stage then start in
-// different 16-byte bank groups, so eight lanes reading eight rows with 16-byte
-// loads never collide.
-__host__ __device__ constexpr int window_bytes(int bytes) {
-  int w = 0;
-  for (int c = 0; c < 16; ++c) {
-    const int x = ((((c * bytes) & 15) + bytes) + 15) & ~15;
-    w = x > w ? x : w;
-  }
-  return ((w / 16) & 1) ? w : w + 16;
-}
+// Packed bytes of one quad of one row (kBytes), and the TMA boxes that carry a
+// quad's window: kBoxes boxes of kBoxBytes (<= 256, the TMA box limit), box j
+// starting 128 * j bytes after the 16-byte-aligned window start.  kBoxBytes
+// is an odd number of 16-byte units, so rows of a packed stage start in
+// different 16-byte bank groups and eight lanes reading eight rows with
+// 16-byte loads never collide.  Q4_0 / Q8_0 rows may end in a partial quad
+// (K a multiple of 64); K-quant rows hold whole super-blocks.
+template <int F> struct Fmt;
+template <> struct Fmt<kQ4_0> { static constexpr int kBytes = 144, kBoxes = 1, kBoxBytes = 144, kMinK = 64; };
+template <> struct Fmt<kQ8_0> { static constexpr int kBytes = 272, kBoxes = 2, kBoxBytes = 144, kMinK = 64; };
+template <> struct Fmt<kQ4_K> { static constexpr int kBytes = 144, kBoxes = 1, kBoxBytes = 144, kMinK = 256; };
+template <> struct Fmt<kQ6_K> { static constexpr int kBytes = 210, kBoxes = 1, kBoxBytes = 240, kMinK = 256; };
 
 constexpr int kGroups = 4;                // dequant warp groups (4 warps = 128 rows each)
 constexpr int kDqWarps = 4 * kGroups;     // warps 2 .. 2+kDqWarps-1
 constexpr int kBWarp = 2 + kDqWarps;      // activation TMA producer warp
-constexpr int kThreads = 32 * (kBWarp + 1);
-constexpr int kAtomBytes = 128 * 128;  // 128 rows x 64 f16
+constexpr int kMma1Warp = kBWarp + 1;     // second MMA-issuing warp (slot tiles up to 64 wide)
+constexpr int kThreads = 32 * (kMma1Warp + 1);
 
 enum : int { kErrTimeoutProducer = 1, kErrTimeoutMma = 2, kErrTimeoutDequant = 3, kErrTimeoutEpilogue = 4 };
 
@@ -71,7 +71,10 @@ struct Args {
   const int32_t* counts;
   const int32_t* offsets;
   const int32_t* tile_base;  // [E+1]
-  int E, m_tiles, splits, kchunks, rows_per_expert, gateup;
+  int E, m_tiles, splits;
+  int kquads;   // quads per row: ceil(K / 256)
+  int k_atoms;  // 64-element atoms per row: K / 64
+  int rows_per_expert, gateup;
   __half* h_out;  // gate/up: [S, out_ld] f16
   float* out;     // down: [splits][S][out_ld] f32
   int64_t out_ld, split_stride;
@@ -180,15 +183,16 @@ __device__ __forceinline__ void dequant_block32_atom(const uint8_t* row, uint32_
 // K-quants: the super-block header is decoded per atom from one 16-byte load.
 __device__ __forceinline__ float f16f(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)bits)); }
 
-// Q4_K atom `at` = qs[32*at .. +31]: low nibbles -> sub-block 2at (words 0..15),
-// high nibbles -> sub-block 2at+1 (words 16..31); value d*sc*q - dmin*m
-__device__ __forceinline__ void q4_k_atom(const uint8_t* blk, int at, uint32_t* out) {
+// Q4_K atom AT = qs[32*AT .. +31]: low nibbles -> sub-block 2AT (words 0..15),
+// high nibbles -> sub-block 2AT+1 (words 16..31); value d*sc*q - dmin*m
+template <int AT>
+__device__ __forceinline__ void q4_k_atom(const uint8_t* blk, uint32_t* out) {
   const uint4 hdr = *reinterpret_cast<const uint4*>(blk);  // d, dmin, scales[12]
   const float d = f16f(hdr.x & 0xFFFFu), dmin = f16f(hdr.x >> 16);
   __half2 dd[2], nm[2];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {  // (scale, min) pair j with the get_scale_min_k4 bit layout
-    const int j = 2 * at + h, sh = 8 * (j & 3);
+    const int j = 2 * AT + h, sh = 8 * (j & 3);
     const uint32_t y = hdr.y >> sh, z = hdr.z >> sh, w4 = hdr.w >> sh;
     const int sc = j < 4 ? (int)(y & 63u) : (int)((w4 & 15u) | (((y >> 6) & 3u) << 4));
     const int m = j < 4 ? (int)(z & 63u) : (int)(((w4 >> 4) & 15u) | (((z >> 6) & 3u) << 4));
@@ -197,7 +201,7 @@ __device__ __forceinline__ void q4_k_atom(const uint8_t* blk, int at, uint32_t* 
   }
   const __half2 k1024 = __float2half2_rn(1024.f);
   const __half2 k16 = __float2half2_rn(0.0625f), km64 = __float2half2_rn(-64.f);  // (1024 + 16q)/16 - 64 = q
-  const uint4* qp = reinterpret_cast<const uint4*>(blk + 16 + 32 * at);
+  const uint4* qp = reinterpret_cast<const uint4*>(blk + 16 + 32 * AT);
   const uint4 qa = qp[0], qb = qp[1];
   const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
@@ -210,8 +214,10 @@ __device__ __forceinline__ void q4_k_atom(const uint8_t* blk, int at, uint32_t* 
   }
 }
 
-// Q6_K super-block at even offset OFF: atom `at` covers quarters 2*(at&1) and
-// 2*(at&1)+1 of half (at>>1); value d*sc*(q - 32)
+// Q6_K super-block at even byte offset OFF of the row: atom `at` covers
+// quarters 2*(at&1) and 2*(at&1)+1 of half (at>>1); value d*sc*(q - 32).
+// Specialised on OFF (16-byte loads, compile-time word alignment); the atom
+// index stays a runtime value so that only eight decoder copies exist.
 template <int OFF>
 __device__ __forceinline__ void q6_k_atom(const uint8_t* row, int at, uint32_t* out) {
   const int n = at >> 1, hiq = at & 1;
@@ -230,36 +236,53 @@ __device__ __forceinline__ void q6_k_atom(const uint8_t* row, int at, uint32_t* 
     const __half2 s_hi = __float2half2_rn(d * (float)sc[2 * qt + 1]);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const uint32_t q6 = ((lw[i] >> ns) & 0x0F0F0F0Fu) | (((hw[i] >> (2 * qt)) & 0x03030303u) << 4);
+      // the 2-bit fields of quarter qt moved to bits 4-5 of every byte; bits 6-7
+      // take neighbouring fields and are cleared together with the magic OR
+      const uint32_t hs = (hw[i] >> (2 * qt)) << 4;
+      const uint32_t lo = lw[i] >> ns;
+      const uint32_t q6 = (lo & 0x0F0F0F0Fu) | (hs & 0xF0F0F0F0u);  // one LOP3; bits 6-7 junk
       const __half2 s = i < 4 ? s_lo : s_hi;
-      out[16 * qq + 2 * i] = as_u32(__hmul2(__hsub2(magic_pair(q6, 0x00FF00FFu), bias), s));
-      out[16 * qq + 2 * i + 1] = as_u32(__hmul2(__hsub2(magic_pair(q6 >> 8, 0x00FF00FFu), bias), s));
+      out[16 * qq + 2 * i] = as_u32(__hmul2(__hsub2(magic_pair(q6, 0x003F003Fu), bias), s));
+      out[16 * qq + 2 * i + 1] = as_u32(__hmul2(__hsub2(magic_pair(q6 >> 8, 0x003F003Fu), bias), s));
     }
   }
 }
 
-// Runtime (warp-uniform) chunk offset -> the specialised decoder.
-template <int F>
-__device__ __forceinline__ void dequant_atom(const uint8_t* row, int off, int at, uint32_t* out) {
+// Atom g (elements 64g .. 64g+63) of a quad, from the packed row `row` of the
+// stage (box 0; box 1 follows 128 rows later) whose window starts `off` bytes
+// before the quad; g is warp-uniform.
+template <int F, int kRowsStride, int G>
+__device__ __forceinline__ void dequant_atom_g(const uint8_t* row, int off, uint32_t* out) {
   if constexpr (F == kQ4_K) {
-    q4_k_atom(row, at, out);
-  } else if constexpr (F == kQ6_K) {
+    q4_k_atom<G>(row, out);
+  } else if constexpr (F == kQ4_0) {  // atom G = blocks 2G, 2G+1 at byte 36G
+    dequant_block32_atom<F, 4 * G>(row + 32 * G, out);
+  } else {  // Q8_0: atom G = blocks 2G, 2G+1 at byte 68G; bytes 128.. come from box 1
+    dequant_block32_atom<F, 4 * G>(row + (G >= 2 ? kRowsStride : 0) + 64 * (G & 1), out);
+  }
+}
+
+// The warp-uniform atom index selects a decoder specialised for it (Q6_K:
+// the window offset does, the atom index stays a runtime value).
+template <int F, int kRowsStride>
+__device__ __forceinline__ void dequant_atom(const uint8_t* row, int off, int g, uint32_t* out) {
+  if constexpr (F == kQ6_K) {
     switch (off) {
-      case 0: q6_k_atom<0>(row, at, out); break;
-      case 2: q6_k_atom<2>(row, at, out); break;
-      case 4: q6_k_atom<4>(row, at, out); break;
-      case 6: q6_k_atom<6>(row, at, out); break;
-      case 8: q6_k_atom<8>(row, at, out); break;
-      case 10: q6_k_atom<10>(row, at, out); break;
-      case 12: q6_k_atom<12>(row, at, out); break;
-      default: q6_k_atom<14>(row, at, out); break;
+      case 0: q6_k_atom<0>(row, g, out); return;
+      case 2: q6_k_atom<2>(row, g, out); return;
+      case 4: q6_k_atom<4>(row, g, out); return;
+      case 6: q6_k_atom<6>(row, g, out); return;
+      case 8: q6_k_atom<8>(row, g, out); return;
+      case 10: q6_k_atom<10>(row, g, out); return;
+      case 12: q6_k_atom<12>(row, g, out); return;
+      default: q6_k_atom<14>(row, g, out); return;
     }
-  } else {  // Q4_0, Q8_0: chunk offsets are multiples of 4
-    switch (off) {
-      case 0: dequant_block32_atom<F, 0>(row, out); break;
-      case 4: dequant_block32_atom<F, 4>(row, out); break;
-      case 8: dequant_block32_atom<F, 8>(row, out); break;
-      default: dequant_block32_atom<F, 12>(row, out); break;
+  } else {
+    switch (g) {
+      case 0: dequant_atom_g<F, kRowsStride, 0>(row, off, out); break;
+      case 1: dequant_atom_g<F, kRowsStride, 1>(row, off, out); break;
+      case 2: dequant_atom_g<F, kRowsStride, 2>(row, off, out); break;
+      default: dequant_atom_g<F, kRowsStride, 3>(row, off, out); break;
     }
   }
 }
@@ -334,50 +357,57 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
   return true;
 }
 
-template <int F, int BN, int A_ST, int B_ST, int P_ST>
+// Tensor memory: two accumulator buffers per issuing thread, then the A ring
+// (one 128-column stage per quad: 32 columns per atom, two f16 K elements per
+// column).  Slot tiles up to 64 wide have two issuing threads: narrow MMAs are
+// bound by how fast one thread issues them, so the two take alternate quads of
+// every tile into their own accumulators and the epilogue adds the two.
+template <int F, int BN, int A_Q, int B_Q, int P_ST>
 struct Cfg {
-  // Slot tiles up to 128 wide keep the A ring in TMEM (32 columns per atom
-  // stage, next to the two accumulators); 256-wide tiles need all 512 columns
-  // for the accumulators and keep A in shared memory.
-  static constexpr bool kTmemA = BN <= 128;
-  static constexpr int kWB = window_bytes(Fmt<F>::kBytes);
-  static constexpr int kPStage = 128 * kWB;
-  static constexpr int kBStage = BN * 128;
-  static constexpr int kOffA = 0;
-  static constexpr int kOffB = kOffA + (kTmemA ? 0 : A_ST * kAtomBytes);
-  static constexpr int kOffP = kOffB + B_ST * kBStage;
+  static constexpr int kIssuers = BN <= 64 ? 2 : 1;
+  using Fm = Fmt<F>;
+  static constexpr int kWB = Fm::kBoxBytes;            // packed stage row stride
+  static constexpr int kPStage = Fm::kBoxes * 128 * kWB;
+  static constexpr int kBAtom = BN * 128;               // one 64-K box of BN activation rows
+  static constexpr int kBQuad = 4 * kBAtom;
+  static constexpr int kOffB = 0;
+  static constexpr int kOffP = kOffB + B_Q * kBQuad;
   static constexpr int kOffBar = kOffP + P_ST * kPStage;
-  static constexpr int kNumBars = 2 * (P_ST + A_ST + B_ST) + 4 + 1;
+  // Stage release: one commit per quad arrives on rel[quad % kRelBars] and
+  // frees that quad's A and B stages.  The producer of quad n waits for quad
+  // n - depth; kRelBars >= depth keeps the barrier from moving on by a whole
+  // phase before that producer has seen it.
+  static constexpr int kRelBars = A_Q > B_Q ? A_Q : B_Q;
+  static constexpr int kNumBars = 2 * P_ST + A_Q + B_Q + kRelBars + 4 + 2;
   static constexpr int kSmem = kOffBar + kNumBars * 8 + 16 + 1024;  // + alignment slack
   static constexpr uint32_t kAccCols = BN < 32 ? 32 : BN;  // one accumulator
-  static constexpr uint32_t kACol0 = 2 * kAccCols;          // first A column (TMEM A)
-  static constexpr uint32_t kUsedCols = kACol0 + (kTmemA ? A_ST * 32 : 0);
-  static constexpr uint32_t kTmemCols = kUsedCols <= 32 ? 32 : kUsedCols <= 64 ? 64 : kUsedCols <= 128 ? 128
-                                      : kUsedCols <= 256 ? 256 : 512;
+  static constexpr uint32_t kACol0 = 2 * kIssuers * kAccCols;  // first A column
+  static constexpr uint32_t kUsedCols = kACol0 + A_Q * 128;
+  static constexpr uint32_t kTmemCols = kUsedCols <= 256 ? 256 : 512;
   static_assert(kUsedCols <= 512, "tensor memory budget");
+  static_assert(kOffP % 1024 == 0 && kBAtom % 1024 == 0, "SWIZZLE_128B stages must be 1024-byte aligned");
+  static_assert((64 * kWB) % 128 == 0, "TMA destinations must be 128-byte aligned");
 };
 
-template <int F, int BN, int A_ST, int B_ST, int P_ST>
+template <int F, int BN, int A_Q, int B_Q, int P_ST>
 __global__ void __launch_bounds__(kThreads, 1)
     expert_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                        const __grid_constant__ CUtensorMap tm_x, const Args args) {
-  using C = Cfg<F, BN, A_ST, B_ST, P_ST>;
-  constexpr int kAtoms = Fmt<F>::kAtoms;
+  using C = Cfg<F, BN, A_Q, B_Q, P_ST>;
+  using Fm = Fmt<F>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem + C::kOffA;
   uint8_t* sB = smem + C::kOffB;
   uint8_t* sP = smem + C::kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   uint64_t* pk_full = bars;
   uint64_t* pk_empty = pk_full + P_ST;
   uint64_t* a_full = pk_empty + P_ST;
-  uint64_t* a_empty = a_full + A_ST;
-  uint64_t* b_full = a_empty + A_ST;
-  uint64_t* b_empty = b_full + B_ST;
-  uint64_t* acc_full = b_empty + B_ST;  // [2]
-  uint64_t* acc_empty = acc_full + 2;   // [2]
-  uint64_t* mma_done = acc_empty + 2;
+  uint64_t* b_full = a_full + A_Q;
+  uint64_t* rel = b_full + B_Q;               // [kRelBars]
+  uint64_t* acc_full = rel + C::kRelBars;     // [2]
+  uint64_t* acc_empty = acc_full + 2;         // [2]
+  uint64_t* mma_done = acc_empty + 2;        // [2], one per issuer
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
@@ -387,17 +417,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long long t_kernel = clock64();
 #endif
   if (threadIdx.x == 0) {
-    // consumer-side barriers count one elected lane per dequant warp
-    // a K-quant chunk is read by every group (one atom each); a 32-element-block
-    // chunk (one atom) by one group
-    for (int i = 0; i < P_ST; ++i) { mbar_init(pk_full + i, 1); mbar_init(pk_empty + i, kAtoms == 4 ? kDqWarps : 4); }
-    static_assert(kAtoms == 4 || P_ST % kGroups == 0, "32-element-block windows: stages owned per group");
-    static_assert(A_ST % kGroups == 0, "A stages owned per group");
-    // every atom is written whole by one warp group (4 warps)
-    for (int i = 0; i < A_ST; ++i) { mbar_init(a_full + i, 4); mbar_init(a_empty + i, 1); }
-    for (int i = 0; i < B_ST; ++i) { mbar_init(b_full + i, 1); mbar_init(b_empty + i, 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(acc_full + b, 1); mbar_init(acc_empty + b, kDqWarps); }
+    // every packed stage and every A stage is read / written by all 16 dequant warps
+    for (int i = 0; i < P_ST; ++i) { mbar_init(pk_full + i, 1); mbar_init(pk_empty + i, kDqWarps); }
+    for (int i = 0; i < A_Q; ++i) mbar_init(a_full + i, kDqWarps);
+    for (int i = 0; i < B_Q; ++i) mbar_init(b_full + i, 1);
+    for (int i = 0; i < C::kRelBars; ++i) mbar_init(rel + i, 1);
+    for (int b = 0; b < 2; ++b) { mbar_init(acc_full + b, C::kIssuers); mbar_init(acc_empty + b, kDqWarps); }
     mbar_init(mma_done, 1);
+    mbar_init(mma_done + 1, 1);
     *s_abort = 0;
     fence_barrier_init();
   }
@@ -413,29 +440,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *s_tmem;
   const int total = __ldg(args.tile_base + args.E);
   int* err = args.err;
+  // Wait until the stages that quad n takes over from quad n - depth are free.
+  auto stage_free = [&](uint32_t n, uint32_t depth, int code, int site) -> bool {
+    if (n < depth) return true;
+    const uint32_t g = n - depth;
+    return wait_bar(rel + g % C::kRelBars, (g / C::kRelBars) & 1, s_abort, err, code, site UAII_WS_ARG);
+  };
+  auto quad_range = [&](const Tile& t, int& q0, int& q1) {
+    q0 = t.split * args.kquads / args.splits;
+    q1 = (t.split + 1) * args.kquads / args.splits;
+  };
+  // 64-element atoms of quad q (4, or fewer in the last quad of a Q4_0 / Q8_0 row)
+  auto quad_atoms = [&](int q) { return min(4, args.k_atoms - 4 * q); };
 
   if (warp == 0) {
     // ------------------------------------------------------------ weight TMA producer
-    if (lane == 0) {
+    // (converged warp, one elected lane issues the copies; as for the MMA issuer)
+    {
       uint32_t pi = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
         const Tile t = decode_tile(args, tile, BN);
         const int row0 = t.e * args.rows_per_expert + t.m_tile * (args.gateup ? 64 : 128);
-        const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
-        for (int c = c0; c < c1 && ok; ++c) {
+        int q0, q1;
+        quad_range(t, q0, q1);
+        for (int q = q0; q < q1 && ok; ++q) {
           const int ps = pi % P_ST;
           if (!(ok = wait_bar(pk_empty + ps, ((pi / P_ST) & 1) ^ 1, s_abort, err, kErrTimeoutProducer, 0 UAII_WS_ARG))) break;
-          mbar_arrive_expect_tx(pk_full + ps, C::kPStage);
-          const int x = (c * Fmt<F>::kBytes) & ~15;
+          const int x = (q * Fm::kBytes) & ~15;
           uint8_t* dst = sP + ps * C::kPStage;
-          if (args.gateup) {
-            tma_load_2d(dst, &tm_w0, pk_full + ps, x, row0);
-            tma_load_2d(dst + 64 * C::kWB, &tm_w1, pk_full + ps, x, row0);
-          } else {
-            tma_load_2d(dst, &tm_w0, pk_full + ps, x, row0);
-            tma_load_2d(dst + 64 * C::kWB, &tm_w0, pk_full + ps, x, row0 + 64);
+          if (elect_one()) {
+            mbar_arrive_expect_tx(pk_full + ps, C::kPStage);
+#pragma unroll
+            for (int j = 0; j < Fm::kBoxes; ++j) {
+              uint8_t* d = dst + j * 128 * C::kWB;
+              if (args.gateup) {
+                tma_load_2d(d, &tm_w0, pk_full + ps, x + 128 * j, row0);
+                tma_load_2d(d + 64 * C::kWB, &tm_w1, pk_full + ps, x + 128 * j, row0);
+              } else {
+                tma_load_2d(d, &tm_w0, pk_full + ps, x + 128 * j, row0);
+                tma_load_2d(d + 64 * C::kWB, &tm_w0, pk_full + ps, x + 128 * j, row0 + 64);
+              }
+            }
           }
+          __syncwarp();
           ++pi;
         }
       }
@@ -446,101 +494,144 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == kBWarp) {
     // ------------------------------------------------------------ activation TMA producer
-    if (lane == 0) {
+    {
       uint32_t bi = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
         const Tile t = decode_tile(args, tile, BN);
         const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
-        const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
-        for (int c = c0; c < c1 && ok; ++c) {
-          for (int at = 0; at < kAtoms && ok; ++at) {
-            const int bs = bi % B_ST;
-            if (!(ok = wait_bar(b_empty + bs, ((bi / B_ST) & 1) ^ 1, s_abort, err, kErrTimeoutProducer, 1 UAII_WS_ARG))) break;
-            mbar_arrive_expect_tx(b_full + bs, C::kBStage);
-            tma_load_2d(sB + bs * C::kBStage, &tm_x, b_full + bs, c * Fmt<F>::kChunk + at * 64, slot0);
-            ++bi;
+        int q0, q1;
+        quad_range(t, q0, q1);
+        for (int q = q0; q < q1 && ok; ++q) {
+          const int bs = bi % B_Q;
+          if (!(ok = stage_free(bi, B_Q, kErrTimeoutProducer, 1))) break;
+          const int na = quad_atoms(q);
+          if (elect_one()) {
+            mbar_arrive_expect_tx(b_full + bs, na * C::kBAtom);
+            for (int j = 0; j < na; ++j)
+              tma_load_2d(sB + bs * C::kBQuad + j * C::kBAtom, &tm_x, b_full + bs, q * kQuadK + 64 * j, slot0);
           }
+          __syncwarp();
+          ++bi;
         }
       }
-      for (uint32_t j = (bi > (uint32_t)B_ST ? bi - B_ST : 0); j < bi; ++j)
-        (void)mbar_wait(b_full + j % B_ST, (j / B_ST) & 1);
+      for (uint32_t j = (bi > (uint32_t)B_Q ? bi - B_Q : 0); j < bi; ++j)
+        (void)mbar_wait(b_full + j % B_Q, (j / B_Q) & 1);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+  } else if (warp == 1 || (warp == kMma1Warp && C::kIssuers == 2)) {
+    // ------------------------------------------------------------ MMA issuer(s)
+    // The whole warp runs the loop (waits, stage bookkeeping) in step and one
+    // elected lane issues the MMAs and commits: converged code issues narrow
+    // MMAs several times faster than a loop run by a single lane.
+    {
+      const int me = warp == 1 ? 0 : 1;  // takes the quads of every tile with local index % kIssuers == me
       constexpr uint32_t idesc = idesc_f16_f32(128, BN);
-      uint32_t ai = 0, bi = 0, it = 0;
+      uint32_t sa = 0, pa = 0;  // A stage and its phase
+      uint32_t sb = 0, pb = 0;  // B stage and its phase
+      uint32_t sr = 0;          // release barrier
+      uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
         const Tile t = decode_tile(args, tile, BN);
-        const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
+        int q0, q1;
+        quad_range(t, q0, q1);
         const uint32_t ab = it & 1;  // accumulator buffer of this tile
         if (!(ok = wait_bar(acc_empty + ab, ((it >> 1) & 1) ^ 1, s_abort, err, kErrTimeoutMma, 2 UAII_WS_ARG))) break;
         tc_fence_after();
-        const uint32_t dacc = tmem + ab * C::kAccCols;
+        const uint32_t dacc = tmem + (ab * C::kIssuers + me) * C::kAccCols;
         uint32_t acc = 0;
-        for (int c = c0; c < c1 && ok; ++c) {
-          for (int at = 0; at < kAtoms; ++at) {
-            const int as = ai % A_ST, bs = bi % B_ST;
-            if (!(ok = wait_bar(a_full + as, (ai / A_ST) & 1, s_abort, err, kErrTimeoutMma, 3 UAII_WS_ARG))) break;
-            if (!(ok = wait_bar(b_full + bs, (bi / B_ST) & 1, s_abort, err, kErrTimeoutMma, 4 UAII_WS_ARG))) break;
-            tc_fence_after();
-            const uint64_t bd = sw128_desc(smem_u32(sB + bs * C::kBStage));
-            if constexpr (C::kTmemA) {
-              const uint32_t at_col = tmem + C::kACol0 + as * 32;  // 8 columns per 16 K elements
+        for (int q = q0; q < q1; ++q) {
+          if ((q - q0) % C::kIssuers != me) {  // the other issuer's quad
+            sa = sa + 1 == A_Q ? (pa ^= 1, 0) : sa + 1;
+            sb = sb + 1 == B_Q ? (pb ^= 1, 0) : sb + 1;
+            sr = sr + 1 == C::kRelBars ? 0 : sr + 1;
+            continue;
+          }
+          if (!(ok = wait_bar(a_full + sa, pa, s_abort, err, kErrTimeoutMma, 3 UAII_WS_ARG))) break;
+          if (!(ok = wait_bar(b_full + sb, pb, s_abort, err, kErrTimeoutMma, 4 UAII_WS_ARG))) break;
+          tc_fence_after();
+#ifdef UAII_UMMA_STATS
+          const long long t_issue = clock64();
+#endif
+          const int na = quad_atoms(q);
+          const uint64_t bd = sw128_desc(smem_u32(sB + sb * C::kBQuad));
+          const uint32_t at = tmem + C::kACol0 + sa * 128;
+          if (elect_one()) {
 #pragma unroll
-              for (int ks = 0; ks < 4; ++ks) {
-                mma_f16_ts(dacc, at_col + 8 * ks, bd + 2 * ks, idesc, acc);
-                acc = 1;
-              }
-            } else {
-              const uint64_t ad = sw128_desc(smem_u32(sA + as * kAtomBytes));
+            for (int j = 0; j < 4; ++j) {
+              if (j < na) {
 #pragma unroll
-              for (int ks = 0; ks < 4; ++ks) {
-                mma_f16(dacc, ad + 2 * ks, bd + 2 * ks, idesc, acc);
-                acc = 1;
+                for (int ks = 0; ks < 4; ++ks) {
+                  mma_f16_ts(dacc, at + 32 * j + 8 * ks, bd + (uint64_t)((j * C::kBAtom) >> 4) + 2 * ks, idesc, acc);
+                  acc = 1;
+                }
               }
             }
-            mma_commit(a_empty + as);
-            mma_commit(b_empty + bs);
-            ++ai;
-            ++bi;
+            mma_commit(rel + sr);
           }
+          __syncwarp();
+          acc = 1;
+#ifdef UAII_UMMA_STATS
+          wstats.cyc[8] += (unsigned long long)(clock64() - t_issue);
+          wstats.cnt[8] += 1;
+#endif
+          sa = sa + 1 == A_Q ? (pa ^= 1, 0) : sa + 1;
+          sb = sb + 1 == B_Q ? (pb ^= 1, 0) : sb + 1;
+          sr = sr + 1 == C::kRelBars ? 0 : sr + 1;
         }
-        if (ok) mma_commit(acc_full + ab);
+        if (ok) {
+          if (elect_one()) mma_commit(acc_full + ab);
+          __syncwarp();
+        }
       }
       // the tensor core must be idle before TMEM is freed
-      mma_commit(mma_done);
-      (void)mbar_wait(mma_done, 0);
+      if (elect_one()) mma_commit(mma_done + me);
+      __syncwarp();
+      (void)mbar_wait(mma_done + me, 0);
     }
     __syncwarp();
   } else if (warp >= 2 && warp < kBWarp) {
     // ------------------------------------------------------------ dequant + epilogue (kDqWarps warps)
     const int q = warp & 3;            // TMEM lane quarter this warp may access
     const int row = 32 * q + lane;     // A-tile row == accumulator lane
-    const int grp = (warp - 2) >> 2;   // warp group 0..kGroups-1; each group covers all 128 rows
+    const int grp = (warp - 2) >> 2;   // warp group 0..kGroups-1 == atom of every quad it makes
     // Gate/up tiles hold 64 features: in every 32-row block (one TMEM lane
     // quarter) lanes 0-15 are gate rows and lanes 16-31 the up rows of the same
     // 16 features, so the SwiGLU epilogue pairs them with one lane shuffle.
     // The packed stage keeps the TMA layout: gate rows 0-63, up rows 64-127.
     const int src_row = args.gateup ? (lane < 16 ? 16 * q + lane : 64 + 16 * q + (lane - 16)) : row;
-    uint32_t pi = 0, ai = 0, it = 0;
+    uint32_t pi = 0, qi = 0, it = 0;
     bool ok = true;
     // Epilogue of tile number `e_it` (accumulator buffer e_it & 1), run after the
     // next tile's dequantization has been issued so that the tensor core keeps
     // working while the accumulator is drained.
+    constexpr int kCols = BN / kGroups;          // columns per group (>= 4)
+    constexpr int kW = kCols >= 8 ? 8 : 4;       // columns per TMEM load
     auto epilogue = [&](const Tile& t, uint32_t e_it) -> bool {
-      // group `grp` owns accumulator columns [grp*BN/kGroups, (grp+1)*BN/kGroups)
       if (!wait_bar(acc_full + (e_it & 1), (e_it >> 1) & 1, s_abort, err, kErrTimeoutEpilogue, 7 UAII_WS_ARG))
         return false;
       tc_fence_after();
       const int n_valid = min(BN, __ldg(args.counts + t.e) - t.n_tile * BN);
       const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
-      const uint32_t taddr = tmem + (e_it & 1) * C::kAccCols + ((uint32_t)(32 * q) << 16);
-      constexpr int kCols = BN / kGroups;          // columns per group (>= 4)
-      constexpr int kW = kCols >= 8 ? 8 : 4;       // columns per TMEM load
+      const uint32_t taddr = tmem + (e_it & 1) * C::kIssuers * C::kAccCols + ((uint32_t)(32 * q) << 16);
+      int q0, q1;
+      quad_range(t, q0, q1);
+      const bool two = C::kIssuers == 2 && q1 - q0 >= 2;  // the second issuer's accumulator holds quads too
+      // kW accumulator columns at `a` (+ the second issuer's at a + kAccCols)
+      auto load_acc = [&](uint32_t a, uint32_t (&r)[8]) {
+        if constexpr (kW == 8) tmem_ld8(a, r);
+        else tmem_ld4(a, r);
+        tmem_ld_wait();
+        if (two) {
+          uint32_t v[8];
+          if constexpr (kW == 8) tmem_ld8(a + C::kAccCols, v);
+          else tmem_ld4(a + C::kAccCols, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < kW; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(v[j]));
+        }
+      };
       if (args.gateup) {
         // lane l < 16 holds gate, lane l + 16 up of feature i0 + 16q + (l & 15); each
         // column pair (n, n+1) is split: the gate lane finishes n, the up lane n + 1
@@ -548,9 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool gate_lane = lane < 16;
         for (int cb = grp * kCols; cb < (grp + 1) * kCols; cb += kW) {
           uint32_t r[8];
-          if constexpr (kW == 8) tmem_ld8(taddr + cb, r);
-          else tmem_ld4(taddr + cb, r);
-          tmem_ld_wait();
+          load_acc(taddr + cb, r);
 #pragma unroll
           for (int j = 0; j < kW; j += 2) {
             const float mine0 = __uint_as_float(r[j]), mine1 = __uint_as_float(r[j + 1]);
@@ -567,9 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* out = args.out + (int64_t)t.split * args.split_stride;
         for (int cb = grp * kCols; cb < (grp + 1) * kCols; cb += kW) {
           uint32_t r[8];
-          if constexpr (kW == 8) tmem_ld8(taddr + cb, r);
-          else tmem_ld4(taddr + cb, r);
-          tmem_ld_wait();
+          load_acc(taddr + cb, r);
 #pragma unroll
           for (int j = 0; j < kW; ++j) {
             const int n = cb + j;
@@ -584,56 +671,66 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     Tile prev{};
     bool have_prev = false;
+    uint32_t sa = 0;
+    // The A stage of a quad is handed to the MMA issuers one quad late: its
+    // TMEM store stays in flight while the next quad is decoded (registers
+    // only), and is waited for and announced just before the next store.
+    bool pending = false;
+    uint32_t pending_sa = 0;
+    auto announce = [&]() {
+      if (!pending) return;
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(a_full + pending_sa);
+      pending = false;
+    };
     for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
       const Tile t = decode_tile(args, tile, BN);
-      const int c0 = t.split * args.kchunks / args.splits, c1 = (t.split + 1) * args.kchunks / args.splits;
-      for (int c = c0; c < c1 && ok; ++c, ++pi) {
+      int q0, q1;
+      quad_range(t, q0, q1);
+      for (int qq = q0; qq < q1 && ok; ++qq, ++pi, ++qi) {
         const int ps = pi % P_ST;
-        // K-quants: group g makes atom g of every super-block.  32-element blocks:
-        // the chunk is one atom, made by group (chunk counter % kGroups).
-        const int at = kAtoms == 4 ? grp : 0;
-        const uint32_t aidx = kAtoms == 4 ? ai + grp : ai;
-        ai += kAtoms;
-        if (kAtoms == 1 && (int)(pi % kGroups) != grp) continue;
+        const bool active = grp < quad_atoms(qq);
         if (!(ok = wait_bar(pk_full + ps, (pi / P_ST) & 1, s_abort, err, kErrTimeoutDequant, 5 UAII_WS_ARG))) break;
-        const uint8_t* rowp = sP + ps * C::kPStage + src_row * C::kWB;
-        const int off = (c * Fmt<F>::kBytes) & 15;
-        const int as = aidx % A_ST;
-        if (!(ok = wait_bar(a_empty + as, ((aidx / A_ST) & 1) ^ 1, s_abort, err, kErrTimeoutDequant, 6 UAII_WS_ARG)))
-          break;
         uint32_t o[32];
+        if (active) {
 #ifdef UAII_UMMA_STATS
-        const long long tq = clock64();
+          const long long tq = clock64();
 #endif
-        dequant_atom<F>(rowp, off, at, o);
+          dequant_atom<F, 128 * C::kWB>(sP + ps * C::kPStage + src_row * C::kWB, (qq * Fm::kBytes) & 15, grp, o);
 #ifdef UAII_UMMA_STATS
-        asm volatile("" ::"r"(o[0]), "r"(o[13]), "r"(o[22]), "r"(o[31]));
-        wstats.cyc[10] += (unsigned long long)(clock64() - tq);
-        wstats.cnt[10] += 1;
+          asm volatile("" ::"r"(o[0]), "r"(o[13]), "r"(o[22]), "r"(o[31]));
+          wstats.cyc[10] += (unsigned long long)(clock64() - tq);
+          wstats.cnt[10] += 1;
+#endif
+        }
+#ifdef UAII_UMMA_STATS
+        const long long t_post = clock64();
 #endif
         __syncwarp();
         if (lane == 0) mbar_arrive(pk_empty + ps);  // the window has been read
-        if constexpr (C::kTmemA) {
-          tc_fence_after();  // after the MMA that last read this stage (a_empty)
-          tmem_st32(tmem + C::kACol0 + as * 32 + ((uint32_t)(32 * q) << 16), o);
-          tmem_st_wait();
-          tc_fence_before();
-        } else {
-          uint8_t* arow = sA + as * kAtomBytes + row * 128;
-#pragma unroll
-          for (int cc = 0; cc < 8; ++cc)
-            *reinterpret_cast<uint4*>(arow + ((cc ^ (row & 7)) << 4)) =
-                make_uint4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]);
-          fence_proxy_async_smem();
+        announce();                                 // the previous quad's A stage
+        if (!(ok = stage_free(qi, A_Q, kErrTimeoutDequant, 6))) break;
+        if (active) {
+          tc_fence_after();  // after the MMAs that last read this stage (stage_free)
+          tmem_st32(tmem + C::kACol0 + sa * 128 + grp * 32 + ((uint32_t)(32 * q) << 16), o);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(a_full + as);
+        pending = true;
+        pending_sa = sa;
+#ifdef UAII_UMMA_STATS
+        wstats.cyc[9] += (unsigned long long)(clock64() - t_post);
+        wstats.cnt[9] += 1;
+#endif
+        sa = sa + 1 == A_Q ? 0 : sa + 1;
       }
       if (!ok) break;
+      announce();  // the MMAs of this tile must be able to finish before any epilogue wait
       if (have_prev && !(ok = epilogue(prev, it - 1))) break;
       prev = t;
       have_prev = true;
     }
+    if (ok) announce();
     if (ok && have_prev) (void)epilogue(prev, it - 1);
   }
 #ifdef UAII_UMMA_STATS
@@ -644,7 +741,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       atomicAdd(&g_wait_cycles[i], wstats.cyc[i]);
       atomicAdd(&g_wait_count[i], (unsigned long long)wstats.cnt[i]);
     }
-
 #endif
   __syncthreads();
   if (warp == 1) {
@@ -722,12 +818,12 @@ int num_sms() {
   return n;
 }
 
-template <int F, int BN, int A_ST, int B_ST, int P_ST>
+template <int F, int BN, int A_Q, int B_Q, int P_ST>
 cudaError_t run_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x, const Args& a,
                      cudaStream_t st) {
-  using C = Cfg<F, BN, A_ST, B_ST, P_ST>;
+  using C = Cfg<F, BN, A_Q, B_Q, P_ST>;
   static_assert(C::kSmem <= 227 * 1024, "shared memory budget");
-  auto kern = expert_gemm_kernel<F, BN, A_ST, B_ST, P_ST>;
+  auto kern = expert_gemm_kernel<F, BN, A_Q, B_Q, P_ST>;
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
@@ -738,32 +834,19 @@ cudaError_t run_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtenso
   return cudaGetLastError();
 }
 
-// Ring depths per (format, slot tile).  Every ring that one warp group can run
-// ahead on has a depth that is a multiple of kGroups, so each stage is always
-// filled (A tiles) or consumed (32-element-block packed windows) by the same
-// group and no waiter is ever more than one barrier phase ahead.  Packed
-// stages: deeper at decode widths (HBM latency); activation stages; then as
-// many A stages (4 or 8) as the shared-memory budget leaves.
+// Ring depths per (format, slot tile), in quads.  A stages: as many 128-column
+// stages as tensor memory leaves next to the two accumulators.  Activation
+// stages: 4 for narrow tiles, fewer as they grow.  Packed windows: the rest of
+// shared memory, up to 8 (decode widths are bound by HBM latency).
 template <int F, int BN>
 struct Stages {
-  static constexpr bool kTmemA = BN <= 128;
-  static constexpr int kWB = window_bytes(Fmt<F>::kBytes);
   static constexpr int kBudget = 224 * 1024;  // stage bytes; barriers and alignment slack come on top
-  static constexpr bool kBlock32 = Fmt<F>::kAtoms == 1;
-  static constexpr int B0 = BN <= 16 ? 8 : 4;
-  // TMEM A: 8 A stages in tensor memory, shared memory goes to the weight ring
-  static constexpr int P_fit = (kBudget - B0 * BN * 128) / (128 * kWB);
-  static constexpr int P_t = P_fit > 8 ? 8 : P_fit;
-  static constexpr int P_tmem = kBlock32 ? (P_t >= 8 ? 8 : 4) : P_t;
-  // shared-memory A (256-wide tiles)
-  static constexpr int P_smem = kBlock32 ? 4 : 2;
-  static constexpr int kP = P_smem * 128 * kWB;
-  static constexpr int B_smem = (kP + B0 * BN * 128 + 4 * kAtomBytes <= kBudget) ? B0 : 3;
-  static constexpr int A_fit = (kBudget - kP - B_smem * BN * 128) / kAtomBytes;
-  static constexpr int P = kTmemA ? P_tmem : P_smem;
-  static constexpr int B = kTmemA ? B0 : B_smem;
-  static constexpr int A = kTmemA ? 8 : (A_fit >= 8 ? 8 : 4);
-  static_assert(kTmemA ? P >= 2 : A_fit >= 4, "shared-memory budget");
+  static constexpr int A = BN <= 32 ? 3 : 2;
+  static constexpr int B = BN <= 32 ? 4 : (BN == 64 ? 3 : 2);
+  static constexpr int kPStage = Fmt<F>::kBoxes * 128 * Fmt<F>::kBoxBytes;
+  static constexpr int P_fit = (kBudget - B * BN * 512) / kPStage;
+  static constexpr int P = P_fit > 8 ? 8 : P_fit;
+  static_assert(P >= 2, "shared-memory budget");
 };
 
 template <int F, int BN>
@@ -781,50 +864,52 @@ cudaError_t dispatch_bn(int bn, const CUtensorMap& w0, const CUtensorMap& w1, co
     case 32: return run_cfg<F, 32>(w0, w1, x, a, st);
     case 64: return run_cfg<F, 64>(w0, w1, x, a, st);
     case 128: return run_cfg<F, 128>(w0, w1, x, a, st);
-    case 256: return run_cfg<F, 256>(w0, w1, x, a, st);
     default: return cudaErrorInvalidValue;
   }
 }
 
-int chunk_elems(int fmt) {
+// K granularity a row of this format must have (64 or 256), 0 if unsupported.
+int min_k(int fmt) {
   switch (fmt) {
-    case kQ4_0: return Fmt<kQ4_0>::kChunk;
-    case kQ8_0: return Fmt<kQ8_0>::kChunk;
-    case kQ4_K: return Fmt<kQ4_K>::kChunk;
-    case kQ6_K: return Fmt<kQ6_K>::kChunk;
-    default: return 0;
-  }
-}
-int chunk_bytes(int fmt) {
-  switch (fmt) {
-    case kQ4_0: return Fmt<kQ4_0>::kBytes;
-    case kQ8_0: return Fmt<kQ8_0>::kBytes;
-    case kQ4_K: return Fmt<kQ4_K>::kBytes;
-    case kQ6_K: return Fmt<kQ6_K>::kBytes;
+    case kQ4_0: return Fmt<kQ4_0>::kMinK;
+    case kQ8_0: return Fmt<kQ8_0>::kMinK;
+    case kQ4_K: return Fmt<kQ4_K>::kMinK;
+    case kQ6_K: return Fmt<kQ6_K>::kMinK;
     default: return 0;
   }
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+template <int F>
+bool make_weight_maps(CUtensorMap* m0, CUtensorMap* m1, const void* W0, const void* W1, int64_t pitch,
+                      int64_t rows_total) {
+  return make_weight_map(m0, W0, pitch, rows_total, Fmt<F>::kBoxBytes) &&
+         make_weight_map(m1, W1, pitch, rows_total, Fmt<F>::kBoxBytes);
+}
+
 cudaError_t launch_common(int fmt, bool gateup, const void* W0, const void* W1, int64_t E, int64_t rows,
                           int64_t K, const void* act16, int64_t S_rows, const int32_t* counts,
                           const int32_t* offsets, int32_t* tile_base, int bn, int splits, void* h16,
                           float* out, int64_t out_ld, int64_t split_stride, int* err, cudaStream_t st) {
-  const int ce = chunk_elems(fmt);
-  if (!ce || K % ce != 0) return cudaErrorNotSupported;
+  const int mk = min_k(fmt);
+  if (!mk || K % mk != 0 || K <= 0) return cudaErrorNotSupported;
   const int64_t pitch = fmt_row_bytes(fmt, K);
   const int m_rows = gateup ? 64 : 128;
   if (rows % m_rows != 0 || pitch % 16 != 0) return cudaErrorNotSupported;
   if (!aligned16(W0) || !aligned16(W1) || !aligned16(act16) || K % 8 != 0) return cudaErrorNotSupported;
-  const int kchunks = (int)(K / ce);
+  const int kquads = (int)((K + kQuadK - 1) / kQuadK);
   if (splits < 1) splits = 1;
-  if (splits > kchunks) splits = kchunks;
-  const int window = window_bytes(chunk_bytes(fmt));
+  if (splits > kquads) splits = kquads;
   CUtensorMap m0, m1, mx;
-  if (!make_weight_map(&m0, W0, pitch, E * rows, window) || !make_weight_map(&m1, W1, pitch, E * rows, window) ||
-      !make_act_map(&mx, act16, K, S_rows, bn))
-    return cudaErrorNotSupported;
+  bool maps = make_act_map(&mx, act16, K, S_rows, bn);
+  switch (fmt) {
+    case kQ4_0: maps = maps && make_weight_maps<kQ4_0>(&m0, &m1, W0, W1, pitch, E * rows); break;
+    case kQ8_0: maps = maps && make_weight_maps<kQ8_0>(&m0, &m1, W0, W1, pitch, E * rows); break;
+    case kQ4_K: maps = maps && make_weight_maps<kQ4_K>(&m0, &m1, W0, W1, pitch, E * rows); break;
+    default: maps = maps && make_weight_maps<kQ6_K>(&m0, &m1, W0, W1, pitch, E * rows); break;
+  }
+  if (!maps) return cudaErrorNotSupported;
   const int m_tiles = (int)(rows / m_rows);
   tile_table_kernel<<<1, 32, 0, st>>>(counts, (int)E, bn, m_tiles, splits, tile_base);
   cudaError_t e = cudaGetLastError();
@@ -836,7 +921,8 @@ cudaError_t launch_common(int fmt, bool gateup, const void* W0, const void* W1, 
   a.E = (int)E;
   a.m_tiles = m_tiles;
   a.splits = splits;
-  a.kchunks = kchunks;
+  a.kquads = kquads;
+  a.k_atoms = (int)(K / 64);
   a.rows_per_expert = (int)rows;
   a.gateup = gateup ? 1 : 0;
   a.h_out = static_cast<__half*>(h16);
@@ -871,11 +957,11 @@ extern "C" __attribute__((visibility("default"))) int uaii_moe_debug_wait_stats(
 }
 #endif
 
-bool umma_format_supported(int fmt) { return chunk_elems(fmt) != 0; }
+bool umma_format_supported(int fmt) { return min_k(fmt) != 0; }
 
 bool umma_shapes_supported(int gfmt, int dfmt, int64_t D, int64_t I) {
   if (!umma_format_supported(gfmt) || !umma_format_supported(dfmt)) return false;
-  if (D % chunk_elems(gfmt) || I % chunk_elems(dfmt) || I % 64 || D % 128) return false;
+  if (D % min_k(gfmt) || I % min_k(dfmt) || I % 64 || D % 128) return false;
   return fmt_row_bytes(gfmt, D) % 16 == 0 && fmt_row_bytes(dfmt, I) % 16 == 0 && D % 8 == 0 && I % 8 == 0;
 }
 
@@ -894,8 +980,7 @@ cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t E, int64_t D, int6
 }
 
 int umma_kchunks(int fmt, int64_t K) {
-  const int ce = chunk_elems(fmt);
-  return ce ? (int)(K / ce) : 0;
+  return umma_format_supported(fmt) ? (int)((K + kQuadK - 1) / kQuadK) : 0;
 }
 
 }  // namespace uaii_b200

@@ -5,12 +5,15 @@
 // (RefGemm::gemm_f32, libs/uaii-kernels/src/gemm_ref.cpp:45-75): for each
 // 64-wide k tile, s = 0 then s += x*w sequentially; c (from 0) += s tile by
 // tile.  Every multiply and add is a separate round-to-nearest operation.
-// Two schedules compute the same values:
-//   * split: one thread per (token, expert, k-tile) partial, then one thread
-//     per (token, expert) adds the partials in tile order -- enough
-//     parallelism for decode-sized batches;
-//   * tiled: a block owns 16 tokens x 64 experts, stages 64-wide k tiles of
-//     x and w in shared memory, and each thread carries 2x2 dot products.
+// Three schedules compute the same values:
+//   * token (small batches): one block per token, one thread per (k tile,
+//     expert) partial, then one thread per expert adds the partials in order;
+//   * chunk: a block owns 16 tokens and walks the row in chunks of 16 k tiles
+//     staged in shared memory with coalesced loads (8 experts per pass),
+//     folding each chunk's partials into running logits in tile order;
+//   * tiled (very many experts): a block owns 16 tokens x 64 experts, stages
+//     64-wide k tiles of x and w in shared memory, and each thread carries 2x2
+//     dot products.
 // softmax (softmax.cpp:55-75): max-subtract, exp, sequential sum over experts,
 // multiply by 1/sum; exp is evaluated in double and rounded once to f32.
 // top_expert is the first strict argmax of probs, stored as an f32 id.
@@ -21,33 +24,163 @@ namespace {
 
 constexpr int kTile = 64;
 
-__global__ void router_partials_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                       int64_t T, int64_t D, int64_t E, int nkt,
-                                       int pairs_per_block, float* __restrict__ logits) {
-  extern __shared__ float part[];  // [pairs_per_block][nkt]
-  const int64_t p0 = (int64_t)blockIdx.x * pairs_per_block;
-  const int64_t npairs = T * E;
-  const int items = pairs_per_block * nkt;
-  for (int it = threadIdx.x; it < items; it += blockDim.x) {
-    const int lp = it / nkt, j = it - lp * nkt;
-    const int64_t p = p0 + lp;
-    if (p >= npairs) continue;
-    const int64_t t = p / E, e = p - t * E;
-    const float* xr = x + t * D;
-    const float* wr = w + e * D;
-    const int64_t k0 = (int64_t)j * kTile;
-    const int64_t k1 = (k0 + kTile < D) ? k0 + kTile : D;
-    float s = 0.0f;
-    for (int64_t k = k0; k < k1; ++k) s = __fadd_rn(s, __fmul_rn(xr[k], wr[k]));
-    part[it] = s;
+constexpr int kEC = 8;   // experts per pass
+constexpr int kTB = 16;  // tokens per block (chunk schedule)
+constexpr int kJC = 16;  // k tiles per chunk (chunk schedule)
+constexpr int kTS = kTile + 1;         // staged tile stride: lanes on consecutive tiles hit distinct banks
+constexpr int kXS = kJC * kTS;          // staged x chunk row (floats)
+
+// Chunk schedule (256 threads): thread (t = tid / kJC, jj = tid % kJC) builds the
+// partial of k tile (chunk + jj) for token t and kEC experts from staged x and
+// w; then thread (t, e) folds the chunk's kJC partials, in tile order, into the
+// running logit.  x is staged once per chunk, w once per (chunk, expert pass).
+__global__ void __launch_bounds__(256) router_chunk_kernel(const float* __restrict__ x,
+                                                           const float* __restrict__ w, int64_t T,
+                                                           int64_t D, int64_t E,
+                                                           float* __restrict__ logits) {
+  extern __shared__ float sm[];
+  float* xs = sm;                         // [kTB][kXS]
+  float* ws = xs + kTB * kXS;             // [kEC][kJC * kTS]
+  float* part = ws + kEC * kJC * kTS;     // [kTB][kEC][kJC]
+  float* run = part + kTB * kEC * kJC;    // [kTB][E] running logits
+  const int tid = threadIdx.x;
+  const int64_t t0 = (int64_t)blockIdx.x * kTB;
+  const int nkt = (int)((D + kTile - 1) / kTile);
+  for (int i = tid; i < kTB * E; i += 256) run[i] = 0.f;
+  const int lt = tid / kJC, jj = tid - lt * kJC;
+  const bool vec = (D & 3) == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
+  for (int jc = 0; jc < nkt; jc += kJC) {
+    const int64_t kc0 = (int64_t)jc * kTile;
+    const int64_t kcn = (kc0 + kJC * kTile < D) ? kJC * kTile : D - kc0;  // valid k in this chunk
+    __syncthreads();
+    // coalesced x chunk; every load of a thread is issued before its stores
+    if (vec && kcn == kJC * kTile && t0 + kTB <= T) {
+      constexpr int kN = kTB * kJC * kTile / 4 / 256;
+      float4 v[kN];
+#pragma unroll
+      for (int u = 0; u < kN; ++u) {
+        const int i = tid + 256 * u, r = i / (kJC * kTile / 4), k4 = i - r * (kJC * kTile / 4);
+        v[u] = __ldg(reinterpret_cast<const float4*>(x + (t0 + r) * D + kc0) + k4);
+      }
+#pragma unroll
+      for (int u = 0; u < kN; ++u) {
+        const int i = tid + 256 * u, r = i / (kJC * kTile / 4), k = 4 * (i - r * (kJC * kTile / 4));
+        float* d = xs + r * kXS + (k / kTile) * kTS + (k % kTile);
+        d[0] = v[u].x; d[1] = v[u].y; d[2] = v[u].z; d[3] = v[u].w;
+      }
+    } else {
+      for (int i = tid; i < kTB * kJC * kTile; i += 256) {
+        const int r = i / (kJC * kTile), k = i - r * (kJC * kTile);
+        xs[r * kXS + (k / kTile) * kTS + (k % kTile)] = (t0 + r < T && k < kcn) ? __ldg(x + (t0 + r) * D + kc0 + k) : 0.f;
+      }
+    }
+    for (int64_t e0 = 0; e0 < E; e0 += kEC) {
+      const int ne = (int)((E - e0 < kEC) ? E - e0 : kEC);
+      __syncthreads();
+      if (vec && kcn == kJC * kTile && ne == kEC) {  // coalesced w chunk
+        constexpr int kN = kEC * kJC * kTile / 4 / 256;
+        float4 v[kN];
+#pragma unroll
+        for (int u = 0; u < kN; ++u) {
+          const int i = tid + 256 * u, c = i / (kJC * kTile / 4), k4 = i - c * (kJC * kTile / 4);
+          v[u] = __ldg(reinterpret_cast<const float4*>(w + (e0 + c) * D + kc0) + k4);
+        }
+#pragma unroll
+        for (int u = 0; u < kN; ++u) {
+          const int i = tid + 256 * u, c = i / (kJC * kTile / 4), k = 4 * (i - c * (kJC * kTile / 4));
+          float* d = ws + c * kXS + (k / kTile) * kTS + (k % kTile);
+          d[0] = v[u].x; d[1] = v[u].y; d[2] = v[u].z; d[3] = v[u].w;
+        }
+      } else {
+        for (int i = tid; i < kEC * kJC * kTile; i += 256) {
+          const int c = i / (kJC * kTile), k = i - c * (kJC * kTile);
+          ws[c * kXS + (k / kTile) * kTS + (k % kTile)] = (c < ne && k < kcn) ? __ldg(w + (e0 + c) * D + kc0 + k) : 0.f;
+        }
+      }
+      __syncthreads();
+      const int64_t ktile0 = (int64_t)jj * kTile;
+      const int kn = (int)((ktile0 + kTile <= kcn) ? kTile : (kcn > ktile0 ? kcn - ktile0 : 0));
+      float sacc[kEC];
+#pragma unroll
+      for (int c = 0; c < kEC; ++c) sacc[c] = 0.f;
+      const float* xr = xs + lt * kXS + jj * kTS;
+      const float* wr = ws + jj * kTS;
+      if (kn == kTile) {
+#pragma unroll 8
+        for (int k = 0; k < kTile; ++k) {
+          const float xv = xr[k];
+#pragma unroll
+          for (int c = 0; c < kEC; ++c) sacc[c] = __fadd_rn(sacc[c], __fmul_rn(xv, wr[c * kXS + k]));
+        }
+      } else {
+        for (int k = 0; k < kn; ++k) {
+          const float xv = xr[k];
+#pragma unroll
+          for (int c = 0; c < kEC; ++c) sacc[c] = __fadd_rn(sacc[c], __fmul_rn(xv, wr[c * kXS + k]));
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < kEC; ++c) part[(lt * kEC + c) * kJC + jj] = sacc[c];
+      __syncthreads();
+      const int ntiles = (int)((kcn + kTile - 1) / kTile);  // tiles of this chunk inside the row
+      for (int idx = tid; idx < kTB * kEC; idx += 256) {
+        const int l2 = idx / kEC, c = idx - l2 * kEC;
+        if (c >= ne) continue;
+        float acc = run[l2 * E + e0 + c];
+        for (int q = 0; q < ntiles; ++q) acc = __fadd_rn(acc, __fmul_rn(1.0f, part[(l2 * kEC + c) * kJC + q]));
+        run[l2 * E + e0 + c] = acc;
+      }
+    }
   }
   __syncthreads();
-  for (int lp = threadIdx.x; lp < pairs_per_block; lp += blockDim.x) {
-    const int64_t p = p0 + lp;
-    if (p >= npairs) continue;
-    float c = 0.0f;
-    for (int j = 0; j < nkt; ++j) c = __fadd_rn(c, __fmul_rn(1.0f, part[lp * nkt + j]));
-    logits[p] = c;
+  for (int i = tid; i < kTB * E; i += 256) {
+    const int l2 = (int)(i / E);
+    const int64_t t = t0 + l2;
+    if (t < T) logits[t * E + (i - l2 * E)] = run[i];
+  }
+}
+
+// Small batches: one block per token, thread (tile j, expert e) builds one
+// partial from x staged in shared memory; thread e then adds its partials in
+// tile order.
+__global__ void __launch_bounds__(1024) router_token_kernel(const float* __restrict__ x,
+                                                            const float* __restrict__ w, int64_t D,
+                                                            int64_t E, float* __restrict__ logits) {
+  extern __shared__ float sm[];
+  const int nkt = (int)((D + kTile - 1) / kTile);
+  float* xs = sm;               // [D]
+  float* part = sm + D;         // [E][nkt]
+  const int64_t t = blockIdx.x;
+  for (int64_t k = threadIdx.x; k < D; k += blockDim.x) xs[k] = __ldg(x + t * D + k);
+  __syncthreads();
+  for (int64_t p = threadIdx.x; p < E * nkt; p += blockDim.x) {
+    const int64_t e = p % E, j = p / E;
+    const int64_t k0 = j * kTile;
+    const int kn = (int)((k0 + kTile < D) ? kTile : D - k0);
+    const float* wr = w + e * D + k0;
+    float s = 0.f;
+    if (kn == kTile && (((reinterpret_cast<uintptr_t>(wr)) & 15) == 0)) {
+      const float4* w4 = reinterpret_cast<const float4*>(wr);
+      float4 buf[kTile / 4];
+#pragma unroll
+      for (int i = 0; i < kTile / 4; ++i) buf[i] = __ldg(w4 + i);
+#pragma unroll
+      for (int i = 0; i < kTile / 4; ++i) {
+        s = __fadd_rn(s, __fmul_rn(xs[k0 + 4 * i], buf[i].x));
+        s = __fadd_rn(s, __fmul_rn(xs[k0 + 4 * i + 1], buf[i].y));
+        s = __fadd_rn(s, __fmul_rn(xs[k0 + 4 * i + 2], buf[i].z));
+        s = __fadd_rn(s, __fmul_rn(xs[k0 + 4 * i + 3], buf[i].w));
+      }
+    } else {
+      for (int k = 0; k < kn; ++k) s = __fadd_rn(s, __fmul_rn(xs[k0 + k], __ldg(wr + k)));
+    }
+    part[e * nkt + j] = s;
+  }
+  __syncthreads();
+  for (int64_t e = threadIdx.x; e < E; e += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < nkt; ++j) acc = __fadd_rn(acc, __fmul_rn(1.0f, part[e * nkt + j]));
+    logits[t * E + e] = acc;
   }
 }
 
@@ -132,14 +265,19 @@ cudaError_t launch_router(const float* x, const float* w, int64_t T, int64_t D, 
                           float* logits, float* probs, float* top, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   if (logits == nullptr) return cudaErrorInvalidValue;
-  const int nkt = (int)((D + kTile - 1) / kTile);
-  if (T * E <= 4096) {
-    int ppb = 256 / nkt;
-    if (ppb < 1) ppb = 1;
-    const int64_t blocks = (T * E + ppb - 1) / ppb;
-    const size_t smem = sizeof(float) * (size_t)ppb * nkt;
-    if (smem > 48 * 1024) return cudaErrorInvalidValue;
-    router_partials_kernel<<<(unsigned)blocks, 256, smem, st>>>(x, w, T, D, E, nkt, ppb, logits);
+  const int64_t nkt = (D + kTile - 1) / kTile;
+  const size_t token_smem = sizeof(float) * (size_t)(D + E * nkt);
+  const size_t chunk_smem = sizeof(float) * (size_t)(kTB * kXS + kEC * kXS + kTB * kEC * kJC + kTB * E);
+  static bool attrs = false;
+  if (!attrs) {
+    attrs = true;
+    (void)cudaFuncSetAttribute(router_token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    (void)cudaFuncSetAttribute(router_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  }
+  if (T < 128 && token_smem <= 200 * 1024) {
+    router_token_kernel<<<(unsigned)T, 512, token_smem, st>>>(x, w, D, E, logits);
+  } else if (chunk_smem <= 200 * 1024) {
+    router_chunk_kernel<<<(unsigned)((T + kTB - 1) / kTB), 256, chunk_smem, st>>>(x, w, T, D, E, logits);
   } else {
     dim3 grid((unsigned)((T + 15) / 16), (unsigned)((E + 63) / 64));
     router_tiled_kernel<<<grid, 256, 0, st>>>(x, w, T, D, E, logits);
