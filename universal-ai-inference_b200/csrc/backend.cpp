@@ -387,7 +387,7 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T) const {
   p.umma = path_ != 1 && umma_ok;
   p.umma_refused = path_ == 2 && !umma_ok;
   const int sms = 148;
-  auto pick_bn = [](double tpe) { return tpe <= 16 ? 16 : tpe <= 32 ? 32 : tpe <= 64 ? 64 : 128; };
+  auto pick_bn = [](double tpe) { return tpe <= 16 ? 16 : tpe <= 32 ? 32 : tpe <= 64 ? 64 : tpe <= 128 ? 128 : 256; };
   auto pick_splits = [&](int64_t tiles, int kchunks) {
     int64_t sp = tiles > 0 ? (2 * sms + tiles - 1) / tiles : 1;
     if (sp > 16) sp = 16;

@@ -362,26 +362,32 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
 // column).  Slot tiles up to 64 wide have two issuing threads: narrow MMAs are
 // bound by how fast one thread issues them, so the two take alternate quads of
 // every tile into their own accumulators and the epilogue adds the two.
+// 256-slot tiles: one accumulator (the epilogue of a tile runs once the next
+// tile's first A stages are made) and activation stages of one 64-K atom
+// (a whole quad of 256 activation rows does not fit twice in shared memory).
 template <int F, int BN, int A_Q, int B_Q, int P_ST>
 struct Cfg {
   static constexpr int kIssuers = BN <= 64 ? 2 : 1;
+  static constexpr bool kWide = BN == 256;
+  static constexpr int kAccBufs = kWide ? 1 : 2;
   using Fm = Fmt<F>;
   static constexpr int kWB = Fm::kBoxBytes;            // packed stage row stride
   static constexpr int kPStage = Fm::kBoxes * 128 * kWB;
   static constexpr int kBAtom = BN * 128;               // one 64-K box of BN activation rows
   static constexpr int kBQuad = 4 * kBAtom;
   static constexpr int kOffB = 0;
-  static constexpr int kOffP = kOffB + B_Q * kBQuad;
+  static constexpr int kBStage = kWide ? kBAtom : kBQuad;  // B_Q stages of this size
+  static constexpr int kOffP = kOffB + B_Q * kBStage;
   static constexpr int kOffBar = kOffP + P_ST * kPStage;
   // Stage release: one commit per quad arrives on rel[quad % kRelBars] and
   // frees that quad's A and B stages.  The producer of quad n waits for quad
   // n - depth; kRelBars >= depth keeps the barrier from moving on by a whole
   // phase before that producer has seen it.
-  static constexpr int kRelBars = A_Q > B_Q ? A_Q : B_Q;
-  static constexpr int kNumBars = 2 * P_ST + A_Q + B_Q + kRelBars + 4 + 2;
+  static constexpr int kRelBars = kWide ? A_Q : (A_Q > B_Q ? A_Q : B_Q);  // wide: A stages only
+  static constexpr int kNumBars = 2 * P_ST + A_Q + 2 * B_Q + kRelBars + 4 + 2;
   static constexpr int kSmem = kOffBar + kNumBars * 8 + 16 + 1024;  // + alignment slack
   static constexpr uint32_t kAccCols = BN < 32 ? 32 : BN;  // one accumulator
-  static constexpr uint32_t kACol0 = 2 * kIssuers * kAccCols;  // first A column
+  static constexpr uint32_t kACol0 = kAccBufs * kIssuers * kAccCols;  // first A column
   static constexpr uint32_t kUsedCols = kACol0 + A_Q * 128;
   static constexpr uint32_t kTmemCols = kUsedCols <= 256 ? 256 : 512;
   static_assert(kUsedCols <= 512, "tensor memory budget");
@@ -405,7 +411,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* a_full = pk_empty + P_ST;
   uint64_t* b_full = a_full + A_Q;
   uint64_t* rel = b_full + B_Q;               // [kRelBars]
-  uint64_t* acc_full = rel + C::kRelBars;     // [2]
+  uint64_t* b_empty = rel + C::kRelBars;      // [B_Q], wide tiles: activation atoms released per atom
+  uint64_t* acc_full = b_empty + B_Q;         // [2]
   uint64_t* acc_empty = acc_full + 2;         // [2]
   uint64_t* mma_done = acc_empty + 2;        // [2], one per issuer
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
@@ -420,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // every packed stage and every A stage is read / written by all 16 dequant warps
     for (int i = 0; i < P_ST; ++i) { mbar_init(pk_full + i, 1); mbar_init(pk_empty + i, kDqWarps); }
     for (int i = 0; i < A_Q; ++i) mbar_init(a_full + i, kDqWarps);
-    for (int i = 0; i < B_Q; ++i) mbar_init(b_full + i, 1);
+    for (int i = 0; i < B_Q; ++i) { mbar_init(b_full + i, 1); mbar_init(b_empty + i, 1); }
     for (int i = 0; i < C::kRelBars; ++i) mbar_init(rel + i, 1);
     for (int b = 0; b < 2; ++b) { mbar_init(acc_full + b, C::kIssuers); mbar_init(acc_empty + b, kDqWarps); }
     mbar_init(mma_done, 1);
@@ -503,16 +510,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         int q0, q1;
         quad_range(t, q0, q1);
         for (int q = q0; q < q1 && ok; ++q) {
-          const int bs = bi % B_Q;
-          if (!(ok = stage_free(bi, B_Q, kErrTimeoutProducer, 1))) break;
           const int na = quad_atoms(q);
-          if (elect_one()) {
-            mbar_arrive_expect_tx(b_full + bs, na * C::kBAtom);
-            for (int j = 0; j < na; ++j)
-              tma_load_2d(sB + bs * C::kBQuad + j * C::kBAtom, &tm_x, b_full + bs, q * kQuadK + 64 * j, slot0);
+          if constexpr (C::kWide) {  // one stage per atom
+            for (int j = 0; j < na && ok; ++j) {
+              const int bs = bi % B_Q;
+              if (!(ok = wait_bar(b_empty + bs, ((bi / B_Q) & 1) ^ 1, s_abort, err, kErrTimeoutProducer, 1 UAII_WS_ARG))) break;
+              if (elect_one()) {
+                mbar_arrive_expect_tx(b_full + bs, C::kBAtom);
+                tma_load_2d(sB + bs * C::kBStage, &tm_x, b_full + bs, q * kQuadK + 64 * j, slot0);
+              }
+              __syncwarp();
+              ++bi;
+            }
+          } else {  // one stage per quad
+            const int bs = bi % B_Q;
+            if (!(ok = stage_free(bi, B_Q, kErrTimeoutProducer, 1))) break;
+            if (elect_one()) {
+              mbar_arrive_expect_tx(b_full + bs, na * C::kBAtom);
+              for (int j = 0; j < na; ++j)
+                tma_load_2d(sB + bs * C::kBStage + j * C::kBAtom, &tm_x, b_full + bs, q * kQuadK + 64 * j, slot0);
+            }
+            __syncwarp();
+            ++bi;
           }
-          __syncwarp();
-          ++bi;
         }
       }
       for (uint32_t j = (bi > (uint32_t)B_Q ? bi - B_Q : 0); j < bi; ++j)
@@ -536,8 +556,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Tile t = decode_tile(args, tile, BN);
         int q0, q1;
         quad_range(t, q0, q1);
-        const uint32_t ab = it & 1;  // accumulator buffer of this tile
-        if (!(ok = wait_bar(acc_empty + ab, ((it >> 1) & 1) ^ 1, s_abort, err, kErrTimeoutMma, 2 UAII_WS_ARG))) break;
+        const uint32_t ab = it % C::kAccBufs;  // accumulator buffer of this tile
+        if (!(ok = wait_bar(acc_empty + ab, ((it / C::kAccBufs) & 1) ^ 1, s_abort, err, kErrTimeoutMma, 2 UAII_WS_ARG)))
+          break;
         tc_fence_after();
         const uint32_t dacc = tmem + (ab * C::kIssuers + me) * C::kAccCols;
         uint32_t acc = 0;
@@ -549,6 +570,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             continue;
           }
           if (!(ok = wait_bar(a_full + sa, pa, s_abort, err, kErrTimeoutMma, 3 UAII_WS_ARG))) break;
+          if constexpr (C::kWide) {
+            tc_fence_after();
+            const int na = quad_atoms(q);
+            const uint32_t at = tmem + C::kACol0 + sa * 128;
+            for (int j = 0; j < na && ok; ++j) {
+              if (!(ok = wait_bar(b_full + sb, pb, s_abort, err, kErrTimeoutMma, 4 UAII_WS_ARG))) break;
+              tc_fence_after();
+              const uint64_t bd = sw128_desc(smem_u32(sB + sb * C::kBStage));
+              if (elect_one()) {
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+                  mma_f16_ts(dacc, at + 32 * j + 8 * ks, bd + 2 * ks, idesc, acc);
+                  acc = 1;
+                }
+                mma_commit(b_empty + sb);
+              }
+              __syncwarp();
+              acc = 1;
+              sb = sb + 1 == B_Q ? (pb ^= 1, 0) : sb + 1;
+            }
+            if (!ok) break;
+            if (elect_one()) mma_commit(rel + sr);
+            __syncwarp();
+            sa = sa + 1 == A_Q ? (pa ^= 1, 0) : sa + 1;
+            sr = sr + 1 == C::kRelBars ? 0 : sr + 1;
+            continue;
+          }
           if (!(ok = wait_bar(b_full + sb, pb, s_abort, err, kErrTimeoutMma, 4 UAII_WS_ARG))) break;
           tc_fence_after();
 #ifdef UAII_UMMA_STATS
@@ -609,12 +657,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kCols = BN / kGroups;          // columns per group (>= 4)
     constexpr int kW = kCols >= 8 ? 8 : 4;       // columns per TMEM load
     auto epilogue = [&](const Tile& t, uint32_t e_it) -> bool {
-      if (!wait_bar(acc_full + (e_it & 1), (e_it >> 1) & 1, s_abort, err, kErrTimeoutEpilogue, 7 UAII_WS_ARG))
+      const uint32_t eb = e_it % C::kAccBufs;
+      if (!wait_bar(acc_full + eb, (e_it / C::kAccBufs) & 1, s_abort, err, kErrTimeoutEpilogue, 7 UAII_WS_ARG))
         return false;
       tc_fence_after();
       const int n_valid = min(BN, __ldg(args.counts + t.e) - t.n_tile * BN);
       const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
-      const uint32_t taddr = tmem + (e_it & 1) * C::kIssuers * C::kAccCols + ((uint32_t)(32 * q) << 16);
+      const uint32_t taddr = tmem + eb * C::kIssuers * C::kAccCols + ((uint32_t)(32 * q) << 16);
       int q0, q1;
       quad_range(t, q0, q1);
       const bool two = C::kIssuers == 2 && q1 - q0 >= 2;  // the second issuer's accumulator holds quads too
@@ -666,7 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty + (e_it & 1));
+      if (lane == 0) mbar_arrive(acc_empty + eb);
       return true;
     };
     Tile prev{};
@@ -718,6 +767,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         pending = true;
         pending_sa = sa;
+        // one accumulator: drain the previous tile as soon as the MMAs of this
+        // tile have A stages to start on (they wait for the drain)
+        if (C::kAccBufs == 1 && have_prev && qq - q0 + 1 == min(A_Q, q1 - q0)) {
+          announce();
+          if (!(ok = epilogue(prev, it - 1))) break;
+          have_prev = false;
+        }
 #ifdef UAII_UMMA_STATS
         wstats.cyc[9] += (unsigned long long)(clock64() - t_post);
         wstats.cnt[9] += 1;
@@ -726,7 +782,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       announce();  // the MMAs of this tile must be able to finish before any epilogue wait
-      if (have_prev && !(ok = epilogue(prev, it - 1))) break;
+      if (C::kAccBufs == 2 && have_prev && !(ok = epilogue(prev, it - 1))) break;
       prev = t;
       have_prev = true;
     }
@@ -842,11 +898,15 @@ template <int F, int BN>
 struct Stages {
   static constexpr int kBudget = 224 * 1024;  // stage bytes; barriers and alignment slack come on top
   static constexpr int A = BN <= 32 ? 3 : 2;
-  static constexpr int B = BN <= 32 ? 4 : (BN == 64 ? 3 : 2);
   static constexpr int kPStage = Fmt<F>::kBoxes * 128 * Fmt<F>::kBoxBytes;
-  static constexpr int P_fit = (kBudget - B * BN * 512) / kPStage;
-  static constexpr int P = P_fit > 8 ? 8 : P_fit;
-  static_assert(P >= 2, "shared-memory budget");
+  // 256-slot tiles: 2-3 packed stages, the rest for 32 KB activation atoms
+  static constexpr int P_wide = kPStage <= 20 * 1024 ? 3 : 2;
+  static constexpr int B_wide_fit = (kBudget - P_wide * kPStage) / (256 * 128);
+  static constexpr int B = BN == 256 ? (B_wide_fit > 6 ? 6 : B_wide_fit) : BN <= 32 ? 4 : (BN == 64 ? 3 : 2);
+  static constexpr int kBBytes = BN == 256 ? B * 256 * 128 : B * BN * 512;
+  static constexpr int P_fit = (kBudget - kBBytes) / kPStage;
+  static constexpr int P = BN == 256 ? P_wide : (P_fit > 8 ? 8 : P_fit);
+  static_assert(P >= 2 && B >= 2, "shared-memory budget");
 };
 
 template <int F, int BN>
@@ -864,6 +924,7 @@ cudaError_t dispatch_bn(int bn, const CUtensorMap& w0, const CUtensorMap& w1, co
     case 32: return run_cfg<F, 32>(w0, w1, x, a, st);
     case 64: return run_cfg<F, 64>(w0, w1, x, a, st);
     case 128: return run_cfg<F, 128>(w0, w1, x, a, st);
+    case 256: return run_cfg<F, 256>(w0, w1, x, a, st);
     default: return cudaErrorInvalidValue;
   }
 }
