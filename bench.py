@@ -45,15 +45,18 @@ WORKLOAD_NOTE = {
     "qwen3": "Qwen3-30B-A3B-shaped layer: d_model 2048, 128 experts top-8, d_ff 768, Q4_0",
     "qwen3_hot": "Qwen3-30B-A3B-shaped layer with a 4x hot expert",
 }
-# DRAM bytes per launch of the dominant kernel from an ncu capture
-# (profiles/*.md gives the command and the raw figures); None until captured.
-NCU_TRAFFIC = {}
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of the same
+# command (dram__bytes_read.sum + dram__bytes_write.sum); absent workloads report null.
+NCU_TRAFFIC = {
+    ("mixtral_T32", "gateup"): 529084672 + 5518336,
+    ("mixtral_T32", "down"): 398761984 + 4418304,
+}
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="mixtral")
@@ -75,58 +78,68 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event (throttle) reasons read through NVML every 2 ms
+    while the timed region runs (read-only queries)."""
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.proc = None
-        self.out = os.path.join("/tmp", f"uaii_clocks_{os.getpid()}.csv")
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self.err = None
+        self._stop = None
+        self._thread = None
+
+    def _handle(self, nv):
+        try:  # the CUDA device's NVML handle by PCI bus id (CUDA_VISIBLE_DEVICES may remap indices)
+            import torch
+            pr = torch.cuda.get_device_properties(self.dev)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:  # noqa: BLE001
+            return nv.nvmlDeviceGetHandleByIndex(self.dev)
 
     def __enter__(self):
+        import threading
         try:
-            self.f = open(self.out, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=self.f, stderr=subprocess.DEVNULL)
-        except (OSError, ValueError):
-            self.proc = None
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception as e:  # noqa: BLE001
+            self.err = f"NVML unavailable: {type(e).__name__}"
+            return self
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                    mask = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for name, bit in self.REASONS.items():
+                        if mask & bit:
+                            self.reasons.add(name)
+                except Exception:  # noqa: BLE001
+                    pass
+                self._stop.wait(0.002)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.f.close()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        if self.proc is None or not os.path.exists(self.out):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        with open(self.out) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    sm.append(float(parts[1]))
-                    smax.append(float(parts[2]))
-                except ValueError:
-                    continue
-                for n, v in zip(names, parts[5:9]):
-                    if v.lower() == "active":
-                        reasons.add(n)
-        os.unlink(self.out)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if self.err:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err]}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "NVML, 2 ms"}
 
 
 # ------------------------------------------------------------------ reference / CPU baseline
@@ -262,6 +275,7 @@ def main():
         phases, launches = be.profile_read()
         be.profile_enable(False)
     ms = ev0.elapsed_time(ev1)
+    plan = be.last_plan()
 
     def max_over_ranks(v: float) -> float:
         if dist is None:
@@ -297,23 +311,28 @@ def main():
     avg_s = dom_ms / max(dom_calls, 1) / 1e3
     S = T * cfg.top_k
     from uaii_moe import packed_nbytes
-    if dom == "gateup":
-        byts = touched * 2 * cfg.I * packed_nbytes(cfg.gate_fmt, cfg.D) + S * cfg.D * 4 + S * cfg.I * 4
+    act = 2 if plan["tensor_cores"] else 4  # bytes per activation element the kernel reads / writes
+    if dom == "gateup":  # packed gate+up rows of the touched experts, x in, h out
+        byts = touched * 2 * cfg.I * packed_nbytes(cfg.gate_fmt, cfg.D) + S * cfg.D * act + S * cfg.I * act
         fl = 2 * S * 2 * cfg.D * cfg.I
-    else:
-        byts = touched * cfg.D * packed_nbytes(cfg.down_fmt, cfg.I) + S * cfg.I * 4 + S * cfg.D * 4
+    else:  # packed down rows, h in, f32 partial sums out
+        byts = touched * cfg.D * packed_nbytes(cfg.down_fmt, cfg.I) + S * cfg.I * act + S * cfg.D * 4
         fl = 2 * S * cfg.D * cfg.I
     tokens_per_expert = S / max(touched, 1)
     if tokens_per_expert < 64:
         roof = {"bound": "hbm", "achieved": byts / avg_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s"}
     else:
-        roof = {"bound": "tensor", "achieved": fl / avg_s / 1e12, "peak": peaks["bf16_tflops_sustained"],
-                "unit": "TFLOP/s"}
+        roof = {"bound": "tensor", "achieved": fl / avg_s / 1e12, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "peak_sustained": peaks["bf16_tflops_sustained"]}
+        roof["frac_sustained"] = roof["achieved"] / roof["peak_sustained"]
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["traffic"] = NCU_TRAFFIC.get((workload, dom))
-    roof["kernel"] = f"{dom} phase ({'CUDA-core GEMV' if args.path in (0, 1) else 'tensor-core GEMM'})"
-    roof["peak_src"] = f"{peaks['src']} ({'hbm_gbs' if roof['bound'] == 'hbm' else 'bf16_tflops_sustained'})"
+    path = ("tensor-core grouped dequant-GEMM (tcgen05, f16 operands, f32 accumulate), "
+            f"{plan['slot_tile']}-slot tiles") if plan["tensor_cores"] else "CUDA-core f32 grouped GEMV"
+    roof["kernel"] = f"{dom} phase: {path}"
+    roof["peak_src"] = f"{peaks['src']} ({'hbm_gbs' if roof['bound'] == 'hbm' else 'bf16_tflops burst'})"
     roof["algorithmic_per_launch"] = byts if roof["bound"] == "hbm" else fl
+    roof["algorithmic_unit"] = "bytes" if roof["bound"] == "hbm" else "flops"
     roof["avg_launch_ms"] = avg_s * 1e3
 
     cpu = None
@@ -328,7 +347,9 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "scaling": "weak", "vs_baseline": None, "dtype": "f16" if plan["tensor_cores"] else "f32",
+                "dtype_note": "GGUF blocks dequantized to f16 tensor-core operands, f32 accumulation; router, "
+                              "softmax and combine in f32" if plan["tensor_cores"] else "f32 throughout",
                 "data": "synthetic (seeded random-init GGUF layer, N(0,1) activations)",
                 "config": {"workload": workload, "note": WORKLOAD_NOTE.get(args.config, ""),
                            "tokens_per_gpu": T, "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",

@@ -239,6 +239,13 @@ UAII_MOE_API int uaii_moe_release_weights(uaii_moe_backend* b, const void* host_
  * 2 = tensor-core grouped GEMM.  No reference counterpart. */
 UAII_MOE_API int uaii_moe_set_expert_path(uaii_moe_backend* b, int path);
 
+/* Schedule of the most recent expert-product call on this backend (routed
+ * experts): *tensor_cores = 1 for the tensor-core grouped GEMM, 0 for the
+ * CUDA-core GEMV; *slot_tile = routed slots per tile (MMA N); *down_splits =
+ * K splits of the down projection.  Any pointer may be NULL.  Diagnostic; no
+ * reference counterpart. */
+UAII_MOE_API int uaii_moe_last_plan(uaii_moe_backend* b, int* tensor_cores, int* slot_tile, int* down_splits);
+
 /* Device-side profile of the MoE phases, measured with CUDA events on the
  * backend's stream.  Phases: 0 router, 1 routing (top-k, permutation, gather),
  * 2 gate/up expert products + SwiGLU, 3 down expert products, 4 shared expert,

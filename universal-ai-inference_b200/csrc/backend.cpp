@@ -414,6 +414,7 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T) const {
 // `scores` rank the experts; `probs_for_w` supplies the weights (may equal scores).
 Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const float* probs_for_w,
                                   const LayerArgs& L, const ExpertPlan& P, int64_t T, float* yd) {
+  last_plan_ = P;
   const int64_t D = L.D, E = L.E, I = L.I;
   const int k = L.top_k;
   const int64_t S = T * k;
@@ -974,6 +975,15 @@ int uaii_moe_profile_read(uaii_moe_backend* b, double* phase_ms, uint64_t* phase
                           uint64_t* kernel_launches) {
   if (!b) return no_backend();
   return report(b->impl.profile_read(phase_ms, phase_calls, kernel_launches));
+}
+
+int uaii_moe_last_plan(uaii_moe_backend* b, int* tensor_cores, int* slot_tile, int* down_splits) {
+  if (!b) return no_backend();
+  const uaii_b200::ExpertPlan P = b->impl.last_plan();
+  if (tensor_cores) *tensor_cores = P.umma ? 1 : 0;
+  if (slot_tile) *slot_tile = P.bn;
+  if (down_splits) *down_splits = P.splits;
+  return report(Error::success());
 }
 
 int uaii_moe_set_expert_path(uaii_moe_backend* b, int path) {

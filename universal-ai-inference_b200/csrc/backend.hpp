@@ -119,6 +119,8 @@ class MoeCudaBackend {
   Error profile_enable(bool on);
   Error profile_read(double* ms, uint64_t* calls, uint64_t* launches);
   void set_expert_path(int p) { path_ = p; }
+  // Schedule chosen by the most recent expert-product call (routed experts).
+  ExpertPlan last_plan() const { return last_plan_; }
   cudaStream_t stream() const { return stream_; }
   int device() const { return device_; }
 
@@ -171,6 +173,7 @@ class MoeCudaBackend {
   cudaStream_t stream_ = nullptr;
   bool own_stream_ = false;
   int path_ = 0;
+  ExpertPlan last_plan_{};
   int* dev_err_ = nullptr;
   bool external_ = false;  // workspace and error flag belong to the caller
   char* ws_ = nullptr;

@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_char_p, c_double, c_float, c_int, c_int32, c_int64, c_size_t, c_uint64, c_void_p
+from ctypes import POINTER, byref, c_char_p, c_double, c_float, c_int, c_int32, c_int64, c_size_t, c_uint64, c_void_p
 
 import numpy as np
 
@@ -87,6 +87,7 @@ def _load():
         "uaii_moe_register_weights": (c_int, [c_void_p, c_void_p, c_uint64]),
         "uaii_moe_release_weights": (c_int, [c_void_p, c_void_p]),
         "uaii_moe_set_expert_path": (c_int, [c_void_p, c_int]),
+        "uaii_moe_last_plan": (c_int, [c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
         "uaii_moe_profile_enable": (c_int, [c_void_p, c_int]),
         "uaii_moe_profile_read": (c_int, [c_void_p, POINTER(c_double), POINTER(c_uint64), POINTER(c_uint64)]),
         "uaii_moe_packed_nbytes": (c_uint64, [c_int, c_int64]),
@@ -107,7 +108,7 @@ EXPORTED = ("uaii_moe_abi_version", "uaii_moe_last_error", "uaii_moe_backend_cre
             "uaii_moe_experts_swiglu", "uaii_moe_ffn_forward", "uaii_moe_ffn_forward_noalloc",
             "uaii_moe_register_weights",
             "uaii_moe_release_weights",
-            "uaii_moe_set_expert_path", "uaii_moe_profile_enable", "uaii_moe_profile_read",
+            "uaii_moe_set_expert_path", "uaii_moe_last_plan", "uaii_moe_profile_enable", "uaii_moe_profile_read",
             "uaii_moe_packed_nbytes", "uaii_moe_quantize_rows",
             "uaii_moe_fill_normal")
 
@@ -178,6 +179,13 @@ class Backend:
 
     def set_expert_path(self, path: int):
         _check(lib.uaii_moe_set_expert_path(self._h, path))
+
+    def last_plan(self) -> dict:
+        """Schedule of the most recent expert-product call: tensor cores or not,
+        slot tile width and down-projection K splits."""
+        tc, bn, sp = c_int(), c_int(), c_int()
+        _check(lib.uaii_moe_last_plan(self._h, byref(tc), byref(bn), byref(sp)))
+        return {"tensor_cores": bool(tc.value), "slot_tile": bn.value, "down_splits": sp.value}
 
     PHASES = ("router", "route", "gateup", "down", "shared", "combine")
 
