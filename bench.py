@@ -233,9 +233,25 @@ def main():
 
     lw = make_layer_weights(cfg)
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda() if a is not None else None
-    arrays = {"router_w": dev(lw.router_w), "gate": dev(lw.gate), "up": dev(lw.up), "down": dev(lw.down),
-              "shared": tuple(dev(a) for a in lw.shared) if lw.shared is not None else None}
-    L = lw.layer_struct(arrays)
+    # N > 1: expert parallelism (rank r holds experts [r*E/N, (r+1)*E/N) and its own tokens; NCCL
+    # all-to-all dispatch and combine every step).  Layers whose expert count N does not divide,
+    # or with a shared expert, run as independent replicas.
+    ep_mode = world > 1 and cfg.E % world == 0 and lw.shared is None
+    if ep_mode:
+        from uaii_moe.ep import ExpertParallelFFN
+        epr = cfg.E // world
+        part = slice(rank * epr, (rank + 1) * epr)
+        arrays = {"router_w": dev(lw.router_w), "gate": dev(lw.gate[part]), "up": dev(lw.up[part]),
+                  "down": dev(lw.down[part])}
+        local_layer = um.make_layer(cfg.D, epr, cfg.I, cfg.top_k, cfg.norm_topk, arrays["router_w"], arrays["gate"],
+                                    cfg.gate_fmt, arrays["up"], cfg.gate_fmt, arrays["down"], cfg.down_fmt)
+        router_layer = um.make_layer(cfg.D, cfg.E, cfg.I, cfg.top_k, cfg.norm_topk, arrays["router_w"],
+                                     arrays["gate"], cfg.gate_fmt, arrays["up"], cfg.gate_fmt, arrays["down"],
+                                     cfg.down_fmt)  # only the router fields are read by the dispatch
+    else:
+        arrays = {"router_w": dev(lw.router_w), "gate": dev(lw.gate), "up": dev(lw.up), "down": dev(lw.down),
+                  "shared": tuple(dev(a) for a in lw.shared) if lw.shared is not None else None}
+        L = lw.layer_struct(arrays)
     x_host = torch.from_numpy(make_tokens(cfg, T, rank)).pin_memory()
     y_host = torch.empty((T, cfg.D), dtype=torch.float32).pin_memory()
     x = x_host.cuda()
@@ -247,14 +263,25 @@ def main():
     if args.path:
         be.set_expert_path(args.path)
 
+    if ep_mode:
+        ep = ExpertParallelFFN(be, router_layer, local_layer, cfg.D, cfg.E, cfg.top_k, rank, world)
+
+        def forward(xin, yout, pr=None):
+            with torch.cuda.stream(stream):  # collectives order against the backend's stream
+                ep.forward(xin, yout, pr)
+    else:
+        def forward(xin, yout, pr=None):
+            be.ffn(L, xin, T, yout, pr)
+
     # routing statistics for the roofline (outside any timed region)
-    be.ffn(L, x, T, y, probs)
+    forward(x, y, probs)
     be.synchronize()
     ids = torch.topk(probs, cfg.top_k, dim=1).indices
     touched = int(torch.unique(ids).numel())
+    local_entries = ep.last_exchange[2] if ep_mode else T * cfg.top_k
 
     for _ in range(args.warmup):
-        be.ffn(L, x, T, y)
+        forward(x, y)
     be.synchronize()
 
     def barrier():
@@ -268,7 +295,7 @@ def main():
         be.profile_enable(True)
         ev0.record(stream)
         for _ in range(args.steps):
-            be.ffn(L, x, T, y)
+            forward(x, y)
         ev1.record(stream)
         torch.cuda.synchronize()
         barrier()
@@ -289,13 +316,25 @@ def main():
 
     e2e = None
     if not args.no_e2e:
+        if ep_mode:  # explicit copies: pinned host x in, host y out, on the backend stream
+            x_in = torch.empty_like(x)
+            y_out = torch.empty_like(y)
+
+            def e2e_step():
+                with torch.cuda.stream(stream):
+                    x_in.copy_(x_host, non_blocking=True)
+                    ep.forward(x_in, y_out)
+                    y_host.copy_(y_out, non_blocking=True)
+        else:
+            def e2e_step():
+                be.ffn(L, x_host, T, y_host)
         for _ in range(2):
-            be.ffn(L, x_host, T, y_host)
+            e2e_step()
         barrier()
         torch.cuda.synchronize()
         ev0.record(stream)
         for _ in range(args.steps):
-            be.ffn(L, x_host, T, y_host)
+            e2e_step()
         ev1.record(stream)
         torch.cuda.synchronize()
         barrier()
@@ -309,7 +348,10 @@ def main():
     dom = max(("gateup", "down"), key=lambda p: phases[p][0])
     dom_ms, dom_calls = phases[dom]
     avg_s = dom_ms / max(dom_calls, 1) / 1e3
-    S = T * cfg.top_k
+    # this rank's expert work: all its experts' packed rows and the (token, expert) pairs it served
+    S = local_entries
+    if ep_mode:
+        touched = cfg.E // world
     from uaii_moe import packed_nbytes
     act = 2 if plan["tensor_cores"] else 4  # bytes per activation element the kernel reads / writes
     if dom == "gateup":  # packed gate+up rows of the touched experts, x in, h out
@@ -352,7 +394,9 @@ def main():
                               "softmax and combine in f32" if plan["tensor_cores"] else "f32 throughout",
                 "data": "synthetic (seeded random-init GGUF layer, N(0,1) activations)",
                 "config": {"workload": workload, "note": WORKLOAD_NOTE.get(args.config, ""),
-                           "tokens_per_gpu": T, "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                           "tokens_per_gpu": T,
+                           "parallelism": (f"expert parallel x{world} (NCCL all-to-all dispatch/combine)" if ep_mode
+                                           else f"replicas x{world}" if world > 1 else "1 GPU"),
                            "l2": "inputs larger than L2 (packed expert weights re-read every step)",
                            "experts_touched": touched},
                 "e2e": e2e, "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu,

@@ -239,6 +239,44 @@ UAII_MOE_API int uaii_moe_release_weights(uaii_moe_backend* b, const void* host_
  * 2 = tensor-core grouped GEMM.  No reference counterpart. */
 UAII_MOE_API int uaii_moe_set_expert_path(uaii_moe_backend* b, int path);
 
+/* ---- Expert parallelism (one process per GPU, R ranks, rank r owns experts
+ * [r*E/R, (r+1)*E/R)).  No reference counterpart: the reference runs the layer in
+ * one host process (kernels::moe_experts_swiglu_f32,
+ * libs/uaii-kernels/src/transformer.cpp:564-609).  The caller moves the buffers
+ * between ranks (an all-to-all by rows, e.g. NCCL); every pointer is device
+ * memory on this backend's device.
+ *
+ * Step 1, on each rank for its own T tokens: router + top-k exactly as
+ * uaii_moe_ffn_forward, then each token is packed ONCE for every rank that owns
+ * one of its experts.  Rows are grouped by destination rank (token order inside
+ * a group).  Outputs (capacity T * min(top_k, world) rows):
+ *   send_x16   [rows, d_model] f16, elements [0, 2, 1, 3] of every group of four;
+ *   send_ids   [rows, top_k] destination-local expert id, -1 where that choice
+ *              lives on another rank;  send_w [rows, top_k] routing weight;
+ *   send_token [rows] source token;  row_of [T, world] row of (token, rank), -1;
+ *   send_counts, send_entries [world] rows and valid entries per destination;
+ *   probs [T, E] (optional).  `layer` supplies router_w, d_model, n_experts (all
+ *   ranks), top_k, norm_topk; its expert pointers are not read. */
+UAII_MOE_API int uaii_moe_ep_dispatch(uaii_moe_backend* b, const uaii_moe_layer* layer, const float* x, int64_t T,
+                                      int rank, int world, void* send_x16, int32_t* send_ids, float* send_w,
+                                      int32_t* send_token, int32_t* row_of, int32_t* send_counts,
+                                      int32_t* send_entries, float* probs);
+
+/* Step 2, on each rank for the rows it received (same layout as step 1's
+ * output, `entries` = valid (row, expert) pairs): `layer` holds this rank's
+ * experts (n_experts = E / world, their gate/up/down weights) and top_k; writes
+ * y_part [rows, d_model] f32 = sum over the row's entries of weight * expert
+ * output, in top-k order.  Tensor-core formats only; no shared expert. */
+UAII_MOE_API int uaii_moe_ep_experts(uaii_moe_backend* b, const uaii_moe_layer* layer, const void* recv_x16,
+                                     const int32_t* recv_ids, const float* recv_w, int64_t rows, int64_t entries,
+                                     float* y_part);
+
+/* Step 3, on each rank after the reverse exchange (y_back [rows, d_model] f32 in
+ * its own send-row order): y[t] = sum over ranks d = 0..world-1 of
+ * y_back[row_of[t, d]] (present rows, fixed rank order). */
+UAII_MOE_API int uaii_moe_ep_combine(uaii_moe_backend* b, const float* y_back, const int32_t* row_of, int64_t T,
+                                     int world, int64_t d_model, float* y);
+
 /* Schedule of the most recent expert-product call on this backend (routed
  * experts): *tensor_cores = 1 for the tensor-core grouped GEMM, 0 for the
  * CUDA-core GEMV; *slot_tile = routed slots per tile (MMA N); *down_splits =

@@ -380,9 +380,9 @@ Error MoeCudaBackend::router(const float* x, const float* gate_w, int64_t T, int
 }
 
 // Which expert-product schedule a layer call uses, and its tile shape.
-ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T) const {
+ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t slots) const {
   ExpertPlan p;
-  const int64_t S = T * L.top_k;
+  const int64_t S = slots >= 0 ? slots : T * L.top_k;
   const bool umma_ok = umma_shapes_supported(L.gate.fmt, L.down.fmt, L.D, L.I);
   p.umma = path_ != 1 && umma_ok;
   p.umma_refused = path_ == 2 && !umma_ok;
@@ -413,8 +413,11 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T) const {
 // Routing + expert products + combine for device-resident x.
 // `scores` rank the experts; `probs_for_w` supplies the weights (may equal scores).
 Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const float* probs_for_w,
-                                  const LayerArgs& L, const ExpertPlan& P, int64_t T, float* yd) {
+                                  const LayerArgs& L, const ExpertPlan& P, int64_t T, float* yd, const EpRows* ep) {
   last_plan_ = P;
+  if (ep && !P.umma)
+    return Error::make(ErrorCode::NotImplemented,
+                       "expert-parallel rows need the tensor-core path (Q4_0/Q8_0/Q4_K/Q6_K, 16-byte row pitches)");
   const int64_t D = L.D, E = L.E, I = L.I;
   const int k = L.top_k;
   const int64_t S = T * k;
@@ -441,14 +444,22 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
   float* out = nullptr;
   int splits = 1;
   phase_begin(kRoute);
-  UAII_CUDA(launch_route_topk(scores, probs_for_w, T, E, k, L.norm_topk, rb, stream_), "route_topk");
+  if (ep) {
+    UAII_CUDA(launch_ep_route(ep->ids, ep->w, T, E, k, rb, stream_), "ep_route");
+  } else {
+    UAII_CUDA(launch_route_topk(scores, probs_for_w, T, E, k, L.norm_topk, rb, stream_), "route_topk");
+  }
   UAII_CUDA(launch_route_scan(T, E, k, rb, stream_), "route_scan");
   if (P.umma) {
     void* xp16 = carve(2 * (size_t)(S * D));
     void* h16 = carve(2 * (size_t)(S * I));
     splits = P.splits;
     out = static_cast<float*>(carve(sizeof(float) * (size_t)(splits * S * D)));
-    UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, nullptr, xp16, stream_), "route_gather");
+    if (ep) {
+      UAII_CUDA(launch_route_gather16(ep->x16, T, D, E, k, rb, xp16, stream_), "route_gather16");
+    } else {
+      UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, nullptr, xp16, stream_), "route_gather");
+    }
     phase_end();
     count_launches(3);
     phase_begin(kGateUp);
@@ -580,6 +591,92 @@ Error check_layer(const LayerArgs& L) {
 }
 
 }  // namespace
+
+// ---------------------------------------------------------------- expert parallelism
+
+Error MoeCudaBackend::ep_dispatch(const LayerArgs& L, const float* x, int64_t T, int rank, int world,
+                                  void* send_x16, int32_t* send_ids, float* send_w, int32_t* send_token,
+                                  int32_t* row_of, int32_t* send_counts, int32_t* send_entries, float* probs) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaSetDevice(device_), "SetDevice");
+  const int64_t D = L.D, E = L.E;
+  const int k = L.top_k;
+  if (!L.router_w || D <= 0 || E <= 0 || k < 1 || k > 32 || k > E || T < 0)
+    return Error::make(ErrorCode::InvalidArgument, "ep dispatch: router weight, d_model, n_experts, top_k");
+  if (world < 1 || world > 255 || rank < 0 || rank >= world || E % world != 0)
+    return Error::make(ErrorCode::InvalidArgument, "ep dispatch: world must divide n_experts (1..255 ranks)");
+  for (const void* p : {static_cast<const void*>(x), static_cast<const void*>(L.router_w),
+                        static_cast<const void*>(send_x16),
+                        static_cast<const void*>(send_ids), static_cast<const void*>(send_w),
+                        static_cast<const void*>(send_token), static_cast<const void*>(row_of),
+                        static_cast<const void*>(send_counts), static_cast<const void*>(send_entries)})
+    if (!is_device_ptr(p)) return Error::make(ErrorCode::InvalidArgument, "ep dispatch: arguments must be device memory");
+  if (probs && !is_device_ptr(probs)) return Error::make(ErrorCode::InvalidArgument, "ep dispatch: probs must be device memory");
+  const size_t lb = sizeof(float) * (size_t)(T * E);
+  UAII_TRY(reserve(3 * align_up(lb) + 2 * align_up(sizeof(int32_t) * (size_t)(T * k)) + align_up((size_t)(E * T)) +
+                   align_up((size_t)(world * T)) + align_up(sizeof(int32_t) * (size_t)(T * world)) +
+                   align_up(sizeof(int32_t) * (size_t)world) + 4 * kAlign));
+  float* logits = static_cast<float*>(carve(lb));
+  float* po = probs ? probs : static_cast<float*>(carve(lb));
+  RouteBuffers rb{};
+  rb.topk_ids = static_cast<int32_t*>(carve(sizeof(int32_t) * (size_t)(T * k)));
+  rb.topk_w = static_cast<float*>(carve(sizeof(float) * (size_t)(T * k)));
+  rb.mask = static_cast<uint8_t*>(carve((size_t)(E * T)));
+  uint8_t* dmask = static_cast<uint8_t*>(carve((size_t)(world * T)));
+  int32_t* rowpos = static_cast<int32_t*>(carve(sizeof(int32_t) * (size_t)(T * world)));
+  int32_t* dcounts = static_cast<int32_t*>(carve(sizeof(int32_t) * (size_t)world));
+  const int epr = (int)(E / world);
+  phase_begin(kRouter);
+  UAII_CUDA(launch_router(x, L.router_w, T, D, E, logits, po, nullptr, stream_), "router");
+  phase_end();
+  phase_begin(kRoute);
+  UAII_CUDA(launch_route_topk(logits, po, T, E, k, L.norm_topk, rb, stream_), "route_topk");
+  UAII_CUDA(launch_ep_plan(rb.topk_ids, T, k, world, epr, dmask, rowpos, dcounts, stream_), "ep_plan");
+  UAII_CUDA(launch_ep_pack(x, T, D, k, world, epr, rb.topk_ids, rb.topk_w, dmask, rowpos, dcounts, send_x16, send_ids,
+                           send_w, send_token, row_of, send_counts, send_entries, stream_),
+            "ep_pack");
+  phase_end();
+  count_launches(7);
+  (void)rank;
+  return Error::success();
+}
+
+Error MoeCudaBackend::ep_experts(const LayerArgs& Lin, const void* recv_x16, const int32_t* recv_ids,
+                                 const float* recv_w, int64_t N, int64_t entries, float* y_part) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaSetDevice(device_), "SetDevice");
+  LayerArgs L = Lin;
+  UAII_TRY(check_layer(L));
+  if (L.I_sh > 0)
+    return Error::make(ErrorCode::NotImplemented, "ep experts: the shared expert runs on the token's own rank");
+  if (N < 0 || entries < 0 || entries > N * L.top_k)
+    return Error::make(ErrorCode::InvalidArgument, "ep experts: rows / entries");
+  if (N == 0) return Error::success();
+  for (const void* p : {static_cast<const void*>(recv_x16), static_cast<const void*>(recv_ids),
+                        static_cast<const void*>(recv_w),
+                        static_cast<const void*>(y_part)})
+    if (!is_device_ptr(p)) return Error::make(ErrorCode::InvalidArgument, "ep experts: arguments must be device memory");
+  const ExpertPlan P = plan_experts(L, N, entries);
+  UAII_TRY(reserve(experts_ws_bytes(L, N, P) + layer_stage_bytes(L)));
+  const EpRows rows{recv_x16, recv_ids, recv_w};
+  return run_experts(nullptr, nullptr, nullptr, L, P, N, y_part, &rows);
+}
+
+Error MoeCudaBackend::ep_combine(const float* y_back, const int32_t* row_of, int64_t T, int world, int64_t D,
+                                 float* y) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaSetDevice(device_), "SetDevice");
+  if (T < 0 || D <= 0 || world < 1) return Error::make(ErrorCode::InvalidArgument, "ep combine: shapes");
+  if (T == 0) return Error::success();
+  for (const void* p : {static_cast<const void*>(y_back), static_cast<const void*>(row_of),
+                        static_cast<const void*>(y)})
+    if (!is_device_ptr(p)) return Error::make(ErrorCode::InvalidArgument, "ep combine: arguments must be device memory");
+  phase_begin(kCombine);
+  UAII_CUDA(launch_ep_combine(y_back, row_of, T, world, D, y, stream_), "ep_combine");
+  phase_end();
+  count_launches(1);
+  return Error::success();
+}
 
 namespace {
 size_t expert_bytes(const ExpertWeights& w, int64_t E) { return (size_t)(E * w.rows) * row_bytes(w.fmt, w.cols); }
@@ -975,6 +1072,37 @@ int uaii_moe_profile_read(uaii_moe_backend* b, double* phase_ms, uint64_t* phase
                           uint64_t* kernel_launches) {
   if (!b) return no_backend();
   return report(b->impl.profile_read(phase_ms, phase_calls, kernel_launches));
+}
+
+int uaii_moe_ep_dispatch(uaii_moe_backend* b, const uaii_moe_layer* l, const float* x, int64_t T, int rank, int world,
+                         void* send_x16, int32_t* send_ids, float* send_w, int32_t* send_token, int32_t* row_of,
+                         int32_t* send_counts, int32_t* send_entries, float* probs) {
+  if (!b) return no_backend();
+  if (!l) return report(Error::make(ErrorCode::InvalidArgument, "null layer"));
+  LayerArgs L{};
+  L.D = l->d_model;
+  L.E = l->n_experts;
+  L.top_k = l->top_k;
+  L.norm_topk = l->norm_topk;
+  L.router_w = l->router_w;
+  return report(b->impl.ep_dispatch(L, x, T, rank, world, send_x16, send_ids, send_w, send_token, row_of,
+                                    send_counts, send_entries, probs));
+}
+
+int uaii_moe_ep_experts(uaii_moe_backend* b, const uaii_moe_layer* l, const void* recv_x16, const int32_t* recv_ids,
+                        const float* recv_w, int64_t rows, int64_t entries, float* y_part) {
+  if (!b) return no_backend();
+  if (!l) return report(Error::make(ErrorCode::InvalidArgument, "null layer"));
+  LayerArgs L;
+  if (!layer_args_from_c(l, &L))
+    return report(Error::make(ErrorCode::InvalidArgument, "ep experts: null expert weights"));
+  return report(b->impl.ep_experts(L, recv_x16, recv_ids, recv_w, rows, entries, y_part));
+}
+
+int uaii_moe_ep_combine(uaii_moe_backend* b, const float* y_back, const int32_t* row_of, int64_t T, int world,
+                        int64_t d_model, float* y) {
+  if (!b) return no_backend();
+  return report(b->impl.ep_combine(y_back, row_of, T, world, d_model, y));
 }
 
 int uaii_moe_last_plan(uaii_moe_backend* b, int* tensor_cores, int* slot_tile, int* down_splits) {

@@ -114,6 +114,14 @@ class MoeCudaBackend {
                 int64_t I, int top_k, int norm_topk, float* y);
   Error ffn(const LayerArgs& L, const float* x, int64_t T, float* y, float* probs);
 
+  // Expert parallelism (device pointers only).  See include/uaii_moe.h.
+  Error ep_dispatch(const LayerArgs& L, const float* x, int64_t T, int rank, int world, void* send_x16,
+                    int32_t* send_ids, float* send_w, int32_t* send_token, int32_t* row_of, int32_t* send_counts,
+                    int32_t* send_entries, float* probs);
+  Error ep_experts(const LayerArgs& L_local, const void* recv_x16, const int32_t* recv_ids, const float* recv_w,
+                   int64_t rows, int64_t entries, float* y_part);
+  Error ep_combine(const float* y_back, const int32_t* row_of, int64_t T, int world, int64_t D, float* y);
+
   Error register_weights(const void* host_ptr, size_t bytes);
   Error release_weights(const void* host_ptr);
   Error profile_enable(bool on);
@@ -137,9 +145,18 @@ class MoeCudaBackend {
   Error stage_input(const void* p, size_t bytes, void* scratch, const void** dev, bool* was_host);
   Error reserve(size_t bytes);
   void* carve(size_t bytes);
-  ExpertPlan plan_experts(const LayerArgs& L, int64_t T) const;
+  // `slots`: routed (token, expert) pairs when known (expert-parallel rows), else T * top_k.
+  ExpertPlan plan_experts(const LayerArgs& L, int64_t T, int64_t slots = -1) const;
+  // Rows received by an expert-parallel rank: f16 activations in operand order and
+  // top_k (local expert | -1, weight) entries per row; replaces the router output.
+  struct EpRows {
+    const void* x16;
+    const int32_t* ids;
+    const float* w;
+  };
   Error run_experts(const float* x_dev, const float* scores, const float* probs_for_w,
-                    const LayerArgs& L, const ExpertPlan& P, int64_t T, float* y_dev);
+                    const LayerArgs& L, const ExpertPlan& P, int64_t T, float* y_dev,
+                    const EpRows* ep = nullptr);
   Error sync_and_check();
 
  public:

@@ -39,6 +39,28 @@ cudaError_t launch_route_scan(int64_t T, int64_t E, int k, const RouteBuffers& r
 // Gathers x rows into expert-contiguous slots: xp_f32 and/or xp_f16 (either may be null).
 // xp_f16 rows are in the tensor-core operand order: elements [0, 2, 1, 3] of
 // every group of four (the expert GEMM builds its weight tiles the same way).
+// ---- expert parallelism (ep.cu).  Rank r of R owns experts [r*epr, (r+1)*epr).
+// dmask [R*T] bytes, rowpos [T*R], dcounts [R]: which ranks each token goes to and
+// its row inside each destination group (token order).
+cudaError_t launch_ep_plan(const int32_t* topk_ids, int64_t T, int k, int R, int epr, uint8_t* dmask,
+                           int32_t* rowpos, int32_t* dcounts, cudaStream_t st);
+// Packs the send rows grouped by destination: f16 x (operand order), k (local
+// expert | -1, weight) entries, source token; row_of [T*R] (-1 where none);
+// send_counts / send_entries [R]: rows and valid entries per destination.
+cudaError_t launch_ep_pack(const float* x, int64_t T, int64_t D, int k, int R, int epr, const int32_t* topk_ids,
+                           const float* topk_w, const uint8_t* dmask, const int32_t* rowpos,
+                           const int32_t* dcounts, void* send_x16, int32_t* send_ids, float* send_w,
+                           int32_t* send_token, int32_t* row_of, int32_t* send_counts, int32_t* send_entries,
+                           cudaStream_t st);
+// Receiving side: routing tables (topk_ids/w, expert mask) from received entries.
+cudaError_t launch_ep_route(const int32_t* ids, const float* w, int64_t N, int64_t E, int k,
+                            const RouteBuffers& rb, cudaStream_t st);
+// Gather of received f16 rows into expert-contiguous slots (absent entries skipped).
+cudaError_t launch_route_gather16(const void* rows, int64_t N, int64_t D, int64_t E, int k, const RouteBuffers& rb,
+                                  void* xp16, cudaStream_t st);
+// y[t] = sum over d = 0..R-1 of y_back[row_of[t*R+d]] (rows that exist), fixed order.
+cudaError_t launch_ep_combine(const float* y_back, const int32_t* row_of, int64_t T, int R, int64_t D, float* y,
+                              cudaStream_t st);
 cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E, int k,
                                 const RouteBuffers& rb, float* xp_f32, void* xp_f16,
                                 cudaStream_t st);

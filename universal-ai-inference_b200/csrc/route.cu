@@ -185,6 +185,7 @@ __global__ void combine_kernel(const float* __restrict__ out, int64_t ld, int sp
   const int64_t t = i / d4, c = i - t * d4;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int r = 0; r < k; ++r) {
+    if (rb.topk_ids[t * k + r] < 0) continue;  // absent entry (expert-parallel rows)
     const int slot = rb.slot_of[t * k + r];
     const float w = rb.topk_w[t * k + r];
     const float4 o = sum_planes(out, ((int64_t)slot * ld) / 4 + c, splits, stride);
@@ -213,6 +214,7 @@ __global__ void combine1_kernel(const float* __restrict__ out, int64_t ld, int s
   const int64_t t = i / D, c = i - t * D;
   float acc = 0.f;
   for (int r = 0; r < k; ++r) {
+    if (rb.topk_ids[t * k + r] < 0) continue;  // absent entry (expert-parallel rows)
     const int64_t at = (int64_t)rb.slot_of[t * k + r] * ld + c;
     float o = out[at];
     for (int s = 1; s < splits; ++s) o = __fadd_rn(o, out[at + s * stride]);

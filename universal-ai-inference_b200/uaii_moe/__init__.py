@@ -88,6 +88,11 @@ def _load():
         "uaii_moe_release_weights": (c_int, [c_void_p, c_void_p]),
         "uaii_moe_set_expert_path": (c_int, [c_void_p, c_int]),
         "uaii_moe_last_plan": (c_int, [c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
+        "uaii_moe_ep_dispatch": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+        "uaii_moe_ep_experts": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
+                                        c_void_p]),
+        "uaii_moe_ep_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p]),
         "uaii_moe_profile_enable": (c_int, [c_void_p, c_int]),
         "uaii_moe_profile_read": (c_int, [c_void_p, POINTER(c_double), POINTER(c_uint64), POINTER(c_uint64)]),
         "uaii_moe_packed_nbytes": (c_uint64, [c_int, c_int64]),
@@ -108,7 +113,8 @@ EXPORTED = ("uaii_moe_abi_version", "uaii_moe_last_error", "uaii_moe_backend_cre
             "uaii_moe_experts_swiglu", "uaii_moe_ffn_forward", "uaii_moe_ffn_forward_noalloc",
             "uaii_moe_register_weights",
             "uaii_moe_release_weights",
-            "uaii_moe_set_expert_path", "uaii_moe_last_plan", "uaii_moe_profile_enable", "uaii_moe_profile_read",
+            "uaii_moe_set_expert_path", "uaii_moe_last_plan", "uaii_moe_ep_dispatch", "uaii_moe_ep_experts",
+            "uaii_moe_ep_combine", "uaii_moe_profile_enable", "uaii_moe_profile_read",
             "uaii_moe_packed_nbytes", "uaii_moe_quantize_rows",
             "uaii_moe_fill_normal")
 
@@ -223,6 +229,20 @@ class Backend:
 
     def ffn(self, layer: Layer, x, T: int, y, probs=None):
         _check(lib.uaii_moe_ffn_forward(self._h, ctypes.byref(layer), ptr(x), T, ptr(y), ptr(probs)))
+
+    # ---- expert parallelism (device tensors; see include/uaii_moe.h)
+    def ep_dispatch(self, layer: Layer, x, T: int, rank: int, world: int, send_x16, send_ids, send_w, send_token,
+                    row_of, send_counts, send_entries, probs=None):
+        _check(lib.uaii_moe_ep_dispatch(self._h, ctypes.byref(layer), ptr(x), T, rank, world, ptr(send_x16),
+                                        ptr(send_ids), ptr(send_w), ptr(send_token), ptr(row_of), ptr(send_counts),
+                                        ptr(send_entries), ptr(probs)))
+
+    def ep_experts(self, layer: Layer, recv_x16, recv_ids, recv_w, rows: int, entries: int, y_part):
+        _check(lib.uaii_moe_ep_experts(self._h, ctypes.byref(layer), ptr(recv_x16), ptr(recv_ids), ptr(recv_w),
+                                       rows, entries, ptr(y_part)))
+
+    def ep_combine(self, y_back, row_of, T: int, world: int, d_model: int, y):
+        _check(lib.uaii_moe_ep_combine(self._h, ptr(y_back), ptr(row_of), T, world, d_model, ptr(y)))
 
     def dispatch(self, op_name: str, inputs, outputs, attrs: dict | None = None, op_version="1"):
         """inputs/outputs: lists of tensor_desc(...) tuples; attrs: {key: int|float|bool}."""
