@@ -277,6 +277,14 @@ UAII_MOE_API int uaii_moe_ep_experts(uaii_moe_backend* b, const uaii_moe_layer* 
 UAII_MOE_API int uaii_moe_ep_combine(uaii_moe_backend* b, const float* y_back, const int32_t* row_of, int64_t T,
                                      int world, int64_t d_model, float* y);
 
+/* Failure-path self-test: launches one block whose threads wait, through the
+ * same bounded wait as the tensor-core kernels, on a barrier nothing arrives
+ * on; they give up after budget_cycles (1e3..4e9 SM cycles) and record an
+ * error code without faulting the device.  Returns UAII_MOE_INTERNAL with the
+ * code in uaii_moe_last_error() when the path works; the backend stays usable.
+ * Diagnostic; no reference counterpart. */
+UAII_MOE_API int uaii_moe_selftest_wait_timeout(uaii_moe_backend* b, int64_t budget_cycles);
+
 /* Schedule of the most recent expert-product call on this backend (routed
  * experts): *tensor_cores = 1 for the tensor-core grouped GEMM, 0 for the
  * CUDA-core GEMV; *slot_tile = routed slots per tile (MMA N); *down_splits =

@@ -662,6 +662,16 @@ Error MoeCudaBackend::ep_experts(const LayerArgs& Lin, const void* recv_x16, con
   return run_experts(nullptr, nullptr, nullptr, L, P, N, y_part, &rows);
 }
 
+Error MoeCudaBackend::selftest_wait_timeout(int64_t budget_cycles) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaSetDevice(device_), "SetDevice");
+  constexpr int kSelftestCode = 9;
+  UAII_CUDA(launch_wait_timeout_selftest(dev_err_, (long long)budget_cycles, kSelftestCode, stream_),
+            "wait_timeout_selftest");
+  count_launches(1);
+  return sync_and_check();
+}
+
 Error MoeCudaBackend::ep_combine(const float* y_back, const int32_t* row_of, int64_t T, int world, int64_t D,
                                  float* y) {
   std::lock_guard<std::mutex> lk(mu_);
@@ -1103,6 +1113,11 @@ int uaii_moe_ep_combine(uaii_moe_backend* b, const float* y_back, const int32_t*
                         int64_t d_model, float* y) {
   if (!b) return no_backend();
   return report(b->impl.ep_combine(y_back, row_of, T, world, d_model, y));
+}
+
+int uaii_moe_selftest_wait_timeout(uaii_moe_backend* b, int64_t budget_cycles) {
+  if (!b) return no_backend();
+  return report(b->impl.selftest_wait_timeout(budget_cycles));
 }
 
 int uaii_moe_last_plan(uaii_moe_backend* b, int* tensor_cores, int* slot_tile, int* down_splits) {

@@ -121,6 +121,8 @@ class MoeCudaBackend {
   Error ep_experts(const LayerArgs& L_local, const void* recv_x16, const int32_t* recv_ids, const float* recv_w,
                    int64_t rows, int64_t entries, float* y_part);
   Error ep_combine(const float* y_back, const int32_t* row_of, int64_t T, int world, int64_t D, float* y);
+  // Runs the bounded-wait self-test kernel and returns the status the host observes.
+  Error selftest_wait_timeout(int64_t budget_cycles);
 
   Error register_weights(const void* host_ptr, size_t bytes);
   Error release_weights(const void* host_ptr);

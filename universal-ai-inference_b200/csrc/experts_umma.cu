@@ -344,17 +344,7 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
 #else
   (void)site;
 #endif
-  if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (*abort) return false;
-    if (clock64() - t0 > kWaitCycles) {
-      *abort = 1;
-      atomicExch(err, code);
-      return false;
-    }
-  }
-  return true;
+  return bounded_wait(bar, parity, abort, err, code);
 }
 
 // Tensor memory: two accumulator buffers per issuing thread, then the A ring

@@ -39,6 +39,11 @@ cudaError_t launch_route_scan(int64_t T, int64_t E, int k, const RouteBuffers& r
 // Gathers x rows into expert-contiguous slots: xp_f32 and/or xp_f16 (either may be null).
 // xp_f16 rows are in the tensor-core operand order: elements [0, 2, 1, 3] of
 // every group of four (the expert GEMM builds its weight tiles the same way).
+// Self-test of the bounded-wait failure path (selftest.cu): one block waits on
+// an mbarrier nothing arrives on, gives up after budget_cycles and records
+// `code` in *err.  Faults nothing; the kernel returns normally.
+cudaError_t launch_wait_timeout_selftest(int* err, long long budget_cycles, int code, cudaStream_t st);
+
 // ---- expert parallelism (ep.cu).  Rank r of R owns experts [r*epr, (r+1)*epr).
 // dmask [R*T] bytes, rowpos [T*R], dcounts [R]: which ranks each token goes to and
 // its row inside each destination group (token order).

@@ -61,6 +61,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return true;
 }
 
+// Wait for the phase with `parity` of `bar` while no other role has given up
+// (*abort) and at most `budget` cycles: on timeout sets *abort and records
+// `code` in the device error word *err (the host turns it into an error status).
+__device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code,
+                                             long long budget = kWaitCycles) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (clock64() - t0 > budget) {
+      *abort = 1;
+      atomicExch(err, code);
+      return false;
+    }
+  }
+  return true;
+}
+
 // One lane of the (converged) warp returns true.
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;

@@ -28,6 +28,7 @@ BLOCK = {F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q5_0: (32, 22
          Q6_K: (256, 210)}
 
 OK = 0
+INVALID_ARGUMENT, NOT_FOUND, NOT_IMPLEMENTED, INTERNAL = 1, 2, 7, 8
 STATUS_NAMES = {0: "Ok", 1: "InvalidArgument", 2: "NotFound", 3: "IoError", 4: "ConfigError",
                 5: "PluginError", 6: "AbiMismatch", 7: "NotImplemented", 8: "Internal"}
 
@@ -93,6 +94,7 @@ def _load():
         "uaii_moe_ep_experts": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                                         c_void_p]),
         "uaii_moe_ep_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p]),
+        "uaii_moe_selftest_wait_timeout": (c_int, [c_void_p, c_int64]),
         "uaii_moe_profile_enable": (c_int, [c_void_p, c_int]),
         "uaii_moe_profile_read": (c_int, [c_void_p, POINTER(c_double), POINTER(c_uint64), POINTER(c_uint64)]),
         "uaii_moe_packed_nbytes": (c_uint64, [c_int, c_int64]),
@@ -114,7 +116,8 @@ EXPORTED = ("uaii_moe_abi_version", "uaii_moe_last_error", "uaii_moe_backend_cre
             "uaii_moe_register_weights",
             "uaii_moe_release_weights",
             "uaii_moe_set_expert_path", "uaii_moe_last_plan", "uaii_moe_ep_dispatch", "uaii_moe_ep_experts",
-            "uaii_moe_ep_combine", "uaii_moe_profile_enable", "uaii_moe_profile_read",
+            "uaii_moe_ep_combine", "uaii_moe_selftest_wait_timeout", "uaii_moe_profile_enable",
+            "uaii_moe_profile_read",
             "uaii_moe_packed_nbytes", "uaii_moe_quantize_rows",
             "uaii_moe_fill_normal")
 
@@ -240,6 +243,10 @@ class Backend:
     def ep_experts(self, layer: Layer, recv_x16, recv_ids, recv_w, rows: int, entries: int, y_part):
         _check(lib.uaii_moe_ep_experts(self._h, ctypes.byref(layer), ptr(recv_x16), ptr(recv_ids), ptr(recv_w),
                                        rows, entries, ptr(y_part)))
+
+    def selftest_wait_timeout(self, budget_cycles: int):
+        """Bounded-wait failure path on the device; raises UaiiMoeError (Internal) when it works."""
+        _check(lib.uaii_moe_selftest_wait_timeout(self._h, budget_cycles))
 
     def ep_combine(self, y_back, row_of, T: int, world: int, d_model: int, y):
         _check(lib.uaii_moe_ep_combine(self._h, ptr(y_back), ptr(row_of), T, world, d_model, ptr(y)))
