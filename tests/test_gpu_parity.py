@@ -77,7 +77,10 @@ def test_router_golden(backend, golden):
 
 
 @pytest.mark.parametrize("T,D,E", [(1, 4096, 8), (32, 4096, 8), (4096, 4096, 8), (257, 2048, 60),
-                                   (1000, 2048, 128), (3, 100, 5)])
+                                   (1000, 2048, 128), (3, 100, 5),
+                                   (300, 1000, 40),    # many experts, a partial last k tile
+                                   (130, 998, 33),     # many experts, rows not float4-aligned
+                                   (200, 512, 256)])   # more experts than one block covers
 def test_router_vs_oracle(backend, oracle, um, T, D, E):
     x = um.fill_normal((T, D), 5, T)
     w = um.fill_normal((E, D), 5, E + 99, 0.0, 0.02)
@@ -330,19 +333,40 @@ def test_tensor_core_path_vs_oracle(backend, oracle, um, gf, df, T, D, E, I, k):
     assert rel_err(y, y_ref) <= REL_TOL
 
 
-def test_tensor_core_path_refuses_unaligned_pitch(backend, um):
-    # Q6_K rows of 256 elements are 210 bytes: not a 16-byte pitch for TMA
-    D, E, I = 256, 4, 256
-    x, w, G, U, Dn = layer_case(um, 14, 16, 2, D, E, I, 2, 3)
+@pytest.mark.parametrize("gf,df,T,D,E,I,k", [
+    (14, 16, 5, 256, 4, 256, 2),      # Q6_K rows of 256 elements: 210 bytes, not a 16-byte pitch
+    (11, 11, 40, 256, 6, 1408, 4),    # Q8_0 rows of 1408 elements (the Qwen2-MoE down projection): 1496 bytes
+    (7, 7, 24, 256, 4, 320, 2),       # Q4_0 rows of 320 elements: 180 bytes; last quad of 64 elements
+])
+def test_tensor_core_path_pads_unaligned_pitch(backend, oracle, um, gf, df, T, D, E, I, k):
+    # rows whose byte pitch is not a multiple of 16 cannot be TMA tensor-map rows: the
+    # backend stages a copy with padded rows, bytes unchanged
+    x, w, G, U, Dn = layer_case(um, gf, df, T, D, E, I, k, 90 + I)
+    _, pr, _ = oracle.router(x, w)
+    y_ref, _, _ = oracle.experts_packed(x, G, gf, U, gf, Dn, df, pr, E, I, k, 1)
+    y = np.empty_like(x)
+    backend.set_expert_path(2)
+    try:
+        backend.ffn(um.make_layer(D, E, I, k, 1, w, G, gf, U, gf, Dn, df), x, T, y)
+        assert backend.last_plan()["tensor_cores"]
+    finally:
+        backend.set_expert_path(0)
+    assert rel_err(y, y_ref) <= REL_TOL
+
+
+def test_tensor_core_path_refuses_unsupported_shapes(backend, um):
+    # d_model must be a multiple of 128 (the weight-row tile of the down projection)
+    D, E, I = 96, 4, 256
+    x, w, G, U, Dn = layer_case(um, 7, 7, 2, D, E, I, 2, 3)
     y = np.empty_like(x)
     backend.set_expert_path(2)
     try:
         with pytest.raises(um.UaiiMoeError) as e:
-            backend.ffn(um.make_layer(D, E, I, 2, 1, w, G, 14, U, 14, Dn, 16), x, 2, y)
+            backend.ffn(um.make_layer(D, E, I, 2, 1, w, G, 7, U, 7, Dn, 7), x, 2, y)
         assert e.value.status == 7
     finally:
         backend.set_expert_path(0)
-    backend.ffn(um.make_layer(D, E, I, 2, 1, w, G, 14, U, 14, Dn, 16), x, 2, y)  # automatic: CUDA cores
+    backend.ffn(um.make_layer(D, E, I, 2, 1, w, G, 7, U, 7, Dn, 7), x, 2, y)  # automatic: CUDA cores
 
 
 def test_tensor_core_shared_expert(backend, oracle, um):

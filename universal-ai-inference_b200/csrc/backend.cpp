@@ -412,19 +412,37 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t s
 
 // Routing + expert products + combine for device-resident x.
 // `scores` rank the experts; `probs_for_w` supplies the weights (may equal scores).
+// Packed rows as the tensor-core path reads them: in place when the row pitch is a
+// multiple of 16 bytes (TMA strides), else a copy with each row padded to 16 bytes.
+Error MoeCudaBackend::umma_rows(const void* w, int fmt, int64_t rows, int64_t K, const void** out, int64_t* pitch) {
+  const int64_t rb = (int64_t)row_bytes(fmt, K);
+  if (rb % 16 == 0) {
+    *out = w;
+    *pitch = rb;
+    return Error::success();
+  }
+  const int64_t pp = umma_pitch(fmt, K);
+  void* d = carve((size_t)(rows * pp));
+  UAII_CUDA(launch_pad_rows(w, rb, rows, rb, d, pp, stream_), "pad_rows");
+  count_launches(1);
+  *out = d;
+  *pitch = pp;
+  return Error::success();
+}
+
 Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const float* probs_for_w,
                                   const LayerArgs& L, const ExpertPlan& P, int64_t T, float* yd, const EpRows* ep) {
   last_plan_ = P;
   if (ep && !P.umma)
     return Error::make(ErrorCode::NotImplemented,
-                       "expert-parallel rows need the tensor-core path (Q4_0/Q8_0/Q4_K/Q6_K, 16-byte row pitches)");
+                       "expert-parallel rows need the tensor-core path (Q4_0/Q8_0/Q4_K/Q6_K, tile-multiple shapes)");
   const int64_t D = L.D, E = L.E, I = L.I;
   const int k = L.top_k;
   const int64_t S = T * k;
   if (P.umma_refused)
     return Error::make(ErrorCode::NotImplemented,
-                       "tensor-core path needs Q4_0/Q8_0/Q4_K/Q6_K weights, d_ff % 64 == 0, d_model % 128 == 0 "
-                       "and 16-byte row pitches");
+                       "tensor-core path needs Q4_0/Q8_0/Q4_K/Q6_K weights, d_ff % 64 == 0 and d_model % 128 == 0 "
+                       "(Q4_K/Q6_K: both multiples of 256)");
   RouteBuffers rb{};
   rb.topk_ids = static_cast<int32_t*>(carve(sizeof(int32_t) * S));
   rb.topk_w = static_cast<float*>(carve(sizeof(float) * S));
@@ -463,13 +481,17 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
     phase_end();
     count_launches(3);
     phase_begin(kGateUp);
-    UAII_CUDA(launch_gateup_umma(L.gate.fmt, gd, ud, E, I, D, xp16, S, rb.counts, rb.offsets, tile_base, P.bn, h16,
-                                 dev_err_, stream_),
+    int64_t gpitch = 0, dpitch = 0;
+    UAII_TRY(umma_rows(gd, L.gate.fmt, E * I, D, &gd, &gpitch));
+    UAII_TRY(umma_rows(ud, L.up.fmt, E * I, D, &ud, &gpitch));
+    UAII_TRY(umma_rows(dd, L.down.fmt, E * D, I, &dd, &dpitch));
+    UAII_CUDA(launch_gateup_umma(L.gate.fmt, gd, ud, gpitch, E, I, D, xp16, S, rb.counts, rb.offsets, tile_base, P.bn,
+                                 h16, dev_err_, stream_),
               "gateup(tensor cores)");
     phase_end();
     phase_begin(kDown);
-    UAII_CUDA(launch_down_umma(L.down.fmt, dd, E, D, I, h16, S, rb.counts, rb.offsets, tile_base, P.bn, splits, out,
-                               dev_err_, stream_),
+    UAII_CUDA(launch_down_umma(L.down.fmt, dd, dpitch, E, D, I, h16, S, rb.counts, rb.offsets, tile_base, P.bn, splits,
+                               out, dev_err_, stream_),
               "down(tensor cores)");
     phase_end();
     count_launches(4);
@@ -512,10 +534,14 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
       sh_splits = P.sh_splits;
       sh_out = static_cast<float*>(carve(sizeof(float) * (size_t)(sh_splits * T * D)));
       UAII_CUDA(launch_to_f16(xd, T * D, x16, stream_), "shared_to_f16");
-      UAII_CUDA(launch_gateup_umma(L.gate_sh.fmt, sg, su, 1, Is, D, x16, T, sh_route + 2, sh_route, sh_tiles,
+      int64_t sgp = 0, sdp = 0;
+      UAII_TRY(umma_rows(sg, L.gate_sh.fmt, Is, D, &sg, &sgp));
+      UAII_TRY(umma_rows(su, L.up_sh.fmt, Is, D, &su, &sgp));
+      UAII_TRY(umma_rows(sd, L.down_sh.fmt, D, Is, &sd, &sdp));
+      UAII_CUDA(launch_gateup_umma(L.gate_sh.fmt, sg, su, sgp, 1, Is, D, x16, T, sh_route + 2, sh_route, sh_tiles,
                                    P.sh_bn, sh_h16, dev_err_, stream_),
                 "shared_gateup(tensor cores)");
-      UAII_CUDA(launch_down_umma(L.down_sh.fmt, sd, 1, D, Is, sh_h16, T, sh_route + 2, sh_route, sh_tiles, P.sh_bn,
+      UAII_CUDA(launch_down_umma(L.down_sh.fmt, sd, sdp, 1, D, Is, sh_h16, T, sh_route + 2, sh_route, sh_tiles, P.sh_bn,
                                  sh_splits, sh_out, dev_err_, stream_),
                 "shared_down(tensor cores)");
       count_launches(6);
@@ -554,16 +580,22 @@ size_t experts_ws_bytes(const LayerArgs& L, int64_t T, const ExpertPlan& P) {
   size_t b = 0;
   b += 5 * align_up(sizeof(int32_t) * S) + align_up((size_t)(L.E * T));
   b += 3 * align_up(sizeof(int32_t) * (L.E + 1));
-  if (P.umma)
+  if (P.umma) {
     b += align_up(2 * (size_t)(S * L.D)) + align_up(2 * (size_t)(S * L.I)) +
          align_up(sizeof(float) * (size_t)(P.splits * S * L.D));
+    if (row_bytes(L.gate.fmt, L.D) % 16) b += 2 * align_up((size_t)(L.E * L.I * umma_pitch(L.gate.fmt, L.D)));
+    if (row_bytes(L.down.fmt, L.I) % 16) b += align_up((size_t)(L.E * L.D * umma_pitch(L.down.fmt, L.I)));
+  }
   else
     b += 2 * align_up(sizeof(float) * S * L.D) + align_up(sizeof(float) * S * L.I);
   if (L.I_sh > 0) {
     b += 2 * kAlign + align_up(sizeof(float) * T);
-    if (P.sh_umma)
+    if (P.sh_umma) {
       b += align_up(2 * (size_t)(T * L.D)) + align_up(2 * (size_t)(T * L.I_sh)) +
            align_up(sizeof(float) * (size_t)(P.sh_splits * T * L.D));
+      if (row_bytes(L.gate_sh.fmt, L.D) % 16) b += 2 * align_up((size_t)(L.I_sh * umma_pitch(L.gate_sh.fmt, L.D)));
+      if (row_bytes(L.down_sh.fmt, L.I_sh) % 16) b += align_up((size_t)(L.D * umma_pitch(L.down_sh.fmt, L.I_sh)));
+    }
     else
       b += align_up(sizeof(float) * T * L.I_sh) + align_up(sizeof(float) * T * L.D);
   }

@@ -160,6 +160,7 @@ class MoeCudaBackend {
                     const LayerArgs& L, const ExpertPlan& P, int64_t T, float* y_dev,
                     const EpRows* ep = nullptr);
   Error sync_and_check();
+  Error umma_rows(const void* w, int fmt, int64_t rows, int64_t K, const void** out, int64_t* pitch);
 
  public:
   Error sync_and_check_public() {

@@ -939,15 +939,14 @@ bool make_weight_maps(CUtensorMap* m0, CUtensorMap* m1, const void* W0, const vo
          make_weight_map(m1, W1, pitch, rows_total, Fmt<F>::kBoxBytes);
 }
 
-cudaError_t launch_common(int fmt, bool gateup, const void* W0, const void* W1, int64_t E, int64_t rows,
-                          int64_t K, const void* act16, int64_t S_rows, const int32_t* counts,
+cudaError_t launch_common(int fmt, bool gateup, const void* W0, const void* W1, int64_t pitch, int64_t E,
+                          int64_t rows, int64_t K, const void* act16, int64_t S_rows, const int32_t* counts,
                           const int32_t* offsets, int32_t* tile_base, int bn, int splits, void* h16,
                           float* out, int64_t out_ld, int64_t split_stride, int* err, cudaStream_t st) {
   const int mk = min_k(fmt);
   if (!mk || K % mk != 0 || K <= 0) return cudaErrorNotSupported;
-  const int64_t pitch = fmt_row_bytes(fmt, K);
   const int m_rows = gateup ? 64 : 128;
-  if (rows % m_rows != 0 || pitch % 16 != 0) return cudaErrorNotSupported;
+  if (rows % m_rows != 0 || pitch % 16 != 0 || pitch < fmt_row_bytes(fmt, K)) return cudaErrorNotSupported;
   if (!aligned16(W0) || !aligned16(W1) || !aligned16(act16) || K % 8 != 0) return cudaErrorNotSupported;
   const int kquads = (int)((K + kQuadK - 1) / kQuadK);
   if (splits < 1) splits = 1;
@@ -1013,21 +1012,49 @@ bool umma_format_supported(int fmt) { return min_k(fmt) != 0; }
 bool umma_shapes_supported(int gfmt, int dfmt, int64_t D, int64_t I) {
   if (!umma_format_supported(gfmt) || !umma_format_supported(dfmt)) return false;
   if (D % min_k(gfmt) || I % min_k(dfmt) || I % 64 || D % 128) return false;
-  return fmt_row_bytes(gfmt, D) % 16 == 0 && fmt_row_bytes(dfmt, I) % 16 == 0 && D % 8 == 0 && I % 8 == 0;
+  return D % 8 == 0 && I % 8 == 0;
 }
 
-cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t E, int64_t I, int64_t D,
+int64_t umma_pitch(int fmt, int64_t K) { return (fmt_row_bytes(fmt, K) + 15) / 16 * 16; }
+
+cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pitch, int64_t E, int64_t I, int64_t D,
                                const void* xp16, int64_t S_rows, const int32_t* counts, const int32_t* offsets,
                                int32_t* tile_base, int bn, void* h16, int* err, cudaStream_t st) {
-  return launch_common(fmt, true, G, U, E, I, D, xp16, S_rows, counts, offsets, tile_base, bn, 1, h16, nullptr,
-                       I, 0, err, st);
+  return launch_common(fmt, true, G, U, pitch, E, I, D, xp16, S_rows, counts, offsets, tile_base, bn, 1, h16,
+                       nullptr, I, 0, err, st);
 }
 
-cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t E, int64_t D, int64_t I, const void* h16,
+cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
                              int64_t S_rows, const int32_t* counts, const int32_t* offsets, int32_t* tile_base,
                              int bn, int splits, float* out, int* err, cudaStream_t st) {
-  return launch_common(fmt, false, Dn, Dn, E, D, I, h16, S_rows, counts, offsets, tile_base, bn, splits, nullptr,
-                       out, D, S_rows * D, err, st);
+  return launch_common(fmt, false, Dn, Dn, pitch, E, D, I, h16, S_rows, counts, offsets, tile_base, bn, splits,
+                       nullptr, out, D, S_rows * D, err, st);
+}
+
+namespace {
+// One thread per 16-bit unit of the padded destination (row bytes are even for every GGUF format).
+__global__ void pad_rows_kernel(const uint16_t* __restrict__ src, int64_t src_pitch2, int64_t rows, int64_t row2,
+                                uint16_t* __restrict__ dst, int64_t dst_pitch2) {
+  const int64_t n = rows * dst_pitch2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / dst_pitch2, c = i - r * dst_pitch2;
+    dst[i] = c < row2 ? src[r * src_pitch2 + c] : (uint16_t)0;
+  }
+}
+}  // namespace
+
+cudaError_t launch_pad_rows(const void* src, int64_t src_pitch, int64_t rows, int64_t row_bytes, void* dst,
+                            int64_t dst_pitch, cudaStream_t st) {
+  if ((src_pitch | row_bytes | dst_pitch) & 1 || (reinterpret_cast<uintptr_t>(src) & 1) || dst_pitch % 16 ||
+      row_bytes > dst_pitch || row_bytes > src_pitch)
+    return cudaErrorInvalidValue;
+  if (rows == 0) return cudaSuccess;
+  const int64_t n = rows * (dst_pitch / 2);
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  pad_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(static_cast<const uint16_t*>(src), src_pitch / 2, rows,
+                                                     row_bytes / 2, static_cast<uint16_t*>(dst), dst_pitch / 2);
+  return cudaGetLastError();
 }
 
 int umma_kchunks(int fmt, int64_t K) {

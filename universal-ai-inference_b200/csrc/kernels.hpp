@@ -96,18 +96,26 @@ cudaError_t launch_down_simt(int dfmt, const void* Dn, int64_t E, int64_t D, int
 
 // ---- experts_umma.cu: tensor-core grouped GEMM (tcgen05 + TMEM + TMA)
 bool umma_format_supported(int fmt);
-// whole-layer check: formats, K chunking, 16-byte row pitches, tile multiples
+// whole-layer check: formats, K chunking and tile multiples (any row pitch: rows that
+// are not 16-byte aligned are staged with a padded pitch, see launch_pad_rows)
 bool umma_shapes_supported(int gate_fmt, int down_fmt, int64_t D, int64_t I);
 int umma_kchunks(int fmt, int64_t K);
+// Row pitch the tensor-core path reads a packed matrix with: row_bytes rounded up to 16.
+int64_t umma_pitch(int fmt, int64_t K);
 // h16[slot, i] = silu(x.G[e,i]) * (x.U[e,i]) in f16; x is xp16 [S_rows, D] f16.
+// G, U rows `pitch` bytes apart (a multiple of 16).
 // tile_base: scratch of E+1 ints.  *err receives a nonzero code if a wait timed out.
-cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t E, int64_t I, int64_t D,
+cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pitch, int64_t E, int64_t I, int64_t D,
                                const void* xp16, int64_t S_rows, const int32_t* counts,
                                const int32_t* offsets, int32_t* tile_base, int bn, void* h16, int* err,
                                cudaStream_t st);
 // out[split][slot, o] = partial of h16[slot] . Dn[e, o] over the split's K range (f32).
-cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t E, int64_t D, int64_t I, const void* h16,
+cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
                              int64_t S_rows, const int32_t* counts, const int32_t* offsets,
                              int32_t* tile_base, int bn, int splits, float* out, int* err, cudaStream_t st);
+// Copies `rows` packed rows of row_bytes (even) from src (src_pitch apart) to dst
+// (dst_pitch apart, a multiple of 16), zero-filling each row's padding.
+cudaError_t launch_pad_rows(const void* src, int64_t src_pitch, int64_t rows, int64_t row_bytes, void* dst,
+                            int64_t dst_pitch, cudaStream_t st);
 
 }  // namespace uaii_b200

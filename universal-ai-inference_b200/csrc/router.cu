@@ -5,7 +5,8 @@
 // (RefGemm::gemm_f32, libs/uaii-kernels/src/gemm_ref.cpp:45-75): for each
 // 64-wide k tile, s = 0 then s += x*w sequentially; c (from 0) += s tile by
 // tile.  Every multiply and add is a separate round-to-nearest operation.
-// Three schedules compute the same values:
+// Four schedules compute the same values (the block schedule, for many experts,
+// is described at router_block_kernel):
 //   * token (small batches): one block per token, one thread per (k tile,
 //     expert) partial, then one thread per expert adds the partials in order;
 //   * chunk: a block owns 16 tokens and walks the row in chunks of 16 k tiles
@@ -137,6 +138,92 @@ __global__ void __launch_bounds__(256) router_chunk_kernel(const float* __restri
     const int l2 = (int)(i / E);
     const int64_t t = t0 + l2;
     if (t < T) logits[t * E + (i - l2 * E)] = run[i];
+  }
+}
+
+// Many experts (E >= 32): thread (token group, expert group) owns the logits of
+// kRT tokens x kRE experts for the whole row.  Tile by tile (x and w of one 64-wide
+// k tile staged in shared memory, k-major), it builds the tile's partials in k
+// order and folds them into its running logits in tile order -- the reference
+// order without any cross-thread combine.  Block: 256 threads = TG x EG groups.
+constexpr int kRT = 4;  // tokens per thread
+constexpr int kRE = 8;  // experts per thread
+
+__global__ void __launch_bounds__(256) router_block_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                           int64_t T, int64_t D, int64_t E, int EG,
+                                                           float* __restrict__ logits) {
+  extern __shared__ float sm[];
+  const int TG = 256 / EG, TB = TG * kRT, EB = EG * kRE;
+  const int XS = TB + 4, WS = EB + 4;  // padded k rows
+  float* xs = sm;                      // [kTile][XS]
+  float* ws = xs + kTile * XS;         // [kTile][WS]
+  const int tid = threadIdx.x, eg = tid % EG, tg = tid / EG;  // EG divides 256: every thread has a group
+  const int64_t t0 = (int64_t)blockIdx.x * TB, e0 = (int64_t)blockIdx.y * EB;
+  float c[kRT][kRE];
+#pragma unroll
+  for (int a = 0; a < kRT; ++a)
+#pragma unroll
+    for (int b = 0; b < kRE; ++b) c[a][b] = 0.f;
+  const bool vec = (D & 3) == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
+  for (int64_t k0 = 0; k0 < D; k0 += kTile) {
+    const int kn = (int)((k0 + kTile < D) ? kTile : D - k0);
+    __syncthreads();
+    if (vec && kn == kTile) {  // coalesced float4 loads, transposed into k-major rows
+      for (int i = tid; i < TB * (kTile / 4); i += 256) {
+        const int r = i / (kTile / 4), k4 = i - r * (kTile / 4);
+        const float4 v = (t0 + r < T) ? __ldg(reinterpret_cast<const float4*>(x + (t0 + r) * D + k0) + k4)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        xs[(4 * k4) * XS + r] = v.x; xs[(4 * k4 + 1) * XS + r] = v.y;
+        xs[(4 * k4 + 2) * XS + r] = v.z; xs[(4 * k4 + 3) * XS + r] = v.w;
+      }
+      for (int i = tid; i < EB * (kTile / 4); i += 256) {
+        const int r = i / (kTile / 4), k4 = i - r * (kTile / 4);
+        const float4 v = (e0 + r < E) ? __ldg(reinterpret_cast<const float4*>(w + (e0 + r) * D + k0) + k4)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        ws[(4 * k4) * WS + r] = v.x; ws[(4 * k4 + 1) * WS + r] = v.y;
+        ws[(4 * k4 + 2) * WS + r] = v.z; ws[(4 * k4 + 3) * WS + r] = v.w;
+      }
+    } else {
+      for (int i = tid; i < TB * kTile; i += 256) {
+        const int r = i / kTile, k = i - r * kTile;
+        xs[k * XS + r] = (t0 + r < T && k < kn) ? __ldg(x + (t0 + r) * D + k0 + k) : 0.f;
+      }
+      for (int i = tid; i < EB * kTile; i += 256) {
+        const int r = i / kTile, k = i - r * kTile;
+        ws[k * WS + r] = (e0 + r < E && k < kn) ? __ldg(w + (e0 + r) * D + k0 + k) : 0.f;
+      }
+    }
+    __syncthreads();
+    float sacc[kRT][kRE];
+#pragma unroll
+    for (int a = 0; a < kRT; ++a)
+#pragma unroll
+      for (int b = 0; b < kRE; ++b) sacc[a][b] = 0.f;
+    for (int k = 0; k < kn; ++k) {
+      const float4 xv = *reinterpret_cast<const float4*>(xs + k * XS + tg * kRT);
+      const float4 wa = *reinterpret_cast<const float4*>(ws + k * WS + eg * kRE);
+      const float4 wb = *reinterpret_cast<const float4*>(ws + k * WS + eg * kRE + 4);
+      const float xa[kRT] = {xv.x, xv.y, xv.z, xv.w};
+      const float wv[kRE] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+      for (int a = 0; a < kRT; ++a)
+#pragma unroll
+        for (int b = 0; b < kRE; ++b) sacc[a][b] = __fadd_rn(sacc[a][b], __fmul_rn(xa[a], wv[b]));
+    }
+#pragma unroll
+    for (int a = 0; a < kRT; ++a)
+#pragma unroll
+      for (int b = 0; b < kRE; ++b) c[a][b] = __fadd_rn(c[a][b], __fmul_rn(1.0f, sacc[a][b]));
+  }
+#pragma unroll
+  for (int a = 0; a < kRT; ++a) {
+    const int64_t t = t0 + tg * kRT + a;
+    if (t >= T) continue;
+#pragma unroll
+    for (int b = 0; b < kRE; ++b) {
+      const int64_t e = e0 + eg * kRE + b;
+      if (e < E) logits[t * E + e] = c[a][b];
+    }
   }
 }
 
@@ -273,8 +360,15 @@ cudaError_t launch_router(const float* x, const float* w, int64_t T, int64_t D, 
     attrs = true;
     (void)cudaFuncSetAttribute(router_token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     (void)cudaFuncSetAttribute(router_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    (void)cudaFuncSetAttribute(router_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   }
-  if (T < 128 && token_smem <= 200 * 1024) {
+  if (E >= 32 && T >= 128) {
+    const int eb = E <= 32 ? 32 : E <= 64 ? 64 : 128;  // expert groups (4, 8, 16) divide the 256 threads
+    const int EG = eb / kRE, TB = (256 / EG) * kRT;
+    const size_t smem = sizeof(float) * (size_t)(kTile * (TB + 4) + kTile * (eb + 4));
+    dim3 grid((unsigned)((T + TB - 1) / TB), (unsigned)((E + eb - 1) / eb));
+    router_block_kernel<<<grid, 256, smem, st>>>(x, w, T, D, E, EG, logits);
+  } else if (T < 128 && token_smem <= 200 * 1024) {
     router_token_kernel<<<(unsigned)T, 512, token_smem, st>>>(x, w, D, E, logits);
   } else if (chunk_smem <= 200 * 1024) {
     router_chunk_kernel<<<(unsigned)((T + kTB - 1) / kTB), 256, chunk_smem, st>>>(x, w, T, D, E, logits);
