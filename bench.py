@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="mixtral")
     ap.add_argument("--tokens", type=int, default=4096)
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="weak: --tokens per GPU; strong: --tokens in total, split across the GPUs")
     ap.add_argument("--path", type=int, default=0, help="0 auto, 1 CUDA-core GEMV, 2 tensor-core GEMM")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -199,8 +201,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     from uaii_moe.synthetic import CONFIGS, algorithmic_bytes, flops, make_layer_weights, make_tokens
     cfg = CONFIGS[args.config]
-    T = args.tokens
-    workload = f"{args.config}_T{T}"
+    T = args.tokens if args.scaling == "weak" else args.tokens // max(1, int(os.environ.get("WORLD_SIZE", "1")))
+    workload = f"{args.config}_T{args.tokens}" + ("" if args.scaling == "weak" else "_total")
 
     if args.impl == "reference":
         if rank != 0:
@@ -210,7 +212,7 @@ def main():
         xs = make_tokens(cfg, n, 0)
         tps, cores, kind = cpu_reference_run(cfg, lw, xs, args.steps, args.warmup)
         line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus,
-                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": args.scaling,
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF layer)",
                 "config": {"workload": workload, "note": WORKLOAD_NOTE.get(args.config, ""),
                            "tokens_per_step": n},
@@ -389,7 +391,7 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f16" if plan["tensor_cores"] else "f32",
+                "scaling": args.scaling, "vs_baseline": None, "dtype": "f16" if plan["tensor_cores"] else "f32",
                 "dtype_note": "GGUF blocks dequantized to f16 tensor-core operands, f32 accumulation; router, "
                               "softmax and combine in f32" if plan["tensor_cores"] else "f32 throughout",
                 "data": "synthetic (seeded random-init GGUF layer, N(0,1) activations)",

@@ -80,7 +80,9 @@ def test_router_golden(backend, golden):
                                    (1000, 2048, 128), (3, 100, 5),
                                    (300, 1000, 40),    # many experts, a partial last k tile
                                    (130, 998, 33),     # many experts, rows not float4-aligned
-                                   (200, 512, 256)])   # more experts than one block covers
+                                   (200, 512, 256),    # more experts than one block covers
+                                   (40, 2048, 128),    # few tokens: rows split across blocks, folded in order
+                                   (600, 1000, 60)])   # split rows with a partial last tile
 def test_router_vs_oracle(backend, oracle, um, T, D, E):
     x = um.fill_normal((T, D), 5, T)
     w = um.fill_normal((E, D), 5, E + 99, 0.0, 0.02)

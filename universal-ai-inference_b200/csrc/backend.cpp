@@ -348,12 +348,14 @@ Error MoeCudaBackend::router(const float* x, const float* gate_w, int64_t T, int
   if (!probs || !top) return Error::make(ErrorCode::InvalidArgument, "moe router outs");
   const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E),
                tb = sizeof(float) * (size_t)T;
-  UAII_TRY(reserve(align_up(xb) + 3 * align_up(pb) + align_up(tb) + 4 * kAlign +
+  const size_t rsb = router_scratch_bytes(T, D, E);
+  UAII_TRY(reserve(align_up(xb) + 3 * align_up(pb) + align_up(tb) + align_up(rsb) + 5 * kAlign +
                    weight_stage_bytes(gate_w, sizeof(float) * (size_t)(E * D))));
   void* xs = carve(xb);
   float* ls = static_cast<float*>(carve(pb));
   float* ps = static_cast<float*>(carve(pb));
   float* ts = static_cast<float*>(carve(tb));
+  float* rscratch = rsb ? static_cast<float*>(carve(rsb)) : nullptr;
   const void* xd = nullptr;
   const void* wd = nullptr;
   bool xh = false;
@@ -367,7 +369,7 @@ Error MoeCudaBackend::router(const float* x, const float* gate_w, int64_t T, int
   float* to = th ? ts : top;
   phase_begin(kRouter);
   UAII_CUDA(launch_router(static_cast<const float*>(xd), static_cast<const float*>(wd), T, D, E,
-                          lo, po, to, stream_),
+                          lo, po, to, stream_, rscratch, rsb),
             "router");
   phase_end();
   count_launches(2);
@@ -645,9 +647,10 @@ Error MoeCudaBackend::ep_dispatch(const LayerArgs& L, const float* x, int64_t T,
     if (!is_device_ptr(p)) return Error::make(ErrorCode::InvalidArgument, "ep dispatch: arguments must be device memory");
   if (probs && !is_device_ptr(probs)) return Error::make(ErrorCode::InvalidArgument, "ep dispatch: probs must be device memory");
   const size_t lb = sizeof(float) * (size_t)(T * E);
+  const size_t rsb = router_scratch_bytes(T, D, E);
   UAII_TRY(reserve(3 * align_up(lb) + 2 * align_up(sizeof(int32_t) * (size_t)(T * k)) + align_up((size_t)(E * T)) +
                    align_up((size_t)(world * T)) + align_up(sizeof(int32_t) * (size_t)(T * world)) +
-                   align_up(sizeof(int32_t) * (size_t)world) + 4 * kAlign));
+                   align_up(sizeof(int32_t) * (size_t)world) + align_up(rsb) + 5 * kAlign));
   float* logits = static_cast<float*>(carve(lb));
   float* po = probs ? probs : static_cast<float*>(carve(lb));
   RouteBuffers rb{};
@@ -657,9 +660,10 @@ Error MoeCudaBackend::ep_dispatch(const LayerArgs& L, const float* x, int64_t T,
   uint8_t* dmask = static_cast<uint8_t*>(carve((size_t)(world * T)));
   int32_t* rowpos = static_cast<int32_t*>(carve(sizeof(int32_t) * (size_t)(T * world)));
   int32_t* dcounts = static_cast<int32_t*>(carve(sizeof(int32_t) * (size_t)world));
+  float* rscratch = rsb ? static_cast<float*>(carve(rsb)) : nullptr;
   const int epr = (int)(E / world);
   phase_begin(kRouter);
-  UAII_CUDA(launch_router(x, L.router_w, T, D, E, logits, po, nullptr, stream_), "router");
+  UAII_CUDA(launch_router(x, L.router_w, T, D, E, logits, po, nullptr, stream_, rscratch, rsb), "router");
   phase_end();
   phase_begin(kRoute);
   UAII_CUDA(launch_route_topk(logits, po, T, E, k, L.norm_topk, rb, stream_), "route_topk");
@@ -789,11 +793,14 @@ Error MoeCudaBackend::ffn(const LayerArgs& Lin, const float* x, int64_t T, float
   const int64_t D = L.D, E = L.E;
   const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E);
   const ExpertPlan P = plan_experts(L, T);
-  UAII_TRY(reserve(experts_ws_bytes(L, T, P) + 2 * align_up(xb) + 2 * align_up(pb) + layer_stage_bytes(L)));
+  const size_t rsb = router_scratch_bytes(T, D, E);
+  UAII_TRY(reserve(experts_ws_bytes(L, T, P) + 2 * align_up(xb) + 2 * align_up(pb) + align_up(rsb) +
+                   layer_stage_bytes(L)));
   void* xs = carve(xb);
   float* ys = static_cast<float*>(carve(xb));
   float* logits = static_cast<float*>(carve(pb));
   float* ps = static_cast<float*>(carve(pb));
+  float* rscratch = rsb ? static_cast<float*>(carve(rsb)) : nullptr;
   const void *xd = nullptr, *wd = nullptr;
   bool xh = false;
   UAII_TRY(stage_input(x, xb, xs, &xd, &xh));
@@ -802,7 +809,7 @@ Error MoeCudaBackend::ffn(const LayerArgs& Lin, const float* x, int64_t T, float
   float* po = (probs && !ph) ? probs : ps;
   phase_begin(kRouter);
   UAII_CUDA(launch_router(static_cast<const float*>(xd), static_cast<const float*>(wd), T, D, E, logits,
-                          po, nullptr, stream_),
+                          po, nullptr, stream_, rscratch, rsb),
             "router");
   phase_end();
   count_launches(2);

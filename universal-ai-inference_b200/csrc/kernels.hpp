@@ -14,7 +14,10 @@ cudaError_t launch_dequant_rows_f32(int fmt, const void* packed, int64_t rows, i
 // ---- router.cu: logits in the reference GEMM order, softmax, argmax
 // probs/top may be null when only logits are wanted; logits may be null.
 cudaError_t launch_router(const float* x, const float* w, int64_t T, int64_t D, int64_t E,
-                          float* logits, float* probs, float* top, cudaStream_t st);
+                          float* logits, float* probs, float* top, cudaStream_t st, float* scratch = nullptr,
+                          size_t scratch_bytes = 0);
+// Scratch launch_router can use to split small batches across more blocks (0: none needed).
+size_t router_scratch_bytes(int64_t T, int64_t D, int64_t E);
 
 // ---- route.cu: top-k selection, stable permutation, gather, combine
 struct RouteBuffers {

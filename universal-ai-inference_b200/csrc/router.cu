@@ -146,12 +146,16 @@ __global__ void __launch_bounds__(256) router_chunk_kernel(const float* __restri
 // k tile staged in shared memory, k-major), it builds the tile's partials in k
 // order and folds them into its running logits in tile order -- the reference
 // order without any cross-thread combine.  Block: 256 threads = TG x EG groups.
-constexpr int kRT = 4;  // tokens per thread
 constexpr int kRE = 8;  // experts per thread
 
+// Small batches split the row across blockIdx.z: each block then covers k tiles
+// [z*tpg, (z+1)*tpg) and writes the tile partials to `partials` (tile-major:
+// [nkt][T*E]) for router_fold_kernel, which adds them in tile order.
+template <int kRT>  // tokens per thread (4, 2 or 1: fewer when the batch is too small to fill the GPU)
 __global__ void __launch_bounds__(256) router_block_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                            int64_t T, int64_t D, int64_t E, int EG,
-                                                           float* __restrict__ logits) {
+                                                           float* __restrict__ logits, float* __restrict__ partials,
+                                                           int tpg) {
   extern __shared__ float sm[];
   const int TG = 256 / EG, TB = TG * kRT, EB = EG * kRE;
   const int XS = TB + 4, WS = EB + 4;  // padded k rows
@@ -165,19 +169,23 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
 #pragma unroll
     for (int b = 0; b < kRE; ++b) c[a][b] = 0.f;
   const bool vec = (D & 3) == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
-  for (int64_t k0 = 0; k0 < D; k0 += kTile) {
+  const int nkt = (int)((D + kTile - 1) / kTile);
+  const int j0 = partials ? (int)blockIdx.z * tpg : 0;
+  const int j1 = partials ? min(nkt, j0 + tpg) : nkt;
+  for (int j = j0; j < j1; ++j) {
+    const int64_t k0 = (int64_t)j * kTile;
     const int kn = (int)((k0 + kTile < D) ? kTile : D - k0);
     __syncthreads();
-    if (vec && kn == kTile) {  // coalesced float4 loads, transposed into k-major rows
-      for (int i = tid; i < TB * (kTile / 4); i += 256) {
-        const int r = i / (kTile / 4), k4 = i - r * (kTile / 4);
+    if (vec && kn == kTile) {  // float4 loads, transposed into k-major rows; lanes take consecutive rows
+      for (int i = tid; i < TB * (kTile / 4); i += 256) {  // so that the transposed stores hit distinct banks
+        const int k4 = i / TB, r = i - k4 * TB;
         const float4 v = (t0 + r < T) ? __ldg(reinterpret_cast<const float4*>(x + (t0 + r) * D + k0) + k4)
                                       : make_float4(0.f, 0.f, 0.f, 0.f);
         xs[(4 * k4) * XS + r] = v.x; xs[(4 * k4 + 1) * XS + r] = v.y;
         xs[(4 * k4 + 2) * XS + r] = v.z; xs[(4 * k4 + 3) * XS + r] = v.w;
       }
       for (int i = tid; i < EB * (kTile / 4); i += 256) {
-        const int r = i / (kTile / 4), k4 = i - r * (kTile / 4);
+        const int k4 = i / EB, r = i - k4 * EB;
         const float4 v = (e0 + r < E) ? __ldg(reinterpret_cast<const float4*>(w + (e0 + r) * D + k0) + k4)
                                       : make_float4(0.f, 0.f, 0.f, 0.f);
         ws[(4 * k4) * WS + r] = v.x; ws[(4 * k4 + 1) * WS + r] = v.y;
@@ -185,11 +193,11 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
       }
     } else {
       for (int i = tid; i < TB * kTile; i += 256) {
-        const int r = i / kTile, k = i - r * kTile;
+        const int k = i / TB, r = i - k * TB;
         xs[k * XS + r] = (t0 + r < T && k < kn) ? __ldg(x + (t0 + r) * D + k0 + k) : 0.f;
       }
       for (int i = tid; i < EB * kTile; i += 256) {
-        const int r = i / kTile, k = i - r * kTile;
+        const int k = i / EB, r = i - k * EB;
         ws[k * WS + r] = (e0 + r < E && k < kn) ? __ldg(w + (e0 + r) * D + k0 + k) : 0.f;
       }
     }
@@ -200,21 +208,42 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
 #pragma unroll
       for (int b = 0; b < kRE; ++b) sacc[a][b] = 0.f;
     for (int k = 0; k < kn; ++k) {
-      const float4 xv = *reinterpret_cast<const float4*>(xs + k * XS + tg * kRT);
+      float xa[kRT];
+      if constexpr (kRT == 4) {
+        const float4 xv = *reinterpret_cast<const float4*>(xs + k * XS + tg * kRT);
+        xa[0] = xv.x; xa[1] = xv.y; xa[2] = xv.z; xa[3] = xv.w;
+      } else if constexpr (kRT == 2) {
+        const float2 xv = *reinterpret_cast<const float2*>(xs + k * XS + tg * kRT);
+        xa[0] = xv.x; xa[1] = xv.y;
+      } else {
+        xa[0] = xs[k * XS + tg];
+      }
       const float4 wa = *reinterpret_cast<const float4*>(ws + k * WS + eg * kRE);
       const float4 wb = *reinterpret_cast<const float4*>(ws + k * WS + eg * kRE + 4);
-      const float xa[kRT] = {xv.x, xv.y, xv.z, xv.w};
       const float wv[kRE] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
       for (int a = 0; a < kRT; ++a)
 #pragma unroll
         for (int b = 0; b < kRE; ++b) sacc[a][b] = __fadd_rn(sacc[a][b], __fmul_rn(xa[a], wv[b]));
     }
+    if (partials) {
+#pragma unroll
+      for (int a = 0; a < kRT; ++a) {
+        const int64_t t = t0 + tg * kRT + a;
+#pragma unroll
+        for (int b = 0; b < kRE; ++b) {
+          const int64_t e = e0 + eg * kRE + b;
+          if (t < T && e < E) partials[(int64_t)j * T * E + t * E + e] = sacc[a][b];
+        }
+      }
+      continue;
+    }
 #pragma unroll
     for (int a = 0; a < kRT; ++a)
 #pragma unroll
       for (int b = 0; b < kRE; ++b) c[a][b] = __fadd_rn(c[a][b], __fmul_rn(1.0f, sacc[a][b]));
   }
+  if (partials) return;
 #pragma unroll
   for (int a = 0; a < kRT; ++a) {
     const int64_t t = t0 + tg * kRT + a;
@@ -225,6 +254,16 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
       if (e < E) logits[t * E + e] = c[a][b];
     }
   }
+}
+
+// logits[t][e] = tile partials added in tile order (the reference's c += 1 * s).
+__global__ void router_fold_kernel(const float* __restrict__ partials, int64_t n, int nkt,
+                                   float* __restrict__ logits) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float c = 0.0f;
+  for (int j = 0; j < nkt; ++j) c = __fadd_rn(c, __fmul_rn(1.0f, partials[(int64_t)j * n + i]));
+  logits[i] = c;
 }
 
 // Small batches: one block per token, thread (tile j, expert e) builds one
@@ -348,8 +387,42 @@ __global__ void softmax_top_kernel(const float* __restrict__ logits, int64_t T, 
 
 }  // namespace
 
+namespace {
+// Block schedule geometry for E >= 32: experts per block, tokens per thread and,
+// for small batches, k-tile groups per row (0: one block walks the whole row).
+struct BlockPlan {
+  int eb, EG, rt, TB, groups, tpg;
+  int64_t eblocks, tblocks;
+};
+BlockPlan block_plan(int64_t T, int64_t D, int64_t E) {
+  BlockPlan p{};
+  p.eb = E <= 32 ? 32 : E <= 64 ? 64 : 128;  // expert groups (4, 8, 16) divide the 256 threads
+  p.EG = p.eb / kRE;
+  p.eblocks = (E + p.eb - 1) / p.eb;
+  p.rt = 4;
+  p.TB = (256 / p.EG) * p.rt;
+  p.tblocks = (T + p.TB - 1) / p.TB;
+  const int nkt = (int)((D + kTile - 1) / kTile);
+  p.groups = 0;
+  if (p.tblocks * p.eblocks < 148 && nkt > 1) {  // under one wave of blocks: split the row, fold after
+    int64_t g = (2 * 148 + p.tblocks * p.eblocks - 1) / (p.tblocks * p.eblocks);
+    if (g > nkt) g = nkt;
+    p.tpg = (int)((nkt + g - 1) / g);
+    p.groups = (nkt + p.tpg - 1) / p.tpg;
+  }
+  return p;
+}
+}  // namespace
+
+size_t router_scratch_bytes(int64_t T, int64_t D, int64_t E) {
+  if (E < 32 || T < 1) return 0;
+  const BlockPlan p = block_plan(T, D, E);
+  return p.groups ? sizeof(float) * (size_t)(T * E) * (size_t)((D + kTile - 1) / kTile) : 0;
+}
+
 cudaError_t launch_router(const float* x, const float* w, int64_t T, int64_t D, int64_t E,
-                          float* logits, float* probs, float* top, cudaStream_t st) {
+                          float* logits, float* probs, float* top, cudaStream_t st, float* scratch,
+                          size_t scratch_bytes) {
   if (T == 0) return cudaSuccess;
   if (logits == nullptr) return cudaErrorInvalidValue;
   const int64_t nkt = (D + kTile - 1) / kTile;
@@ -360,14 +433,23 @@ cudaError_t launch_router(const float* x, const float* w, int64_t T, int64_t D, 
     attrs = true;
     (void)cudaFuncSetAttribute(router_token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     (void)cudaFuncSetAttribute(router_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    (void)cudaFuncSetAttribute(router_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    (void)cudaFuncSetAttribute(router_block_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   }
-  if (E >= 32 && T >= 128) {
-    const int eb = E <= 32 ? 32 : E <= 64 ? 64 : 128;  // expert groups (4, 8, 16) divide the 256 threads
-    const int EG = eb / kRE, TB = (256 / EG) * kRT;
-    const size_t smem = sizeof(float) * (size_t)(kTile * (TB + 4) + kTile * (eb + 4));
-    dim3 grid((unsigned)((T + TB - 1) / TB), (unsigned)((E + eb - 1) / eb));
-    router_block_kernel<<<grid, 256, smem, st>>>(x, w, T, D, E, EG, logits);
+  const size_t need = router_scratch_bytes(T, D, E);
+  if (E >= 32 && (T >= 128 || (need && scratch && scratch_bytes >= need))) {
+    const BlockPlan p = block_plan(T, D, E);
+    const bool split = p.groups > 0 && scratch && scratch_bytes >= need;
+    const size_t smem = sizeof(float) * (size_t)(kTile * (p.TB + 4) + kTile * (p.eb + 4));
+    dim3 grid((unsigned)p.tblocks, (unsigned)p.eblocks, split ? (unsigned)p.groups : 1u);
+    router_block_kernel<4><<<grid, 256, smem, st>>>(x, w, T, D, E, p.EG, logits, split ? scratch : nullptr,
+                                                    split ? p.tpg : 0);
+    if (split) {
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return e;
+      const int64_t n = T * E;
+      router_fold_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(scratch, n, (int)((D + kTile - 1) / kTile),
+                                                                       logits);
+    }
   } else if (T < 128 && token_smem <= 200 * 1024) {
     router_token_kernel<<<(unsigned)T, 512, token_smem, st>>>(x, w, D, E, logits);
   } else if (chunk_smem <= 200 * 1024) {
