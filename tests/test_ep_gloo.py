@@ -107,7 +107,7 @@ class FakeEpBackend:
             y[t] = acc
 
 
-def _worker(rank: int, world: int, port: int, q, fail_rank: int):
+def _worker(rank: int, world: int, port: int, q, fail_rank: int, chunks: int = 1):
     try:
         sys.path.insert(0, REPO)
         sys.path.insert(0, os.path.join(REPO, "universal-ai-inference_b200"))
@@ -124,7 +124,8 @@ def _worker(rank: int, world: int, port: int, q, fail_rank: int):
             def broken(*a, **kw):
                 raise RuntimeError("planted dispatch failure")
             fake.ep_dispatch = broken
-        ep = ExpertParallelFFN(fake, None, rank * (E // world), D, E, k, rank, world, device="cpu")
+        ep = ExpertParallelFFN(fake, None, rank * (E // world), D, E, k, rank, world, device="cpu", chunks=chunks,
+                               min_chunk=1)
         x = torch.from_numpy(_tokens(rank, T, D))
         y = torch.zeros((T, D), dtype=torch.float32)
         try:
@@ -140,12 +141,12 @@ def _worker(rank: int, world: int, port: int, q, fail_rank: int):
         q.put((rank, "crash", traceback.format_exc(), None))
 
 
-def _run(world: int, fail_rank: int = -1, timeout: float = 120.0):
+def _run(world: int, fail_rank: int = -1, timeout: float = 120.0, chunks: int = 1):
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, fail_rank)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, fail_rank, chunks)) for r in range(world)]
     for p in procs:
         p.start()
     out = {}
@@ -163,9 +164,10 @@ def _run(world: int, fail_rank: int = -1, timeout: float = 120.0):
     return out
 
 
-def test_ep_two_ranks_match_single_process(oracle):
+@pytest.mark.parametrize("chunks", [1, 3])  # 3: tokens split into chunks with overlapped exchanges
+def test_ep_two_ranks_match_single_process(oracle, chunks):
     D, E, I, k, T, w_router, G, U, Dn = _layer_case()
-    out = _run(2)
+    out = _run(2, chunks=chunks)
     assert set(out) == {0, 1}, out
     for rank in (0, 1):
         status, y, exch = out[rank]

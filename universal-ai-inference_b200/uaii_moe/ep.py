@@ -26,6 +26,20 @@ import torch
 import torch.distributed as dist
 
 
+class _Chunk:
+    """Send-side buffers of one token chunk."""
+
+    def __init__(self, T: int, D: int, k: int, R: int, dev):
+        cap = max(T * min(k, R), 1)
+        self.T = T
+        self.x16 = torch.empty((cap, D), dtype=torch.float16, device=dev)
+        self.ids = torch.empty((cap, k), dtype=torch.int32, device=dev)
+        self.w = torch.empty((cap, k), dtype=torch.float32, device=dev)
+        self.token = torch.empty((cap,), dtype=torch.int32, device=dev)
+        self.row_of = torch.empty((max(T, 1), R), dtype=torch.int32, device=dev)
+        self.counts = torch.empty((2, R), dtype=torch.int32, device=dev)  # rows, entries per destination
+
+
 class ExpertParallelFFN:
     """Expert-parallel forward of one MoE FFN layer.
 
@@ -34,10 +48,15 @@ class ExpertParallelFFN:
     struct carrying the router weight, d_model, the global expert count, top_k
     and norm_topk; ``local_layer`` carries this rank's experts (n_experts =
     E / world).  ``group`` is the torch.distributed process group (default: world).
+
+    ``chunks`` > 1 splits the local tokens: every chunk is dispatched up front
+    (one host read of all split sizes), then the exchanges run asynchronously so
+    that the experts of chunk i overlap the rows of chunk i+1 in flight and the
+    return of chunk i overlaps the experts of chunk i+1.
     """
 
     def __init__(self, backend, router_layer, local_layer, d_model: int, n_experts: int, top_k: int,
-                 rank: int, world: int, group=None, device="cuda"):
+                 rank: int, world: int, group=None, device="cuda", chunks: int = 2, min_chunk: int = 256):
         if n_experts % world != 0:
             raise ValueError("the world size must divide the expert count")
         self.be = backend
@@ -47,50 +66,72 @@ class ExpertParallelFFN:
         self.rank, self.world = rank, world
         self.group = group
         self.device = torch.device(device)
-        self._cap = -1
-        self.last_exchange = None  # (rows sent per rank, rows received per rank, entries received)
+        self.chunks, self.min_chunk = max(1, chunks), min_chunk
+        self._bufs = {}
+        self.last_exchange = None  # (rows sent per rank, rows received per rank, entries received), all chunks
 
-    def _buffers(self, T: int):
-        cap = T * min(self.k, self.world)
-        if cap != self._cap:
-            dev, D, k, R = self.device, self.D, self.k, self.world
-            self.send_x16 = torch.empty((max(cap, 1), D), dtype=torch.float16, device=dev)
-            self.send_ids = torch.empty((max(cap, 1), k), dtype=torch.int32, device=dev)
-            self.send_w = torch.empty((max(cap, 1), k), dtype=torch.float32, device=dev)
-            self.send_token = torch.empty((max(cap, 1),), dtype=torch.int32, device=dev)
-            self.row_of = torch.empty((max(T, 1), R), dtype=torch.int32, device=dev)
-            self.counts = torch.empty((2, R), dtype=torch.int32, device=dev)  # rows, entries per destination
-            self._cap = cap
+    def _chunk_bufs(self, i: int, T: int) -> _Chunk:
+        b = self._bufs.get(i)
+        if b is None or b.T != T:
+            b = _Chunk(T, self.D, self.k, self.world, self.device)
+            self._bufs[i] = b
+        return b
 
     def forward(self, x: torch.Tensor, y: torch.Tensor, probs: torch.Tensor | None = None) -> torch.Tensor:
         T = int(x.shape[0])
         D, k, R = self.D, self.k, self.world
-        self._buffers(T)
-        self.be.ep_dispatch(self.router_layer, x, T, self.rank, R, self.send_x16, self.send_ids, self.send_w,
-                            self.send_token, self.row_of, self.counts[0], self.counts[1], probs)
-        # rows and entries per destination -> per source
-        meta_send = self.counts.t().contiguous().to(torch.int64)  # [R, 2]
+        n = self.chunks if T >= self.chunks * self.min_chunk else 1
+        bounds = [T * c // n for c in range(n + 1)]
+        parts = []
+        for c in range(n):  # 1. dispatch every chunk on the device
+            t0, t1 = bounds[c], bounds[c + 1]
+            b = self._chunk_bufs(c, t1 - t0)
+            self.be.ep_dispatch(self.router_layer, x[t0:t1], t1 - t0, self.rank, R, b.x16, b.ids, b.w, b.token,
+                                b.row_of, b.counts[0], b.counts[1], None if probs is None else probs[t0:t1])
+            parts.append(b)
+        # 2. rows / entries per destination of every chunk -> per source (one exchange, one host read)
+        meta_send = torch.stack([b.counts.t() for b in parts], dim=1).reshape(R, 2 * n).to(torch.int64)
         meta_recv = torch.empty_like(meta_send)
-        dist.all_to_all_single(meta_recv, meta_send, group=self.group)
-        both = torch.cat([meta_send[:, 0], meta_recv[:, 0], meta_recv[:, 1]]).cpu().tolist()
-        send_rows, recv_rows, recv_entries = both[:R], both[R:2 * R], both[2 * R:]
-        n_send, n_recv, entries = sum(send_rows), sum(recv_rows), sum(recv_entries)
-        self.last_exchange = (send_rows, recv_rows, entries)
+        dist.all_to_all_single(meta_recv, meta_send.contiguous(), group=self.group)
+        host = torch.cat([meta_send.reshape(-1), meta_recv.reshape(-1)]).cpu().view(2, R, n, 2).tolist()
         dev = self.device
-        recv_x16 = torch.empty((max(n_recv, 1), D), dtype=torch.float16, device=dev)
-        recv_ids = torch.empty((max(n_recv, 1), k), dtype=torch.int32, device=dev)
-        recv_w = torch.empty((max(n_recv, 1), k), dtype=torch.float32, device=dev)
-        dist.all_to_all_single(recv_x16[:n_recv], self.send_x16[:n_send], output_split_sizes=recv_rows,
-                               input_split_sizes=send_rows, group=self.group)
-        dist.all_to_all_single(recv_ids[:n_recv], self.send_ids[:n_send], output_split_sizes=recv_rows,
-                               input_split_sizes=send_rows, group=self.group)
-        dist.all_to_all_single(recv_w[:n_recv], self.send_w[:n_send], output_split_sizes=recv_rows,
-                               input_split_sizes=send_rows, group=self.group)
-        y_part = torch.empty((max(n_recv, 1), D), dtype=torch.float32, device=dev)
-        if n_recv:
-            self.be.ep_experts(self.local_layer, recv_x16, recv_ids, recv_w, n_recv, entries, y_part)
-        y_back = torch.empty((max(n_send, 1), D), dtype=torch.float32, device=dev)
-        dist.all_to_all_single(y_back[:n_send], y_part[:n_recv], output_split_sizes=send_rows,
-                               input_split_sizes=recv_rows, group=self.group)
-        self.be.ep_combine(y_back, self.row_of, T, R, D, y)
+        plans = []
+        for c, b in enumerate(parts):
+            send_rows = [host[0][r][c][0] for r in range(R)]
+            recv_rows = [host[1][r][c][0] for r in range(R)]
+            entries = sum(host[1][r][c][1] for r in range(R))
+            plans.append((send_rows, recv_rows, entries))
+        self.last_exchange = (
+            [sum(p[0][r] for p in plans) for r in range(R)], [sum(p[1][r] for p in plans) for r in range(R)],
+            sum(p[2] for p in plans))
+        # 3. rows of every chunk in flight
+        recv, works = [], []
+        for (send_rows, recv_rows, entries), b in zip(plans, parts):
+            ns, nr = sum(send_rows), sum(recv_rows)
+            rx = torch.empty((max(nr, 1), D), dtype=torch.float16, device=dev)
+            ri = torch.empty((max(nr, 1), k), dtype=torch.int32, device=dev)
+            rw = torch.empty((max(nr, 1), k), dtype=torch.float32, device=dev)
+            w = [dist.all_to_all_single(dst[:nr], src[:ns], output_split_sizes=recv_rows,
+                                        input_split_sizes=send_rows, group=self.group, async_op=True)
+                 for dst, src in ((rx, b.x16), (ri, b.ids), (rw, b.w))]
+            recv.append((rx, ri, rw))
+            works.append(w)
+        # 4. experts of chunk c as soon as its rows are in, return its rows asynchronously
+        backs, rworks = [], []
+        for c, ((send_rows, recv_rows, entries), (rx, ri, rw)) in enumerate(zip(plans, recv)):
+            for w in works[c]:
+                w.wait()
+            ns, nr = sum(send_rows), sum(recv_rows)
+            y_part = torch.empty((max(nr, 1), D), dtype=torch.float32, device=dev)
+            if nr:
+                self.be.ep_experts(self.local_layer, rx, ri, rw, nr, entries, y_part)
+            y_back = torch.empty((max(ns, 1), D), dtype=torch.float32, device=dev)
+            rworks.append(dist.all_to_all_single(y_back[:ns], y_part[:nr], output_split_sizes=send_rows,
+                                                 input_split_sizes=recv_rows, group=self.group, async_op=True))
+            backs.append(y_back)
+        # 5. combine each chunk in rank order
+        for c, b in enumerate(parts):
+            rworks[c].wait()
+            t0, t1 = bounds[c], bounds[c + 1]
+            self.be.ep_combine(backs[c], b.row_of, t1 - t0, R, D, y[t0:t1])
         return y
