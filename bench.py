@@ -63,7 +63,8 @@ def parse():
     ap.add_argument("--tokens", type=int, default=4096)
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="weak: --tokens per GPU; strong: --tokens in total, split across the GPUs")
-    ap.add_argument("--path", type=int, default=0, help="0 auto, 1 CUDA-core GEMV, 2 tensor-core GEMM")
+    ap.add_argument("--path", type=int, default=0,
+                    help="0 auto, 1 CUDA-core GEMV, 2 tcgen05 tensor-core GEMM, 3 warp-MMA tensor-core GEMM")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -264,6 +265,12 @@ def main():
     be = um.Backend(local, stream.cuda_stream)
     if args.path:
         be.set_expert_path(args.path)
+    # a serving process registers its (constant) weights once: layouts derived from them, such as
+    # 16-byte-pitch copies of rows the tensor maps cannot address, are then made once, not per call
+    for a in arrays.values():
+        for t in (a if isinstance(a, tuple) else (a,)):
+            if t is not None:
+                be.register_weights(t)
 
     if ep_mode:
         ep = ExpertParallelFFN(be, router_layer, local_layer, cfg.D, cfg.E, cfg.top_k, rank, world)
@@ -371,7 +378,8 @@ def main():
         roof["frac_sustained"] = roof["achieved"] / roof["peak_sustained"]
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["traffic"] = NCU_TRAFFIC.get((workload, dom))
-    path = ("tensor-core grouped dequant-GEMM (tcgen05, f16 operands, f32 accumulate), "
+    sched = {"tcgen05": "tcgen05", "warp_mma": "warp-level mma.sync m16n8k16"}.get(plan.get("schedule"), "tcgen05")
+    path = (f"tensor-core grouped dequant-GEMM ({sched}, f16 operands, f32 accumulate), "
             f"{plan['slot_tile']}-slot tiles") if plan["tensor_cores"] else "CUDA-core f32 grouped GEMV"
     roof["kernel"] = f"{dom} phase: {path}"
     roof["peak_src"] = f"{peaks['src']} ({'hbm_gbs' if roof['bound'] == 'hbm' else 'bf16_tflops burst'})"

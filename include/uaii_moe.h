@@ -208,11 +208,14 @@ UAII_MOE_API int uaii_moe_experts_swiglu(uaii_moe_backend* b, const float* x, co
 UAII_MOE_API int uaii_moe_ffn_forward(uaii_moe_backend* b, const uaii_moe_layer* layer, const float* x,
                          int64_t T, float* y, float* probs);
 
-/* Upload a host weight buffer once and reuse the device copy whenever a call
- * passes the same (pointer, bytes); the caller keeps the host buffer unchanged
- * until uaii_moe_release_weights().  No reference counterpart: the reference
- * never uploads weights (its Session keeps them in host memory,
- * libs/uaii-runtime/src/session.cpp:259-367). */
+/* Declare a weight buffer constant until uaii_moe_release_weights().  A host
+ * buffer is uploaded once and the device copy is reused whenever a call passes
+ * the same (pointer, bytes).  For host and device buffers alike, layouts the
+ * library derives from the weights (rows copied to a 16-byte pitch for the
+ * tensor maps, when a format's row size is not a multiple of 16) are made on
+ * first use and kept.  The caller keeps the buffer unchanged until it is
+ * released.  No reference counterpart: the reference never uploads weights
+ * (its Session keeps them in host memory, libs/uaii-runtime/src/session.cpp:259-367). */
 UAII_MOE_API int uaii_moe_register_weights(uaii_moe_backend* b, const void* host_ptr, uint64_t bytes);
 
 /* The whole MoE FFN layer, like uaii_moe_ffn_forward, for callers that cannot
@@ -235,8 +238,12 @@ UAII_MOE_API int uaii_moe_ffn_forward_noalloc(int device, void* stream, const ua
 /* Drop the device copy of a registered host weight buffer. */
 UAII_MOE_API int uaii_moe_release_weights(uaii_moe_backend* b, const void* host_ptr);
 
-/* Select the expert-product schedule: 0 = automatic, 1 = CUDA-core f32 GEMV,
- * 2 = tensor-core grouped GEMM.  No reference counterpart. */
+/* Select the expert-product schedule: 0 = automatic (tensor cores when the layer
+ * qualifies: the warp-MMA schedule at <= 16 routed slots per expert, tcgen05
+ * above), 1 = CUDA-core f32 GEMV, 2 = tensor cores on the tcgen05 schedule only,
+ * 3 = tensor cores on the warp-MMA (mma.sync) schedule for every slot count
+ * (d_model and d_ff multiples of 128; expert-parallel rows stay on tcgen05).
+ * No reference counterpart. */
 UAII_MOE_API int uaii_moe_set_expert_path(uaii_moe_backend* b, int path);
 
 /* ---- Expert parallelism (one process per GPU, R ranks, rank r owns experts
@@ -286,10 +293,10 @@ UAII_MOE_API int uaii_moe_ep_combine(uaii_moe_backend* b, const float* y_back, c
 UAII_MOE_API int uaii_moe_selftest_wait_timeout(uaii_moe_backend* b, int64_t budget_cycles);
 
 /* Schedule of the most recent expert-product call on this backend (routed
- * experts): *tensor_cores = 1 for the tensor-core grouped GEMM, 0 for the
- * CUDA-core GEMV; *slot_tile = routed slots per tile (MMA N); *down_splits =
- * K splits of the down projection.  Any pointer may be NULL.  Diagnostic; no
- * reference counterpart. */
+ * experts): *tensor_cores = 1 for the tcgen05 grouped GEMM, 2 for the warp-MMA
+ * one, 0 for the CUDA-core GEMV; *slot_tile = routed slots per tile (MMA N);
+ * *down_splits = K splits of the down projection.  Any pointer may be NULL.
+ * Diagnostic; no reference counterpart. */
 UAII_MOE_API int uaii_moe_last_plan(uaii_moe_backend* b, int* tensor_cores, int* slot_tile, int* down_splits);
 
 /* Device-side profile of the MoE phases, measured with CUDA events on the

@@ -389,3 +389,132 @@ def test_tensor_core_shared_expert(backend, oracle, um):
     finally:
         backend.set_expert_path(0)
     assert rel_err(y, y_ref) <= REL_TOL
+
+
+# ---------------------------------------------------------------- warp-MMA schedule (decode widths)
+
+@pytest.mark.parametrize("gf,df,T,D,E,I,k", [
+    (14, 16, 1, 1024, 8, 2048, 2),     # Mixtral formats, one token: 8-slot tiles, split-K down
+    (14, 16, 32, 1024, 8, 2048, 2),    # Mixtral formats, 8 slots per expert
+    (14, 16, 60, 512, 8, 1024, 2),     # 16-slot tiles
+    (7, 7, 3, 1024, 8, 2816, 2),       # config 1 shapes (Q4_0)
+    (11, 11, 9, 512, 12, 384, 4),      # Q8_0 (two boxes per window); K % 256 == 128 for down
+    (7, 7, 5, 384, 4, 640, 2),         # Q4_0 with a half quad at the end of both projections
+    (7, 7, 50, 512, 32, 256, 8),       # Qwen3 formats, many experts
+    (14, 16, 5, 256, 4, 256, 2),       # Q6_K rows of 210 bytes: padded pitch
+    (7, 7, 300, 256, 4, 256, 2),       # forced far above decode widths: many 16-slot tiles per expert
+])
+def test_warp_mma_path_vs_oracle(backend, oracle, um, gf, df, T, D, E, I, k):
+    x, w, G, U, Dn = layer_case(um, gf, df, T, D, E, I, k, 120 + T)
+    _, pr, _ = oracle.router(x, w)
+    y_ref, _, _ = oracle.experts_packed(x, G, gf, U, gf, Dn, df, pr, E, I, k, 1)
+    L = um.make_layer(D, E, I, k, 1, w, G, gf, U, gf, Dn, df)
+    y = np.empty_like(x)
+    backend.set_expert_path(3)
+    try:
+        backend.ffn(L, x, T, y)
+        plan = backend.last_plan()
+    finally:
+        backend.set_expert_path(0)
+    assert plan["schedule"] == "warp_mma" and plan["slot_tile"] in (8, 16)
+    assert rel_err(y, y_ref) <= REL_TOL
+
+
+def test_automatic_schedule_picks_warp_mma_for_decode(backend, um):
+    D, E, I, k = 1024, 8, 2048, 2
+    # tiles hold the mean slots per expert plus two standard deviations below 32 slots
+    for T, sched, tile in ((1, "warp_mma", 8), (8, "warp_mma", 8), (32, "tcgen05", 16), (64, "tcgen05", 32),
+                           (512, "tcgen05", 128)):
+        x, w, G, U, Dn = layer_case(um, 14, 16, T, D, E, I, k, 5)
+        y = np.empty_like(x)
+        backend.ffn(um.make_layer(D, E, I, k, 1, w, G, 14, U, 14, Dn, 16), x, T, y)
+        plan = backend.last_plan()
+        assert (plan["schedule"], plan["slot_tile"]) == (sched, tile), (T, plan)
+
+
+def test_warp_mma_and_tcgen05_agree(backend, um):
+    # same operands, different accumulation order: the two schedules agree to f32 rounding
+    T, D, E, I, k = 12, 1024, 8, 1024, 2
+    x, w, G, U, Dn = layer_case(um, 14, 16, T, D, E, I, k, 8)
+    L = um.make_layer(D, E, I, k, 1, w, G, 14, U, 14, Dn, 16)
+    ys = []
+    for path in (2, 3):
+        y = np.empty_like(x)
+        backend.set_expert_path(path)
+        try:
+            backend.ffn(L, x, T, y)
+        finally:
+            backend.set_expert_path(0)
+        ys.append(y)
+    assert rel_err(ys[1], ys[0]) <= 1e-4
+
+
+def test_warp_mma_refuses_unsupported_shapes(backend, um):
+    # d_ff = 320 is a tcgen05 shape (multiple of 64) but not a warp-MMA one (multiple of 128)
+    D, E, I = 256, 4, 320
+    x, w, G, U, Dn = layer_case(um, 7, 7, 2, D, E, I, 2, 3)
+    y = np.empty_like(x)
+    backend.set_expert_path(3)
+    try:
+        with pytest.raises(um.UaiiMoeError) as e:
+            backend.ffn(um.make_layer(D, E, I, 2, 1, w, G, 7, U, 7, Dn, 7), x, 2, y)
+        assert e.value.status == 7
+    finally:
+        backend.set_expert_path(0)
+    backend.ffn(um.make_layer(D, E, I, 2, 1, w, G, 7, U, 7, Dn, 7), x, 2, y)  # automatic: tcgen05
+    assert backend.last_plan()["schedule"] == "tcgen05"
+
+
+@pytest.mark.parametrize("T", [4, 16])
+def test_warp_mma_shared_expert(backend, oracle, um, T):
+    D, E, I, Ish, k = 512, 8, 256, 1024, 4
+    x, w, G, U, Dn = layer_case(um, 11, 11, T, D, E, I, k, 79)
+    Gs = um.quantize_rows(11, um.fill_normal((Ish, D), 79, 6, 0.0, 0.02))
+    Us = um.quantize_rows(11, um.fill_normal((Ish, D), 79, 7, 0.0, 0.02))
+    Ds = um.quantize_rows(11, um.fill_normal((D, Ish), 79, 8, 0.0, 0.02))
+    gi = um.fill_normal((D,), 79, 9, 0.0, 0.02)
+    _, pr, _ = oracle.router(x, w)
+    y_ref, _, _ = oracle.experts_packed(x, G, 11, U, 11, Dn, 11, pr, E, I, k, 0)
+    oracle.shared_packed(x, Gs, 11, Us, 11, Ds, 11, gi, Ish, y_ref)
+    L = um.make_layer(D, E, I, k, 0, w, G, 11, U, 11, Dn, 11, shared=(Ish, Gs, 11, Us, 11, Ds, 11, gi))
+    y = np.empty_like(x)
+    backend.set_expert_path(3)
+    try:
+        backend.ffn(L, x, T, y)
+    finally:
+        backend.set_expert_path(0)
+    assert rel_err(y, y_ref) <= REL_TOL
+
+
+def test_registered_device_weights_keep_padded_rows(backend, oracle, um):
+    # Q8_0 rows of 1408 elements (1496 bytes) need a 16-byte pitch for the tensor maps: for
+    # registered device weights the padded copy is made once, and results do not change
+    torch = pytest.importorskip("torch")
+    T, D, E, I, k = 8, 256, 6, 1408, 4
+    x, w, G, U, Dn = layer_case(um, 11, 11, T, D, E, I, k, 31)
+    _, pr, _ = oracle.router(x, w)
+    y_ref, _, _ = oracle.experts_packed(x, G, 11, U, 11, Dn, 11, pr, E, I, k, 1)
+    dev = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (w, G, U, Dn)]
+    L = um.make_layer(D, E, I, k, 1, dev[0], dev[1], 11, dev[2], 11, dev[3], 11)
+    y0 = np.empty_like(x)
+    backend.ffn(L, x, T, y0)
+    for a in dev:
+        backend.register_weights(a)
+    try:
+        ys = []
+        for _ in range(2):
+            backend.profile_enable(True)
+            y = np.empty_like(x)
+            backend.ffn(L, x, T, y)
+            _, launches = backend.profile_read()
+            backend.profile_enable(False)
+            ys.append((y, launches))
+        assert bits_equal(ys[0][0], y0) and bits_equal(ys[1][0], y0)
+        assert ys[1][1] == ys[0][1] - 1  # the second call reuses the padded down rows (one launch fewer)
+    finally:
+        for a in dev:
+            backend.release_weights(a)
+    assert rel_err(y0, y_ref) <= REL_TOL
+    y2 = np.empty_like(x)
+    backend.ffn(L, x, T, y2)  # released: padded per call again
+    assert bits_equal(y2, y0)

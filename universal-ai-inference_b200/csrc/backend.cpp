@@ -12,6 +12,8 @@
 // device_allocs_ (libs/uaii-backends/src/cuda_backend.cpp:68-78).
 #include "backend.hpp"
 
+#include <cmath>
+
 #include <cstring>
 #include <string>
 
@@ -122,8 +124,11 @@ void MoeCudaBackend::shutdown() noexcept {
   }
   (void)cudaSetDevice(device_);
   if (stream_) (void)cudaStreamSynchronize(stream_);
+  for (auto& kv : padded_) (void)cudaFree(kv.second.dev);
+  padded_.clear();
   for (auto& kv : weights_) (void)cudaFree(kv.second);
   weights_.clear();
+  const_dev_.clear();
   for (auto& m : marks_) { (void)cudaEventDestroy(m.start); (void)cudaEventDestroy(m.stop); }
   marks_.clear();
   for (auto e : event_pool_) (void)cudaEventDestroy(e);
@@ -263,11 +268,37 @@ Error MoeCudaBackend::stage_weight(const void* p, size_t bytes, const void** dev
   return Error::success();
 }
 
+bool MoeCudaBackend::weight_is_constant(const void* p, size_t bytes) const {
+  if (weights_.count(std::make_pair(p, bytes))) return true;
+  const char* c = static_cast<const char*>(p);
+  auto it = const_dev_.upper_bound(p);  // first registered buffer starting after p
+  if (it == const_dev_.begin()) return false;
+  --it;
+  const char* b = static_cast<const char*>(it->first);
+  return c >= b && c + bytes <= b + it->second;
+}
+
+void MoeCudaBackend::drop_padded(const char* lo, const char* hi) {
+  for (auto it = padded_.begin(); it != padded_.end();) {
+    const char* src = static_cast<const char*>(std::get<0>(it->first));
+    if (src >= lo && src < hi) {
+      (void)cudaFree(it->second.dev);
+      it = padded_.erase(it);
+    } else {
+      ++it;
+    }
+  }
+}
+
 Error MoeCudaBackend::register_weights(const void* p, size_t bytes) {
   std::lock_guard<std::mutex> lk(mu_);
   UAII_CUDA(cudaSetDevice(device_), "SetDevice");
   if (p == nullptr || bytes == 0) return Error::make(ErrorCode::InvalidArgument, "register_weights: empty buffer");
-  if (is_device_ptr(p)) return Error::make(ErrorCode::InvalidArgument, "register_weights: pointer is device memory");
+  if (is_device_ptr(p)) {  // nothing to upload; layouts derived from it may be kept
+    size_t& have = const_dev_[p];
+    if (bytes > have) have = bytes;
+    return Error::success();
+  }
   auto key = std::make_pair(p, bytes);
   if (weights_.count(key)) return Error::success();
   void* d = nullptr;
@@ -287,12 +318,22 @@ Error MoeCudaBackend::release_weights(const void* host_ptr) {
   for (auto it = weights_.begin(); it != weights_.end();) {
     if (it->first.first == host_ptr) {
       UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+      const char* d = static_cast<const char*>(it->second);
+      drop_padded(d, d + it->first.second);
       (void)cudaFree(it->second);
       it = weights_.erase(it);
       found = true;
     } else {
       ++it;
     }
+  }
+  auto dv = const_dev_.find(host_ptr);
+  if (dv != const_dev_.end()) {
+    UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+    const char* d = static_cast<const char*>(dv->first);
+    drop_padded(d, d + dv->second);
+    const_dev_.erase(dv);
+    found = true;
   }
   return found ? Error::success()
                : Error::make(ErrorCode::NotFound, "pointer has no cached device copy");
@@ -382,41 +423,79 @@ Error MoeCudaBackend::router(const float* x, const float* gate_w, int64_t T, int
 }
 
 // Which expert-product schedule a layer call uses, and its tile shape.
-ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t slots) const {
+// Automatic: tensor cores whenever the layer qualifies; the warp-MMA schedule
+// when no expert gets more than 16 routed slots on average (decode), tcgen05
+// above.  allow_warp_mma = false keeps the tcgen05 operand order (rows that
+// arrive packed by another rank).
+ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t slots, bool allow_warp_mma) const {
   ExpertPlan p;
   const int64_t S = slots >= 0 ? slots : T * L.top_k;
   const bool umma_ok = umma_shapes_supported(L.gate.fmt, L.down.fmt, L.D, L.I);
+  const bool warp_ok = allow_warp_mma && warp_mma_shapes_supported(L.gate.fmt, L.down.fmt, L.D, L.I);
   p.umma = path_ != 1 && umma_ok;
-  p.umma_refused = path_ == 2 && !umma_ok;
+  p.umma_refused = (path_ == 2 && !umma_ok) || (path_ == 3 && allow_warp_mma && !warp_ok);
   const int sms = 148;
-  auto pick_bn = [](double tpe) { return tpe <= 16 ? 16 : tpe <= 32 ? 32 : tpe <= 64 ? 64 : tpe <= 128 ? 128 : 256; };
+  // Slots an expert's tile must hold: the mean plus two standard deviations of a
+  // Poisson count at small means (an expert just above a tile width costs a second
+  // pass over its weights), the mean at large ones (half-empty tiles cost MMA time).
+  auto need = [](double tpe) { return tpe < 32 ? tpe + 2.0 * std::sqrt(tpe) : tpe; };
+  auto pick_bn = [&](double tpe) {
+    const double n = need(tpe);
+    return n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : 256;
+  };
+  // warp-MMA use: forced (path 3), never (paths 1, 2), or (path 0) when 8-slot tiles
+  // hold every expert's slots -- measured faster than tcgen05 there, slower at 16 slots
+  auto use_warp = [&](bool ok, double tpe) { return ok && (path_ == 3 || (path_ == 0 && need(tpe) <= 8)); };
+  auto warp_bn = [&](double tpe) { return need(tpe) <= 8 ? 8 : 16; };
+  // K splits of the down projection: the split count whose last wave ends first.  A
+  // unit is one (tile, split); every unit costs its quads plus about two quads of
+  // pipeline fill and epilogue, and the units run in waves of one per SM.
   auto pick_splits = [&](int64_t tiles, int kchunks) {
-    int64_t sp = tiles > 0 ? (2 * sms + tiles - 1) / tiles : 1;
-    if (sp > 16) sp = 16;
-    if (sp > kchunks) sp = kchunks;
-    return (int)(sp < 1 ? 1 : sp);
+    if (tiles <= 0 || kchunks <= 1) return 1;
+    int best = 1;
+    double best_cost = 0;
+    for (int sp = 1; sp <= 16 && sp <= kchunks; ++sp) {
+      const double waves = (double)((tiles * sp + sms - 1) / sms);
+      const double cost = waves * ((kchunks + sp - 1) / sp + 2);
+      if (sp == 1 || cost < best_cost) {
+        best = sp;
+        best_cost = cost;
+      }
+    }
+    return best;
   };
   const int64_t active = S < L.E ? S : L.E;
   const double tpe = active > 0 ? (double)S / (double)active : 1.0;
   p.bn = pick_bn(tpe);
   if (p.umma) {
+    p.warp_mma = use_warp(warp_ok, tpe);
+    if (p.warp_mma) p.bn = warp_bn(tpe);
     const int64_t n_tiles = (int64_t)((tpe + p.bn - 1) / p.bn);
     p.splits = pick_splits(active * n_tiles * (L.D / 128), umma_kchunks(L.down.fmt, L.I));
   }
   if (L.I_sh > 0) {
     p.sh_umma = p.umma && umma_shapes_supported(L.gate_sh.fmt, L.down_sh.fmt, L.D, L.I_sh);
-    p.sh_bn = pick_bn((double)T);
-    if (p.sh_umma)
+    p.sh_bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+    if (p.sh_umma) {
+      p.sh_warp_mma = warp_mma_shapes_supported(L.gate_sh.fmt, L.down_sh.fmt, L.D, L.I_sh) &&
+                      (path_ == 3 || (path_ == 0 && T <= 8));
+      if (p.sh_warp_mma) p.sh_bn = T <= 8 ? 8 : 16;  // the shared expert owns every token: no spread
       p.sh_splits = pick_splits(((T + p.sh_bn - 1) / p.sh_bn) * (L.D / 128), umma_kchunks(L.down_sh.fmt, L.I_sh));
+    }
   }
   return p;
 }
 
 // Routing + expert products + combine for device-resident x.
 // `scores` rank the experts; `probs_for_w` supplies the weights (may equal scores).
+namespace {
+size_t expert_bytes(const ExpertWeights& w, int64_t E) { return (size_t)(E * w.rows) * row_bytes(w.fmt, w.cols); }
+}  // namespace
+
 // Packed rows as the tensor-core path reads them: in place when the row pitch is a
 // multiple of 16 bytes (TMA strides), else a copy with each row padded to 16 bytes.
-Error MoeCudaBackend::umma_rows(const void* w, int fmt, int64_t rows, int64_t K, const void** out, int64_t* pitch) {
+Error MoeCudaBackend::umma_rows(const void* w, int fmt, int64_t rows, int64_t K, bool constant, const void** out,
+                                int64_t* pitch) {
   const int64_t rb = (int64_t)row_bytes(fmt, K);
   if (rb % 16 == 0) {
     *out = w;
@@ -424,6 +503,24 @@ Error MoeCudaBackend::umma_rows(const void* w, int fmt, int64_t rows, int64_t K,
     return Error::success();
   }
   const int64_t pp = umma_pitch(fmt, K);
+  if (constant) {  // registered weights: pad once, keep the copy until the buffer is released
+    const auto key = std::make_tuple(w, fmt, K, rows);
+    auto it = padded_.find(key);
+    if (it == padded_.end()) {
+      void* d = nullptr;
+      UAII_CUDA(cudaMalloc(&d, (size_t)(rows * pp)), "Malloc(padded weights)");
+      cudaError_t st = launch_pad_rows(w, rb, rows, rb, d, pp, stream_);
+      if (st != cudaSuccess) {
+        (void)cudaFree(d);
+        return cuda_status(st, "pad_rows");
+      }
+      count_launches(1);
+      it = padded_.emplace(key, Padded{d, pp}).first;
+    }
+    *out = it->second.dev;
+    *pitch = it->second.pitch;
+    return Error::success();
+  }
   void* d = carve((size_t)(rows * pp));
   UAII_CUDA(launch_pad_rows(w, rb, rows, rb, d, pp, stream_), "pad_rows");
   count_launches(1);
@@ -444,7 +541,7 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
   if (P.umma_refused)
     return Error::make(ErrorCode::NotImplemented,
                        "tensor-core path needs Q4_0/Q8_0/Q4_K/Q6_K weights, d_ff % 64 == 0 and d_model % 128 == 0 "
-                       "(Q4_K/Q6_K: both multiples of 256)");
+                       "(Q4_K/Q6_K: both multiples of 256; warp-MMA schedule: both multiples of 128)");
   RouteBuffers rb{};
   rb.topk_ids = static_cast<int32_t*>(carve(sizeof(int32_t) * S));
   rb.topk_w = static_cast<float*>(carve(sizeof(float) * S));
@@ -475,25 +572,27 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
     void* h16 = carve(2 * (size_t)(S * I));
     splits = P.splits;
     out = static_cast<float*>(carve(sizeof(float) * (size_t)(splits * S * D)));
-    if (ep) {
+    if (ep) {  // rows arrive in the tcgen05 operand order
+      if (P.warp_mma) return Error::make(ErrorCode::Internal, "expert-parallel rows planned on the warp-MMA schedule");
       UAII_CUDA(launch_route_gather16(ep->x16, T, D, E, k, rb, xp16, stream_), "route_gather16");
     } else {
-      UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, nullptr, xp16, stream_), "route_gather");
+      UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, nullptr, xp16, stream_, P.warp_mma), "route_gather");
     }
     phase_end();
     count_launches(3);
     phase_begin(kGateUp);
     int64_t gpitch = 0, dpitch = 0;
-    UAII_TRY(umma_rows(gd, L.gate.fmt, E * I, D, &gd, &gpitch));
-    UAII_TRY(umma_rows(ud, L.up.fmt, E * I, D, &ud, &gpitch));
-    UAII_TRY(umma_rows(dd, L.down.fmt, E * D, I, &dd, &dpitch));
+    UAII_TRY(umma_rows(gd, L.gate.fmt, E * I, D, weight_is_constant(L.gate.data, expert_bytes(L.gate, E)), &gd, &gpitch));
+    UAII_TRY(umma_rows(ud, L.up.fmt, E * I, D, weight_is_constant(L.up.data, expert_bytes(L.up, E)), &ud, &gpitch));
+    UAII_TRY(umma_rows(dd, L.down.fmt, E * D, I, weight_is_constant(L.down.data, expert_bytes(L.down, E)), &dd,
+                       &dpitch));
     UAII_CUDA(launch_gateup_umma(L.gate.fmt, gd, ud, gpitch, E, I, D, xp16, S, rb.counts, rb.offsets, tile_base, P.bn,
-                                 h16, dev_err_, stream_),
+                                 h16, dev_err_, stream_, P.warp_mma),
               "gateup(tensor cores)");
     phase_end();
     phase_begin(kDown);
     UAII_CUDA(launch_down_umma(L.down.fmt, dd, dpitch, E, D, I, h16, S, rb.counts, rb.offsets, tile_base, P.bn, splits,
-                               out, dev_err_, stream_),
+                               out, dev_err_, stream_, P.warp_mma),
               "down(tensor cores)");
     phase_end();
     count_launches(4);
@@ -535,16 +634,19 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
       void* sh_h16 = carve(2 * (size_t)(T * Is));
       sh_splits = P.sh_splits;
       sh_out = static_cast<float*>(carve(sizeof(float) * (size_t)(sh_splits * T * D)));
-      UAII_CUDA(launch_to_f16(xd, T * D, x16, stream_), "shared_to_f16");
+      UAII_CUDA(launch_to_f16(xd, T * D, x16, stream_, P.sh_warp_mma), "shared_to_f16");
       int64_t sgp = 0, sdp = 0;
-      UAII_TRY(umma_rows(sg, L.gate_sh.fmt, Is, D, &sg, &sgp));
-      UAII_TRY(umma_rows(su, L.up_sh.fmt, Is, D, &su, &sgp));
-      UAII_TRY(umma_rows(sd, L.down_sh.fmt, D, Is, &sd, &sdp));
+      UAII_TRY(umma_rows(sg, L.gate_sh.fmt, Is, D, weight_is_constant(L.gate_sh.data, expert_bytes(L.gate_sh, 1)), &sg,
+                         &sgp));
+      UAII_TRY(umma_rows(su, L.up_sh.fmt, Is, D, weight_is_constant(L.up_sh.data, expert_bytes(L.up_sh, 1)), &su,
+                         &sgp));
+      UAII_TRY(umma_rows(sd, L.down_sh.fmt, D, Is, weight_is_constant(L.down_sh.data, expert_bytes(L.down_sh, 1)), &sd,
+                         &sdp));
       UAII_CUDA(launch_gateup_umma(L.gate_sh.fmt, sg, su, sgp, 1, Is, D, x16, T, sh_route + 2, sh_route, sh_tiles,
-                                   P.sh_bn, sh_h16, dev_err_, stream_),
+                                   P.sh_bn, sh_h16, dev_err_, stream_, P.sh_warp_mma),
                 "shared_gateup(tensor cores)");
       UAII_CUDA(launch_down_umma(L.down_sh.fmt, sd, sdp, 1, D, Is, sh_h16, T, sh_route + 2, sh_route, sh_tiles, P.sh_bn,
-                                 sh_splits, sh_out, dev_err_, stream_),
+                                 sh_splits, sh_out, dev_err_, stream_, P.sh_warp_mma),
                 "shared_down(tensor cores)");
       count_launches(6);
     } else {
@@ -577,7 +679,10 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
 
 namespace {
 
-size_t experts_ws_bytes(const LayerArgs& L, int64_t T, const ExpertPlan& P) {
+// pad_*: how many padded row copies (gate and up: 0..2) live in the workspace
+// (unregistered sources)
+size_t experts_ws_bytes(const LayerArgs& L, int64_t T, const ExpertPlan& P, int pad_gateup, bool pad_down,
+                        int pad_gateup_sh, bool pad_down_sh) {
   const int64_t S = T * L.top_k;
   size_t b = 0;
   b += 5 * align_up(sizeof(int32_t) * S) + align_up((size_t)(L.E * T));
@@ -585,8 +690,10 @@ size_t experts_ws_bytes(const LayerArgs& L, int64_t T, const ExpertPlan& P) {
   if (P.umma) {
     b += align_up(2 * (size_t)(S * L.D)) + align_up(2 * (size_t)(S * L.I)) +
          align_up(sizeof(float) * (size_t)(P.splits * S * L.D));
-    if (row_bytes(L.gate.fmt, L.D) % 16) b += 2 * align_up((size_t)(L.E * L.I * umma_pitch(L.gate.fmt, L.D)));
-    if (row_bytes(L.down.fmt, L.I) % 16) b += align_up((size_t)(L.E * L.D * umma_pitch(L.down.fmt, L.I)));
+    if (row_bytes(L.gate.fmt, L.D) % 16)
+      b += (size_t)pad_gateup * align_up((size_t)(L.E * L.I * umma_pitch(L.gate.fmt, L.D)));
+    if (pad_down && row_bytes(L.down.fmt, L.I) % 16)
+      b += align_up((size_t)(L.E * L.D * umma_pitch(L.down.fmt, L.I)));
   }
   else
     b += 2 * align_up(sizeof(float) * S * L.D) + align_up(sizeof(float) * S * L.I);
@@ -595,8 +702,10 @@ size_t experts_ws_bytes(const LayerArgs& L, int64_t T, const ExpertPlan& P) {
     if (P.sh_umma) {
       b += align_up(2 * (size_t)(T * L.D)) + align_up(2 * (size_t)(T * L.I_sh)) +
            align_up(sizeof(float) * (size_t)(P.sh_splits * T * L.D));
-      if (row_bytes(L.gate_sh.fmt, L.D) % 16) b += 2 * align_up((size_t)(L.I_sh * umma_pitch(L.gate_sh.fmt, L.D)));
-      if (row_bytes(L.down_sh.fmt, L.I_sh) % 16) b += align_up((size_t)(L.D * umma_pitch(L.down_sh.fmt, L.I_sh)));
+      if (row_bytes(L.gate_sh.fmt, L.D) % 16)
+        b += (size_t)pad_gateup_sh * align_up((size_t)(L.I_sh * umma_pitch(L.gate_sh.fmt, L.D)));
+      if (pad_down_sh && row_bytes(L.down_sh.fmt, L.I_sh) % 16)
+        b += align_up((size_t)(L.D * umma_pitch(L.down_sh.fmt, L.I_sh)));
     }
     else
       b += align_up(sizeof(float) * T * L.I_sh) + align_up(sizeof(float) * T * L.D);
@@ -625,6 +734,13 @@ Error check_layer(const LayerArgs& L) {
 }
 
 }  // namespace
+
+size_t MoeCudaBackend::experts_ws(const LayerArgs& L, int64_t T, const ExpertPlan& P) const {
+  auto copies = [&](const ExpertWeights& w, int64_t E) { return weight_is_constant(w.data, expert_bytes(w, E)) ? 0 : 1; };
+  const bool sh = L.I_sh > 0;
+  return experts_ws_bytes(L, T, P, copies(L.gate, L.E) + copies(L.up, L.E), copies(L.down, L.E) != 0,
+                          sh ? copies(L.gate_sh, 1) + copies(L.up_sh, 1) : 0, sh && copies(L.down_sh, 1) != 0);
+}
 
 // ---------------------------------------------------------------- expert parallelism
 
@@ -692,8 +808,8 @@ Error MoeCudaBackend::ep_experts(const LayerArgs& Lin, const void* recv_x16, con
                         static_cast<const void*>(recv_w),
                         static_cast<const void*>(y_part)})
     if (!is_device_ptr(p)) return Error::make(ErrorCode::InvalidArgument, "ep experts: arguments must be device memory");
-  const ExpertPlan P = plan_experts(L, N, entries);
-  UAII_TRY(reserve(experts_ws_bytes(L, N, P) + layer_stage_bytes(L)));
+  const ExpertPlan P = plan_experts(L, N, entries, /*allow_warp_mma=*/false);
+  UAII_TRY(reserve(experts_ws(L, N, P) + layer_stage_bytes(L)));
   const EpRows rows{recv_x16, recv_ids, recv_w};
   return run_experts(nullptr, nullptr, nullptr, L, P, N, y_part, &rows);
 }
@@ -723,10 +839,6 @@ Error MoeCudaBackend::ep_combine(const float* y_back, const int32_t* row_of, int
   count_launches(1);
   return Error::success();
 }
-
-namespace {
-size_t expert_bytes(const ExpertWeights& w, int64_t E) { return (size_t)(E * w.rows) * row_bytes(w.fmt, w.cols); }
-}  // namespace
 
 size_t MoeCudaBackend::layer_stage_bytes(const LayerArgs& L) const {
   size_t b = weight_stage_bytes(L.gate.data, expert_bytes(L.gate, L.E)) +
@@ -760,7 +872,7 @@ Error MoeCudaBackend::experts(const float* x, const ExpertWeights& g, const Expe
   if (T == 0) return Error::success();
   const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E);
   const ExpertPlan P = plan_experts(L, T);
-  UAII_TRY(reserve(experts_ws_bytes(L, T, P) + 2 * align_up(xb) + align_up(pb) + layer_stage_bytes(L)));
+  UAII_TRY(reserve(experts_ws(L, T, P) + 2 * align_up(xb) + align_up(pb) + layer_stage_bytes(L)));
   void* xs = carve(xb);
   void* ps = carve(pb);
   float* ys = static_cast<float*>(carve(xb));
@@ -794,7 +906,7 @@ Error MoeCudaBackend::ffn(const LayerArgs& Lin, const float* x, int64_t T, float
   const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E);
   const ExpertPlan P = plan_experts(L, T);
   const size_t rsb = router_scratch_bytes(T, D, E);
-  UAII_TRY(reserve(experts_ws_bytes(L, T, P) + 2 * align_up(xb) + 2 * align_up(pb) + align_up(rsb) +
+  UAII_TRY(reserve(experts_ws(L, T, P) + 2 * align_up(xb) + 2 * align_up(pb) + align_up(rsb) +
                    layer_stage_bytes(L)));
   void* xs = carve(xb);
   float* ys = static_cast<float*>(carve(xb));
@@ -1162,7 +1274,7 @@ int uaii_moe_selftest_wait_timeout(uaii_moe_backend* b, int64_t budget_cycles) {
 int uaii_moe_last_plan(uaii_moe_backend* b, int* tensor_cores, int* slot_tile, int* down_splits) {
   if (!b) return no_backend();
   const uaii_b200::ExpertPlan P = b->impl.last_plan();
-  if (tensor_cores) *tensor_cores = P.umma ? 1 : 0;
+  if (tensor_cores) *tensor_cores = P.umma ? (P.warp_mma ? 2 : 1) : 0;
   if (slot_tile) *slot_tile = P.bn;
   if (down_splits) *down_splits = P.splits;
   return report(Error::success());
@@ -1170,7 +1282,7 @@ int uaii_moe_last_plan(uaii_moe_backend* b, int* tensor_cores, int* slot_tile, i
 
 int uaii_moe_set_expert_path(uaii_moe_backend* b, int path) {
   if (!b) return no_backend();
-  if (path < 0 || path > 2) return report(Error::make(ErrorCode::InvalidArgument, "path must be 0, 1 or 2"));
+  if (path < 0 || path > 3) return report(Error::make(ErrorCode::InvalidArgument, "path must be 0, 1, 2 or 3"));
   b->impl.set_expert_path(path);
   return report(Error::success());
 }

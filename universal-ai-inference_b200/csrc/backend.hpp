@@ -12,6 +12,7 @@
 
 #include <cstdint>
 #include <map>
+#include <tuple>
 #include <mutex>
 #include <string>
 #include <utility>
@@ -84,10 +85,11 @@ struct LayerArgs {
 
 struct ExpertPlan {
   bool umma = false;   // tensor-core grouped GEMM (else CUDA-core GEMV)
+  bool warp_mma = false;      // ... on the warp-MMA (mma.sync) schedule, else tcgen05
   bool umma_refused = false;  // tensor cores forced but the layer does not qualify
   int bn = 16;         // slots per tile (MMA N)
   int splits = 1;      // K splits of the down projection
-  bool sh_umma = false;
+  bool sh_umma = false, sh_warp_mma = false;
   int sh_bn = 16, sh_splits = 1;
 };
 
@@ -148,7 +150,7 @@ class MoeCudaBackend {
   Error reserve(size_t bytes);
   void* carve(size_t bytes);
   // `slots`: routed (token, expert) pairs when known (expert-parallel rows), else T * top_k.
-  ExpertPlan plan_experts(const LayerArgs& L, int64_t T, int64_t slots = -1) const;
+  ExpertPlan plan_experts(const LayerArgs& L, int64_t T, int64_t slots = -1, bool allow_warp_mma = true) const;
   // Rows received by an expert-parallel rank: f16 activations in operand order and
   // top_k (local expert | -1, weight) entries per row; replaces the router output.
   struct EpRows {
@@ -160,7 +162,12 @@ class MoeCudaBackend {
                     const LayerArgs& L, const ExpertPlan& P, int64_t T, float* y_dev,
                     const EpRows* ep = nullptr);
   Error sync_and_check();
-  Error umma_rows(const void* w, int fmt, int64_t rows, int64_t K, const void** out, int64_t* pitch);
+  // Packed rows as the tensor-core path reads them (16-byte pitch).  `constant`: the
+  // source is a registered buffer, so a padded copy is made once and kept.
+  Error umma_rows(const void* w, int fmt, int64_t rows, int64_t K, bool constant, const void** out, int64_t* pitch);
+  // Registered (host copy or device buffer): unchanged until released.
+  bool weight_is_constant(const void* p, size_t bytes) const;
+  size_t experts_ws(const LayerArgs& L, int64_t T, const ExpertPlan& P) const;
 
  public:
   Error sync_and_check_public() {
@@ -199,7 +206,15 @@ class MoeCudaBackend {
   char* ws_ = nullptr;
   size_t ws_cap_ = 0;
   size_t ws_used_ = 0;
-  std::map<std::pair<const void*, size_t>, void*> weights_;
+  std::map<std::pair<const void*, size_t>, void*> weights_;   // registered host buffer -> device copy
+  std::map<const void*, size_t> const_dev_;                     // registered device buffers
+  struct Padded {
+    void* dev;
+    int64_t pitch;
+  };
+  // (source device rows, format, K, rows) -> copy with 16-byte row pitch, for constant sources
+  std::map<std::tuple<const void*, int, int64_t, int64_t>, Padded> padded_;
+  void drop_padded(const char* lo, const char* hi);
   std::mutex mu_;
 };
 

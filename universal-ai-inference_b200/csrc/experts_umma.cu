@@ -37,6 +37,7 @@
 
 #include "gguf_blocks.cuh"
 #include "kernels.hpp"
+#include "operand_order.cuh"
 #include "umma.cuh"
 
 namespace uaii_b200 {
@@ -286,9 +287,6 @@ __device__ __forceinline__ void dequant_atom(const uint8_t* row, int off, int g,
     }
   }
 }
-
-// position of K element i in the operand order [0, 2, 1, 3] of every group of four
-__device__ __forceinline__ int k_perm(int i) { return (i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1); }
 
 struct Tile {
   int e, m_tile, n_tile, split;
@@ -674,7 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (args.gateup) {
         // lane l < 16 holds gate, lane l + 16 up of feature i0 + 16q + (l & 15); each
         // column pair (n, n+1) is split: the gate lane finishes n, the up lane n + 1
-        const int feat = k_perm(t.m_tile * 64 + 16 * q + (lane & 15));
+        const int feat = (int)tc_kpos(t.m_tile * 64 + 16 * q + (lane & 15));
         const bool gate_lane = lane < 16;
         for (int cb = grp * kCols; cb < (grp + 1) * kCols; cb += kW) {
           uint32_t r[8];
@@ -793,6 +791,420 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
   }
+}
+
+// ======================================================================
+// Warp-MMA schedule for narrow slot tiles (8 or 16 routed slots: decode).
+//
+// At N <= 16 the tcgen05 schedule spends most of each quad moving the
+// dequantized A tile into tensor memory and handing it to the issuing thread.
+// Here every compute warp keeps its dequantized A fragments in registers and
+// multiplies them with mma.sync.m16n8k16 (f16 x f16 -> f32): no A store, no
+// issuing thread, no A barriers.  Warp w of the 16 compute warps owns weight
+// rows 16*(w%8) .. +15 of the 128-row tile and K half w/8 of every quad; its
+// lane (g = lane/4, t = lane%4) decodes rows g and g+8 of that block for the
+// 32 K elements [32t, 32t+32) of the half -- one Q4_0 / Q8_0 block or one
+// K-quant sub-block, so one scale per row.  The activation and h rows are
+// stored in the matching order (wm_kpos).  The two K halves are added in
+// shared memory after each tile.  Warp 16 is the TMA producer of the packed
+// weight windows and of the activation tiles (SWIZZLE_128B, read with
+// ldmatrix).  Each dequantized operand equals the tcgen05 schedule's.
+constexpr int kWmWarps = 16;                   // compute warps
+constexpr int kWmThreads = 32 * (kWmWarps + 1);
+
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Named barrier over `n` threads that also ORs a predicate across them.
+__device__ __forceinline__ bool bar_any(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+// NW 32-bit words starting at an even byte offset `off` of shared memory row
+// `p` (4-byte aligned): 4-byte loads joined by a funnel shift of 0 or 16 bits.
+template <int NW>
+__device__ __forceinline__ void words_at(const uint8_t* p, int off, uint32_t (&w)[NW]) {
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(p + (off & ~3));
+  const uint32_t sh = (uint32_t)(off & 2) * 8u;
+  uint32_t u[NW + 1];
+#pragma unroll
+  for (int j = 0; j <= NW; ++j) u[j] = src[j];
+#pragma unroll
+  for (int j = 0; j < NW; ++j) w[j] = __funnelshift_r(u[j], u[j + 1], sh);
+}
+
+// One row's unit t of half h (32 K elements): loaded and scaled once per quad,
+// then unpacked two f16 pairs per k-step: pair(ks) gives lo = elements
+// (4ks, 4ks+2) and hi = (4ks+1, 4ks+3) of the unit -- the fragment registers of
+// positions (2t, 2t+1) and (2t+8, 2t+9) of k-step ks.  Unpacking per k-step
+// lets the MMA of one k-step run while the next one is unpacked.  `row` is the
+// row in box 0 of the packed stage, `row1` the same row in box 1 (Q8_0), `off`
+// the quad's offset in its window (Q6_K; 0 for the others).
+template <int F> struct WmUnit;
+
+// Q4_K: sub-block sb = 4h + t = nibble (t & 1) of qs[32 * (sb / 2) ..]; value
+// d*sc*q - dmin*m.  Low nibble: (1024 + q) - 1024; high nibble: (1024 + 16q) / 16 - 64
+// (both exact), so one code path serves both with per-lane mask and constants.
+template <> struct WmUnit<kQ4_K> {
+  struct Lane {
+    int sb, sh;
+    uint32_t mask;
+    __half2 c1, c0;
+    __device__ Lane(int h, int t)
+        : sb(4 * h + t), sh(8 * (t & 3)), mask((t & 1) ? 0x00F000F0u : 0x000F000Fu),
+          c1(__float2half2_rn((t & 1) ? 0.0625f : 1.0f)), c0(__float2half2_rn((t & 1) ? -64.f : -1024.f)) {}
+  };
+  uint32_t w[8];
+  __half2 dd, nm;
+  __device__ __forceinline__ void load(const uint8_t* row, const uint8_t*, int, const Lane& L) {
+    const uint4 hdr = *reinterpret_cast<const uint4*>(row);  // d, dmin, scales[12]
+    const float d = f16f(hdr.x & 0xFFFFu), dmin = f16f(hdr.x >> 16);
+    const uint32_t y = hdr.y >> L.sh, z = hdr.z >> L.sh, w4 = hdr.w >> L.sh;
+    const int sc = L.sb < 4 ? (int)(y & 63u) : (int)((w4 & 15u) | (((y >> 6) & 3u) << 4));
+    const int m = L.sb < 4 ? (int)(z & 63u) : (int)(((w4 >> 4) & 15u) | (((z >> 6) & 3u) << 4));
+    dd = __float2half2_rn(d * (float)sc);
+    nm = __float2half2_rn(-(dmin * (float)m));
+    const uint4* qp = reinterpret_cast<const uint4*>(row + 16 + 32 * (L.sb >> 1));
+    const uint4 qa = qp[0], qb = qp[1];
+    w[0] = qa.x; w[1] = qa.y; w[2] = qa.z; w[3] = qa.w;
+    w[4] = qb.x; w[5] = qb.y; w[6] = qb.z; w[7] = qb.w;
+  }
+  __device__ __forceinline__ void pair(int ks, const Lane& L, uint32_t& lo, uint32_t& hi) const {
+    lo = as_u32(__hfma2(__hfma2(magic_pair(w[ks], L.mask), L.c1, L.c0), dd, nm));
+    hi = as_u32(__hfma2(__hfma2(magic_pair(w[ks] >> 8, L.mask), L.c1, L.c0), dd, nm));
+  }
+};
+
+// Q4_0: block b = 4h + t at byte 18b {f16 d; u8 qs[16]}: low nibbles -> elements
+// 0..15 (k-steps 0-3), high -> 16..31 (k-steps 4-7); value (q - 8) * d.
+template <> struct WmUnit<kQ4_0> {
+  struct Lane {
+    int b;
+    __device__ Lane(int h, int t) : b(4 * h + t) {}
+  };
+  uint32_t w[4];
+  __half2 d;
+  __device__ __forceinline__ void load(const uint8_t* row, const uint8_t*, int, const Lane& L) {
+    const __half dh = __ushort_as_half((unsigned short)ld_u16(row + 18 * L.b));
+    d = __halves2half2(dh, dh);
+    words_at<4>(row, 18 * L.b + 2, w);
+  }
+  __device__ __forceinline__ void pair(int ks, const Lane&, uint32_t& lo, uint32_t& hi) const {
+    const uint32_t q = w[ks & 3];
+    if (ks < 4) {
+      const __half2 bias = __float2half2_rn(1032.f);
+      lo = as_u32(__hmul2(__hsub2(magic_pair(q, 0x000F000Fu), bias), d));
+      hi = as_u32(__hmul2(__hsub2(magic_pair(q >> 8, 0x000F000Fu), bias), d));
+    } else {
+      const __half2 k16 = __float2half2_rn(0.0625f), bias = __float2half2_rn(-72.f);
+      lo = as_u32(__hmul2(__hfma2(magic_pair(q, 0x00F000F0u), k16, bias), d));
+      hi = as_u32(__hmul2(__hfma2(magic_pair(q >> 8, 0x00F000F0u), k16, bias), d));
+    }
+  }
+};
+
+// Q8_0: block b = 4h + t at byte 34b {f16 d; i8 qs[32]}; blocks 4..7 are read from
+// box 1 (window byte 128 on).  q ^ 0x80 = q + 128 as an unsigned byte.
+template <> struct WmUnit<kQ8_0> {
+  struct Lane {
+    int b;
+    __device__ Lane(int h, int t) : b(4 * h + t) {}
+  };
+  uint32_t w[8];
+  __half2 d;
+  __device__ __forceinline__ void load(const uint8_t* row, const uint8_t* row1, int, const Lane& L) {
+    const uint8_t* base = L.b < 4 ? row : row1 - 128;
+    const __half dh = __ushort_as_half((unsigned short)ld_u16(base + 34 * L.b));
+    d = __halves2half2(dh, dh);
+    words_at<8>(base, 34 * L.b + 2, w);
+  }
+  __device__ __forceinline__ void pair(int ks, const Lane&, uint32_t& lo, uint32_t& hi) const {
+    const __half2 bias = __float2half2_rn(1152.f);
+    const uint32_t q = w[ks] ^ 0x80808080u;
+    lo = as_u32(__hmul2(__hsub2(magic_pair(q, 0x00FF00FFu), bias), d));
+    hi = as_u32(__hmul2(__hsub2(magic_pair(q >> 8, 0x00FF00FFu), bias), d));
+  }
+};
+
+// Q6_K half h, quarter t: ql nibble (t >> 1) of ql[64h + 32(t & 1) ..], bits 2t of
+// qh[32h ..], scales sc[8h + 2t] (k-steps 0-3) and sc[8h + 2t + 1]; value d*sc*(q - 32).
+template <> struct WmUnit<kQ6_K> {
+  struct Lane {
+    int h, t;
+    uint32_t ns, hsh;
+    __device__ Lane(int h_, int t_) : h(h_), t(t_), ns(4u * (uint32_t)(t_ >> 1)), hsh(2u * (uint32_t)t_) {}
+  };
+  uint32_t q6[8];  // 6-bit values in the low bits of each byte (bits 6-7: junk)
+  __half2 s0, s1;
+  // OFF = the super-block's offset in its 16-byte aligned window (even, 0..14)
+  template <int OFF>
+  __device__ __forceinline__ void load_off(const uint8_t* row, const Lane& L) {
+    uint32_t w[8];
+    load_words<OFF, 8>(row, 4 * L.h + 2 * (L.t & 1), w);  // ql bytes 64h + 32(t & 1) ..
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q6[i] = (w[i] >> L.ns) & 0x0F0F0F0Fu;
+    load_words<OFF, 8>(row, 8 + 2 * L.h, w);  // qh bytes 128 + 32h ..
+    // bits 6-7 of every byte carry junk from the neighbouring 2-bit fields; the 0x3F mask in pair() drops them
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q6[i] |= ((w[i] >> L.hsh) << 4) & 0xF0F0F0F0u;
+    const int8_t* sc = reinterpret_cast<const int8_t*>(row + OFF + 192 + 8 * L.h + 2 * L.t);
+    const float d = f16f(ld_u16(row + OFF + 208));
+    s0 = __float2half2_rn(d * (float)sc[0]);
+    s1 = __float2half2_rn(d * (float)sc[1]);
+  }
+  __device__ __forceinline__ void pair(int ks, const Lane&, uint32_t& lo, uint32_t& hi) const {
+    const __half2 s = ks < 4 ? s0 : s1;
+    const __half2 bias = __float2half2_rn(1056.f);
+    lo = as_u32(__hmul2(__hsub2(magic_pair(q6[ks], 0x003F003Fu), bias), s));
+    hi = as_u32(__hmul2(__hsub2(magic_pair(q6[ks] >> 8, 0x003F003Fu), bias), s));
+  }
+};
+
+template <int F, int NT, int ST>
+struct WmCfg {
+  using Fm = Fmt<F>;
+  static constexpr int BN = 8 * NT;
+  static constexpr int kWB = Fm::kBoxBytes;
+  static constexpr int kPStage = Fm::kBoxes * 128 * kWB;
+  static constexpr int kBAtom = BN * 128;  // one 64-K SWIZZLE_128B box of BN activation rows
+  static constexpr int kBQuad = 4 * kBAtom;
+  static constexpr int kOffB = 0;
+  static constexpr int kOffP = kOffB + ST * kBQuad;
+  static constexpr int kRedBytes = 8 * 32 * 4 * NT * 4;  // [8 row blocks][32 lanes][4 NT] f32
+  static constexpr int kOffR = kOffP + ST * kPStage;
+  static constexpr int kOffBar = kOffR + kRedBytes;
+  static constexpr int kNumBars = 2 * ST;
+  static constexpr int kSmem = kOffBar + kNumBars * 8 + 16 + 1024;
+  static_assert(kOffP % 1024 == 0 && kBAtom % 1024 == 0, "SWIZZLE_128B stages must be 1024-byte aligned");
+};
+
+template <int F, int NT, int ST>
+__global__ void __launch_bounds__(kWmThreads, 1)
+    expert_warp_mma_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
+                           const __grid_constant__ CUtensorMap tm_x, const Args args) {
+  using C = WmCfg<F, NT, ST>;
+  using Fm = Fmt<F>;
+  constexpr int BN = C::BN;
+  constexpr int kCompute = kWmWarps * 32;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sB = smem + C::kOffB;
+  uint8_t* sP = smem + C::kOffP;
+  float* sR = reinterpret_cast<float*>(smem + C::kOffR);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* full = bars;        // weight window + activation tile of a quad landed
+  uint64_t* empty = full + ST;  // every compute warp is done with the stage
+  volatile int* s_abort = reinterpret_cast<volatile int*>(bars + C::kNumBars);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, kWmWarps);
+    }
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == kWmWarps && lane == 0) {
+    prefetch_tmap(&tm_w0);
+    prefetch_tmap(&tm_w1);
+    prefetch_tmap(&tm_x);
+  }
+  __syncthreads();
+  const int total = __ldg(args.tile_base + args.E);
+  int* err = args.err;
+  auto quad_range = [&](const Tile& t, int& q0, int& q1) {
+    q0 = t.split * args.kquads / args.splits;
+    q1 = (t.split + 1) * args.kquads / args.splits;
+  };
+  auto quad_atoms = [&](int q) { return min(4, args.k_atoms - 4 * q); };
+
+  if (warp == kWmWarps) {
+    // ------------------------------------------------------------ TMA producer
+    uint32_t n = 0;  // stages issued
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+      const Tile t = decode_tile(args, tile, BN);
+      const int row0 = t.e * args.rows_per_expert + t.m_tile * (args.gateup ? 64 : 128);
+      const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
+      int q0, q1;
+      quad_range(t, q0, q1);
+      for (int q = q0; q < q1; ++q) {
+        const int s = n % ST;
+        if (!(ok = bounded_wait(empty + s, ((n / ST) & 1) ^ 1, s_abort, err, kErrTimeoutProducer))) break;
+        const int x = (q * Fm::kBytes) & ~15;
+        const int na = quad_atoms(q);
+        uint8_t* dst = sP + s * C::kPStage;
+        if (elect_one()) {
+          mbar_arrive_expect_tx(full + s, C::kPStage + na * C::kBAtom);
+#pragma unroll
+          for (int j = 0; j < Fm::kBoxes; ++j) {
+            uint8_t* d = dst + j * 128 * C::kWB;
+            tma_load_2d(d, &tm_w0, full + s, x + 128 * j, row0);
+            if (args.gateup) tma_load_2d(d + 64 * C::kWB, &tm_w1, full + s, x + 128 * j, row0);
+            else tma_load_2d(d + 64 * C::kWB, &tm_w0, full + s, x + 128 * j, row0 + 64);
+          }
+          for (int j = 0; j < na; ++j)
+            tma_load_2d(sB + s * C::kBQuad + j * C::kBAtom, &tm_x, full + s, q * kQuadK + 64 * j, slot0);
+        }
+        __syncwarp();
+        ++n;
+      }
+    }
+    // never leave with copies in flight: the last ST stages
+    for (uint32_t j = n > (uint32_t)ST ? n - ST : 0; j < n; ++j) (void)mbar_wait(full + j % ST, (j / ST) & 1);
+  } else {
+    // ------------------------------------------------------------ compute warps
+    const int mw = warp & 7, h = warp >> 3;   // 16-row block, K half of every quad
+    const int g = lane >> 2, tq = lane & 3;   // fragment row group, K unit
+    const int r0 = 16 * mw + g, r1 = r0 + 8;  // packed stage rows (gate/up: gate 0-63, up 64-127)
+    // ldmatrix: lanes 8i .. 8i+7 address the rows of matrix i = (slot octet i/2, k octet i%2)
+    const int ld_mi = lane >> 3, ld_n = 8 * (ld_mi >> 1) + (lane & 7), ld_kh = ld_mi & 1;
+    float* red = sR + (mw * 32 + lane) * 4 * NT;
+    const typename WmUnit<F>::Lane ul(h, tq);
+    uint32_t pi = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+      const Tile t = decode_tile(args, tile, BN);
+      int q0, q1;
+      quad_range(t, q0, q1);
+      float acc[2][4];  // NT accumulators; for NT == 1 the even / odd k-step halves of one
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[n][i] = 0.f;
+      WmUnit<F> u0, u1;
+      auto fetch = [&](WmUnit<F>& x0, WmUnit<F>& x1, int q, uint32_t p) -> bool {
+        if (!bounded_wait(full + p % ST, (p / ST) & 1, s_abort, err, kErrTimeoutDequant)) return false;
+        if (2 * h < quad_atoms(q)) {  // this half of the quad exists (K % 256 == 128 leaves it out)
+          const int off = (q * Fm::kBytes) & 15;
+          const uint8_t* stage = sP + (p % ST) * C::kPStage;
+          if constexpr (F == kQ6_K) {  // 16-byte loads with the window offset as a constant
+            switch (off) {
+#define UAII_WM_Q6(O)                                              \
+  case O:                                                          \
+    x0.template load_off<O>(stage + r0 * C::kWB, ul);              \
+    x1.template load_off<O>(stage + r1 * C::kWB, ul);              \
+    break;
+              UAII_WM_Q6(0) UAII_WM_Q6(2) UAII_WM_Q6(4) UAII_WM_Q6(6)
+              UAII_WM_Q6(8) UAII_WM_Q6(10) UAII_WM_Q6(12) UAII_WM_Q6(14)
+#undef UAII_WM_Q6
+              default: break;
+            }
+          } else {
+            x0.load(stage + r0 * C::kWB, stage + (128 + r0) * C::kWB, off, ul);
+            x1.load(stage + r1 * C::kWB, stage + (128 + r1) * C::kWB, off, ul);
+          }
+        }
+        return true;
+      };
+      auto multiply = [&](const WmUnit<F>& x0, const WmUnit<F>& x1, int q, uint32_t p) {
+        if (2 * h < quad_atoms(q)) {
+          const uint8_t* bq = sB + (p % ST) * C::kBQuad;
+          __syncwarp();  // ldmatrix / mma.sync below need the whole warp converged
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            uint32_t a[4];  // rows g, g + 8 at positions (2tq, 2tq+1); the same at (2tq+8, 2tq+9)
+            x0.pair(ks, ul, a[0], a[2]);
+            x1.pair(ks, ul, a[1], a[3]);
+            // k-step ks of half h = operand positions 128h + 16ks .. +15: atom 2h + ks/4, 16-byte chunk
+            // 2(ks % 4) + k octet, stored at chunk ^ (row % 8) (SWIZZLE_128B)
+            const int chunk = 2 * (ks & 3) + ld_kh;
+            const uint32_t addr =
+                smem_u32(bq + (2 * h + (ks >> 2)) * C::kBAtom + ld_n * 128 + ((chunk ^ (ld_n & 7)) << 4));
+            if constexpr (NT == 2) {
+              uint32_t b[4];
+              asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
+                           : "r"(addr));
+              mma_16816(acc[0], a, b[0], b[1]);
+              mma_16816(acc[NT - 1], a, b[2], b[3]);
+            } else {  // even and odd k-steps in two accumulators: two independent MMA chains
+              uint32_t b[2];
+              asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];"
+                           : "=r"(b[0]), "=r"(b[1])
+                           : "r"(addr));
+              mma_16816(acc[ks & 1], a, b[0], b[1]);
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + p % ST);
+      };
+      for (int q = q0; q < q1 && ok; ++q) {
+        if (!(ok = fetch(u0, u1, q, pi))) break;
+        multiply(u0, u1, q, pi++);
+      }
+      if constexpr (NT == 1) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[0][i] += acc[1][i];
+      }
+      // every compute warp reaches this barrier once per tile; a wait that gave up stops all of them
+      if (bar_any(1, kCompute, !ok)) break;
+      if (h == 1) {  // K half 1 hands its sums to half 0
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) red[4 * n + i] = acc[n][i];
+      }
+      bar_sync(1, kCompute);
+      if (h == 1) continue;
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[n][i] += red[4 * n + i];
+      // accumulator (n, i): row g + 8(i / 2) of the block, slot 8n + 2tq + i % 2
+      const int n_valid = min(BN, __ldg(args.counts + t.e) - t.n_tile * BN);
+      const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
+      if (args.gateup) {  // up rows (blocks 4-7) meet the gate rows (blocks 0-3) of the same features
+        if (mw >= 4) {
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) red[4 * n + i] = acc[n][i];
+        }
+        bar_sync(2, kCompute / 2);
+        if (mw < 4) {
+          const float* up = sR + ((mw + 4) * 32 + lane) * 4 * NT;
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int feat = t.m_tile * 64 + 16 * mw + g + 8 * (i >> 1);
+              const int sl = 8 * n + 2 * tq + (i & 1);
+              const float gv = acc[n][i], uv = up[4 * n + i];
+              const float sig = 1.0f / (1.0f + __expf(-gv));
+              if (sl < n_valid)
+                args.h_out[(int64_t)(slot0 + sl) * args.out_ld + wm_kpos(feat)] = __float2half_rn((gv * sig) * uv);
+            }
+        }
+      } else {
+        float* out = args.out + (int64_t)t.split * args.split_stride;
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int o = t.m_tile * 128 + 16 * mw + g + 8 * (i >> 1);
+            const int sl = 8 * n + 2 * tq + (i & 1);
+            if (sl < n_valid) out[(int64_t)(slot0 + sl) * args.out_ld + o] = acc[n][i];
+          }
+      }
+    }
+  }
+  __syncthreads();
 }
 
 __global__ void tile_table_kernel(const int32_t* counts, int E, int bn, int m_tiles, int splits,
@@ -919,6 +1331,44 @@ cudaError_t dispatch_bn(int bn, const CUtensorMap& w0, const CUtensorMap& w1, co
   }
 }
 
+// Warp-MMA schedule: ST (packed window + activation) stage pairs, as many as
+// fit next to the K-half exchange area, up to 8.
+template <int F, int NT>
+struct WmStages {
+  static constexpr int kBudget = 220 * 1024;
+  static constexpr int kPair = Fmt<F>::kBoxes * 128 * Fmt<F>::kBoxBytes + 4 * 8 * NT * 128;
+  static constexpr int kFit = (kBudget - 8 * 32 * 4 * NT * 4) / kPair;
+  static constexpr int ST = kFit > 8 ? 8 : kFit;
+  static_assert(ST >= 2, "shared-memory budget");
+};
+
+template <int F, int NT>
+cudaError_t run_warp_mma(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x, const Args& a,
+                         cudaStream_t st) {
+  constexpr int ST = WmStages<F, NT>::ST;
+  using C = WmCfg<F, NT, ST>;
+  static_assert(C::kSmem <= 227 * 1024, "shared memory budget");
+  auto kern = expert_warp_mma_kernel<F, NT, ST>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  kern<<<num_sms(), kWmThreads, C::kSmem, st>>>(w0, w1, x, a);
+  return cudaGetLastError();
+}
+
+template <int F>
+cudaError_t dispatch_warp(int bn, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
+                          const Args& a, cudaStream_t st) {
+  switch (bn) {
+    case 8: return run_warp_mma<F, 1>(w0, w1, x, a, st);
+    case 16: return run_warp_mma<F, 2>(w0, w1, x, a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 // K granularity a row of this format must have (64 or 256), 0 if unsupported.
 int min_k(int fmt) {
   switch (fmt) {
@@ -939,12 +1389,15 @@ bool make_weight_maps(CUtensorMap* m0, CUtensorMap* m1, const void* W0, const vo
          make_weight_map(m1, W1, pitch, rows_total, Fmt<F>::kBoxBytes);
 }
 
-cudaError_t launch_common(int fmt, bool gateup, const void* W0, const void* W1, int64_t pitch, int64_t E,
-                          int64_t rows, int64_t K, const void* act16, int64_t S_rows, const int32_t* counts,
-                          const int32_t* offsets, int32_t* tile_base, int bn, int splits, void* h16,
-                          float* out, int64_t out_ld, int64_t split_stride, int* err, cudaStream_t st) {
+// warp_mma: the mma.sync schedule (slot tiles of 8 or 16, K % 128 == 0, operand
+// rows in wm_kpos order); else tcgen05 (slot tiles 16..256, tc_kpos order).
+cudaError_t launch_common(bool warp_mma, int fmt, bool gateup, const void* W0, const void* W1, int64_t pitch,
+                          int64_t E, int64_t rows, int64_t K, const void* act16, int64_t S_rows,
+                          const int32_t* counts, const int32_t* offsets, int32_t* tile_base, int bn, int splits,
+                          void* h16, float* out, int64_t out_ld, int64_t split_stride, int* err, cudaStream_t st) {
   const int mk = min_k(fmt);
   if (!mk || K % mk != 0 || K <= 0) return cudaErrorNotSupported;
+  if (warp_mma && (K % 128 != 0 || (bn != 8 && bn != 16))) return cudaErrorNotSupported;
   const int m_rows = gateup ? 64 : 128;
   if (rows % m_rows != 0 || pitch % 16 != 0 || pitch < fmt_row_bytes(fmt, K)) return cudaErrorNotSupported;
   if (!aligned16(W0) || !aligned16(W1) || !aligned16(act16) || K % 8 != 0) return cudaErrorNotSupported;
@@ -980,6 +1433,15 @@ cudaError_t launch_common(int fmt, bool gateup, const void* W0, const void* W1, 
   a.out_ld = out_ld;
   a.split_stride = split_stride;
   a.err = err;
+  if (warp_mma) {
+    switch (fmt) {
+      case kQ4_0: return dispatch_warp<kQ4_0>(bn, m0, m1, mx, a, st);
+      case kQ8_0: return dispatch_warp<kQ8_0>(bn, m0, m1, mx, a, st);
+      case kQ4_K: return dispatch_warp<kQ4_K>(bn, m0, m1, mx, a, st);
+      case kQ6_K: return dispatch_warp<kQ6_K>(bn, m0, m1, mx, a, st);
+      default: return cudaErrorNotSupported;
+    }
+  }
   switch (fmt) {
     case kQ4_0: return dispatch_bn<kQ4_0>(bn, m0, m1, mx, a, st);
     case kQ8_0: return dispatch_bn<kQ8_0>(bn, m0, m1, mx, a, st);
@@ -1017,18 +1479,22 @@ bool umma_shapes_supported(int gfmt, int dfmt, int64_t D, int64_t I) {
 
 int64_t umma_pitch(int fmt, int64_t K) { return (fmt_row_bytes(fmt, K) + 15) / 16 * 16; }
 
+bool warp_mma_shapes_supported(int gfmt, int dfmt, int64_t D, int64_t I) {
+  return umma_shapes_supported(gfmt, dfmt, D, I) && D % 128 == 0 && I % 128 == 0;
+}
+
 cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pitch, int64_t E, int64_t I, int64_t D,
                                const void* xp16, int64_t S_rows, const int32_t* counts, const int32_t* offsets,
-                               int32_t* tile_base, int bn, void* h16, int* err, cudaStream_t st) {
-  return launch_common(fmt, true, G, U, pitch, E, I, D, xp16, S_rows, counts, offsets, tile_base, bn, 1, h16,
-                       nullptr, I, 0, err, st);
+                               int32_t* tile_base, int bn, void* h16, int* err, cudaStream_t st, bool warp_mma) {
+  return launch_common(warp_mma, fmt, true, G, U, pitch, E, I, D, xp16, S_rows, counts, offsets, tile_base, bn, 1,
+                       h16, nullptr, I, 0, err, st);
 }
 
 cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
                              int64_t S_rows, const int32_t* counts, const int32_t* offsets, int32_t* tile_base,
-                             int bn, int splits, float* out, int* err, cudaStream_t st) {
-  return launch_common(fmt, false, Dn, Dn, pitch, E, D, I, h16, S_rows, counts, offsets, tile_base, bn, splits,
-                       nullptr, out, D, S_rows * D, err, st);
+                             int bn, int splits, float* out, int* err, cudaStream_t st, bool warp_mma) {
+  return launch_common(warp_mma, fmt, false, Dn, Dn, pitch, E, D, I, h16, S_rows, counts, offsets, tile_base, bn,
+                       splits, nullptr, out, D, S_rows * D, err, st);
 }
 
 namespace {

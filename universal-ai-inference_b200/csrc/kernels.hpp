@@ -39,9 +39,6 @@ cudaError_t launch_route_topk(const float* scores, const float* probs, int64_t T
 cudaError_t launch_identity_route(int32_t* buf, int64_t T, cudaStream_t st);
 cudaError_t launch_route_scan(int64_t T, int64_t E, int k, const RouteBuffers& rb,
                               cudaStream_t st);
-// Gathers x rows into expert-contiguous slots: xp_f32 and/or xp_f16 (either may be null).
-// xp_f16 rows are in the tensor-core operand order: elements [0, 2, 1, 3] of
-// every group of four (the expert GEMM builds its weight tiles the same way).
 // Self-test of the bounded-wait failure path (selftest.cu): one block waits on
 // an mbarrier nothing arrives on, gives up after budget_cycles and records
 // `code` in *err.  Faults nothing; the kernel returns normally.
@@ -69,9 +66,12 @@ cudaError_t launch_route_gather16(const void* rows, int64_t N, int64_t D, int64_
 // y[t] = sum over d = 0..R-1 of y_back[row_of[t*R+d]] (rows that exist), fixed order.
 cudaError_t launch_ep_combine(const float* y_back, const int32_t* row_of, int64_t T, int R, int64_t D, float* y,
                               cudaStream_t st);
+// Gathers x rows into expert-contiguous slots: xp_f32 and/or xp_f16 (either may be null).
+// xp_f16 rows are in an operand K order (operand_order.cuh): tc_kpos for the
+// tcgen05 schedule, wm_kpos (wm_order, D % 128 == 0) for the warp-MMA one.
 cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E, int k,
                                 const RouteBuffers& rb, float* xp_f32, void* xp_f16,
-                                cudaStream_t st);
+                                cudaStream_t st, bool wm_order = false);
 // y[t] = sum_r w[t,r] * out[slot_of[t,r]] (rank order, from 0), then
 // y[t] += gate[t] * shared_out[t] when shared_out is given (gate may be null = 1).
 // `out` (and `shared_out`) may hold `splits` partial planes `split_stride`
@@ -80,8 +80,9 @@ cudaError_t launch_combine(const float* out, int64_t out_ld, int splits, int64_t
                            int64_t T, int64_t D, int k, const RouteBuffers& rb,
                            const float* shared_out, int sh_splits, int64_t sh_split_stride,
                            const float* shared_gate, float* y, cudaStream_t st);
-// x rows -> f16 copy (shared-expert operand in token order, tensor-core operand K order)
-cudaError_t launch_to_f16(const float* x, int64_t n, void* out, cudaStream_t st);
+// x rows -> f16 copy (shared-expert operand in token order; operand K order tc_kpos,
+// or wm_kpos with wm_order and n % 128 == 0)
+cudaError_t launch_to_f16(const float* x, int64_t n, void* out, cudaStream_t st, bool wm_order = false);
 // gate[t] = sigmoid(x[t] . w) with the reference GEMM summation order
 cudaError_t launch_shared_gate(const float* x, const float* w, int64_t T, int64_t D,
                                float* gate, cudaStream_t st);
@@ -105,17 +106,23 @@ bool umma_shapes_supported(int gate_fmt, int down_fmt, int64_t D, int64_t I);
 int umma_kchunks(int fmt, int64_t K);
 // Row pitch the tensor-core path reads a packed matrix with: row_bytes rounded up to 16.
 int64_t umma_pitch(int fmt, int64_t K);
+// The warp-MMA schedule (mma.sync, slot tiles of 8 or 16) also needs D and I to be
+// multiples of 128; its operand rows are in wm_kpos order (operand_order.cuh).
+bool warp_mma_shapes_supported(int gate_fmt, int down_fmt, int64_t D, int64_t I);
 // h16[slot, i] = silu(x.G[e,i]) * (x.U[e,i]) in f16; x is xp16 [S_rows, D] f16.
-// G, U rows `pitch` bytes apart (a multiple of 16).
+// G, U rows `pitch` bytes apart (a multiple of 16).  warp_mma selects the
+// mma.sync schedule (bn 8 or 16; x and h in wm_kpos order), else tcgen05
+// (bn 16..256; tc_kpos order).
 // tile_base: scratch of E+1 ints.  *err receives a nonzero code if a wait timed out.
 cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pitch, int64_t E, int64_t I, int64_t D,
                                const void* xp16, int64_t S_rows, const int32_t* counts,
                                const int32_t* offsets, int32_t* tile_base, int bn, void* h16, int* err,
-                               cudaStream_t st);
+                               cudaStream_t st, bool warp_mma = false);
 // out[split][slot, o] = partial of h16[slot] . Dn[e, o] over the split's K range (f32).
 cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
                              int64_t S_rows, const int32_t* counts, const int32_t* offsets,
-                             int32_t* tile_base, int bn, int splits, float* out, int* err, cudaStream_t st);
+                             int32_t* tile_base, int bn, int splits, float* out, int* err, cudaStream_t st,
+                             bool warp_mma = false);
 // Copies `rows` packed rows of row_bytes (even) from src (src_pitch apart) to dst
 // (dst_pitch apart, a multiple of 16), zero-filling each row's padding.
 cudaError_t launch_pad_rows(const void* src, int64_t src_pitch, int64_t rows, int64_t row_bytes, void* dst,

@@ -14,6 +14,7 @@
 #include <cuda_fp16.h>
 
 #include "kernels.hpp"
+#include "operand_order.cuh"
 
 namespace uaii_b200 {
 namespace {
@@ -124,7 +125,7 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int64_t T, int k, Rout
 // Offsets by a block-wide exclusive scan of counts; then one warp per (t, r).
 __global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int64_t D,
                                     int64_t E, int k, RouteBuffers rb, float* xp32,
-                                    __half* xp16) {
+                                    __half* xp16, bool wm_order) {
   extern __shared__ int offs[];  // [E+1]
   if (threadIdx.x == 0) {
     int run = 0;
@@ -146,7 +147,7 @@ __global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int6
       for (int64_t i = lane; i < D; i += 32) {
         const float v = x[t * D + i];
         if (xp32) xp32[(int64_t)slot * D + i] = v;
-        if (xp16) xp16[(int64_t)slot * D + ((i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1))] = __float2half_rn(v);
+        if (xp16) xp16[(int64_t)slot * D + tc_kpos(i)] = __float2half_rn(v);  // D % 128 != 0: never wm_order
       }
       continue;
     }
@@ -154,10 +155,11 @@ __global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int6
     for (int64_t i = lane; i < D / 4; i += 32) {
       const float4 v = src[i];
       if (xp32) reinterpret_cast<float4*>(xp32 + (int64_t)slot * D)[i] = v;
-      if (xp16) {  // tensor-core operand order: [0, 2, 1, 3] inside each group of four
-        __half2* d2 = reinterpret_cast<__half2*>(xp16 + (int64_t)slot * D) + 2 * i;
-        d2[0] = __floats2half2_rn(v.x, v.z);
-        d2[1] = __floats2half2_rn(v.y, v.w);
+      if (xp16) {  // elements (4i, 4i+2) and (4i+1, 4i+3) land on adjacent pairs in both orders
+        __half* row = xp16 + (int64_t)slot * D;
+        const int64_t p0 = wm_order ? wm_kpos(4 * i) : 4 * i, p1 = wm_order ? p0 + 8 : p0 + 2;
+        *reinterpret_cast<__half2*>(row + p0) = __floats2half2_rn(v.x, v.z);
+        *reinterpret_cast<__half2*>(row + p1) = __floats2half2_rn(v.y, v.w);
       }
     }
   }
@@ -228,11 +230,11 @@ __global__ void combine1_kernel(const float* __restrict__ out, int64_t ld, int s
   y[i] = acc;
 }
 
-// f16 copy in the tensor-core operand order ([0, 2, 1, 3] inside each group of
-// four consecutive elements; n is a multiple of 4)
-__global__ void to_f16_kernel(const float* __restrict__ x, int64_t n, __half* __restrict__ o) {
+// f16 copy in an operand K order (tc_kpos: n % 4 == 0; wm_kpos: the row width
+// and n are multiples of 128, so the order restarts with every row)
+__global__ void to_f16_kernel(const float* __restrict__ x, int64_t n, __half* __restrict__ o, bool wm_order) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i < n) o[(i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1)] = __float2half_rn(x[i]);
+  if (i < n) o[wm_order ? wm_kpos(i) : tc_kpos(i)] = __float2half_rn(x[i]);
 }
 
 // gate[t] = 1 / (1 + exp(-(x[t] . w))), one warp per token.
@@ -281,13 +283,14 @@ cudaError_t launch_route_scan(int64_t T, int64_t E, int k, const RouteBuffers& r
 
 cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E, int k,
                                 const RouteBuffers& rb, float* xp_f32, void* xp_f16,
-                                cudaStream_t st) {
+                                cudaStream_t st, bool wm_order) {
+  if (wm_order && D % 128 != 0) return cudaErrorInvalidValue;
   int64_t blocks = (T * k + 7) / 8;
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
   const size_t smem = sizeof(int) * (size_t)(E + 1);
   route_gather_kernel<<<(unsigned)blocks, 256, smem, st>>>(x, T, D, E, k, rb, xp_f32,
-                                                           static_cast<__half*>(xp_f16));
+                                                           static_cast<__half*>(xp_f16), wm_order);
   return cudaGetLastError();
 }
 
@@ -311,9 +314,10 @@ cudaError_t launch_combine(const float* out, int64_t out_ld, int splits, int64_t
   return cudaGetLastError();
 }
 
-cudaError_t launch_to_f16(const float* x, int64_t n, void* out, cudaStream_t st) {
+cudaError_t launch_to_f16(const float* x, int64_t n, void* out, cudaStream_t st, bool wm_order) {
   if (n == 0) return cudaSuccess;
-  to_f16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, n, static_cast<__half*>(out));
+  if (wm_order && n % 128 != 0) return cudaErrorInvalidValue;
+  to_f16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, n, static_cast<__half*>(out), wm_order);
   return cudaGetLastError();
 }
 

@@ -191,10 +191,12 @@ class Backend:
 
     def last_plan(self) -> dict:
         """Schedule of the most recent expert-product call: tensor cores or not,
-        slot tile width and down-projection K splits."""
+        which tensor-core schedule ("tcgen05", "warp_mma" or None), slot tile
+        width and down-projection K splits."""
         tc, bn, sp = c_int(), c_int(), c_int()
         _check(lib.uaii_moe_last_plan(self._h, byref(tc), byref(bn), byref(sp)))
-        return {"tensor_cores": bool(tc.value), "slot_tile": bn.value, "down_splits": sp.value}
+        sched = {1: "tcgen05", 2: "warp_mma"}.get(tc.value)
+        return {"tensor_cores": bool(tc.value), "schedule": sched, "slot_tile": bn.value, "down_splits": sp.value}
 
     PHASES = ("router", "route", "gateup", "down", "shared", "combine")
 
@@ -213,11 +215,14 @@ class Backend:
     def handle(self):
         return self._h
 
-    def register_weights(self, host_array):
-        _check(lib.uaii_moe_register_weights(self._h, ptr(host_array), host_array.nbytes))
+    def register_weights(self, array):
+        """Declare a weight buffer constant until release_weights(): a host buffer is
+        uploaded once; for host and device buffers alike, layouts derived from the
+        weights (padded rows) are made once and kept."""
+        _check(lib.uaii_moe_register_weights(self._h, ptr(array), array.nbytes))
 
-    def release_weights(self, host_array):
-        _check(lib.uaii_moe_release_weights(self._h, ptr(host_array)))
+    def release_weights(self, array):
+        _check(lib.uaii_moe_release_weights(self._h, ptr(array)))
 
     def dequant_rows(self, fmt: int, packed, rows: int, cols: int, out):
         _check(lib.uaii_moe_dequant_rows(self._h, fmt, ptr(packed), rows, cols, ptr(out)))
