@@ -60,13 +60,10 @@ __device__ void adjust_heap(Pair* h, int hole, int len, Pair v) {
   push_heap(h, hole, top, v);
 }
 
-// One thread per token.  k <= 32.
-__global__ void route_topk_kernel(const float* __restrict__ scores, const float* __restrict__ probs,
-                                  int64_t T, int64_t E, int k, int norm_topk, RouteBuffers rb) {
-  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (t >= T) return;
-  const float* row = scores + t * E;
-  Pair h[32];
+// The reference procedure for one token, serially: a heap over the first k
+// pairs, each later pair replacing the root only when strictly greater, then a
+// heap sort.  Writes the k ranked pairs to h.
+__device__ void topk_heap(const float* __restrict__ row, int64_t E, int k, Pair* h) {
   for (int i = 0; i < k; ++i) h[i] = Pair{row[i], i};
   if (k >= 2)
     for (int parent = (k - 2) / 2;; --parent) {
@@ -83,15 +80,60 @@ __global__ void route_topk_kernel(const float* __restrict__ scores, const float*
     h[last] = h[0];
     adjust_heap(h, 0, last, v);
   }
-  float ps[32];
-  for (int r = 0; r < k; ++r) ps[r] = (probs == scores) ? h[r].p : probs[t * E + h[r].e];
-  float mass = 0.0f;
-  for (int r = 0; r < k; ++r) mass = __fadd_rn(mass, ps[r]);
-  if (!(mass > 0.0f)) mass = 1.0f;
-  for (int r = 0; r < k; ++r) {
-    rb.topk_ids[t * k + r] = h[r].e;
-    rb.topk_w[t * k + r] = norm_topk ? __fdiv_rn(ps[r], mass) : ps[r];
-    rb.mask[(int64_t)h[r].e * T + t] = (uint8_t)(r + 1);
+}
+
+// One warp per token, k <= 32, E <= 1024.  The warp extracts the k + 1 largest
+// scores one at a time (warp arg-max rounds).  When those values are all
+// distinct the reference's result is fixed -- the k largest in descending
+// order -- and the rounds give it; any tie among them (selection or order then
+// depend on the heap procedure) hands the token to lane 0, which runs the
+// reference procedure itself.
+__global__ void route_topk_kernel(const float* __restrict__ scores, const float* __restrict__ probs,
+                                  int64_t T, int64_t E, int k, int norm_topk, RouteBuffers rb) {
+  __shared__ Pair sel[8][33];
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  Pair* h = sel[wib];
+  const int rounds = k < E ? k + 1 : k;
+  for (int64_t t = blockIdx.x * 8 + wib; t < T; t += (int64_t)gridDim.x * 8) {
+    const float* row = scores + t * E;
+    uint32_t taken = 0;  // bit j: element lane + 32j already extracted
+    bool tie = false;
+    for (int r = 0; r < rounds; ++r) {
+      float bv = 0.0f;
+      int be = -1;
+      for (int64_t e = lane, j = 0; e < E; e += 32, ++j) {
+        const float v = row[e];
+        if (!((taken >> j) & 1u) && (be < 0 || v > bv)) { bv = v; be = (int)e; }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {  // larger value wins; equal values: smaller index
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+        if (oe >= 0 && (be < 0 || ov > bv || (ov == bv && oe < be))) { bv = ov; be = oe; }
+      }
+      if ((be & 31) == lane) taken |= 1u << (be >> 5);
+      if (r > 0 && !(h[r - 1].p != bv)) tie = true;  // equal (or unordered) neighbours
+      __syncwarp();
+      if (lane == 0) h[r] = Pair{bv, be};
+      __syncwarp();
+    }
+    if (tie) {
+      if (lane == 0) topk_heap(row, E, k, h);
+      __syncwarp();
+    }
+    if (lane == 0) {
+      float ps[32];
+      for (int r = 0; r < k; ++r) ps[r] = (probs == scores) ? h[r].p : probs[t * E + h[r].e];
+      float mass = 0.0f;
+      for (int r = 0; r < k; ++r) mass = __fadd_rn(mass, ps[r]);
+      if (!(mass > 0.0f)) mass = 1.0f;
+      for (int r = 0; r < k; ++r) {
+        rb.topk_ids[t * k + r] = h[r].e;
+        rb.topk_w[t * k + r] = norm_topk ? __fdiv_rn(ps[r], mass) : ps[r];
+        rb.mask[(int64_t)h[r].e * T + t] = (uint8_t)(r + 1);
+      }
+    }
+    __syncwarp();
   }
 }
 
@@ -269,8 +311,9 @@ cudaError_t launch_route_topk(const float* scores, const float* probs, int64_t T
   if (E > 1024 || k < 1 || k > 32 || k > E) return cudaErrorInvalidValue;
   cudaError_t err = cudaMemsetAsync(rb.mask, 0, (size_t)(E * T), st);
   if (err != cudaSuccess) return err;
-  route_topk_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(scores, probs, T, E, k, norm_topk,
-                                                                 rb);
+  int64_t blocks = (T + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  route_topk_kernel<<<(unsigned)blocks, 256, 0, st>>>(scores, probs, T, E, k, norm_topk, rb);
   return cudaGetLastError();
 }
 

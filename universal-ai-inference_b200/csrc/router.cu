@@ -360,29 +360,49 @@ __global__ void __launch_bounds__(256) router_tiled_kernel(const float* __restri
   }
 }
 
+// One warp per token (8 per block).  The maximum and the final scaling are
+// order-free and run across the lanes; the exponentials too.  The sum keeps the
+// reference's order (index 0 up, one rounding per add), so one lane adds the
+// warp's staged exponentials in sequence.  `top` = first index of the largest
+// probability.
 __global__ void softmax_top_kernel(const float* __restrict__ logits, int64_t T, int64_t E,
                                    float* __restrict__ probs, float* __restrict__ top) {
-  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (t >= T) return;
-  const float* l = logits + t * E;
-  float* p = probs + t * E;
-  float mx = -__int_as_float(0x7f800000);
-  for (int64_t e = 0; e < E; ++e) mx = (mx < l[e]) ? l[e] : mx;
-  float sum = 0.0f;
-  for (int64_t e = 0; e < E; ++e) {
-    const float v = (float)exp((double)__fsub_rn(l[e], mx));
-    p[e] = v;
-    sum = __fadd_rn(sum, v);
+  extern __shared__ float sv_all[];  // [8][E]
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  float* sv = sv_all + (int64_t)wib * E;
+  for (int64_t t = blockIdx.x * 8 + wib; t < T; t += (int64_t)gridDim.x * 8) {
+    const float* l = logits + t * E;
+    float* p = probs + t * E;
+    float mx = -__int_as_float(0x7f800000);
+    for (int64_t e = lane; e < E; e += 32) mx = (mx < l[e]) ? l[e] : mx;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, mx, o);
+      mx = (mx < m2) ? m2 : mx;
+    }
+    for (int64_t e = lane; e < E; e += 32) sv[e] = (float)exp((double)__fsub_rn(l[e], mx));
+    __syncwarp();
+    float sum = 0.0f;
+    if (lane == 0)
+      for (int64_t e = 0; e < E; ++e) sum = __fadd_rn(sum, sv[e]);
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    const float inv = (sum > 0.0f) ? __fdiv_rn(1.0f, sum) : 0.0f;
+    float bp = 0.0f;
+    int best = -1;
+    for (int64_t e = lane; e < E; e += 32) {
+      const float v = __fmul_rn(sv[e], inv);
+      p[e] = v;
+      if (best < 0 || v > bp) { bp = v; best = (int)e; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {  // larger value wins; equal values: smaller index
+      const float ov = __shfl_xor_sync(0xffffffffu, bp, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, best, o);
+      if (oe >= 0 && (best < 0 || ov > bp || (ov == bp && oe < best))) { bp = ov; best = oe; }
+    }
+    if (top && lane == 0) top[t] = (float)best;
+    __syncwarp();  // sv is rewritten for the next token
   }
-  const float inv = (sum > 0.0f) ? __fdiv_rn(1.0f, sum) : 0.0f;
-  int best = 0;
-  float bp = 0.0f;
-  for (int64_t e = 0; e < E; ++e) {
-    const float v = __fmul_rn(p[e], inv);
-    p[e] = v;
-    if (e == 0 || v > bp) { bp = v; best = (int)e; }
-  }
-  if (top) top[t] = (float)best;
 }
 
 }  // namespace
@@ -460,7 +480,14 @@ cudaError_t launch_router(const float* x, const float* w, int64_t T, int64_t D, 
   }
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess || probs == nullptr) return err;
-  softmax_top_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(logits, T, E, probs, top);
+  int64_t blocks = (T + 7) / 8;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  const size_t smem = sizeof(float) * 8 * (size_t)E;
+  if (smem > 48 * 1024) {
+    err = cudaFuncSetAttribute(softmax_top_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return err;
+  }
+  softmax_top_kernel<<<(unsigned)blocks, 256, smem, st>>>(logits, T, E, probs, top);
   return cudaGetLastError();
 }
 
