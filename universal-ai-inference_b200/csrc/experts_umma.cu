@@ -292,6 +292,13 @@ struct Tile {
   int e, m_tile, n_tile, split;
 };
 
+// Tile order inside an expert: K splits fastest, then bands of kBandM weight-row
+// tiles -- the row tiles of a band fastest, then the slot tiles.  The tiles in
+// flight at once (one per SM) then share kBandM weight tiles and about
+// SMs / kBandM activation tiles, so an expert with many slot tiles re-reads
+// neither its weights nor its activations once per wave from HBM.
+constexpr int kBandM = 32;
+
 __device__ __forceinline__ Tile decode_tile(const Args& a, int tile, int bn) {
   int lo = 0, hi = a.E;  // largest e with tile_base[e] <= tile (always a non-empty expert)
   while (hi - lo > 1) {
@@ -304,8 +311,12 @@ __device__ __forceinline__ Tile decode_tile(const Args& a, int tile, int bn) {
   t.split = local % a.splits;
   local /= a.splits;
   const int nt = (__ldg(a.counts + lo) + bn - 1) / bn;
-  t.n_tile = local % nt;
-  t.m_tile = local / nt;
+  const int band = local / (kBandM * nt);
+  const int m0 = band * kBandM;
+  const int bm = min(kBandM, a.m_tiles - m0);  // the last band may be narrower
+  const int r = local - band * kBandM * nt;
+  t.n_tile = r / bm;
+  t.m_tile = m0 + r % bm;
   return t;
 }
 
