@@ -65,6 +65,8 @@ def parse():
                     help="weak: --tokens per GPU; strong: --tokens in total, split across the GPUs")
     ap.add_argument("--path", type=int, default=0,
                     help="0 auto, 1 CUDA-core GEMV, 2 tcgen05 tensor-core GEMM, 3 warp-MMA tensor-core GEMM")
+    ap.add_argument("--ep-chunks", type=int, default=1,
+                    help="N > 1: token chunks whose exchanges overlap the previous chunk's experts")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -273,7 +275,8 @@ def main():
                 be.register_weights(t)
 
     if ep_mode:
-        ep = ExpertParallelFFN(be, router_layer, local_layer, cfg.D, cfg.E, cfg.top_k, rank, world)
+        ep = ExpertParallelFFN(be, router_layer, local_layer, cfg.D, cfg.E, cfg.top_k, rank, world,
+                               chunks=args.ep_chunks)
 
         def forward(xin, yout, pr=None):
             with torch.cuda.stream(stream):  # collectives order against the backend's stream

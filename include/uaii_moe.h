@@ -153,6 +153,12 @@ UAII_MOE_API int uaii_moe_backend_create(int device, void* stream, uaii_moe_back
  * Replaces CudaBackend::shutdown (cuda_backend.cpp:68-78). */
 UAII_MOE_API void uaii_moe_backend_destroy(uaii_moe_backend* b);
 
+/* The CUDA stream (cudaStream_t) this backend queues its work on: the one given
+ * to uaii_moe_backend_create, or the backend's own non-blocking stream when that
+ * was NULL.  Callers that order other work against the backend's (collectives,
+ * copies) use this stream.  No reference counterpart. */
+UAII_MOE_API int uaii_moe_backend_stream(uaii_moe_backend* b, void** stream);
+
 /* Wait for all work queued by this backend.  Replaces IBackend::synchronize
  * (include/uaii/interfaces/backend.hpp:74) / native::cuda_synchronize. */
 UAII_MOE_API int uaii_moe_synchronize(uaii_moe_backend* b);
@@ -277,6 +283,18 @@ UAII_MOE_API int uaii_moe_ep_dispatch(uaii_moe_backend* b, const uaii_moe_layer*
 UAII_MOE_API int uaii_moe_ep_experts(uaii_moe_backend* b, const uaii_moe_layer* layer, const void* recv_x16,
                                      const int32_t* recv_ids, const float* recv_w, int64_t rows, int64_t entries,
                                      float* y_part);
+
+/* Steps 1 and 2 with each exchanged row as ONE record, so that a single
+ * all-to-all moves rows, ids and weights: record = f16 x [d_model] (operand
+ * order as above), then top_k int32 ids, then top_k f32 weights, rec_bytes
+ * apart (a multiple of 16, >= 2*d_model + 8*top_k; d_model a multiple of 8).
+ * Same outputs and semantics as uaii_moe_ep_dispatch / uaii_moe_ep_experts. */
+UAII_MOE_API int uaii_moe_ep_dispatch_records(uaii_moe_backend* b, const uaii_moe_layer* layer, const float* x,
+                                              int64_t T, int rank, int world, void* send_rec, int64_t rec_bytes,
+                                              int32_t* send_token, int32_t* row_of, int32_t* send_counts,
+                                              int32_t* send_entries, float* probs);
+UAII_MOE_API int uaii_moe_ep_experts_records(uaii_moe_backend* b, const uaii_moe_layer* layer, const void* recv_rec,
+                                             int64_t rec_bytes, int64_t rows, int64_t entries, float* y_part);
 
 /* Step 3, on each rank after the reverse exchange (y_back [rows, d_model] f32 in
  * its own send-row order): y[t] = sum over ranks d = 0..world-1 of

@@ -97,6 +97,21 @@ class FakeEpBackend:
                 acc = acc + np.float32(recv_w[i, r]) * ye[0]
             y_part[i] = torch.from_numpy(acc.astype(np.float32))
 
+    @staticmethod
+    def _fields(rec, D, k):  # views of the record columns (same layout as the C ABI)
+        return (rec[:, :2 * D].view(torch.float16), rec[:, 2 * D:2 * D + 4 * k].view(torch.int32),
+                rec[:, 2 * D + 4 * k:2 * D + 8 * k].view(torch.float32))
+
+    def ep_dispatch_records(self, layer, x, T, rank, world, send_rec, rec_bytes, send_token, row_of, send_counts,
+                            send_entries, probs=None):
+        assert rec_bytes == send_rec.shape[1] and rec_bytes % 16 == 0
+        x16, ids, w = self._fields(send_rec, x.shape[1], self.k)
+        self.ep_dispatch(layer, x, T, rank, world, x16, ids, w, send_token, row_of, send_counts, send_entries, probs)
+
+    def ep_experts_records(self, layer, recv_rec, rec_bytes, rows, entries, y_part):
+        x16, ids, w = self._fields(recv_rec, y_part.shape[1], self.k)
+        self.ep_experts(layer, x16, ids, w, rows, entries, y_part)
+
     def ep_combine(self, y_back, row_of, T, world, D, y):
         for t in range(T):
             acc = torch.zeros(D, dtype=torch.float32)

@@ -43,7 +43,7 @@ def _dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-def _emulated(um, backend, D, E, I, k, gf, df, R, T, seed):
+def _emulated(um, backend, D, E, I, k, gf, df, R, T, seed, records=False):
     w, G, U, Dn = _layer(um, D, E, I, k, gf, df, seed)
     wd, Gd, Ud, Dd = (_dev(a) for a in (w, G, U, Dn))
     full = um.make_layer(D, E, I, k, 1, wd, Gd, gf, Ud, gf, Dd, df)
@@ -66,8 +66,15 @@ def _emulated(um, backend, D, E, I, k, gf, df, R, T, seed):
                  row_of=torch.empty((T, R), dtype=torch.int32, device="cuda"),
                  counts=torch.empty((R,), dtype=torch.int32, device="cuda"),
                  entries=torch.empty((R,), dtype=torch.int32, device="cuda"))
-        backend.ep_dispatch(full, xs[r], T, r, R, b["x16"], b["ids"], b["w"], b["tok"], b["row_of"], b["counts"],
-                            b["entries"])
+        if records:  # one record per row: f16 x, k int32 ids, k f32 weights (padded to 16 bytes)
+            rb = (2 * D + 8 * k + 15) // 16 * 16
+            rec = torch.empty((cap, rb), dtype=torch.uint8, device="cuda")
+            backend.ep_dispatch_records(full, xs[r], T, r, R, rec, rb, b["tok"], b["row_of"], b["counts"],
+                                        b["entries"])
+            b["rec"] = rec
+        else:
+            backend.ep_dispatch(full, xs[r], T, r, R, b["x16"], b["ids"], b["w"], b["tok"], b["row_of"],
+                                b["counts"], b["entries"])
         send.append(b)
     torch.cuda.synchronize()
     counts = [s["counts"].cpu().tolist() for s in send]  # counts[src][dst]
@@ -75,15 +82,23 @@ def _emulated(um, backend, D, E, I, k, gf, df, R, T, seed):
     # exchange: rank d receives, from every source s in order, the rows s sent to d
     y_parts = []
     for d in range(R):
-        rx = torch.cat([send[s]["x16"][offs[s][d]:offs[s][d + 1]] for s in range(R)])
-        ri = torch.cat([send[s]["ids"][offs[s][d]:offs[s][d + 1]] for s in range(R)])
-        rw = torch.cat([send[s]["w"][offs[s][d]:offs[s][d + 1]] for s in range(R)])
         entries = int(sum(send[s]["entries"][d].item() for s in range(R)))
+        if records:
+            rr = torch.cat([send[s]["rec"][offs[s][d]:offs[s][d + 1]] for s in range(R)])
+            ri = rr[:, 2 * D:2 * D + 4 * k].contiguous().view(torch.int32)
+            n = rr.shape[0]
+        else:
+            rx = torch.cat([send[s]["x16"][offs[s][d]:offs[s][d + 1]] for s in range(R)])
+            ri = torch.cat([send[s]["ids"][offs[s][d]:offs[s][d + 1]] for s in range(R)])
+            rw = torch.cat([send[s]["w"][offs[s][d]:offs[s][d + 1]] for s in range(R)])
+            n = rx.shape[0]
         assert entries == int((ri >= 0).sum().item())
-        yp = torch.empty((max(rx.shape[0], 1), D), dtype=torch.float32, device="cuda")
-        if rx.shape[0]:
-            backend.ep_experts(shards[d][3], rx, ri, rw, rx.shape[0], entries, yp)
-        y_parts.append(yp[:rx.shape[0]])
+        yp = torch.empty((max(n, 1), D), dtype=torch.float32, device="cuda")
+        if n and records:
+            backend.ep_experts_records(shards[d][3], rr, rr.shape[1], n, entries, yp)
+        elif n:
+            backend.ep_experts(shards[d][3], rx, ri, rw, n, entries, yp)
+        y_parts.append(yp[:n])
     # reverse exchange and combine on every source rank
     out = []
     for s in range(R):
@@ -104,12 +119,22 @@ def _emulated(um, backend, D, E, I, k, gf, df, R, T, seed):
         err = np.abs(a - b).max() / max(np.abs(b).max(), 1e-30)
         assert err <= REL_TOL, (r, err)
         assert err <= 1e-4, (r, err)  # only the per-rank regrouping of the top-k sum differs
+    return [o.cpu() for o in out]
 
 
 @pytest.mark.parametrize("R", [2, 4])
 def test_ep_emulated_ranks_mixtral_formats(um, backend, R):
     _need_gpu()
     _emulated(um, backend, D=512, E=8, I=2048, k=2, gf=um.Q4_K, df=um.Q6_K, R=R, T=48, seed=3)  # 16-byte Q6_K pitch
+
+
+def test_ep_records_match_separate_buffers(um, backend):
+    # one record per exchanged row (x, ids, weights) gives the same bits as three buffers
+    _need_gpu()
+    a = _emulated(um, backend, D=512, E=8, I=2048, k=3, gf=um.Q4_K, df=um.Q6_K, R=4, T=40, seed=5)
+    b = _emulated(um, backend, D=512, E=8, I=2048, k=3, gf=um.Q4_K, df=um.Q6_K, R=4, T=40, seed=5, records=True)
+    for x, y in zip(a, b):
+        assert torch.equal(x.view(torch.int32), y.view(torch.int32))
 
 
 def test_ep_emulated_ranks_qwen3_formats(um, backend):
@@ -155,11 +180,12 @@ def _nccl_worker(rank, world, port, q):
         g = Gd.view(E, I, -1)[rank * epr:(rank + 1) * epr].contiguous()
         u = Ud.view(E, I, -1)[rank * epr:(rank + 1) * epr].contiguous()
         d = Dd.view(E, D, -1)[rank * epr:(rank + 1) * epr].contiguous()
-        be = um.Backend(rank, torch.cuda.current_stream().cuda_stream)
+        be = um.Backend(rank, torch.cuda.Stream().cuda_stream)  # ExpertParallelFFN orders its collectives on it
         full = um.make_layer(D, E, I, k, 1, wd, Gd, um.Q4_K, Ud, um.Q4_K, Dd, um.Q6_K)
         local = um.make_layer(D, epr, I, k, 1, wd, g, um.Q4_K, u, um.Q4_K, d, um.Q6_K)
         x = _dev(um.fill_normal((T, D), 50 + rank, 1))
         y = torch.empty((T, D), device="cuda")
+        torch.cuda.synchronize()  # inputs written on the default stream
         ExpertParallelFFN(be, full, local, D, E, k, rank, world).forward(x, y)
         y_ref = torch.empty((T, D), device="cuda")
         be.ffn(full, x, T, y_ref)

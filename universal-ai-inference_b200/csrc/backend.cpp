@@ -562,7 +562,7 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
   int splits = 1;
   phase_begin(kRoute);
   if (ep) {
-    UAII_CUDA(launch_ep_route(ep->ids, ep->w, T, E, k, rb, stream_), "ep_route");
+    UAII_CUDA(launch_ep_route(ep->ids, ep->w, T, E, k, rb, stream_, ep->e_pitch), "ep_route");
   } else {
     UAII_CUDA(launch_route_topk(scores, probs_for_w, T, E, k, L.norm_topk, rb, stream_), "route_topk");
   }
@@ -574,7 +574,7 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
     out = static_cast<float*>(carve(sizeof(float) * (size_t)(splits * S * D)));
     if (ep) {  // rows arrive in the tcgen05 operand order
       if (P.warp_mma) return Error::make(ErrorCode::Internal, "expert-parallel rows planned on the warp-MMA schedule");
-      UAII_CUDA(launch_route_gather16(ep->x16, T, D, E, k, rb, xp16, stream_), "route_gather16");
+      UAII_CUDA(launch_route_gather16(ep->x16, T, D, E, k, rb, xp16, stream_, ep->x_pitch), "route_gather16");
     } else {
       UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, nullptr, xp16, stream_, P.warp_mma), "route_gather");
     }
@@ -746,7 +746,8 @@ size_t MoeCudaBackend::experts_ws(const LayerArgs& L, int64_t T, const ExpertPla
 
 Error MoeCudaBackend::ep_dispatch(const LayerArgs& L, const float* x, int64_t T, int rank, int world,
                                   void* send_x16, int32_t* send_ids, float* send_w, int32_t* send_token,
-                                  int32_t* row_of, int32_t* send_counts, int32_t* send_entries, float* probs) {
+                                  int32_t* row_of, int32_t* send_counts, int32_t* send_entries, float* probs,
+                                  int64_t x_pitch, int64_t e_pitch) {
   std::lock_guard<std::mutex> lk(mu_);
   UAII_CUDA(cudaSetDevice(device_), "SetDevice");
   const int64_t D = L.D, E = L.E;
@@ -785,7 +786,7 @@ Error MoeCudaBackend::ep_dispatch(const LayerArgs& L, const float* x, int64_t T,
   UAII_CUDA(launch_route_topk(logits, po, T, E, k, L.norm_topk, rb, stream_), "route_topk");
   UAII_CUDA(launch_ep_plan(rb.topk_ids, T, k, world, epr, dmask, rowpos, dcounts, stream_), "ep_plan");
   UAII_CUDA(launch_ep_pack(x, T, D, k, world, epr, rb.topk_ids, rb.topk_w, dmask, rowpos, dcounts, send_x16, send_ids,
-                           send_w, send_token, row_of, send_counts, send_entries, stream_),
+                           send_w, send_token, row_of, send_counts, send_entries, stream_, x_pitch, e_pitch),
             "ep_pack");
   phase_end();
   count_launches(7);
@@ -794,7 +795,8 @@ Error MoeCudaBackend::ep_dispatch(const LayerArgs& L, const float* x, int64_t T,
 }
 
 Error MoeCudaBackend::ep_experts(const LayerArgs& Lin, const void* recv_x16, const int32_t* recv_ids,
-                                 const float* recv_w, int64_t N, int64_t entries, float* y_part) {
+                                 const float* recv_w, int64_t N, int64_t entries, float* y_part, int64_t x_pitch,
+                                 int64_t e_pitch) {
   std::lock_guard<std::mutex> lk(mu_);
   UAII_CUDA(cudaSetDevice(device_), "SetDevice");
   LayerArgs L = Lin;
@@ -810,7 +812,7 @@ Error MoeCudaBackend::ep_experts(const LayerArgs& Lin, const void* recv_x16, con
     if (!is_device_ptr(p)) return Error::make(ErrorCode::InvalidArgument, "ep experts: arguments must be device memory");
   const ExpertPlan P = plan_experts(L, N, entries, /*allow_warp_mma=*/false);
   UAII_TRY(reserve(experts_ws(L, N, P) + layer_stage_bytes(L)));
-  const EpRows rows{recv_x16, recv_ids, recv_w};
+  const EpRows rows{recv_x16, recv_ids, recv_w, x_pitch, e_pitch};
   return run_experts(nullptr, nullptr, nullptr, L, P, N, y_part, &rows);
 }
 
@@ -1147,6 +1149,13 @@ int uaii_moe_backend_create(int device, void* stream, uaii_moe_backend** out) {
 
 void uaii_moe_backend_destroy(uaii_moe_backend* b) { delete b; }
 
+int uaii_moe_backend_stream(uaii_moe_backend* b, void** stream) {
+  if (!b) return no_backend();
+  if (!stream) return report(Error::make(ErrorCode::InvalidArgument, "null stream pointer"));
+  *stream = static_cast<void*>(b->impl.stream());
+  return report(Error::success());
+}
+
 int uaii_moe_synchronize(uaii_moe_backend* b) {
   if (!b) return no_backend();
   return report(b->impl.synchronize());
@@ -1248,6 +1257,55 @@ int uaii_moe_ep_dispatch(uaii_moe_backend* b, const uaii_moe_layer* l, const flo
   L.router_w = l->router_w;
   return report(b->impl.ep_dispatch(L, x, T, rank, world, send_x16, send_ids, send_w, send_token, row_of,
                                     send_counts, send_entries, probs));
+}
+
+namespace {
+// Record of one exchanged row: f16 x (d_model), then top_k int32 ids, then top_k f32 weights.
+Error record_layout(int64_t D, int k, int64_t rec_bytes) {
+  if (D <= 0 || k < 1 || rec_bytes % 16 != 0 || rec_bytes < 2 * D + 8 * (int64_t)k || (2 * D) % 16 != 0)
+    return Error::make(ErrorCode::InvalidArgument,
+                       "ep records: rec_bytes must be a multiple of 16 and hold 2*d_model + 8*top_k bytes "
+                       "(d_model a multiple of 8)");
+  return Error::success();
+}
+}  // namespace
+
+int uaii_moe_ep_dispatch_records(uaii_moe_backend* b, const uaii_moe_layer* l, const float* x, int64_t T, int rank,
+                                 int world, void* send_rec, int64_t rec_bytes, int32_t* send_token, int32_t* row_of,
+                                 int32_t* send_counts, int32_t* send_entries, float* probs) {
+  if (!b) return no_backend();
+  if (!l) return report(Error::make(ErrorCode::InvalidArgument, "null layer"));
+  {
+    const Error le = record_layout(l->d_model, (int)l->top_k, rec_bytes);
+    if (!le.ok()) return report(le);
+  }
+  LayerArgs L{};
+  L.D = l->d_model;
+  L.E = l->n_experts;
+  L.top_k = l->top_k;
+  L.norm_topk = l->norm_topk;
+  L.router_w = l->router_w;
+  char* r = static_cast<char*>(send_rec);
+  return report(b->impl.ep_dispatch(L, x, T, rank, world, r, reinterpret_cast<int32_t*>(r + 2 * L.D),
+                                    reinterpret_cast<float*>(r + 2 * L.D + 4 * L.top_k), send_token, row_of,
+                                    send_counts, send_entries, probs, rec_bytes / 2, rec_bytes / 4));
+}
+
+int uaii_moe_ep_experts_records(uaii_moe_backend* b, const uaii_moe_layer* l, const void* recv_rec, int64_t rec_bytes,
+                                int64_t rows, int64_t entries, float* y_part) {
+  if (!b) return no_backend();
+  if (!l) return report(Error::make(ErrorCode::InvalidArgument, "null layer"));
+  {
+    const Error le = record_layout(l->d_model, (int)l->top_k, rec_bytes);
+    if (!le.ok()) return report(le);
+  }
+  LayerArgs L;
+  if (!layer_args_from_c(l, &L))
+    return report(Error::make(ErrorCode::InvalidArgument, "ep experts: null expert weights"));
+  const char* r = static_cast<const char*>(recv_rec);
+  return report(b->impl.ep_experts(L, r, reinterpret_cast<const int32_t*>(r + 2 * L.D),
+                                   reinterpret_cast<const float*>(r + 2 * L.D + 4 * L.top_k), rows, entries, y_part,
+                                   rec_bytes / 2, rec_bytes / 4));
 }
 
 int uaii_moe_ep_experts(uaii_moe_backend* b, const uaii_moe_layer* l, const void* recv_x16, const int32_t* recv_ids,

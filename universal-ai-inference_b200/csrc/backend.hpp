@@ -117,11 +117,12 @@ class MoeCudaBackend {
   Error ffn(const LayerArgs& L, const float* x, int64_t T, float* y, float* probs);
 
   // Expert parallelism (device pointers only).  See include/uaii_moe.h.
+  // x_pitch (f16 elements) / e_pitch (entries) between rows; 0 = dense.
   Error ep_dispatch(const LayerArgs& L, const float* x, int64_t T, int rank, int world, void* send_x16,
                     int32_t* send_ids, float* send_w, int32_t* send_token, int32_t* row_of, int32_t* send_counts,
-                    int32_t* send_entries, float* probs);
+                    int32_t* send_entries, float* probs, int64_t x_pitch = 0, int64_t e_pitch = 0);
   Error ep_experts(const LayerArgs& L_local, const void* recv_x16, const int32_t* recv_ids, const float* recv_w,
-                   int64_t rows, int64_t entries, float* y_part);
+                   int64_t rows, int64_t entries, float* y_part, int64_t x_pitch = 0, int64_t e_pitch = 0);
   Error ep_combine(const float* y_back, const int32_t* row_of, int64_t T, int world, int64_t D, float* y);
   // Runs the bounded-wait self-test kernel and returns the status the host observes.
   Error selftest_wait_timeout(int64_t budget_cycles);
@@ -157,6 +158,7 @@ class MoeCudaBackend {
     const void* x16;
     const int32_t* ids;
     const float* w;
+    int64_t x_pitch, e_pitch;  // 0 = dense
   };
   Error run_experts(const float* x_dev, const float* scores, const float* probs_for_w,
                     const LayerArgs& L, const ExpertPlan& P, int64_t T, float* y_dev,

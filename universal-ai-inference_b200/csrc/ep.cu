@@ -39,8 +39,8 @@ __global__ void ep_plan_kernel(const int32_t* __restrict__ topk_ids, int64_t T, 
 __global__ void ep_pack_kernel(const float* __restrict__ x, int64_t T, int64_t D, int k, int R, int epr,
                                const int32_t* __restrict__ topk_ids, const float* __restrict__ topk_w,
                                const uint8_t* __restrict__ dmask, const int32_t* __restrict__ rowpos,
-                               const int32_t* __restrict__ dcounts, __half* __restrict__ send_x16,
-                               int32_t* __restrict__ send_ids, float* __restrict__ send_w,
+                               const int32_t* __restrict__ dcounts, __half* __restrict__ send_x16, int64_t xs,
+                               int32_t* __restrict__ send_ids, float* __restrict__ send_w, int64_t es,
                                int32_t* __restrict__ send_token, int32_t* __restrict__ row_of,
                                int32_t* __restrict__ send_counts, int32_t* __restrict__ send_entries) {
   extern __shared__ int offs[];  // [R]
@@ -72,17 +72,17 @@ __global__ void ep_pack_kernel(const float* __restrict__ x, int64_t T, int64_t D
     if (lane < k) {
       const int e = topk_ids[t * k + lane];
       const bool mine = e / epr == d;
-      send_ids[row * k + lane] = mine ? e - d * epr : -1;
-      send_w[row * k + lane] = mine ? topk_w[t * k + lane] : 0.0f;
+      send_ids[row * es + lane] = mine ? e - d * epr : -1;
+      send_w[row * es + lane] = mine ? topk_w[t * k + lane] : 0.0f;
     }
     if (D % 4 != 0) {
       for (int64_t i = lane; i < D; i += 32)
-        send_x16[row * D + ((i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1))] = __float2half_rn(x[t * D + i]);
+        send_x16[row * xs + ((i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1))] = __float2half_rn(x[t * D + i]);
     } else {
       const float4* src = reinterpret_cast<const float4*>(x + t * D);
       for (int64_t i = lane; i < D / 4; i += 32) {
         const float4 v = src[i];
-        __half2* d2 = reinterpret_cast<__half2*>(send_x16 + row * D) + 2 * i;
+        __half2* d2 = reinterpret_cast<__half2*>(send_x16 + row * xs) + 2 * i;
         d2[0] = __floats2half2_rn(v.x, v.z);
         d2[1] = __floats2half2_rn(v.y, v.w);
       }
@@ -99,21 +99,21 @@ __global__ void ep_entries_kernel(const int32_t* __restrict__ topk_ids, int64_t 
 }
 
 // Receiving side: routing tables from the received entries (-1 = absent).
-__global__ void ep_route_kernel(const int32_t* __restrict__ ids, const float* __restrict__ w, int64_t N,
-                                int k, RouteBuffers rb) {
+__global__ void ep_route_kernel(const int32_t* __restrict__ ids, const float* __restrict__ w, int64_t es,
+                                int64_t N, int k, RouteBuffers rb) {
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (t >= N) return;
   for (int r = 0; r < k; ++r) {
-    const int e = ids[t * k + r];
+    const int e = ids[t * es + r];
     rb.topk_ids[t * k + r] = e;
-    rb.topk_w[t * k + r] = w[t * k + r];
+    rb.topk_w[t * k + r] = w[t * es + r];
     if (e >= 0) rb.mask[(int64_t)e * N + t] = (uint8_t)(r + 1);
   }
 }
 
 // Gather received f16 rows (already in operand order) into expert-contiguous slots.
-__global__ void route_gather16_kernel(const __half* __restrict__ rows, int64_t N, int64_t D, int64_t E, int k,
-                                      RouteBuffers rb, __half* __restrict__ xp16) {
+__global__ void route_gather16_kernel(const __half* __restrict__ rows, int64_t xs, int64_t N, int64_t D, int64_t E,
+                                      int k, RouteBuffers rb, __half* __restrict__ xp16) {
   extern __shared__ int offs[];  // [E+1]
   if (threadIdx.x == 0) {
     int run = 0;
@@ -131,12 +131,12 @@ __global__ void route_gather16_kernel(const __half* __restrict__ rows, int64_t N
     const int64_t t = p / k;
     const int slot = offs[e] + rb.slot_local[p];
     if (lane == 0) { rb.slot_of[p] = slot; rb.token_of[slot] = (int32_t)t; }
-    if (D % 8 == 0) {
-      const uint4* src = reinterpret_cast<const uint4*>(rows + t * D);
+    if (D % 8 == 0 && xs % 8 == 0) {
+      const uint4* src = reinterpret_cast<const uint4*>(rows + t * xs);
       uint4* dst = reinterpret_cast<uint4*>(xp16 + (int64_t)slot * D);
       for (int64_t i = lane; i < D / 8; i += 32) dst[i] = src[i];
     } else {
-      for (int64_t i = lane; i < D; i += 32) xp16[(int64_t)slot * D + i] = rows[t * D + i];
+      for (int64_t i = lane; i < D; i += 32) xp16[(int64_t)slot * D + i] = rows[t * xs + i];
     }
   }
 }
@@ -175,14 +175,17 @@ cudaError_t launch_ep_pack(const float* x, int64_t T, int64_t D, int k, int R, i
                            const float* topk_w, const uint8_t* dmask, const int32_t* rowpos,
                            const int32_t* dcounts, void* send_x16, int32_t* send_ids, float* send_w,
                            int32_t* send_token, int32_t* row_of, int32_t* send_counts, int32_t* send_entries,
-                           cudaStream_t st) {
+                           cudaStream_t st, int64_t x_pitch, int64_t e_pitch) {
   if (k > 32) return cudaErrorInvalidValue;
+  if (x_pitch <= 0) x_pitch = D;
+  if (e_pitch <= 0) e_pitch = k;
+  if (x_pitch < D || e_pitch < k || (D % 4 == 0 && x_pitch % 2 != 0)) return cudaErrorInvalidValue;
   int64_t blocks = (T * R + 7) / 8;
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
   ep_pack_kernel<<<(unsigned)blocks, 256, sizeof(int) * (size_t)R, st>>>(
-      x, T, D, k, R, epr, topk_ids, topk_w, dmask, rowpos, dcounts, static_cast<__half*>(send_x16), send_ids,
-      send_w, send_token, row_of, send_counts, send_entries);
+      x, T, D, k, R, epr, topk_ids, topk_w, dmask, rowpos, dcounts, static_cast<__half*>(send_x16), x_pitch,
+      send_ids, send_w, e_pitch, send_token, row_of, send_counts, send_entries);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || T == 0) return e;
   ep_entries_kernel<<<(unsigned)((T + 255) / 256), 256, 0, st>>>(topk_ids, T, k, epr, send_entries);
@@ -190,20 +193,24 @@ cudaError_t launch_ep_pack(const float* x, int64_t T, int64_t D, int k, int R, i
 }
 
 cudaError_t launch_ep_route(const int32_t* ids, const float* w, int64_t N, int64_t E, int k,
-                            const RouteBuffers& rb, cudaStream_t st) {
+                            const RouteBuffers& rb, cudaStream_t st, int64_t e_pitch) {
+  if (e_pitch <= 0) e_pitch = k;
+  if (e_pitch < k) return cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(rb.mask, 0, (size_t)(E * N), st);
   if (e != cudaSuccess || N == 0) return e;
-  ep_route_kernel<<<(unsigned)((N + 127) / 128), 128, 0, st>>>(ids, w, N, k, rb);
+  ep_route_kernel<<<(unsigned)((N + 127) / 128), 128, 0, st>>>(ids, w, e_pitch, N, k, rb);
   return cudaGetLastError();
 }
 
 cudaError_t launch_route_gather16(const void* rows, int64_t N, int64_t D, int64_t E, int k, const RouteBuffers& rb,
-                                  void* xp16, cudaStream_t st) {
+                                  void* xp16, cudaStream_t st, int64_t x_pitch) {
+  if (x_pitch <= 0) x_pitch = D;
+  if (x_pitch < D) return cudaErrorInvalidValue;
   int64_t blocks = (N * k + 7) / 8;
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
   route_gather16_kernel<<<(unsigned)blocks, 256, sizeof(int) * (size_t)(E + 1), st>>>(
-      static_cast<const __half*>(rows), N, D, E, k, rb, static_cast<__half*>(xp16));
+      static_cast<const __half*>(rows), x_pitch, N, D, E, k, rb, static_cast<__half*>(xp16));
   return cudaGetLastError();
 }
 

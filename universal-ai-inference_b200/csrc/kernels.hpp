@@ -52,17 +52,18 @@ cudaError_t launch_ep_plan(const int32_t* topk_ids, int64_t T, int k, int R, int
 // Packs the send rows grouped by destination: f16 x (operand order), k (local
 // expert | -1, weight) entries, source token; row_of [T*R] (-1 where none);
 // send_counts / send_entries [R]: rows and valid entries per destination.
+// x_pitch (f16 elements) and e_pitch (entries) between rows; 0 = dense (D, k).
 cudaError_t launch_ep_pack(const float* x, int64_t T, int64_t D, int k, int R, int epr, const int32_t* topk_ids,
                            const float* topk_w, const uint8_t* dmask, const int32_t* rowpos,
                            const int32_t* dcounts, void* send_x16, int32_t* send_ids, float* send_w,
                            int32_t* send_token, int32_t* row_of, int32_t* send_counts, int32_t* send_entries,
-                           cudaStream_t st);
+                           cudaStream_t st, int64_t x_pitch = 0, int64_t e_pitch = 0);
 // Receiving side: routing tables (topk_ids/w, expert mask) from received entries.
 cudaError_t launch_ep_route(const int32_t* ids, const float* w, int64_t N, int64_t E, int k,
-                            const RouteBuffers& rb, cudaStream_t st);
+                            const RouteBuffers& rb, cudaStream_t st, int64_t e_pitch = 0);
 // Gather of received f16 rows into expert-contiguous slots (absent entries skipped).
 cudaError_t launch_route_gather16(const void* rows, int64_t N, int64_t D, int64_t E, int k, const RouteBuffers& rb,
-                                  void* xp16, cudaStream_t st);
+                                  void* xp16, cudaStream_t st, int64_t x_pitch = 0);
 // y[t] = sum over d = 0..R-1 of y_back[row_of[t*R+d]] (rows that exist), fixed order.
 cudaError_t launch_ep_combine(const float* y_back, const int32_t* row_of, int64_t T, int R, int64_t D, float* y,
                               cudaStream_t st);

@@ -88,12 +88,17 @@ def _load():
         "uaii_moe_register_weights": (c_int, [c_void_p, c_void_p, c_uint64]),
         "uaii_moe_release_weights": (c_int, [c_void_p, c_void_p]),
         "uaii_moe_set_expert_path": (c_int, [c_void_p, c_int]),
+        "uaii_moe_backend_stream": (c_int, [c_void_p, POINTER(c_void_p)]),
         "uaii_moe_last_plan": (c_int, [c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
         "uaii_moe_ep_dispatch": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
         "uaii_moe_ep_experts": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                                         c_void_p]),
         "uaii_moe_ep_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p]),
+        "uaii_moe_ep_dispatch_records": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p,
+                                                 c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+        "uaii_moe_ep_experts_records": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                                c_void_p]),
         "uaii_moe_selftest_wait_timeout": (c_int, [c_void_p, c_int64]),
         "uaii_moe_profile_enable": (c_int, [c_void_p, c_int]),
         "uaii_moe_profile_read": (c_int, [c_void_p, POINTER(c_double), POINTER(c_uint64), POINTER(c_uint64)]),
@@ -115,8 +120,9 @@ EXPORTED = ("uaii_moe_abi_version", "uaii_moe_last_error", "uaii_moe_backend_cre
             "uaii_moe_experts_swiglu", "uaii_moe_ffn_forward", "uaii_moe_ffn_forward_noalloc",
             "uaii_moe_register_weights",
             "uaii_moe_release_weights",
-            "uaii_moe_set_expert_path", "uaii_moe_last_plan", "uaii_moe_ep_dispatch", "uaii_moe_ep_experts",
-            "uaii_moe_ep_combine", "uaii_moe_selftest_wait_timeout", "uaii_moe_profile_enable",
+            "uaii_moe_set_expert_path", "uaii_moe_backend_stream", "uaii_moe_last_plan", "uaii_moe_ep_dispatch", "uaii_moe_ep_experts",
+            "uaii_moe_ep_combine", "uaii_moe_ep_dispatch_records", "uaii_moe_ep_experts_records",
+            "uaii_moe_selftest_wait_timeout", "uaii_moe_profile_enable",
             "uaii_moe_profile_read",
             "uaii_moe_packed_nbytes", "uaii_moe_quantize_rows",
             "uaii_moe_fill_normal")
@@ -182,6 +188,13 @@ class Backend:
             self.close()
         except Exception:
             pass
+
+    @property
+    def stream(self) -> int:
+        """cudaStream_t handle the backend queues its work on (its own stream if none was given)."""
+        h = c_void_p()
+        _check(lib.uaii_moe_backend_stream(self._h, ctypes.byref(h)))
+        return int(h.value or 0)
 
     def synchronize(self):
         _check(lib.uaii_moe_synchronize(self._h))
@@ -252,6 +265,17 @@ class Backend:
     def selftest_wait_timeout(self, budget_cycles: int):
         """Bounded-wait failure path on the device; raises UaiiMoeError (Internal) when it works."""
         _check(lib.uaii_moe_selftest_wait_timeout(self._h, budget_cycles))
+
+    def ep_dispatch_records(self, layer: Layer, x, T: int, rank: int, world: int, send_rec, rec_bytes: int,
+                            send_token, row_of, send_counts, send_entries, probs=None):
+        """ep_dispatch with each row one record: f16 x, top_k int32 ids, top_k f32 weights."""
+        _check(lib.uaii_moe_ep_dispatch_records(self._h, ctypes.byref(layer), ptr(x), T, rank, world, ptr(send_rec),
+                                                rec_bytes, ptr(send_token), ptr(row_of), ptr(send_counts),
+                                                ptr(send_entries), ptr(probs)))
+
+    def ep_experts_records(self, layer: Layer, recv_rec, rec_bytes: int, rows: int, entries: int, y_part):
+        _check(lib.uaii_moe_ep_experts_records(self._h, ctypes.byref(layer), ptr(recv_rec), rec_bytes, rows, entries,
+                                               ptr(y_part)))
 
     def ep_combine(self, y_back, row_of, T: int, world: int, d_model: int, y):
         _check(lib.uaii_moe_ep_combine(self._h, ptr(y_back), ptr(row_of), T, world, d_model, ptr(y)))

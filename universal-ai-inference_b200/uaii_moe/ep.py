@@ -7,8 +7,8 @@ forward is
 1. ``ep_dispatch`` (device): router + top-k for the local tokens, then each token
    packed once per rank that owns one of its experts (f16 row + top_k
    (local expert | -1, weight) entries), grouped by destination rank;
-2. an all-to-all of the per-destination row and entry counts, then of the rows
-   (f16 activations, expert ids, weights);
+2. an all-to-all of the per-destination row and entry counts, then one of the
+   rows, each a single record (f16 activations, expert ids, weights);
 3. ``ep_experts`` (device): the grouped expert GEMM over the received rows,
    producing one f32 row per received row (its weighted expert sum);
 4. the reverse all-to-all of those rows;
@@ -26,15 +26,18 @@ import torch
 import torch.distributed as dist
 
 
+def record_bytes(D: int, k: int) -> int:
+    """Bytes of one exchanged row: f16 x [D], k int32 ids, k f32 weights, padded to 16."""
+    return (2 * D + 8 * k + 15) // 16 * 16
+
+
 class _Chunk:
-    """Send-side buffers of one token chunk."""
+    """Send-side buffers of one token chunk: one record per row."""
 
     def __init__(self, T: int, D: int, k: int, R: int, dev):
         cap = max(T * min(k, R), 1)
         self.T = T
-        self.x16 = torch.empty((cap, D), dtype=torch.float16, device=dev)
-        self.ids = torch.empty((cap, k), dtype=torch.int32, device=dev)
-        self.w = torch.empty((cap, k), dtype=torch.float32, device=dev)
+        self.rec = torch.empty((cap, record_bytes(D, k)), dtype=torch.uint8, device=dev)
         self.token = torch.empty((cap,), dtype=torch.int32, device=dev)
         self.row_of = torch.empty((max(T, 1), R), dtype=torch.int32, device=dev)
         self.counts = torch.empty((2, R), dtype=torch.int32, device=dev)  # rows, entries per destination
@@ -78,16 +81,28 @@ class ExpertParallelFFN:
         return b
 
     def forward(self, x: torch.Tensor, y: torch.Tensor, probs: torch.Tensor | None = None) -> torch.Tensor:
+        """The collectives and buffer allocations are ordered on the backend's stream;
+        x must be ready on it (or on a stream it waits for) when forward is called."""
+        stream = getattr(self.be, "stream", None)
+        if self.device.type == "cuda" and stream is not None:
+            ext = torch.cuda.ExternalStream(stream, device=self.device) if stream else \
+                torch.cuda.default_stream(self.device)
+            with torch.cuda.stream(ext):
+                return self._forward(x, y, probs)
+        return self._forward(x, y, probs)
+
+    def _forward(self, x: torch.Tensor, y: torch.Tensor, probs: torch.Tensor | None = None) -> torch.Tensor:
         T = int(x.shape[0])
         D, k, R = self.D, self.k, self.world
+        rb = record_bytes(D, k)
         n = self.chunks if T >= self.chunks * self.min_chunk else 1
         bounds = [T * c // n for c in range(n + 1)]
         parts = []
         for c in range(n):  # 1. dispatch every chunk on the device
             t0, t1 = bounds[c], bounds[c + 1]
             b = self._chunk_bufs(c, t1 - t0)
-            self.be.ep_dispatch(self.router_layer, x[t0:t1], t1 - t0, self.rank, R, b.x16, b.ids, b.w, b.token,
-                                b.row_of, b.counts[0], b.counts[1], None if probs is None else probs[t0:t1])
+            self.be.ep_dispatch_records(self.router_layer, x[t0:t1], t1 - t0, self.rank, R, b.rec, rb, b.token,
+                                        b.row_of, b.counts[0], b.counts[1], None if probs is None else probs[t0:t1])
             parts.append(b)
         # 2. rows / entries per destination of every chunk -> per source (one exchange, one host read)
         meta_send = torch.stack([b.counts.t() for b in parts], dim=1).reshape(R, 2 * n).to(torch.int64)
@@ -104,27 +119,22 @@ class ExpertParallelFFN:
         self.last_exchange = (
             [sum(p[0][r] for p in plans) for r in range(R)], [sum(p[1][r] for p in plans) for r in range(R)],
             sum(p[2] for p in plans))
-        # 3. rows of every chunk in flight
+        # 3. rows of every chunk in flight (one all-to-all of records per chunk)
         recv, works = [], []
         for (send_rows, recv_rows, entries), b in zip(plans, parts):
             ns, nr = sum(send_rows), sum(recv_rows)
-            rx = torch.empty((max(nr, 1), D), dtype=torch.float16, device=dev)
-            ri = torch.empty((max(nr, 1), k), dtype=torch.int32, device=dev)
-            rw = torch.empty((max(nr, 1), k), dtype=torch.float32, device=dev)
-            w = [dist.all_to_all_single(dst[:nr], src[:ns], output_split_sizes=recv_rows,
-                                        input_split_sizes=send_rows, group=self.group, async_op=True)
-                 for dst, src in ((rx, b.x16), (ri, b.ids), (rw, b.w))]
-            recv.append((rx, ri, rw))
-            works.append(w)
+            rrec = torch.empty((max(nr, 1), rb), dtype=torch.uint8, device=dev)
+            works.append(dist.all_to_all_single(rrec[:nr], b.rec[:ns], output_split_sizes=recv_rows,
+                                                input_split_sizes=send_rows, group=self.group, async_op=True))
+            recv.append(rrec)
         # 4. experts of chunk c as soon as its rows are in, return its rows asynchronously
         backs, rworks = [], []
-        for c, ((send_rows, recv_rows, entries), (rx, ri, rw)) in enumerate(zip(plans, recv)):
-            for w in works[c]:
-                w.wait()
+        for c, ((send_rows, recv_rows, entries), rrec) in enumerate(zip(plans, recv)):
+            works[c].wait()
             ns, nr = sum(send_rows), sum(recv_rows)
             y_part = torch.empty((max(nr, 1), D), dtype=torch.float32, device=dev)
             if nr:
-                self.be.ep_experts(self.local_layer, rx, ri, rw, nr, entries, y_part)
+                self.be.ep_experts_records(self.local_layer, rrec, rb, nr, entries, y_part)
             y_back = torch.empty((max(ns, 1), D), dtype=torch.float32, device=dev)
             rworks.append(dist.all_to_all_single(y_back[:ns], y_part[:nr], output_split_sizes=send_rows,
                                                  input_split_sizes=recv_rows, group=self.group, async_op=True))
