@@ -161,6 +161,9 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
   const int XS = TB + 4, WS = EB + 4;  // padded k rows
   float* xs = sm;                      // [kTile][XS]
   float* ws = xs + kTile * XS;         // [kTile][WS]
+  // Column of block expert r in a w row: experts 4..7 of every group after experts 0..3 of all
+  // groups, so the 16-byte reads of one k step by all expert groups are contiguous.
+  auto wcol = [EB](int r) { return ((r & 7) >> 2) * (EB / 2) + (r >> 3) * 4 + (r & 3); };
   const int tid = threadIdx.x, eg = tid % EG, tg = tid / EG;  // EG divides 256: every thread has a group
   const int64_t t0 = (int64_t)blockIdx.x * TB, e0 = (int64_t)blockIdx.y * EB;
   float c[kRT][kRE];
@@ -188,8 +191,9 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
         const int k4 = i / EB, r = i - k4 * EB;
         const float4 v = (e0 + r < E) ? __ldg(reinterpret_cast<const float4*>(w + (e0 + r) * D + k0) + k4)
                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-        ws[(4 * k4) * WS + r] = v.x; ws[(4 * k4 + 1) * WS + r] = v.y;
-        ws[(4 * k4 + 2) * WS + r] = v.z; ws[(4 * k4 + 3) * WS + r] = v.w;
+        const int cr = wcol(r);
+        ws[(4 * k4) * WS + cr] = v.x; ws[(4 * k4 + 1) * WS + cr] = v.y;
+        ws[(4 * k4 + 2) * WS + cr] = v.z; ws[(4 * k4 + 3) * WS + cr] = v.w;
       }
     } else {
       for (int i = tid; i < TB * kTile; i += 256) {
@@ -198,7 +202,7 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
       }
       for (int i = tid; i < EB * kTile; i += 256) {
         const int k = i / EB, r = i - k * EB;
-        ws[k * WS + r] = (e0 + r < E && k < kn) ? __ldg(w + (e0 + r) * D + k0 + k) : 0.f;
+        ws[k * WS + wcol(r)] = (e0 + r < E && k < kn) ? __ldg(w + (e0 + r) * D + k0 + k) : 0.f;
       }
     }
     __syncthreads();
@@ -207,7 +211,7 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
     for (int a = 0; a < kRT; ++a)
 #pragma unroll
       for (int b = 0; b < kRE; ++b) sacc[a][b] = 0.f;
-    for (int k = 0; k < kn; ++k) {
+    auto kstep = [&](int k) {
       float xa[kRT];
       if constexpr (kRT == 4) {
         const float4 xv = *reinterpret_cast<const float4*>(xs + k * XS + tg * kRT);
@@ -218,13 +222,19 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
       } else {
         xa[0] = xs[k * XS + tg];
       }
-      const float4 wa = *reinterpret_cast<const float4*>(ws + k * WS + eg * kRE);
-      const float4 wb = *reinterpret_cast<const float4*>(ws + k * WS + eg * kRE + 4);
+      const float4 wa = *reinterpret_cast<const float4*>(ws + k * WS + eg * 4);
+      const float4 wb = *reinterpret_cast<const float4*>(ws + k * WS + EB / 2 + eg * 4);
       const float wv[kRE] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
       for (int a = 0; a < kRT; ++a)
 #pragma unroll
         for (int b = 0; b < kRE; ++b) sacc[a][b] = __fadd_rn(sacc[a][b], __fmul_rn(xa[a], wv[b]));
+    };
+    if (kn == kTile) {  // full tile: unrolled, shared-memory offsets become immediates
+#pragma unroll 4
+      for (int k = 0; k < kTile; ++k) kstep(k);
+    } else {
+      for (int k = 0; k < kn; ++k) kstep(k);
     }
     if (partials) {
 #pragma unroll
