@@ -214,6 +214,18 @@ UAII_MOE_API int uaii_moe_experts_swiglu(uaii_moe_backend* b, const float* x, co
 UAII_MOE_API int uaii_moe_ffn_forward(uaii_moe_backend* b, const uaii_moe_layer* layer, const float* x,
                          int64_t T, float* y, float* probs);
 
+/* Dense projection with a packed GGUF weight: y[M,N] = x[M,K] . dequant(w)^T,
+ * w = N packed rows of K elements in w_fmt (any GGUF block format); relu != 0
+ * applies max(y, 0) (the MatMulRelu op).  Replaces kernels::quant_gemm_f32
+ * (libs/uaii-kernels/src/quant_gemm.cpp:22-70), which dispatch_cpu runs for
+ * MatMul / MatMulRelu with a packed B and transpose_b
+ * (libs/uaii-kernels/src/dispatch.cpp:82-100); uaii_moe_dispatch takes those ops
+ * in the same form.  Q4_0/Q8_0/Q4_K/Q6_K with N % 128 == 0 run on the tensor
+ * cores (f16 operands, f32 accumulate), everything else on the CUDA cores in f32.
+ * Residency as above; x, y may be host or device memory. */
+UAII_MOE_API int uaii_moe_quant_matmul(uaii_moe_backend* b, const float* x, int64_t M, int64_t K, const void* w,
+                                       int w_fmt, int64_t N, int relu, float* y);
+
 /* Declare a weight buffer constant until uaii_moe_release_weights().  A host
  * buffer is uploaded once and the device copy is reused whenever a call passes
  * the same (pointer, bytes).  For host and device buffers alike, layouts the

@@ -270,6 +270,32 @@ int uo_dequant_rows(int fmt, const uint8_t* p, int64_t rows, int64_t cols, int64
   return UO_OK;
 }
 
+/* Dense projection with a packed B, restating kernels::quant_gemm_f32
+ * (libs/uaii-kernels/src/quant_gemm.cpp:22-70): for every output column j the
+ * packed row B[j] is dequantized (dequant_gguf_row), then for every row i
+ * c[i][j] = sum over k of a[i][k] * row[k], one rounding per multiply and per
+ * add, k ascending from 0.  relu != 0 then maps every value v to v > 0 ? v : 0
+ * (MatMulRelu, libs/uaii-kernels/src/dispatch.cpp:82-100). */
+int uo_quant_gemm(const float* a, int64_t M, int64_t K, const uint8_t* b, int fmt, int64_t N, int relu, float* c) {
+  const int64_t stride = (int64_t)uo_packed_nbytes(fmt, K);
+  float* row = (float*)malloc(sizeof(float) * (size_t)K);
+  if (!row) return UO_INVALID_ARGUMENT;
+  for (int64_t j = 0; j < N; ++j) {
+    int st = uo_dequant_row(fmt, b + j * stride, K, row);
+    if (st != UO_OK) {
+      free(row);
+      return st;
+    }
+    for (int64_t i = 0; i < M; ++i) {
+      float sum = 0.0f;
+      for (int64_t k = 0; k < K; ++k) sum += a[i * K + k] * row[k];
+      c[i * N + j] = (!relu || sum > 0.0f) ? sum : 0.0f; /* relu_f32: x > 0 ? x : 0 (elementwise.cpp:44-52) */
+    }
+  }
+  free(row);
+  return UO_OK;
+}
+
 /* Router logits in the Ref tiled GEMM order: per element, 64-wide k tiles summed
  * sequentially from 0, and each tile partial added in order to c (initialised 0)
  * (libs/uaii-kernels/src/gemm_ref.cpp:45-75, via matmul.cpp:22-56 with

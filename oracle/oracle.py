@@ -49,6 +49,7 @@ class Oracle:
                                                                                   c_void_p]),
             "uo_shared_expert_packed": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int,
                                                 c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+            "uo_quant_gemm": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int, c_int64, c_int, c_void_p]),
         }
         for n, (r, a) in sig.items():
             f = getattr(L, n)
@@ -100,6 +101,13 @@ class Oracle:
                                                    I, top_k, norm, _p(y), _p(ids), _p(w)) == 0
         return y, ids, w
 
+    def quant_gemm(self, a, b_packed, fmt, N, relu=False):
+        """c[M,N] = a[M,K] . dequant(b_packed[N rows])^T (kernels::quant_gemm_f32), max(., 0) with relu."""
+        M, K = a.shape
+        c = np.empty((M, N), np.float32)
+        assert self.L.uo_quant_gemm(_p(a), M, K, _p(b_packed), fmt, N, int(relu), _p(c)) == 0
+        return c
+
     def shared_packed(self, x, G, gf, U, uf, Dn, df, wsg, Ish, y):
         T, D = x.shape
         assert self.L.uo_shared_expert_packed(_p(x), _p(G), gf, _p(U), uf, _p(Dn), df, _p(wsg), T, D, Ish,
@@ -121,6 +129,7 @@ class Reference:
             "uref_matmul_bt": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
             "uref_moe_experts_swiglu": (c_int, [c_void_p] * 5 + [c_int64] * 4 + [c_int, c_void_p]),
             "uref_moe_experts_swiglu_mt": (c_int, [c_void_p] * 5 + [c_int64] * 4 + [c_int, c_void_p, c_int]),
+            "uref_quant_gemm": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p]),
         }
         for n, (r, a) in sig.items():
             f = getattr(L, n)
@@ -130,6 +139,12 @@ class Reference:
     def _chk(self, st):
         if st != 0:
             raise ValueError(f"reference status {st}: {self.L.uref_last_error().decode()}")
+
+    def quant_gemm(self, a, b_packed, fmt, N):
+        M, K = a.shape
+        c = np.empty((M, N), np.float32)
+        self._chk(self.L.uref_quant_gemm(_p(a), M, K, _p(b_packed), fmt, N, _p(c)))
+        return c
 
     def dequant(self, fmt, packed: np.ndarray, rows: int, cols: int, pitch: int) -> np.ndarray:
         out = np.empty((rows, cols), np.float32)

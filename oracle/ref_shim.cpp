@@ -1,16 +1,19 @@
 // ref_shim.cpp -- extern "C" entry points over the reference's OWN compiled code.
 //
 // TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
-// eleven unmodified source files of the reference (arjun988/Universal-AI-Inference)
+// twelve unmodified source files of the reference (arjun988/Universal-AI-Inference)
 // into oracle/_ref/libuaii_ref.so.  Nothing here re-implements the reference:
 // each function only builds the reference's TensorView arguments and calls
 //   uaii::quant::dequant_gguf_row      (libs/uaii-quant/src/gguf_dequant.cpp:420-439)
 //   uaii::kernels::moe_router_f32      (libs/uaii-kernels/src/transformer.cpp:446-481)
 //   uaii::kernels::moe_experts_swiglu_f32 (libs/uaii-kernels/src/transformer.cpp:522-612)
 //   uaii::kernels::matmul_f32          (libs/uaii-kernels/src/matmul.cpp:22-56)
+//   uaii::kernels::quant_gemm_f32      (libs/uaii-kernels/src/quant_gemm.cpp:22-70)
 // It is used by tests/ to pin oracle/moe_oracle.c, by tests/golden/make_golden.py
 // to produce fixtures, and by bench.py's reference arm as the timed CPU path.
 #include "uaii/kernels/kernels.hpp"
+#include "uaii/kernels/quant_gemm.hpp"
+#include "uaii/quant/formats.hpp"
 #include "uaii/quant/gguf_dequant.hpp"
 
 #include <cstdint>
@@ -69,6 +72,23 @@ int uref_matmul_bt(const float* a, const float* b, std::int64_t M, std::int64_t 
   const std::int64_t sa[2] = {M, K}, sb[2] = {N, K}, sc[2] = {M, N};
   TensorView va = f32_view(a, sa, 2), vb = f32_view(b, sb, 2), vc = f32_view(c, sc, 2);
   return status(uaii::kernels::matmul_f32(va, vb, &vc, false, true));
+}
+
+// MatMul with a packed B (the dispatch_cpu MatMul branch with transpose_b):
+// c[M,N] = a[M,K] . dequant(b[N rows of K])^T.
+int uref_quant_gemm(const float* a, std::int64_t M, std::int64_t K, const std::uint8_t* b, int fmt,
+                    std::int64_t N, float* c) {
+  const std::int64_t sa[2] = {M, K}, sb[2] = {N, K}, sc[2] = {M, N};
+  TensorView va = f32_view(a, sa, 2), vc = f32_view(c, sc, 2);
+  TensorView vb;
+  vb.dtype = DType::Unknown;
+  vb.shape = sb;
+  vb.rank = 2;
+  vb.data = const_cast<std::uint8_t*>(b);
+  vb.quant_format = static_cast<uaii::quant::QuantFormat>(fmt);
+  vb.nbytes = static_cast<std::size_t>(N) *
+              uaii::quant::packed_nbytes(vb.quant_format, static_cast<std::size_t>(K));
+  return status(uaii::kernels::quant_gemm_f32(va, vb, &vc, true));
 }
 
 int uref_moe_experts_swiglu(const float* x, const float* G, const float* U, const float* Dn,

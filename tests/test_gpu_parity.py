@@ -518,3 +518,91 @@ def test_registered_device_weights_keep_padded_rows(backend, oracle, um):
     y2 = np.empty_like(x)
     backend.ffn(L, x, T, y2)  # released: padded per call again
     assert bits_equal(y2, y0)
+
+
+# ---------------------------------------------------------------- MatMul with a packed B (quant_gemm_f32)
+
+def _qrows(um, fmt, rows, cols, seed):
+    if fmt in (um.Q4_0, um.Q8_0, um.Q4_K, um.Q6_K):
+        return um.quantize_rows(fmt, um.fill_normal((rows, cols), seed, 3, 0.0, 0.05))
+    return random_blocks(um, np.random.default_rng(seed), fmt, rows, cols)
+
+
+@pytest.mark.parametrize("fmt,M,K,N,path,sched", [
+    (14, 1, 1024, 256, 0, "warp_mma"),       # Q4_K decode row: warp-MMA, split K
+    (16, 5, 2048, 512, 0, "warp_mma"),       # Q6_K
+    (7, 64, 512, 384, 0, "tcgen05"),         # Q4_0, 64-slot tile
+    (11, 300, 256, 128, 0, "tcgen05"),       # Q8_0, 256-slot tiles
+    (11, 3, 1408, 256, 2, "tcgen05"),        # Q8_0 rows of 1496 bytes (padded pitch), forced tcgen05
+    (7, 40, 384, 128, 3, "warp_mma"),        # forced warp-MMA above decode width; K % 256 == 128
+])
+def test_quant_matmul_tensor_cores_vs_oracle(backend, oracle, um, fmt, M, K, N, path, sched):
+    x = um.fill_normal((M, K), 17 + M, 1)
+    W = _qrows(um, fmt, N, K, 5 + N)
+    y_ref = oracle.quant_gemm(x, W, fmt, N)
+    y = np.empty((M, N), np.float32)
+    backend.set_expert_path(path)
+    try:
+        backend.quant_matmul(x, M, K, W, fmt, N, y)
+        plan = backend.last_plan()
+    finally:
+        backend.set_expert_path(0)
+    assert plan["schedule"] == sched, plan
+    assert rel_err(y, y_ref) <= REL_TOL
+
+
+@pytest.mark.parametrize("fmt,M,K,N", [
+    (15, 7, 512, 128),    # Q5_K: no tensor-core decoder -> CUDA cores, f32
+    (7, 9, 256, 100),     # N not a multiple of 128
+    (13, 2, 768, 64),     # Q3_K
+])
+def test_quant_matmul_cuda_cores_vs_oracle(backend, oracle, um, fmt, M, K, N):
+    x = um.fill_normal((M, K), 23 + M, 1)
+    W = _qrows(um, fmt, N, K, 9 + N)
+    y_ref = oracle.quant_gemm(x, W, fmt, N)
+    y = np.empty((M, N), np.float32)
+    backend.quant_matmul(x, M, K, W, fmt, N, y)
+    assert not backend.last_plan()["tensor_cores"]
+    assert rel_err(y, y_ref) <= 1e-5
+
+
+def test_matmul_dispatch_packed_b_and_relu(backend, oracle, um):
+    # dispatch_cpu's MatMul / MatMulRelu with a packed B and transpose_b (dispatch.cpp:82-100)
+    M, K, N = 6, 512, 256
+    x = um.fill_normal((M, K), 31, 1)
+    W = _qrows(um, um.Q4_K, N, K, 31)
+    y_ref = oracle.quant_gemm(x, W, um.Q4_K, N)
+    for op, relu in (("MatMul", False), ("MatMulRelu", True)):
+        y = np.full((M, N), np.nan, np.float32)
+        backend.dispatch(op, [um.f32_desc(x), um.packed_desc(W, um.Q4_K, (N, K))], [um.f32_desc(y)],
+                         {"transpose_b": True})
+        ref = np.where(y_ref > 0, y_ref, np.float32(0)) if relu else y_ref
+        assert rel_err(y, ref) <= REL_TOL, op
+        if relu:
+            assert (y >= 0).all()
+    with pytest.raises(um.UaiiMoeError) as e:  # f32 B stays with the backend's own MatMul
+        backend.dispatch("MatMul", [um.f32_desc(x), um.f32_desc(np.zeros((N, K), np.float32))],
+                         [um.f32_desc(np.empty((M, N), np.float32))], {"transpose_b": True})
+    assert e.value.status == 7
+
+
+def test_quant_matmul_device_buffers_and_registered_weights(backend, oracle, um):
+    torch = pytest.importorskip("torch")
+    M, K, N = 4, 1408, 256  # Q8_0 rows of 1496 bytes: padded once when registered
+    x = um.fill_normal((M, K), 41, 1)
+    W = _qrows(um, um.Q8_0, N, K, 41)
+    y_ref = oracle.quant_gemm(x, W, um.Q8_0, N)
+    xd, Wd = torch.from_numpy(x).cuda(), torch.from_numpy(W).cuda()
+    yd = torch.empty((M, N), device="cuda")
+    backend.quant_matmul(xd, M, K, Wd, um.Q8_0, N, yd)
+    backend.synchronize()
+    y0 = yd.cpu().numpy()
+    assert rel_err(y0, y_ref) <= REL_TOL
+    backend.register_weights(Wd)
+    try:
+        for _ in range(2):
+            backend.quant_matmul(xd, M, K, Wd, um.Q8_0, N, yd)
+            backend.synchronize()
+            assert bits_equal(yd.cpu().numpy(), y0)
+    finally:
+        backend.release_weights(Wd)

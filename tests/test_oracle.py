@@ -152,3 +152,31 @@ def test_packed_experts_vs_reference_q4k_q6k(oracle, reference, um):
     Uf = oracle.dequant(um.Q4_K, U, E * I, D).reshape(E, I, D)
     Df = oracle.dequant(um.Q6_K, Dn, E * D, I).reshape(E, D, I)
     assert bits_equal(y, reference.experts(x, Gf, Uf, Df, pr, k))
+
+
+def _tame_rows(um, rng, fmt, rows, cols):
+    """GGUF rows: the library quantizer where it has one, else random bytes with small f16 scales."""
+    if fmt in (um.Q4_0, um.Q8_0, um.Q4_K, um.Q6_K):
+        return um.quantize_rows(fmt, (rng.standard_normal((rows, cols)) * 0.05).astype(np.float32))
+    from golden.make_golden import D_OFFSET
+    qk, bb = um.BLOCK[fmt]
+    p = rng.integers(0, 256, size=(rows, cols // qk, bb), dtype=np.uint8)
+    scale = np.float16(0.002).view(np.uint16)
+    for o in [D_OFFSET[fmt]] + ([D_OFFSET[fmt] + 2] if fmt in (8, 10, 12, 14, 15) else []):
+        p[:, :, o] = scale & 0xFF
+        p[:, :, o + 1] = scale >> 8
+    return p.reshape(rows, -1)
+
+
+@pytest.mark.parametrize("fmt", GGUF_FORMATS)
+def test_quant_gemm_vs_reference(oracle, reference, um, fmt):
+    """MatMul with a packed B: the restatement equals the reference build bit for bit."""
+    rng = np.random.default_rng(70 + fmt)
+    M, K, N = 5, 512, 24
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    b = _tame_rows(um, rng, fmt, N, K)
+    c = oracle.quant_gemm(a, b, fmt, N)
+    assert np.isfinite(c).all()
+    assert bits_equal(c, reference.quant_gemm(a, b, fmt, N))
+    r = oracle.quant_gemm(a, b, fmt, N, relu=True)
+    assert bits_equal(r, np.where(c > 0, c, np.float32(0.0)).astype(np.float32))  # relu_f32: x > 0 ? x : 0

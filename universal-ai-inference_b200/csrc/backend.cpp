@@ -422,6 +422,27 @@ Error MoeCudaBackend::router(const float* x, const float* gate_w, int64_t T, int
   return Error::success();
 }
 
+namespace {
+constexpr int kSms = 148;
+// K splits of a down-style projection: the split count whose last wave ends first.  A
+// unit is one (tile, split); every unit costs its quads plus about two quads of
+// pipeline fill and epilogue, and the units run in waves of one per SM.
+int pick_down_splits(int64_t tiles, int kchunks) {
+  if (tiles <= 0 || kchunks <= 1) return 1;
+  int best = 1;
+  double best_cost = 0;
+  for (int sp = 1; sp <= 16 && sp <= kchunks; ++sp) {
+    const double waves = (double)((tiles * sp + kSms - 1) / kSms);
+    const double cost = waves * ((kchunks + sp - 1) / sp + 2);
+    if (sp == 1 || cost < best_cost) {
+      best = sp;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+}  // namespace
+
 // Which expert-product schedule a layer call uses, and its tile shape.
 // Automatic: tensor cores whenever the layer qualifies; the warp-MMA schedule
 // when no expert gets more than 16 routed slots on average (decode), tcgen05
@@ -434,7 +455,6 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t s
   const bool warp_ok = allow_warp_mma && warp_mma_shapes_supported(L.gate.fmt, L.down.fmt, L.D, L.I);
   p.umma = path_ != 1 && umma_ok;
   p.umma_refused = (path_ == 2 && !umma_ok) || (path_ == 3 && allow_warp_mma && !warp_ok);
-  const int sms = 148;
   // Slots an expert's tile must hold: the mean plus two standard deviations of a
   // Poisson count at small means (an expert just above a tile width costs a second
   // pass over its weights), the mean at large ones (half-empty tiles cost MMA time).
@@ -447,23 +467,7 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t s
   // hold every expert's slots -- measured faster than tcgen05 there, slower at 16 slots
   auto use_warp = [&](bool ok, double tpe) { return ok && (path_ == 3 || (path_ == 0 && need(tpe) <= 8)); };
   auto warp_bn = [&](double tpe) { return need(tpe) <= 8 ? 8 : 16; };
-  // K splits of the down projection: the split count whose last wave ends first.  A
-  // unit is one (tile, split); every unit costs its quads plus about two quads of
-  // pipeline fill and epilogue, and the units run in waves of one per SM.
-  auto pick_splits = [&](int64_t tiles, int kchunks) {
-    if (tiles <= 0 || kchunks <= 1) return 1;
-    int best = 1;
-    double best_cost = 0;
-    for (int sp = 1; sp <= 16 && sp <= kchunks; ++sp) {
-      const double waves = (double)((tiles * sp + sms - 1) / sms);
-      const double cost = waves * ((kchunks + sp - 1) / sp + 2);
-      if (sp == 1 || cost < best_cost) {
-        best = sp;
-        best_cost = cost;
-      }
-    }
-    return best;
-  };
+  auto pick_splits = pick_down_splits;
   const int64_t active = S < L.E ? S : L.E;
   const double tpe = active > 0 ? (double)S / (double)active : 1.0;
   p.bn = pick_bn(tpe);
@@ -743,6 +747,90 @@ size_t MoeCudaBackend::experts_ws(const LayerArgs& L, int64_t T, const ExpertPla
 }
 
 // ---------------------------------------------------------------- expert parallelism
+
+// Dense projection with a packed weight: the reference's quant_gemm_f32
+// (libs/uaii-kernels/src/quant_gemm.cpp:22-70, reached from dispatch_cpu's MatMul case,
+// libs/uaii-kernels/src/dispatch.cpp:82-100).  One "expert" owning every row: the
+// tensor-core down projection (f16 operands, f32 accumulate, K splits added in order),
+// or the CUDA-core f32 GEMV for formats and shapes the tensor path does not take.
+Error MoeCudaBackend::quant_matmul(const float* x, int64_t M, int64_t K, const void* w, int fmt, int64_t N,
+                                   float* y, bool relu) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaSetDevice(device_), "SetDevice");
+  if (!x || !w || !y || M < 0 || K <= 0 || N <= 0)
+    return Error::make(ErrorCode::InvalidArgument, "quant_gemm shape mismatch");
+  if (!fmt_is_gguf(fmt)) return Error::make(ErrorCode::InvalidArgument, "quant_gemm B quant unsupported");
+  UAII_TRY(check_cols("quant_gemm B", fmt, K));
+  if (M == 0) return Error::success();
+  const size_t wbytes = (size_t)N * row_bytes(fmt, K);
+  const bool tc = path_ != 1 && umma_down_supported(fmt, N, K, false);
+  const bool wm = tc && umma_down_supported(fmt, N, K, true) && (path_ == 3 || (path_ == 0 && M <= 8));
+  if ((path_ == 2 && !tc) || (path_ == 3 && !wm))
+    return Error::make(ErrorCode::NotImplemented,
+                       "tensor-core quant matmul needs Q4_0/Q8_0/Q4_K/Q6_K weights, N % 128 == 0 and K a multiple "
+                       "of the format's tile (64; K-quants 256; warp-MMA schedule 128)");
+  const int bn = wm ? (M <= 8 ? 8 : 16) : (M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256);
+  const int splits = tc ? pick_down_splits(((M + bn - 1) / bn) * (N / 128), umma_kchunks(fmt, K)) : 1;
+  const bool const_w = weight_is_constant(w, wbytes);
+  const size_t xb = sizeof(float) * (size_t)(M * K), yb = sizeof(float) * (size_t)(M * N);
+  const bool planes = tc && (splits > 1 || relu);
+  size_t ws = align_up(xb) + align_up(yb) + 2 * kAlign + weight_stage_bytes(w, wbytes);
+  if (tc) {
+    ws += align_up(2 * (size_t)(M * K));
+    if (planes) ws += align_up(sizeof(float) * (size_t)splits * (size_t)(M * N));
+    if (!const_w && row_bytes(fmt, K) % 16) ws += align_up((size_t)N * (size_t)umma_pitch(fmt, K));
+  }
+  UAII_TRY(reserve(ws + 4 * kAlign));
+  void* xs = carve(xb);
+  float* ys = static_cast<float*>(carve(yb));
+  int32_t* route = static_cast<int32_t*>(carve(sizeof(int32_t) * 4));
+  int32_t* tiles = static_cast<int32_t*>(carve(sizeof(int32_t) * 2));
+  const void *xd = nullptr, *wd = nullptr;
+  bool xh = false;
+  UAII_TRY(stage_input(x, xb, xs, &xd, &xh));
+  UAII_TRY(stage_weight(w, wbytes, &wd));
+  const bool yh = !is_device_ptr(y);
+  float* yo = yh ? ys : y;
+  ExpertPlan P;
+  P.umma = tc;
+  P.warp_mma = wm;
+  P.bn = bn;
+  P.splits = splits;
+  last_plan_ = P;
+  phase_begin(kDown);
+  UAII_CUDA(launch_identity_route(route, M, stream_), "identity_route");  // offsets {0, M}, counts {M}
+  if (tc) {
+    void* x16 = carve(2 * (size_t)(M * K));
+    UAII_CUDA(launch_to_f16(static_cast<const float*>(xd), M * K, x16, stream_, wm), "to_f16");
+    int64_t pitch = 0;
+    UAII_TRY(umma_rows(wd, fmt, N, K, const_w, &wd, &pitch));
+    float* out = planes ? static_cast<float*>(carve(sizeof(float) * (size_t)splits * (size_t)(M * N))) : yo;
+    UAII_CUDA(launch_down_umma(fmt, wd, pitch, 1, N, K, x16, M, route + 2, route, tiles, bn, splits, out, dev_err_,
+                               stream_, wm),
+              "quant_matmul(tensor cores)");
+    count_launches(4);
+    if (planes) {
+      UAII_CUDA(launch_sum_planes(out, splits, M * N, M * N, yo, relu, stream_), "sum_planes");
+      count_launches(1);
+    }
+  } else {
+    UAII_CUDA(launch_down_simt(fmt, wd, 1, N, K, (int64_t)row_bytes(fmt, K), static_cast<const float*>(xd), route,
+                               route + 2, yo, stream_),
+              "quant_matmul");
+    count_launches(2);
+    if (relu) {
+      UAII_CUDA(launch_sum_planes(yo, 1, 0, M * N, yo, true, stream_), "relu");
+      count_launches(1);
+    }
+  }
+  phase_end();
+  if (yh) {
+    UAII_CUDA(cudaMemcpyAsync(y, yo, yb, cudaMemcpyDeviceToHost, stream_), "D2H");
+    UAII_TRY(sync_and_check());
+  }
+  (void)xh;
+  return Error::success();
+}
 
 Error MoeCudaBackend::ep_dispatch(const LayerArgs& L, const float* x, int64_t T, int rank, int world,
                                   void* send_x16, int32_t* send_ids, float* send_w, int32_t* send_token,
@@ -1068,6 +1156,27 @@ Error MoeCudaBackend::dispatch(const std::string& op_name, const std::string& /*
     float* probs = outputs->size() == 2 ? static_cast<float*>((*outputs)[1].data) : nullptr;
     return ffn(L, static_cast<const float*>(x.data), T, static_cast<float*>(y.data), probs);
   }
+  if (op_name == "MatMul" || op_name == "MatMulRelu") {
+    // Only a packed B with transpose_b (the reference's quant_gemm_f32 branch) runs here; f32
+    // operands stay with the backend's own MatMul (NotImplemented = its usual fallback signal).
+    if (inputs.size() != 2 || outputs->size() != 1)
+      return Error::make(ErrorCode::InvalidArgument, "MatMul expects 2 inputs / 1 output");
+    const TensorView &a = inputs[0], &b = inputs[1];
+    TensorView& c = (*outputs)[0];
+    if (!fmt_is_gguf(b.quant_format) || attr_int(attrs, "transpose_b", 0) == 0)
+      return Error::make(ErrorCode::NotImplemented, "CUDA native MatMul here takes packed GGUF B with transpose_b");
+    if (a.dtype != DType::F32 || a.rank != 2 || a.data == nullptr)
+      return Error::make(ErrorCode::InvalidArgument, "quant_gemm A must be f32 [M,K]");
+    if (c.dtype != DType::F32 || c.rank != 2 || c.data == nullptr)
+      return Error::make(ErrorCode::InvalidArgument, "quant_gemm C must be f32");
+    const int64_t M = a.dim(0), K = a.dim(1), N = b.dim(0);
+    if (b.dim(1) != K || c.dim(0) != M || c.dim(1) != N)
+      return Error::make(ErrorCode::InvalidArgument, "quant_gemm shape mismatch");
+    if (b.nbytes != 0 && b.nbytes < (size_t)N * row_bytes(b.quant_format, K))
+      return Error::make(ErrorCode::InvalidArgument, "quant_gemm B: buffer smaller than its shape");
+    return quant_matmul(static_cast<const float*>(a.data), M, K, b.data, b.quant_format, N,
+                        static_cast<float*>(c.data), op_name == "MatMulRelu");
+  }
   return Error::make(ErrorCode::NotImplemented, "CUDA native op not implemented: " + op_name);
 }
 
@@ -1154,6 +1263,12 @@ int uaii_moe_backend_stream(uaii_moe_backend* b, void** stream) {
   if (!stream) return report(Error::make(ErrorCode::InvalidArgument, "null stream pointer"));
   *stream = static_cast<void*>(b->impl.stream());
   return report(Error::success());
+}
+
+int uaii_moe_quant_matmul(uaii_moe_backend* b, const float* x, int64_t M, int64_t K, const void* w, int w_fmt,
+                          int64_t N, int relu, float* y) {
+  if (!b) return no_backend();
+  return report(b->impl.quant_matmul(x, M, K, w, w_fmt, N, y, relu != 0));
 }
 
 int uaii_moe_synchronize(uaii_moe_backend* b) {

@@ -115,6 +115,8 @@ class MoeCudaBackend {
                 const ExpertWeights& d, const float* probs, int64_t T, int64_t D, int64_t E,
                 int64_t I, int top_k, int norm_topk, float* y);
   Error ffn(const LayerArgs& L, const float* x, int64_t T, float* y, float* probs);
+  // y[M,N] = x[M,K] . dequant(W[N,K])^T (kernels::quant_gemm_f32), max(y, 0) with relu.
+  Error quant_matmul(const float* x, int64_t M, int64_t K, const void* w, int fmt, int64_t N, float* y, bool relu);
 
   // Expert parallelism (device pointers only).  See include/uaii_moe.h.
   // x_pitch (f16 elements) / e_pitch (entries) between rows; 0 = dense.

@@ -1490,6 +1490,11 @@ bool umma_shapes_supported(int gfmt, int dfmt, int64_t D, int64_t I) {
 
 int64_t umma_pitch(int fmt, int64_t K) { return (fmt_row_bytes(fmt, K) + 15) / 16 * 16; }
 
+bool umma_down_supported(int fmt, int64_t N, int64_t K, bool warp_mma) {
+  const int mk = min_k(fmt);
+  return mk != 0 && K % mk == 0 && K % 64 == 0 && N % 128 == 0 && (!warp_mma || K % 128 == 0);
+}
+
 bool warp_mma_shapes_supported(int gfmt, int dfmt, int64_t D, int64_t I) {
   return umma_shapes_supported(gfmt, dfmt, D, I) && D % 128 == 0 && I % 128 == 0;
 }

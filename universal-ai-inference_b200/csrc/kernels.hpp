@@ -81,6 +81,9 @@ cudaError_t launch_combine(const float* out, int64_t out_ld, int splits, int64_t
                            int64_t T, int64_t D, int k, const RouteBuffers& rb,
                            const float* shared_out, int sh_splits, int64_t sh_split_stride,
                            const float* shared_gate, float* y, cudaStream_t st);
+// y[i] = sum over s of planes[s*plane_stride + i] (in plane order), max(., 0) when relu; y may alias planes.
+cudaError_t launch_sum_planes(const float* planes, int splits, int64_t plane_stride, int64_t n, float* y, bool relu,
+                              cudaStream_t st);
 // x rows -> f16 copy (shared-expert operand in token order; operand K order tc_kpos,
 // or wm_kpos with wm_order and n % 128 == 0)
 cudaError_t launch_to_f16(const float* x, int64_t n, void* out, cudaStream_t st, bool wm_order = false);
@@ -110,6 +113,9 @@ int64_t umma_pitch(int fmt, int64_t K);
 // The warp-MMA schedule (mma.sync, slot tiles of 8 or 16) also needs D and I to be
 // multiples of 128; its operand rows are in wm_kpos order (operand_order.cuh).
 bool warp_mma_shapes_supported(int gate_fmt, int down_fmt, int64_t D, int64_t I);
+// A single projection out[N] = W[N, K] . x on tensor cores (launch_down_umma with E = 1):
+// format and K chunking, N a multiple of 128 (and K of 128 for the warp-MMA schedule).
+bool umma_down_supported(int fmt, int64_t N, int64_t K, bool warp_mma);
 // h16[slot, i] = silu(x.G[e,i]) * (x.U[e,i]) in f16; x is xp16 [S_rows, D] f16.
 // G, U rows `pitch` bytes apart (a multiple of 16).  warp_mma selects the
 // mma.sync schedule (bn 8 or 16; x and h in wm_kpos order), else tcgen05

@@ -337,6 +337,28 @@ cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E,
   return cudaGetLastError();
 }
 
+namespace {
+// y[i] = planes[0][i] + planes[1][i] + ... (plane order, one rounding per add), then v > 0 ? v : 0 with relu
+__global__ void sum_planes_kernel(const float* __restrict__ planes, int splits, int64_t stride, int64_t n,
+                                  float* __restrict__ y, int relu) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = planes[i];
+    for (int s = 1; s < splits; ++s) v = __fadd_rn(v, planes[s * stride + i]);
+    y[i] = (!relu || v > 0.0f) ? v : 0.0f;  // the reference's relu: v > 0 ? v : 0 (-0 and NaN give 0)
+  }
+}
+}  // namespace
+
+cudaError_t launch_sum_planes(const float* planes, int splits, int64_t plane_stride, int64_t n, float* y, bool relu,
+                              cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  if (splits < 1) return cudaErrorInvalidValue;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  sum_planes_kernel<<<(unsigned)blocks, 256, 0, st>>>(planes, splits, plane_stride, n, y, relu ? 1 : 0);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_combine(const float* out, int64_t out_ld, int splits, int64_t split_stride,
                            int64_t T, int64_t D, int k, const RouteBuffers& rb,
                            const float* shared_out, int sh_splits, int64_t sh_split_stride,

@@ -89,6 +89,8 @@ def _load():
         "uaii_moe_release_weights": (c_int, [c_void_p, c_void_p]),
         "uaii_moe_set_expert_path": (c_int, [c_void_p, c_int]),
         "uaii_moe_backend_stream": (c_int, [c_void_p, POINTER(c_void_p)]),
+        "uaii_moe_quant_matmul": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int, c_int64, c_int,
+                                          c_void_p]),
         "uaii_moe_last_plan": (c_int, [c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
         "uaii_moe_ep_dispatch": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
@@ -120,7 +122,7 @@ EXPORTED = ("uaii_moe_abi_version", "uaii_moe_last_error", "uaii_moe_backend_cre
             "uaii_moe_experts_swiglu", "uaii_moe_ffn_forward", "uaii_moe_ffn_forward_noalloc",
             "uaii_moe_register_weights",
             "uaii_moe_release_weights",
-            "uaii_moe_set_expert_path", "uaii_moe_backend_stream", "uaii_moe_last_plan", "uaii_moe_ep_dispatch", "uaii_moe_ep_experts",
+            "uaii_moe_set_expert_path", "uaii_moe_backend_stream", "uaii_moe_quant_matmul", "uaii_moe_last_plan", "uaii_moe_ep_dispatch", "uaii_moe_ep_experts",
             "uaii_moe_ep_combine", "uaii_moe_ep_dispatch_records", "uaii_moe_ep_experts_records",
             "uaii_moe_selftest_wait_timeout", "uaii_moe_profile_enable",
             "uaii_moe_profile_read",
@@ -252,6 +254,10 @@ class Backend:
         _check(lib.uaii_moe_ffn_forward(self._h, ctypes.byref(layer), ptr(x), T, ptr(y), ptr(probs)))
 
     # ---- expert parallelism (device tensors; see include/uaii_moe.h)
+    def quant_matmul(self, x, M: int, K: int, w, fmt: int, N: int, y, relu: bool = False):
+        """y[M,N] = x[M,K] . dequant(w[N rows of K, fmt])^T (the MatMul op with a packed B)."""
+        _check(lib.uaii_moe_quant_matmul(self._h, ptr(x), M, K, ptr(w), fmt, N, int(relu), ptr(y)))
+
     def ep_dispatch(self, layer: Layer, x, T: int, rank: int, world: int, send_x16, send_ids, send_w, send_token,
                     row_of, send_counts, send_entries, probs=None):
         _check(lib.uaii_moe_ep_dispatch(self._h, ctypes.byref(layer), ptr(x), T, rank, world, ptr(send_x16),
