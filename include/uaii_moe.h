@@ -214,6 +214,38 @@ UAII_MOE_API int uaii_moe_experts_swiglu(uaii_moe_backend* b, const float* x, co
 UAII_MOE_API int uaii_moe_ffn_forward(uaii_moe_backend* b, const uaii_moe_layer* layer, const float* x,
                          int64_t T, float* y, float* probs);
 
+/* ---- GGUF files, packed loading.  A file is mapped read-only;
+ * header, metadata and tensor index are parsed once and tensor data is handed
+ * out as pointers into the mapping (no copy; pass them to
+ * uaii_moe_register_weights to upload once).  Replaces gguf_read_header /
+ * gguf_load_tensor_raw (libs/uaii-loaders/src/gguf.cpp:374-443, :558-602),
+ * which read the whole file into memory for the header and for every tensor.
+ * Shapes are outermost first (the reference's dims_to_shape, gguf.cpp:272-280);
+ * `fmt` is a uaii_moe_format, or -1 for tensor types without one (data NULL). */
+typedef struct uaii_moe_gguf uaii_moe_gguf;
+UAII_MOE_API int uaii_moe_gguf_open(const char* path, uaii_moe_gguf** out);
+UAII_MOE_API void uaii_moe_gguf_close(uaii_moe_gguf* g);
+UAII_MOE_API int64_t uaii_moe_gguf_tensor_count(const uaii_moe_gguf* g);
+/* shape holds up to 8 entries; any output pointer may be NULL. */
+UAII_MOE_API int uaii_moe_gguf_tensor_at(const uaii_moe_gguf* g, int64_t index, const char** name,
+                                         const void** data, int* fmt, int64_t* shape, int* rank, uint64_t* nbytes);
+UAII_MOE_API int uaii_moe_gguf_tensor(const uaii_moe_gguf* g, const char* name, const void** data, int* fmt,
+                                      int64_t* shape, int* rank, uint64_t* nbytes);
+/* Metadata: integer (any integer width, bool), number (integers and floats), string. */
+UAII_MOE_API int uaii_moe_gguf_kv_int(const uaii_moe_gguf* g, const char* key, int64_t* out);
+UAII_MOE_API int uaii_moe_gguf_kv_float(const uaii_moe_gguf* g, const char* key, double* out);
+UAII_MOE_API int uaii_moe_gguf_kv_string(const uaii_moe_gguf* g, const char* key, const char** out);
+/* The MoE FFN layer of block `block` as the reference's GGUF graph builds it
+ * (gguf.cpp:1078-1128): blk.N.ffn_gate_inp (f32 router), ffn_{gate,up,down}_exps,
+ * expert_count / expert_used_count from `{arch}.`, `llama.` or `general.` keys
+ * (top_k default 2, clamped to the expert count), renormalised top-k, and the
+ * ungated shared expert ffn_{gate,up,down}_shexp when present.  With flags &
+ * UAII_MOE_GGUF_SHEXP_GATE the shared expert is also gated by sigmoid(x .
+ * ffn_gate_inp_shexp) (Qwen2-MoE; the reference graph has no such gate).  The
+ * layer's pointers point into the mapping: keep the file open while it is used. */
+#define UAII_MOE_GGUF_SHEXP_GATE 1
+UAII_MOE_API int uaii_moe_gguf_moe_layer(const uaii_moe_gguf* g, int block, int flags, uaii_moe_layer* layer);
+
 /* Dense projection with a packed GGUF weight: y[M,N] = x[M,K] . dequant(w)^T,
  * w = N packed rows of K elements in w_fmt (any GGUF block format); relu != 0
  * applies max(y, 0) (the MatMulRelu op).  Replaces kernels::quant_gemm_f32

@@ -130,6 +130,8 @@ class Reference:
             "uref_moe_experts_swiglu": (c_int, [c_void_p] * 5 + [c_int64] * 4 + [c_int, c_void_p]),
             "uref_moe_experts_swiglu_mt": (c_int, [c_void_p] * 5 + [c_int64] * 4 + [c_int, c_void_p, c_int]),
             "uref_quant_gemm": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p]),
+            "uref_gguf_tensor_raw": (c_int64, [c_char_p, c_char_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
+            "uref_gguf_write_f32": (c_int, [c_char_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
         }
         for n, (r, a) in sig.items():
             f = getattr(L, n)
@@ -145,6 +147,27 @@ class Reference:
         c = np.empty((M, N), np.float32)
         self._chk(self.L.uref_quant_gemm(_p(a), M, K, _p(b_packed), fmt, N, _p(c)))
         return c
+
+    def gguf_tensor_raw(self, path: str, name: str, cap: int):
+        """(bytes, shape outermost first, ggml type) of one tensor through the reference loader."""
+        out = np.empty(cap, np.uint8)
+        shape = np.zeros(8, np.int64)
+        rank, typ = ctypes.c_int(), ctypes.c_int()
+        n = self.L.uref_gguf_tensor_raw(os.fsencode(path), name.encode(), _p(out), cap, _p(shape),
+                                        ctypes.addressof(rank), ctypes.addressof(typ))
+        if n < 0:
+            raise ValueError(f"reference gguf status {-n}: {self.L.uref_last_error().decode()}")
+        return out[:n].copy(), tuple(int(d) for d in shape[:rank.value]), typ.value
+
+    def gguf_write_f32(self, path: str, tensors):
+        """tensors: [(name, f32 array)] written by the reference's gguf_write_f32 (dims reversed as GGUF)."""
+        n = len(tensors)
+        names = (ctypes.c_char_p * n)(*[t[0].encode() for t in tensors])
+        ranks = (ctypes.c_int * n)(*[t[1].ndim for t in tensors])
+        dims = np.array([d for _, a in tensors for d in reversed(a.shape)], np.uint64)
+        arrs = [np.ascontiguousarray(a, np.float32) for _, a in tensors]
+        data = (ctypes.c_void_p * n)(*[a.ctypes.data for a in arrs])
+        self._chk(self.L.uref_gguf_write_f32(os.fsencode(path), n, names, ranks, _p(dims), data))
 
     def dequant(self, fmt, packed: np.ndarray, rows: int, cols: int, pitch: int) -> np.ndarray:
         out = np.empty((rows, cols), np.float32)

@@ -1,7 +1,7 @@
 // ref_shim.cpp -- extern "C" entry points over the reference's OWN compiled code.
 //
 // TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
-// twelve unmodified source files of the reference (arjun988/Universal-AI-Inference)
+// fifteen unmodified source files of the reference (arjun988/Universal-AI-Inference)
 // into oracle/_ref/libuaii_ref.so.  Nothing here re-implements the reference:
 // each function only builds the reference's TensorView arguments and calls
 //   uaii::quant::dequant_gguf_row      (libs/uaii-quant/src/gguf_dequant.cpp:420-439)
@@ -9,17 +9,22 @@
 //   uaii::kernels::moe_experts_swiglu_f32 (libs/uaii-kernels/src/transformer.cpp:522-612)
 //   uaii::kernels::matmul_f32          (libs/uaii-kernels/src/matmul.cpp:22-56)
 //   uaii::kernels::quant_gemm_f32      (libs/uaii-kernels/src/quant_gemm.cpp:22-70)
+//   uaii::loaders::gguf_read_header / gguf_load_tensor_raw / gguf_write_f32
+//                                      (libs/uaii-loaders/src/gguf.cpp:374-443, :558-650)
 // It is used by tests/ to pin oracle/moe_oracle.c, by tests/golden/make_golden.py
 // to produce fixtures, and by bench.py's reference arm as the timed CPU path.
 #include "uaii/kernels/kernels.hpp"
 #include "uaii/kernels/quant_gemm.hpp"
+#include "uaii/loaders/gguf.hpp"
 #include "uaii/quant/formats.hpp"
 #include "uaii/quant/gguf_dequant.hpp"
 
+#include <algorithm>
 #include <cstdint>
 #include <cstdlib>
 #include <string>
 #include <thread>
+#include <unordered_map>
 #include <vector>
 
 using uaii::DType;
@@ -89,6 +94,49 @@ int uref_quant_gemm(const float* a, std::int64_t M, std::int64_t K, const std::u
   vb.nbytes = static_cast<std::size_t>(N) *
               uaii::quant::packed_nbytes(vb.quant_format, static_cast<std::size_t>(K));
   return status(uaii::kernels::quant_gemm_f32(va, vb, &vc, true));
+}
+
+// One tensor of a GGUF file through the reference loader: header, then the raw bytes.
+// Returns the byte count (or -status); shape outermost first, type = ggml type.
+std::int64_t uref_gguf_tensor_raw(const char* path, const char* name, std::uint8_t* out, std::int64_t cap,
+                                  std::int64_t* shape, int* rank, int* type) {
+  uaii::loaders::GgufFile file;
+  uaii::Error e = uaii::loaders::gguf_read_header(path, &file);
+  if (!e.ok()) return -status(e);
+  std::vector<std::uint8_t> bytes;
+  uaii::Shape shp;
+  uaii::loaders::GgufType t{};
+  e = uaii::loaders::gguf_load_tensor_raw(file, name, &bytes, &shp, &t);
+  if (!e.ok()) return -status(e);
+  if ((std::int64_t)bytes.size() > cap) return -1;
+  std::copy(bytes.begin(), bytes.end(), out);
+  *rank = (int)shp.dims.size();
+  for (std::size_t i = 0; i < shp.dims.size() && i < 8; ++i) shape[i] = shp.dims[i];
+  *type = static_cast<int>(t);
+  return (std::int64_t)bytes.size();
+}
+
+// A GGUF file written by the reference's own writer: f32 tensors (dims innermost
+// first, as GGUF stores them) and two metadata keys.
+int uref_gguf_write_f32(const char* path, int n, const char* const* names, const int* ranks,
+                        const std::uint64_t* dims, const float* const* data) {
+  std::unordered_map<std::string, uaii::loaders::GgufValue> kv;
+  kv["general.architecture"] = std::string("llama");
+  kv["llama.expert_count"] = std::uint32_t{4};
+  std::vector<std::pair<uaii::loaders::GgufTensorInfo, std::vector<float>>> tensors;
+  std::size_t d0 = 0;
+  for (int i = 0; i < n; ++i) {
+    uaii::loaders::GgufTensorInfo info;
+    info.name = names[i];
+    std::size_t numel = 1;
+    for (int r = 0; r < ranks[i]; ++r) {
+      info.dims.push_back(dims[d0 + r]);
+      numel *= (std::size_t)dims[d0 + r];
+    }
+    d0 += (std::size_t)ranks[i];
+    tensors.emplace_back(info, std::vector<float>(data[i], data[i] + numel));
+  }
+  return status(uaii::loaders::gguf_write_f32(path, kv, tensors));
 }
 
 int uref_moe_experts_swiglu(const float* x, const float* G, const float* U, const float* Dn,

@@ -91,6 +91,17 @@ def _load():
         "uaii_moe_backend_stream": (c_int, [c_void_p, POINTER(c_void_p)]),
         "uaii_moe_quant_matmul": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int, c_int64, c_int,
                                           c_void_p]),
+        "uaii_moe_gguf_open": (c_int, [c_char_p, POINTER(c_void_p)]),
+        "uaii_moe_gguf_close": (None, [c_void_p]),
+        "uaii_moe_gguf_tensor_count": (c_int64, [c_void_p]),
+        "uaii_moe_gguf_tensor_at": (c_int, [c_void_p, c_int64, POINTER(c_char_p), POINTER(c_void_p), POINTER(c_int),
+                                            POINTER(c_int64), POINTER(c_int), POINTER(c_uint64)]),
+        "uaii_moe_gguf_tensor": (c_int, [c_void_p, c_char_p, POINTER(c_void_p), POINTER(c_int), POINTER(c_int64),
+                                         POINTER(c_int), POINTER(c_uint64)]),
+        "uaii_moe_gguf_kv_int": (c_int, [c_void_p, c_char_p, POINTER(c_int64)]),
+        "uaii_moe_gguf_kv_float": (c_int, [c_void_p, c_char_p, POINTER(c_double)]),
+        "uaii_moe_gguf_kv_string": (c_int, [c_void_p, c_char_p, POINTER(c_char_p)]),
+        "uaii_moe_gguf_moe_layer": (c_int, [c_void_p, c_int, c_int, c_void_p]),
         "uaii_moe_last_plan": (c_int, [c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
         "uaii_moe_ep_dispatch": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
@@ -122,7 +133,10 @@ EXPORTED = ("uaii_moe_abi_version", "uaii_moe_last_error", "uaii_moe_backend_cre
             "uaii_moe_experts_swiglu", "uaii_moe_ffn_forward", "uaii_moe_ffn_forward_noalloc",
             "uaii_moe_register_weights",
             "uaii_moe_release_weights",
-            "uaii_moe_set_expert_path", "uaii_moe_backend_stream", "uaii_moe_quant_matmul", "uaii_moe_last_plan", "uaii_moe_ep_dispatch", "uaii_moe_ep_experts",
+            "uaii_moe_set_expert_path", "uaii_moe_backend_stream", "uaii_moe_quant_matmul", "uaii_moe_last_plan",
+            "uaii_moe_gguf_open", "uaii_moe_gguf_close", "uaii_moe_gguf_tensor_count", "uaii_moe_gguf_tensor_at",
+            "uaii_moe_gguf_tensor", "uaii_moe_gguf_kv_int", "uaii_moe_gguf_kv_float", "uaii_moe_gguf_kv_string",
+            "uaii_moe_gguf_moe_layer", "uaii_moe_ep_dispatch", "uaii_moe_ep_experts",
             "uaii_moe_ep_combine", "uaii_moe_ep_dispatch_records", "uaii_moe_ep_experts_records",
             "uaii_moe_selftest_wait_timeout", "uaii_moe_profile_enable",
             "uaii_moe_profile_read",
@@ -326,6 +340,82 @@ def packed_desc(a, fmt: int, shape):
     """Packed GGUF expert tensor [E, rows, cols] (dtype Unknown, quant_format = fmt)."""
     rows = int(np.prod(shape[:-1]))
     return (DTYPE_UNKNOWN, fmt, tuple(shape), a, rows * packed_nbytes(fmt, shape[-1]))
+
+
+GGUF_SHEXP_GATE = 1
+
+
+class GgufFile:
+    """A GGUF file mapped read-only (uaii_moe_gguf_*).  Tensor data are numpy uint8
+    views into the mapping; layers and views stay valid while this object is open."""
+
+    def __init__(self, path: str):
+        h = c_void_p()
+        _check(lib.uaii_moe_gguf_open(os.fsencode(path), ctypes.byref(h)))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            lib.uaii_moe_gguf_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001
+            pass
+
+    def _info(self, getter, *args):
+        data, fmt, rank, nb = c_void_p(), c_int(), c_int(), c_uint64()
+        shape = (c_int64 * 8)()
+        _check(getter(self._h, *args, ctypes.byref(data), ctypes.byref(fmt), shape, ctypes.byref(rank),
+                      ctypes.byref(nb)))
+        return data.value, fmt.value, tuple(shape[i] for i in range(rank.value)), nb.value
+
+    def tensors(self):
+        """[(name, fmt, shape, nbytes)] in file order (fmt -1: type without a format)."""
+        out = []
+        for i in range(int(lib.uaii_moe_gguf_tensor_count(self._h))):
+            name = c_char_p()
+            data, fmt, shape, nb = self._info(lambda h, i_, *r: lib.uaii_moe_gguf_tensor_at(h, i_, ctypes.byref(name),
+                                                                                          *r), i)
+            out.append((name.value.decode(), fmt, shape, nb))
+        return out
+
+    def tensor(self, name: str):
+        """(numpy uint8 view of the packed bytes, fmt, shape)."""
+        data, fmt, shape, nb = self._info(lib.uaii_moe_gguf_tensor, name.encode())
+        if not data:
+            raise UaiiMoeError(NOT_IMPLEMENTED, f"{name}: tensor type without a format")
+        arr = np.ctypeslib.as_array((ctypes.c_uint8 * nb).from_address(data))
+        return arr, fmt, shape
+
+    def kv_int(self, key: str) -> int:
+        v = c_int64()
+        _check(lib.uaii_moe_gguf_kv_int(self._h, key.encode(), ctypes.byref(v)))
+        return v.value
+
+    def kv_float(self, key: str) -> float:
+        v = c_double()
+        _check(lib.uaii_moe_gguf_kv_float(self._h, key.encode(), ctypes.byref(v)))
+        return v.value
+
+    def kv_str(self, key: str) -> str:
+        v = c_char_p()
+        _check(lib.uaii_moe_gguf_kv_string(self._h, key.encode(), ctypes.byref(v)))
+        return v.value.decode()
+
+    def moe_layer(self, block: int, shexp_gate: bool = False) -> "Layer":
+        L = Layer()
+        _check(lib.uaii_moe_gguf_moe_layer(self._h, block, GGUF_SHEXP_GATE if shexp_gate else 0, ctypes.byref(L)))
+        L._keep = self  # the layer points into this mapping
+        return L
 
 
 def make_layer(D, E, I, top_k, norm_topk, router_w, gate, gfmt, up, ufmt, down, dfmt,
