@@ -67,6 +67,7 @@ def parse():
                     help="0 auto, 1 CUDA-core GEMV, 2 tcgen05 tensor-core GEMM, 3 warp-MMA tensor-core GEMM")
     ap.add_argument("--ep-chunks", type=int, default=1,
                     help="N > 1: token chunks whose exchanges overlap the previous chunk's experts")
+    ap.add_argument("--no-graphs", action="store_true", help="plain launches instead of CUDA-graph replay")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -267,6 +268,8 @@ def main():
     be = um.Backend(local, stream.cuda_stream)
     if args.path:
         be.set_expert_path(args.path)
+    if args.no_graphs:
+        be.set_graphs(False)
     # a serving process registers its (constant) weights once: layouts derived from them, such as
     # 16-byte-pitch copies of rows the tensor maps cannot address, are then made once, not per call
     for a in arrays.values():
@@ -304,7 +307,7 @@ def main():
     with ClockSampler(local) as clk:
         barrier()
         torch.cuda.synchronize()
-        be.profile_enable(True)
+        be.profile_enable(True)  # per-phase CUDA events inside the timed region (plain launches)
         ev0.record(stream)
         for _ in range(args.steps):
             forward(x, y)
@@ -314,6 +317,21 @@ def main():
         phases, launches = be.profile_read()
         be.profile_enable(False)
     ms = ev0.elapsed_time(ev1)
+    # Decode widths are launch-bound: the same steps replayed from the CUDA graph the library
+    # captures for repeated device-resident calls (phase events off), reported beside the value.
+    graph_replay = None
+    if not ep_mode and not args.no_graphs and T <= 64:
+        for _ in range(3):
+            forward(x, y)
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(args.steps):
+            forward(x, y)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gms = g0.elapsed_time(g1)
+        graph_replay = {"value": T * args.steps / (gms / 1e3), "unit": UNIT, "ms_per_step": gms / args.steps}
     plan = be.last_plan()
 
     def max_over_ranks(v: float) -> float:
@@ -412,7 +430,8 @@ def main():
                                            else f"replicas x{world}" if world > 1 else "1 GPU"),
                            "l2": "inputs larger than L2 (packed expert weights re-read every step)",
                            "experts_touched": touched},
-                "e2e": e2e, "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu,
+                "e2e": e2e, "gpu_launches": launches, "graph_replay": graph_replay, "roofline": roof,
+                "cpu_baseline": cpu,
                 "clocks": clk.summary(),
                 "phases_ms_per_step": {p: v[0] / args.steps for p, v in phases.items()}}
         print(json.dumps(line), flush=True)

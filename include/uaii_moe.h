@@ -153,6 +153,16 @@ UAII_MOE_API int uaii_moe_backend_create(int device, void* stream, uaii_moe_back
  * Replaces CudaBackend::shutdown (cuda_backend.cpp:68-78). */
 UAII_MOE_API void uaii_moe_backend_destroy(uaii_moe_backend* b);
 
+/* CUDA-graph replay of layer calls (default on): a uaii_moe_ffn_forward whose
+ * activations, outputs and weights are all device-resident (or registered)
+ * is captured into a CUDA graph the second time the same call (same shapes,
+ * pointers, schedule) is made and replayed from then on, so a decode loop pays
+ * one graph launch per layer instead of ~10 kernel launches.  Replays read the
+ * buffers' current contents.  Graphs are dropped when weights are registered
+ * or released, the schedule changes or the workspace grows.  No reference
+ * counterpart. */
+UAII_MOE_API int uaii_moe_set_graphs(uaii_moe_backend* b, int on);
+
 /* The CUDA stream (cudaStream_t) this backend queues its work on: the one given
  * to uaii_moe_backend_create, or the backend's own non-blocking stream when that
  * was NULL.  Callers that order other work against the backend's (collectives,

@@ -646,3 +646,33 @@ def test_layer_from_gguf_file_matches_arrays(backend, oracle, um, tmp_path):
     y_o, _, _ = oracle.experts_packed(x, w["gate"], um.Q4_K, w["up"], um.Q4_K, w["down"], um.Q8_0, pr, 4, 128, 2, 1)
     oracle.shared_packed(x, w["gs"], um.Q8_0, w["us"], um.Q8_0, w["ds"], um.Q8_0, None, 256, y_o)
     assert rel_err(y_ref, y_o) <= REL_TOL
+
+
+def test_graph_replay_matches_launches(backend, um):
+    # repeated device-resident calls are captured into a CUDA graph and replayed; replays read
+    # the buffers' current contents and give the same bits as plain launches
+    torch = pytest.importorskip("torch")
+    T, D, E, I, k = 3, 1024, 8, 2048, 2
+    x, w, G, U, Dn = layer_case(um, 14, 16, T, D, E, I, k, 44)
+    dev = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (w, G, U, Dn)]
+    L = um.make_layer(D, E, I, k, 1, dev[0], dev[1], um.Q4_K, dev[2], um.Q4_K, dev[3], um.Q6_K)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty((T, D), device="cuda")
+    backend.set_graphs(False)
+    try:
+        backend.ffn(L, xd, T, yd)
+        backend.synchronize()
+        y_plain = yd.cpu().numpy().copy()
+        xd2 = torch.from_numpy(um.fill_normal((T, D), 45, 1)).cuda()
+        backend.ffn(L, xd2, T, yd)
+        backend.synchronize()
+        y_plain2 = yd.cpu().numpy().copy()
+    finally:
+        backend.set_graphs(True)
+    xg = torch.empty_like(xd)
+    for i in range(5):  # plain, capture, replays
+        xg.copy_(xd if i % 2 == 0 else xd2)
+        torch.cuda.synchronize()
+        backend.ffn(L, xg, T, yd)
+        backend.synchronize()
+        assert bits_equal(yd.cpu().numpy(), y_plain if i % 2 == 0 else y_plain2), i

@@ -124,6 +124,7 @@ void MoeCudaBackend::shutdown() noexcept {
   }
   (void)cudaSetDevice(device_);
   if (stream_) (void)cudaStreamSynchronize(stream_);
+  drop_graphs();
   for (auto& kv : padded_) (void)cudaFree(kv.second.dev);
   padded_.clear();
   for (auto& kv : weights_) (void)cudaFree(kv.second);
@@ -170,6 +171,7 @@ Error MoeCudaBackend::reserve(size_t bytes) {
                                                        " bytes of scratch; the fixed scratch holds " +
                                                        std::to_string(ws_cap_));
   UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+  drop_graphs();  // captured launches point into the old workspace
   if (ws_) UAII_CUDA(cudaFree(ws_), "Free");
   ws_ = nullptr;
   ws_cap_ = 0;
@@ -294,6 +296,7 @@ Error MoeCudaBackend::register_weights(const void* p, size_t bytes) {
   std::lock_guard<std::mutex> lk(mu_);
   UAII_CUDA(cudaSetDevice(device_), "SetDevice");
   if (p == nullptr || bytes == 0) return Error::make(ErrorCode::InvalidArgument, "register_weights: empty buffer");
+  drop_graphs();  // calls that used the unregistered weights launched differently
   if (is_device_ptr(p)) {  // nothing to upload; layouts derived from it may be kept
     size_t& have = const_dev_[p];
     if (bytes > have) have = bytes;
@@ -314,6 +317,7 @@ Error MoeCudaBackend::register_weights(const void* p, size_t bytes) {
 
 Error MoeCudaBackend::release_weights(const void* host_ptr) {
   std::lock_guard<std::mutex> lk(mu_);
+  drop_graphs();  // captured launches may read the copies freed here
   bool found = false;
   for (auto it = weights_.begin(); it != weights_.end();) {
     if (it->first.first == host_ptr) {
@@ -981,6 +985,23 @@ Error MoeCudaBackend::experts(const float* x, const ExpertWeights& g, const Expe
   return Error::success();
 }
 
+void MoeCudaBackend::drop_graphs() {
+  for (auto& kv : graphs_)
+    if (kv.second.exec) (void)cudaGraphExecDestroy(kv.second.exec);
+  graphs_.clear();
+}
+
+// The launches of one layer forward (router, routing, expert GEMMs, combine).
+Error MoeCudaBackend::ffn_launch(const LayerArgs& L, const ExpertPlan& P, int64_t T, const float* xd, const float* wd,
+                                 float* logits, float* po, float* rscratch, size_t rsb, float* yo) {
+  phase_begin(kRouter);
+  UAII_CUDA(launch_router(xd, wd, T, L.D, L.E, logits, po, nullptr, stream_, rscratch, rsb), "router");
+  phase_end();
+  count_launches(2);
+  // Rank on the exact logits (same order as the probabilities), weight with probs.
+  return run_experts(xd, logits, po, L, P, T, yo);
+}
+
 Error MoeCudaBackend::ffn(const LayerArgs& Lin, const float* x, int64_t T, float* y, float* probs) {
   std::lock_guard<std::mutex> lk(mu_);
   UAII_CUDA(cudaSetDevice(device_), "SetDevice");
@@ -1009,16 +1030,48 @@ Error MoeCudaBackend::ffn(const LayerArgs& Lin, const float* x, int64_t T, float
   UAII_TRY(stage_weight(L.router_w, sizeof(float) * (size_t)(E * D), &wd));
   const bool ph = probs != nullptr && !is_device_ptr(probs);
   float* po = (probs && !ph) ? probs : ps;
-  phase_begin(kRouter);
-  UAII_CUDA(launch_router(static_cast<const float*>(xd), static_cast<const float*>(wd), T, D, E, logits,
-                          po, nullptr, stream_, rscratch, rsb),
-            "router");
-  phase_end();
-  count_launches(2);
   const bool yh = !is_device_ptr(y);
   float* yo = yh ? ys : y;
-  // Rank on the exact logits (same order as the probabilities), weight with probs.
-  UAII_TRY(run_experts(static_cast<const float*>(xd), logits, po, L, P, T, yo));
+  // Device-resident calls with device (or registered) weights are pure launch sequences:
+  // replayed from a CUDA graph once the same call has been seen twice.
+  const bool graphable = graphs_on_ && !profiling_ && !external_ && !xh && !yh && !ph && layer_stage_bytes(L) == 0;
+  GraphEntry* ge = nullptr;
+  if (graphable) {
+    const std::vector<int64_t> key = {
+        T, L.D, L.E, L.I, L.top_k, L.norm_topk, L.I_sh, path_,
+        (int64_t)(uintptr_t)x, (int64_t)(uintptr_t)y, (int64_t)(uintptr_t)probs, (int64_t)(uintptr_t)L.router_w,
+        (int64_t)(uintptr_t)L.gate.data, L.gate.fmt, (int64_t)(uintptr_t)L.up.data, L.up.fmt,
+        (int64_t)(uintptr_t)L.down.data, L.down.fmt, (int64_t)(uintptr_t)L.gate_sh.data, L.gate_sh.fmt,
+        (int64_t)(uintptr_t)L.up_sh.data, L.up_sh.fmt, (int64_t)(uintptr_t)L.down_sh.data, L.down_sh.fmt,
+        (int64_t)(uintptr_t)L.gate_inp_sh, (int64_t)(uintptr_t)ws_};
+    if (graphs_.size() >= 64 && !graphs_.count(key)) drop_graphs();  // bound the cache (varying batch sizes)
+    ge = &graphs_[key];
+    if (ge->exec) {
+      UAII_CUDA(cudaGraphLaunch(ge->exec, stream_), "GraphLaunch");
+      last_plan_ = P;
+      return Error::success();
+    }
+    if (ge->seen++ < 1) ge = nullptr;  // first sighting: plain launches (settles workspace and padded copies)
+  }
+  if (ge) {
+    UAII_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "StreamBeginCapture");
+    const Error e = ffn_launch(L, P, T, static_cast<const float*>(xd), static_cast<const float*>(wd), logits, po,
+                               rscratch, rsb, yo);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(stream_, &graph);
+    if (!e.ok()) {
+      if (graph) (void)cudaGraphDestroy(graph);
+      return e;
+    }
+    UAII_CUDA(ce, "StreamEndCapture");
+    const cudaError_t ie = cudaGraphInstantiate(&ge->exec, graph, 0);
+    (void)cudaGraphDestroy(graph);
+    UAII_CUDA(ie, "GraphInstantiate");
+    UAII_CUDA(cudaGraphLaunch(ge->exec, stream_), "GraphLaunch");
+    return Error::success();
+  }
+  UAII_TRY(ffn_launch(L, P, T, static_cast<const float*>(xd), static_cast<const float*>(wd), logits, po, rscratch,
+                      rsb, yo));
   bool any_host = false;
   if (yh) { UAII_CUDA(cudaMemcpyAsync(y, yo, xb, cudaMemcpyDeviceToHost, stream_), "D2H"); any_host = true; }
   if (ph) { UAII_CUDA(cudaMemcpyAsync(probs, po, pb, cudaMemcpyDeviceToHost, stream_), "D2H"); any_host = true; }
@@ -1257,6 +1310,12 @@ int uaii_moe_backend_create(int device, void* stream, uaii_moe_backend** out) {
 }
 
 void uaii_moe_backend_destroy(uaii_moe_backend* b) { delete b; }
+
+int uaii_moe_set_graphs(uaii_moe_backend* b, int on) {
+  if (!b) return no_backend();
+  b->impl.set_graphs(on != 0);
+  return report(Error::success());
+}
 
 int uaii_moe_backend_stream(uaii_moe_backend* b, void** stream) {
   if (!b) return no_backend();

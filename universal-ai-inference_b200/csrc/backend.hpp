@@ -133,7 +133,15 @@ class MoeCudaBackend {
   Error release_weights(const void* host_ptr);
   Error profile_enable(bool on);
   Error profile_read(double* ms, uint64_t* calls, uint64_t* launches);
-  void set_expert_path(int p) { path_ = p; }
+  void set_expert_path(int p) {
+    path_ = p;
+    drop_graphs();
+  }
+  // Replay repeated device-resident layer calls from CUDA graphs (default on).
+  void set_graphs(bool on) {
+    graphs_on_ = on;
+    if (!on) drop_graphs();
+  }
   // Schedule chosen by the most recent expert-product call (routed experts).
   ExpertPlan last_plan() const { return last_plan_; }
   cudaStream_t stream() const { return stream_; }
@@ -219,6 +227,17 @@ class MoeCudaBackend {
   // (source device rows, format, K, rows) -> copy with 16-byte row pitch, for constant sources
   std::map<std::tuple<const void*, int, int64_t, int64_t>, Padded> padded_;
   void drop_padded(const char* lo, const char* hi);
+  // CUDA graphs of device-resident layer calls, keyed by everything the launch sequence
+  // depends on: captured on the second identical call, replayed from the third.
+  struct GraphEntry {
+    int seen = 0;
+    cudaGraphExec_t exec = nullptr;
+  };
+  std::map<std::vector<int64_t>, GraphEntry> graphs_;
+  bool graphs_on_ = true;
+  void drop_graphs();
+  Error ffn_launch(const LayerArgs& L, const ExpertPlan& P, int64_t T, const float* xd, const float* wd, float* logits,
+                   float* po, float* rscratch, size_t rsb, float* yo);
   std::mutex mu_;
 };
 

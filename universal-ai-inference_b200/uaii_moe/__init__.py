@@ -89,6 +89,7 @@ def _load():
         "uaii_moe_release_weights": (c_int, [c_void_p, c_void_p]),
         "uaii_moe_set_expert_path": (c_int, [c_void_p, c_int]),
         "uaii_moe_backend_stream": (c_int, [c_void_p, POINTER(c_void_p)]),
+        "uaii_moe_set_graphs": (c_int, [c_void_p, c_int]),
         "uaii_moe_quant_matmul": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int, c_int64, c_int,
                                           c_void_p]),
         "uaii_moe_gguf_open": (c_int, [c_char_p, POINTER(c_void_p)]),
@@ -133,7 +134,7 @@ EXPORTED = ("uaii_moe_abi_version", "uaii_moe_last_error", "uaii_moe_backend_cre
             "uaii_moe_experts_swiglu", "uaii_moe_ffn_forward", "uaii_moe_ffn_forward_noalloc",
             "uaii_moe_register_weights",
             "uaii_moe_release_weights",
-            "uaii_moe_set_expert_path", "uaii_moe_backend_stream", "uaii_moe_quant_matmul", "uaii_moe_last_plan",
+            "uaii_moe_set_expert_path", "uaii_moe_set_graphs", "uaii_moe_backend_stream", "uaii_moe_quant_matmul", "uaii_moe_last_plan",
             "uaii_moe_gguf_open", "uaii_moe_gguf_close", "uaii_moe_gguf_tensor_count", "uaii_moe_gguf_tensor_at",
             "uaii_moe_gguf_tensor", "uaii_moe_gguf_kv_int", "uaii_moe_gguf_kv_float", "uaii_moe_gguf_kv_string",
             "uaii_moe_gguf_moe_layer", "uaii_moe_ep_dispatch", "uaii_moe_ep_experts",
@@ -217,6 +218,10 @@ class Backend:
 
     def set_expert_path(self, path: int):
         _check(lib.uaii_moe_set_expert_path(self._h, path))
+
+    def set_graphs(self, on: bool):
+        """CUDA-graph replay of repeated device-resident layer calls (default on)."""
+        _check(lib.uaii_moe_set_graphs(self._h, int(on)))
 
     def last_plan(self) -> dict:
         """Schedule of the most recent expert-product call: tensor cores or not,
