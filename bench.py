@@ -50,6 +50,8 @@ WORKLOAD_NOTE = {
 NCU_TRAFFIC = {
     ("mixtral_T32", "gateup"): 529084672 + 5518336,
     ("mixtral_T32", "down"): 398761984 + 4418304,
+    ("mixtral_T4096", "gateup"): 601846784 + 218835200,
+    ("mixtral_T4096", "down"): 930714112 + 116809728,
 }
 
 
