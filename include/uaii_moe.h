@@ -217,6 +217,16 @@ UAII_MOE_API int uaii_moe_experts_swiglu(uaii_moe_backend* b, const float* x, co
                             const void* down_exps, int down_fmt, const float* probs, int64_t T,
                             int64_t D, int64_t E, int64_t I, int top_k, int norm_topk, float* y);
 
+/* The token -> expert assignment the fused layer computes: router logits (the
+ * reference GEMM order) and probabilities, then the top-k experts of every
+ * token in rank order -- the selection of moe_experts_swiglu_f32
+ * (libs/uaii-kernels/src/transformer.cpp:564-580) applied to the router's
+ * output, ranked on the exact logits -- with their weights (renormalised when
+ * norm_topk).  topk_ids [T, top_k] int32, topk_w [T, top_k] f32; host or device
+ * memory.  Exposed so that callers and tests can check assignments bit for bit. */
+UAII_MOE_API int uaii_moe_route(uaii_moe_backend* b, const float* x, const float* gate_w, int64_t T, int64_t D,
+                                int64_t E, int top_k, int norm_topk, int32_t* topk_ids, float* topk_w);
+
 /* The whole MoE FFN layer (router + experts [+ shared expert]) in one call:
  * the MoERouter -> MoEExpertsSwiGLU node pair (and the shared-expert nodes) the
  * reference GGUF loader emits per layer (libs/uaii-loaders/src/gguf.cpp:1078-1128).

@@ -78,6 +78,18 @@ def test_config_full_size_vs_oracle(um, oracle, name, T, n_check):
     xs = np.ascontiguousarray(x[rows])
     _, pr, _ = oracle.router(xs, lw.router_w)
     assert _rel(probs[rows], pr) <= PROB_TOL
+    # token -> expert assignments of the whole batch, checked bit for bit on the sampled rows
+    ids = np.empty((T, cfg.top_k), np.int32)
+    wts = np.empty((T, cfg.top_k), np.float32)
+    be2 = um.Backend(0)
+    try:
+        be2.route(xd, arrays["router_w"], T, cfg.D, cfg.E, cfg.top_k, cfg.norm_topk, ids, wts)
+    finally:
+        be2.close()
+    for j, r in enumerate(rows):
+        ref_ids, ref_w = oracle.topk(pr[j], cfg.top_k, cfg.norm_topk)
+        assert np.array_equal(ids[r], ref_ids), (r, ids[r], ref_ids)
+        assert _rel(wts[r], ref_w) <= PROB_TOL
     y_ref, _, _ = oracle.experts_packed(xs, lw.gate, cfg.gate_fmt, lw.up, cfg.gate_fmt, lw.down, cfg.down_fmt, pr,
                                         cfg.E, cfg.I, cfg.top_k, cfg.norm_topk)
     if lw.shared is not None:

@@ -676,3 +676,22 @@ def test_graph_replay_matches_launches(backend, um):
         backend.ffn(L, xg, T, yd)
         backend.synchronize()
         assert bits_equal(yd.cpu().numpy(), y_plain if i % 2 == 0 else y_plain2), i
+
+
+@pytest.mark.parametrize("T,D,E,k", [(1, 64, 8, 2), (37, 256, 16, 4), (300, 512, 60, 4), (64, 2048, 128, 8)])
+def test_route_assignments_bitwise(backend, oracle, um, T, D, E, k):
+    # the fused layer's token -> expert assignment equals the reference procedure on the
+    # reference probabilities, including exact ties (duplicated router rows)
+    x = um.fill_normal((T, D), 50 + E, 1)
+    w = um.fill_normal((E, D), 50 + E, 2, 0.0, 0.05)
+    w[E // 2] = w[1]  # experts with identical logits: the heap procedure orders the tie
+    w[E - 1] = w[2]
+    for norm in (1, 0):
+        ids = np.empty((T, k), np.int32)
+        wts = np.empty((T, k), np.float32)
+        backend.route(x, w, T, D, E, k, norm, ids, wts)
+        _, pr, _ = oracle.router(x, w)
+        for t in range(T):
+            ref_ids, ref_w = oracle.topk(pr[t], k, norm)
+            assert np.array_equal(ids[t], ref_ids), (t, ids[t], ref_ids)
+            assert rel_err(wts[t], ref_w) <= 4e-7

@@ -385,6 +385,52 @@ Error MoeCudaBackend::dequant_rows(int fmt, const void* packed, int64_t rows, in
   return Error::success();
 }
 
+// The token -> expert assignment of the fused layer: router logits and probabilities, then the
+// top-k procedure ranking on the exact logits with weights from the probabilities (the
+// selection inside moe_experts_swiglu_f32, transformer.cpp:564-580).  ids [T, k] in rank order.
+Error MoeCudaBackend::route(const float* x, const float* gate_w, int64_t T, int64_t D, int64_t E, int k,
+                            int norm_topk, int32_t* ids, float* w) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaSetDevice(device_), "SetDevice");
+  if (T < 0 || D <= 0 || E <= 0 || k < 1 || k > 32 || k > E || E > 1024 || !x || !gate_w || !ids || !w)
+    return Error::make(ErrorCode::InvalidArgument, "moe route arguments");
+  if (T == 0) return Error::success();
+  const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E);
+  const size_t ib = sizeof(int32_t) * (size_t)(T * k), wb = sizeof(float) * (size_t)(T * k);
+  const size_t rsb = router_scratch_bytes(T, D, E);
+  UAII_TRY(reserve(align_up(xb) + 2 * align_up(pb) + 2 * align_up(ib) + 2 * align_up(wb) + align_up((size_t)(E * T)) +
+                   2 * align_up(sizeof(int32_t) * (size_t)(T * k)) + align_up(rsb) + 10 * kAlign +
+                   weight_stage_bytes(gate_w, sizeof(float) * (size_t)(E * D))));
+  void* xs = carve(xb);
+  float* logits = static_cast<float*>(carve(pb));
+  float* probs = static_cast<float*>(carve(pb));
+  RouteBuffers rb{};
+  rb.topk_ids = static_cast<int32_t*>(carve(ib));
+  rb.topk_w = static_cast<float*>(carve(wb));
+  rb.mask = static_cast<uint8_t*>(carve((size_t)(E * T)));
+  float* rscratch = rsb ? static_cast<float*>(carve(rsb)) : nullptr;
+  const void *xd = nullptr, *wd = nullptr;
+  bool xh = false;
+  UAII_TRY(stage_input(x, xb, xs, &xd, &xh));
+  UAII_TRY(stage_weight(gate_w, sizeof(float) * (size_t)(E * D), &wd));
+  const bool ih = !is_device_ptr(ids), wh = !is_device_ptr(w);
+  phase_begin(kRouter);
+  UAII_CUDA(launch_router(static_cast<const float*>(xd), static_cast<const float*>(wd), T, D, E, logits, probs, nullptr,
+                          stream_, rscratch, rsb),
+            "router");
+  phase_end();
+  phase_begin(kRoute);
+  UAII_CUDA(launch_route_topk(logits, probs, T, E, k, norm_topk, rb, stream_), "route_topk");
+  phase_end();
+  count_launches(3);
+  if (ih) UAII_CUDA(cudaMemcpyAsync(ids, rb.topk_ids, ib, cudaMemcpyDeviceToHost, stream_), "D2H");
+  else UAII_CUDA(cudaMemcpyAsync(ids, rb.topk_ids, ib, cudaMemcpyDeviceToDevice, stream_), "D2D");
+  if (wh) UAII_CUDA(cudaMemcpyAsync(w, rb.topk_w, wb, cudaMemcpyDeviceToHost, stream_), "D2H");
+  else UAII_CUDA(cudaMemcpyAsync(w, rb.topk_w, wb, cudaMemcpyDeviceToDevice, stream_), "D2D");
+  if (ih || wh) UAII_TRY(sync_and_check());
+  return Error::success();
+}
+
 Error MoeCudaBackend::router(const float* x, const float* gate_w, int64_t T, int64_t D,
                              int64_t E, float* probs, float* top, float* logits) {
   std::lock_guard<std::mutex> lk(mu_);
@@ -1310,6 +1356,12 @@ int uaii_moe_backend_create(int device, void* stream, uaii_moe_backend** out) {
 }
 
 void uaii_moe_backend_destroy(uaii_moe_backend* b) { delete b; }
+
+int uaii_moe_route(uaii_moe_backend* b, const float* x, const float* gate_w, int64_t T, int64_t D, int64_t E,
+                   int top_k, int norm_topk, int32_t* topk_ids, float* topk_w) {
+  if (!b) return no_backend();
+  return report(b->impl.route(x, gate_w, T, D, E, top_k, norm_topk, topk_ids, topk_w));
+}
 
 int uaii_moe_set_graphs(uaii_moe_backend* b, int on) {
   if (!b) return no_backend();

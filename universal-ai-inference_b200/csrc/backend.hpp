@@ -115,6 +115,9 @@ class MoeCudaBackend {
                 const ExpertWeights& d, const float* probs, int64_t T, int64_t D, int64_t E,
                 int64_t I, int top_k, int norm_topk, float* y);
   Error ffn(const LayerArgs& L, const float* x, int64_t T, float* y, float* probs);
+  // The fused layer's token -> expert assignment: ids [T, k] (rank order) and weights.
+  Error route(const float* x, const float* gate_w, int64_t T, int64_t D, int64_t E, int k, int norm_topk,
+              int32_t* ids, float* w);
   // y[M,N] = x[M,K] . dequant(W[N,K])^T (kernels::quant_gemm_f32), max(y, 0) with relu.
   Error quant_matmul(const float* x, int64_t M, int64_t K, const void* w, int fmt, int64_t N, float* y, bool relu);
 

@@ -90,6 +90,8 @@ def _load():
         "uaii_moe_set_expert_path": (c_int, [c_void_p, c_int]),
         "uaii_moe_backend_stream": (c_int, [c_void_p, POINTER(c_void_p)]),
         "uaii_moe_set_graphs": (c_int, [c_void_p, c_int]),
+        "uaii_moe_route": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int, c_void_p,
+                                   c_void_p]),
         "uaii_moe_quant_matmul": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int, c_int64, c_int,
                                           c_void_p]),
         "uaii_moe_gguf_open": (c_int, [c_char_p, POINTER(c_void_p)]),
@@ -134,7 +136,7 @@ EXPORTED = ("uaii_moe_abi_version", "uaii_moe_last_error", "uaii_moe_backend_cre
             "uaii_moe_experts_swiglu", "uaii_moe_ffn_forward", "uaii_moe_ffn_forward_noalloc",
             "uaii_moe_register_weights",
             "uaii_moe_release_weights",
-            "uaii_moe_set_expert_path", "uaii_moe_set_graphs", "uaii_moe_backend_stream", "uaii_moe_quant_matmul", "uaii_moe_last_plan",
+            "uaii_moe_set_expert_path", "uaii_moe_set_graphs", "uaii_moe_route", "uaii_moe_backend_stream", "uaii_moe_quant_matmul", "uaii_moe_last_plan",
             "uaii_moe_gguf_open", "uaii_moe_gguf_close", "uaii_moe_gguf_tensor_count", "uaii_moe_gguf_tensor_at",
             "uaii_moe_gguf_tensor", "uaii_moe_gguf_kv_int", "uaii_moe_gguf_kv_float", "uaii_moe_gguf_kv_string",
             "uaii_moe_gguf_moe_layer", "uaii_moe_ep_dispatch", "uaii_moe_ep_experts",
@@ -273,6 +275,10 @@ class Backend:
         _check(lib.uaii_moe_ffn_forward(self._h, ctypes.byref(layer), ptr(x), T, ptr(y), ptr(probs)))
 
     # ---- expert parallelism (device tensors; see include/uaii_moe.h)
+    def route(self, x, gate_w, T: int, D: int, E: int, k: int, norm_topk: int, ids, w):
+        """The fused layer's token -> expert assignment: ids [T, k] int32 in rank order, weights [T, k]."""
+        _check(lib.uaii_moe_route(self._h, ptr(x), ptr(gate_w), T, D, E, k, norm_topk, ptr(ids), ptr(w)))
+
     def quant_matmul(self, x, M: int, K: int, w, fmt: int, N: int, y, relu: bool = False):
         """y[M,N] = x[M,K] . dequant(w[N rows of K, fmt])^T (the MatMul op with a packed B)."""
         _check(lib.uaii_moe_quant_matmul(self._h, ptr(x), M, K, ptr(w), fmt, N, int(relu), ptr(y)))
