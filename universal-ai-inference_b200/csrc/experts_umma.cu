@@ -253,7 +253,9 @@ __device__ __forceinline__ void q6_k_atom(const uint8_t* row, int at, uint32_t* 
     for (int i = 0; i < 8; ++i) {
       // the 2-bit fields of quarter qt moved to bits 4-5 of every byte; bits 6-7
       // take neighbouring fields and are cleared together with the magic OR
-      const uint32_t hs = (hw[i] >> (2 * qt)) << 4;
+      // rotate so bits 2qt..2qt+1 of every byte land on bits 4-5 (one funnel shift; wrapped
+      // bits reach only bits 0-3, cleared below, and bits 6-7, dropped by the magic mask)
+      const uint32_t hs = __funnelshift_r(hw[i], hw[i], (uint32_t)(2 * qt + 28) & 31u);
       const uint32_t lo = lw[i] >> ns;
       const uint32_t q6 = (lo & 0x0F0F0F0Fu) | (hs & 0xF0F0F0F0u);  // one LOP3; bits 6-7 junk
       const __half2 s = i < 4 ? s_lo : s_hi;
@@ -968,8 +970,9 @@ template <> struct WmUnit<kQ8_0> {
 template <> struct WmUnit<kQ6_K> {
   struct Lane {
     int h, t;
-    uint32_t ns, hsh;
-    __device__ Lane(int h_, int t_) : h(h_), t(t_), ns(4u * (uint32_t)(t_ >> 1)), hsh(2u * (uint32_t)t_) {}
+    uint32_t ns, hrot;  // hrot: rotation taking bits 2t..2t+1 of every byte to bits 4-5
+    __device__ Lane(int h_, int t_)
+        : h(h_), t(t_), ns(4u * (uint32_t)(t_ >> 1)), hrot((2u * (uint32_t)t_ + 28u) & 31u) {}
   };
   uint32_t q6[8];  // 6-bit values in the low bits of each byte (bits 6-7: junk)
   __half2 s0, s1;
@@ -983,7 +986,7 @@ template <> struct WmUnit<kQ6_K> {
     load_words<OFF, 8>(row, 8 + 2 * L.h, w);  // qh bytes 128 + 32h ..
     // bits 6-7 of every byte carry junk from the neighbouring 2-bit fields; the 0x3F mask in pair() drops them
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q6[i] |= ((w[i] >> L.hsh) << 4) & 0xF0F0F0F0u;
+    for (int i = 0; i < 8; ++i) q6[i] |= __funnelshift_r(w[i], w[i], L.hrot) & 0xF0F0F0F0u;
     const __half2 s2 = q6k_scales(ld_u16(row + OFF + 208), ld_u16(row + OFF + 192 + 8 * L.h + 2 * L.t));
     s0 = __low2half2(s2);
     s1 = __high2half2(s2);
