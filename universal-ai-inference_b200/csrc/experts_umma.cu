@@ -561,7 +561,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // MMAs several times faster than a loop run by a single lane.
     {
       const int me = warp == 1 ? 0 : 1;  // takes the quads of every tile with local index % kIssuers == me
-      constexpr uint32_t idesc = idesc_f16_f32(128, BN);
       uint32_t sa = 0, pa = 0;  // A stage and its phase
       uint32_t sb = 0, pb = 0;  // B stage and its phase
       uint32_t sr = 0;          // release barrier
@@ -571,6 +570,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Tile t = decode_tile(args, tile, BN);
         int q0, q1;
         quad_range(t, q0, q1);
+        // MMA width: the tile's valid slots rounded up to 16 (the M = 128 minimum
+        // step), so an expert's last, partly filled slot tile costs only its columns.
+        // The epilogue stores only the valid slots; the columns left out are never read.
+        const int n_valid = min(BN, __ldg(args.counts + t.e) - t.n_tile * BN);
+        const uint32_t idesc = idesc_f16_f32(128, min(BN, max(16, (n_valid + 15) & ~15)));
         const uint32_t ab = it % C::kAccBufs;  // accumulator buffer of this tile
         if (!(ok = wait_bar(acc_empty + ab, ((it / C::kAccBufs) & 1) ^ 1, s_abort, err, kErrTimeoutMma, 2 UAII_WS_ARG)))
           break;
