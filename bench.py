@@ -119,22 +119,31 @@ class ClockSampler:
             self.err = f"NVML unavailable: {type(e).__name__}"
             return self
         self._stop = threading.Event()
+        self._nv, self._h = nv, h
 
         def run():
             while not self._stop.is_set():
-                try:
-                    self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
-                    mask = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                    for name, bit in self.REASONS.items():
-                        if mask & bit:
-                            self.reasons.add(name)
-                except Exception:  # noqa: BLE001
-                    pass
+                self.sample_now()
                 self._stop.wait(0.002)
 
         self._thread = threading.Thread(target=run, daemon=True)
         self._thread.start()
         return self
+
+    def sample_now(self):
+        """One reading (also called from the timing thread while queued work runs, so a
+        short timed region has at least one sample under load)."""
+        if self._stop is None:
+            return
+        nv, h = self._nv, self._h
+        try:
+            self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+            mask = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            for name, bit in self.REASONS.items():
+                if mask & bit:
+                    self.reasons.add(name)
+        except Exception:  # noqa: BLE001
+            pass
 
     def __exit__(self, *exc):
         if self._thread is not None:
@@ -314,6 +323,7 @@ def main():
         for _ in range(args.steps):
             forward(x, y)
         ev1.record(stream)
+        clk.sample_now()
         torch.cuda.synchronize()
         barrier()
         phases, launches = be.profile_read()
