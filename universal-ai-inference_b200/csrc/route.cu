@@ -249,6 +249,52 @@ __global__ void combine_kernel(const float* __restrict__ out, int64_t ld, int sp
   reinterpret_cast<float4*>(y + t * D)[c] = acc;
 }
 
+// combine_kernel for k <= KMAX: every entry's slot and weight first, then all k
+// row loads in flight together, then the same ordered sum (bit-identical).
+template <int KMAX>
+__global__ void combine_k_kernel(const float* __restrict__ out, int64_t ld, int splits, int64_t stride,
+                                 int64_t T, int64_t D, int k, RouteBuffers rb, const float* __restrict__ sh,
+                                 int sh_splits, int64_t sh_stride, const float* __restrict__ gate,
+                                 float* __restrict__ y) {
+  const int64_t d4 = D / 4;
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= T * d4) return;
+  const int64_t t = i / d4, c = i - t * d4;
+  int slot[KMAX];
+  float w[KMAX];
+#pragma unroll
+  for (int r = 0; r < KMAX; ++r) {
+    slot[r] = -1;
+    w[r] = 0.f;
+    if (r < k && rb.topk_ids[t * k + r] >= 0) {  // absent entries (expert-parallel rows) stay -1
+      slot[r] = rb.slot_of[t * k + r];
+      w[r] = rb.topk_w[t * k + r];
+    }
+  }
+  float4 o[KMAX];
+#pragma unroll
+  for (int r = 0; r < KMAX; ++r)
+    if (slot[r] >= 0) o[r] = sum_planes(out, ((int64_t)slot[r] * ld) / 4 + c, splits, stride);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int r = 0; r < KMAX; ++r) {
+    if (slot[r] < 0) continue;
+    acc.x = __fadd_rn(acc.x, __fmul_rn(w[r], o[r].x));
+    acc.y = __fadd_rn(acc.y, __fmul_rn(w[r], o[r].y));
+    acc.z = __fadd_rn(acc.z, __fmul_rn(w[r], o[r].z));
+    acc.w = __fadd_rn(acc.w, __fmul_rn(w[r], o[r].w));
+  }
+  if (sh) {
+    const float g = gate ? gate[t] : 1.0f;
+    const float4 s = sum_planes(sh, t * d4 + c, sh_splits, sh_stride);
+    acc.x = __fadd_rn(acc.x, __fmul_rn(g, s.x));
+    acc.y = __fadd_rn(acc.y, __fmul_rn(g, s.y));
+    acc.z = __fadd_rn(acc.z, __fmul_rn(g, s.z));
+    acc.w = __fadd_rn(acc.w, __fmul_rn(g, s.w));
+  }
+  reinterpret_cast<float4*>(y + t * D)[c] = acc;
+}
+
 __global__ void combine1_kernel(const float* __restrict__ out, int64_t ld, int splits, int64_t stride,
                                 int64_t T, int64_t D, int k, RouteBuffers rb, const float* __restrict__ sh,
                                 int sh_splits, int64_t sh_stride, const float* __restrict__ gate,
@@ -373,9 +419,17 @@ cudaError_t launch_combine(const float* out, int64_t out_ld, int splits, int64_t
     return cudaGetLastError();
   }
   const int64_t n = T * (D / 4);
-  combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(out, out_ld, splits, split_stride, T, D, k, rb,
-                                                              shared_out, sh_splits, sh_split_stride,
-                                                              shared_gate, y);
+  const unsigned blocks = (unsigned)((n + 255) / 256);
+#define UAII_COMBINE_K(KM)                                                                                  \
+  combine_k_kernel<KM><<<blocks, 256, 0, st>>>(out, out_ld, splits, split_stride, T, D, k, rb, shared_out, \
+                                               sh_splits, sh_split_stride, shared_gate, y)
+  if (k <= 2) UAII_COMBINE_K(2);
+  else if (k <= 4) UAII_COMBINE_K(4);
+  else if (k <= 8) UAII_COMBINE_K(8);
+  else
+    combine_kernel<<<blocks, 256, 0, st>>>(out, out_ld, splits, split_stride, T, D, k, rb, shared_out, sh_splits,
+                                           sh_split_stride, shared_gate, y);
+#undef UAII_COMBINE_K
   return cudaGetLastError();
 }
 
