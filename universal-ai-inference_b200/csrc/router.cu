@@ -151,19 +151,22 @@ constexpr int kRE = 8;  // experts per thread
 // Small batches split the row across blockIdx.z: each block then covers k tiles
 // [z*tpg, (z+1)*tpg) and writes the tile partials to `partials` (tile-major:
 // [nkt][T*E]) for router_fold_kernel, which adds them in tile order.
-template <int kRT>  // tokens per thread (4, 2 or 1: fewer when the batch is too small to fill the GPU)
+// kRT: tokens per thread; EG: expert groups (4, 8 or 16, dividing the 256 threads).  Both are
+// compile-time so that the staging index arithmetic is shifts and the k-step shared-memory
+// offsets are immediates.
+template <int kRT, int EG>
 __global__ void __launch_bounds__(256) router_block_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                           int64_t T, int64_t D, int64_t E, int EG,
+                                                           int64_t T, int64_t D, int64_t E,
                                                            float* __restrict__ logits, float* __restrict__ partials,
                                                            int tpg) {
   extern __shared__ float sm[];
-  const int TG = 256 / EG, TB = TG * kRT, EB = EG * kRE;
-  const int XS = TB + 4, WS = EB + 4;  // padded k rows
+  constexpr int TG = 256 / EG, TB = TG * kRT, EB = EG * kRE;
+  constexpr int XS = TB + 4, WS = EB + 4;  // padded k rows
   float* xs = sm;                      // [kTile][XS]
   float* ws = xs + kTile * XS;         // [kTile][WS]
   // Column of block expert r in a w row: experts 4..7 of every group after experts 0..3 of all
   // groups, so the 16-byte reads of one k step by all expert groups are contiguous.
-  auto wcol = [EB](int r) { return ((r & 7) >> 2) * (EB / 2) + (r >> 3) * 4 + (r & 3); };
+  auto wcol = [](int r) { return ((r & 7) >> 2) * (EB / 2) + (r >> 3) * 4 + (r & 3); };
   const int tid = threadIdx.x, eg = tid % EG, tg = tid / EG;  // EG divides 256: every thread has a group
   const int64_t t0 = (int64_t)blockIdx.x * TB, e0 = (int64_t)blockIdx.y * EB;
   float c[kRT][kRE];
@@ -463,7 +466,9 @@ cudaError_t launch_router(const float* x, const float* w, int64_t T, int64_t D, 
     attrs = true;
     (void)cudaFuncSetAttribute(router_token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     (void)cudaFuncSetAttribute(router_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    (void)cudaFuncSetAttribute(router_block_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    (void)cudaFuncSetAttribute(router_block_kernel<4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    (void)cudaFuncSetAttribute(router_block_kernel<4, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    (void)cudaFuncSetAttribute(router_block_kernel<4, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   }
   const size_t need = router_scratch_bytes(T, D, E);
   if (E >= 32 && (T >= 128 || (need && scratch && scratch_bytes >= need))) {
@@ -471,8 +476,11 @@ cudaError_t launch_router(const float* x, const float* w, int64_t T, int64_t D, 
     const bool split = p.groups > 0 && scratch && scratch_bytes >= need;
     const size_t smem = sizeof(float) * (size_t)(kTile * (p.TB + 4) + kTile * (p.eb + 4));
     dim3 grid((unsigned)p.tblocks, (unsigned)p.eblocks, split ? (unsigned)p.groups : 1u);
-    router_block_kernel<4><<<grid, 256, smem, st>>>(x, w, T, D, E, p.EG, logits, split ? scratch : nullptr,
-                                                    split ? p.tpg : 0);
+    float* part = split ? scratch : nullptr;
+    const int tpg = split ? p.tpg : 0;
+    if (p.EG == 4) router_block_kernel<4, 4><<<grid, 256, smem, st>>>(x, w, T, D, E, logits, part, tpg);
+    else if (p.EG == 8) router_block_kernel<4, 8><<<grid, 256, smem, st>>>(x, w, T, D, E, logits, part, tpg);
+    else router_block_kernel<4, 16><<<grid, 256, smem, st>>>(x, w, T, D, E, logits, part, tpg);
     if (split) {
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return e;
