@@ -142,6 +142,26 @@ def test_ep_emulated_ranks_qwen3_formats(um, backend):
     _emulated(um, backend, D=256, E=16, I=256, k=4, gf=um.Q4_0, df=um.Q4_0, R=4, T=64, seed=7)
 
 
+@pytest.mark.parametrize("R,D", [(2, 512), (4, 512), (8, 256), (12, 128), (4, 6)])
+def test_ep_combine_rank_order_bitwise(um, backend, R, D):
+    # y[t] = sum over d = 0..R-1 of y_back[row_of[t, d]] (rows that exist), f32 adds in rank order
+    _need_gpu()
+    T = 37
+    rng = np.random.default_rng(R * 100 + D)
+    row_of = np.where(rng.random((T, R)) < 0.4, -1, 0).astype(np.int32)
+    n = int((row_of >= 0).sum())
+    row_of[row_of >= 0] = rng.permutation(n)
+    y_back = (rng.standard_normal((n, D)) * 3).astype(np.float32)
+    ref = np.zeros((T, D), np.float32)
+    for d in range(R):
+        m = row_of[:, d] >= 0
+        ref[m] = ref[m] + y_back[row_of[m, d]]
+    y = torch.full((T, D), float("nan"), device="cuda")
+    backend.ep_combine(_dev(y_back), _dev(row_of), T, R, D, y)
+    torch.cuda.synchronize()
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
 def test_ep_dispatch_rejects_bad_world(um, backend):
     _need_gpu()
     D, E, I, k, T = 256, 6, 128, 2, 4

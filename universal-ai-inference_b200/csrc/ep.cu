@@ -155,6 +155,34 @@ __global__ void ep_combine_kernel(const float* __restrict__ y_back, const int32_
   y[i] = acc;
 }
 
+// ep_combine_kernel on float4 columns for R <= RMAX: a token's row indices first, then
+// all its row loads in flight together, then the same rank-ordered sum (bit-identical).
+template <int RMAX>
+__global__ void ep_combine4_kernel(const float* __restrict__ y_back, const int32_t* __restrict__ row_of,
+                                   int64_t T, int R, int64_t D, float* __restrict__ y) {
+  const int64_t d4 = D / 4;
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= T * d4) return;
+  const int64_t t = i / d4, c = i - t * d4;
+  int row[RMAX];
+#pragma unroll
+  for (int d = 0; d < RMAX; ++d) row[d] = d < R ? row_of[t * R + d] : -1;
+  float4 v[RMAX];
+#pragma unroll
+  for (int d = 0; d < RMAX; ++d)
+    if (row[d] >= 0) v[d] = reinterpret_cast<const float4*>(y_back + (int64_t)row[d] * D)[c];
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int d = 0; d < RMAX; ++d) {
+    if (row[d] < 0) continue;
+    acc.x = __fadd_rn(acc.x, v[d].x);
+    acc.y = __fadd_rn(acc.y, v[d].y);
+    acc.z = __fadd_rn(acc.z, v[d].z);
+    acc.w = __fadd_rn(acc.w, v[d].w);
+  }
+  reinterpret_cast<float4*>(y + t * D)[c] = acc;
+}
+
 }  // namespace
 
 cudaError_t launch_ep_plan(const int32_t* topk_ids, int64_t T, int k, int R, int epr, uint8_t* dmask,
@@ -217,7 +245,12 @@ cudaError_t launch_route_gather16(const void* rows, int64_t N, int64_t D, int64_
 cudaError_t launch_ep_combine(const float* y_back, const int32_t* row_of, int64_t T, int R, int64_t D, float* y,
                               cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  ep_combine_kernel<<<(unsigned)((T * D + 255) / 256), 256, 0, st>>>(y_back, row_of, T, R, D, y);
+  const bool vec = D % 4 == 0 && ((reinterpret_cast<uintptr_t>(y_back) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  const unsigned blocks4 = (unsigned)((T * (D / 4) + 255) / 256);
+  if (vec && R <= 2) ep_combine4_kernel<2><<<blocks4, 256, 0, st>>>(y_back, row_of, T, R, D, y);
+  else if (vec && R <= 4) ep_combine4_kernel<4><<<blocks4, 256, 0, st>>>(y_back, row_of, T, R, D, y);
+  else if (vec && R <= 8) ep_combine4_kernel<8><<<blocks4, 256, 0, st>>>(y_back, row_of, T, R, D, y);
+  else ep_combine_kernel<<<(unsigned)((T * D + 255) / 256), 256, 0, st>>>(y_back, row_of, T, R, D, y);
   return cudaGetLastError();
 }
 
