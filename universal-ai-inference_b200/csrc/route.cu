@@ -199,9 +199,15 @@ __global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int6
       if (xp32) reinterpret_cast<float4*>(xp32 + (int64_t)slot * D)[i] = v;
       if (xp16) {  // elements (4i, 4i+2) and (4i+1, 4i+3) land on adjacent pairs in both orders
         __half* row = xp16 + (int64_t)slot * D;
-        const int64_t p0 = wm_order ? wm_kpos(4 * i) : 4 * i, p1 = wm_order ? p0 + 8 : p0 + 2;
-        *reinterpret_cast<__half2*>(row + p0) = __floats2half2_rn(v.x, v.z);
-        *reinterpret_cast<__half2*>(row + p1) = __floats2half2_rn(v.y, v.w);
+        const __half2 lo = __floats2half2_rn(v.x, v.z), hi = __floats2half2_rn(v.y, v.w);
+        if (wm_order) {
+          const int64_t p0 = wm_kpos(4 * i);
+          *reinterpret_cast<__half2*>(row + p0) = lo;
+          *reinterpret_cast<__half2*>(row + p0 + 8) = hi;
+        } else {  // tc_kpos: the pairs sit at 4i and 4i + 2, one 8-byte store (D % 4 == 0)
+          *reinterpret_cast<uint2*>(row + 4 * i) =
+              make_uint2(reinterpret_cast<const uint32_t&>(lo), reinterpret_cast<const uint32_t&>(hi));
+        }
       }
     }
   }

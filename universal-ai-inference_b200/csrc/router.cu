@@ -153,7 +153,10 @@ constexpr int kRE = 8;  // experts per thread
 // [nkt][T*E]) for router_fold_kernel, which adds them in tile order.
 // kRT: tokens per thread; EG: expert groups (4, 8 or 16, dividing the 256 threads).  Both are
 // compile-time so that the staging index arithmetic is shifts and the k-step shared-memory
-// offsets are immediates.
+// offsets are immediates.  Block x owns tokens [x*T/gridDim.x, (x+1)*T/gridDim.x) (at most TB:
+// the grid has at least ceil(T/TB) blocks), so a grid sized to whole waves of resident blocks
+// spreads the tokens evenly; warps whose tokens all lie past the block's range skip the
+// arithmetic.
 template <int kRT, int EG>
 __global__ void __launch_bounds__(256) router_block_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                            int64_t T, int64_t D, int64_t E,
@@ -168,7 +171,9 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
   // groups, so the 16-byte reads of one k step by all expert groups are contiguous.
   auto wcol = [](int r) { return ((r & 7) >> 2) * (EB / 2) + (r >> 3) * 4 + (r & 3); };
   const int tid = threadIdx.x, eg = tid % EG, tg = tid / EG;  // EG divides 256: every thread has a group
-  const int64_t t0 = (int64_t)blockIdx.x * TB, e0 = (int64_t)blockIdx.y * EB;
+  const int64_t t0 = (int64_t)blockIdx.x * T / gridDim.x, e0 = (int64_t)blockIdx.y * EB;
+  const int tn = (int)((int64_t)(blockIdx.x + 1) * T / gridDim.x - t0);  // tokens of this block (<= TB)
+  const bool idle = (tid >> 5) * (32 / EG) * kRT >= tn;                  // warp-uniform
   float c[kRT][kRE];
 #pragma unroll
   for (int a = 0; a < kRT; ++a)
@@ -185,8 +190,8 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
     if (vec && kn == kTile) {  // float4 loads, transposed into k-major rows; lanes take consecutive rows
       for (int i = tid; i < TB * (kTile / 4); i += 256) {  // so that the transposed stores hit distinct banks
         const int k4 = i / TB, r = i - k4 * TB;
-        const float4 v = (t0 + r < T) ? __ldg(reinterpret_cast<const float4*>(x + (t0 + r) * D + k0) + k4)
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 v = r < tn ? __ldg(reinterpret_cast<const float4*>(x + (t0 + r) * D + k0) + k4)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
         xs[(4 * k4) * XS + r] = v.x; xs[(4 * k4 + 1) * XS + r] = v.y;
         xs[(4 * k4 + 2) * XS + r] = v.z; xs[(4 * k4 + 3) * XS + r] = v.w;
       }
@@ -201,7 +206,7 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
     } else {
       for (int i = tid; i < TB * kTile; i += 256) {
         const int k = i / TB, r = i - k * TB;
-        xs[k * XS + r] = (t0 + r < T && k < kn) ? __ldg(x + (t0 + r) * D + k0 + k) : 0.f;
+        xs[k * XS + r] = (r < tn && k < kn) ? __ldg(x + (t0 + r) * D + k0 + k) : 0.f;
       }
       for (int i = tid; i < EB * kTile; i += 256) {
         const int k = i / EB, r = i - k * EB;
@@ -233,7 +238,8 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
 #pragma unroll
         for (int b = 0; b < kRE; ++b) sacc[a][b] = __fadd_rn(sacc[a][b], __fmul_rn(xa[a], wv[b]));
     };
-    if (kn == kTile) {  // full tile: unrolled, shared-memory offsets become immediates
+    if (idle) {
+    } else if (kn == kTile) {  // full tile: unrolled, shared-memory offsets become immediates
 #pragma unroll 4
       for (int k = 0; k < kTile; ++k) kstep(k);
     } else {
@@ -246,7 +252,7 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
 #pragma unroll
         for (int b = 0; b < kRE; ++b) {
           const int64_t e = e0 + eg * kRE + b;
-          if (t < T && e < E) partials[(int64_t)j * T * E + t * E + e] = sacc[a][b];
+          if (tg * kRT + a < tn && e < E) partials[(int64_t)j * T * E + t * E + e] = sacc[a][b];
         }
       }
       continue;
@@ -260,7 +266,7 @@ __global__ void __launch_bounds__(256) router_block_kernel(const float* __restri
 #pragma unroll
   for (int a = 0; a < kRT; ++a) {
     const int64_t t = t0 + tg * kRT + a;
-    if (t >= T) continue;
+    if (tg * kRT + a >= tn) continue;
 #pragma unroll
     for (int b = 0; b < kRE; ++b) {
       const int64_t e = e0 + eg * kRE + b;
@@ -462,20 +468,43 @@ cudaError_t launch_router(const float* x, const float* w, int64_t T, int64_t D, 
   const size_t token_smem = sizeof(float) * (size_t)(D + E * nkt);
   const size_t chunk_smem = sizeof(float) * (size_t)(kTB * kXS + kEC * kXS + kTB * kEC * kJC + kTB * E);
   static bool attrs = false;
-  if (!attrs) {
+  static int block_slots[3] = {0, 0, 0};  // resident block-schedule blocks on the GPU, per EG = 4, 8, 16
+  if (!attrs) {  // first call: before any stream capture of a layer call
     attrs = true;
     (void)cudaFuncSetAttribute(router_token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     (void)cudaFuncSetAttribute(router_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     (void)cudaFuncSetAttribute(router_block_kernel<4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     (void)cudaFuncSetAttribute(router_block_kernel<4, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     (void)cudaFuncSetAttribute(router_block_kernel<4, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess) {
+      const void* fns[3] = {reinterpret_cast<const void*>(router_block_kernel<4, 4>),
+                            reinterpret_cast<const void*>(router_block_kernel<4, 8>),
+                            reinterpret_cast<const void*>(router_block_kernel<4, 16>)};
+      for (int i = 0; i < 3; ++i) {
+        const int eg = 4 << i, tb = (256 / eg) * 4, eb = eg * kRE;
+        const size_t sm_bytes = sizeof(float) * (size_t)(kTile * (tb + 4) + kTile * (eb + 4));
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fns[i], 256, sm_bytes) == cudaSuccess)
+          block_slots[i] = per_sm * sms;
+      }
+    }
+    (void)cudaGetLastError();
   }
   const size_t need = router_scratch_bytes(T, D, E);
   if (E >= 32 && (T >= 128 || (need && scratch && scratch_bytes >= need))) {
     const BlockPlan p = block_plan(T, D, E);
     const bool split = p.groups > 0 && scratch && scratch_bytes >= need;
     const size_t smem = sizeof(float) * (size_t)(kTile * (p.TB + 4) + kTile * (p.eb + 4));
-    dim3 grid((unsigned)p.tblocks, (unsigned)p.eblocks, split ? (unsigned)p.groups : 1u);
+    // token blocks: whole waves of resident blocks, the tokens spread evenly over them
+    int64_t bx = p.tblocks;
+    const int64_t slots = block_slots[p.EG == 4 ? 0 : p.EG == 8 ? 1 : 2];
+    if (!split && slots > 0) {
+      const int64_t waves = (p.tblocks * p.eblocks + slots - 1) / slots;
+      const int64_t want = (waves * slots + p.eblocks - 1) / p.eblocks;
+      if (want > bx) bx = want < T ? want : T;
+    }
+    dim3 grid((unsigned)bx, (unsigned)p.eblocks, split ? (unsigned)p.groups : 1u);
     float* part = split ? scratch : nullptr;
     const int tpg = split ? p.tpg : 0;
     if (p.EG == 4) router_block_kernel<4, 4><<<grid, 256, smem, st>>>(x, w, T, D, E, logits, part, tpg);
