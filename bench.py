@@ -207,6 +207,51 @@ def cpu_sample_tokens(cfg, T: int) -> int:
     return max(1, min(T, n))
 
 
+PARITY_TOL = 2e-3  # max |y - y_ref| / max |y_ref| over the checked rows (the layer-output bar)
+
+
+def parity_rows(cfg, probs: np.ndarray, seed: int) -> np.ndarray:
+    """A seeded sample of this rank's tokens whose top-k choices cover every expert the
+    tokens reach (greedy over a seeded permutation), plus four random rows; bounded to about
+    20 s of oracle work."""
+    T = probs.shape[0]
+    per_row_s = 2 * 3 * cfg.D * (cfg.I * cfg.top_k + cfg.I_sh) / 1.0e9
+    cap = int(max(4, min(64, 20.0 / per_row_s)))
+    ids = np.argsort(-probs, axis=1, kind="stable")[:, :cfg.top_k]
+    reach = set(np.unique(ids).tolist())
+    rng = np.random.default_rng(seed)
+    order = rng.permutation(T)
+    rows, covered = [], set()
+    for t in order:
+        new = set(ids[t].tolist()) - covered
+        if new:
+            rows.append(int(t))
+            covered |= new
+        if covered == reach or len(rows) >= cap - 4:
+            break
+    extra = [int(t) for t in order[-4:] if int(t) not in rows]
+    return np.array(sorted(rows + extra[: max(0, cap - len(rows))]), np.int64)
+
+
+def parity_check(cfg, lw, x: np.ndarray, y: np.ndarray, probs: np.ndarray, seed: int) -> dict:
+    """The device layer output on sampled rows against the oracle (the C restatement pinned to
+    the reference build), run on the same seeded inputs: a check, never part of the timing."""
+    from oracle.oracle import Oracle
+    O = Oracle()
+    rows = parity_rows(cfg, probs, seed)
+    xs = np.ascontiguousarray(x[rows])
+    _, pr, _ = O.router(xs, lw.router_w)
+    y_ref, ids, _ = O.experts_packed(xs, lw.gate, cfg.gate_fmt, lw.up, cfg.gate_fmt, lw.down, cfg.down_fmt, pr,
+                                     cfg.E, cfg.I, cfg.top_k, cfg.norm_topk)
+    if lw.shared is not None:
+        g, u, d, gi = lw.shared
+        O.shared_packed(xs, g, cfg.shared_fmt, u, cfg.shared_fmt, d, cfg.shared_fmt, gi, cfg.I_sh, y_ref)
+    err = float(np.abs(y[rows].astype(np.float64) - y_ref).max() / max(float(np.abs(y_ref).max()), 1e-30))
+    return {"rows": int(len(rows)), "experts_covered": int(len(np.unique(ids))), "max_rel": err,
+            "bar": PARITY_TOL, "oracle": "oracle/moe_oracle.c (pinned to the reference build)",
+            "_experts": np.unique(ids)}
+
+
 # ------------------------------------------------------------------ main
 
 def main():
@@ -214,17 +259,20 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    from uaii_moe.synthetic import CONFIGS, algorithmic_bytes, flops, make_layer_weights, make_tokens
-    cfg = CONFIGS[args.config]
     T = args.tokens if args.scaling == "weak" else args.tokens // max(1, int(os.environ.get("WORLD_SIZE", "1")))
     workload = f"{args.config}_T{args.tokens}" + ("" if args.scaling == "weak" else "_total")
 
     if args.impl == "reference":
         if rank != 0:
             return 0
-        lw = make_layer_weights(cfg)
+        # Inputs from the numpy restatement of the library's seeded generator and quantizer
+        # (byte-identical, pinned by tests/test_oracle.py): this process loads the reference
+        # build only, never the product library.
+        from oracle.synth import CONFIGS as SYNTH_CONFIGS, make_layer, make_tokens as synth_tokens
+        cfg = SYNTH_CONFIGS[args.config]
+        lw = make_layer(cfg, workers=min(16, os.cpu_count() or 1))
         n = cpu_sample_tokens(cfg, T)
-        xs = make_tokens(cfg, n, 0)
+        xs = synth_tokens(cfg, n, 0)
         tps, cores, kind = cpu_reference_run(cfg, lw, xs, args.steps, args.warmup)
         line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": args.scaling,
@@ -240,6 +288,8 @@ def main():
 
     import torch
     import uaii_moe as um
+    from uaii_moe.synthetic import CONFIGS, make_layer_weights, make_tokens
+    cfg = CONFIGS[args.config]
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
@@ -305,6 +355,21 @@ def main():
     ids = torch.topk(probs, cfg.top_k, dim=1).indices
     touched = int(torch.unique(ids).numel())
     local_entries = ep.last_exchange[2] if ep_mode else T * cfg.top_k
+    # correctness of this rank's output before anything is timed (every rank, every N): sampled
+    # rows covering every expert its tokens reach, against the oracle; a miss fails the run
+    parity = parity_check(cfg, lw, x_host.numpy(), y.cpu().numpy(), probs.cpu().numpy(), 777 + rank)
+    covered = torch.zeros(cfg.E, dtype=torch.float64, device="cuda")
+    covered[torch.from_numpy(parity.pop("_experts").astype(np.int64)).cuda()] = 1.0
+    if dist is not None:  # worst error, all checked rows and the experts they reach, over all ranks
+        worst = torch.tensor([parity["max_rel"]], dtype=torch.float64, device="cuda")
+        nrows = torch.tensor([float(parity["rows"])], dtype=torch.float64, device="cuda")
+        dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+        dist.all_reduce(nrows, op=dist.ReduceOp.SUM)
+        dist.all_reduce(covered, op=dist.ReduceOp.MAX)
+        parity["max_rel"] = float(worst.item())
+        parity["rows"] = int(nrows.item())
+        parity["ranks"] = world
+    parity["experts_covered"] = int(covered.sum().item())
 
     for _ in range(args.warmup):
         forward(x, y)
@@ -445,12 +510,16 @@ def main():
                 "e2e": e2e, "gpu_launches": launches, "graph_replay": graph_replay, "roofline": roof,
                 "cpu_baseline": cpu,
                 "clocks": clk.summary(),
-                "phases_ms_per_step": {p: v[0] / args.steps for p, v in phases.items()}}
+                "phases_ms_per_step": {p: v[0] / args.steps for p, v in phases.items()},
+                "parity": parity}
         print(json.dumps(line), flush=True)
     be.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+    if not parity["max_rel"] <= PARITY_TOL:
+        print(f"bench: parity check failed: max_rel {parity['max_rel']:.3e} > {PARITY_TOL}", file=sys.stderr)
+        return 1
     return 0
 
 

@@ -298,10 +298,18 @@ UAII_MOE_API int uaii_moe_register_weights(uaii_moe_backend* b, const void* host
  * cudaStream_t, NULL for the default stream) and the call returns after it has
  * finished.  The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress), so make it before any stream capture.  A call that
- * needs more than 32 MiB of scratch returns UAII_MOE_INVALID_ARGUMENT.  All
+ * needs more than 32 MiB of scratch returns UAII_MOE_INVALID_ARGUMENT: routing
+ * tables, f16 activations, hidden activations and partial sums grow with T, so
+ * this serves decode-sized batches (the Mixtral-shaped layer needs ~140 KB per
+ * token: up to about 200 tokens), not large prefill batches.  Weights whose packed rows are not a
+ * multiple of 16 bytes (e.g. Q8_0 rows of 1408 elements, the Qwen2-MoE down
+ * projection) are copied with a 16-byte row pitch on every call, and that copy
+ * is carved from the same 32 MiB, so such layers fit only when their padded
+ * copy does (the Qwen2-MoE down stack needs ~180 MB and never fits).  All
  * calls share the array; calls are serialized inside one process because
- * overlapping GPU work on it would race.  No reference counterpart: the
- * reference runs this operator only on the host. */
+ * overlapping GPU work on it would race.  The device current on entry is
+ * current again on return.  No reference counterpart: the reference runs this
+ * operator only on the host. */
 UAII_MOE_API int uaii_moe_ffn_forward_noalloc(int device, void* stream, const uaii_moe_layer* layer,
                                               const float* x, int64_t T, float* y, float* probs);
 

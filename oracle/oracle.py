@@ -131,6 +131,7 @@ class Reference:
             "uref_moe_experts_swiglu_mt": (c_int, [c_void_p] * 5 + [c_int64] * 4 + [c_int, c_void_p, c_int]),
             "uref_quant_gemm": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p]),
             "uref_gguf_tensor_raw": (c_int64, [c_char_p, c_char_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
+            "uref_gguf_tensor_f32": (c_int64, [c_char_p, c_char_p, c_void_p, c_int64]),
             "uref_gguf_write_f32": (c_int, [c_char_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
         }
         for n, (r, a) in sig.items():
@@ -158,6 +159,15 @@ class Reference:
         if n < 0:
             raise ValueError(f"reference gguf status {-n}: {self.L.uref_last_error().decode()}")
         return out[:n].copy(), tuple(int(d) for d in shape[:rank.value]), typ.value
+
+    def gguf_tensor_f32(self, path: str, name: str, n: int) -> np.ndarray:
+        """One tensor dequantized at load time by the reference loader (gguf_load_tensor_f32),
+        as the reference Session does with its default options."""
+        out = np.empty(n, np.float32)
+        got = self.L.uref_gguf_tensor_f32(os.fsencode(path), name.encode(), _p(out), n)
+        if got < 0:
+            raise ValueError(f"reference gguf status {-got}: {self.L.uref_last_error().decode()}")
+        return out[:got].copy()
 
     def gguf_write_f32(self, path: str, tensors):
         """tensors: [(name, f32 array)] written by the reference's gguf_write_f32 (dims reversed as GGUF)."""

@@ -9,8 +9,8 @@
 //   uaii::kernels::moe_experts_swiglu_f32 (libs/uaii-kernels/src/transformer.cpp:522-612)
 //   uaii::kernels::matmul_f32          (libs/uaii-kernels/src/matmul.cpp:22-56)
 //   uaii::kernels::quant_gemm_f32      (libs/uaii-kernels/src/quant_gemm.cpp:22-70)
-//   uaii::loaders::gguf_read_header / gguf_load_tensor_raw / gguf_write_f32
-//                                      (libs/uaii-loaders/src/gguf.cpp:374-443, :558-650)
+//   uaii::loaders::gguf_read_header / gguf_load_tensor_f32 / gguf_load_tensor_raw /
+//   gguf_write_f32                     (libs/uaii-loaders/src/gguf.cpp:374-650)
 // It is used by tests/ to pin oracle/moe_oracle.c, by tests/golden/make_golden.py
 // to produce fixtures, and by bench.py's reference arm as the timed CPU path.
 #include "uaii/kernels/kernels.hpp"
@@ -114,6 +114,22 @@ std::int64_t uref_gguf_tensor_raw(const char* path, const char* name, std::uint8
   for (std::size_t i = 0; i < shp.dims.size() && i < 8; ++i) shape[i] = shp.dims[i];
   *type = static_cast<int>(t);
   return (std::int64_t)bytes.size();
+}
+
+// A tensor as the reference's Session loads it by default: gguf_load_tensor_f32,
+// the load-time dequantization (libs/uaii-loaders/src/gguf.cpp:445-556).  Returns
+// the element count, or minus the status.
+std::int64_t uref_gguf_tensor_f32(const char* path, const char* name, float* out, std::int64_t cap) {
+  uaii::loaders::GgufFile file;
+  uaii::Error e = uaii::loaders::gguf_read_header(path, &file);
+  if (!e.ok()) return -status(e);
+  std::vector<float> vals;
+  uaii::Shape shp;
+  e = uaii::loaders::gguf_load_tensor_f32(file, name, &vals, &shp);
+  if (!e.ok()) return -status(e);
+  if ((std::int64_t)vals.size() > cap) return -1;
+  std::copy(vals.begin(), vals.end(), out);
+  return (std::int64_t)vals.size();
 }
 
 // A GGUF file written by the reference's own writer: f32 tensors (dims innermost

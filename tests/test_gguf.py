@@ -9,7 +9,8 @@ import os
 import numpy as np
 import pytest
 
-from gguf_writer import (ARRAY, F32, GGML_F32, GGML_I32, GGML_Q4_K, GGML_Q8_0, STRING, U32, as_bytes,
+from gguf_writer import (ARRAY, F32, GGML_F32, GGML_I32, GGML_Q4_0, GGML_Q4_K, GGML_Q6_K, GGML_Q8_0, STRING, U32,
+                         as_bytes,
                          write_gguf)
 
 D, E, I, ISH = 256, 4, 128, 256
@@ -127,3 +128,33 @@ def test_gguf_reads_reference_writer_output(um, reference, tmp_path):
             view, fmt, shape = g.tensor(name)
             assert fmt == um.F32 and shape == arr.shape
             assert np.array_equal(view.view(np.float32).reshape(arr.shape), arr)
+
+
+def test_reference_session_q4_0_load_order_differs_by_interleave(um, reference, oracle, tmp_path):
+    """Pins the reference discrepancy this library records and does not replicate: the
+    stock Session dequantizes Q4_0 at load time with gguf_load_tensor_f32, which writes the
+    two nibbles of byte j to elements 2j and 2j+1 (libs/uaii-loaders/src/gguf.cpp:514-520),
+    while dequant_gguf_row -- the GGUF/ggml order this library and the oracle follow -- puts
+    them at j and j+16 (libs/uaii-quant/src/gguf_dequant.cpp:126-131).  Both run here
+    through the reference build; they must differ by exactly that permutation.  Q8_0 and
+    the K-quants load identically through both routes."""
+    rows, cols = 6, 256
+    src = um.fill_normal((rows, cols), 3, 1, 0.0, 0.02)
+    path = str(tmp_path / "q.gguf")
+    tensors = []
+    packed = {}
+    for fmt, gt in ((um.Q4_0, GGML_Q4_0), (um.Q8_0, GGML_Q8_0), (um.Q4_K, GGML_Q4_K), (um.Q6_K, GGML_Q6_K)):
+        packed[fmt] = um.quantize_rows(fmt, src)
+        tensors.append((f"t{fmt}", gt, (rows, cols), packed[fmt].tobytes()))
+    write_gguf(path, [("general.architecture", STRING, "llama")], tensors)
+    for fmt in packed:
+        loaded = reference.gguf_tensor_f32(path, f"t{fmt}", rows * cols).reshape(rows, cols)
+        row_order = reference.dequant(fmt, packed[fmt], rows, cols, packed[fmt].shape[1])
+        assert np.array_equal(row_order, oracle.dequant(fmt, packed[fmt], rows, cols))
+        if fmt != um.Q4_0:
+            assert np.array_equal(loaded.view(np.uint32), row_order.view(np.uint32)), fmt
+            continue
+        assert not np.array_equal(loaded, row_order)
+        blocks = row_order.reshape(-1, 2, 16)            # [block][lo/hi nibble][byte j]
+        interleaved = blocks.transpose(0, 2, 1).reshape(rows, cols)  # element 2j = lo(j), 2j+1 = hi(j)
+        assert np.array_equal(loaded.view(np.uint32), interleaved.view(np.uint32))

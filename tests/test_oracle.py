@@ -180,3 +180,50 @@ def test_quant_gemm_vs_reference(oracle, reference, um, fmt):
     assert bits_equal(c, reference.quant_gemm(a, b, fmt, N))
     r = oracle.quant_gemm(a, b, fmt, N, relu=True)
     assert bits_equal(r, np.where(c > 0, c, np.float32(0.0)).astype(np.float32))  # relu_f32: x > 0 ? x : 0
+
+
+# ---- the numpy input synthesizer used by bench.py's reference arm (oracle/synth.py)
+
+@pytest.mark.parametrize("shape,seed,stream,mean,std", [
+    ((3, 5001), 42, 7, 0.0, 1.0), ((1 << 20,), 1, 1000, 0.0, 0.02), ((77,), 3, 50, 0.5, 2.0)])
+def test_synth_fill_normal_matches_library(um, shape, seed, stream, mean, std):
+    from oracle import synth
+    a = um.fill_normal(shape, seed, stream, mean, std)
+    b = synth.fill_normal(shape, seed, stream, mean, std)
+    # numpy's double log/sin/cos may differ from the C library's in the last bit; after rounding
+    # to f32 that changes (almost) nothing: at most 1 in 1e5 values, by one f32 ulp
+    diff = a.view(np.uint32).astype(np.int64) - b.view(np.uint32).astype(np.int64)
+    assert np.abs(diff).max() <= 1 and np.count_nonzero(diff) <= max(1, a.size // 100000)
+
+
+@pytest.mark.parametrize("fmt_name", ["Q4_0", "Q8_0", "Q4_K", "Q6_K"])
+def test_synth_quantizer_matches_library(um, fmt_name):
+    from oracle import synth
+    fmt = getattr(um, fmt_name)
+    src = um.fill_normal((300, 1024), 5, 9, 0.0, 0.02)
+    src[3, :40] = 0.0                                       # all-zero blocks
+    src[4, 256:512] = 1e-9                                  # f16-subnormal scales
+    src[5, :] = 70000.0 * (np.arange(1024) % 3 - 1)         # f16-overflowing scales
+    src[6, :] = -np.abs(src[6, :])                          # one-signed blocks
+    assert np.array_equal(um.quantize_rows(fmt, src), synth.quantize_rows(fmt, src))
+
+
+def test_synth_configs_and_layer_match_library(um):
+    from oracle import synth
+    from uaii_moe.synthetic import CONFIGS, make_layer_weights, make_tokens
+    assert set(synth.CONFIGS) == set(CONFIGS)
+    for name, c in synth.CONFIGS.items():
+        p = CONFIGS[name]
+        for f in ("D", "E", "I", "top_k", "gate_fmt", "down_fmt", "norm_topk", "I_sh", "shared_fmt",
+                  "shared_gate", "routing", "seed"):
+            assert getattr(c, f) == getattr(p, f), (name, f)
+    # a whole (small) layer with skewed routing and a gated shared expert, byte for byte
+    import dataclasses
+    small = synth.Config("t", 256, 6, 256, 2, synth.Q8_0, synth.Q4_K, norm_topk=0, I_sh=512,
+                         shared_fmt=synth.Q4_0, shared_gate=True, routing="zipf1.1", seed=5)
+    ours = make_layer_weights(type(CONFIGS["mixtral"])(**dataclasses.asdict(small)))
+    theirs = synth.make_layer(small)
+    for a, b in [(ours.router_w, theirs.router_w), (ours.gate, theirs.gate), (ours.up, theirs.up),
+                 (ours.down, theirs.down)] + list(zip(ours.shared, theirs.shared)):
+        assert np.array_equal(a, b)
+    assert np.array_equal(make_tokens(CONFIGS["qwen3_hot"], 9, 2), synth.make_tokens(synth.CONFIGS["qwen3_hot"], 9, 2))

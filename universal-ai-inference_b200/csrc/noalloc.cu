@@ -18,7 +18,8 @@
 // looks the address up with cudaGetSymbolAddress (with that device current)
 // and keeps it for later calls, so that first call should come before any
 // stream capture.  Calls that need more scratch than the array holds are
-// rejected with UAII_MOE_INVALID_ARGUMENT before any work is queued.
+// rejected with UAII_MOE_INVALID_ARGUMENT before any work is queued.  The
+// device that was current when the call began is current again when it returns.
 //
 // Every call shares the array and finds the previous call's leftovers in it:
 // the error flag and the expert routing mask are cleared on each call and
@@ -58,6 +59,20 @@ Error scratch_address(int device, void** out) {
 
 bool on_device_or_null(const void* p) { return p == nullptr || is_device_ptr(p); }
 
+// Makes `device` current for the call and gives the caller back the device that
+// was current before, on every return path.
+struct DeviceGuard {
+  int prev = -1;
+  cudaError_t st = cudaSuccess;
+  explicit DeviceGuard(int device) {
+    st = cudaGetDevice(&prev);
+    if (st == cudaSuccess) st = cudaSetDevice(device);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) (void)cudaSetDevice(prev);
+  }
+};
+
 }  // namespace
 }  // namespace uaii_b200
 
@@ -68,8 +83,8 @@ extern "C" int uaii_moe_ffn_forward_noalloc(int device, void* stream, const uaii
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (layer == nullptr || x == nullptr || y == nullptr)
     return report_status(Error::make(ErrorCode::InvalidArgument, "noalloc ffn: null argument"));
-  cudaError_t st = cudaSetDevice(device);
-  if (st != cudaSuccess) return report_status(cuda_status(st, "SetDevice"));
+  DeviceGuard dg(device);
+  if (dg.st != cudaSuccess) return report_status(cuda_status(dg.st, "SetDevice"));
   LayerArgs L;
   if (!layer_args_from_c(layer, &L))
     return report_status(Error::make(ErrorCode::InvalidArgument, "noalloc ffn: null expert weights"));
