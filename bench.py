@@ -66,7 +66,8 @@ def parse():
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="weak: --tokens per GPU; strong: --tokens in total, split across the GPUs")
     ap.add_argument("--path", type=int, default=0,
-                    help="0 auto, 1 CUDA-core GEMV, 2 tcgen05 tensor-core GEMM, 3 warp-MMA tensor-core GEMM")
+                    help="0 auto, 1 CUDA-core GEMV, 2 tcgen05 tensor-core GEMM, 3 warp-MMA tensor-core GEMM "
+                         "(whole super-blocks for K-quants), 4 warp-MMA with one 32-element unit per lane")
     ap.add_argument("--ep-chunks", type=int, default=1,
                     help="N > 1: token chunks whose exchanges overlap the previous chunk's experts")
     ap.add_argument("--no-graphs", action="store_true", help="plain launches instead of CUDA-graph replay")
@@ -476,7 +477,9 @@ def main():
         roof["frac_sustained"] = roof["achieved"] / roof["peak_sustained"]
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["traffic"] = NCU_TRAFFIC.get((workload, dom))
-    sched = {"tcgen05": "tcgen05", "warp_mma": "warp-level mma.sync m16n8k16"}.get(plan.get("schedule"), "tcgen05")
+    sched = {"tcgen05": "tcgen05", "warp_mma": "warp-level mma.sync m16n8k16",
+             "quad_mma": "warp-level mma.sync m16n8k16 over whole K-quant super-blocks"}.get(plan.get("schedule"),
+                                                                                           "tcgen05")
     path = (f"tensor-core grouped dequant-GEMM ({sched}, f16 operands, f32 accumulate), "
             f"{plan['slot_tile']}-slot tiles") if plan["tensor_cores"] else "CUDA-core f32 grouped GEMV"
     roof["kernel"] = f"{dom} phase: {path}"

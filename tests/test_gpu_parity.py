@@ -419,14 +419,51 @@ def test_warp_mma_path_vs_oracle(backend, oracle, um, gf, df, T, D, E, I, k):
         plan = backend.last_plan()
     finally:
         backend.set_expert_path(0)
-    assert plan["schedule"] == "warp_mma" and plan["slot_tile"] in (8, 16)
+    kquant = gf in (14, 16) and df in (14, 16)
+    assert plan["schedule"] == ("quad_mma" if kquant else "warp_mma") and plan["slot_tile"] in (8, 16)
     assert rel_err(y, y_ref) <= REL_TOL
+
+
+@pytest.mark.parametrize("gf,df,T,D,E,I,k", [
+    (14, 16, 1, 1024, 8, 2048, 2),     # Mixtral formats: Q6_K windows at all eight 16-byte offsets
+    (14, 16, 60, 512, 8, 1024, 2),     # 16-slot tiles
+    (16, 14, 5, 512, 4, 768, 2),       # Q6_K gate/up, Q4_K down; three quads per down row (odd)
+    (14, 14, 9, 768, 6, 512, 3),       # Q4_K only, three quads per gate/up row
+    (16, 16, 3, 256, 4, 512, 2),       # one quad per gate/up row: the odd-quad warps idle; padded pitch
+    (14, 16, 20, 512, 32, 512, 8),     # many experts, top-8
+    (14, 16, 300, 256, 4, 256, 2),     # forced far above decode widths: many 16-slot tiles per expert
+])
+def test_quad_schedule_vs_oracle_and_unit_schedule(backend, oracle, um, gf, df, T, D, E, I, k):
+    """The warp-MMA schedule over whole K-quant super-blocks: against the oracle within the
+    layer bar, and against the per-unit warp-MMA schedule (path 4).  Q4_K enters the quad
+    schedule's products unrounded (q*sc exact in f16, d and dmin in f32) where the other
+    schedules round fp16(d*sc*q - dmin*m); Q6_K operands are the same values."""
+    x, w, G, U, Dn = layer_case(um, gf, df, T, D, E, I, k, 300 + T)
+    _, pr, _ = oracle.router(x, w)
+    y_ref, _, _ = oracle.experts_packed(x, G, gf, U, gf, Dn, df, pr, E, I, k, 1)
+    L = um.make_layer(D, E, I, k, 1, w, G, gf, U, gf, Dn, df)
+    ys = {}
+    for path in (3, 4):
+        y = np.empty_like(x)
+        backend.set_expert_path(path)
+        try:
+            backend.ffn(L, x, T, y)
+            ys[path] = (y, backend.last_plan())
+        finally:
+            backend.set_expert_path(0)
+    assert ys[3][1]["schedule"] == "quad_mma" and ys[4][1]["schedule"] == "warp_mma"
+    err_quad, err_unit = rel_err(ys[3][0], y_ref), rel_err(ys[4][0], y_ref)
+    assert err_quad <= REL_TOL
+    # no less accurate than the per-unit schedule (Q4_K: more accurate, its weights are unrounded)
+    assert err_quad <= 1.25 * max(err_unit, 1e-4), (err_quad, err_unit)
+    if gf == 16 and df == 16:  # identical Q6_K operands: only the f32 summation order differs
+        assert rel_err(ys[3][0], ys[4][0]) <= 1e-4
 
 
 def test_automatic_schedule_picks_warp_mma_for_decode(backend, um):
     D, E, I, k = 1024, 8, 2048, 2
     # tiles hold the mean slots per expert plus two standard deviations below 32 slots
-    for T, sched, tile in ((1, "warp_mma", 8), (8, "warp_mma", 8), (32, "tcgen05", 16), (64, "tcgen05", 32),
+    for T, sched, tile in ((1, "quad_mma", 8), (8, "quad_mma", 8), (32, "tcgen05", 16), (64, "tcgen05", 32),
                            (512, "tcgen05", 128)):
         x, w, G, U, Dn = layer_case(um, 14, 16, T, D, E, I, k, 5)
         y = np.empty_like(x)
@@ -441,7 +478,7 @@ def test_warp_mma_and_tcgen05_agree(backend, um):
     x, w, G, U, Dn = layer_case(um, 14, 16, T, D, E, I, k, 8)
     L = um.make_layer(D, E, I, k, 1, w, G, 14, U, 14, Dn, 16)
     ys = []
-    for path in (2, 3):
+    for path in (2, 4):
         y = np.empty_like(x)
         backend.set_expert_path(path)
         try:
@@ -695,3 +732,31 @@ def test_route_assignments_bitwise(backend, oracle, um, T, D, E, k):
             ref_ids, ref_w = oracle.topk(pr[t], k, norm)
             assert np.array_equal(ids[t], ref_ids), (t, ids[t], ref_ids)
             assert rel_err(wts[t], ref_w) <= 4e-7
+
+
+@pytest.mark.parametrize("T", [4096, 7000])
+def test_ffn_host_buffers_in_overlapped_chunks(backend, oracle, um, T):
+    """Host x and y with device-resident weights: the batch runs in chunks of at least 2048
+    tokens whose host copies overlap the neighbouring chunks' layer work.  Token rows are
+    independent, so the probabilities must equal the one-shot device call bit for bit and
+    the outputs must agree within f32 regrouping (a chunk's plan may pick other down-
+    projection splits, which regroups f32 sums); sampled rows are checked against the oracle."""
+    D, E, I, k = 1024, 8, 1024, 2
+    x, w, G, U, Dn = layer_case(um, 14, 16, T, D, E, I, k, 21)
+    xd, wd, Gd, Ud, Dd = (dev(a) for a in (x, w, G, U, Dn))
+    Ld = um.make_layer(D, E, I, k, 1, wd, Gd, 14, Ud, 14, Dd, 16)
+    y_dev = torch.empty((T, D), device="cuda")
+    p_dev = torch.empty((T, E), device="cuda")
+    backend.ffn(Ld, xd, T, y_dev, p_dev)
+    backend.synchronize()
+    xh = torch.from_numpy(x).pin_memory()
+    yh = torch.full((T, D), float("nan")).pin_memory()
+    ph = torch.full((T, E), float("nan")).pin_memory()
+    for _ in range(2):  # the second call finds the first call's streams and staging in place
+        backend.ffn(Ld, xh, T, yh, ph)
+        assert bits_equal(ph.numpy(), p_dev.cpu().numpy())
+        assert rel_err(yh.numpy(), y_dev.cpu().numpy()) <= 1e-5
+    rows = np.sort(np.random.default_rng(T).choice(T, size=6, replace=False))
+    _, pr, _ = oracle.router(np.ascontiguousarray(x[rows]), w)
+    y_ref, _, _ = oracle.experts_packed(np.ascontiguousarray(x[rows]), G, 14, U, 14, Dn, 16, pr, E, I, k, 1)
+    assert rel_err(yh.numpy()[rows], y_ref) <= REL_TOL

@@ -19,6 +19,7 @@
 
 #include "../../include/uaii_moe.h"
 #include "gguf_format.hpp"
+#include "operand_order.cuh"
 
 namespace uaii_b200 {
 
@@ -139,6 +140,11 @@ void MoeCudaBackend::shutdown() noexcept {
   ws_cap_ = ws_used_ = 0;
   if (dev_err_) (void)cudaFree(dev_err_);
   dev_err_ = nullptr;
+  for (auto e : chunk_events_) (void)cudaEventDestroy(e);
+  chunk_events_.clear();
+  if (in_stream_) (void)cudaStreamDestroy(in_stream_);
+  if (out_stream_) (void)cudaStreamDestroy(out_stream_);
+  in_stream_ = out_stream_ = nullptr;
   if (own_stream_ && stream_) (void)cudaStreamDestroy(stream_);
   stream_ = nullptr;
   device_ = -1;
@@ -504,7 +510,7 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t s
   const bool umma_ok = umma_shapes_supported(L.gate.fmt, L.down.fmt, L.D, L.I);
   const bool warp_ok = allow_warp_mma && warp_mma_shapes_supported(L.gate.fmt, L.down.fmt, L.D, L.I);
   p.umma = path_ != 1 && umma_ok;
-  p.umma_refused = (path_ == 2 && !umma_ok) || (path_ == 3 && allow_warp_mma && !warp_ok);
+  p.umma_refused = (path_ == 2 && !umma_ok) || ((path_ == 3 || path_ == 4) && allow_warp_mma && !warp_ok);
   // Slots an expert's tile must hold: the mean plus two standard deviations of a
   // Poisson count at small means (an expert just above a tile width costs a second
   // pass over its weights), the mean at large ones (half-empty tiles cost MMA time).
@@ -515,7 +521,9 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t s
   };
   // warp-MMA use: forced (path 3), never (paths 1, 2), or (path 0) when 8-slot tiles
   // hold every expert's slots -- measured faster than tcgen05 there, slower at 16 slots
-  auto use_warp = [&](bool ok, double tpe) { return ok && (path_ == 3 || (path_ == 0 && need(tpe) <= 8)); };
+  auto use_warp = [&](bool ok, double tpe) {
+    return ok && (path_ == 3 || path_ == 4 || (path_ == 0 && need(tpe) <= 8));
+  };
   auto warp_bn = [&](double tpe) { return need(tpe) <= 8 ? 8 : 16; };
   auto pick_splits = pick_down_splits;
   const int64_t active = S < L.E ? S : L.E;
@@ -524,6 +532,8 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t s
   if (p.umma) {
     p.warp_mma = use_warp(warp_ok, tpe);
     if (p.warp_mma) p.bn = warp_bn(tpe);
+    // K-quant layers run the warp schedule over whole super-blocks (path 4 keeps the per-unit one)
+    p.quad_mma = p.warp_mma && path_ != 4 && quad_mma_format(L.gate.fmt) && quad_mma_format(L.down.fmt);
     const int64_t n_tiles = (int64_t)((tpe + p.bn - 1) / p.bn);
     p.splits = pick_splits(active * n_tiles * (L.D / 128), umma_kchunks(L.down.fmt, L.I));
   }
@@ -532,7 +542,7 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t s
     p.sh_bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
     if (p.sh_umma) {
       p.sh_warp_mma = warp_mma_shapes_supported(L.gate_sh.fmt, L.down_sh.fmt, L.D, L.I_sh) &&
-                      (path_ == 3 || (path_ == 0 && T <= 8));
+                      (path_ == 3 || path_ == 4 || (path_ == 0 && T <= 8));
       if (p.sh_warp_mma) p.sh_bn = T <= 8 ? 8 : 16;  // the shared expert owns every token: no spread
       p.sh_splits = pick_splits(((T + p.sh_bn - 1) / p.sh_bn) * (L.D / 128), umma_kchunks(L.down_sh.fmt, L.I_sh));
     }
@@ -622,6 +632,10 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
   }
   UAII_CUDA(launch_route_scan(T, E, k, rb, stream_), "route_scan");
   if (P.umma) {
+    // operand orders: x in the gate/up kernel's, h in the down kernel's (operand_order.cuh)
+    const int sched = P.quad_mma ? kSchedQuadMma : P.warp_mma ? kSchedWarpMma : kSchedTcgen05;
+    const int x_order = P.quad_mma ? (L.gate.fmt == kQ4_K ? kOrderQ4K : kOrderQ6K) : P.warp_mma ? kOrderWm : kOrderTc;
+    const int h_order = P.quad_mma ? (L.down.fmt == kQ4_K ? kOrderQ4K : kOrderQ6K) : P.warp_mma ? kOrderWm : kOrderTc;
     void* xp16 = carve(2 * (size_t)(S * D));
     void* h16 = carve(2 * (size_t)(S * I));
     splits = P.splits;
@@ -630,7 +644,7 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
       if (P.warp_mma) return Error::make(ErrorCode::Internal, "expert-parallel rows planned on the warp-MMA schedule");
       UAII_CUDA(launch_route_gather16(ep->x16, T, D, E, k, rb, xp16, stream_, ep->x_pitch), "route_gather16");
     } else {
-      UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, nullptr, xp16, stream_, P.warp_mma), "route_gather");
+      UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, nullptr, xp16, stream_, x_order), "route_gather");
     }
     phase_end();
     count_launches(3);
@@ -641,12 +655,12 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
     UAII_TRY(umma_rows(dd, L.down.fmt, E * D, I, weight_is_constant(L.down.data, expert_bytes(L.down, E)), &dd,
                        &dpitch));
     UAII_CUDA(launch_gateup_umma(L.gate.fmt, gd, ud, gpitch, E, I, D, xp16, S, rb.counts, rb.offsets, tile_base, P.bn,
-                                 h16, dev_err_, stream_, P.warp_mma),
+                                 h16, dev_err_, stream_, sched, h_order),
               "gateup(tensor cores)");
     phase_end();
     phase_begin(kDown);
     UAII_CUDA(launch_down_umma(L.down.fmt, dd, dpitch, E, D, I, h16, S, rb.counts, rb.offsets, tile_base, P.bn, splits,
-                               out, dev_err_, stream_, P.warp_mma),
+                               out, dev_err_, stream_, sched),
               "down(tensor cores)");
     phase_end();
     count_launches(4);
@@ -814,8 +828,8 @@ Error MoeCudaBackend::quant_matmul(const float* x, int64_t M, int64_t K, const v
   if (M == 0) return Error::success();
   const size_t wbytes = (size_t)N * row_bytes(fmt, K);
   const bool tc = path_ != 1 && umma_down_supported(fmt, N, K, false);
-  const bool wm = tc && umma_down_supported(fmt, N, K, true) && (path_ == 3 || (path_ == 0 && M <= 8));
-  if ((path_ == 2 && !tc) || (path_ == 3 && !wm))
+  const bool wm = tc && umma_down_supported(fmt, N, K, true) && (path_ == 3 || path_ == 4 || (path_ == 0 && M <= 8));
+  if ((path_ == 2 && !tc) || ((path_ == 3 || path_ == 4) && !wm))
     return Error::make(ErrorCode::NotImplemented,
                        "tensor-core quant matmul needs Q4_0/Q8_0/Q4_K/Q6_K weights, N % 128 == 0 and K a multiple "
                        "of the format's tile (64; K-quants 256; warp-MMA schedule 128)");
@@ -1048,6 +1062,72 @@ Error MoeCudaBackend::ffn_launch(const LayerArgs& L, const ExpertPlan& P, int64_
   return run_experts(xd, logits, po, L, P, T, yo);
 }
 
+Error MoeCudaBackend::ensure_copy_streams(int chunks) {
+  if (!in_stream_) UAII_CUDA(cudaStreamCreateWithFlags(&in_stream_, cudaStreamNonBlocking), "StreamCreate(in)");
+  if (!out_stream_) UAII_CUDA(cudaStreamCreateWithFlags(&out_stream_, cudaStreamNonBlocking), "StreamCreate(out)");
+  while ((int)chunk_events_.size() < 2 * chunks + 1) {
+    cudaEvent_t e = nullptr;
+    UAII_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "EventCreate");
+    chunk_events_.push_back(e);
+  }
+  return Error::success();
+}
+
+// Chunk c: its x rows go host -> device on in_stream_, the layer runs on stream_ once
+// they have landed, and its y rows (and probabilities) go back on out_stream_ once the
+// layer is done, so the copies of chunk c+1 (in) and c-1 (out) overlap the layer of c.
+// Token rows are independent (the reference's GEMMs tile over rows only), so chunking
+// changes only the order of work and, through each chunk's plan, the grouping of the
+// down projection's f32 partial sums.  Returns after the last copy back.
+Error MoeCudaBackend::ffn_host_chunked(const LayerArgs& L, const float* x, int64_t T, float* y, float* probs,
+                                       int chunks) {
+  const int64_t D = L.D, E = L.E;
+  const int64_t tc_max = (T + chunks - 1) / chunks;
+  const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E);
+  const ExpertPlan Pmax = plan_experts(L, tc_max);
+  const size_t rsb = router_scratch_bytes(tc_max, D, E);
+  UAII_TRY(ensure_copy_streams(chunks));
+  UAII_TRY(reserve(experts_ws(L, tc_max, Pmax) + 2 * align_up(xb) + 2 * align_up(pb) + align_up(rsb)));
+  float* xs = static_cast<float*>(carve(xb));
+  float* ys = static_cast<float*>(carve(xb));
+  float* logits = static_cast<float*>(carve(pb));
+  float* ps = static_cast<float*>(carve(pb));
+  float* rscratch = rsb ? static_cast<float*>(carve(rsb)) : nullptr;
+  const void* wd = nullptr;
+  UAII_TRY(stage_weight(L.router_w, sizeof(float) * (size_t)(E * D), &wd));
+  const size_t mark = ws_used_;
+  cudaEvent_t* ev = chunk_events_.data();
+  // the copies in must not overtake work of an earlier call that still reads the staging buffers
+  UAII_CUDA(cudaEventRecord(ev[2 * chunks], stream_), "EventRecord");
+  UAII_CUDA(cudaStreamWaitEvent(in_stream_, ev[2 * chunks], 0), "StreamWaitEvent");
+  for (int c = 0; c < chunks; ++c) {
+    const int64_t t0 = T * c / chunks, t1 = T * (c + 1) / chunks;
+    UAII_CUDA(cudaMemcpyAsync(xs + t0 * D, x + t0 * D, sizeof(float) * (size_t)((t1 - t0) * D),
+                              cudaMemcpyHostToDevice, in_stream_), "MemcpyAsync(H2D chunk)");
+    UAII_CUDA(cudaEventRecord(ev[2 * c], in_stream_), "EventRecord");
+  }
+  ExpertPlan last{};
+  for (int c = 0; c < chunks; ++c) {
+    const int64_t t0 = T * c / chunks, t1 = T * (c + 1) / chunks, tc = t1 - t0;
+    UAII_CUDA(cudaStreamWaitEvent(stream_, ev[2 * c], 0), "StreamWaitEvent");
+    ws_used_ = mark;  // chunks run one after another on stream_: each reuses the same expert workspace
+    const ExpertPlan P = plan_experts(L, tc);
+    UAII_TRY(ffn_launch(L, P, tc, xs + t0 * D, static_cast<const float*>(wd), logits + t0 * E, ps + t0 * E, rscratch,
+                        router_scratch_bytes(tc, D, E), ys + t0 * D));
+    last = P;
+    UAII_CUDA(cudaEventRecord(ev[2 * c + 1], stream_), "EventRecord");
+    UAII_CUDA(cudaStreamWaitEvent(out_stream_, ev[2 * c + 1], 0), "StreamWaitEvent");
+    UAII_CUDA(cudaMemcpyAsync(y + t0 * D, ys + t0 * D, sizeof(float) * (size_t)(tc * D), cudaMemcpyDeviceToHost,
+                              out_stream_), "MemcpyAsync(D2H chunk)");
+    if (probs)
+      UAII_CUDA(cudaMemcpyAsync(probs + t0 * E, ps + t0 * E, sizeof(float) * (size_t)(tc * E), cudaMemcpyDeviceToHost,
+                                out_stream_), "MemcpyAsync(D2H chunk)");
+  }
+  last_plan_ = last;
+  UAII_CUDA(cudaStreamSynchronize(out_stream_), "StreamSynchronize(out)");
+  return sync_and_check();
+}
+
 Error MoeCudaBackend::ffn(const LayerArgs& Lin, const float* x, int64_t T, float* y, float* probs) {
   std::lock_guard<std::mutex> lk(mu_);
   UAII_CUDA(cudaSetDevice(device_), "SetDevice");
@@ -1060,6 +1140,15 @@ Error MoeCudaBackend::ffn(const LayerArgs& Lin, const float* x, int64_t T, float
   if (T < 0) return Error::make(ErrorCode::InvalidArgument, "moe ffn: negative token count");
   if (T == 0) return Error::success();
   const int64_t D = L.D, E = L.E;
+  // Large batches in and out of host memory: copies overlapped with the layer, in chunks
+  // of at least 2048 tokens (at most 8 chunks), when no weight has to be staged per call.
+  // Smaller chunks lose more in the expert products (each chunk decodes every weight tile
+  // again, and its experts' last slot tiles are partly empty; Mixtral-shaped layer, 4096
+  // tokens: one call 2.55 ms, 2 x 2048 tokens 3.06 ms, 4 x 1024 tokens 4.28 ms) than
+  // their copies hide.
+  if (!external_ && T >= 4096 && !is_device_ptr(x) && !is_device_ptr(y) && (!probs || !is_device_ptr(probs)) &&
+      layer_stage_bytes(L) == 0)
+    return ffn_host_chunked(L, x, T, y, probs, (int)std::min<int64_t>(8, T / 2048));
   const size_t xb = sizeof(float) * (size_t)(T * D), pb = sizeof(float) * (size_t)(T * E);
   const ExpertPlan P = plan_experts(L, T);
   const size_t rsb = router_scratch_bytes(T, D, E);
@@ -1558,7 +1647,7 @@ int uaii_moe_selftest_wait_timeout(uaii_moe_backend* b, int64_t budget_cycles) {
 int uaii_moe_last_plan(uaii_moe_backend* b, int* tensor_cores, int* slot_tile, int* down_splits) {
   if (!b) return no_backend();
   const uaii_b200::ExpertPlan P = b->impl.last_plan();
-  if (tensor_cores) *tensor_cores = P.umma ? (P.warp_mma ? 2 : 1) : 0;
+  if (tensor_cores) *tensor_cores = P.umma ? (P.quad_mma ? 3 : P.warp_mma ? 2 : 1) : 0;
   if (slot_tile) *slot_tile = P.bn;
   if (down_splits) *down_splits = P.splits;
   return report(Error::success());
@@ -1566,7 +1655,7 @@ int uaii_moe_last_plan(uaii_moe_backend* b, int* tensor_cores, int* slot_tile, i
 
 int uaii_moe_set_expert_path(uaii_moe_backend* b, int path) {
   if (!b) return no_backend();
-  if (path < 0 || path > 3) return report(Error::make(ErrorCode::InvalidArgument, "path must be 0, 1, 2 or 3"));
+  if (path < 0 || path > 4) return report(Error::make(ErrorCode::InvalidArgument, "path must be 0, 1, 2, 3 or 4"));
   b->impl.set_expert_path(path);
   return report(Error::success());
 }

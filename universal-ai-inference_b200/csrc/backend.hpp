@@ -85,7 +85,8 @@ struct LayerArgs {
 
 struct ExpertPlan {
   bool umma = false;   // tensor-core grouped GEMM (else CUDA-core GEMV)
-  bool warp_mma = false;      // ... on the warp-MMA (mma.sync) schedule, else tcgen05
+  bool warp_mma = false;      // ... on an mma.sync schedule (decode widths), else tcgen05
+  bool quad_mma = false;      // ... the mma.sync schedule over whole K-quant super-blocks
   bool umma_refused = false;  // tensor cores forced but the layer does not qualify
   int bn = 16;         // slots per tile (MMA N)
   int splits = 1;      // K splits of the down projection
@@ -241,6 +242,12 @@ class MoeCudaBackend {
   void drop_graphs();
   Error ffn_launch(const LayerArgs& L, const ExpertPlan& P, int64_t T, const float* xd, const float* wd, float* logits,
                    float* po, float* rscratch, size_t rsb, float* yo);
+  // Host x and y (and host or no probs) with device-resident weights: the batch in
+  // chunks whose host copies overlap the neighbouring chunks' device work.
+  Error ffn_host_chunked(const LayerArgs& L, const float* x, int64_t T, float* y, float* probs, int chunks);
+  cudaStream_t in_stream_ = nullptr, out_stream_ = nullptr;  // host copies of the chunked path
+  std::vector<cudaEvent_t> chunk_events_;
+  Error ensure_copy_streams(int chunks);
   std::mutex mu_;
 };
 

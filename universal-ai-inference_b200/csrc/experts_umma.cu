@@ -76,7 +76,8 @@ struct Args {
   int kquads;   // quads per row: ceil(K / 256)
   int k_atoms;  // 64-element atoms per row: K / 64
   int rows_per_expert, gateup;
-  __half* h_out;  // gate/up: [S, out_ld] f16
+  __half* h_out;  // gate/up: [S, out_ld] f16, K order h_order (quad schedule; the others use their own)
+  int h_order;
   float* out;     // down: [splits][S][out_ld] f32
   int64_t out_ld, split_stride;
   int* err;
@@ -1236,6 +1237,342 @@ __global__ void __launch_bounds__(kWmThreads, 1)
   __syncthreads();
 }
 
+// ---- Quad schedule: mma.sync over whole K-quant super-blocks (decode widths) ----
+//
+// The warp-MMA schedule above gives each lane one 32-element unit of each of
+// its two rows per quad, so a lane decodes a super-block header for every 32
+// elements, and its Q4_K operands carry d*sc and dmin*m in every element.  Here
+// warp w owns rows 16*(w%8) .. +15 of the 128-row tile and every other quad of
+// the tile (half h = w/8 takes the quads q0 + h, q0 + h + 2, ...): a lane decodes
+// 64 elements of each of its two rows per header (K order q4k_kpos / q6k_kpos,
+// operand_order.cuh).
+//   Q4_K: the operand is q*sc, exact in f16 (at most 945): one f16 FMA per pair,
+//         fma(1024 + q, sc, -1024 sc) for low nibbles and fma(1024 + 16q, sc/16,
+//         -64 sc) for high ones; a second MMA per k-step multiplies the
+//         activations by the sub-block minima m (exact in f16); d and dmin are
+//         applied once per quad in f32: acc += d * M1 - dmin * M2.  The weights
+//         enter the products unrounded, unlike the other schedules' fp16(d*sc*q -
+//         dmin*m).
+//   Q6_K: quarters are assembled with one select-LOP3 per word from the low or
+//         high nibbles and the 2-bit fields; the operand is fp16((q - 32) *
+//         fp16(d*sc)), the same value as the other schedules.
+// Warp 16 is the TMA producer of the packed weight windows and activation tiles,
+// as in the warp-MMA schedule; the two halves' sums meet in shared memory after
+// each tile and gate/up rows of the same features meet there for SwiGLU.
+template <int F> struct QuadUnit;
+
+template <> struct QuadUnit<kQ4_K> {
+  uint32_t w[8];                   // qs bytes [32t, 32t + 32)
+  __half2 f_lo, b_lo, f_hi, b_hi;  // fold constants of sub-blocks 2t and 2t + 1
+  uint32_t m_lo, m_hi;             // (m, m) of the two sub-blocks, f16
+  float d, dmin;
+  __device__ __forceinline__ void load(const uint8_t* row, int t) {
+    const uint4 hdr = *reinterpret_cast<const uint4*>(row);  // d, dmin, scales[12]
+    const uint4 qa = *reinterpret_cast<const uint4*>(row + 16 + 32 * t);
+    const uint4 qb = *reinterpret_cast<const uint4*>(row + 32 + 32 * t);
+    w[0] = qa.x; w[1] = qa.y; w[2] = qa.z; w[3] = qa.w;
+    w[4] = qb.x; w[5] = qb.y; w[6] = qb.z; w[7] = qb.w;
+    // (scale, min) of sub-blocks j = 2t, 2t + 1 in the get_scale_min_k4 bit layout, as byte pairs
+    const uint32_t sh = 16u * (uint32_t)(t & 1);
+    const uint32_t y2 = hdr.y >> sh, z2 = hdr.z >> sh, w2 = hdr.w >> sh;
+    uint32_t sc2, m2;
+    if (t < 2) {
+      sc2 = y2 & 0x3F3Fu;
+      m2 = z2 & 0x3F3Fu;
+    } else {
+      sc2 = (w2 & 0x0F0Fu) | ((y2 >> 2) & 0x3030u);
+      m2 = ((w2 >> 4) & 0x0F0Fu) | ((z2 >> 2) & 0x3030u);
+    }
+    const __half2 k1024 = __float2half2_rn(1024.f);
+    const __half2 scf = __hsub2(as_h2(__byte_perm(sc2, 0, 0x4140) | kMagic), k1024);  // (sc_a, sc_b)
+    const __half2 mf = __hsub2(as_h2(__byte_perm(m2, 0, 0x4140) | kMagic), k1024);   // (m_a, m_b)
+    const __half2 fb = __hmul2(scf, __floats2half2_rn(1.0f, 0.0625f));
+    const __half2 bb = __hmul2(scf, __floats2half2_rn(-1024.0f, -64.0f));
+    f_lo = __low2half2(fb);
+    f_hi = __high2half2(fb);
+    b_lo = __low2half2(bb);
+    b_hi = __high2half2(bb);
+    m_lo = as_u32(__low2half2(mf));
+    m_hi = as_u32(__high2half2(mf));
+    const __half2 dm = as_h2(hdr.x);
+    d = __low2float(dm);
+    dmin = __high2float(dm);
+  }
+  // k-step s: the pair at positions (2t, 2t+1) (bytes 0, 2 of word s % 8) and at
+  // (2t+8, 2t+9) (bytes 1, 3), low nibbles for s < 8, high nibbles after
+  __device__ __forceinline__ void pair(int s, uint32_t& lo, uint32_t& hi) const {
+    const uint32_t q = w[s & 7], q8 = q >> 8;
+    if (s < 8) {
+      lo = as_u32(__hfma2(magic_pair(q, 0x000F000Fu), f_lo, b_lo));
+      hi = as_u32(__hfma2(magic_pair(q8, 0x000F000Fu), f_lo, b_lo));
+    } else {
+      lo = as_u32(__hfma2(magic_pair(q, 0x00F000F0u), f_hi, b_hi));
+      hi = as_u32(__hfma2(magic_pair(q8, 0x00F000F0u), f_hi, b_hi));
+    }
+  }
+  __device__ __forceinline__ uint32_t min_pair(int s) const { return s < 8 ? m_lo : m_hi; }
+};
+
+template <> struct QuadUnit<kQ6_K> {
+  uint32_t q6[16];  // [4c + w]: 6-bit values of quarter c, positions 16pp + 4w .. +3 (bits 6-7 junk)
+  __half2 s[4];     // (d*sc, d*sc) of sub-block 8hf + pp + 2c
+  // OFF: the super-block's offset in its 16-byte aligned window (even, 0..14)
+  template <int OFF>
+  __device__ __forceinline__ void load(const uint8_t* row, int t) {
+    const int hf = t >> 1, pp = t & 1;
+    uint32_t l0[4], l1[4], qh[4];
+    load_words<OFF, 4>(row, 4 * hf + pp, l0);      // ql[64hf + 16pp .. +15]
+    load_words<OFF, 4>(row, 4 * hf + 2 + pp, l1);  // ql[64hf + 32 + 16pp .. +15]
+    load_words<OFF, 4>(row, 8 + 2 * hf + pp, qh);  // qh[32hf + 16pp .. +15]
+    constexpr uint32_t kHi = 0xF0F0F0F0u;  // bits 4-7 from the 2-bit fields, 0-3 from a nibble
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      q6[i] = (l0[i] & ~kHi) | ((qh[i] << 4) & kHi);
+      q6[4 + i] = (l1[i] & ~kHi) | ((qh[i] << 2) & kHi);
+      q6[8 + i] = ((l0[i] >> 4) & ~kHi) | (qh[i] & kHi);
+      q6[12 + i] = ((l1[i] >> 4) & ~kHi) | ((qh[i] >> 2) & kHi);
+    }
+    uint32_t sw[2];
+    words_at<2>(row, OFF + 192 + 8 * hf, sw);  // scales[8hf .. 8hf + 7]
+    const uint32_t dd = ld_u16(row + OFF + 208);
+    const __half2 bias = __float2half2_rn(1152.f);  // 1024 + 128
+    const __half2 d2 = as_h2(dd | (dd << 16));
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {  // scales pp + 4*h2 + {0, 2}: bytes pp and pp + 2 of word h2
+      const uint32_t v = ((sw[h2] >> (8 * pp)) & 0x00FF00FFu) ^ 0x00800080u;  // sc + 128 as unsigned
+      const __half2 p = __hmul2(d2, __hsub2(as_h2(v | kMagic), bias));      // (d*sc, d*sc')
+      s[2 * h2] = __low2half2(p);
+      s[2 * h2 + 1] = __high2half2(p);
+    }
+  }
+  // k-step s = 4c + w: bytes (0, 2) and (1, 3) of quarter c's word w, value d*sc*(q - 32)
+  __device__ __forceinline__ void pair(int k, uint32_t& lo, uint32_t& hi) const {
+    const __half2 bias = __float2half2_rn(1056.f);  // 1024 + 32
+    const uint32_t q = q6[k];
+    lo = as_u32(__hmul2(__hsub2(magic_pair(q, 0x003F003Fu), bias), s[k >> 2]));
+    hi = as_u32(__hmul2(__hsub2(magic_pair(q >> 8, 0x003F003Fu), bias), s[k >> 2]));
+  }
+};
+
+template <int F, int NT, int ST>
+__global__ void __launch_bounds__(kWmThreads, 1)
+    expert_quad_mma_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
+                           const __grid_constant__ CUtensorMap tm_x, const Args args) {
+  static_assert(F == kQ4_K || F == kQ6_K, "quad schedule: K-quants only");
+  using C = WmCfg<F, NT, ST>;
+  using Fm = Fmt<F>;
+  constexpr int BN = C::BN;
+  constexpr int kCompute = kWmWarps * 32;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sB = smem + C::kOffB;
+  uint8_t* sP = smem + C::kOffP;
+  float* sR = reinterpret_cast<float*>(smem + C::kOffR);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* full = bars;        // weight window + activation tile of a quad landed
+  uint64_t* empty = full + ST;  // the half that used the stage is done with it
+  volatile int* s_abort = reinterpret_cast<volatile int*>(bars + C::kNumBars);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, kWmWarps / 2);
+    }
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == kWmWarps && lane == 0) {
+    prefetch_tmap(&tm_w0);
+    prefetch_tmap(&tm_w1);
+    prefetch_tmap(&tm_x);
+  }
+  __syncthreads();
+  const int total = __ldg(args.tile_base + args.E);
+  int* err = args.err;
+  auto quad_range = [&](const Tile& t, int& q0, int& q1) {
+    q0 = t.split * args.kquads / args.splits;
+    q1 = (t.split + 1) * args.kquads / args.splits;
+  };
+
+  if (warp == kWmWarps) {
+    // ------------------------------------------------------------ TMA producer
+    uint32_t n = 0;  // stages issued
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+      const Tile t = decode_tile(args, tile, BN);
+      const int row0 = t.e * args.rows_per_expert + t.m_tile * (args.gateup ? 64 : 128);
+      const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
+      int q0, q1;
+      quad_range(t, q0, q1);
+      for (int q = q0; q < q1; ++q) {
+        const int s = n % ST;
+        if (!(ok = bounded_wait(empty + s, ((n / ST) & 1) ^ 1, s_abort, err, kErrTimeoutProducer))) break;
+        const int x = (q * Fm::kBytes) & ~15;
+        uint8_t* dst = sP + s * C::kPStage;
+        if (elect_one()) {
+          mbar_arrive_expect_tx(full + s, C::kPStage + 4 * C::kBAtom);
+          tma_load_2d(dst, &tm_w0, full + s, x, row0);
+          if (args.gateup) tma_load_2d(dst + 64 * C::kWB, &tm_w1, full + s, x, row0);
+          else tma_load_2d(dst + 64 * C::kWB, &tm_w0, full + s, x, row0 + 64);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tma_load_2d(sB + s * C::kBQuad + j * C::kBAtom, &tm_x, full + s, q * kQuadK + 64 * j, slot0);
+        }
+        __syncwarp();
+        ++n;
+      }
+    }
+    // never leave with copies in flight: the last ST stages
+    for (uint32_t j = n > (uint32_t)ST ? n - ST : 0; j < n; ++j) (void)mbar_wait(full + j % ST, (j / ST) & 1);
+  } else {
+    // ------------------------------------------------------------ compute warps
+    const int mw = warp & 7, h = warp >> 3;   // 16-row block, quad parity of the tile
+    const int g = lane >> 2, tq = lane & 3;   // fragment row group, lane quarter
+    const int r0 = 16 * mw + g, r1 = r0 + 8;  // packed stage rows (gate/up: gate 0-63, up 64-127)
+    // ldmatrix: lanes 8i .. 8i+7 address the rows of matrix i = (slot octet i/2, k octet i%2);
+    // k-step s reads 16-byte chunk 2(s%4) + (k octet) of atom s/4, stored at chunk ^ (row % 8)
+    const int ld_mi = lane >> 3, ld_n = 8 * (ld_mi >> 1) + (lane & 7);
+    const uint32_t cx = (uint32_t)((ld_mi & 1) ^ (lane & 7));
+    uint32_t boff[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) boff[j] = (uint32_t)(ld_n * 128) + (((uint32_t)(2 * j) ^ cx) << 4);
+    const uint32_t sB0 = smem_u32(sB);
+    float* red = sR + (mw * 32 + lane) * 4 * NT;
+    uint32_t pi = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+      const Tile t = decode_tile(args, tile, BN);
+      int q0, q1;
+      quad_range(t, q0, q1);
+      float acc[NT][4];
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[n][i] = 0.f;
+      for (int q = q0; q < q1; ++q, ++pi) {
+        if (((q - q0) & 1) != h) continue;  // the other half's quad
+        if (!(ok = bounded_wait(full + pi % ST, (pi / ST) & 1, s_abort, err, kErrTimeoutDequant))) break;
+        const uint8_t* stage = sP + (pi % ST) * C::kPStage;
+        QuadUnit<F> u0, u1;
+        if constexpr (F == kQ6_K) {  // 16-byte loads with the window offset as a constant
+          switch ((q * Fm::kBytes) & 15) {
+#define UAII_QM_Q6(O)                                  \
+  case O:                                              \
+    u0.template load<O>(stage + r0 * C::kWB, tq);      \
+    u1.template load<O>(stage + r1 * C::kWB, tq);      \
+    break;
+            UAII_QM_Q6(0) UAII_QM_Q6(2) UAII_QM_Q6(4) UAII_QM_Q6(6)
+            UAII_QM_Q6(8) UAII_QM_Q6(10) UAII_QM_Q6(12) UAII_QM_Q6(14)
+#undef UAII_QM_Q6
+            default: break;
+          }
+        } else {
+          u0.load(stage + r0 * C::kWB, tq);
+          u1.load(stage + r1 * C::kWB, tq);
+        }
+        const uint32_t bq = sB0 + (pi % ST) * C::kBQuad;
+        float m1[NT][4], m2[NT][4];  // Q4_K: this quad's sum of q*sc*x and of m*x
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) m1[n][i] = m2[n][i] = 0.f;
+        __syncwarp();  // ldmatrix / mma.sync below need the whole warp converged
+#pragma unroll
+        for (int s = 0; s < 16; ++s) {
+          uint32_t a[4];  // rows g, g + 8 at positions (2tq, 2tq+1); the same at (2tq+8, 2tq+9)
+          u0.pair(s, a[0], a[2]);
+          u1.pair(s, a[1], a[3]);
+          const uint32_t addr = bq + (s >> 2) * C::kBAtom + boff[s & 3];
+          uint32_t b[2 * NT];
+          if constexpr (NT == 2) {
+            asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
+                         : "r"(addr));
+          } else {
+            asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];"
+                         : "=r"(b[0]), "=r"(b[1])
+                         : "r"(addr));
+          }
+          if constexpr (F == kQ4_K) {
+            const uint32_t am[4] = {u0.min_pair(s), u1.min_pair(s), u0.min_pair(s), u1.min_pair(s)};
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+              mma_16816(m1[n], a, b[2 * n], b[2 * n + 1]);
+              mma_16816(m2[n], am, b[2 * n], b[2 * n + 1]);
+            }
+          } else {
+#pragma unroll
+            for (int n = 0; n < NT; ++n) mma_16816(acc[n], a, b[2 * n], b[2 * n + 1]);
+          }
+        }
+        if constexpr (F == kQ4_K) {  // accumulator (n, i): row g + 8(i / 2)
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float dv = i < 2 ? u0.d : u1.d, mv = i < 2 ? u0.dmin : u1.dmin;
+              acc[n][i] = fmaf(-mv, m2[n][i], fmaf(dv, m1[n][i], acc[n][i]));
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + pi % ST);
+      }
+      // every compute warp reaches this barrier once per tile; a wait that gave up stops all of them
+      if (bar_any(1, kCompute, !ok)) break;
+      if (h == 1) {  // the odd quads' sums go to the even half
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) red[4 * n + i] = acc[n][i];
+      }
+      bar_sync(1, kCompute);
+      if (h == 1) continue;
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[n][i] += red[4 * n + i];
+      // accumulator (n, i): row g + 8(i / 2) of the block, slot 8n + 2tq + i % 2
+      const int n_valid = min(BN, __ldg(args.counts + t.e) - t.n_tile * BN);
+      const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
+      if (args.gateup) {  // up rows (blocks 4-7) meet the gate rows (blocks 0-3) of the same features
+        if (mw >= 4) {
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) red[4 * n + i] = acc[n][i];
+        }
+        bar_sync(2, kCompute / 2);
+        if (mw < 4) {
+          const float* up = sR + ((mw + 4) * 32 + lane) * 4 * NT;
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int feat = t.m_tile * 64 + 16 * mw + g + 8 * (i >> 1);
+              const int sl = 8 * n + 2 * tq + (i & 1);
+              const float gv = acc[n][i], uv = up[4 * n + i];
+              const float sig = 1.0f / (1.0f + __expf(-gv));
+              if (sl < n_valid)
+                args.h_out[(int64_t)(slot0 + sl) * args.out_ld + operand_pos(args.h_order, feat)] =
+                    __float2half_rn((gv * sig) * uv);
+            }
+        }
+      } else {
+        float* out = args.out + (int64_t)t.split * args.split_stride;
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int o = t.m_tile * 128 + 16 * mw + g + 8 * (i >> 1);
+            const int sl = 8 * n + 2 * tq + (i & 1);
+            if (sl < n_valid) out[(int64_t)(slot0 + sl) * args.out_ld + o] = acc[n][i];
+          }
+      }
+    }
+  }
+  __syncthreads();
+}
+
 __global__ void tile_table_kernel(const int32_t* counts, int E, int bn, int m_tiles, int splits,
                                   int32_t* tile_base) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
@@ -1388,6 +1725,33 @@ cudaError_t run_warp_mma(const CUtensorMap& w0, const CUtensorMap& w1, const CUt
   return cudaGetLastError();
 }
 
+template <int F, int NT>
+cudaError_t run_quad_mma(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x, const Args& a,
+                         cudaStream_t st) {
+  constexpr int ST = WmStages<F, NT>::ST;
+  using C = WmCfg<F, NT, ST>;
+  static_assert(C::kSmem <= 227 * 1024, "shared memory budget");
+  auto kern = expert_quad_mma_kernel<F, NT, ST>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  kern<<<num_sms(), kWmThreads, C::kSmem, st>>>(w0, w1, x, a);
+  return cudaGetLastError();
+}
+
+template <int F>
+cudaError_t dispatch_quad(int bn, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
+                          const Args& a, cudaStream_t st) {
+  switch (bn) {
+    case 8: return run_quad_mma<F, 1>(w0, w1, x, a, st);
+    case 16: return run_quad_mma<F, 2>(w0, w1, x, a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 template <int F>
 cudaError_t dispatch_warp(int bn, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
                           const Args& a, cudaStream_t st) {
@@ -1418,15 +1782,21 @@ bool make_weight_maps(CUtensorMap* m0, CUtensorMap* m1, const void* W0, const vo
          make_weight_map(m1, W1, pitch, rows_total, Fmt<F>::kBoxBytes);
 }
 
-// warp_mma: the mma.sync schedule (slot tiles of 8 or 16, K % 128 == 0, operand
-// rows in wm_kpos order); else tcgen05 (slot tiles 16..256, tc_kpos order).
-cudaError_t launch_common(bool warp_mma, int fmt, bool gateup, const void* W0, const void* W1, int64_t pitch,
+// sched: kSchedWarpMma, the mma.sync schedule (slot tiles of 8 or 16, K % 128 == 0,
+// operand rows in wm_kpos order); kSchedQuadMma, mma.sync over whole K-quant
+// super-blocks (slot tiles of 8 or 16, Q4_K / Q6_K, operand rows in q4k_kpos /
+// q6k_kpos order); else tcgen05 (slot tiles 16..256, tc_kpos order).  h_order: the
+// order the quad schedule's gate/up epilogue writes h in.
+cudaError_t launch_common(int sched, int fmt, bool gateup, const void* W0, const void* W1, int64_t pitch,
                           int64_t E, int64_t rows, int64_t K, const void* act16, int64_t S_rows,
                           const int32_t* counts, const int32_t* offsets, int32_t* tile_base, int bn, int splits,
-                          void* h16, float* out, int64_t out_ld, int64_t split_stride, int* err, cudaStream_t st) {
+                          void* h16, float* out, int64_t out_ld, int64_t split_stride, int* err, cudaStream_t st,
+                          int h_order) {
   const int mk = min_k(fmt);
+  const bool warp_mma = sched == kSchedWarpMma, quad = sched == kSchedQuadMma;
   if (!mk || K % mk != 0 || K <= 0) return cudaErrorNotSupported;
-  if (warp_mma && (K % 128 != 0 || (bn != 8 && bn != 16))) return cudaErrorNotSupported;
+  if ((warp_mma || quad) && (K % 128 != 0 || (bn != 8 && bn != 16))) return cudaErrorNotSupported;
+  if (quad && fmt != kQ4_K && fmt != kQ6_K) return cudaErrorNotSupported;
   const int m_rows = gateup ? 64 : 128;
   if (rows % m_rows != 0 || pitch % 16 != 0 || pitch < fmt_row_bytes(fmt, K)) return cudaErrorNotSupported;
   if (!aligned16(W0) || !aligned16(W1) || !aligned16(act16) || K % 8 != 0) return cudaErrorNotSupported;
@@ -1458,10 +1828,13 @@ cudaError_t launch_common(bool warp_mma, int fmt, bool gateup, const void* W0, c
   a.rows_per_expert = (int)rows;
   a.gateup = gateup ? 1 : 0;
   a.h_out = static_cast<__half*>(h16);
+  a.h_order = h_order;
   a.out = out;
   a.out_ld = out_ld;
   a.split_stride = split_stride;
   a.err = err;
+  if (quad) return fmt == kQ4_K ? dispatch_quad<kQ4_K>(bn, m0, m1, mx, a, st)
+                                : dispatch_quad<kQ6_K>(bn, m0, m1, mx, a, st);
   if (warp_mma) {
     switch (fmt) {
       case kQ4_0: return dispatch_warp<kQ4_0>(bn, m0, m1, mx, a, st);
@@ -1519,16 +1892,17 @@ bool warp_mma_shapes_supported(int gfmt, int dfmt, int64_t D, int64_t I) {
 
 cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pitch, int64_t E, int64_t I, int64_t D,
                                const void* xp16, int64_t S_rows, const int32_t* counts, const int32_t* offsets,
-                               int32_t* tile_base, int bn, void* h16, int* err, cudaStream_t st, bool warp_mma) {
-  return launch_common(warp_mma, fmt, true, G, U, pitch, E, I, D, xp16, S_rows, counts, offsets, tile_base, bn, 1,
-                       h16, nullptr, I, 0, err, st);
+                               int32_t* tile_base, int bn, void* h16, int* err, cudaStream_t st, int sched,
+                               int h_order) {
+  return launch_common(sched, fmt, true, G, U, pitch, E, I, D, xp16, S_rows, counts, offsets, tile_base, bn, 1,
+                       h16, nullptr, I, 0, err, st, h_order);
 }
 
 cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
                              int64_t S_rows, const int32_t* counts, const int32_t* offsets, int32_t* tile_base,
-                             int bn, int splits, float* out, int* err, cudaStream_t st, bool warp_mma) {
-  return launch_common(warp_mma, fmt, false, Dn, Dn, pitch, E, D, I, h16, S_rows, counts, offsets, tile_base, bn,
-                       splits, nullptr, out, D, S_rows * D, err, st);
+                             int bn, int splits, float* out, int* err, cudaStream_t st, int sched) {
+  return launch_common(sched, fmt, false, Dn, Dn, pitch, E, D, I, h16, S_rows, counts, offsets, tile_base, bn,
+                       splits, nullptr, out, D, S_rows * D, err, st, kOrderTc);
 }
 
 namespace {

@@ -68,11 +68,12 @@ cudaError_t launch_route_gather16(const void* rows, int64_t N, int64_t D, int64_
 cudaError_t launch_ep_combine(const float* y_back, const int32_t* row_of, int64_t T, int R, int64_t D, float* y,
                               cudaStream_t st);
 // Gathers x rows into expert-contiguous slots: xp_f32 and/or xp_f16 (either may be null).
-// xp_f16 rows are in an operand K order (operand_order.cuh): tc_kpos for the
-// tcgen05 schedule, wm_kpos (wm_order, D % 128 == 0) for the warp-MMA one.
+// xp_f16 rows are in an operand K order (operand_order.cuh, OperandOrder): tc_kpos for
+// the tcgen05 schedule, wm_kpos (D % 128 == 0) for the warp-MMA one, q4k_kpos / q6k_kpos
+// (D % 256 == 0) for the quad schedule.
 cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E, int k,
                                 const RouteBuffers& rb, float* xp_f32, void* xp_f16,
-                                cudaStream_t st, bool wm_order = false);
+                                cudaStream_t st, int order = 0);
 // y[t] = sum_r w[t,r] * out[slot_of[t,r]] (rank order, from 0), then
 // y[t] += gate[t] * shared_out[t] when shared_out is given (gate may be null = 1).
 // `out` (and `shared_out`) may hold `splits` partial planes `split_stride`
@@ -116,20 +117,28 @@ bool warp_mma_shapes_supported(int gate_fmt, int down_fmt, int64_t D, int64_t I)
 // A single projection out[N] = W[N, K] . x on tensor cores (launch_down_umma with E = 1):
 // format and K chunking, N a multiple of 128 (and K of 128 for the warp-MMA schedule).
 bool umma_down_supported(int fmt, int64_t N, int64_t K, bool warp_mma);
+// Expert-product schedules on the tensor cores.
+enum ExpertSchedule : int {
+  kSchedTcgen05 = 0,  // tcgen05/TMEM/TMA, slot tiles 16..256, operands in tc_kpos order
+  kSchedWarpMma = 1,  // mma.sync, slot tiles 8 or 16, a 32-element unit per lane and row, wm_kpos order
+  kSchedQuadMma = 2,  // mma.sync over whole K-quant super-blocks (Q4_K, Q6_K), q4k_kpos / q6k_kpos order
+};
+// The schedules the quad kernel takes: K-quant formats with whole super-blocks.
+inline bool quad_mma_format(int fmt) { return fmt == 14 || fmt == 16; }
 // h16[slot, i] = silu(x.G[e,i]) * (x.U[e,i]) in f16; x is xp16 [S_rows, D] f16.
-// G, U rows `pitch` bytes apart (a multiple of 16).  warp_mma selects the
-// mma.sync schedule (bn 8 or 16; x and h in wm_kpos order), else tcgen05
-// (bn 16..256; tc_kpos order).
+// G, U rows `pitch` bytes apart (a multiple of 16).  sched selects the schedule; x is
+// in that schedule's order for the gate format; h is written in the tc_kpos
+// (tcgen05), wm_kpos (warp-MMA) or h_order (quad: the order of the down format) order.
 // tile_base: scratch of E+1 ints.  *err receives a nonzero code if a wait timed out.
 cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pitch, int64_t E, int64_t I, int64_t D,
                                const void* xp16, int64_t S_rows, const int32_t* counts,
                                const int32_t* offsets, int32_t* tile_base, int bn, void* h16, int* err,
-                               cudaStream_t st, bool warp_mma = false);
+                               cudaStream_t st, int sched = kSchedTcgen05, int h_order = 0);
 // out[split][slot, o] = partial of h16[slot] . Dn[e, o] over the split's K range (f32).
 cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
                              int64_t S_rows, const int32_t* counts, const int32_t* offsets,
                              int32_t* tile_base, int bn, int splits, float* out, int* err, cudaStream_t st,
-                             bool warp_mma = false);
+                             int sched = kSchedTcgen05);
 // Copies `rows` packed rows of row_bytes (even) from src (src_pitch apart) to dst
 // (dst_pitch apart, a multiple of 16), zero-filling each row's padding.
 cudaError_t launch_pad_rows(const void* src, int64_t src_pitch, int64_t rows, int64_t row_bytes, void* dst,

@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int64_t T, int k, Rout
 // Offsets by a block-wide exclusive scan of counts; then one warp per (t, r).
 __global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int64_t D,
                                     int64_t E, int k, RouteBuffers rb, float* xp32,
-                                    __half* xp16, bool wm_order) {
+                                    __half* xp16, int order) {
   extern __shared__ int offs[];  // [E+1]
   if (threadIdx.x == 0) {
     int run = 0;
@@ -189,7 +189,7 @@ __global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int6
       for (int64_t i = lane; i < D; i += 32) {
         const float v = x[t * D + i];
         if (xp32) xp32[(int64_t)slot * D + i] = v;
-        if (xp16) xp16[(int64_t)slot * D + tc_kpos(i)] = __float2half_rn(v);  // D % 128 != 0: never wm_order
+        if (xp16) xp16[(int64_t)slot * D + tc_kpos(i)] = __float2half_rn(v);  // D % 128 != 0: tc order only
       }
       continue;
     }
@@ -200,8 +200,8 @@ __global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int6
       if (xp16) {  // elements (4i, 4i+2) and (4i+1, 4i+3) land on adjacent pairs in both orders
         __half* row = xp16 + (int64_t)slot * D;
         const __half2 lo = __floats2half2_rn(v.x, v.z), hi = __floats2half2_rn(v.y, v.w);
-        if (wm_order) {
-          const int64_t p0 = wm_kpos(4 * i);
+        if (order != kOrderTc) {  // warp-MMA and quad orders: the pairs sit at p0 and p0 + 8
+          const int64_t p0 = operand_pos(order, 4 * i);
           *reinterpret_cast<__half2*>(row + p0) = lo;
           *reinterpret_cast<__half2*>(row + p0 + 8) = hi;
         } else {  // tc_kpos: the pairs sit at 4i and 4i + 2, one 8-byte store (D % 4 == 0)
@@ -378,14 +378,15 @@ cudaError_t launch_route_scan(int64_t T, int64_t E, int k, const RouteBuffers& r
 
 cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E, int k,
                                 const RouteBuffers& rb, float* xp_f32, void* xp_f16,
-                                cudaStream_t st, bool wm_order) {
-  if (wm_order && D % 128 != 0) return cudaErrorInvalidValue;
+                                cudaStream_t st, int order) {
+  if ((order == kOrderWm && D % 128 != 0) || ((order == kOrderQ4K || order == kOrderQ6K) && D % 256 != 0))
+    return cudaErrorInvalidValue;
   int64_t blocks = (T * k + 7) / 8;
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
   const size_t smem = sizeof(int) * (size_t)(E + 1);
   route_gather_kernel<<<(unsigned)blocks, 256, smem, st>>>(x, T, D, E, k, rb, xp_f32,
-                                                           static_cast<__half*>(xp_f16), wm_order);
+                                                           static_cast<__half*>(xp_f16), order);
   return cudaGetLastError();
 }
 
