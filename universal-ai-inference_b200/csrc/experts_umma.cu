@@ -1262,7 +1262,7 @@ __global__ void __launch_bounds__(kWmThreads, 1)
 template <int F> struct QuadUnit;
 
 template <> struct QuadUnit<kQ4_K> {
-  uint32_t w[8];                   // qs bytes [32t, 32t + 32)
+  uint32_t w[8], w8[8];            // qs bytes [32t, 32t + 32), and each word shifted right by 8
   __half2 f_lo, b_lo, f_hi, b_hi;  // fold constants of sub-blocks 2t and 2t + 1
   uint32_t m_lo, m_hi;             // (m, m) of the two sub-blocks, f16
   float d, dmin;
@@ -1272,6 +1272,8 @@ template <> struct QuadUnit<kQ4_K> {
     const uint4 qb = *reinterpret_cast<const uint4*>(row + 32 + 32 * t);
     w[0] = qa.x; w[1] = qa.y; w[2] = qa.z; w[3] = qa.w;
     w[4] = qb.x; w[5] = qb.y; w[6] = qb.z; w[7] = qb.w;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w8[i] = w[i] >> 8;
     // (scale, min) of sub-blocks j = 2t, 2t + 1 in the get_scale_min_k4 bit layout, as byte pairs
     const uint32_t sh = 16u * (uint32_t)(t & 1);
     const uint32_t y2 = hdr.y >> sh, z2 = hdr.z >> sh, w2 = hdr.w >> sh;
@@ -1301,7 +1303,7 @@ template <> struct QuadUnit<kQ4_K> {
   // k-step s: the pair at positions (2t, 2t+1) (bytes 0, 2 of word s % 8) and at
   // (2t+8, 2t+9) (bytes 1, 3), low nibbles for s < 8, high nibbles after
   __device__ __forceinline__ void pair(int s, uint32_t& lo, uint32_t& hi) const {
-    const uint32_t q = w[s & 7], q8 = q >> 8;
+    const uint32_t q = w[s & 7], q8 = w8[s & 7];
     if (s < 8) {
       lo = as_u32(__hfma2(magic_pair(q, 0x000F000Fu), f_lo, b_lo));
       hi = as_u32(__hfma2(magic_pair(q8, 0x000F000Fu), f_lo, b_lo));
@@ -1310,7 +1312,6 @@ template <> struct QuadUnit<kQ4_K> {
       hi = as_u32(__hfma2(magic_pair(q8, 0x00F000F0u), f_hi, b_hi));
     }
   }
-  __device__ __forceinline__ uint32_t min_pair(int s) const { return s < 8 ? m_lo : m_hi; }
 };
 
 template <> struct QuadUnit<kQ6_K> {
@@ -1470,7 +1471,16 @@ __global__ void __launch_bounds__(kWmThreads, 1)
           u0.load(stage + r0 * C::kWB, tq);
           u1.load(stage + r1 * C::kWB, tq);
         }
+        // the four lane addresses of the stage's k-step columns; atoms are constant offsets from them
         const uint32_t bq = sB0 + (pi % ST) * C::kBQuad;
+        const uint32_t bqa[4] = {bq + boff[0], bq + boff[1], bq + boff[2], bq + boff[3]};
+        uint32_t am_lo[4], am_hi[4];  // Q4_K min operands: rows g, g + 8 of sub-block 2t, then 2t + 1
+        if constexpr (F == kQ4_K) {
+          am_lo[0] = am_lo[2] = u0.m_lo;
+          am_lo[1] = am_lo[3] = u1.m_lo;
+          am_hi[0] = am_hi[2] = u0.m_hi;
+          am_hi[1] = am_hi[3] = u1.m_hi;
+        }
         float m1[NT][4], m2[NT][4];  // Q4_K: this quad's sum of q*sc*x and of m*x
 #pragma unroll
         for (int n = 0; n < NT; ++n)
@@ -1482,7 +1492,7 @@ __global__ void __launch_bounds__(kWmThreads, 1)
           uint32_t a[4];  // rows g, g + 8 at positions (2tq, 2tq+1); the same at (2tq+8, 2tq+9)
           u0.pair(s, a[0], a[2]);
           u1.pair(s, a[1], a[3]);
-          const uint32_t addr = bq + (s >> 2) * C::kBAtom + boff[s & 3];
+          const uint32_t addr = bqa[s & 3] + (s >> 2) * C::kBAtom;
           uint32_t b[2 * NT];
           if constexpr (NT == 2) {
             asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -1494,11 +1504,10 @@ __global__ void __launch_bounds__(kWmThreads, 1)
                          : "r"(addr));
           }
           if constexpr (F == kQ4_K) {
-            const uint32_t am[4] = {u0.min_pair(s), u1.min_pair(s), u0.min_pair(s), u1.min_pair(s)};
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
               mma_16816(m1[n], a, b[2 * n], b[2 * n + 1]);
-              mma_16816(m2[n], am, b[2 * n], b[2 * n + 1]);
+              mma_16816(m2[n], s < 8 ? am_lo : am_hi, b[2 * n], b[2 * n + 1]);
             }
           } else {
 #pragma unroll
