@@ -404,6 +404,82 @@ UAII_MOE_API int uaii_moe_profile_enable(uaii_moe_backend* b, int enable);
 UAII_MOE_API int uaii_moe_profile_read(uaii_moe_backend* b, double* phase_ms, uint64_t* phase_calls,
                                        uint64_t* kernel_launches);
 
+/* ---- Batched greedy decode of a GGUF MoE transformer on the device.  Replaces the
+ * reference's decode loop, Session::generate (libs/uaii-runtime/src/session.cpp:910-1046),
+ * over the seq-1 transformer graph its GGUF loader builds
+ * (libs/uaii-loaders/src/gguf.cpp:905-1210) with a host f32 KV cache of batch 1
+ * (include/uaii/runtime/kv_cache.hpp:16-190, session.cpp:852).  Here `batch`
+ * sequences advance one position per step together, every activation and the KV
+ * cache (f16, [batch, n_kv_heads, max_seq, head_dim] per layer) stay on the device:
+ * embedding, per block RMSNorm -> Q/K/V projection (packed MatMul) -> RoPE -> KV
+ * append -> grouped-query attention -> O projection -> residual Add -> RMSNorm -> MoE
+ * FFN layer -> residual Add, then RMSNorm -> output projection -> arg-max (the
+ * reference's greedy sampler, libs/uaii-runtime/src/sampling.cpp:38-50).  All weights
+ * must be device memory and stay valid while the decoder lives. */
+typedef struct uaii_moe_decoder_config {
+  int64_t n_layers;
+  int64_t d_model;
+  int64_t n_heads;
+  int64_t n_kv_heads;
+  int64_t head_dim;  /* 128 */
+  int64_t vocab;
+  int64_t batch;
+  int64_t max_seq;   /* cache positions per sequence */
+  float rope_theta;
+  float rms_eps;
+  int32_t rope_mode; /* 0: pairs (2i, 2i+1) as for llama/Mixtral; 2: NeoX pairs (i, i + head_dim/2) */
+} uaii_moe_decoder_config;
+
+/* One block: attention (GGUF blk.N.attn_*) and the MoE FFN layer.  Norm weights f32 [d_model];
+ * wq [n_heads*head_dim, d_model], wk / wv [n_kv_heads*head_dim, d_model], wo [d_model,
+ * n_heads*head_dim] in GGUF block formats. */
+typedef struct uaii_moe_decoder_block {
+  const float* attn_norm;
+  const void* wq;
+  int32_t wq_fmt;
+  const void* wk;
+  int32_t wk_fmt;
+  const void* wv;
+  int32_t wv_fmt;
+  const void* wo;
+  int32_t wo_fmt;
+  const float* ffn_norm;
+  uaii_moe_layer moe;
+} uaii_moe_decoder_block;
+
+typedef struct uaii_moe_decoder uaii_moe_decoder;
+
+/* blocks [n_layers]; output_norm f32 [d_model]; token_embd [vocab, d_model] (GGUF format, f16
+ * or f32); output [vocab, d_model] (GGUF format) or NULL for tied embeddings (the reference
+ * reuses the table, gguf.cpp:1195-1200).  The decode position starts at 0. */
+UAII_MOE_API int uaii_moe_decoder_create(uaii_moe_backend* b, const uaii_moe_decoder_config* cfg,
+                                         const uaii_moe_decoder_block* blocks, const float* output_norm,
+                                         const void* token_embd, int embd_fmt, const void* output, int output_fmt,
+                                         uaii_moe_decoder** out);
+UAII_MOE_API void uaii_moe_decoder_destroy(uaii_moe_decoder* d);
+/* Cache positions [0, n_pos) of layer `layer` from f32 k, v [batch, n_kv_heads, n_pos, head_dim]
+ * (host or device; stored in f16); the decode position becomes n_pos. */
+UAII_MOE_API int uaii_moe_decoder_set_kv(uaii_moe_decoder* d, int64_t layer, const float* k, const float* v,
+                                         int64_t n_pos);
+/* Synthetic prefill: K and V of every layer at positions [0, n_pos) drawn N(0, 1) from the
+ * counter-based generator keyed by (seed, layer, sequence, head); the position becomes n_pos. */
+UAII_MOE_API int uaii_moe_decoder_fill_kv(uaii_moe_decoder* d, int64_t n_pos, uint64_t seed);
+/* One step at the current position: tokens [batch]; logits [batch, vocab] and next [batch]
+ * (host, device or NULL).  Returns after the copies when an output is host memory. */
+UAII_MOE_API int uaii_moe_decoder_step(uaii_moe_decoder* d, const int32_t* tokens, float* logits, int32_t* next);
+/* `steps` greedy steps from tokens [batch]: out [steps, batch] token ids (host or device). */
+UAII_MOE_API int uaii_moe_decoder_generate(uaii_moe_decoder* d, const int32_t* tokens, int64_t steps, int32_t* out);
+UAII_MOE_API int64_t uaii_moe_decoder_position(const uaii_moe_decoder* d);
+
+/* Device-side synthetic inputs (no reference counterpart): uaii_moe_fill_normal's draws
+ * written on the backend's stream (equal to the host generator's up to the last bit of the
+ * device's double-precision log/sin/cos), and uaii_moe_quantize_rows on the device (the same
+ * bytes as the host quantizer for the same f32 input).  Device pointers only. */
+UAII_MOE_API int uaii_moe_fill_normal_device(uaii_moe_backend* b, float* out, int64_t n, uint64_t seed, uint64_t stream,
+                                             float mean, float std);
+UAII_MOE_API int uaii_moe_quantize_rows_device(uaii_moe_backend* b, int fmt, const float* src, int64_t rows,
+                                               int64_t cols, void* dst);
+
 /* Bytes of one row of n elements in `fmt` (include/uaii/quant/formats.hpp:81-102). */
 UAII_MOE_API uint64_t uaii_moe_packed_nbytes(int fmt, int64_t n);
 

@@ -132,6 +132,12 @@ class Reference:
             "uref_quant_gemm": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p]),
             "uref_gguf_tensor_raw": (c_int64, [c_char_p, c_char_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
             "uref_gguf_tensor_f32": (c_int64, [c_char_p, c_char_p, c_void_p, c_int64]),
+            "uref_rmsnorm": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p]),
+            "uref_rope": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_float, c_int64, c_int, c_void_p]),
+            "uref_attention_kv": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p,
+                                          c_void_p, c_int64, c_void_p]),
+            "uref_embedding": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int64, c_int64, c_void_p]),
+            "uref_softmax": (c_int, [c_void_p, c_int64, c_int64, c_void_p]),
             "uref_gguf_write_f32": (c_int, [c_char_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
         }
         for n, (r, a) in sig.items():
@@ -168,6 +174,39 @@ class Reference:
         if got < 0:
             raise ValueError(f"reference gguf status {-got}: {self.L.uref_last_error().decode()}")
         return out[:got].copy()
+
+    # ---- decode-step kernels (rows are independent sequences)
+    def rmsnorm(self, x, w, eps):
+        y = np.empty_like(x)
+        self._chk(self.L.uref_rmsnorm(_p(x), _p(w), x.shape[0], x.shape[1], eps, _p(y)))
+        return y
+
+    def rope(self, x, positions, theta, head_dim, mode):
+        y = np.empty_like(x)
+        pos = np.ascontiguousarray(positions, np.float32)
+        self._chk(self.L.uref_rope(_p(x), _p(pos), x.shape[0], x.shape[1], theta, head_dim, mode, _p(y)))
+        return y
+
+    def attention_kv(self, q, k, v, num_heads, past_k, past_v):
+        """q [B, q_dim], k/v [B, kv_dim], past_k/v [B, past, kv_dim] (past may be 0)."""
+        B, q_dim = q.shape
+        out = np.empty_like(q)
+        past = past_k.shape[1]
+        self._chk(self.L.uref_attention_kv(_p(q), _p(k), _p(v), B, q_dim, k.shape[1], num_heads,
+                                           _p(past_k) if past else None, _p(past_v) if past else None, past,
+                                           _p(out)))
+        return out
+
+    def embedding(self, tokens, table, fmt, vocab, D):
+        t = np.ascontiguousarray(tokens, np.float32)
+        out = np.empty((t.shape[0], D), np.float32)
+        self._chk(self.L.uref_embedding(_p(t), t.shape[0], _p(table), fmt, vocab, D, _p(out)))
+        return out
+
+    def softmax(self, x):
+        y = np.empty_like(x)
+        self._chk(self.L.uref_softmax(_p(x), x.shape[0], x.shape[1], _p(y)))
+        return y
 
     def gguf_write_f32(self, path: str, tensors):
         """tensors: [(name, f32 array)] written by the reference's gguf_write_f32 (dims reversed as GGUF)."""

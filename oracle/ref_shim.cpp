@@ -1,7 +1,7 @@
 // ref_shim.cpp -- extern "C" entry points over the reference's OWN compiled code.
 //
 // TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
-// fifteen unmodified source files of the reference (arjun988/Universal-AI-Inference)
+// sixteen unmodified source files of the reference (arjun988/Universal-AI-Inference)
 // into oracle/_ref/libuaii_ref.so.  Nothing here re-implements the reference:
 // each function only builds the reference's TensorView arguments and calls
 //   uaii::quant::dequant_gguf_row      (libs/uaii-quant/src/gguf_dequant.cpp:420-439)
@@ -9,6 +9,9 @@
 //   uaii::kernels::moe_experts_swiglu_f32 (libs/uaii-kernels/src/transformer.cpp:522-612)
 //   uaii::kernels::matmul_f32          (libs/uaii-kernels/src/matmul.cpp:22-56)
 //   uaii::kernels::quant_gemm_f32      (libs/uaii-kernels/src/quant_gemm.cpp:22-70)
+//   uaii::kernels::rmsnorm_f32 / rope_f32 / attention_kv_f32 / embedding_f32 / softmax_f32
+//                                      (libs/uaii-kernels/src/norm.cpp:89-130, transformer.cpp:61-345,
+//                                       softmax.cpp:11-77)
 //   uaii::loaders::gguf_read_header / gguf_load_tensor_f32 / gguf_load_tensor_raw /
 //   gguf_write_f32                     (libs/uaii-loaders/src/gguf.cpp:374-650)
 // It is used by tests/ to pin oracle/moe_oracle.c, by tests/golden/make_golden.py
@@ -130,6 +133,61 @@ std::int64_t uref_gguf_tensor_f32(const char* path, const char* name, float* out
   if ((std::int64_t)vals.size() > cap) return -1;
   std::copy(vals.begin(), vals.end(), out);
   return (std::int64_t)vals.size();
+}
+
+// ---- the decode step's other reference kernels, batch rows at a time (the reference runs
+// them with batch 1 per sequence; each row is independent).
+int uref_rmsnorm(const float* x, const float* w, std::int64_t rows, std::int64_t D, float eps, float* y) {
+  const std::int64_t s[2] = {rows, D}, sw[1] = {D};
+  TensorView vx = f32_view(x, s, 2), vy = f32_view(y, s, 2), vw = f32_view(w, sw, 1);
+  return status(uaii::kernels::rmsnorm_f32(vx, &vw, &vy, eps));
+}
+
+// RoPE of rows [rows, dim] at positions[r] (f32), per head of head_dim (transformer.cpp:144-225).
+int uref_rope(const float* x, const float* positions, std::int64_t rows, std::int64_t dim, float theta,
+              std::int64_t head_dim, int mode, float* y) {
+  const std::int64_t s[2] = {rows, dim}, sp[1] = {rows};
+  TensorView vx = f32_view(x, s, 2), vy = f32_view(y, s, 2), vp = f32_view(positions, sp, 1);
+  return status(uaii::kernels::rope_f32(vx, &vp, &vy, theta, head_dim, mode));
+}
+
+// One new position per sequence over past K/V [B, past, kv_dim] (transformer.cpp:227-345).
+int uref_attention_kv(const float* q, const float* k, const float* v, std::int64_t B, std::int64_t q_dim,
+                      std::int64_t kv_dim, int num_heads, const float* past_k, const float* past_v, std::int64_t past,
+                      float* out) {
+  const std::int64_t sq[2] = {B, q_dim}, sk[2] = {B, kv_dim}, sp[3] = {B, past, kv_dim};
+  TensorView vq = f32_view(q, sq, 2), vk = f32_view(k, sk, 2), vv = f32_view(v, sk, 2), vo = f32_view(out, sq, 2);
+  TensorView pk = f32_view(past_k, sp, 3), pv = f32_view(past_v, sp, 3);
+  return status(uaii::kernels::attention_kv_f32(vq, vk, vv, &vo, num_heads, 0.0f, true, past > 0 ? &pk : nullptr,
+                                                past > 0 ? &pv : nullptr, nullptr, nullptr));
+}
+
+// Token rows of a packed (GGUF) or f32 table [vocab, D] (transformer.cpp:61-138).
+int uref_embedding(const float* tokens, std::int64_t B, const void* table, int fmt, std::int64_t vocab, std::int64_t D,
+                   float* out) {
+  const std::int64_t st[2] = {B, 1}, sw[2] = {vocab, D}, so[2] = {B, D};
+  TensorView vt = f32_view(tokens, st, 2), vo = f32_view(out, so, 2);
+  TensorView vw;
+  vw.shape = sw;
+  vw.rank = 2;
+  vw.data = const_cast<void*>(table);
+  if (fmt == 0) {
+    vw.dtype = DType::F32;
+    vw.nbytes = sizeof(float) * (std::size_t)(vocab * D);
+  } else {
+    vw.dtype = DType::Unknown;
+    vw.quant_format = static_cast<uaii::quant::QuantFormat>(fmt);
+    vw.quant_rows = vocab;
+    vw.quant_cols = D;
+    vw.nbytes = uaii::quant::packed_nbytes(vw.quant_format, (std::size_t)D) * (std::size_t)vocab;
+  }
+  return status(uaii::kernels::embedding_f32(vt, vw, &vo));
+}
+
+int uref_softmax(const float* x, std::int64_t rows, std::int64_t n, float* y) {
+  const std::int64_t s[2] = {rows, n};
+  TensorView vx = f32_view(x, s, 2), vy = f32_view(y, s, 2);
+  return status(uaii::kernels::softmax_f32(vx, &vy, -1));
 }
 
 // A GGUF file written by the reference's own writer: f32 tensors (dims innermost

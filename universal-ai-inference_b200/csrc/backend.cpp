@@ -40,12 +40,6 @@ Error cuda_status(cudaError_t st, const char* what) {
   return Error::make(ErrorCode::Internal, std::string("CUDA ") + what + ": " + cudaGetErrorString(st));
 }
 
-#define UAII_TRY(expr)                   \
-  do {                                   \
-    Error _e = (expr);                   \
-    if (!_e.ok()) return _e;             \
-  } while (0)
-#define UAII_CUDA(expr, what) UAII_TRY(cuda_status((expr), what))
 
 namespace {
 
@@ -1183,6 +1177,7 @@ Error MoeCudaBackend::ffn(const LayerArgs& Lin, const float* x, int64_t T, float
     ge = &graphs_[key];
     if (ge->exec) {
       UAII_CUDA(cudaGraphLaunch(ge->exec, stream_), "GraphLaunch");
+      count_launches(ge->launches);
       last_plan_ = P;
       return Error::success();
     }
@@ -1190,8 +1185,10 @@ Error MoeCudaBackend::ffn(const LayerArgs& Lin, const float* x, int64_t T, float
   }
   if (ge) {
     UAII_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "StreamBeginCapture");
+    const uint64_t before = launches_;
     const Error e = ffn_launch(L, P, T, static_cast<const float*>(xd), static_cast<const float*>(wd), logits, po,
                                rscratch, rsb, yo);
+    ge->launches = launches_ - before;
     cudaGraph_t graph = nullptr;
     const cudaError_t ce = cudaStreamEndCapture(stream_, &graph);
     if (!e.ok()) {
@@ -1395,9 +1392,6 @@ bool uaii_b200::layer_args_from_c(const uaii_moe_layer* l, LayerArgs* out) {
 // extern "C" shim (include/uaii_moe.h)
 using namespace uaii_b200;
 
-struct uaii_moe_backend {
-  MoeCudaBackend impl;
-};
 
 namespace {
 thread_local std::string g_last_error;

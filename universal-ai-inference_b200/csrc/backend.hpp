@@ -149,6 +149,9 @@ class MoeCudaBackend {
   // Schedule chosen by the most recent expert-product call (routed experts).
   ExpertPlan last_plan() const { return last_plan_; }
   cudaStream_t stream() const { return stream_; }
+  // Kernels launched on this backend's stream by code built on it (the decoder's own kernels),
+  // added to the launch count uaii_moe_profile_read reports.
+  void add_launches(uint64_t n) { count_launches(n); }
   int device() const { return device_; }
 
  private:
@@ -236,6 +239,7 @@ class MoeCudaBackend {
   struct GraphEntry {
     int seen = 0;
     cudaGraphExec_t exec = nullptr;
+    uint64_t launches = 0;  // kernels in the captured sequence (counted again on every replay)
   };
   std::map<std::vector<int64_t>, GraphEntry> graphs_;
   bool graphs_on_ = true;
@@ -260,3 +264,15 @@ int report_status(const Error& e);
 Error cuda_status(cudaError_t st, const char* what);
 
 }  // namespace uaii_b200
+
+// The C ABI's opaque backend handle (include/uaii_moe.h).
+struct uaii_moe_backend {
+  uaii_b200::MoeCudaBackend impl;
+};
+
+#define UAII_TRY(expr)                   \
+  do {                                   \
+    ::uaii_b200::Error _e = (expr);      \
+    if (!_e.ok()) return _e;             \
+  } while (0)
+#define UAII_CUDA(expr, what) UAII_TRY(::uaii_b200::cuda_status((expr), what))

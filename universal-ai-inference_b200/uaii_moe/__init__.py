@@ -121,6 +121,16 @@ def _load():
         "uaii_moe_packed_nbytes": (c_uint64, [c_int, c_int64]),
         "uaii_moe_quantize_rows": (c_int, [c_int, c_void_p, c_int64, c_int64, c_void_p]),
         "uaii_moe_fill_normal": (c_int, [c_void_p, c_int64, c_uint64, c_uint64, c_float, c_float]),
+        "uaii_moe_decoder_create": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int,
+                                            POINTER(c_void_p)]),
+        "uaii_moe_decoder_destroy": (None, [c_void_p]),
+        "uaii_moe_decoder_set_kv": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64]),
+        "uaii_moe_decoder_fill_kv": (c_int, [c_void_p, c_int64, c_uint64]),
+        "uaii_moe_decoder_step": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+        "uaii_moe_decoder_generate": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
+        "uaii_moe_decoder_position": (c_int64, [c_void_p]),
+        "uaii_moe_fill_normal_device": (c_int, [c_void_p, c_void_p, c_int64, c_uint64, c_uint64, c_float, c_float]),
+        "uaii_moe_quantize_rows_device": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_int64, c_void_p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -144,7 +154,10 @@ EXPORTED = ("uaii_moe_abi_version", "uaii_moe_last_error", "uaii_moe_backend_cre
             "uaii_moe_selftest_wait_timeout", "uaii_moe_profile_enable",
             "uaii_moe_profile_read",
             "uaii_moe_packed_nbytes", "uaii_moe_quantize_rows",
-            "uaii_moe_fill_normal")
+            "uaii_moe_fill_normal", "uaii_moe_decoder_create", "uaii_moe_decoder_destroy",
+            "uaii_moe_decoder_set_kv", "uaii_moe_decoder_fill_kv", "uaii_moe_decoder_step",
+            "uaii_moe_decoder_generate", "uaii_moe_decoder_position", "uaii_moe_fill_normal_device",
+            "uaii_moe_quantize_rows_device")
 
 
 def _check(status: int):
@@ -427,6 +440,81 @@ class GgufFile:
         _check(lib.uaii_moe_gguf_moe_layer(self._h, block, GGUF_SHEXP_GATE if shexp_gate else 0, ctypes.byref(L)))
         L._keep = self  # the layer points into this mapping
         return L
+
+
+class DecoderConfig(ctypes.Structure):
+    _fields_ = [("n_layers", c_int64), ("d_model", c_int64), ("n_heads", c_int64), ("n_kv_heads", c_int64),
+                ("head_dim", c_int64), ("vocab", c_int64), ("batch", c_int64), ("max_seq", c_int64),
+                ("rope_theta", c_float), ("rms_eps", c_float), ("rope_mode", c_int32)]
+
+
+class DecoderBlock(ctypes.Structure):
+    _fields_ = [("attn_norm", c_void_p), ("wq", c_void_p), ("wq_fmt", c_int32), ("wk", c_void_p),
+                ("wk_fmt", c_int32), ("wv", c_void_p), ("wv_fmt", c_int32), ("wo", c_void_p), ("wo_fmt", c_int32),
+                ("ffn_norm", c_void_p), ("moe", Layer)]
+
+
+class Decoder:
+    """Batched greedy decode of a GGUF MoE transformer on the device (uaii_moe_decoder_*).
+
+    blocks: list of dicts with attn_norm, wq, wk, wv, wo (+ *_fmt), ffn_norm and moe (a Layer);
+    every array is device memory (torch CUDA tensors), kept alive by this object."""
+
+    def __init__(self, backend: "Backend", n_layers, d_model, n_heads, n_kv_heads, vocab, batch, max_seq, blocks,
+                 output_norm, token_embd, embd_fmt, output=None, output_fmt=0, head_dim=128, rope_theta=1e6,
+                 rms_eps=1e-5, rope_mode=0):
+        self._keep = [blocks, output_norm, token_embd, output]
+        cfg = DecoderConfig(n_layers, d_model, n_heads, n_kv_heads, head_dim, vocab, batch, max_seq, rope_theta,
+                            rms_eps, rope_mode)
+        arr = (DecoderBlock * n_layers)()
+        for i, b in enumerate(blocks):
+            arr[i] = DecoderBlock(ptr(b["attn_norm"]), ptr(b["wq"]), b["wq_fmt"], ptr(b["wk"]), b["wk_fmt"],
+                                  ptr(b["wv"]), b["wv_fmt"], ptr(b["wo"]), b["wo_fmt"], ptr(b["ffn_norm"]), b["moe"])
+        self._cfg, self._arr = cfg, arr
+        h = c_void_p()
+        _check(lib.uaii_moe_decoder_create(backend.handle, ctypes.byref(cfg), arr, ptr(output_norm), ptr(token_embd),
+                                           embd_fmt, ptr(output), output_fmt, ctypes.byref(h)))
+        self._h = h
+        self.batch, self.vocab = batch, vocab
+
+    def close(self):
+        if self._h:
+            lib.uaii_moe_decoder_destroy(self._h)
+            self._h = c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def position(self) -> int:
+        return int(lib.uaii_moe_decoder_position(self._h))
+
+    def set_kv(self, layer: int, k, v, n_pos: int):
+        """K, V [batch, n_kv_heads, n_pos, head_dim] f32 (host or device) for positions [0, n_pos)."""
+        _check(lib.uaii_moe_decoder_set_kv(self._h, layer, ptr(k), ptr(v), n_pos))
+
+    def fill_kv(self, n_pos: int, seed: int = 0):
+        _check(lib.uaii_moe_decoder_fill_kv(self._h, n_pos, seed))
+
+    def step(self, tokens, logits=None, next_tokens=None):
+        _check(lib.uaii_moe_decoder_step(self._h, ptr(tokens), ptr(logits), ptr(next_tokens)))
+
+    def generate(self, tokens, steps: int, out):
+        _check(lib.uaii_moe_decoder_generate(self._h, ptr(tokens), steps, ptr(out)))
+
+
+def fill_normal_device(backend: "Backend", out, seed: int, stream: int, mean: float = 0.0, std: float = 1.0):
+    """uaii_moe_fill_normal's draws written on the device (out: a CUDA f32 tensor)."""
+    _check(lib.uaii_moe_fill_normal_device(backend.handle, ptr(out), out.numel(), seed, stream, mean, std))
+
+
+def quantize_rows_device(backend: "Backend", fmt: int, src, dst):
+    """GGUF blocks of the f32 rows src [rows, cols] into dst (CUDA tensors), as quantize_rows does."""
+    rows, cols = src.shape
+    _check(lib.uaii_moe_quantize_rows_device(backend.handle, fmt, ptr(src), rows, cols, ptr(dst)))
 
 
 def make_layer(D, E, I, top_k, norm_topk, router_w, gate, gfmt, up, ufmt, down, dfmt,
