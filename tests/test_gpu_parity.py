@@ -460,6 +460,29 @@ def test_quad_schedule_vs_oracle_and_unit_schedule(backend, oracle, um, gf, df, 
         assert rel_err(ys[3][0], ys[4][0]) <= 1e-4
 
 
+@pytest.mark.parametrize("gf,df", [(14, 16), (14, 14)])
+def test_mixed_schedule_at_16_slot_tiles(backend, oracle, um, gf, df):
+    """16-slot tiles of a K-quant layer: gate/up on tcgen05 (operands in tc_kpos order), the down
+    projection on the quad schedule (its h written by the tcgen05 epilogue in the quad order)."""
+    T, D, E, I, k = 32, 1024, 8, 1024, 2
+    x, w, G, U, Dn = layer_case(um, gf, df, T, D, E, I, k, 77)
+    _, pr, _ = oracle.router(x, w)
+    y_ref, _, _ = oracle.experts_packed(x, G, gf, U, gf, Dn, df, pr, E, I, k, 1)
+    L = um.make_layer(D, E, I, k, 1, w, G, gf, U, gf, Dn, df)
+    y = np.empty_like(x)
+    backend.ffn(L, x, T, y)
+    plan = backend.last_plan()
+    assert (plan["schedule"], plan["slot_tile"]) == ("tcgen05", 16), plan
+    assert rel_err(y, y_ref) <= REL_TOL
+    y2 = np.empty_like(x)
+    backend.set_expert_path(2)  # tcgen05 for both projections
+    try:
+        backend.ffn(L, x, T, y2)
+    finally:
+        backend.set_expert_path(0)
+    assert rel_err(y, y2) <= 1e-3
+
+
 def test_automatic_schedule_picks_warp_mma_for_decode(backend, um):
     D, E, I, k = 1024, 8, 2048, 2
     # tiles hold the mean slots per expert plus two standard deviations below 32 slots

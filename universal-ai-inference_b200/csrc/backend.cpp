@@ -528,6 +528,10 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t s
     if (p.warp_mma) p.bn = warp_bn(tpe);
     // K-quant layers run the warp schedule over whole super-blocks (path 4 keeps the per-unit one)
     p.quad_mma = p.warp_mma && path_ != 4 && quad_mma_format(L.gate.fmt) && quad_mma_format(L.down.fmt);
+    // 16-slot tiles: the down projection is faster on the quad schedule, gate/up on tcgen05
+    // (Mixtral-shaped layer, 32 tokens: down 0.160 -> 0.121 ms; gate/up 0.191 vs 0.247 ms)
+    p.down_quad = !p.warp_mma && path_ == 0 && warp_ok && p.bn == 16 && quad_mma_format(L.gate.fmt) &&
+                  quad_mma_format(L.down.fmt);
     const int64_t n_tiles = (int64_t)((tpe + p.bn - 1) / p.bn);
     p.splits = pick_splits(active * n_tiles * (L.D / 128), umma_kchunks(L.down.fmt, L.I));
   }
@@ -628,8 +632,11 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
   if (P.umma) {
     // operand orders: x in the gate/up kernel's, h in the down kernel's (operand_order.cuh)
     const int sched = P.quad_mma ? kSchedQuadMma : P.warp_mma ? kSchedWarpMma : kSchedTcgen05;
+    const int dn_sched = P.down_quad ? kSchedQuadMma : sched;
     const int x_order = P.quad_mma ? (L.gate.fmt == kQ4_K ? kOrderQ4K : kOrderQ6K) : P.warp_mma ? kOrderWm : kOrderTc;
-    const int h_order = P.quad_mma ? (L.down.fmt == kQ4_K ? kOrderQ4K : kOrderQ6K) : P.warp_mma ? kOrderWm : kOrderTc;
+    const int h_order = dn_sched == kSchedQuadMma ? (L.down.fmt == kQ4_K ? kOrderQ4K : kOrderQ6K)
+                        : P.warp_mma                ? kOrderWm
+                                                    : kOrderTc;
     void* xp16 = carve(2 * (size_t)(S * D));
     void* h16 = carve(2 * (size_t)(S * I));
     splits = P.splits;
@@ -654,7 +661,7 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
     phase_end();
     phase_begin(kDown);
     UAII_CUDA(launch_down_umma(L.down.fmt, dd, dpitch, E, D, I, h16, S, rb.counts, rb.offsets, tile_base, P.bn, splits,
-                               out, dev_err_, stream_, sched),
+                               out, dev_err_, stream_, dn_sched),
               "down(tensor cores)");
     phase_end();
     count_launches(4);

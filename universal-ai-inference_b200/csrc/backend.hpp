@@ -87,6 +87,7 @@ struct ExpertPlan {
   bool umma = false;   // tensor-core grouped GEMM (else CUDA-core GEMV)
   bool warp_mma = false;      // ... on an mma.sync schedule (decode widths), else tcgen05
   bool quad_mma = false;      // ... the mma.sync schedule over whole K-quant super-blocks
+  bool down_quad = false;     // the down projection alone on the quad schedule (16-slot tiles, gate/up on tcgen05)
   bool umma_refused = false;  // tensor cores forced but the layer does not qualify
   int bn = 16;         // slots per tile (MMA N)
   int splits = 1;      // K splits of the down projection

@@ -19,25 +19,31 @@ cudaError_t launch_add_rmsnorm(float* x, const float* delta, const float* w, int
 cudaError_t launch_rope_append(const float* qkv, int64_t B, int64_t H, int64_t Hkv, int64_t hd, const float* freq,
                                int64_t pos, int mode, float* q_out, void* kc, void* vc, int64_t max_seq,
                                cudaStream_t st);
-// Splits (of 256 positions) of the attention over len positions; partial buffers hold
+// Splits (of 128 positions) of the attention over len positions; partial buffers hold
 // B*H*splits*hd (po) and B*H*splits (pm, pl) floats.
 int attn_splits(int64_t len);
-// out [B, H*hd] = attention of q over the first len cached positions (hd = 128).
-cudaError_t launch_attn_decode(const float* q, const void* kc, const void* vc, int64_t B, int64_t H, int64_t Hkv,
+// TMA map (128 bytes, CUtensorMap) of an f16 KV cache of `rows` rows of 128 elements.
+constexpr int kKvMapBytes = 128;
+bool make_kv_map(void* map, const void* cache, int64_t rows);
+// out [B, H*hd] = attention of q over the first len cached positions (hd = 128) on the tensor
+// cores; kmap / vmap from make_kv_map.  A copy that never lands sets *err after about a
+// second instead of hanging.
+cudaError_t launch_attn_decode(const void* kmap, const void* vmap, const float* q, int64_t B, int64_t H, int64_t Hkv,
                                int64_t hd, int64_t len, int64_t max_seq, float* po, float* pm, float* pl, float* out,
-                               cudaStream_t st);
+                               int* err, cudaStream_t st);
 // dst[r * dst_pitch + c] = f16(src[r * cols + c]) (KV-cache rows from f32).
 cudaError_t launch_to_half_rows(const float* src, int64_t rows, int64_t cols, void* dst, int64_t dst_pitch,
                                 cudaStream_t st);
 // out[b] = first index of the largest logit of row b (the reference's greedy sampler).
 cudaError_t launch_argmax(const float* logits, int64_t B, int64_t V, int32_t* out, cudaStream_t st);
-// Device-side synthetic inputs: the counter-based normals of uaii_moe_fill_normal (f32 or
-// rounded to f16) and the GGUF block quantizers of uaii_moe_quantize_rows.
+// Device-side synthetic inputs: the counter-based normals of uaii_moe_fill_normal (f32, or
+// rounded to f16 row by row) and the GGUF block quantizers of uaii_moe_quantize_rows.
 uint64_t normal_key(uint64_t seed, uint64_t stream);
 cudaError_t launch_fill_normal(float* out, int64_t n, uint64_t seed, uint64_t stream, float mean, float std,
                                cudaStream_t st);
-cudaError_t launch_fill_normal_f16(void* out, int64_t n, uint64_t seed, uint64_t stream, float mean, float std,
-                                   cudaStream_t st);
+// rows of cols f16 draws, pitch elements apart; row r uses generator stream stream0 + r.
+cudaError_t launch_fill_normal_f16_rows(void* out, int64_t rows, int64_t cols, int64_t pitch, uint64_t seed,
+                                        uint64_t stream0, float mean, float std, cudaStream_t st);
 cudaError_t launch_quantize_rows(int fmt, const float* src, int64_t rows, int64_t cols, void* dst, cudaStream_t st);
 
 }  // namespace uaii_b200

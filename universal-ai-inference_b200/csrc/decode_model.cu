@@ -12,6 +12,7 @@
 // transformer.cpp:61-433) with explicit round-to-nearest intrinsics, so nvcc cannot
 // contract a multiply and an add; reductions are tree-shaped (rounding-level
 // differences from the reference's sequential sums).
+#include <cuda.h>
 #include <cuda_fp16.h>
 
 #include <cfloat>
@@ -61,26 +62,53 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 // ---- x += delta (the graph's residual Add, when delta is given); y = RMSNorm(x) * w:
 // ms = sum(x^2) / D, inv = 1 / sqrt(ms + eps), y = (x * inv) * w (norm.cpp:114-128).
-__global__ void add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
-                                   int64_t D, float eps, float* __restrict__ y) {
+// One block per row, float4 columns; a thread keeps its (at most kNormVec) float4s of x in
+// registers between the two passes, so every load of a row is issued at once.
+constexpr int kNormVec = 4;
+__global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta,
+                                                          const float* __restrict__ w, int D, float eps,
+                                                          float* __restrict__ y) {
   __shared__ float red[32];
-  float* xr = x + blockIdx.x * D;
-  const float* dr = delta ? delta + blockIdx.x * D : nullptr;
+  float4* xr = reinterpret_cast<float4*>(x + (int64_t)blockIdx.x * D);
+  const float4* dr = delta ? reinterpret_cast<const float4*>(delta + (int64_t)blockIdx.x * D) : nullptr;
+  const int n4 = D / 4;
+  float4 v[kNormVec];
   float ss = 0.f;
-  for (int64_t i = threadIdx.x; i < D; i += blockDim.x) {
-    float v = xr[i];
-    if (dr) {
-      v = __fadd_rn(v, dr[i]);
-      xr[i] = v;
+#pragma unroll
+  for (int k = 0; k < kNormVec; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i < n4) {
+      v[k] = xr[i];
+      if (dr) {
+        const float4 d = dr[i];
+        v[k].x = __fadd_rn(v[k].x, d.x);
+        v[k].y = __fadd_rn(v[k].y, d.y);
+        v[k].z = __fadd_rn(v[k].z, d.z);
+        v[k].w = __fadd_rn(v[k].w, d.w);
+        xr[i] = v[k];
+      }
+      ss = __fmaf_rn(v[k].x, v[k].x, ss);
+      ss = __fmaf_rn(v[k].y, v[k].y, ss);
+      ss = __fmaf_rn(v[k].z, v[k].z, ss);
+      ss = __fmaf_rn(v[k].w, v[k].w, ss);
     }
-    ss = __fmaf_rn(v, v, ss);
   }
   const float ms = __fdiv_rn(block_sum(ss, red), (float)D);
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
-  float* yr = y + blockIdx.x * D;
-  for (int64_t i = threadIdx.x; i < D; i += blockDim.x) {
-    const float v = __fmul_rn(xr[i], inv);
-    yr[i] = w ? __fmul_rn(v, w[i]) : v;
+  float4* yr = reinterpret_cast<float4*>(y + (int64_t)blockIdx.x * D);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int k = 0; k < kNormVec; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i < n4) {
+      float4 o = make_float4(__fmul_rn(v[k].x, inv), __fmul_rn(v[k].y, inv), __fmul_rn(v[k].z, inv),
+                             __fmul_rn(v[k].w, inv));
+      if (wr) {
+        const float4 g = wr[i];
+        o = make_float4(__fmul_rn(o.x, g.x), __fmul_rn(o.y, g.y), __fmul_rn(o.z, g.z), __fmul_rn(o.w, g.w));
+      }
+      yr[i] = o;
+    }
   }
 }
 
@@ -98,18 +126,18 @@ __global__ void rope_append_kernel(const float* __restrict__ qkv, int64_t H, int
                                    const float* __restrict__ freq, int64_t pos, int mode, float* __restrict__ q_out,
                                    __half* __restrict__ kc, __half* __restrict__ vc, int64_t max_seq) {
   const int64_t b = blockIdx.x;
-  const int64_t q_dim = H * hd, kv_dim = Hkv * hd, half = hd / 2;
+  const int q_dim = (int)(H * hd), kv_dim = (int)(Hkv * hd), half = (int)(hd / 2), nq = (int)H * half;
   const float* row = qkv + b * (q_dim + 2 * kv_dim);
   const float fpos = (float)pos;
   // pairs: H * half of q, then Hkv * half of k
-  for (int64_t p = threadIdx.x; p < (H + Hkv) * half; p += blockDim.x) {
-    const bool is_q = p < H * half;
-    const int64_t pp = is_q ? p : p - H * half;
-    const int64_t h = pp / half, i = pp % half;
+  for (int p = threadIdx.x; p < nq + (int)Hkv * half; p += blockDim.x) {
+    const bool is_q = p < nq;
+    const int pp = is_q ? p : p - nq;
+    const int h = pp / half, i = pp - h * half;
     const float angle = __fmul_rn(fpos, freq[i]);
     float s, c;
     sincosf(angle, &s, &c);
-    const int64_t ia = mode == 2 ? i : 2 * i, ib = mode == 2 ? i + half : 2 * i + 1;
+    const int ia = mode == 2 ? i : 2 * i, ib = mode == 2 ? i + half : 2 * i + 1;
     const float* src = row + (is_q ? 0 : q_dim) + h * hd;
     float oa, ob;
     rotate(src[ia], src[ib], c, s, oa, ob);
@@ -122,145 +150,217 @@ __global__ void rope_append_kernel(const float* __restrict__ qkv, int64_t H, int
       dst[ib] = __float2half_rn(ob);
     }
   }
-  for (int64_t j = threadIdx.x; j < kv_dim; j += blockDim.x) {
-    const int64_t h = j / hd, d = j % hd;
+  for (int j = threadIdx.x; j < kv_dim; j += blockDim.x) {
+    const int h = j / (int)hd, d = j - h * (int)hd;
     vc[((b * Hkv + h) * max_seq + pos) * hd + d] = __float2half_rn(row[q_dim + kv_dim + j]);
   }
 }
 
 // ---- attention of one new position over the cache (attention_kv_f32, transformer.cpp:227-345:
-// scores q.k * scale, softmax over positions 0..len-1, sum of p * v), split over the
-// positions: CTA (split, kv head, b) handles a chunk for the G = H / Hkv query heads that
-// share the kv head and writes their unnormalised partial sums, maxima and denominators.
-// Threads = head_dim (128): phase 1 has each thread score whole positions for all G heads
-// (K rows read once), phase 3 has thread d accumulate dimension d for all G heads (V rows
-// read coalesced).
-constexpr int kAttnChunk = 256;   // positions per split
+// scores q.k * scale, softmax over positions 0..len-1, sum of p * v), on the tensor cores.
+// CTA (split, kv head, b) handles kAttnChunk positions for the G = H / Hkv query heads that
+// share the kv head (rows 0..G-1 of 16-row mma.sync tiles) and writes their unnormalised
+// partial sums, maxima and denominators.  TMA brings the chunk's K and V rows (f16, 128 dims
+// as two 64-column SWIZZLE_128B boxes each) into shared memory; warp w scores positions
+// 32w .. 32w+31 (S = Q K^T, m16n8k16, K rows as the B operand through ldmatrix), the row
+// maxima and sums meet across the warps in shared memory, and the same warp multiplies its
+// probabilities (the S accumulators re-packed as the A operand) by its V rows (ldmatrix.trans).
+// q and p enter the products rounded to f16; scores, exponentials and sums are f32.
+constexpr int kAttnChunk = 128;   // positions per split
+constexpr int kAttnWarps = 4;     // 32 positions each
 
-template <int HD, int G>
-__global__ void __launch_bounds__(HD) attn_decode_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
-                                                         const __half* __restrict__ vc, int64_t H, int64_t Hkv,
-                                                         int64_t len, int64_t max_seq, float scale,
-                                                         float* __restrict__ po, float* __restrict__ pm,
-                                                         float* __restrict__ pl) {
-  static_assert(HD == 128, "head_dim 128: one thread per dimension");
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// byte offset of (row, 16-byte chunk c of 8) in a [rows][128 B] SWIZZLE_128B box
+__device__ __forceinline__ uint32_t swz(int row, int c) { return (uint32_t)(row * 128 + ((c ^ (row & 7)) << 4)); }
+
+template <int G>
+__global__ void __launch_bounds__(32 * kAttnWarps) attn_mma_kernel(const __grid_constant__ CUtensorMap tk,
+                                                                   const __grid_constant__ CUtensorMap tv,
+                                                                   const float* __restrict__ q, int64_t H, int64_t Hkv,
+                                                                   int64_t len, int64_t max_seq, float scale,
+                                                                   float* __restrict__ po, float* __restrict__ pm,
+                                                                   float* __restrict__ pl, int* err) {
+  static_assert(G >= 1 && G <= 8, "query heads per kv head");
+  constexpr int kBox = kAttnChunk * 128;  // bytes of one 64-column box
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sk = smem;             // K: box 0 (dims 0-63), box 1 (dims 64-127)
+  uint8_t* sv = smem + 2 * kBox;  // V: the same
+  float* red = reinterpret_cast<float*>(smem + 4 * kBox);  // [2][kAttnWarps][8]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(red + 2 * kAttnWarps * 8);
   const int64_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int64_t nsplit = gridDim.x;
-  const int64_t j0 = split * kAttnChunk, j1 = min(len, j0 + kAttnChunk);
-  __shared__ __align__(16) float sq[G][HD];
-  __shared__ __align__(16) float sp[G][kAttnChunk];
-  __shared__ float red[G][HD / 32];
-  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
-#pragma unroll
-  for (int g = 0; g < G; ++g) sq[g][t] = q[(b * H + kvh * G + g) * HD + t];
-  __syncthreads();
-  const __half* K = kc + (b * Hkv + kvh) * max_seq * HD;
-  const __half* V = vc + (b * Hkv + kvh) * max_seq * HD;
-  // phase 1: thread t scores positions j0 + t, j0 + t + HD, ... for all G heads (each K row read once)
-  float mloc[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) mloc[g] = -FLT_MAX;
-  for (int64_t j = j0 + t; j < j1; j += HD) {
-    float acc[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = 0.f;
-    const uint4* kr = reinterpret_cast<const uint4*>(K + j * HD);
-#pragma unroll 2
-    for (int c = 0; c < HD / 8; ++c) {
-      const uint4 u = kr[c];
-      const __half2* h2 = reinterpret_cast<const __half2*>(&u);
-      float kf[8];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 kv = __half22float2(h2[e]);
-        kf[2 * e] = kv.x;
-        kf[2 * e + 1] = kv.y;
-      }
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float4 qa = *reinterpret_cast<const float4*>(&sq[g][8 * c]);
-        const float4 qb = *reinterpret_cast<const float4*>(&sq[g][8 * c + 4]);
-        acc[g] = __fmaf_rn(qa.x, kf[0], acc[g]);
-        acc[g] = __fmaf_rn(qa.y, kf[1], acc[g]);
-        acc[g] = __fmaf_rn(qa.z, kf[2], acc[g]);
-        acc[g] = __fmaf_rn(qa.w, kf[3], acc[g]);
-        acc[g] = __fmaf_rn(qb.x, kf[4], acc[g]);
-        acc[g] = __fmaf_rn(qb.y, kf[5], acc[g]);
-        acc[g] = __fmaf_rn(qb.z, kf[6], acc[g]);
-        acc[g] = __fmaf_rn(qb.w, kf[7], acc[g]);
-      }
-    }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float s = __fmul_rn(acc[g], scale);
-      sp[g][j - j0] = s;
-      mloc[g] = fmaxf(mloc[g], s);
-    }
-  }
-  // phase 2: chunk maximum, exponentials and their sum
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float m = mloc[g];
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[g][w] = m;
+  const int64_t j0 = split * kAttnChunk;
+  const int n = (int)min((int64_t)kAttnChunk, len - j0);
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5, g = lane >> 2, tq = lane & 3;
+  if (t == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  float M[G];
+  if (t == 0) {
+    const int row0 = (int)((b * Hkv + kvh) * max_seq + j0);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(4 * kBox)
+                 : "memory");
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float m = -FLT_MAX;
-    for (int i = 0; i < HD / 32; ++i) m = fmaxf(m, red[g][i]);
-    M[g] = m;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float l = 0.f;
-    for (int64_t j = j0 + t; j < j1; j += HD) {
-      const float e = __expf(__fsub_rn(sp[g][j - j0], M[g]));
-      sp[g][j - j0] = e;
-      l = __fadd_rn(l, e);
-    }
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) red[g][w] = l;
-  }
-  __syncthreads();
-  // phase 3: o[g][t] = sum_j p[g][j] v[j][t]; V rows read coalesced, p four positions at a time
-  float o[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) o[g] = 0.f;
-  const int64_t n = j1 - j0;
-  int64_t jj = 0;
-  for (; jj + 4 <= n; jj += 4) {
-    float v[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = __half2float(V[(j0 + jj + e) * HD + t]);
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float4 p = *reinterpret_cast<const float4*>(&sp[g][jj]);
-      o[g] = __fmaf_rn(p.x, v[0], o[g]);
-      o[g] = __fmaf_rn(p.y, v[1], o[g]);
-      o[g] = __fmaf_rn(p.z, v[2], o[g]);
-      o[g] = __fmaf_rn(p.w, v[3], o[g]);
+    for (int box = 0; box < 2; ++box) {
+      asm volatile(
+          "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+          ::"r"(smem_addr(sk + box * kBox)), "l"(&tk), "r"(smem_addr(bar)), "r"(64 * box), "r"(row0) : "memory");
+      asm volatile(
+          "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+          ::"r"(smem_addr(sv + box * kBox)), "l"(&tv), "r"(smem_addr(bar)), "r"(64 * box), "r"(row0) : "memory");
     }
   }
-  for (; jj < n; ++jj) {
-    const float v = __half2float(V[(j0 + jj) * HD + t]);
+  // Q rows g < G as the A operand of the 8 k-steps: pairs (2tq, 2tq+1) and (2tq+8, 2tq+9)
+  uint32_t qa[8][2];
+  {
+    const float* qr = q + (b * H + kvh * G + (g < G ? g : 0)) * 128;
 #pragma unroll
-    for (int g = 0; g < G; ++g) o[g] = __fmaf_rn(sp[g][jj], v, o[g]);
+    for (int ks = 0; ks < 8; ++ks) {
+      const float2 lo = *reinterpret_cast<const float2*>(qr + 16 * ks + 2 * tq);
+      const float2 hi = *reinterpret_cast<const float2*>(qr + 16 * ks + 2 * tq + 8);
+      qa[ks][0] = g < G ? pack_h2(lo.x, lo.y) : 0u;
+      qa[ks][1] = g < G ? pack_h2(hi.x, hi.y) : 0u;
+    }
   }
+  {  // bounded wait for the copies (about a second): a lost copy records an error instead of hanging
+    uint32_t done = 0;
+    const long long t0 = clock64();
+    while (true) {
+      asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0, 1000000;\n\t"
+                   "selp.u32 %0, 1, 0, p;\n\t}\n" : "=r"(done) : "r"(smem_addr(bar)) : "memory");
+      if (done || clock64() - t0 > 2000000000LL) break;
+    }
+    if (!done && t == 0) atomicExch(err, 17);
+  }
+  if (n < kAttnChunk) {  // the last chunk: V rows past the end (other sequences, or never written) become zeros,
+    // so that the zero probabilities of masked positions cannot meet a non-finite value there
+    for (int i = t; i < (kAttnChunk - n) * 16; i += 32 * kAttnWarps) {
+      const int row = n + (i >> 4), c = i & 15;  // 16 chunks of 16 bytes per row: 8 per box
+      *reinterpret_cast<uint4*>(sv + (c >> 3) * kBox + row * 128 + ((c & 7) << 4)) = make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();
+  }
+  // S = Q K^T for positions 32w + 8nt + (0..7); ldmatrix.x4: k-steps ks, ks+1, low and high 8 dims
+  float sc[4][4];
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sc[nt][i] = 0.f;
+  const int mi = lane >> 3, r8 = lane & 7;
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    const int pos = 32 * w + 8 * nt + r8;
+#pragma unroll
+    for (int ks = 0; ks < 8; ks += 2) {
+      const int kstep = ks + (mi >> 1);  // matrices: (ks, lo), (ks, hi), (ks+1, lo), (ks+1, hi)
+      const int chunk = 2 * (kstep & 3) + (mi & 1);
+      const uint32_t addr = smem_addr(sk + (kstep >> 2) * kBox) + swz(pos, chunk);
+      uint32_t b0, b1, b2, b3;
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3) : "r"(addr));
+      mma16816(sc[nt], qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
+      mma16816(sc[nt], qa[ks + 1][0], 0u, qa[ks + 1][1], 0u, b2, b3);
+    }
+  }
+  // scale, mask positions past the end, row maxima (rows g: accumulators 0, 1; columns 2tq, 2tq+1)
+  float m = -FLT_MAX;
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int p = 32 * w + 8 * nt + 2 * tq + i;
+      sc[nt][i] = p < n ? __fmul_rn(sc[nt][i], scale) : -FLT_MAX;
+      m = fmaxf(m, sc[nt][i]);
+    }
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  if (tq == 0) red[w * 8 + g] = m;
+  __syncthreads();
+  float M = red[g];
+#pragma unroll
+  for (int i = 1; i < kAttnWarps; ++i) M = fmaxf(M, red[i * 8 + g]);
+  float l = 0.f;
+  uint32_t pa[2][2];  // P as the A operand of the two 16-position k-steps
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    float e[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      e[i] = sc[nt][i] > -FLT_MAX ? __expf(__fsub_rn(sc[nt][i], M)) : 0.f;
+      l = __fadd_rn(l, e[i]);
+    }
+    pa[nt >> 1][nt & 1] = pack_h2(e[0], e[1]);
+  }
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  if (tq == 0) red[kAttnWarps * 8 + w * 8 + g] = l;
+  // O = P V over this warp's 32 positions: 16 column tiles of 8 dims; ldmatrix.trans x4 gives
+  // (positions lo, hi) x (dims tile dn, dn + 1)
+  float o[16][4];
+#pragma unroll
+  for (int dn = 0; dn < 16; ++dn)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[dn][i] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < 2; ++kk) {
+#pragma unroll
+    for (int dn = 0; dn < 16; dn += 2) {
+      const int pos = 32 * w + 16 * kk + 8 * (mi & 1) + r8;
+      const int chunk = dn + (mi >> 1);  // 8-dim tile = 16-byte chunk; 8 chunks per box
+      const uint32_t addr = smem_addr(sv + (chunk >> 3) * kBox) + swz(pos, chunk & 7);
+      uint32_t b0, b1, b2, b3;
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3) : "r"(addr));
+      mma16816(o[dn], pa[kk][0], 0u, pa[kk][1], 0u, b0, b1);
+      mma16816(o[dn + 1], pa[kk][0], 0u, pa[kk][1], 0u, b2, b3);
+    }
+  }
+  __syncthreads();  // every warp is done with K: its space holds the four warps' partial O rows
+  float* ored = reinterpret_cast<float*>(sk);  // [kAttnWarps][8 rows][128 dims]
+  if (g < G) {
+#pragma unroll
+    for (int dn = 0; dn < 16; ++dn) {
+      float2* d = reinterpret_cast<float2*>(ored + (w * 8 + g) * 128 + 8 * dn + 2 * tq);
+      *d = make_float2(o[dn][0], o[dn][1]);
+    }
+  }
+  __syncthreads();
   const int64_t base = (b * H + kvh * G) * nsplit + split;
+  for (int i = t; i < G * 128; i += 32 * kAttnWarps) {
+    const int row = i >> 7, d = i & 127;
+    float s = ored[row * 128 + d];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    po[(base + g * nsplit) * HD + t] = o[g];
-    if (t == 0) {
-      float l = 0.f;
-      for (int i = 0; i < HD / 32; ++i) l += red[g][i];
-      pm[base + g * nsplit] = n > 0 ? M[g] : -FLT_MAX;
-      pl[base + g * nsplit] = n > 0 ? l : 0.f;
+    for (int ww = 1; ww < kAttnWarps; ++ww) s = __fadd_rn(s, ored[(ww * 8 + row) * 128 + d]);
+    po[(base + row * nsplit) * 128 + d] = s;
+  }
+  if (t < G) {
+    float L = 0.f, MM = red[t];
+    for (int ww = 0; ww < kAttnWarps; ++ww) {
+      L = __fadd_rn(L, red[kAttnWarps * 8 + ww * 8 + t]);
+      MM = fmaxf(MM, red[ww * 8 + t]);
     }
+    pm[base + t * nsplit] = n > 0 ? MM : -FLT_MAX;
+    pl[base + t * nsplit] = n > 0 ? L : 0.f;
   }
 }
+
+constexpr int kAttnSmem = 4 * kAttnChunk * 128 + 4 * 2 * kAttnWarps * 8 + 16 + 1024;
 
 // out[b, h] = sum_s exp(m_s - M) o_s / sum_s exp(m_s - M) l_s
 template <int HD>
@@ -335,9 +435,17 @@ __global__ void fill_normal_kernel(float* __restrict__ out, int64_t n, uint64_t 
     out[i] = normal_at(key, i, mean, std);
 }
 
-__global__ void fill_normal_f16_kernel(__half* __restrict__ out, int64_t n, uint64_t key, float mean, float std) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = __float2half_rn(normal_at(key, i, mean, std));
+__device__ __forceinline__ uint64_t key_of(uint64_t seed, uint64_t stream) {
+  return mix64(seed ^ mix64(stream * 0xD1B54A32D192ED03ull + 0x7F4A7C15ull));
+}
+
+// rows of `cols` f16 draws, `pitch` apart; row r is stream stream0 + r of the generator
+__global__ void fill_normal_f16_rows_kernel(__half* __restrict__ out, int64_t rows, int64_t cols, int64_t pitch,
+                                            uint64_t seed, uint64_t stream0, float mean, float std) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rows * cols; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cols, c = i - r * cols;
+    out[r * pitch + c] = __float2half_rn(normal_at(key_of(seed, stream0 + (uint64_t)r), c, mean, std));
+  }
 }
 
 // GGUF block quantizers of uaii_moe_quantize_rows (round to nearest, per-block max-abs scales;
@@ -511,7 +619,8 @@ cudaError_t launch_embed(int fmt, const void* table, int64_t vocab, int64_t D, c
 cudaError_t launch_add_rmsnorm(float* x, const float* delta, const float* w, int64_t B, int64_t D, float eps, float* y,
                                cudaStream_t st) {
   if (B == 0) return cudaSuccess;
-  add_rmsnorm_kernel<<<(unsigned)B, 256, 0, st>>>(x, delta, w, D, eps, y);
+  if (D % 4 != 0 || D > 4 * 256 * kNormVec) return cudaErrorInvalidValue;
+  add_rmsnorm_kernel<<<(unsigned)B, 256, 0, st>>>(x, delta, w, (int)D, eps, y);
   return cudaGetLastError();
 }
 
@@ -524,25 +633,59 @@ cudaError_t launch_rope_append(const float* qkv, int64_t B, int64_t H, int64_t H
   return cudaGetLastError();
 }
 
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+bool make_kv_map(void* map, const void* cache, int64_t rows) {
+  static EncodeTiledFn enc = nullptr;
+  if (!enc) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qr{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) != cudaSuccess ||
+        qr != cudaDriverEntryPointSuccess)
+      return false;
+    enc = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  if (reinterpret_cast<uintptr_t>(cache) & 15) return false;
+  const cuuint64_t dims[2] = {128, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {256};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kAttnChunk};
+  const cuuint32_t es[2] = {1, 1};
+  return enc(static_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(cache), dims,
+             strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int attn_splits(int64_t len) { return (int)((len + kAttnChunk - 1) / kAttnChunk); }
 
-cudaError_t launch_attn_decode(const float* q, const void* kc, const void* vc, int64_t B, int64_t H, int64_t Hkv,
+cudaError_t launch_attn_decode(const void* kmap, const void* vmap, const float* q, int64_t B, int64_t H, int64_t Hkv,
                                int64_t hd, int64_t len, int64_t max_seq, float* po, float* pm, float* pl, float* out,
-                               cudaStream_t st) {
-  if (hd != 128 || Hkv <= 0 || H % Hkv || len <= 0 || len > max_seq) return cudaErrorInvalidValue;
+                               int* err, cudaStream_t st) {
+  if (hd != 128 || Hkv <= 0 || H % Hkv || len <= 0 || len > max_seq || H / Hkv > 8) return cudaErrorInvalidValue;
   const int ns = attn_splits(len);
   const float scale = 1.0f / sqrtf((float)hd);  // attention_kv_f32's default scale
   const dim3 grid((unsigned)ns, (unsigned)Hkv, (unsigned)B);
-  const __half* k = static_cast<const __half*>(kc);
-  const __half* v = static_cast<const __half*>(vc);
+  const CUtensorMap& tk = *static_cast<const CUtensorMap*>(kmap);
+  const CUtensorMap& tv = *static_cast<const CUtensorMap*>(vmap);
+  auto run = [&](auto kern, int gi) -> cudaError_t {
+    static bool attr[9] = {};
+    if (!attr[gi]) {
+      const cudaError_t a = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+      if (a != cudaSuccess) return a;
+      attr[gi] = true;
+    }
+    kern<<<grid, 32 * kAttnWarps, kAttnSmem, st>>>(tk, tv, q, H, Hkv, len, max_seq, scale, po, pm, pl, err);
+    return cudaGetLastError();
+  };
+  cudaError_t e;
   switch (H / Hkv) {
-    case 1: attn_decode_kernel<128, 1><<<grid, 128, 0, st>>>(q, k, v, H, Hkv, len, max_seq, scale, po, pm, pl); break;
-    case 2: attn_decode_kernel<128, 2><<<grid, 128, 0, st>>>(q, k, v, H, Hkv, len, max_seq, scale, po, pm, pl); break;
-    case 4: attn_decode_kernel<128, 4><<<grid, 128, 0, st>>>(q, k, v, H, Hkv, len, max_seq, scale, po, pm, pl); break;
-    case 8: attn_decode_kernel<128, 8><<<grid, 128, 0, st>>>(q, k, v, H, Hkv, len, max_seq, scale, po, pm, pl); break;
+    case 1: e = run(attn_mma_kernel<1>, 1); break;
+    case 2: e = run(attn_mma_kernel<2>, 2); break;
+    case 4: e = run(attn_mma_kernel<4>, 4); break;
+    case 8: e = run(attn_mma_kernel<8>, 8); break;
     default: return cudaErrorInvalidValue;
   }
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   attn_combine_kernel<128><<<(unsigned)(B * H), 128, 0, st>>>(po, pm, pl, ns, out);
   return cudaGetLastError();
@@ -568,11 +711,11 @@ cudaError_t launch_fill_normal(float* out, int64_t n, uint64_t seed, uint64_t st
   return cudaGetLastError();
 }
 
-cudaError_t launch_fill_normal_f16(void* out, int64_t n, uint64_t seed, uint64_t stream, float mean, float std,
-                                   cudaStream_t st) {
-  if (n == 0) return cudaSuccess;
-  fill_normal_f16_kernel<<<grid_for(n, 256), 256, 0, st>>>(static_cast<__half*>(out), n, normal_key(seed, stream),
-                                                           mean, std);
+cudaError_t launch_fill_normal_f16_rows(void* out, int64_t rows, int64_t cols, int64_t pitch, uint64_t seed,
+                                        uint64_t stream0, float mean, float std, cudaStream_t st) {
+  if (rows * cols == 0) return cudaSuccess;
+  fill_normal_f16_rows_kernel<<<grid_for(rows * cols, 256), 256, 0, st>>>(static_cast<__half*>(out), rows, cols, pitch,
+                                                                          seed, stream0, mean, std);
   return cudaGetLastError();
 }
 

@@ -112,9 +112,15 @@ class Decoder {
     const size_t kv_bytes = sizeof(uint16_t) * (size_t)(B * Hkv) * (size_t)c.max_seq * (size_t)hd;
     kc_.assign((size_t)L, nullptr);
     vc_.assign((size_t)L, nullptr);
+    maps_.assign((size_t)(2 * L), KvMap{});
     for (int64_t l = 0; l < L; ++l) {
       UAII_TRY(dmalloc(&kc_[(size_t)l], kv_bytes, "Malloc(K cache)"));
       UAII_TRY(dmalloc(&vc_[(size_t)l], kv_bytes, "Malloc(V cache)"));
+      UAII_CUDA(cudaMemsetAsync(kc_[(size_t)l], 0, kv_bytes, st), "Memset(K cache)");
+      UAII_CUDA(cudaMemsetAsync(vc_[(size_t)l], 0, kv_bytes, st), "Memset(V cache)");
+      if (!make_kv_map(maps_[(size_t)(2 * l)].bytes, kc_[(size_t)l], B * Hkv * c.max_seq) ||
+          !make_kv_map(maps_[(size_t)(2 * l + 1)].bytes, vc_[(size_t)l], B * Hkv * c.max_seq))
+        return Error::make(ErrorCode::Internal, "decoder: KV-cache tensor map");
     }
     UAII_TRY(dmalloc((void**)&x_, sizeof(float) * (size_t)(B * D), "Malloc(x)"));
     UAII_TRY(dmalloc((void**)&n_, sizeof(float) * (size_t)(B * D), "Malloc(n)"));
@@ -185,14 +191,10 @@ class Decoder {
     UAII_CUDA(cudaSetDevice(be_->device()), "SetDevice");
     const int64_t rows = cfg_.batch * cfg_.n_kv_heads, hd = cfg_.head_dim;
     for (int64_t l = 0; l < cfg_.n_layers; ++l)
-      for (int kv = 0; kv < 2; ++kv)
-        for (int64_t r = 0; r < rows; ++r) {  // each (sequence, kv head) row of positions is contiguous
-          char* base = static_cast<char*>(kv ? vc_[(size_t)l] : kc_[(size_t)l]) +
-                       sizeof(uint16_t) * (size_t)(r * cfg_.max_seq * hd);
-          UAII_CUDA(launch_fill_normal_f16(base, n * hd, seed, (uint64_t)((l * 2 + kv) * rows + r), 0.0f, 1.0f,
-                                           be_->stream()),
-                    "fill_kv");
-        }
+      for (int kv = 0; kv < 2; ++kv)  // (sequence, kv head) rows of n * head_dim values, max_seq * head_dim apart
+        UAII_CUDA(launch_fill_normal_f16_rows(kv ? vc_[(size_t)l] : kc_[(size_t)l], rows, n * hd, cfg_.max_seq * hd,
+                                              seed, (uint64_t)((l * 2 + kv) * rows), 0.0f, 1.0f, be_->stream()),
+                  "fill_kv");
     UAII_CUDA(cudaStreamSynchronize(be_->stream()), "StreamSynchronize");
     pos_ = n;
     return Error::success();
@@ -221,8 +223,8 @@ class Decoder {
       UAII_CUDA(launch_rope_append(qkv_, B, H, Hkv, hd, freq_, pos_, cfg_.rope_mode, q_, kc_[(size_t)l],
                                    vc_[(size_t)l], cfg_.max_seq, st),
                 "rope_append");
-      UAII_CUDA(launch_attn_decode(q_, kc_[(size_t)l], vc_[(size_t)l], B, H, Hkv, hd, pos_ + 1, cfg_.max_seq, po_, pm_,
-                                   pl_, attn_, st),
+      UAII_CUDA(launch_attn_decode(maps_[(size_t)(2 * l)].bytes, maps_[(size_t)(2 * l + 1)].bytes, q_, B, H, Hkv, hd,
+                                   pos_ + 1, cfg_.max_seq, po_, pm_, pl_, attn_, err_, st),
                 "attention");
       UAII_TRY(be_->quant_matmul(attn_, B, q_dim_, b.wo, b.wo_fmt, D, o_, false));
       UAII_CUDA(launch_add_rmsnorm(x_, o_, b.ffn_norm, B, D, cfg_.rms_eps, n_, st), "rmsnorm(ffn)");
@@ -279,6 +281,7 @@ class Decoder {
     UAII_CUDA(cudaMemcpy(&flag, err_, sizeof(int), cudaMemcpyDeviceToHost), "Memcpy(error flag)");
     if (flag) {
       (void)cudaMemset(err_, 0, sizeof(int));
+      if (flag == 17) return Error::make(ErrorCode::Internal, "attention: a KV-cache copy did not complete");
       return Error::make(ErrorCode::InvalidArgument, "embedding token id out of range");
     }
     return Error::success();
@@ -294,6 +297,10 @@ class Decoder {
   int embd_fmt_ = 0, output_fmt_ = 0;
   float* freq_ = nullptr;
   std::vector<void*> kc_, vc_;
+  struct KvMap {
+    alignas(64) unsigned char bytes[kKvMapBytes];
+  };
+  std::vector<KvMap> maps_;  // TMA maps of each layer's K and V caches
   float *x_ = nullptr, *n_ = nullptr, *o_ = nullptr, *ff_ = nullptr, *qkv_ = nullptr, *q_ = nullptr, *attn_ = nullptr;
   float *po_ = nullptr, *pm_ = nullptr, *pl_ = nullptr, *logits_ = nullptr;
   int32_t *tokens_ = nullptr, *next_ = nullptr;

@@ -76,7 +76,7 @@ struct Args {
   int kquads;   // quads per row: ceil(K / 256)
   int k_atoms;  // 64-element atoms per row: K / 64
   int rows_per_expert, gateup;
-  __half* h_out;  // gate/up: [S, out_ld] f16, K order h_order (quad schedule; the others use their own)
+  __half* h_out;  // gate/up: [S, out_ld] f16 in K order h_order (tcgen05 and quad; the per-unit warp schedule: wm_kpos)
   int h_order;
   float* out;     // down: [splits][S][out_ld] f32
   int64_t out_ld, split_stride;
@@ -704,7 +704,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (args.gateup) {
         // lane l < 16 holds gate, lane l + 16 up of feature i0 + 16q + (l & 15); each
         // column pair (n, n+1) is split: the gate lane finishes n, the up lane n + 1
-        const int feat = (int)tc_kpos(t.m_tile * 64 + 16 * q + (lane & 15));
+        const int feat = (int)operand_pos(args.h_order, t.m_tile * 64 + 16 * q + (lane & 15));
         const bool gate_lane = lane < 16;
         for (int cb = grp * kCols; cb < (grp + 1) * kCols; cb += kW) {
           uint32_t r[8];
@@ -1582,15 +1582,25 @@ __global__ void __launch_bounds__(kWmThreads, 1)
   __syncthreads();
 }
 
+// tile_base[e] = tiles of the experts before e (an exclusive scan over one warp, 32 experts
+// per round), tile_base[E] = all tiles.
 __global__ void tile_table_kernel(const int32_t* counts, int E, int bn, int m_tiles, int splits,
                                   int32_t* tile_base) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const int lane = threadIdx.x;
   int run = 0;
-  for (int e = 0; e < E; ++e) {
-    tile_base[e] = run;
-    run += ((counts[e] + bn - 1) / bn) * m_tiles * splits;
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    const int e = e0 + lane;
+    const int n = e < E ? ((counts[e] + bn - 1) / bn) * m_tiles * splits : 0;
+    int incl = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (e < E) tile_base[e] = run + incl - n;
+    run += __shfl_sync(0xffffffffu, incl, 31);
   }
-  tile_base[E] = run;
+  if (lane == 0) tile_base[E] = run;
 }
 
 // ---- host side ----------------------------------------------------------
