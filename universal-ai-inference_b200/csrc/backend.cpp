@@ -614,6 +614,7 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
   rb.counts = static_cast<int32_t*>(carve(sizeof(int32_t) * E));
   rb.offsets = static_cast<int32_t*>(carve(sizeof(int32_t) * (E + 1)));
   int32_t* tile_base = static_cast<int32_t*>(carve(sizeof(int32_t) * (E + 1)));
+  int32_t* tile_base_dn = static_cast<int32_t*>(carve(sizeof(int32_t) * (E + 1)));
 
   const void *gd = nullptr, *ud = nullptr, *dd = nullptr;
   UAII_TRY(stage_weight(L.gate.data, (size_t)(E * I) * row_bytes(L.gate.fmt, D), &gd));
@@ -639,14 +640,25 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
                                                     : kOrderTc;
     void* xp16 = carve(2 * (size_t)(S * D));
     void* h16 = carve(2 * (size_t)(S * I));
+    void* xsum = nullptr;  // Q4_K on the quad schedule: the activations' sub-block sums
     splits = P.splits;
     out = static_cast<float*>(carve(sizeof(float) * (size_t)(splits * S * D)));
     if (ep) {  // rows arrive in the tcgen05 operand order
       if (P.warp_mma) return Error::make(ErrorCode::Internal, "expert-parallel rows planned on the warp-MMA schedule");
       UAII_CUDA(launch_route_gather16(ep->x16, T, D, E, k, rb, xp16, stream_, ep->x_pitch), "route_gather16");
     } else {
-      UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, nullptr, xp16, stream_, x_order), "route_gather");
+      TileTables tt;  // built by the gather from the same counts: no tile-table launches
+      tt.gu = tile_base;
+      tt.dn = tile_base_dn;
+      tt.bn = P.bn;
+      tt.gu_mtiles = (int)(I / 64);
+      tt.dn_mtiles = (int)(D / 128);
+      tt.dn_splits = std::min(splits, umma_kchunks(L.down.fmt, I));
+      if (P.quad_mma && L.gate.fmt == kQ4_K) tt.xsum = carve(2 * (size_t)(S * (D / 256) * 16));
+      xsum = tt.xsum;
+      UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, nullptr, xp16, stream_, x_order, &tt), "route_gather");
     }
+    const bool tables = ep == nullptr;
     phase_end();
     count_launches(3);
     phase_begin(kGateUp);
@@ -656,15 +668,16 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
     UAII_TRY(umma_rows(dd, L.down.fmt, E * D, I, weight_is_constant(L.down.data, expert_bytes(L.down, E)), &dd,
                        &dpitch));
     UAII_CUDA(launch_gateup_umma(L.gate.fmt, gd, ud, gpitch, E, I, D, xp16, S, rb.counts, rb.offsets, tile_base, P.bn,
-                                 h16, dev_err_, stream_, sched, h_order),
+                                 h16, dev_err_, stream_, sched, h_order, tables, xsum),
               "gateup(tensor cores)");
     phase_end();
     phase_begin(kDown);
-    UAII_CUDA(launch_down_umma(L.down.fmt, dd, dpitch, E, D, I, h16, S, rb.counts, rb.offsets, tile_base, P.bn, splits,
-                               out, dev_err_, stream_, dn_sched),
+    UAII_CUDA(launch_down_umma(L.down.fmt, dd, dpitch, E, D, I, h16, S, rb.counts, rb.offsets,
+                               tables ? tile_base_dn : tile_base, P.bn, splits, out, dev_err_, stream_, dn_sched,
+                               tables),
               "down(tensor cores)");
     phase_end();
-    count_launches(4);
+    count_launches(tables ? 2 : 4);
   } else {
     float* xp = static_cast<float*>(carve(sizeof(float) * S * D));
     float* h = static_cast<float*>(carve(sizeof(float) * S * I));
@@ -755,10 +768,11 @@ size_t experts_ws_bytes(const LayerArgs& L, int64_t T, const ExpertPlan& P, int 
   const int64_t S = T * L.top_k;
   size_t b = 0;
   b += 5 * align_up(sizeof(int32_t) * S) + align_up((size_t)(L.E * T));
-  b += 3 * align_up(sizeof(int32_t) * (L.E + 1));
+  b += 4 * align_up(sizeof(int32_t) * (L.E + 1));  // counts, offsets, two tile tables
   if (P.umma) {
     b += align_up(2 * (size_t)(S * L.D)) + align_up(2 * (size_t)(S * L.I)) +
          align_up(sizeof(float) * (size_t)(P.splits * S * L.D));
+    if (P.quad_mma && L.gate.fmt == kQ4_K) b += align_up(2 * (size_t)(S * (L.D / 256) * 16));  // sub-block sums
     if (row_bytes(L.gate.fmt, L.D) % 16)
       b += (size_t)pad_gateup * align_up((size_t)(L.E * L.I * umma_pitch(L.gate.fmt, L.D)));
     if (pad_down && row_bytes(L.down.fmt, L.I) % 16)
@@ -863,22 +877,25 @@ Error MoeCudaBackend::quant_matmul(const float* x, int64_t M, int64_t K, const v
   P.splits = splits;
   last_plan_ = P;
   phase_begin(kDown);
-  UAII_CUDA(launch_identity_route(route, M, stream_), "identity_route");  // offsets {0, M}, counts {M}
   if (tc) {
+    // one prep launch: f16 operand rows, the one-expert route (offsets {0, M}, counts {M}), the tile table
     void* x16 = carve(2 * (size_t)(M * K));
-    UAII_CUDA(launch_to_f16(static_cast<const float*>(xd), M * K, x16, stream_, wm), "to_f16");
+    UAII_CUDA(launch_to_f16_route(static_cast<const float*>(xd), M, K, x16, wm, route, tiles, bn, (int)(N / 128),
+                                  std::min(splits, umma_kchunks(fmt, K)), stream_),
+              "to_f16_route");
     int64_t pitch = 0;
     UAII_TRY(umma_rows(wd, fmt, N, K, const_w, &wd, &pitch));
     float* out = planes ? static_cast<float*>(carve(sizeof(float) * (size_t)splits * (size_t)(M * N))) : yo;
     UAII_CUDA(launch_down_umma(fmt, wd, pitch, 1, N, K, x16, M, route + 2, route, tiles, bn, splits, out, dev_err_,
-                               stream_, wm),
+                               stream_, wm, true),
               "quant_matmul(tensor cores)");
-    count_launches(4);
+    count_launches(2);
     if (planes) {
       UAII_CUDA(launch_sum_planes(out, splits, M * N, M * N, yo, relu, stream_), "sum_planes");
       count_launches(1);
     }
   } else {
+    UAII_CUDA(launch_identity_route(route, M, stream_), "identity_route");  // offsets {0, M}, counts {M}
     UAII_CUDA(launch_down_simt(fmt, wd, 1, N, K, (int64_t)row_bytes(fmt, K), static_cast<const float*>(xd), route,
                                route + 2, yo, stream_),
               "quant_matmul");

@@ -81,6 +81,11 @@ struct Args {
   float* out;     // down: [splits][S][out_ld] f32
   int64_t out_ld, split_stride;
   int* err;
+  // Quad schedule, Q4_K activations: per slot and quad, the f32 sums of the eight 32-element
+  // sub-blocks of the f16 activations as f16 (hi) and f16 (remainder) pairs, [S_rows][kquads][16];
+  // null: the minima go through one MMA per k-step instead.
+  const __half* xsum;
+  int64_t S_rows;
 };
 
 __device__ __forceinline__ __half2 as_h2(uint32_t v) {
@@ -1265,6 +1270,7 @@ template <> struct QuadUnit<kQ4_K> {
   uint32_t w[8], w8[8];            // qs bytes [32t, 32t + 32), and each word shifted right by 8
   __half2 f_lo, b_lo, f_hi, b_hi;  // fold constants of sub-blocks 2t and 2t + 1
   uint32_t m_lo, m_hi;             // (m, m) of the two sub-blocks, f16
+  uint32_t mf;                     // (m of sub-block 2t, m of 2t + 1), f16
   float d, dmin;
   __device__ __forceinline__ void load(const uint8_t* row, int t) {
     const uint4 hdr = *reinterpret_cast<const uint4*>(row);  // d, dmin, scales[12]
@@ -1296,6 +1302,7 @@ template <> struct QuadUnit<kQ4_K> {
     b_hi = __high2half2(bb);
     m_lo = as_u32(__low2half2(mf));
     m_hi = as_u32(__high2half2(mf));
+    this->mf = as_u32(mf);
     const __half2 dm = as_h2(hdr.x);
     d = __low2float(dm);
     dmin = __high2float(dm);
@@ -1355,11 +1362,12 @@ template <> struct QuadUnit<kQ6_K> {
   }
 };
 
-template <int F, int NT, int ST>
+template <int F, int NT, int ST, bool kXSum>
 __global__ void __launch_bounds__(kWmThreads, 1)
     expert_quad_mma_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                            const __grid_constant__ CUtensorMap tm_x, const Args args) {
   static_assert(F == kQ4_K || F == kQ6_K, "quad schedule: K-quants only");
+  static_assert(!kXSum || F == kQ4_K, "activation sub-block sums serve the Q4_K minima");
   using C = WmCfg<F, NT, ST>;
   using Fm = Fmt<F>;
   constexpr int BN = C::BN;
@@ -1454,6 +1462,20 @@ __global__ void __launch_bounds__(kWmThreads, 1)
         if (((q - q0) & 1) != h) continue;  // the other half's quad
         if (!(ok = bounded_wait(full + pi % ST, (pi / ST) & 1, s_abort, err, kErrTimeoutDequant))) break;
         const uint8_t* stage = sP + (pi % ST) * C::kPStage;
+        // Q4_K with activation sums: this quad's sub-block sums of slots g (and g + 8), issued
+        // first so that their latency hides behind the decode below
+        uint32_t xs[NT][2];
+        if constexpr (kXSum) {
+          const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
+#pragma unroll
+          for (int n = 0; n < NT; ++n) {
+            const int64_t slot = min((int64_t)(slot0 + 8 * n + g), args.S_rows - 1);
+            const uint32_t* p =
+                reinterpret_cast<const uint32_t*>(args.xsum + (slot * args.kquads + q) * 16) + tq;
+            xs[n][0] = __ldg(p);      // (S[2tq], S[2tq+1]) rounded to f16
+            xs[n][1] = __ldg(p + 4);  // their remainders
+          }
+        }
         QuadUnit<F> u0, u1;
         if constexpr (F == kQ6_K) {  // 16-byte loads with the window offset as a constant
           switch ((q * Fm::kBytes) & 15) {
@@ -1475,7 +1497,7 @@ __global__ void __launch_bounds__(kWmThreads, 1)
         const uint32_t bq = sB0 + (pi % ST) * C::kBQuad;
         const uint32_t bqa[4] = {bq + boff[0], bq + boff[1], bq + boff[2], bq + boff[3]};
         uint32_t am_lo[4], am_hi[4];  // Q4_K min operands: rows g, g + 8 of sub-block 2t, then 2t + 1
-        if constexpr (F == kQ4_K) {
+        if constexpr (F == kQ4_K && !kXSum) {
           am_lo[0] = am_lo[2] = u0.m_lo;
           am_lo[1] = am_lo[3] = u1.m_lo;
           am_hi[0] = am_hi[2] = u0.m_hi;
@@ -1507,11 +1529,19 @@ __global__ void __launch_bounds__(kWmThreads, 1)
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
               mma_16816(m1[n], a, b[2 * n], b[2 * n + 1]);
-              mma_16816(m2[n], s < 8 ? am_lo : am_hi, b[2 * n], b[2 * n + 1]);
+              if constexpr (!kXSum) mma_16816(m2[n], s < 8 ? am_lo : am_hi, b[2 * n], b[2 * n + 1]);
             }
           } else {
 #pragma unroll
             for (int n = 0; n < NT; ++n) mma_16816(acc[n], a, b[2 * n], b[2 * n + 1]);
+          }
+        }
+        if constexpr (kXSum) {  // sum_k m(row, sub-block k) S(slot, k): one k-step of 8 sub-blocks (+ 8 zeros), twice
+          const uint32_t amf[4] = {u0.mf, u1.mf, 0u, 0u};
+#pragma unroll
+          for (int n = 0; n < NT; ++n) {
+            mma_16816(m2[n], amf, xs[n][0], 0u);
+            mma_16816(m2[n], amf, xs[n][1], 0u);
           }
         }
         if constexpr (F == kQ4_K) {  // accumulator (n, i): row g + 8(i / 2)
@@ -1744,13 +1774,13 @@ cudaError_t run_warp_mma(const CUtensorMap& w0, const CUtensorMap& w1, const CUt
   return cudaGetLastError();
 }
 
-template <int F, int NT>
+template <int F, int NT, bool kXSum = false>
 cudaError_t run_quad_mma(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x, const Args& a,
                          cudaStream_t st) {
   constexpr int ST = WmStages<F, NT>::ST;
   using C = WmCfg<F, NT, ST>;
   static_assert(C::kSmem <= 227 * 1024, "shared memory budget");
-  auto kern = expert_quad_mma_kernel<F, NT, ST>;
+  auto kern = expert_quad_mma_kernel<F, NT, ST, kXSum>;
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
@@ -1764,6 +1794,15 @@ cudaError_t run_quad_mma(const CUtensorMap& w0, const CUtensorMap& w1, const CUt
 template <int F>
 cudaError_t dispatch_quad(int bn, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
                           const Args& a, cudaStream_t st) {
+  if constexpr (F == kQ4_K) {
+    if (a.xsum) {
+      switch (bn) {
+        case 8: return run_quad_mma<F, 1, true>(w0, w1, x, a, st);
+        case 16: return run_quad_mma<F, 2, true>(w0, w1, x, a, st);
+        default: return cudaErrorInvalidValue;
+      }
+    }
+  }
   switch (bn) {
     case 8: return run_quad_mma<F, 1>(w0, w1, x, a, st);
     case 16: return run_quad_mma<F, 2>(w0, w1, x, a, st);
@@ -1810,7 +1849,7 @@ cudaError_t launch_common(int sched, int fmt, bool gateup, const void* W0, const
                           int64_t E, int64_t rows, int64_t K, const void* act16, int64_t S_rows,
                           const int32_t* counts, const int32_t* offsets, int32_t* tile_base, int bn, int splits,
                           void* h16, float* out, int64_t out_ld, int64_t split_stride, int* err, cudaStream_t st,
-                          int h_order) {
+                          int h_order, bool table_ready, const void* xsum) {
   const int mk = min_k(fmt);
   const bool warp_mma = sched == kSchedWarpMma, quad = sched == kSchedQuadMma;
   if (!mk || K % mk != 0 || K <= 0) return cudaErrorNotSupported;
@@ -1832,9 +1871,11 @@ cudaError_t launch_common(int sched, int fmt, bool gateup, const void* W0, const
   }
   if (!maps) return cudaErrorNotSupported;
   const int m_tiles = (int)(rows / m_rows);
-  tile_table_kernel<<<1, 32, 0, st>>>(counts, (int)E, bn, m_tiles, splits, tile_base);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  if (!table_ready) {
+    tile_table_kernel<<<1, 32, 0, st>>>(counts, (int)E, bn, m_tiles, splits, tile_base);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   Args a{};
   a.counts = counts;
   a.offsets = offsets;
@@ -1848,6 +1889,8 @@ cudaError_t launch_common(int sched, int fmt, bool gateup, const void* W0, const
   a.gateup = gateup ? 1 : 0;
   a.h_out = static_cast<__half*>(h16);
   a.h_order = h_order;
+  a.xsum = quad && fmt == kQ4_K ? static_cast<const __half*>(xsum) : nullptr;
+  a.S_rows = S_rows;
   a.out = out;
   a.out_ld = out_ld;
   a.split_stride = split_stride;
@@ -1912,16 +1955,17 @@ bool warp_mma_shapes_supported(int gfmt, int dfmt, int64_t D, int64_t I) {
 cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pitch, int64_t E, int64_t I, int64_t D,
                                const void* xp16, int64_t S_rows, const int32_t* counts, const int32_t* offsets,
                                int32_t* tile_base, int bn, void* h16, int* err, cudaStream_t st, int sched,
-                               int h_order) {
+                               int h_order, bool table_ready, const void* xsum) {
   return launch_common(sched, fmt, true, G, U, pitch, E, I, D, xp16, S_rows, counts, offsets, tile_base, bn, 1,
-                       h16, nullptr, I, 0, err, st, h_order);
+                       h16, nullptr, I, 0, err, st, h_order, table_ready, xsum);
 }
 
 cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
                              int64_t S_rows, const int32_t* counts, const int32_t* offsets, int32_t* tile_base,
-                             int bn, int splits, float* out, int* err, cudaStream_t st, int sched) {
+                             int bn, int splits, float* out, int* err, cudaStream_t st, int sched,
+                             bool table_ready) {
   return launch_common(sched, fmt, false, Dn, Dn, pitch, E, D, I, h16, S_rows, counts, offsets, tile_base, bn,
-                       splits, nullptr, out, D, S_rows * D, err, st, kOrderTc);
+                       splits, nullptr, out, D, S_rows * D, err, st, kOrderTc, table_ready, nullptr);
 }
 
 namespace {

@@ -71,9 +71,23 @@ cudaError_t launch_ep_combine(const float* y_back, const int32_t* row_of, int64_
 // xp_f16 rows are in an operand K order (operand_order.cuh, OperandOrder): tc_kpos for
 // the tcgen05 schedule, wm_kpos (D % 128 == 0) for the warp-MMA one, q4k_kpos / q6k_kpos
 // (D % 256 == 0) for the quad schedule.
+// Optional: the gate/up and down expert GEMMs' tile tables ([E+1] each, as
+// tile_table_kernel builds them) written by the gather from the same counts.
+struct TileTables {
+  int32_t* gu = nullptr;
+  int32_t* dn = nullptr;
+  int bn = 16, gu_mtiles = 0, dn_mtiles = 0, dn_splits = 1;
+  // Quad schedule with Q4_K weights: the activations' 32-element sub-block sums (xsum_kpos order,
+  // see launch_gateup_umma), or null.
+  void* xsum = nullptr;
+};
 cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E, int k,
                                 const RouteBuffers& rb, float* xp_f32, void* xp_f16,
-                                cudaStream_t st, int order = 0);
+                                cudaStream_t st, int order = 0, const TileTables* tables = nullptr);
+// The packed MatMul's operand prep in one launch: x [M, K] -> f16 operand order (tc_kpos, or
+// wm_kpos), route = {0, M, M} (one expert owning every row) and its tile table {0, tiles}.
+cudaError_t launch_to_f16_route(const float* x, int64_t M, int64_t K, void* out, bool wm_order, int32_t* route,
+                                int32_t* tile_base, int bn, int m_tiles, int splits, cudaStream_t st);
 // y[t] = sum_r w[t,r] * out[slot_of[t,r]] (rank order, from 0), then
 // y[t] += gate[t] * shared_out[t] when shared_out is given (gate may be null = 1).
 // `out` (and `shared_out`) may hold `splits` partial planes `split_stride`
@@ -130,15 +144,21 @@ inline bool quad_mma_format(int fmt) { return fmt == 14 || fmt == 16; }
 // in that schedule's order for the gate format; h is written in the tc_kpos
 // (tcgen05), wm_kpos (warp-MMA) or h_order (quad: the order of the down format) order.
 // tile_base: scratch of E+1 ints.  *err receives a nonzero code if a wait timed out.
+// table_ready: tile_base already holds the tile table (route_gather or the prep kernel built
+// it), so no tile-table kernel is launched.  xsum (quad schedule, Q4_K): per slot and 256-element
+// quad, the f32 sums of the eight 32-element sub-blocks of the f16 activations as 8 f16 values
+// then their 8 f16 remainders ([S_rows][kquads][16] f16, route_gather writes them), so the Q4_K
+// minima take two MMAs per quad instead of one per k-step.
 cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pitch, int64_t E, int64_t I, int64_t D,
                                const void* xp16, int64_t S_rows, const int32_t* counts,
                                const int32_t* offsets, int32_t* tile_base, int bn, void* h16, int* err,
-                               cudaStream_t st, int sched = kSchedTcgen05, int h_order = 0);
+                               cudaStream_t st, int sched = kSchedTcgen05, int h_order = 0,
+                               bool table_ready = false, const void* xsum = nullptr);
 // out[split][slot, o] = partial of h16[slot] . Dn[e, o] over the split's K range (f32).
 cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
                              int64_t S_rows, const int32_t* counts, const int32_t* offsets,
                              int32_t* tile_base, int bn, int splits, float* out, int* err, cudaStream_t st,
-                             int sched = kSchedTcgen05);
+                             int sched = kSchedTcgen05, bool table_ready = false);
 // Copies `rows` packed rows of row_bytes (even) from src (src_pitch apart) to dst
 // (dst_pitch apart, a multiple of 16), zero-filling each row's padding.
 cudaError_t launch_pad_rows(const void* src, int64_t src_pitch, int64_t rows, int64_t row_bytes, void* dst,

@@ -167,12 +167,24 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int64_t T, int k, Rout
 // Offsets by a block-wide exclusive scan of counts; then one warp per (t, r).
 __global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int64_t D,
                                     int64_t E, int k, RouteBuffers rb, float* xp32,
-                                    __half* xp16, int order) {
+                                    __half* xp16, int order, TileTables tt) {
   extern __shared__ int offs[];  // [E+1]
   if (threadIdx.x == 0) {
     int run = 0;
     for (int64_t e = 0; e < E; ++e) { offs[e] = run; run += rb.counts[e]; }
     offs[E] = run;
+    if (blockIdx.x == 0 && tt.gu) {  // the expert GEMMs' tile tables, from the same counts
+      int tg = 0, td = 0;
+      for (int64_t e = 0; e < E; ++e) {
+        tt.gu[e] = tg;
+        tt.dn[e] = td;
+        const int c = rb.counts[e];
+        tg += ((c + tt.bn - 1) / tt.bn) * tt.gu_mtiles;
+        td += ((c + tt.bn - 1) / tt.bn) * tt.dn_mtiles * tt.dn_splits;
+      }
+      tt.gu[E] = tg;
+      tt.dn[E] = td;
+    }
   }
   __syncthreads();
   if (blockIdx.x == 0)
@@ -204,6 +216,20 @@ __global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int6
           const int64_t p0 = operand_pos(order, 4 * i);
           *reinterpret_cast<__half2*>(row + p0) = lo;
           *reinterpret_cast<__half2*>(row + p0 + 8) = hi;
+          if (tt.xsum) {  // sub-block (8 float4s, lanes 8m .. 8m+7) sums of the f16 values, f32
+            const float2 a = __half22float2(lo), c = __half22float2(hi);
+            float sum = (a.x + a.y) + (c.x + c.y);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+            if ((lane & 7) == 0) {
+              const int64_t j = i >> 3;  // sub-block
+              __half* xs = static_cast<__half*>(tt.xsum) + ((int64_t)slot * (D / 256) + (j >> 3)) * 16;
+              const __half hs = __float2half_rn(sum);
+              xs[j & 7] = hs;
+              xs[8 + (j & 7)] = __float2half_rn(sum - __half2float(hs));
+            }
+          }
         } else {  // tc_kpos: the pairs sit at 4i and 4i + 2, one 8-byte store (D % 4 == 0)
           *reinterpret_cast<uint2*>(row + 4 * i) =
               make_uint2(reinterpret_cast<const uint32_t&>(lo), reinterpret_cast<const uint32_t&>(hi));
@@ -350,7 +376,31 @@ __global__ void identity_route_kernel(int32_t* buf, int64_t T) {
   buf[2] = (int32_t)T;
 }
 
+// The packed MatMul's operand prep in one launch: x rows -> f16 operand order, the one-expert
+// route (offsets {0, M}, counts {M}) and its tile table {0, tiles}.
+__global__ void to_f16_route_kernel(const float* __restrict__ x, int64_t n, __half* __restrict__ o, bool wm_order,
+                                    int32_t* route, int32_t* tile_base, int64_t M, int bn, int m_tiles, int splits) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i == 0) {
+    route[0] = 0;
+    route[1] = (int32_t)M;
+    route[2] = (int32_t)M;
+    tile_base[0] = 0;
+    tile_base[1] = (int32_t)((M + bn - 1) / bn) * m_tiles * splits;
+  }
+  if (i < n) o[wm_order ? wm_kpos(i) : tc_kpos(i)] = __float2half_rn(x[i]);
+}
+
 }  // namespace
+
+cudaError_t launch_to_f16_route(const float* x, int64_t M, int64_t K, void* out, bool wm_order, int32_t* route,
+                                int32_t* tile_base, int bn, int m_tiles, int splits, cudaStream_t st) {
+  if (wm_order && K % 128 != 0) return cudaErrorInvalidValue;
+  const int64_t n = M * K;
+  to_f16_route_kernel<<<(unsigned)((n + 255) / 256 > 0 ? (n + 255) / 256 : 1), 256, 0, st>>>(
+      x, n, static_cast<__half*>(out), wm_order, route, tile_base, M, bn, m_tiles, splits);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_identity_route(int32_t* buf, int64_t T, cudaStream_t st) {
   identity_route_kernel<<<1, 1, 0, st>>>(buf, T);
@@ -378,15 +428,16 @@ cudaError_t launch_route_scan(int64_t T, int64_t E, int k, const RouteBuffers& r
 
 cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E, int k,
                                 const RouteBuffers& rb, float* xp_f32, void* xp_f16,
-                                cudaStream_t st, int order) {
+                                cudaStream_t st, int order, const TileTables* tables) {
   if ((order == kOrderWm && D % 128 != 0) || ((order == kOrderQ4K || order == kOrderQ6K) && D % 256 != 0))
     return cudaErrorInvalidValue;
+  const TileTables tt = tables ? *tables : TileTables{};
   int64_t blocks = (T * k + 7) / 8;
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
   const size_t smem = sizeof(int) * (size_t)(E + 1);
   route_gather_kernel<<<(unsigned)blocks, 256, smem, st>>>(x, T, D, E, k, rb, xp_f32,
-                                                           static_cast<__half*>(xp_f16), order);
+                                                           static_cast<__half*>(xp_f16), order, tt);
   return cudaGetLastError();
 }
 
