@@ -501,6 +501,27 @@ static int uo_experts_impl(const float* x, const uo_wsrc* G, const uo_wsrc* U,
   return UO_OK;
 }
 
+/* MoEExperts (legacy top-1 linear experts): y[b] = x[b] . W[e]^T with W [E, D, D] f32,
+ * e = (int)top_expert[b], expert 0 when that is outside [0, E); per output a sequential
+ * f32 sum over i of x*w (libs/uaii-kernels/src/transformer.cpp:483-520).  The range test
+ * is written on the float so that NaN and huge ids also select expert 0, as the
+ * reference's truncating conversion followed by its range check does on x86. */
+int uo_moe_experts_linear(const float* x, const float* W, const float* top, int64_t B, int64_t D,
+                          int64_t E, float* y) {
+  if (!x || !W || !top || !y || B < 0 || D <= 0 || E <= 0) return UO_INVALID_ARGUMENT;
+  for (int64_t b = 0; b < B; ++b) {
+    const float v = top[b];
+    const int64_t e = (v > -1.0f && v < (float)E) ? (int64_t)(int)v : 0;
+    const float* We = W + e * D * D;
+    for (int64_t o = 0; o < D; ++o) {
+      float sum = 0.0f;
+      for (int64_t i = 0; i < D; ++i) sum += x[b * D + i] * We[o * D + i];
+      y[b * D + o] = sum;
+    }
+  }
+  return UO_OK;
+}
+
 /* Dense f32 expert weights: gate/up [E,I,D], down [E,D,I] (kernels.hpp:104-114). */
 int uo_moe_experts_swiglu(const float* x, const float* G, const float* U, const float* Dn,
                           const float* probs, int64_t T, int64_t D, int64_t E, int64_t I,

@@ -50,6 +50,7 @@ class Oracle:
             "uo_shared_expert_packed": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int,
                                                 c_void_p, c_int64, c_int64, c_int64, c_void_p]),
             "uo_quant_gemm": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int, c_int64, c_int, c_void_p]),
+            "uo_moe_experts_linear": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
         }
         for n, (r, a) in sig.items():
             f = getattr(L, n)
@@ -90,6 +91,13 @@ class Oracle:
         assert self.L.uo_moe_experts_swiglu(_p(x), _p(G), _p(U), _p(Dn), _p(probs), T, D, E, I, top_k, norm,
                                             _p(y), _p(ids), _p(w)) == 0
         return y, ids, w
+
+    def experts_linear(self, x, W, top):
+        """MoEExperts: y[b] = x[b] . W[top[b]]^T (top-1 linear experts, W [E, D, D])."""
+        B, D = x.shape
+        y = np.empty((B, D), np.float32)
+        assert self.L.uo_moe_experts_linear(_p(x), _p(W), _p(top), B, D, W.shape[0], _p(y)) == 0
+        return y
 
     def experts_packed(self, x, G, gf, U, uf, Dn, df, probs, E, I, top_k, norm=1):
         T, D = x.shape
@@ -138,6 +146,7 @@ class Reference:
                                           c_void_p, c_int64, c_void_p]),
             "uref_embedding": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int64, c_int64, c_void_p]),
             "uref_softmax": (c_int, [c_void_p, c_int64, c_int64, c_void_p]),
+            "uref_moe_experts": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
             "uref_gguf_write_f32": (c_int, [c_char_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
         }
         for n, (r, a) in sig.items():
@@ -224,6 +233,12 @@ class Reference:
         for r in range(rows):
             self._chk(self.L.uref_dequant_row(fmt, base + r * pitch, cols, out.ctypes.data + r * cols * 4))
         return out
+
+    def experts_linear(self, x, W, top):
+        B, D = x.shape
+        y = np.empty((B, D), np.float32)
+        self._chk(self.L.uref_moe_experts(_p(x), _p(W), _p(top), B, D, W.shape[0], _p(y)))
+        return y
 
     def router(self, x, w):
         T, D = x.shape

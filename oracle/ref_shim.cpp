@@ -223,6 +223,14 @@ int uref_moe_experts_swiglu(const float* x, const float* G, const float* U, cons
                                                       static_cast<int>(E), top_k));
 }
 
+int uref_moe_experts(const float* x, const float* W, const float* top, std::int64_t B, std::int64_t D,
+                     std::int64_t E, float* y) {
+  const std::int64_t sx[2] = {B, D}, sw[3] = {E, D, D}, st[2] = {B, 1};
+  TensorView vx = f32_view(x, sx, 2), vw = f32_view(W, sw, 3), vt = f32_view(top, st, 2);
+  TensorView vy = f32_view(y, sx, 2);
+  return status(uaii::kernels::moe_experts_f32(vx, vw, vt, &vy, static_cast<int>(E)));
+}
+
 // Same call, with the token rows split across `threads` host threads.  Each
 // thread runs the unmodified reference function on its own contiguous token
 // range (the function is independent per token row), so the arithmetic per

@@ -31,9 +31,9 @@ def test_library_exports_every_declared_symbol(um):
 
 def test_abi_version_and_ops(um):
     assert um.lib.uaii_moe_abi_version() == 1
-    for op in (b"MoERouter", b"MoEExpertsSwiGLU", b"MoEFFN"):
+    for op in (b"MoERouter", b"MoEExperts", b"MoEExpertsSwiGLU", b"MoEFFN"):
         assert um.lib.uaii_moe_supports_op(op) == 1
-    for op in (b"MatMul", b"Attention", b"MoEExperts", b""):
+    for op in (b"MatMul", b"Attention", b""):
         assert um.lib.uaii_moe_supports_op(op) == 0
 
 

@@ -143,6 +143,43 @@ def test_experts_tie_order_golden(backend, golden, um, k):
     assert rel_err(y, golden[f"ties_y_k{k}"]) <= 1e-5
 
 
+@pytest.mark.parametrize("B,D,E,where", [(7, 300, 3, "host"), (64, 1024, 8, "device"), (1, 4096, 2, "host")])
+def test_legacy_experts_dispatch_vs_oracle(backend, oracle, um, B, D, E, where):
+    """MoEExperts (top-1 linear experts, dense f32 W [E, D, D]) bit for bit, out-of-range ids included."""
+    rng = np.random.default_rng(B + D)
+    x = rng.standard_normal((B, D)).astype(np.float32)
+    W = (rng.standard_normal((E, D, D)) * 0.05).astype(np.float32)
+    top = rng.integers(0, E, size=(B, 1)).astype(np.float32)
+    if B >= 6:
+        top[:6, 0] = [np.nan, 1e30, -0.7, E - 0.3, -1e30, E]
+    ref = oracle.experts_linear(x, W, top)
+    if where == "host":
+        y = np.empty_like(x)
+        backend.dispatch("MoEExperts", [um.f32_desc(x), um.f32_desc(W), um.f32_desc(top)], [um.f32_desc(y)],
+                         {"num_experts": E})
+    else:
+        xd, Wd, td = dev(x), dev(W), dev(top)
+        yd = torch.empty_like(xd)
+        backend.dispatch("MoEExperts", [um.f32_desc(xd), um.f32_desc(Wd), um.f32_desc(td)], [um.f32_desc(yd)],
+                         {"num_experts": E})
+        backend.synchronize()
+        y = yd.cpu().numpy()
+    assert bits_equal(y, ref)
+
+
+def test_legacy_experts_dispatch_checks(backend, um):
+    x = np.zeros((2, 8), np.float32)
+    W = np.zeros((3, 8, 8), np.float32)
+    top = np.zeros((2, 1), np.float32)
+    y = np.empty_like(x)
+    with pytest.raises(um.UaiiMoeError) as e:
+        backend.dispatch("MoEExperts", [um.f32_desc(x), um.f32_desc(W)], [um.f32_desc(y)], {"num_experts": 3})
+    assert "MoEExperts expects x,experts_w,top_expert" in e.value.message
+    with pytest.raises(um.UaiiMoeError) as e:  # num_experts defaults to 1
+        backend.dispatch("MoEExperts", [um.f32_desc(x), um.f32_desc(W), um.f32_desc(top)], [um.f32_desc(y)])
+    assert "experts_w shape" in e.value.message
+
+
 def test_reference_smoke_demo_on_device(backend, golden, um):
     """The reference's MoE smoke demo shapes (E=2, D=4, I=3) through dispatch."""
     x, w = golden["smoke_x"], golden["smoke_w"]

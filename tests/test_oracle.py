@@ -182,6 +182,18 @@ def test_quant_gemm_vs_reference(oracle, reference, um, fmt):
     assert bits_equal(r, np.where(c > 0, c, np.float32(0.0)).astype(np.float32))  # relu_f32: x > 0 ? x : 0
 
 
+@pytest.mark.parametrize("B,D,E", [(6, 37, 3), (16, 64, 4), (1, 1, 1), (0, 8, 2)])
+def test_experts_linear_vs_reference(oracle, reference, B, D, E):
+    """MoEExperts (top-1 linear experts): bitwise, including ids the reference maps to expert 0."""
+    rng = np.random.default_rng(90 + D)
+    x = rng.standard_normal((B, D)).astype(np.float32)
+    W = rng.standard_normal((E, D, D)).astype(np.float32)
+    top = rng.integers(-2, E + 2, size=(B, 1)).astype(np.float32)
+    if B >= 6:
+        top[:6, 0] = [np.nan, 1e30, -0.7, E - 0.3, -1e30, E]
+    assert bits_equal(oracle.experts_linear(x, W, top), reference.experts_linear(x, W, top))
+
+
 # ---- the numpy input synthesizer used by bench.py's reference arm (oracle/synth.py)
 
 @pytest.mark.parametrize("shape,seed,stream,mean,std", [

@@ -472,6 +472,37 @@ Error MoeCudaBackend::router(const float* x, const float* gate_w, int64_t T, int
   return Error::success();
 }
 
+Error MoeCudaBackend::experts_linear(const float* x, const float* W, const float* top, int64_t B, int64_t D,
+                                     int64_t E, float* y) {
+  std::lock_guard<std::mutex> lk(mu_);
+  UAII_CUDA(cudaSetDevice(device_), "SetDevice");
+  if (B < 0 || D <= 0 || E <= 0) return Error::make(ErrorCode::InvalidArgument, "moe experts shape");
+  if (!x || !W || !top || !y) return Error::make(ErrorCode::InvalidArgument, "moe experts out");
+  const size_t xb = sizeof(float) * (size_t)(B * D), tb = sizeof(float) * (size_t)B;
+  const size_t wb = sizeof(float) * (size_t)E * (size_t)(D * D);
+  UAII_TRY(reserve(2 * align_up(xb) + align_up(tb) + 4 * kAlign + weight_stage_bytes(W, wb)));
+  void* xs = carve(xb);
+  void* ts = carve(tb);
+  float* ys = static_cast<float*>(carve(xb));
+  if (B == 0) return Error::success();
+  const void *xd = nullptr, *td = nullptr, *wd = nullptr;
+  bool xh = false, th = false;
+  UAII_TRY(stage_input(x, xb, xs, &xd, &xh));
+  UAII_TRY(stage_input(top, tb, ts, &td, &th));
+  UAII_TRY(stage_weight(W, wb, &wd));
+  const bool yh = !is_device_ptr(y);
+  float* yo = yh ? ys : y;
+  UAII_CUDA(launch_experts_linear(static_cast<const float*>(xd), static_cast<const float*>(wd),
+                                  static_cast<const float*>(td), B, D, E, yo, stream_),
+            "experts_linear");
+  count_launches(1);
+  if (yh) {
+    UAII_CUDA(cudaMemcpyAsync(y, yo, xb, cudaMemcpyDeviceToHost, stream_), "D2H");
+    UAII_CUDA(cudaStreamSynchronize(stream_), "StreamSynchronize");
+  }
+  return Error::success();
+}
+
 namespace {
 constexpr int kSms = 148;
 // K splits of a down-style projection: the split count whose last wave ends first.  A
@@ -1299,6 +1330,32 @@ Error MoeCudaBackend::dispatch(const std::string& op_name, const std::string& /*
     return router(static_cast<const float*>(x.data), static_cast<const float*>(g.data), T, D, E,
                   static_cast<float*>(p.data), static_cast<float*>(t.data), nullptr);
   }
+  if (op_name == "MoEExperts") {
+    // checks in the order of dispatch_cpu and moe_experts_f32 (dispatch.cpp:231-238,
+    // transformer.cpp:483-500); out and top_expert extents are checked as well here
+    if (inputs.size() != 3 || outputs->size() != 1)
+      return Error::make(ErrorCode::InvalidArgument, "MoEExperts expects x,experts_w,top_expert");
+    const TensorView &x = inputs[0], &w = inputs[1], &top = inputs[2];
+    TensorView& y = (*outputs)[0];
+    if (x.rank != 2 || y.rank != 2 || w.rank != 3)
+      return Error::make(ErrorCode::InvalidArgument, "moe experts expects x[B,D], W[E,D,D], out[B,D]");
+    const int64_t B = x.dim(0), D = x.dim(1);
+    const int64_t num_experts = attr_int(attrs, "num_experts", 1);
+    if (w.dim(0) != num_experts || w.dim(1) != D || w.dim(2) != D)
+      return Error::make(ErrorCode::InvalidArgument, "experts_w shape");
+    if (y.dim(0) != B || y.dim(1) != D)
+      return Error::make(ErrorCode::InvalidArgument, "moe experts expects x[B,D], W[E,D,D], out[B,D]");
+    int64_t top_n = 1;
+    for (size_t i = 0; i < top.rank; ++i) top_n *= top.shape[i];
+    if (top.dtype != DType::F32 || top.data == nullptr || top_n < B)
+      return Error::make(ErrorCode::InvalidArgument, "top_expert must be f32 with one id per row");
+    if (w.dtype != DType::F32 || w.data == nullptr || fmt_is_gguf(w.quant_format))
+      return Error::make(ErrorCode::NotImplemented, "MoEExperts takes dense f32 expert weights");
+    UAII_TRY(f32_2d(x, "x"));
+    UAII_TRY(f32_2d(y, "out"));
+    return experts_linear(static_cast<const float*>(x.data), static_cast<const float*>(w.data),
+                          static_cast<const float*>(top.data), B, D, num_experts, static_cast<float*>(y.data));
+  }
   if (op_name == "MoEExpertsSwiGLU") {
     if (inputs.size() != 5 || outputs->size() != 1)
       return Error::make(ErrorCode::InvalidArgument, "MoEExpertsSwiGLU expects x,gate,up,down,probs");
@@ -1497,7 +1554,7 @@ int uaii_moe_synchronize(uaii_moe_backend* b) {
 int uaii_moe_supports_op(const char* op) {
   if (!op) return 0;
   const std::string s(op);
-  return (s == "MoERouter" || s == "MoEExpertsSwiGLU" || s == "MoEFFN") ? 1 : 0;
+  return (s == "MoERouter" || s == "MoEExperts" || s == "MoEExpertsSwiGLU" || s == "MoEFFN") ? 1 : 0;
 }
 
 int uaii_moe_dispatch(uaii_moe_backend* b, const char* op_name, const char* op_version,

@@ -113,6 +113,9 @@ class MoeCudaBackend {
   Error dequant_rows(int fmt, const void* packed, int64_t rows, int64_t cols, float* out);
   Error router(const float* x, const float* gate_w, int64_t T, int64_t D, int64_t E,
                float* probs, float* top, float* logits);
+  // MoEExperts (top-1 linear experts, moe_experts_f32): y[b] = x[b] . W[e_b]^T
+  Error experts_linear(const float* x, const float* W, const float* top, int64_t B, int64_t D, int64_t E,
+                       float* y);
   Error experts(const float* x, const ExpertWeights& g, const ExpertWeights& u,
                 const ExpertWeights& d, const float* probs, int64_t T, int64_t D, int64_t E,
                 int64_t I, int top_k, int norm_topk, float* y);

@@ -172,7 +172,51 @@ cudaError_t down(const void* Dn, int64_t E, int64_t D, int64_t I, int64_t dp, co
   return cudaGetLastError();
 }
 
+// MoEExperts (legacy top-1 linear experts, libs/uaii-kernels/src/transformer.cpp:483-520):
+// y[b, o] = sum_i x[b, i] * W[e, o, i], i ascending, products and sums rounded
+// separately, e = (int)top[b] or expert 0 outside [0, E).  One block owns 128 outputs
+// of one token; 32-column tiles of its 128 weight rows are staged through shared memory
+// with coalesced loads (row pitch 33 floats: thread o reads row o without bank
+// conflicts) and every thread walks its row's tile in order.
+constexpr int kLinRows = 128, kLinCols = 32;
+
+__global__ void __launch_bounds__(kLinRows) experts_linear_kernel(const float* __restrict__ x,
+                                                                  const float* __restrict__ W,
+                                                                  const float* __restrict__ top, int64_t D,
+                                                                  int64_t E, float* __restrict__ y) {
+  __shared__ float sw[kLinRows][kLinCols + 1];
+  __shared__ float sx[kLinCols];
+  const int64_t b = blockIdx.x;
+  const int64_t o0 = (int64_t)blockIdx.y * kLinRows;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float v = top[b];
+  const int64_t e = (v > -1.0f && v < (float)E) ? (int64_t)(int)v : 0;
+  const float* We = W + e * D * D;
+  float sum = 0.0f;
+  for (int64_t i0 = 0; i0 < D; i0 += kLinCols) {
+    const int64_t i = i0 + lane;
+    for (int r = warp; r < kLinRows; r += kLinRows / 32)
+      sw[r][lane] = (o0 + r < D && i < D) ? __ldg(We + (o0 + r) * D + i) : 0.0f;
+    if (warp == 0) sx[lane] = i < D ? __ldg(x + b * D + i) : 0.0f;
+    __syncthreads();
+    const int n = D - i0 < kLinCols ? (int)(D - i0) : kLinCols;
+    for (int j = 0; j < n; ++j) sum = __fadd_rn(sum, __fmul_rn(sx[j], sw[threadIdx.x][j]));
+    __syncthreads();
+  }
+  if (o0 + threadIdx.x < D) y[b * D + o0 + threadIdx.x] = sum;
+}
+
 }  // namespace
+
+cudaError_t launch_experts_linear(const float* x, const float* W, const float* top, int64_t B, int64_t D,
+                                  int64_t E, float* y, cudaStream_t st) {
+  if (B == 0) return cudaSuccess;
+  if (B < 0 || D <= 0 || E <= 0 || B > INT32_MAX || (D + kLinRows - 1) / kLinRows > 65535)
+    return cudaErrorInvalidValue;
+  experts_linear_kernel<<<dim3((unsigned)B, (unsigned)((D + kLinRows - 1) / kLinRows)), kLinRows, 0, st>>>(
+      x, W, top, D, E, y);
+  return cudaGetLastError();
+}
 
 #define UAII_FMT_CASES(M)                                                          \
   M(kF32) M(kF16) M(kQ4_0) M(kQ4_1) M(kQ5_0) M(kQ5_1) M(kQ8_0) M(kQ2_K) M(kQ3_K)  \

@@ -1267,7 +1267,7 @@ __global__ void __launch_bounds__(kWmThreads, 1)
 template <int F> struct QuadUnit;
 
 template <> struct QuadUnit<kQ4_K> {
-  uint32_t w[8], w8[8];            // qs bytes [32t, 32t + 32), and each word shifted right by 8
+  uint32_t w[8];                   // qs bytes [32t, 32t + 32)
   __half2 f_lo, b_lo, f_hi, b_hi;  // fold constants of sub-blocks 2t and 2t + 1
   uint32_t m_lo, m_hi;             // (m, m) of the two sub-blocks, f16
   uint32_t mf;                     // (m of sub-block 2t, m of 2t + 1), f16
@@ -1278,8 +1278,6 @@ template <> struct QuadUnit<kQ4_K> {
     const uint4 qb = *reinterpret_cast<const uint4*>(row + 32 + 32 * t);
     w[0] = qa.x; w[1] = qa.y; w[2] = qa.z; w[3] = qa.w;
     w[4] = qb.x; w[5] = qb.y; w[6] = qb.z; w[7] = qb.w;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) w8[i] = w[i] >> 8;
     // (scale, min) of sub-blocks j = 2t, 2t + 1 in the get_scale_min_k4 bit layout, as byte pairs
     const uint32_t sh = 16u * (uint32_t)(t & 1);
     const uint32_t y2 = hdr.y >> sh, z2 = hdr.z >> sh, w2 = hdr.w >> sh;
@@ -1308,9 +1306,10 @@ template <> struct QuadUnit<kQ4_K> {
     dmin = __high2float(dm);
   }
   // k-step s: the pair at positions (2t, 2t+1) (bytes 0, 2 of word s % 8) and at
-  // (2t+8, 2t+9) (bytes 1, 3), low nibbles for s < 8, high nibbles after
+  // (2t+8, 2t+9) (bytes 1, 3), low nibbles for s < 8, high nibbles after.  The caller
+  // runs k-steps s and s + 8 back to back, so the shifted word is formed once for both.
   __device__ __forceinline__ void pair(int s, uint32_t& lo, uint32_t& hi) const {
-    const uint32_t q = w[s & 7], q8 = w8[s & 7];
+    const uint32_t q = w[s & 7], q8 = w[s & 7] >> 8;
     if (s < 8) {
       lo = as_u32(__hfma2(magic_pair(q, 0x000F000Fu), f_lo, b_lo));
       hi = as_u32(__hfma2(magic_pair(q8, 0x000F000Fu), f_lo, b_lo));
@@ -1453,11 +1452,11 @@ __global__ void __launch_bounds__(kWmThreads, 1)
       const Tile t = decode_tile(args, tile, BN);
       int q0, q1;
       quad_range(t, q0, q1);
-      float acc[NT][4];
+      float acc[NT][4], acc2[NT][4];  // acc2: Q6_K odd k-steps with one slot octet
 #pragma unroll
       for (int n = 0; n < NT; ++n)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[n][i] = 0.f;
+        for (int i = 0; i < 4; ++i) acc[n][i] = acc2[n][i] = 0.f;
       for (int q = q0; q < q1; ++q, ++pi) {
         if (((q - q0) & 1) != h) continue;  // the other half's quad
         if (!(ok = bounded_wait(full + pi % ST, (pi / ST) & 1, s_abort, err, kErrTimeoutDequant))) break;
@@ -1503,14 +1502,20 @@ __global__ void __launch_bounds__(kWmThreads, 1)
           am_hi[0] = am_hi[2] = u0.m_hi;
           am_hi[1] = am_hi[3] = u1.m_hi;
         }
-        float m1[NT][4], m2[NT][4];  // Q4_K: this quad's sum of q*sc*x and of m*x
+        // Q4_K: this quad's sums of q*sc*x and of m*x.  With one slot octet (NT == 1) the odd
+        // k-steps accumulate into a second register set (m1o, and acc2 for Q6_K), so the warp's
+        // MMAs form two dependency chains instead of one.
+        constexpr int kChains = NT == 1 ? 2 : 1;
+        float m1[NT][4], m2[NT][4], m1o[NT][4];
 #pragma unroll
         for (int n = 0; n < NT; ++n)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) m1[n][i] = m2[n][i] = 0.f;
+          for (int i = 0; i < 4; ++i) m1[n][i] = m2[n][i] = m1o[n][i] = 0.f;
         __syncwarp();  // ldmatrix / mma.sync below need the whole warp converged
 #pragma unroll
-        for (int s = 0; s < 16; ++s) {
+        for (int idx = 0; idx < 16; ++idx) {
+          // Q4_K: k-steps j and j + 8 (the low and high nibbles of packed word j) back to back
+          const int s = F == kQ4_K ? (idx >> 1) + 8 * (idx & 1) : idx;
           uint32_t a[4];  // rows g, g + 8 at positions (2tq, 2tq+1); the same at (2tq+8, 2tq+9)
           u0.pair(s, a[0], a[2]);
           u1.pair(s, a[1], a[3]);
@@ -1525,15 +1530,16 @@ __global__ void __launch_bounds__(kWmThreads, 1)
                          : "=r"(b[0]), "=r"(b[1])
                          : "r"(addr));
           }
+          const bool odd = kChains == 2 && (idx & 1);
           if constexpr (F == kQ4_K) {
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
-              mma_16816(m1[n], a, b[2 * n], b[2 * n + 1]);
+              mma_16816(odd ? m1o[n] : m1[n], a, b[2 * n], b[2 * n + 1]);
               if constexpr (!kXSum) mma_16816(m2[n], s < 8 ? am_lo : am_hi, b[2 * n], b[2 * n + 1]);
             }
           } else {
 #pragma unroll
-            for (int n = 0; n < NT; ++n) mma_16816(acc[n], a, b[2 * n], b[2 * n + 1]);
+            for (int n = 0; n < NT; ++n) mma_16816(odd ? acc2[n] : acc[n], a, b[2 * n], b[2 * n + 1]);
           }
         }
         if constexpr (kXSum) {  // sum_k m(row, sub-block k) S(slot, k): one k-step of 8 sub-blocks (+ 8 zeros), twice
@@ -1550,11 +1556,16 @@ __global__ void __launch_bounds__(kWmThreads, 1)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const float dv = i < 2 ? u0.d : u1.d, mv = i < 2 ? u0.dmin : u1.dmin;
-              acc[n][i] = fmaf(-mv, m2[n][i], fmaf(dv, m1[n][i], acc[n][i]));
+              const float p = kChains == 2 ? m1[n][i] + m1o[n][i] : m1[n][i];
+              acc[n][i] = fmaf(-mv, m2[n][i], fmaf(dv, p, acc[n][i]));
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty + pi % ST);
+      }
+      if constexpr (F == kQ6_K && NT == 1) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[0][i] += acc2[0][i];
       }
       // every compute warp reaches this barrier once per tile; a wait that gave up stops all of them
       if (bar_any(1, kCompute, !ok)) break;

@@ -117,6 +117,11 @@ cudaError_t launch_down_simt(int dfmt, const void* Dn, int64_t E, int64_t D, int
                              int64_t d_pitch, const float* h, const int32_t* offsets,
                              const int32_t* counts, float* out, cudaStream_t st);
 
+// MoEExperts (top-1 linear experts): y[b] = x[b] . W[e_b]^T, W [E, D, D] f32, e_b = (int)top[b]
+// (expert 0 outside [0, E)), sequential f32 sums in the reference order.
+cudaError_t launch_experts_linear(const float* x, const float* W, const float* top, int64_t B, int64_t D,
+                                  int64_t E, float* y, cudaStream_t st);
+
 // ---- experts_umma.cu: tensor-core grouped GEMM (tcgen05 + TMEM + TMA)
 bool umma_format_supported(int fmt);
 // whole-layer check: formats, K chunking and tile multiples (any row pitch: rows that
