@@ -91,6 +91,19 @@ int urt_session_get_f32(void* s, const char* name, float* out, size_t cap, size_
   return 0;
 }
 
+// Session::generate (libs/uaii-runtime/src/session.cpp:910-1046), greedy, as uaii_session_generate
+// calls it: the prompt is prefilled one token per run, then max_new tokens are sampled.
+int urt_session_generate(void* s, const int64_t* prompt, size_t n, int64_t max_new, int64_t* out, size_t cap,
+                         size_t* out_n) {
+  std::vector<std::int64_t> toks;
+  const int st = status(static_cast<uaii::runtime::Session*>(s)->generate(
+      std::vector<std::int64_t>(prompt, prompt + n), max_new, &toks));
+  if (st != 0) return st;
+  *out_n = toks.size() < cap ? toks.size() : cap;
+  for (size_t i = 0; i < *out_n; ++i) out[i] = toks[i];
+  return 0;
+}
+
 const char* urt_session_backend_details(void* s) {
   static thread_local std::string d;
   const auto* b = static_cast<uaii::runtime::Session*>(s)->backend();

@@ -15,6 +15,11 @@ wherever the reference's top-two margin exceeds twice the observed logit error.
 Teacher forcing: both sides consume the reference's tokens, so one close call cannot
 derail the rest of the run.
 """
+import json
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 
@@ -165,3 +170,60 @@ def test_device_synthetic_inputs_match_host(um, backend):
         um.quantize_rows_device(backend, fmt, src_d, dst)
         backend.synchronize()
         assert np.array_equal(dst.cpu().numpy(), um.quantize_rows(fmt, src)), fmt
+
+
+def test_decoder_matches_the_reference_session_generate(um, backend, tmp_path):
+    """The f1 oracle of the reference itself: its unmodified Session (oracle/_ref runtime build)
+    loads a GGUF file of a 2-layer Mixtral-shaped model, prefills a 4-token prompt one token per
+    run and generates greedily (tests/reference_decoder_session.py, a child process, CPU).  The
+    device decoder gets the same packed tensors, steps through the same prompt from an empty cache
+    (two identical sequences in the batch) and, teacher forced with the reference's tokens, must
+    give logits within LOGIT_TOL of the largest logit at every generated position and the same
+    greedy token wherever the reference's top-two margin exceeds twice the observed error."""
+    so = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref",
+                      "libuaii_ref_runtime.so")
+    if not os.path.exists(so):
+        pytest.skip("reference runtime not built")
+    helper = os.path.join(os.path.dirname(os.path.abspath(__file__)), "reference_decoder_session.py")
+    p = subprocess.run([sys.executable, helper, str(tmp_path)], capture_output=True, text=True, timeout=600)
+    lines = [ln for ln in p.stdout.splitlines() if ln.startswith("{")]
+    assert p.returncode == 0 and lines, p.stderr[-2000:]
+    ref = json.loads(lines[-1])
+    W = dict(np.load(tmp_path / "weights.npz"))
+    nl, hd, steps = 2, 128, len(ref["tokens"])
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    blocks, keep = [], []
+    for l in range(nl):
+        g = lambda n: dev(W[f"blk.{l}.{n}.weight"])
+        d = {n: g(n) for n in ("attn_norm", "ffn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate_inp",
+                               "ffn_gate_exps", "ffn_up_exps", "ffn_down_exps")}
+        keep.append(d)
+        moe = um.make_layer(D, E, I, TOPK, 1, d["ffn_gate_inp"], d["ffn_gate_exps"], um.Q4_K, d["ffn_up_exps"],
+                            um.Q4_K, d["ffn_down_exps"], um.Q6_K)
+        blocks.append({"attn_norm": d["attn_norm"], "ffn_norm": d["ffn_norm"], "wq": d["attn_q"], "wq_fmt": um.Q8_0,
+                       "wk": d["attn_k"], "wk_fmt": um.Q8_0, "wv": d["attn_v"], "wv_fmt": um.Q8_0,
+                       "wo": d["attn_output"], "wo_fmt": um.Q8_0, "moe": moe})
+    emb, out_norm = dev(W["token_embd.weight"]), dev(W["output_norm.weight"])
+    prompt = ref["prompt"]
+    dec = um.Decoder(backend, nl, D, H, HKV, V, 2, len(prompt) + steps, blocks, out_norm, emb, um.Q8_0,
+                     rope_theta=THETA, rms_eps=EPS, head_dim=hd)
+    dec._keep.append(keep)
+    try:
+        for t in prompt[:-1]:  # positions 0 .. P-2
+            dec.step(np.array([t, t], np.int32), None, np.empty(2, np.int32))
+        tok = prompt[-1]
+        for j in range(steps):
+            logits = np.empty((2, V), np.float32)
+            nxt = np.empty(2, np.int32)
+            dec.step(np.array([tok, tok], np.int32), logits, nxt)
+            r = np.asarray(ref["logits"][j], np.float64)
+            scale = float(np.abs(r).max())
+            err = float(np.abs(logits.astype(np.float64) - r[None, :]).max())
+            assert err <= LOGIT_TOL * scale, (j, err / scale)
+            assert np.array_equal(logits[0], logits[1])
+            top2 = np.sort(r)[-2:]
+            if top2[1] - top2[0] > 2 * err:
+                assert int(nxt[0]) == ref["tokens"][j], (j, int(nxt[0]), ref["tokens"][j])
+            tok = ref["tokens"][j]  # teacher forcing
+    finally:
+        dec.close()

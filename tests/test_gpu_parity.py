@@ -497,6 +497,31 @@ def test_quad_schedule_vs_oracle_and_unit_schedule(backend, oracle, um, gf, df, 
         assert rel_err(ys[3][0], ys[4][0]) <= 1e-4
 
 
+@pytest.mark.parametrize("T,I", [(1, 1024), (2, 1024)])
+def test_quad_tail_split_vs_oracle_and_repeatable(backend, oracle, um, T, I):
+    """Gate/up tiles of a last wave that fills at most half of the GPU are cut into K ranges
+    run by different CTAs (2 experts x I/64 tiles here, all in one partial wave); the CTA that
+    finishes a tile's last range adds the ranges in order.  Against the oracle, and
+    bit-identical over repeated calls (the per-tile counters are left at zero)."""
+    gf, df, D, E, k = 14, 16, 4096, 8, 2
+    x, w, G, U, Dn = layer_case(um, gf, df, T, D, E, I, k, 900 + T)
+    _, pr, _ = oracle.router(x, w)
+    y_ref, _, _ = oracle.experts_packed(x, G, gf, U, gf, Dn, df, pr, E, I, k, 1)
+    L = um.make_layer(D, E, I, k, 1, w, G, gf, U, gf, Dn, df)
+    backend.set_graphs(False)
+    try:
+        ys = []
+        for _ in range(3):
+            y = np.empty_like(x)
+            backend.ffn(L, x, T, y)
+            ys.append(y)
+        assert backend.last_plan()["schedule"] == "quad_mma"
+    finally:
+        backend.set_graphs(True)
+    assert rel_err(ys[0], y_ref) <= REL_TOL
+    assert bits_equal(ys[0], ys[1]) and bits_equal(ys[0], ys[2])
+
+
 @pytest.mark.parametrize("gf,df", [(14, 16), (14, 14)])
 def test_mixed_schedule_at_16_slot_tiles(backend, oracle, um, gf, df):
     """16-slot tiles of a K-quant layer: gate/up on tcgen05 (operands in tc_kpos order), the down

@@ -81,6 +81,10 @@ Error MoeCudaBackend::initialize(int device, cudaStream_t stream) {
   device_ = device;
   UAII_CUDA(cudaMalloc(&dev_err_, sizeof(int)), "Malloc(error flag)");
   UAII_CUDA(cudaMemset(dev_err_, 0, sizeof(int)), "Memset(error flag)");
+  // the quad schedule's tail-split partials and counters (the counters stay zero between launches)
+  UAII_CUDA(cudaMalloc(&tail_.part, tail_bytes()), "Malloc(tail split)");
+  tail_.cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(tail_.part) + tail_part_bytes());
+  UAII_CUDA(cudaMemset(tail_.cnt, 0, sizeof(int) * kTailMaxUnits), "Memset(tail split)");
   if (stream == nullptr) {
     UAII_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "StreamCreate");
     own_stream_ = true;
@@ -134,6 +138,8 @@ void MoeCudaBackend::shutdown() noexcept {
   ws_cap_ = ws_used_ = 0;
   if (dev_err_) (void)cudaFree(dev_err_);
   dev_err_ = nullptr;
+  if (tail_.part) (void)cudaFree(tail_.part);
+  tail_ = TailSplit{};
   for (auto e : chunk_events_) (void)cudaEventDestroy(e);
   chunk_events_.clear();
   if (in_stream_) (void)cudaStreamDestroy(in_stream_);
@@ -157,6 +163,7 @@ Error MoeCudaBackend::sync_and_check() {
   UAII_CUDA(cudaMemcpy(&code, dev_err_, sizeof(int), cudaMemcpyDeviceToHost), "Memcpy(error flag)");
   if (code != 0) {
     (void)cudaMemset(dev_err_, 0, sizeof(int));
+    if (tail_.cnt) (void)cudaMemset(tail_.cnt, 0, sizeof(int) * kTailMaxUnits);  // a kernel may have stopped mid-tile
     return Error::make(ErrorCode::Internal,
                        "tensor-core expert kernel gave up waiting (code " + std::to_string(code) + ")");
   }
@@ -699,7 +706,7 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
     UAII_TRY(umma_rows(dd, L.down.fmt, E * D, I, weight_is_constant(L.down.data, expert_bytes(L.down, E)), &dd,
                        &dpitch));
     UAII_CUDA(launch_gateup_umma(L.gate.fmt, gd, ud, gpitch, E, I, D, xp16, S, rb.counts, rb.offsets, tile_base, P.bn,
-                                 h16, dev_err_, stream_, sched, h_order, tables, xsum),
+                                 h16, dev_err_, stream_, sched, h_order, tables, xsum, &tail_),
               "gateup(tensor cores)");
     phase_end();
     phase_begin(kDown);

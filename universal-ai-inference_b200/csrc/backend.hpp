@@ -225,6 +225,9 @@ class MoeCudaBackend {
   int path_ = 0;
   ExpertPlan last_plan_{};
   int* dev_err_ = nullptr;
+  TailSplit tail_{};  // quad schedule tail split (null in external mode: no split)
+  static size_t tail_part_bytes() { return sizeof(float) * (size_t)kTailMaxUnits * 128 * kTailMaxBn; }
+  static size_t tail_bytes() { return tail_part_bytes() + sizeof(int) * (size_t)kTailMaxUnits; }
   bool external_ = false;  // workspace and error flag belong to the caller
   char* ws_ = nullptr;
   size_t ws_cap_ = 0;

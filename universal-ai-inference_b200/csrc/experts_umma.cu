@@ -76,6 +76,7 @@ struct Args {
   int kquads;   // quads per row: ceil(K / 256)
   int k_atoms;  // 64-element atoms per row: K / 64
   int rows_per_expert, gateup;
+  int band_m;  // weight-row tiles per band of the tile order (see decode_tile)
   __half* h_out;  // gate/up: [S, out_ld] f16 in K order h_order (tcgen05 and quad; the per-unit warp schedule: wm_kpos)
   int h_order;
   float* out;     // down: [splits][S][out_ld] f32
@@ -86,6 +87,12 @@ struct Args {
   // null: the minima go through one MMA per k-step instead.
   const __half* xsum;
   int64_t S_rows;
+  // Quad schedule, gate/up: when the last wave of tiles fills at most half of the grid, its
+  // tiles are cut into K ranges run by different CTAs; tail_part [tiles][ranges][128][BN] f32
+  // holds the ranges' sums and tail_cnt [tiles] (zero between launches) counts finished ranges.
+  // Null: no tail split.
+  float* tail_part;
+  int* tail_cnt;
 };
 
 __device__ __forceinline__ __half2 as_h2(uint32_t v) {
@@ -314,12 +321,18 @@ struct Tile {
   int e, m_tile, n_tile, split;
 };
 
-// Tile order inside an expert: K splits fastest, then bands of kBandM weight-row
+// Tile order inside an expert: K splits fastest, then bands of band_m weight-row
 // tiles -- the row tiles of a band fastest, then the slot tiles.  The tiles in
-// flight at once (one per SM) then share kBandM weight tiles and about
-// SMs / kBandM activation tiles, so an expert with many slot tiles re-reads
-// neither its weights nor its activations once per wave from HBM.
+// flight at once (one per SM) then share band_m weight tiles and about
+// SMs / band_m activation tiles, so an expert with many slot tiles re-reads
+// neither its weights nor its activations once per wave from HBM.  An expert whose
+// tiles straddle two waves is read in both: with wide bands its weights (every
+// slot tile needs all rows), with one-tile bands its activations.  Gate/up uses
+// bands of kBandM (its activations are the small operand either way); the down
+// projection uses one-tile bands, where the f16 hidden rows are smaller than the
+// expert's down weights (Mixtral: 29 MB against 48 MB).
 constexpr int kBandM = 32;
+constexpr int kDownBandM = 1;
 
 __device__ __forceinline__ Tile decode_tile(const Args& a, int tile, int bn) {
   int lo = 0, hi = a.E;  // largest e with tile_base[e] <= tile (always a non-empty expert)
@@ -333,10 +346,10 @@ __device__ __forceinline__ Tile decode_tile(const Args& a, int tile, int bn) {
   t.split = local % a.splits;
   local /= a.splits;
   const int nt = (__ldg(a.counts + lo) + bn - 1) / bn;
-  const int band = local / (kBandM * nt);
-  const int m0 = band * kBandM;
-  const int bm = min(kBandM, a.m_tiles - m0);  // the last band may be narrower
-  const int r = local - band * kBandM * nt;
+  const int band = local / (a.band_m * nt);
+  const int m0 = band * a.band_m;
+  const int bm = min(a.band_m, a.m_tiles - m0);  // the last band may be narrower
+  const int r = local - band * a.band_m * nt;
   t.n_tile = r / bm;
   t.m_tile = m0 + r % bm;
   return t;
@@ -1395,11 +1408,39 @@ __global__ void __launch_bounds__(kWmThreads, 1)
     prefetch_tmap(&tm_x);
   }
   __syncthreads();
-  const int total = __ldg(args.tile_base + args.E);
+  const int tiles = __ldg(args.tile_base + args.E);
   int* err = args.err;
-  auto quad_range = [&](const Tile& t, int& q0, int& q1) {
+  // Tail split (gate/up): `rem` tiles of a last wave that fills at most half of the grid each
+  // become `ts` units of consecutive quads (at least two, one per half); the CTA that finishes
+  // a tile's last unit adds the units' sums in unit order and runs the epilogue.
+  int tail_base = tiles, ts = 1;
+  if (args.tail_part != nullptr && args.gateup) {
+    const int G = (int)gridDim.x, rem = tiles % G, smax = args.kquads / 2;
+    if (rem > 0 && 2 * rem <= G && smax >= 2) {
+      ts = min(smax, G / rem);
+      tail_base = tiles - rem;
+    }
+  }
+  const int total = tail_base + (tiles - tail_base) * ts;
+  // unit -> tile, quad range, and (tail units) the tail tile index and the unit's rank in it
+  auto unit_tile = [&](int unit, Tile& t, int& q0, int& q1, int& tail, int& tsp) {
+    int tile = unit;
+    tail = -1;
+    tsp = 0;
+    if (unit >= tail_base) {
+      const int u = unit - tail_base;
+      tail = u / ts;
+      tsp = u - tail * ts;
+      tile = tail_base + tail;
+    }
+    t = decode_tile(args, tile, BN);
     q0 = t.split * args.kquads / args.splits;
     q1 = (t.split + 1) * args.kquads / args.splits;
+    if (tail >= 0) {
+      const int a0 = q0, nq = q1 - q0;
+      q0 = a0 + tsp * nq / ts;
+      q1 = a0 + (tsp + 1) * nq / ts;
+    }
   };
 
   if (warp == kWmWarps) {
@@ -1407,11 +1448,11 @@ __global__ void __launch_bounds__(kWmThreads, 1)
     uint32_t n = 0;  // stages issued
     bool ok = true;
     for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-      const Tile t = decode_tile(args, tile, BN);
+      Tile t;
+      int q0, q1, tail, tsp;
+      unit_tile(tile, t, q0, q1, tail, tsp);
       const int row0 = t.e * args.rows_per_expert + t.m_tile * (args.gateup ? 64 : 128);
       const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
-      int q0, q1;
-      quad_range(t, q0, q1);
       for (int q = q0; q < q1; ++q) {
         const int s = n % ST;
         if (!(ok = bounded_wait(empty + s, ((n / ST) & 1) ^ 1, s_abort, err, kErrTimeoutProducer))) break;
@@ -1449,9 +1490,9 @@ __global__ void __launch_bounds__(kWmThreads, 1)
     uint32_t pi = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
-      const Tile t = decode_tile(args, tile, BN);
-      int q0, q1;
-      quad_range(t, q0, q1);
+      Tile t;
+      int q0, q1, tail, tsp;
+      unit_tile(tile, t, q0, q1, tail, tsp);
       float acc[NT][4], acc2[NT][4];  // acc2: Q6_K odd k-steps with one slot octet
 #pragma unroll
       for (int n = 0; n < NT; ++n)
@@ -1581,6 +1622,30 @@ __global__ void __launch_bounds__(kWmThreads, 1)
       for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[n][i] += red[4 * n + i];
+      if (tail >= 0) {  // a tail unit: publish this range's sums; the tile's last unit adds them all
+        float* part = args.tail_part + (int64_t)tail * ts * (128 * BN);
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            part[(int64_t)tsp * (128 * BN) + (16 * mw + g + 8 * (i >> 1)) * BN + 8 * n + 2 * tq + (i & 1)] =
+                acc[n][i];
+        __threadfence();
+        bar_sync(2, kCompute / 2);
+        const bool last = bar_any(2, kCompute / 2, threadIdx.x == 0 && atomicAdd(args.tail_cnt + tail, 1) == ts - 1);
+        if (!last) continue;
+        __threadfence();
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float* src = part + (16 * mw + g + 8 * (i >> 1)) * BN + 8 * n + 2 * tq + (i & 1);
+            float v = 0.f;
+            for (int r = 0; r < ts; ++r) v += __ldcg(src + (int64_t)r * (128 * BN));
+            acc[n][i] = v;
+          }
+        if (threadIdx.x == 0) args.tail_cnt[tail] = 0;  // zero again for the next launch
+      }
       // accumulator (n, i): row g + 8(i / 2) of the block, slot 8n + 2tq + i % 2
       const int n_valid = min(BN, __ldg(args.counts + t.e) - t.n_tile * BN);
       const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
@@ -1860,7 +1925,7 @@ cudaError_t launch_common(int sched, int fmt, bool gateup, const void* W0, const
                           int64_t E, int64_t rows, int64_t K, const void* act16, int64_t S_rows,
                           const int32_t* counts, const int32_t* offsets, int32_t* tile_base, int bn, int splits,
                           void* h16, float* out, int64_t out_ld, int64_t split_stride, int* err, cudaStream_t st,
-                          int h_order, bool table_ready, const void* xsum) {
+                          int h_order, bool table_ready, const void* xsum, const TailSplit* tail) {
   const int mk = min_k(fmt);
   const bool warp_mma = sched == kSchedWarpMma, quad = sched == kSchedQuadMma;
   if (!mk || K % mk != 0 || K <= 0) return cudaErrorNotSupported;
@@ -1898,10 +1963,16 @@ cudaError_t launch_common(int sched, int fmt, bool gateup, const void* W0, const
   a.k_atoms = (int)(K / 64);
   a.rows_per_expert = (int)rows;
   a.gateup = gateup ? 1 : 0;
+  a.band_m = gateup ? kBandM : kDownBandM;
   a.h_out = static_cast<__half*>(h16);
   a.h_order = h_order;
   a.xsum = quad && fmt == kQ4_K ? static_cast<const __half*>(xsum) : nullptr;
   a.S_rows = S_rows;
+  if (quad && gateup && tail != nullptr && tail->part != nullptr && tail->cnt != nullptr && bn <= kTailMaxBn &&
+      num_sms() <= kTailMaxUnits) {
+    a.tail_part = tail->part;
+    a.tail_cnt = tail->cnt;
+  }
   a.out = out;
   a.out_ld = out_ld;
   a.split_stride = split_stride;
@@ -1966,9 +2037,9 @@ bool warp_mma_shapes_supported(int gfmt, int dfmt, int64_t D, int64_t I) {
 cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pitch, int64_t E, int64_t I, int64_t D,
                                const void* xp16, int64_t S_rows, const int32_t* counts, const int32_t* offsets,
                                int32_t* tile_base, int bn, void* h16, int* err, cudaStream_t st, int sched,
-                               int h_order, bool table_ready, const void* xsum) {
+                               int h_order, bool table_ready, const void* xsum, const TailSplit* tail) {
   return launch_common(sched, fmt, true, G, U, pitch, E, I, D, xp16, S_rows, counts, offsets, tile_base, bn, 1,
-                       h16, nullptr, I, 0, err, st, h_order, table_ready, xsum);
+                       h16, nullptr, I, 0, err, st, h_order, table_ready, xsum, tail);
 }
 
 cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
@@ -1976,7 +2047,7 @@ cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, 
                              int bn, int splits, float* out, int* err, cudaStream_t st, int sched,
                              bool table_ready) {
   return launch_common(sched, fmt, false, Dn, Dn, pitch, E, D, I, h16, S_rows, counts, offsets, tile_base, bn,
-                       splits, nullptr, out, D, S_rows * D, err, st, kOrderTc, table_ready, nullptr);
+                       splits, nullptr, out, D, S_rows * D, err, st, kOrderTc, table_ready, nullptr, nullptr);
 }
 
 namespace {

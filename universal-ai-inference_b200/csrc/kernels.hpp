@@ -154,11 +154,20 @@ inline bool quad_mma_format(int fmt) { return fmt == 14 || fmt == 16; }
 // quad, the f32 sums of the eight 32-element sub-blocks of the f16 activations as 8 f16 values
 // then their 8 f16 remainders ([S_rows][kquads][16] f16, route_gather writes them), so the Q4_K
 // minima take two MMAs per quad instead of one per k-step.
+// Tail split of the quad schedule's gate/up launch (see the kernel): part holds
+// kTailMaxUnits x 128 x kTailMaxBn f32, cnt kTailMaxUnits ints, zero before the first launch
+// (every launch leaves them zero).  A null or absent TailSplit turns the split off.
+constexpr int kTailMaxUnits = 256, kTailMaxBn = 16;
+struct TailSplit {
+  float* part = nullptr;
+  int* cnt = nullptr;
+};
 cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pitch, int64_t E, int64_t I, int64_t D,
                                const void* xp16, int64_t S_rows, const int32_t* counts,
                                const int32_t* offsets, int32_t* tile_base, int bn, void* h16, int* err,
                                cudaStream_t st, int sched = kSchedTcgen05, int h_order = 0,
-                               bool table_ready = false, const void* xsum = nullptr);
+                               bool table_ready = false, const void* xsum = nullptr,
+                               const TailSplit* tail = nullptr);
 // out[split][slot, o] = partial of h16[slot] . Dn[e, o] over the split's K range (f32).
 cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
                              int64_t S_rows, const int32_t* counts, const int32_t* offsets,

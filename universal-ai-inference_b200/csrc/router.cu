@@ -444,10 +444,20 @@ BlockPlan block_plan(int64_t T, int64_t D, int64_t E) {
   const int nkt = (int)((D + kTile - 1) / kTile);
   p.groups = 0;
   if (p.tblocks * p.eblocks < 148 && nkt > 1) {  // under one wave of blocks: split the row, fold after
-    int64_t g = (2 * 148 + p.tblocks * p.eblocks - 1) / (p.tblocks * p.eblocks);
-    if (g > nkt) g = nkt;
-    p.tpg = (int)((nkt + g - 1) / g);
-    p.groups = (nkt + p.tpg - 1) / p.tpg;
+    // the group count whose busiest SM does the least work: ceil(blocks / SMs) blocks of
+    // ceil(tiles / groups) tiles each (the smaller count on a tie: less to fold)
+    const int64_t tb = p.tblocks * p.eblocks;
+    int64_t best_g = 1, best = -1;
+    for (int64_t g = 1; g <= nkt; ++g) {
+      const int64_t tpg = (nkt + g - 1) / g, groups = (nkt + tpg - 1) / tpg;
+      const int64_t cost = ((tb * groups + 147) / 148) * tpg;
+      if (best < 0 || cost < best) {
+        best = cost;
+        best_g = groups;
+      }
+    }
+    p.tpg = (int)((nkt + best_g - 1) / best_g);
+    p.groups = (int)((nkt + p.tpg - 1) / p.tpg);
   }
   return p;
 }
