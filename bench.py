@@ -633,7 +633,7 @@ def main():
                 "data": "synthetic (seeded random-init GGUF layer, N(0,1) activations)",
                 "config": {"workload": workload, "note": WORKLOAD_NOTE.get(args.config, ""),
                            "tokens_per_gpu": T,
-                           "parallelism": (f"expert parallel x{world} (NCCL all-to-all dispatch/combine)" if ep_mode
+                           "parallelism": (f"expert parallel x{world} (NCCL all-to-all dispatch/combine, f16 return rows)" if ep_mode
                                            else f"replicas x{world}" if world > 1 else "1 GPU"),
                            "l2": "inputs larger than L2 (packed expert weights re-read every step)",
                            "experts_touched": touched},

@@ -374,6 +374,15 @@ UAII_MOE_API int uaii_moe_ep_experts_records(uaii_moe_backend* b, const uaii_moe
 UAII_MOE_API int uaii_moe_ep_combine(uaii_moe_backend* b, const float* y_back, const int32_t* row_of, int64_t T,
                                      int world, int64_t d_model, float* y);
 
+/* Steps 2 and 3 with f16 return rows (half the bytes of the reverse exchange): each
+ * received row's weighted expert sum is rounded once to f16 (d_model a multiple of 4),
+ * and the source rank adds the returned f16 rows in f32, in rank order. */
+UAII_MOE_API int uaii_moe_ep_experts_records_f16(uaii_moe_backend* b, const uaii_moe_layer* layer,
+                                                 const void* recv_rec, int64_t rec_bytes, int64_t rows,
+                                                 int64_t entries, void* y_part_f16);
+UAII_MOE_API int uaii_moe_ep_combine_f16(uaii_moe_backend* b, const void* y_back_f16, const int32_t* row_of,
+                                         int64_t T, int world, int64_t d_model, float* y);
+
 /* Failure-path self-test: launches one block whose threads wait, through the
  * same bounded wait as the tensor-core kernels, on a barrier nothing arrives
  * on; they give up after budget_cycles (1e3..4e9 SM cycles) and record an

@@ -630,7 +630,7 @@ Error MoeCudaBackend::umma_rows(const void* w, int fmt, int64_t rows, int64_t K,
 }
 
 Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const float* probs_for_w,
-                                  const LayerArgs& L, const ExpertPlan& P, int64_t T, float* yd, const EpRows* ep) {
+                                  const LayerArgs& L, const ExpertPlan& P, int64_t T, void* yd, const EpRows* ep) {
   last_plan_ = P;
   if (ep && !P.umma)
     return Error::make(ErrorCode::NotImplemented,
@@ -790,7 +790,8 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
     phase_end();
   }
   phase_begin(kCombine);
-  UAII_CUDA(launch_combine(out, D, splits, S * D, T, D, k, rb, sh_out, sh_splits, T * D, sh_gate, yd, stream_),
+  UAII_CUDA(launch_combine(out, D, splits, S * D, T, D, k, rb, sh_out, sh_splits, T * D, sh_gate, yd, stream_,
+                           ep != nullptr && ep->y_f16),
             "combine");
   phase_end();
   count_launches(1);
@@ -1003,8 +1004,8 @@ Error MoeCudaBackend::ep_dispatch(const LayerArgs& L, const float* x, int64_t T,
 }
 
 Error MoeCudaBackend::ep_experts(const LayerArgs& Lin, const void* recv_x16, const int32_t* recv_ids,
-                                 const float* recv_w, int64_t N, int64_t entries, float* y_part, int64_t x_pitch,
-                                 int64_t e_pitch) {
+                                 const float* recv_w, int64_t N, int64_t entries, void* y_part, int64_t x_pitch,
+                                 int64_t e_pitch, bool y_f16) {
   std::lock_guard<std::mutex> lk(mu_);
   UAII_CUDA(cudaSetDevice(device_), "SetDevice");
   LayerArgs L = Lin;
@@ -1020,7 +1021,8 @@ Error MoeCudaBackend::ep_experts(const LayerArgs& Lin, const void* recv_x16, con
     if (!is_device_ptr(p)) return Error::make(ErrorCode::InvalidArgument, "ep experts: arguments must be device memory");
   const ExpertPlan P = plan_experts(L, N, entries, /*allow_warp_mma=*/false);
   UAII_TRY(reserve(experts_ws(L, N, P) + layer_stage_bytes(L)));
-  const EpRows rows{recv_x16, recv_ids, recv_w, x_pitch, e_pitch};
+  if (y_f16 && L.D % 4 != 0) return Error::make(ErrorCode::InvalidArgument, "ep experts: f16 rows need d_model % 4 == 0");
+  const EpRows rows{recv_x16, recv_ids, recv_w, x_pitch, e_pitch, y_f16};
   return run_experts(nullptr, nullptr, nullptr, L, P, N, y_part, &rows);
 }
 
@@ -1034,8 +1036,8 @@ Error MoeCudaBackend::selftest_wait_timeout(int64_t budget_cycles) {
   return sync_and_check();
 }
 
-Error MoeCudaBackend::ep_combine(const float* y_back, const int32_t* row_of, int64_t T, int world, int64_t D,
-                                 float* y) {
+Error MoeCudaBackend::ep_combine(const void* y_back, const int32_t* row_of, int64_t T, int world, int64_t D,
+                                 float* y, bool y_back_f16) {
   std::lock_guard<std::mutex> lk(mu_);
   UAII_CUDA(cudaSetDevice(device_), "SetDevice");
   if (T < 0 || D <= 0 || world < 1) return Error::make(ErrorCode::InvalidArgument, "ep combine: shapes");
@@ -1044,7 +1046,8 @@ Error MoeCudaBackend::ep_combine(const float* y_back, const int32_t* row_of, int
                         static_cast<const void*>(y)})
     if (!is_device_ptr(p)) return Error::make(ErrorCode::InvalidArgument, "ep combine: arguments must be device memory");
   phase_begin(kCombine);
-  UAII_CUDA(launch_ep_combine(y_back, row_of, T, world, D, y, stream_), "ep_combine");
+  if (y_back_f16) UAII_CUDA(launch_ep_combine_f16(y_back, row_of, T, world, D, y, stream_), "ep_combine_f16");
+  else UAII_CUDA(launch_ep_combine(static_cast<const float*>(y_back), row_of, T, world, D, y, stream_), "ep_combine");
   phase_end();
   count_launches(1);
   return Error::success();
@@ -1703,6 +1706,29 @@ int uaii_moe_ep_experts_records(uaii_moe_backend* b, const uaii_moe_layer* l, co
   return report(b->impl.ep_experts(L, r, reinterpret_cast<const int32_t*>(r + 2 * L.D),
                                    reinterpret_cast<const float*>(r + 2 * L.D + 4 * L.top_k), rows, entries, y_part,
                                    rec_bytes / 2, rec_bytes / 4));
+}
+
+int uaii_moe_ep_experts_records_f16(uaii_moe_backend* b, const uaii_moe_layer* l, const void* recv_rec,
+                                    int64_t rec_bytes, int64_t rows, int64_t entries, void* y_part_f16) {
+  if (!b) return no_backend();
+  if (!l) return report(Error::make(ErrorCode::InvalidArgument, "null layer"));
+  {
+    const Error le = record_layout(l->d_model, (int)l->top_k, rec_bytes);
+    if (!le.ok()) return report(le);
+  }
+  LayerArgs L;
+  if (!layer_args_from_c(l, &L))
+    return report(Error::make(ErrorCode::InvalidArgument, "ep experts: null expert weights"));
+  const char* r = static_cast<const char*>(recv_rec);
+  return report(b->impl.ep_experts(L, r, reinterpret_cast<const int32_t*>(r + 2 * L.D),
+                                   reinterpret_cast<const float*>(r + 2 * L.D + 4 * L.top_k), rows, entries,
+                                   y_part_f16, rec_bytes / 2, rec_bytes / 4, /*y_f16=*/true));
+}
+
+int uaii_moe_ep_combine_f16(uaii_moe_backend* b, const void* y_back_f16, const int32_t* row_of, int64_t T, int world,
+                            int64_t d_model, float* y) {
+  if (!b) return no_backend();
+  return report(b->impl.ep_combine(y_back_f16, row_of, T, world, d_model, y, /*y_back_f16=*/true));
 }
 
 int uaii_moe_ep_experts(uaii_moe_backend* b, const uaii_moe_layer* l, const void* recv_x16, const int32_t* recv_ids,

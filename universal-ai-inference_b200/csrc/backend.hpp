@@ -131,9 +131,12 @@ class MoeCudaBackend {
   Error ep_dispatch(const LayerArgs& L, const float* x, int64_t T, int rank, int world, void* send_x16,
                     int32_t* send_ids, float* send_w, int32_t* send_token, int32_t* row_of, int32_t* send_counts,
                     int32_t* send_entries, float* probs, int64_t x_pitch = 0, int64_t e_pitch = 0);
+  // y_part f32, or f16 when y_f16 (each row's sum rounded once: half the return bytes)
   Error ep_experts(const LayerArgs& L_local, const void* recv_x16, const int32_t* recv_ids, const float* recv_w,
-                   int64_t rows, int64_t entries, float* y_part, int64_t x_pitch = 0, int64_t e_pitch = 0);
-  Error ep_combine(const float* y_back, const int32_t* row_of, int64_t T, int world, int64_t D, float* y);
+                   int64_t rows, int64_t entries, void* y_part, int64_t x_pitch = 0, int64_t e_pitch = 0,
+                   bool y_f16 = false);
+  Error ep_combine(const void* y_back, const int32_t* row_of, int64_t T, int world, int64_t D, float* y,
+                   bool y_back_f16 = false);
   // Runs the bounded-wait self-test kernel and returns the status the host observes.
   Error selftest_wait_timeout(int64_t budget_cycles);
 
@@ -180,9 +183,10 @@ class MoeCudaBackend {
     const int32_t* ids;
     const float* w;
     int64_t x_pitch, e_pitch;  // 0 = dense
+    bool y_f16;                // the per-row sums written as f16
   };
   Error run_experts(const float* x_dev, const float* scores, const float* probs_for_w,
-                    const LayerArgs& L, const ExpertPlan& P, int64_t T, float* y_dev,
+                    const LayerArgs& L, const ExpertPlan& P, int64_t T, void* y_dev,
                     const EpRows* ep = nullptr);
   Error sync_and_check();
   // Packed rows as the tensor-core path reads them (16-byte pitch).  `constant`: the

@@ -183,6 +183,51 @@ __global__ void ep_combine4_kernel(const float* __restrict__ y_back, const int32
   reinterpret_cast<float4*>(y + t * D)[c] = acc;
 }
 
+// ep_combine_kernel on f16 returned rows (any rank count).
+__global__ void ep_combine_h_kernel(const __half* __restrict__ y_back, const int32_t* __restrict__ row_of,
+                                    int64_t T, int R, int64_t D, float* __restrict__ y) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= T * D) return;
+  const int64_t t = i / D, c = i - t * D;
+  float acc = 0.0f;
+  for (int d = 0; d < R; ++d) {
+    const int row = row_of[t * R + d];
+    if (row >= 0) acc = __fadd_rn(acc, __half2float(y_back[(int64_t)row * D + c]));
+  }
+  y[i] = acc;
+}
+
+// ep_combine4_kernel on f16 returned rows: four halves per load, f32 sums in rank order.
+template <int RMAX>
+__global__ void ep_combine4h_kernel(const __half* __restrict__ y_back, const int32_t* __restrict__ row_of,
+                                    int64_t T, int R, int64_t D, float* __restrict__ y) {
+  const int64_t d4 = D / 4;
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= T * d4) return;
+  const int64_t t = i / d4, c = i - t * d4;
+  int row[RMAX];
+#pragma unroll
+  for (int d = 0; d < RMAX; ++d) row[d] = d < R ? row_of[t * R + d] : -1;
+  uint2 v[RMAX];
+#pragma unroll
+  for (int d = 0; d < RMAX; ++d)
+    if (row[d] >= 0) v[d] = reinterpret_cast<const uint2*>(y_back + (int64_t)row[d] * D)[c];
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int d = 0; d < RMAX; ++d) {
+    if (row[d] < 0) continue;
+    __half2 a, b;
+    memcpy(&a, &v[d].x, 4);
+    memcpy(&b, &v[d].y, 4);
+    const float2 fa = __half22float2(a), fb = __half22float2(b);
+    acc.x = __fadd_rn(acc.x, fa.x);
+    acc.y = __fadd_rn(acc.y, fa.y);
+    acc.z = __fadd_rn(acc.z, fb.x);
+    acc.w = __fadd_rn(acc.w, fb.y);
+  }
+  reinterpret_cast<float4*>(y + t * D)[c] = acc;
+}
+
 }  // namespace
 
 cudaError_t launch_ep_plan(const int32_t* topk_ids, int64_t T, int k, int R, int epr, uint8_t* dmask,
@@ -251,6 +296,21 @@ cudaError_t launch_ep_combine(const float* y_back, const int32_t* row_of, int64_
   else if (vec && R <= 4) ep_combine4_kernel<4><<<blocks4, 256, 0, st>>>(y_back, row_of, T, R, D, y);
   else if (vec && R <= 8) ep_combine4_kernel<8><<<blocks4, 256, 0, st>>>(y_back, row_of, T, R, D, y);
   else ep_combine_kernel<<<(unsigned)((T * D + 255) / 256), 256, 0, st>>>(y_back, row_of, T, R, D, y);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_combine_f16(const void* y_back16, const int32_t* row_of, int64_t T, int R, int64_t D, float* y,
+                                  cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  const __half* yb = static_cast<const __half*>(y_back16);
+  if (D % 4 != 0 || R > 8 || ((reinterpret_cast<uintptr_t>(y_back16) & 7) | (reinterpret_cast<uintptr_t>(y) & 15))) {
+    ep_combine_h_kernel<<<(unsigned)((T * D + 255) / 256), 256, 0, st>>>(yb, row_of, T, R, D, y);
+    return cudaGetLastError();
+  }
+  const unsigned blocks4 = (unsigned)((T * (D / 4) + 255) / 256);
+  if (R <= 2) ep_combine4h_kernel<2><<<blocks4, 256, 0, st>>>(yb, row_of, T, R, D, y);
+  else if (R <= 4) ep_combine4h_kernel<4><<<blocks4, 256, 0, st>>>(yb, row_of, T, R, D, y);
+  else ep_combine4h_kernel<8><<<blocks4, 256, 0, st>>>(yb, row_of, T, R, D, y);
   return cudaGetLastError();
 }
 

@@ -67,6 +67,9 @@ cudaError_t launch_route_gather16(const void* rows, int64_t N, int64_t D, int64_
 // y[t] = sum over d = 0..R-1 of y_back[row_of[t*R+d]] (rows that exist), fixed order.
 cudaError_t launch_ep_combine(const float* y_back, const int32_t* row_of, int64_t T, int R, int64_t D, float* y,
                               cudaStream_t st);
+// launch_ep_combine on f16 returned rows (added in f32, the same rank order).
+cudaError_t launch_ep_combine_f16(const void* y_back16, const int32_t* row_of, int64_t T, int R, int64_t D, float* y,
+                                  cudaStream_t st);
 // Gathers x rows into expert-contiguous slots: xp_f32 and/or xp_f16 (either may be null).
 // xp_f16 rows are in an operand K order (operand_order.cuh, OperandOrder): tc_kpos for
 // the tcgen05 schedule, wm_kpos (D % 128 == 0) for the warp-MMA one, q4k_kpos / q6k_kpos
@@ -91,11 +94,12 @@ cudaError_t launch_to_f16_route(const float* x, int64_t M, int64_t K, void* out,
 // y[t] = sum_r w[t,r] * out[slot_of[t,r]] (rank order, from 0), then
 // y[t] += gate[t] * shared_out[t] when shared_out is given (gate may be null = 1).
 // `out` (and `shared_out`) may hold `splits` partial planes `split_stride`
-// elements apart; the planes are added in order before weighting.
+// elements apart; the planes are added in order before weighting.  y is f32, or f16
+// (y_f16: each sum rounded once; needs D and the strides to be multiples of 4).
 cudaError_t launch_combine(const float* out, int64_t out_ld, int splits, int64_t split_stride,
                            int64_t T, int64_t D, int k, const RouteBuffers& rb,
                            const float* shared_out, int sh_splits, int64_t sh_split_stride,
-                           const float* shared_gate, float* y, cudaStream_t st);
+                           const float* shared_gate, void* y, cudaStream_t st, bool y_f16 = false);
 // y[i] = sum over s of planes[s*plane_stride + i] (in plane order), max(., 0) when relu; y may alias planes.
 cudaError_t launch_sum_planes(const float* planes, int splits, int64_t plane_stride, int64_t n, float* y, bool relu,
                               cudaStream_t st);

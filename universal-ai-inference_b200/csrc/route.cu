@@ -251,10 +251,21 @@ __device__ __forceinline__ float4 sum_planes(const float* base, int64_t off4, in
   return o;
 }
 
+// Four consecutive outputs: f32, or rounded to f16 (expert-parallel return rows).
+__device__ __forceinline__ void store4(float* y, int64_t i4, const float4& v) { reinterpret_cast<float4*>(y)[i4] = v; }
+__device__ __forceinline__ void store4(__half* y, int64_t i4, const float4& v) {
+  const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+  uint2 u;
+  memcpy(&u.x, &a, 4);
+  memcpy(&u.y, &b, 4);
+  reinterpret_cast<uint2*>(y)[i4] = u;
+}
+
+template <typename OT>
 __global__ void combine_kernel(const float* __restrict__ out, int64_t ld, int splits, int64_t stride,
                                int64_t T, int64_t D, int k, RouteBuffers rb, const float* __restrict__ sh,
                                int sh_splits, int64_t sh_stride, const float* __restrict__ gate,
-                               float* __restrict__ y) {
+                               OT* __restrict__ y) {
   const int64_t d4 = D / 4;
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= T * d4) return;
@@ -278,16 +289,16 @@ __global__ void combine_kernel(const float* __restrict__ out, int64_t ld, int sp
     acc.z = __fadd_rn(acc.z, __fmul_rn(g, s.z));
     acc.w = __fadd_rn(acc.w, __fmul_rn(g, s.w));
   }
-  reinterpret_cast<float4*>(y + t * D)[c] = acc;
+  store4(y, t * d4 + c, acc);
 }
 
 // combine_kernel for k <= KMAX: every entry's slot and weight first, then all k
 // row loads in flight together, then the same ordered sum (bit-identical).
-template <int KMAX>
+template <int KMAX, typename OT>
 __global__ void combine_k_kernel(const float* __restrict__ out, int64_t ld, int splits, int64_t stride,
                                  int64_t T, int64_t D, int k, RouteBuffers rb, const float* __restrict__ sh,
                                  int sh_splits, int64_t sh_stride, const float* __restrict__ gate,
-                                 float* __restrict__ y) {
+                                 OT* __restrict__ y) {
   const int64_t d4 = D / 4;
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= T * d4) return;
@@ -324,7 +335,7 @@ __global__ void combine_k_kernel(const float* __restrict__ out, int64_t ld, int 
     acc.z = __fadd_rn(acc.z, __fmul_rn(g, s.z));
     acc.w = __fadd_rn(acc.w, __fmul_rn(g, s.w));
   }
-  reinterpret_cast<float4*>(y + t * D)[c] = acc;
+  store4(y, t * d4 + c, acc);
 }
 
 __global__ void combine1_kernel(const float* __restrict__ out, int64_t ld, int splits, int64_t stride,
@@ -463,32 +474,48 @@ cudaError_t launch_sum_planes(const float* planes, int splits, int64_t plane_str
   return cudaGetLastError();
 }
 
-cudaError_t launch_combine(const float* out, int64_t out_ld, int splits, int64_t split_stride,
-                           int64_t T, int64_t D, int k, const RouteBuffers& rb,
-                           const float* shared_out, int sh_splits, int64_t sh_split_stride,
-                           const float* shared_gate, float* y, cudaStream_t st) {
-  if (T == 0) return cudaSuccess;
-  if (splits < 1) splits = 1;
-  if (sh_splits < 1) sh_splits = 1;
-  if (D % 4 != 0 || out_ld % 4 != 0 || split_stride % 4 != 0 || sh_split_stride % 4 != 0) {
-    combine1_kernel<<<(unsigned)((T * D + 255) / 256), 256, 0, st>>>(out, out_ld, splits, split_stride, T, D, k,
-                                                                     rb, shared_out, sh_splits, sh_split_stride,
-                                                                     shared_gate, y);
-    return cudaGetLastError();
-  }
+namespace {
+template <typename OT>
+cudaError_t combine_vec(const float* out, int64_t out_ld, int splits, int64_t split_stride, int64_t T, int64_t D,
+                        int k, const RouteBuffers& rb, const float* shared_out, int sh_splits, int64_t sh_split_stride,
+                        const float* shared_gate, OT* y, cudaStream_t st) {
   const int64_t n = T * (D / 4);
   const unsigned blocks = (unsigned)((n + 255) / 256);
-#define UAII_COMBINE_K(KM)                                                                                  \
-  combine_k_kernel<KM><<<blocks, 256, 0, st>>>(out, out_ld, splits, split_stride, T, D, k, rb, shared_out, \
-                                               sh_splits, sh_split_stride, shared_gate, y)
+#define UAII_COMBINE_K(KM)                                                                                      \
+  combine_k_kernel<KM, OT><<<blocks, 256, 0, st>>>(out, out_ld, splits, split_stride, T, D, k, rb, shared_out, \
+                                                   sh_splits, sh_split_stride, shared_gate, y)
   if (k <= 2) UAII_COMBINE_K(2);
   else if (k <= 4) UAII_COMBINE_K(4);
   else if (k <= 8) UAII_COMBINE_K(8);
   else
-    combine_kernel<<<blocks, 256, 0, st>>>(out, out_ld, splits, split_stride, T, D, k, rb, shared_out, sh_splits,
-                                           sh_split_stride, shared_gate, y);
+    combine_kernel<OT><<<blocks, 256, 0, st>>>(out, out_ld, splits, split_stride, T, D, k, rb, shared_out,
+                                               sh_splits, sh_split_stride, shared_gate, y);
 #undef UAII_COMBINE_K
   return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_combine(const float* out, int64_t out_ld, int splits, int64_t split_stride,
+                           int64_t T, int64_t D, int k, const RouteBuffers& rb,
+                           const float* shared_out, int sh_splits, int64_t sh_split_stride,
+                           const float* shared_gate, void* y, cudaStream_t st, bool y_f16) {
+  if (T == 0) return cudaSuccess;
+  if (splits < 1) splits = 1;
+  if (sh_splits < 1) sh_splits = 1;
+  const bool vec = D % 4 == 0 && out_ld % 4 == 0 && split_stride % 4 == 0 && sh_split_stride % 4 == 0;
+  if (y_f16) {
+    if (!vec) return cudaErrorInvalidValue;
+    return combine_vec(out, out_ld, splits, split_stride, T, D, k, rb, shared_out, sh_splits, sh_split_stride,
+                       shared_gate, static_cast<__half*>(y), st);
+  }
+  if (!vec) {
+    combine1_kernel<<<(unsigned)((T * D + 255) / 256), 256, 0, st>>>(out, out_ld, splits, split_stride, T, D, k,
+                                                                     rb, shared_out, sh_splits, sh_split_stride,
+                                                                     shared_gate, static_cast<float*>(y));
+    return cudaGetLastError();
+  }
+  return combine_vec(out, out_ld, splits, split_stride, T, D, k, rb, shared_out, sh_splits, sh_split_stride,
+                     shared_gate, static_cast<float*>(y), st);
 }
 
 cudaError_t launch_to_f16(const float* x, int64_t n, void* out, cudaStream_t st, bool wm_order) {

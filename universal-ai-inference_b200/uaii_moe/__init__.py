@@ -111,6 +111,9 @@ def _load():
         "uaii_moe_ep_experts": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                                         c_void_p]),
         "uaii_moe_ep_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p]),
+        "uaii_moe_ep_combine_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p]),
+        "uaii_moe_ep_experts_records_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                                    c_void_p]),
         "uaii_moe_ep_dispatch_records": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p,
                                                  c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
         "uaii_moe_ep_experts_records": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
@@ -151,6 +154,7 @@ EXPORTED = ("uaii_moe_abi_version", "uaii_moe_last_error", "uaii_moe_backend_cre
             "uaii_moe_gguf_tensor", "uaii_moe_gguf_kv_int", "uaii_moe_gguf_kv_float", "uaii_moe_gguf_kv_string",
             "uaii_moe_gguf_moe_layer", "uaii_moe_ep_dispatch", "uaii_moe_ep_experts",
             "uaii_moe_ep_combine", "uaii_moe_ep_dispatch_records", "uaii_moe_ep_experts_records",
+            "uaii_moe_ep_experts_records_f16", "uaii_moe_ep_combine_f16",
             "uaii_moe_selftest_wait_timeout", "uaii_moe_profile_enable",
             "uaii_moe_profile_read",
             "uaii_moe_packed_nbytes", "uaii_moe_quantize_rows",
@@ -320,6 +324,15 @@ class Backend:
     def ep_experts_records(self, layer: Layer, recv_rec, rec_bytes: int, rows: int, entries: int, y_part):
         _check(lib.uaii_moe_ep_experts_records(self._h, ctypes.byref(layer), ptr(recv_rec), rec_bytes, rows, entries,
                                                ptr(y_part)))
+
+    def ep_experts_records_f16(self, layer: Layer, recv_rec, rec_bytes: int, rows: int, entries: int, y_part):
+        """As ep_experts_records with y_part f16 [rows, d_model] (each row's sum rounded once)."""
+        _check(lib.uaii_moe_ep_experts_records_f16(self._h, ctypes.byref(layer), ptr(recv_rec), rec_bytes, rows,
+                                                   entries, ptr(y_part)))
+
+    def ep_combine_f16(self, y_back, row_of, T: int, world: int, d_model: int, y):
+        """As ep_combine with f16 returned rows (added in f32, rank order)."""
+        _check(lib.uaii_moe_ep_combine_f16(self._h, ptr(y_back), ptr(row_of), T, world, d_model, ptr(y)))
 
     def ep_combine(self, y_back, row_of, T: int, world: int, d_model: int, y):
         _check(lib.uaii_moe_ep_combine(self._h, ptr(y_back), ptr(row_of), T, world, d_model, ptr(y)))

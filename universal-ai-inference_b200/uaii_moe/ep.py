@@ -10,9 +10,10 @@ forward is
 2. an all-to-all of the per-destination row and entry counts, then one of the
    rows, each a single record (f16 activations, expert ids, weights);
 3. ``ep_experts`` (device): the grouped expert GEMM over the received rows,
-   producing one f32 row per received row (its weighted expert sum);
+   producing one row per received row (its weighted expert sum), f16 by default
+   (rounded once: half the bytes of the return exchange) or f32;
 4. the reverse all-to-all of those rows;
-5. ``ep_combine`` (device): each token adds its returned rows in rank order.
+5. ``ep_combine`` (device): each token adds its returned rows in rank order, in f32.
 
 The exchange uses ``torch.distributed.all_to_all_single`` (NCCL over NVLink on
 GPUs, gloo for the CPU tests); the device steps go through the library's C ABI.
@@ -51,6 +52,7 @@ class ExpertParallelFFN:
     struct carrying the router weight, d_model, the global expert count, top_k
     and norm_topk; ``local_layer`` carries this rank's experts (n_experts =
     E / world).  ``group`` is the torch.distributed process group (default: world).
+    ``return_f16`` sends the per-rank partial rows back as f16 (default: on CUDA).
 
     ``chunks`` > 1 splits the local tokens: every chunk is dispatched up front
     (one host read of all split sizes), then the exchanges run asynchronously so
@@ -59,7 +61,8 @@ class ExpertParallelFFN:
     """
 
     def __init__(self, backend, router_layer, local_layer, d_model: int, n_experts: int, top_k: int,
-                 rank: int, world: int, group=None, device="cuda", chunks: int = 2, min_chunk: int = 256):
+                 rank: int, world: int, group=None, device="cuda", chunks: int = 2, min_chunk: int = 256,
+                 return_f16: bool | None = None):
         if n_experts % world != 0:
             raise ValueError("the world size must divide the expert count")
         self.be = backend
@@ -70,6 +73,7 @@ class ExpertParallelFFN:
         self.group = group
         self.device = torch.device(device)
         self.chunks, self.min_chunk = max(1, chunks), min_chunk
+        self.return_f16 = self.device.type == "cuda" if return_f16 is None else bool(return_f16)
         self._bufs = {}
         self.last_exchange = None  # (rows sent per rank, rows received per rank, entries received), all chunks
 
@@ -132,10 +136,14 @@ class ExpertParallelFFN:
         for c, ((send_rows, recv_rows, entries), rrec) in enumerate(zip(plans, recv)):
             works[c].wait()
             ns, nr = sum(send_rows), sum(recv_rows)
-            y_part = torch.empty((max(nr, 1), D), dtype=torch.float32, device=dev)
+            rdt = torch.float16 if self.return_f16 else torch.float32
+            y_part = torch.empty((max(nr, 1), D), dtype=rdt, device=dev)
             if nr:
-                self.be.ep_experts_records(self.local_layer, rrec, rb, nr, entries, y_part)
-            y_back = torch.empty((max(ns, 1), D), dtype=torch.float32, device=dev)
+                if self.return_f16:
+                    self.be.ep_experts_records_f16(self.local_layer, rrec, rb, nr, entries, y_part)
+                else:
+                    self.be.ep_experts_records(self.local_layer, rrec, rb, nr, entries, y_part)
+            y_back = torch.empty((max(ns, 1), D), dtype=rdt, device=dev)
             rworks.append(dist.all_to_all_single(y_back[:ns], y_part[:nr], output_split_sizes=send_rows,
                                                  input_split_sizes=recv_rows, group=self.group, async_op=True))
             backs.append(y_back)
@@ -143,5 +151,8 @@ class ExpertParallelFFN:
         for c, b in enumerate(parts):
             rworks[c].wait()
             t0, t1 = bounds[c], bounds[c + 1]
-            self.be.ep_combine(backs[c], b.row_of, t1 - t0, R, D, y[t0:t1])
+            if self.return_f16:
+                self.be.ep_combine_f16(backs[c], b.row_of, t1 - t0, R, D, y[t0:t1])
+            else:
+                self.be.ep_combine(backs[c], b.row_of, t1 - t0, R, D, y[t0:t1])
         return y
