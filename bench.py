@@ -551,25 +551,50 @@ def main():
 
     e2e = None
     if not args.no_e2e:
-        if ep_mode:  # explicit copies: pinned host x in, host y out, on the backend stream
-            x_in = torch.empty_like(x)
-            y_out = torch.empty_like(y)
+        if ep_mode:
+            # explicit copies, pinned host x in and host y out every step, double-buffered across
+            # steps: step i+1's input is copied in (its own stream) while step i computes, and
+            # step i's output is copied out (another stream) while step i+1 computes
+            x_in = [torch.empty_like(x) for _ in range(2)]
+            y_out = [torch.empty_like(y) for _ in range(2)]
+            s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+            ev_in = [torch.cuda.Event() for _ in range(2)]
+            ev_done = [torch.cuda.Event() for _ in range(2)]
+            ev_out = [torch.cuda.Event() for _ in range(2)]
+            for e in ev_done + ev_out:
+                e.record(stream)
 
-            def e2e_step():
-                with torch.cuda.stream(stream):
-                    x_in.copy_(x_host, non_blocking=True)
-                    ep.forward(x_in, y_out)
-                    y_host.copy_(y_out, non_blocking=True)
+            def e2e_run(n):
+                with torch.cuda.stream(s_in):
+                    s_in.wait_event(ev_done[0])
+                    x_in[0].copy_(x_host, non_blocking=True)
+                    ev_in[0].record(s_in)
+                for i in range(n):
+                    b = i % 2
+                    stream.wait_event(ev_in[b])
+                    stream.wait_event(ev_out[b])  # y_out[b] was copied out two steps ago
+                    with torch.cuda.stream(stream):
+                        ep.forward(x_in[b], y_out[b])
+                        ev_done[b].record(stream)
+                    if i + 1 < n:
+                        with torch.cuda.stream(s_in):
+                            s_in.wait_event(ev_done[1 - b])  # x_in[1-b] read by step i-1
+                            x_in[1 - b].copy_(x_host, non_blocking=True)
+                            ev_in[1 - b].record(s_in)
+                    with torch.cuda.stream(s_out):
+                        s_out.wait_event(ev_done[b])
+                        y_host.copy_(y_out[b], non_blocking=True)
+                        ev_out[b].record(s_out)
+                stream.wait_stream(s_out)
         else:
-            def e2e_step():
-                be.ffn(L, x_host, T, y_host)
-        for _ in range(2):
-            e2e_step()
+            def e2e_run(n):
+                for _ in range(n):
+                    be.ffn(L, x_host, T, y_host)
+        e2e_run(2)
         barrier()
         torch.cuda.synchronize()
         ev0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
+        e2e_run(args.steps)
         ev1.record(stream)
         torch.cuda.synchronize()
         barrier()
