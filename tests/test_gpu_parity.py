@@ -522,6 +522,28 @@ def test_quad_tail_split_vs_oracle_and_repeatable(backend, oracle, um, T, I):
     assert bits_equal(ys[0], ys[1]) and bits_equal(ys[0], ys[2])
 
 
+@pytest.mark.parametrize("T,D,E,k", [(1, 4096, 8, 2), (7, 2048, 60, 4), (16, 2048, 128, 8), (3, 1024, 5, 5), (32, 4096, 8, 2)])
+def test_decode_routing_launch_matches_separate_kernels(backend, oracle, um, T, D, E, k):
+    """At decode widths the layer routes in one launch (router, softmax, top-k, slot numbering):
+    its probabilities equal the router kernels' bit for bit, its output meets the layer bar
+    against the oracle (the top-k path included), and repeated calls give the same bits."""
+    I, gf, df = 256, um.Q4_0, um.Q4_0
+    x, w, G, U, Dn = layer_case(um, gf, df, T, D, E, I, k, 1500 + T)
+    L = um.make_layer(D, E, I, k, 1, w, G, gf, U, gf, Dn, df)
+    probs_ffn = np.empty((T, E), np.float32)
+    y = np.empty_like(x)
+    backend.ffn(L, x, T, y, probs_ffn)
+    probs_r, top_r = np.empty((T, E), np.float32), np.empty((T, 1), np.float32)
+    backend.router(x, w, T, D, E, probs_r, top_r)
+    assert bits_equal(probs_ffn, probs_r)
+    _, pr, _ = oracle.router(x, w)
+    y_ref = oracle.experts_packed(x, G, gf, U, gf, Dn, df, pr, E, I, k, 1)[0]
+    assert rel_err(y, y_ref) <= REL_TOL
+    y2 = np.empty_like(x)
+    backend.ffn(L, x, T, y2)
+    assert bits_equal(y, y2)
+
+
 @pytest.mark.parametrize("gf,df", [(14, 16), (14, 14)])
 def test_mixed_schedule_at_16_slot_tiles(backend, oracle, um, gf, df):
     """16-slot tiles of a K-quant layer: gate/up on tcgen05 (operands in tc_kpos order), the down

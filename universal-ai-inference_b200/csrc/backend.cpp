@@ -84,7 +84,8 @@ Error MoeCudaBackend::initialize(int device, cudaStream_t stream) {
   // the quad schedule's tail-split partials and counters (the counters stay zero between launches)
   UAII_CUDA(cudaMalloc(&tail_.part, tail_bytes()), "Malloc(tail split)");
   tail_.cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(tail_.part) + tail_part_bytes());
-  UAII_CUDA(cudaMemset(tail_.cnt, 0, sizeof(int) * kTailMaxUnits), "Memset(tail split)");
+  route_done_ = tail_.cnt + kTailMaxUnits;
+  UAII_CUDA(cudaMemset(tail_.cnt, 0, sizeof(int) * (kTailMaxUnits + 16)), "Memset(tail split)");
   if (stream == nullptr) {
     UAII_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "StreamCreate");
     own_stream_ = true;
@@ -140,6 +141,7 @@ void MoeCudaBackend::shutdown() noexcept {
   dev_err_ = nullptr;
   if (tail_.part) (void)cudaFree(tail_.part);
   tail_ = TailSplit{};
+  route_done_ = nullptr;
   for (auto e : chunk_events_) (void)cudaEventDestroy(e);
   chunk_events_.clear();
   if (in_stream_) (void)cudaStreamDestroy(in_stream_);
@@ -163,7 +165,7 @@ Error MoeCudaBackend::sync_and_check() {
   UAII_CUDA(cudaMemcpy(&code, dev_err_, sizeof(int), cudaMemcpyDeviceToHost), "Memcpy(error flag)");
   if (code != 0) {
     (void)cudaMemset(dev_err_, 0, sizeof(int));
-    if (tail_.cnt) (void)cudaMemset(tail_.cnt, 0, sizeof(int) * kTailMaxUnits);  // a kernel may have stopped mid-tile
+    if (tail_.cnt) (void)cudaMemset(tail_.cnt, 0, sizeof(int) * (kTailMaxUnits + 16));  // a kernel may have stopped mid-tile
     return Error::make(ErrorCode::Internal,
                        "tensor-core expert kernel gave up waiting (code " + std::to_string(code) + ")");
   }
@@ -630,7 +632,8 @@ Error MoeCudaBackend::umma_rows(const void* w, int fmt, int64_t rows, int64_t K,
 }
 
 Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const float* probs_for_w,
-                                  const LayerArgs& L, const ExpertPlan& P, int64_t T, void* yd, const EpRows* ep) {
+                                  const LayerArgs& L, const ExpertPlan& P, int64_t T, void* yd, const EpRows* ep,
+                                  const DecodeRoute* dr) {
   last_plan_ = P;
   if (ep && !P.umma)
     return Error::make(ErrorCode::NotImplemented,
@@ -662,12 +665,19 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
   float* out = nullptr;
   int splits = 1;
   phase_begin(kRoute);
-  if (ep) {
-    UAII_CUDA(launch_ep_route(ep->ids, ep->w, T, E, k, rb, stream_, ep->e_pitch), "ep_route");
+  if (dr) {  // router, softmax, top-k and slot numbering in one launch
+    UAII_CUDA(launch_route_decode(xd, dr->router_w, T, D, E, k, L.norm_topk, dr->logits, dr->probs, rb, route_done_,
+                                  stream_),
+              "route_decode");
+    count_launches(1);
   } else {
-    UAII_CUDA(launch_route_topk(scores, probs_for_w, T, E, k, L.norm_topk, rb, stream_), "route_topk");
+    if (ep) {
+      UAII_CUDA(launch_ep_route(ep->ids, ep->w, T, E, k, rb, stream_, ep->e_pitch), "ep_route");
+    } else {
+      UAII_CUDA(launch_route_topk(scores, probs_for_w, T, E, k, L.norm_topk, rb, stream_), "route_topk");
+    }
+    UAII_CUDA(launch_route_scan(T, E, k, rb, stream_), "route_scan");
   }
-  UAII_CUDA(launch_route_scan(T, E, k, rb, stream_), "route_scan");
   if (P.umma) {
     // operand orders: x in the gate/up kernel's, h in the down kernel's (operand_order.cuh)
     const int sched = P.quad_mma ? kSchedQuadMma : P.warp_mma ? kSchedWarpMma : kSchedTcgen05;
@@ -1113,6 +1123,10 @@ void MoeCudaBackend::drop_graphs() {
 // The launches of one layer forward (router, routing, expert GEMMs, combine).
 Error MoeCudaBackend::ffn_launch(const LayerArgs& L, const ExpertPlan& P, int64_t T, const float* xd, const float* wd,
                                  float* logits, float* po, float* rscratch, size_t rsb, float* yo) {
+  if (route_done_ != nullptr && route_decode_supported(T, L.D, L.E, L.top_k)) {  // one routing launch
+    const DecodeRoute dr{wd, logits, po};
+    return run_experts(xd, logits, po, L, P, T, yo, nullptr, &dr);
+  }
   phase_begin(kRouter);
   UAII_CUDA(launch_router(xd, wd, T, L.D, L.E, logits, po, nullptr, stream_, rscratch, rsb), "router");
   phase_end();

@@ -185,9 +185,16 @@ class MoeCudaBackend {
     int64_t x_pitch, e_pitch;  // 0 = dense
     bool y_f16;                // the per-row sums written as f16
   };
+  // Decode widths: the router runs inside the routing step (launch_route_decode), writing the
+  // logits and probabilities here.
+  struct DecodeRoute {
+    const float* router_w;
+    float* logits;
+    float* probs;
+  };
   Error run_experts(const float* x_dev, const float* scores, const float* probs_for_w,
                     const LayerArgs& L, const ExpertPlan& P, int64_t T, void* y_dev,
-                    const EpRows* ep = nullptr);
+                    const EpRows* ep = nullptr, const DecodeRoute* dr = nullptr);
   Error sync_and_check();
   // Packed rows as the tensor-core path reads them (16-byte pitch).  `constant`: the
   // source is a registered buffer, so a padded copy is made once and kept.
@@ -231,7 +238,8 @@ class MoeCudaBackend {
   int* dev_err_ = nullptr;
   TailSplit tail_{};  // quad schedule tail split (null in external mode: no split)
   static size_t tail_part_bytes() { return sizeof(float) * (size_t)kTailMaxUnits * 128 * kTailMaxBn; }
-  static size_t tail_bytes() { return tail_part_bytes() + sizeof(int) * (size_t)kTailMaxUnits; }
+  static size_t tail_bytes() { return tail_part_bytes() + sizeof(int) * (size_t)(kTailMaxUnits + 16); }
+  int* route_done_ = nullptr;  // launch_route_decode's counter (after the tail-split counters)
   bool external_ = false;  // workspace and error flag belong to the caller
   char* ws_ = nullptr;
   size_t ws_cap_ = 0;

@@ -33,6 +33,15 @@ struct RouteBuffers {
 // `scores` [T,E] rank the experts in the order of the reference's
 // std::partial_sort (value descending, ties as the reference orders them); the
 // routing weights are taken from `probs` [T,E] (which may be the same array).
+// Decode widths: router + softmax + top-k + the per-expert slot numbering of tokens in ONE
+// launch (T <= kDecodeRouteMaxT): logits, probs [T, E]; rb.topk_ids / topk_w / slot_local /
+// counts as launch_route_topk + launch_route_scan leave them (rb.mask is not written).  `done`:
+// one int, zero before the first launch (every launch leaves it zero).  cudaErrorNotSupported
+// when the shapes do not fit (the caller then runs the separate kernels).
+constexpr int64_t kDecodeRouteMaxT = 32;
+bool route_decode_supported(int64_t T, int64_t D, int64_t E, int k);
+cudaError_t launch_route_decode(const float* x, const float* w, int64_t T, int64_t D, int64_t E, int k, int norm_topk,
+                                float* logits, float* probs, const RouteBuffers& rb, int* done, cudaStream_t st);
 cudaError_t launch_route_topk(const float* scores, const float* probs, int64_t T, int64_t E,
                               int k, int norm_topk, const RouteBuffers& rb, cudaStream_t st);
 // offsets = {0, T}, counts = {T} in buf[0..2]: one expert that owns every token.

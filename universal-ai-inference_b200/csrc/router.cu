@@ -19,6 +19,7 @@
 // multiply by 1/sum; exp is evaluated in double and rounded once to f32.
 // top_expert is the first strict argmax of probs, stored as an f32 id.
 #include "kernels.hpp"
+#include "topk.cuh"
 
 namespace uaii_b200 {
 namespace {
@@ -285,18 +286,13 @@ __global__ void router_fold_kernel(const float* __restrict__ partials, int64_t n
   logits[i] = c;
 }
 
-// Small batches: one block per token, thread (tile j, expert e) builds one
-// partial from x staged in shared memory; thread e then adds its partials in
-// tile order.
-__global__ void __launch_bounds__(1024) router_token_kernel(const float* __restrict__ x,
-                                                            const float* __restrict__ w, int64_t D,
-                                                            int64_t E, float* __restrict__ logits) {
-  extern __shared__ float sm[];
+// One block, one token: thread (tile j, expert e) builds one partial from x staged in shared
+// memory (xs [D]); thread e then adds its partials (part [E][nkt]) in tile order.  The logits go
+// to out[e] (global or shared).
+__device__ __forceinline__ void token_logits(const float* __restrict__ xrow, const float* __restrict__ w, int64_t D,
+                                             int64_t E, float* xs, float* part, float* out) {
   const int nkt = (int)((D + kTile - 1) / kTile);
-  float* xs = sm;               // [D]
-  float* part = sm + D;         // [E][nkt]
-  const int64_t t = blockIdx.x;
-  for (int64_t k = threadIdx.x; k < D; k += blockDim.x) xs[k] = __ldg(x + t * D + k);
+  for (int64_t k = threadIdx.x; k < D; k += blockDim.x) xs[k] = __ldg(xrow + k);
   __syncthreads();
   for (int64_t p = threadIdx.x; p < E * nkt; p += blockDim.x) {
     const int64_t e = p % E, j = p / E;
@@ -325,8 +321,17 @@ __global__ void __launch_bounds__(1024) router_token_kernel(const float* __restr
   for (int64_t e = threadIdx.x; e < E; e += blockDim.x) {
     float acc = 0.f;
     for (int j = 0; j < nkt; ++j) acc = __fadd_rn(acc, __fmul_rn(1.0f, part[e * nkt + j]));
-    logits[t * E + e] = acc;
+    out[e] = acc;
   }
+}
+
+// Small batches: one block per token (token_logits).
+__global__ void __launch_bounds__(1024) router_token_kernel(const float* __restrict__ x,
+                                                            const float* __restrict__ w, int64_t D,
+                                                            int64_t E, float* __restrict__ logits) {
+  extern __shared__ float sm[];
+  const int64_t t = blockIdx.x;
+  token_logits(x + t * D, w, D, E, sm, sm + D, logits + t * E);
 }
 
 // 16 tokens x 64 experts per block, 256 threads, each 2 tokens x 2 experts.
@@ -384,14 +389,12 @@ __global__ void __launch_bounds__(256) router_tiled_kernel(const float* __restri
 // reference's order (index 0 up, one rounding per add), so one lane adds the
 // warp's staged exponentials in sequence.  `top` = first index of the largest
 // probability.
-__global__ void softmax_top_kernel(const float* __restrict__ logits, int64_t T, int64_t E,
-                                   float* __restrict__ probs, float* __restrict__ top) {
-  extern __shared__ float sv_all[];  // [8][E]
-  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-  float* sv = sv_all + (int64_t)wib * E;
-  for (int64_t t = blockIdx.x * 8 + wib; t < T; t += (int64_t)gridDim.x * 8) {
-    const float* l = logits + t * E;
-    float* p = probs + t * E;
+// One warp, one token: p[e] = softmax of l (max-subtract, exp in double rounded to f32, the
+// denominator summed in index order on one lane, multiply by 1 / sum), sv [E] scratch; returns
+// the first index of the largest probability on every lane.
+__device__ __forceinline__ int warp_softmax(const float* __restrict__ l, int64_t E, float* __restrict__ p, float* sv,
+                                            int lane) {
+  {
     float mx = -__int_as_float(0x7f800000);
     for (int64_t e = lane; e < E; e += 32) mx = (mx < l[e]) ? l[e] : mx;
 #pragma unroll
@@ -419,6 +422,77 @@ __global__ void softmax_top_kernel(const float* __restrict__ logits, int64_t T, 
       const int oe = __shfl_xor_sync(0xffffffffu, best, o);
       if (oe >= 0 && (best < 0 || ov > bp || (ov == bp && oe < best))) { bp = ov; best = oe; }
     }
+    return best;
+  }
+}
+
+// Decode widths (T <= kDecodeRouteMaxT): router (token_logits), softmax (warp_softmax) and the
+// reference top-k (warp_topk on the logits, weights from the probabilities, renormalised) of
+// token t in block t, then the stable per-expert slot numbering of route_scan_kernel by the
+// block that finishes last (a counter in `done`, zero between launches; no block waits on
+// another).  One launch instead of the router, the softmax, the mask clear, the top-k and the
+// scan.
+__global__ void __launch_bounds__(1024) route_decode_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                            int64_t T, int64_t D, int64_t E, int k, int norm_topk,
+                                                            float* __restrict__ logits, float* __restrict__ probs,
+                                                            RouteBuffers rb, int* done) {
+  extern __shared__ float sm[];
+  const int nkt = (int)((D + kTile - 1) / kTile);
+  float* xs = sm;                // [D]
+  float* part = xs + D;          // [E][nkt]
+  float* lg = part + E * nkt;    // [E] logits of this token
+  float* sv = lg + E;            // [E] softmax scratch
+  Pair* h = reinterpret_cast<Pair*>(sv + E);  // [33]
+  const int64_t t = blockIdx.x;
+  token_logits(x + t * D, w, D, E, xs, part, lg);
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x < 32) {
+    for (int64_t e = lane; e < E; e += 32) logits[t * E + e] = lg[e];
+    (void)warp_softmax(lg, E, probs + t * E, sv, lane);
+    warp_topk(lg, E, k, h, lane);
+    if (lane == 0) {
+      float ps[32];
+      for (int r = 0; r < k; ++r) ps[r] = probs[t * E + h[r].e];
+      float mass = 0.0f;
+      for (int r = 0; r < k; ++r) mass = __fadd_rn(mass, ps[r]);
+      if (!(mass > 0.0f)) mass = 1.0f;
+      for (int r = 0; r < k; ++r) {
+        rb.topk_ids[t * k + r] = h[r].e;
+        rb.topk_w[t * k + r] = norm_topk ? __fdiv_rn(ps[r], mass) : ps[r];
+      }
+      __threadfence();
+    }
+  }
+  __shared__ int last;
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(done, 1) == (int)T - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const int64_t S = T * k;
+  for (int64_t s = threadIdx.x; s < S; s += blockDim.x) {  // earlier tokens' slots with the same expert
+    const int e = __ldcg(rb.topk_ids + s);
+    const int64_t first = (s / k) * k;
+    int before = 0;
+    for (int64_t s2 = 0; s2 < first; ++s2) before += __ldcg(rb.topk_ids + s2) == e;
+    rb.slot_local[s] = before;
+  }
+  for (int64_t e = threadIdx.x; e < E; e += blockDim.x) {
+    int c = 0;
+    for (int64_t s2 = 0; s2 < S; ++s2) c += __ldcg(rb.topk_ids + s2) == (int)e;
+    rb.counts[e] = c;
+  }
+  if (threadIdx.x == 0) *done = 0;  // ready for the next launch
+}
+
+__global__ void softmax_top_kernel(const float* __restrict__ logits, int64_t T, int64_t E,
+                                   float* __restrict__ probs, float* __restrict__ top) {
+  extern __shared__ float sv_all[];  // [8][E]
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  float* sv = sv_all + (int64_t)wib * E;
+  for (int64_t t = blockIdx.x * 8 + wib; t < T; t += (int64_t)gridDim.x * 8) {
+    const int best = warp_softmax(logits + t * E, E, probs + t * E, sv, lane);
     if (top && lane == 0) top[t] = (float)best;
     __syncwarp();  // sv is rewritten for the next token
   }
@@ -545,6 +619,33 @@ cudaError_t launch_router(const float* x, const float* w, int64_t T, int64_t D, 
     if (err != cudaSuccess) return err;
   }
   softmax_top_kernel<<<(unsigned)blocks, 256, smem, st>>>(logits, T, E, probs, top);
+  return cudaGetLastError();
+}
+
+namespace {
+size_t route_decode_smem(int64_t D, int64_t E) {
+  const int64_t nkt = (D + kTile - 1) / kTile;
+  return sizeof(float) * (size_t)(D + E * nkt + 2 * E) + 33 * sizeof(Pair);
+}
+}  // namespace
+
+bool route_decode_supported(int64_t T, int64_t D, int64_t E, int k) {
+  return T >= 1 && T <= kDecodeRouteMaxT && D >= 1 && E >= 1 && E <= 1024 && k >= 1 && k <= 32 && k <= E &&
+         route_decode_smem(D, E) <= 200 * 1024;
+}
+
+cudaError_t launch_route_decode(const float* x, const float* w, int64_t T, int64_t D, int64_t E, int k, int norm_topk,
+                                float* logits, float* probs, const RouteBuffers& rb, int* done, cudaStream_t st) {
+  const size_t smem = route_decode_smem(D, E);
+  if (!route_decode_supported(T, D, E, k) || done == nullptr) return cudaErrorNotSupported;
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(route_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  route_decode_kernel<<<(unsigned)T, 1024, smem, st>>>(x, w, T, D, E, k, norm_topk, logits, probs, rb, done);
   return cudaGetLastError();
 }
 
