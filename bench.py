@@ -67,7 +67,8 @@ def parse():
                     help="weak: --tokens per GPU; strong: --tokens in total, split across the GPUs")
     ap.add_argument("--path", type=int, default=0,
                     help="0 auto, 1 CUDA-core GEMV, 2 tcgen05 tensor-core GEMM, 3 warp-MMA tensor-core GEMM "
-                         "(whole super-blocks for K-quants), 4 warp-MMA with one 32-element unit per lane")
+                         "(whole super-blocks for K-quants), 4 warp-MMA with one 32-element unit per lane, "
+                         "5 auto with the Q4_K quad gate/up on f16 instead of 16-bit integer activations")
     ap.add_argument("--ep-chunks", type=int, default=1,
                     help="N > 1: token chunks whose exchanges overlap the previous chunk's experts")
     ap.add_argument("--no-graphs", action="store_true", help="plain launches instead of CUDA-graph replay")
@@ -630,9 +631,12 @@ def main():
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["traffic"] = NCU_TRAFFIC.get((workload, dom))
     sched = {"tcgen05": "tcgen05", "warp_mma": "warp-level mma.sync m16n8k16",
-             "quad_mma": "warp-level mma.sync m16n8k16 over whole K-quant super-blocks"}.get(plan.get("schedule"),
-                                                                                           "tcgen05")
-    path = (f"tensor-core grouped dequant-GEMM ({sched}, f16 operands, f32 accumulate), "
+             "quad_mma": "warp-level mma.sync m16n8k16 over whole K-quant super-blocks",
+             "quad_mma_i8": "warp-level mma.sync over whole K-quant super-blocks"}.get(plan.get("schedule"), "tcgen05")
+    operands = ("gate/up: m16n8k32 int8 on Q4_K nibbles x 16-bit integer activations (two byte planes), exact "
+                "int32 per sub-block; down: m16n8k16 f16 operands, f32 accumulate"
+                if plan.get("schedule") == "quad_mma_i8" else "f16 operands, f32 accumulate")
+    path = (f"tensor-core grouped dequant-GEMM ({sched}, {operands}), "
             f"{plan['slot_tile']}-slot tiles") if plan["tensor_cores"] else "CUDA-core f32 grouped GEMV"
     roof["kernel"] = f"{dom} phase: {path}"
     roof["peak_src"] = f"{peaks['src']} ({'hbm_gbs' if roof['bound'] == 'hbm' else 'bf16_tflops burst'})"
@@ -653,8 +657,12 @@ def main():
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
                 "scaling": args.scaling, "vs_baseline": None, "dtype": "f16" if plan["tensor_cores"] else "f32",
-                "dtype_note": "GGUF blocks dequantized to f16 tensor-core operands, f32 accumulation; router, "
-                              "softmax and combine in f32" if plan["tensor_cores"] else "f32 throughout",
+                "dtype_note": ("Q4_K gate/up: raw nibbles (int8) x activations quantized per 256 elements to 16-bit "
+                               "integers, exact int32 sub-block sums, f32 scale; down: GGUF blocks dequantized to f16 "
+                               "tensor-core operands, f32 accumulation; router, softmax and combine in f32"
+                               if plan.get("schedule") == "quad_mma_i8" else
+                               "GGUF blocks dequantized to f16 tensor-core operands, f32 accumulation; router, "
+                               "softmax and combine in f32") if plan["tensor_cores"] else "f32 throughout",
                 "data": "synthetic (seeded random-init GGUF layer, N(0,1) activations)",
                 "config": {"workload": workload, "note": WORKLOAD_NOTE.get(args.config, ""),
                            "tokens_per_gpu": T,

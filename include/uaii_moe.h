@@ -320,8 +320,10 @@ UAII_MOE_API int uaii_moe_release_weights(uaii_moe_backend* b, const void* host_
  * qualifies: the warp-MMA schedule at <= 16 routed slots per expert, tcgen05
  * above), 1 = CUDA-core f32 GEMV, 2 = tensor cores on the tcgen05 schedule only,
  * 3 = tensor cores on the warp-MMA (mma.sync) schedule for every slot count
- * (d_model and d_ff multiples of 128; expert-parallel rows stay on tcgen05).
- * No reference counterpart. */
+ * (d_model and d_ff multiples of 128; expert-parallel rows stay on tcgen05),
+ * 4 = as 3 with the per-32-element warp schedule for K-quants too,
+ * 5 = automatic, with the Q4_K gate/up of 8-slot tiles on f16 activations instead
+ * of 16-bit integer ones.  No reference counterpart. */
 UAII_MOE_API int uaii_moe_set_expert_path(uaii_moe_backend* b, int path);
 
 /* ---- Expert parallelism (one process per GPU, R ranks, rank r owns experts
@@ -393,7 +395,9 @@ UAII_MOE_API int uaii_moe_selftest_wait_timeout(uaii_moe_backend* b, int64_t bud
 
 /* Schedule of the most recent expert-product call on this backend (routed
  * experts): *tensor_cores = 1 for the tcgen05 grouped GEMM, 2 for the warp-MMA
- * one, 0 for the CUDA-core GEMV; *slot_tile = routed slots per tile (MMA N);
+ * one, 3 for the warp-MMA over whole K-quant super-blocks (quad schedule), 4 for the
+ * quad schedule with its Q4_K gate/up on 16-bit integer activations (int8 mma.sync),
+ * 0 for the CUDA-core GEMV; *slot_tile = routed slots per tile (MMA N);
  * *down_splits = K splits of the down projection.  Any pointer may be NULL.
  * Diagnostic; no reference counterpart. */
 UAII_MOE_API int uaii_moe_last_plan(uaii_moe_backend* b, int* tensor_cores, int* slot_tile, int* down_splits);

@@ -457,7 +457,8 @@ def test_warp_mma_path_vs_oracle(backend, oracle, um, gf, df, T, D, E, I, k):
     finally:
         backend.set_expert_path(0)
     kquant = gf in (14, 16) and df in (14, 16)
-    assert plan["schedule"] == ("quad_mma" if kquant else "warp_mma") and plan["slot_tile"] in (8, 16)
+    quad = ("quad_mma_i8" if gf == 14 and plan["slot_tile"] == 8 else "quad_mma") if kquant else "warp_mma"
+    assert plan["schedule"] == quad and plan["slot_tile"] in (8, 16)
     assert rel_err(y, y_ref) <= REL_TOL
 
 
@@ -488,7 +489,9 @@ def test_quad_schedule_vs_oracle_and_unit_schedule(backend, oracle, um, gf, df, 
             ys[path] = (y, backend.last_plan())
         finally:
             backend.set_expert_path(0)
-    assert ys[3][1]["schedule"] == "quad_mma" and ys[4][1]["schedule"] == "warp_mma"
+    # Q4_K gate/up at 8-slot tiles runs on 16-bit integer activations (test_quad_integer_activations_vs_oracle)
+    i8 = gf == 14 and ys[3][1]["slot_tile"] == 8
+    assert ys[3][1]["schedule"] == ("quad_mma_i8" if i8 else "quad_mma") and ys[4][1]["schedule"] == "warp_mma"
     err_quad, err_unit = rel_err(ys[3][0], y_ref), rel_err(ys[4][0], y_ref)
     assert err_quad <= REL_TOL
     # no less accurate than the per-unit schedule (Q4_K: more accurate, its weights are unrounded)
@@ -497,29 +500,68 @@ def test_quad_schedule_vs_oracle_and_unit_schedule(backend, oracle, um, gf, df, 
         assert rel_err(ys[3][0], ys[4][0]) <= 1e-4
 
 
-@pytest.mark.parametrize("T,I", [(1, 1024), (2, 1024)])
-def test_quad_tail_split_vs_oracle_and_repeatable(backend, oracle, um, T, I):
+@pytest.mark.parametrize("T,I,path", [(1, 1024, 0), (2, 1024, 0), (1, 1024, 5), (2, 1024, 5)])
+def test_quad_tail_split_vs_oracle_and_repeatable(backend, oracle, um, T, I, path):
     """Gate/up tiles of a last wave that fills at most half of the GPU are cut into K ranges
     run by different CTAs (2 experts x I/64 tiles here, all in one partial wave); the CTA that
     finishes a tile's last range adds the ranges in order.  Against the oracle, and
-    bit-identical over repeated calls (the per-tile counters are left at zero)."""
+    bit-identical over repeated calls (the per-tile counters are left at zero); on integer
+    (path 0) and f16 (path 5) activations."""
     gf, df, D, E, k = 14, 16, 4096, 8, 2
     x, w, G, U, Dn = layer_case(um, gf, df, T, D, E, I, k, 900 + T)
     _, pr, _ = oracle.router(x, w)
     y_ref, _, _ = oracle.experts_packed(x, G, gf, U, gf, Dn, df, pr, E, I, k, 1)
     L = um.make_layer(D, E, I, k, 1, w, G, gf, U, gf, Dn, df)
     backend.set_graphs(False)
+    backend.set_expert_path(path)
     try:
         ys = []
         for _ in range(3):
             y = np.empty_like(x)
             backend.ffn(L, x, T, y)
             ys.append(y)
-        assert backend.last_plan()["schedule"] == "quad_mma"
+        assert backend.last_plan()["schedule"] == ("quad_mma_i8" if path == 0 else "quad_mma")
     finally:
+        backend.set_expert_path(0)
         backend.set_graphs(True)
     assert rel_err(ys[0], y_ref) <= REL_TOL
     assert bits_equal(ys[0], ys[1]) and bits_equal(ys[0], ys[2])
+
+
+@pytest.mark.parametrize("T,D,I,case", [(1, 4096, 1024, "normal"), (5, 4096, 2048, "normal"), (8, 1024, 1024, "normal"),
+                                        (16, 4096, 1024, "normal"), (8, 1024, 512, "outliers"),
+                                        (8, 1024, 512, "zero_quads"), (3, 256, 256, "normal")])
+def test_quad_integer_activations_vs_oracle(backend, oracle, um, T, D, I, case):
+    """The Q4_K quad gate/up on 16-bit integer activations (int8 mma.sync over the raw nibbles,
+    exact int32 sub-block sums): against the oracle at the layer bar, and no further from it
+    than twice the f16-activation path's error (plus 1e-5).  Cases: N(0,1) activations; an
+    outlier 100 times the rest in every quad (it sets the scale of the other 255; far larger ones
+    overflow the f16 hidden activations of either path);
+    whole quads and a whole row of zeros (zero scale)."""
+    gf, df, E, k = 14, 16, 8, 2
+    x, w, G, U, Dn = layer_case(um, gf, df, T, D, E, I, k, 2100 + T + D)
+    if case == "outliers":
+        x[:, ::256] *= 100.0
+    elif case == "zero_quads":
+        x[:, 256:512] = 0.0
+        x[T // 2, :] = 0.0
+    x = np.ascontiguousarray(x, np.float32)
+    _, pr, _ = oracle.router(x, w)
+    y_ref, _, _ = oracle.experts_packed(x, G, gf, U, gf, Dn, df, pr, E, I, k, 1)
+    L = um.make_layer(D, E, I, k, 1, w, G, gf, U, gf, Dn, df)
+    ys = {}
+    try:
+        for path in (0, 5):
+            backend.set_expert_path(path)
+            y = np.empty_like(x)
+            backend.ffn(L, x, T, y)
+            ys[path] = (y, backend.last_plan()["schedule"])
+    finally:
+        backend.set_expert_path(0)
+    assert ys[0][1] == "quad_mma_i8" and ys[5][1] == "quad_mma"
+    e_i8, e_f16 = rel_err(ys[0][0], y_ref), rel_err(ys[5][0], y_ref)
+    assert e_i8 <= REL_TOL, (e_i8, e_f16)
+    assert e_i8 <= 2 * e_f16 + 1e-5, (e_i8, e_f16)
 
 
 @pytest.mark.parametrize("T,D,E,k", [(1, 4096, 8, 2), (7, 2048, 60, 4), (16, 2048, 128, 8), (3, 1024, 5, 5), (32, 4096, 8, 2)])
@@ -570,7 +612,7 @@ def test_mixed_schedule_at_16_slot_tiles(backend, oracle, um, gf, df):
 def test_automatic_schedule_picks_warp_mma_for_decode(backend, um):
     D, E, I, k = 1024, 8, 2048, 2
     # tiles hold the mean slots per expert plus two standard deviations below 32 slots
-    for T, sched, tile in ((1, "quad_mma", 8), (8, "quad_mma", 8), (32, "tcgen05", 16), (64, "tcgen05", 32),
+    for T, sched, tile in ((1, "quad_mma_i8", 8), (8, "quad_mma_i8", 8), (32, "tcgen05", 16), (64, "tcgen05", 32),
                            (512, "tcgen05", 128)):
         x, w, G, U, Dn = layer_case(um, 14, 16, T, D, E, I, k, 5)
         y = np.empty_like(x)

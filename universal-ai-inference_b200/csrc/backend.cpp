@@ -568,6 +568,8 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t s
     if (p.warp_mma) p.bn = warp_bn(tpe);
     // K-quant layers run the warp schedule over whole super-blocks (path 4 keeps the per-unit one)
     p.quad_mma = p.warp_mma && path_ != 4 && quad_mma_format(L.gate.fmt) && quad_mma_format(L.down.fmt);
+    // Q4_K gate/up at 8-slot tiles: integer activations (path 5 keeps the f16 ones)
+    p.quad_i8 = p.quad_mma && !f16_quad_ && L.gate.fmt == kQ4_K && L.up.fmt == kQ4_K && p.bn == 8;
     // 16-slot tiles: the down projection is faster on the quad schedule, gate/up on tcgen05
     // (Mixtral-shaped layer, 32 tokens: down 0.160 -> 0.121 ms; gate/up 0.191 vs 0.247 ms)
     p.down_quad = !p.warp_mma && path_ == 0 && warp_ok && p.bn == 16 && quad_mma_format(L.gate.fmt) &&
@@ -682,13 +684,17 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
     // operand orders: x in the gate/up kernel's, h in the down kernel's (operand_order.cuh)
     const int sched = P.quad_mma ? kSchedQuadMma : P.warp_mma ? kSchedWarpMma : kSchedTcgen05;
     const int dn_sched = P.down_quad ? kSchedQuadMma : sched;
-    const int x_order = P.quad_mma ? (L.gate.fmt == kQ4_K ? kOrderQ4K : kOrderQ6K) : P.warp_mma ? kOrderWm : kOrderTc;
+    const int x_order = P.quad_i8    ? kOrderQ4KI8
+                        : P.quad_mma ? (L.gate.fmt == kQ4_K ? kOrderQ4K : kOrderQ6K)
+                        : P.warp_mma ? kOrderWm
+                                     : kOrderTc;
     const int h_order = dn_sched == kSchedQuadMma ? (L.down.fmt == kQ4_K ? kOrderQ4K : kOrderQ6K)
                         : P.warp_mma                ? kOrderWm
                                                     : kOrderTc;
     void* xp16 = carve(2 * (size_t)(S * D));
     void* h16 = carve(2 * (size_t)(S * I));
-    void* xsum = nullptr;  // Q4_K on the quad schedule: the activations' sub-block sums
+    void* xsum = nullptr;    // Q4_K on the quad schedule: the activations' sub-block sums
+    float* xscale = nullptr;  // ... and with integer activations their dequant scales
     splits = P.splits;
     out = static_cast<float*>(carve(sizeof(float) * (size_t)(splits * S * D)));
     if (ep) {  // rows arrive in the tcgen05 operand order
@@ -703,7 +709,9 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
       tt.dn_mtiles = (int)(D / 128);
       tt.dn_splits = std::min(splits, umma_kchunks(L.down.fmt, I));
       if (P.quad_mma && L.gate.fmt == kQ4_K) tt.xsum = carve(2 * (size_t)(S * (D / 256) * 16));
+      if (P.quad_i8) tt.xscale = static_cast<float*>(carve(sizeof(float) * (size_t)(S * (D / 256))));
       xsum = tt.xsum;
+      xscale = tt.xscale;
       UAII_CUDA(launch_route_gather(xd, T, D, E, k, rb, nullptr, xp16, stream_, x_order, &tt), "route_gather");
     }
     const bool tables = ep == nullptr;
@@ -716,7 +724,7 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
     UAII_TRY(umma_rows(dd, L.down.fmt, E * D, I, weight_is_constant(L.down.data, expert_bytes(L.down, E)), &dd,
                        &dpitch));
     UAII_CUDA(launch_gateup_umma(L.gate.fmt, gd, ud, gpitch, E, I, D, xp16, S, rb.counts, rb.offsets, tile_base, P.bn,
-                                 h16, dev_err_, stream_, sched, h_order, tables, xsum, &tail_),
+                                 h16, dev_err_, stream_, sched, h_order, tables, xsum, &tail_, xscale),
               "gateup(tensor cores)");
     phase_end();
     phase_begin(kDown);
@@ -1769,7 +1777,7 @@ int uaii_moe_selftest_wait_timeout(uaii_moe_backend* b, int64_t budget_cycles) {
 int uaii_moe_last_plan(uaii_moe_backend* b, int* tensor_cores, int* slot_tile, int* down_splits) {
   if (!b) return no_backend();
   const uaii_b200::ExpertPlan P = b->impl.last_plan();
-  if (tensor_cores) *tensor_cores = P.umma ? (P.quad_mma ? 3 : P.warp_mma ? 2 : 1) : 0;
+  if (tensor_cores) *tensor_cores = P.umma ? (P.quad_i8 ? 4 : P.quad_mma ? 3 : P.warp_mma ? 2 : 1) : 0;
   if (slot_tile) *slot_tile = P.bn;
   if (down_splits) *down_splits = P.splits;
   return report(Error::success());
@@ -1777,7 +1785,7 @@ int uaii_moe_last_plan(uaii_moe_backend* b, int* tensor_cores, int* slot_tile, i
 
 int uaii_moe_set_expert_path(uaii_moe_backend* b, int path) {
   if (!b) return no_backend();
-  if (path < 0 || path > 4) return report(Error::make(ErrorCode::InvalidArgument, "path must be 0, 1, 2, 3 or 4"));
+  if (path < 0 || path > 5) return report(Error::make(ErrorCode::InvalidArgument, "path must be 0 .. 5"));
   b->impl.set_expert_path(path);
   return report(Error::success());
 }

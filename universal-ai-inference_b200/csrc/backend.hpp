@@ -88,6 +88,7 @@ struct ExpertPlan {
   bool warp_mma = false;      // ... on an mma.sync schedule (decode widths), else tcgen05
   bool quad_mma = false;      // ... the mma.sync schedule over whole K-quant super-blocks
   bool down_quad = false;     // the down projection alone on the quad schedule (16-slot tiles, gate/up on tcgen05)
+  bool quad_i8 = false;       // quad gate/up (Q4_K, 8-slot tiles) on 16-bit integer activations, int8 mma.sync
   bool umma_refused = false;  // tensor cores forced but the layer does not qualify
   int bn = 16;         // slots per tile (MMA N)
   int splits = 1;      // K splits of the down projection
@@ -144,8 +145,10 @@ class MoeCudaBackend {
   Error release_weights(const void* host_ptr);
   Error profile_enable(bool on);
   Error profile_read(double* ms, uint64_t* calls, uint64_t* launches);
+  // 0..4 as uaii_moe_set_expert_path; 5 = automatic with the Q4_K quad gate/up on f16 activations
   void set_expert_path(int p) {
-    path_ = p;
+    path_ = p == 5 ? 0 : p;
+    f16_quad_ = p == 5;
     drop_graphs();
   }
   // Replay repeated device-resident layer calls from CUDA graphs (default on).
@@ -234,6 +237,7 @@ class MoeCudaBackend {
   cudaStream_t stream_ = nullptr;
   bool own_stream_ = false;
   int path_ = 0;
+  bool f16_quad_ = false;
   ExpertPlan last_plan_{};
   int* dev_err_ = nullptr;
   TailSplit tail_{};  // quad schedule tail split (null in external mode: no split)

@@ -86,6 +86,10 @@ struct Args {
   // sub-blocks of the f16 activations as f16 (hi) and f16 (remainder) pairs, [S_rows][kquads][16];
   // null: the minima go through one MMA per k-step instead.
   const __half* xsum;
+  // Integer variant: per slot and quad the activations' dequant scale, [S_rows][kquads] f32 (the
+  // activations are the int8 hi / lo planes of route_gather's kOrderQ4KI8 and xsum holds their
+  // integer sub-block sums / 1024); null: f16 activations.
+  const float* xscale;
   int64_t S_rows;
   // Quad schedule, gate/up: when the last wave of tiles fills at most half of the grid, its
   // tiles are cut into K ranges run by different CTAs; tail_part [tiles][ranges][128][BN] f32
@@ -869,6 +873,21 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4],
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// Integer products m16n8k32: u8 weights times s8 (hi) or u8 (lo) activation bytes, exact int32
+// sums, no accumulator input (the products of one sub-block are scaled before they are added).
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void mma_u8u8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+
 // Named barrier over `n` threads that also ORs a predicate across them.
 __device__ __forceinline__ bool bar_any(int id, int n, bool v) {
   uint32_t r;
@@ -1374,12 +1393,49 @@ template <> struct QuadUnit<kQ6_K> {
   }
 };
 
-template <int F, int NT, int ST, bool kXSum>
+// Integer variant (Q4_K gate/up, 8-slot tiles).  The activations arrive as 16-bit integers per
+// (slot, quad): x ~ s * a, s = max|x| / 32767 over the quad's 256 elements, a = 256 * hi + lo
+// split into an s8 byte plane (hi) and a u8 plane (lo) (route_gather, kOrderQ4KI8).  One k-step
+// of m16n8k32 is one 32-element sub-block: the operands are the raw nibbles as bytes -- q for
+// the low-nibble sub-blocks (one AND per 4 elements), 16 q for the high-nibble ones -- and the
+// exact int32 products of each plane are scaled by the sub-block's 6-bit scale and added in
+// int32 (no overflow: at most 9.9e8 per quad).  The minima use the activations' integer
+// sub-block sums (f16 hi + lo, divided by 1024) in one f16 MMA per sum word, as above.  Per quad
+// and output: acc += s * (d / 16 * (256 * main_hi + main_lo) - 1024 * dmin * sum_m).  Within a
+// sub-block, K position 4t + i holds element 8t + i and 16 + 4t + i holds 8t + 4 + i (t = lane
+// quarter, i < 4), so a lane's operand words are qs words 8p + 2t and 8p + 2t + 1.
+struct QuadI8 {
+  uint32_t sc[2];  // 6-bit scales of sub-blocks 0-3 and 4-7, one per byte
+  uint32_t mf;     // (m of sub-block 2t, m of 2t + 1), f16: A operand of the minima MMA
+  float d16, dm1024;
+  // qs words 8p + 2t and 8p + 2t + 1 of sub-block pair p (loaded where they are used)
+  __device__ __forceinline__ static uint2 words(const uint8_t* row, int p, int t) {
+    return *reinterpret_cast<const uint2*>(row + 16 + 32 * p + 8 * t);
+  }
+  __device__ __forceinline__ void load(const uint8_t* row, int t) {
+    const uint4 hdr = *reinterpret_cast<const uint4*>(row);  // d, dmin, scales[12]
+    // get_scale_min_k4 for all eight sub-blocks at once, one byte each
+    sc[0] = hdr.y & 0x3F3F3F3Fu;
+    sc[1] = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+    const uint32_t m_lo = hdr.z & 0x3F3F3F3Fu;
+    const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
+    const uint32_t mw = (t < 2 ? m_lo : m_hi) >> (16u * (uint32_t)(t & 1));  // bytes m(2t), m(2t + 1)
+    mf = as_u32(__hsub2(as_h2(__byte_perm(mw, 0, 0x4140) | kMagic), __float2half2_rn(1024.f)));
+    const float2 dm = __half22float2(as_h2(hdr.x));
+    d16 = dm.x * 0.0625f;
+    dm1024 = dm.y * 1024.f;
+  }
+  // scale of sub-block j (compile-time) as an integer
+  __device__ __forceinline__ int scale(int j) const { return (int)__byte_perm(sc[j >> 2], 0, 0x4440 | (j & 3)); }
+};
+
+template <int F, int NT, int ST, bool kXSum, bool kI8 = false>
 __global__ void __launch_bounds__(kWmThreads, 1)
     expert_quad_mma_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                            const __grid_constant__ CUtensorMap tm_x, const Args args) {
   static_assert(F == kQ4_K || F == kQ6_K, "quad schedule: K-quants only");
   static_assert(!kXSum || F == kQ4_K, "activation sub-block sums serve the Q4_K minima");
+  static_assert(!kI8 || (F == kQ4_K && kXSum && NT == 1), "integer activations: Q4_K, 8-slot tiles");
   using C = WmCfg<F, NT, ST>;
   using Fm = Fmt<F>;
   constexpr int BN = C::BN;
@@ -1485,6 +1541,15 @@ __global__ void __launch_bounds__(kWmThreads, 1)
     uint32_t boff[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) boff[j] = (uint32_t)(ld_n * 128) + (((uint32_t)(2 * j) ^ cx) << 4);
+    // integer variant: matrices (hi, K 0-15), (hi, K 16-31), (lo, K 0-15), (lo, K 16-31) of a sub-block;
+    // sub-block j sits in atom 2 * plane + j / 4 at chunks 2 (j % 4) and 2 (j % 4) + 1
+    uint32_t i8off[4];
+    if constexpr (kI8) {
+      const uint32_t r8 = (uint32_t)(lane & 7), half = (uint32_t)(ld_mi & 1), plane = (uint32_t)(ld_mi >> 1);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        i8off[j] = plane * 2u * (uint32_t)C::kBAtom + r8 * 128u + ((((uint32_t)(2 * j) + half) ^ r8) << 4);
+    }
     const uint32_t sB0 = smem_u32(sB);
     float* red = sR + (mw * 32 + lane) * 4 * NT;
     uint32_t pi = 0;
@@ -1498,23 +1563,90 @@ __global__ void __launch_bounds__(kWmThreads, 1)
       for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[n][i] = acc2[n][i] = 0.f;
-      for (int q = q0; q < q1; ++q, ++pi) {
-        if (((q - q0) & 1) != h) continue;  // the other half's quad
-        if (!(ok = bounded_wait(full + pi % ST, (pi / ST) & 1, s_abort, err, kErrTimeoutDequant))) break;
-        const uint8_t* stage = sP + (pi % ST) * C::kPStage;
+      // per-tile bases of the slot-side records: sub-block sums of slots g (+ 8n), read as
+      // (S[2tq], S[2tq+1]) words, and (integer variant) the scales of accumulator columns 2tq, 2tq+1
+      const uint32_t* xs_row[NT];
+      const float *xsc_row0 = nullptr, *xsc_row1 = nullptr;
+      if constexpr (kXSum) {
+        const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          const int64_t slot = min((int64_t)(slot0 + 8 * n + g), args.S_rows - 1);
+          xs_row[n] = reinterpret_cast<const uint32_t*>(args.xsum + slot * args.kquads * 16) + tq;
+        }
+        if constexpr (kI8) {
+          xsc_row0 = args.xscale + min((int64_t)(slot0 + 2 * tq), args.S_rows - 1) * args.kquads;
+          xsc_row1 = args.xscale + min((int64_t)(slot0 + 2 * tq + 1), args.S_rows - 1) * args.kquads;
+        }
+      }
+      // this half's quads q0 + h, q0 + h + 2, ...; quad q sits in stage (pi + q - q0) % ST
+      const uint32_t pi0 = pi;
+      pi += (uint32_t)(q1 - q0);
+      for (int q = q0 + h; q < q1; q += 2) {
+        const uint32_t ps = pi0 + (uint32_t)(q - q0);
+        if (!(ok = bounded_wait(full + ps % ST, (ps / ST) & 1, s_abort, err, kErrTimeoutDequant))) break;
+        const uint8_t* stage = sP + (ps % ST) * C::kPStage;
         // Q4_K with activation sums: this quad's sub-block sums of slots g (and g + 8), issued
         // first so that their latency hides behind the decode below
         uint32_t xs[NT][2];
         if constexpr (kXSum) {
-          const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
 #pragma unroll
           for (int n = 0; n < NT; ++n) {
-            const int64_t slot = min((int64_t)(slot0 + 8 * n + g), args.S_rows - 1);
-            const uint32_t* p =
-                reinterpret_cast<const uint32_t*>(args.xsum + (slot * args.kquads + q) * 16) + tq;
-            xs[n][0] = __ldg(p);      // (S[2tq], S[2tq+1]) rounded to f16
-            xs[n][1] = __ldg(p + 4);  // their remainders
+            xs[n][0] = __ldg(xs_row[n] + 8 * q);      // (S[2tq], S[2tq+1]) rounded to f16
+            xs[n][1] = __ldg(xs_row[n] + 8 * q + 4);  // their remainders
           }
+        }
+        if constexpr (kI8) {
+          const float xsc0 = __ldg(xsc_row0 + q);  // dequant scales of columns 2tq, 2tq+1
+          const float xsc1 = __ldg(xsc_row1 + q);
+          const uint8_t* row0 = stage + r0 * C::kWB;
+          const uint8_t* row1 = stage + r1 * C::kWB;
+          QuadI8 v0, v1;
+          v0.load(row0, tq);
+          v1.load(row1, tq);
+          const uint32_t bq = sB0 + (ps % ST) * C::kBQuad;
+          int ah[4], al[4];  // per accumulator: 16 x sum_j sc_j sum_k q_k (hi and lo plane bytes)
+          __syncwarp();            // ldmatrix / mma.sync below need the whole warp converged
+          uint2 w0 = QuadI8::words(row0, 0, tq), w1 = QuadI8::words(row1, 0, tq);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t M = (j & 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;  // 16 q (high nibbles) or q
+            const int nb = j & 1;
+            if (j > 0 && nb == 0) {
+              w0 = QuadI8::words(row0, j >> 1, tq);
+              w1 = QuadI8::words(row1, j >> 1, tq);
+            }
+            const uint32_t a[4] = {w0.x & M, w1.x & M, w0.y & M, w1.y & M};
+            uint32_t b[4];
+            asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
+                         : "r"(bq + i8off[j & 3] + (uint32_t)((j >> 2) * C::kBAtom)));
+            int ph[4], pl[4];
+            mma_u8s8(ph, a, b[0], b[1]);
+            mma_u8u8(pl, a, b[2], b[3]);
+            // scales of rows g (accumulators 0, 1) and g + 8 (2, 3); x16 where the operand is q, not 16 q
+            const int s0 = v0.scale(j) << (nb ? 0 : 4), s1 = v1.scale(j) << (nb ? 0 : 4);
+            if (j == 0) {
+              ah[0] = s0 * ph[0]; ah[1] = s0 * ph[1]; ah[2] = s1 * ph[2]; ah[3] = s1 * ph[3];
+              al[0] = s0 * pl[0]; al[1] = s0 * pl[1]; al[2] = s1 * pl[2]; al[3] = s1 * pl[3];
+            } else {
+              ah[0] += s0 * ph[0]; ah[1] += s0 * ph[1]; ah[2] += s1 * ph[2]; ah[3] += s1 * ph[3];
+              al[0] += s0 * pl[0]; al[1] += s0 * pl[1]; al[2] += s1 * pl[2]; al[3] += s1 * pl[3];
+            }
+          }
+          float m2[4] = {0.f, 0.f, 0.f, 0.f};  // sum_k m(row, k) S(slot, k) / 1024
+          const uint32_t amf[4] = {v0.mf, v1.mf, 0u, 0u};
+          mma_16816(m2, amf, xs[0][0], 0u);
+          mma_16816(m2, amf, xs[0][1], 0u);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float d16 = i < 2 ? v0.d16 : v1.d16, dm = i < 2 ? v0.dm1024 : v1.dm1024;
+            const float main = fmaf(256.f, (float)ah[i], (float)al[i]);  // 16 x sum_j sc_j sum_k q_k a_k
+            acc[0][i] = fmaf((i & 1) ? xsc1 : xsc0, fmaf(d16, main, -dm * m2[i]), acc[0][i]);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty + ps % ST);
+          continue;
         }
         QuadUnit<F> u0, u1;
         if constexpr (F == kQ6_K) {  // 16-byte loads with the window offset as a constant
@@ -1534,7 +1666,7 @@ __global__ void __launch_bounds__(kWmThreads, 1)
           u1.load(stage + r1 * C::kWB, tq);
         }
         // the four lane addresses of the stage's k-step columns; atoms are constant offsets from them
-        const uint32_t bq = sB0 + (pi % ST) * C::kBQuad;
+        const uint32_t bq = sB0 + (ps % ST) * C::kBQuad;
         const uint32_t bqa[4] = {bq + boff[0], bq + boff[1], bq + boff[2], bq + boff[3]};
         uint32_t am_lo[4], am_hi[4];  // Q4_K min operands: rows g, g + 8 of sub-block 2t, then 2t + 1
         if constexpr (F == kQ4_K && !kXSum) {
@@ -1602,7 +1734,7 @@ __global__ void __launch_bounds__(kWmThreads, 1)
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty + pi % ST);
+        if (lane == 0) mbar_arrive(empty + ps % ST);
       }
       if constexpr (F == kQ6_K && NT == 1) {
 #pragma unroll
@@ -1850,13 +1982,13 @@ cudaError_t run_warp_mma(const CUtensorMap& w0, const CUtensorMap& w1, const CUt
   return cudaGetLastError();
 }
 
-template <int F, int NT, bool kXSum = false>
+template <int F, int NT, bool kXSum = false, bool kI8 = false>
 cudaError_t run_quad_mma(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x, const Args& a,
                          cudaStream_t st) {
   constexpr int ST = WmStages<F, NT>::ST;
   using C = WmCfg<F, NT, ST>;
   static_assert(C::kSmem <= 227 * 1024, "shared memory budget");
-  auto kern = expert_quad_mma_kernel<F, NT, ST, kXSum>;
+  auto kern = expert_quad_mma_kernel<F, NT, ST, kXSum, kI8>;
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
@@ -1871,6 +2003,7 @@ template <int F>
 cudaError_t dispatch_quad(int bn, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
                           const Args& a, cudaStream_t st) {
   if constexpr (F == kQ4_K) {
+    if (a.xscale) return bn == 8 && a.xsum ? run_quad_mma<F, 1, true, true>(w0, w1, x, a, st) : cudaErrorInvalidValue;
     if (a.xsum) {
       switch (bn) {
         case 8: return run_quad_mma<F, 1, true>(w0, w1, x, a, st);
@@ -1925,7 +2058,8 @@ cudaError_t launch_common(int sched, int fmt, bool gateup, const void* W0, const
                           int64_t E, int64_t rows, int64_t K, const void* act16, int64_t S_rows,
                           const int32_t* counts, const int32_t* offsets, int32_t* tile_base, int bn, int splits,
                           void* h16, float* out, int64_t out_ld, int64_t split_stride, int* err, cudaStream_t st,
-                          int h_order, bool table_ready, const void* xsum, const TailSplit* tail) {
+                          int h_order, bool table_ready, const void* xsum, const TailSplit* tail,
+                          const float* xscale) {
   const int mk = min_k(fmt);
   const bool warp_mma = sched == kSchedWarpMma, quad = sched == kSchedQuadMma;
   if (!mk || K % mk != 0 || K <= 0) return cudaErrorNotSupported;
@@ -1967,6 +2101,8 @@ cudaError_t launch_common(int sched, int fmt, bool gateup, const void* W0, const
   a.h_out = static_cast<__half*>(h16);
   a.h_order = h_order;
   a.xsum = quad && fmt == kQ4_K ? static_cast<const __half*>(xsum) : nullptr;
+  a.xscale = quad && fmt == kQ4_K && gateup ? xscale : nullptr;
+  if (xscale != nullptr && a.xscale == nullptr) return cudaErrorInvalidValue;
   a.S_rows = S_rows;
   if (quad && gateup && tail != nullptr && tail->part != nullptr && tail->cnt != nullptr && bn <= kTailMaxBn &&
       num_sms() <= kTailMaxUnits) {
@@ -2037,9 +2173,10 @@ bool warp_mma_shapes_supported(int gfmt, int dfmt, int64_t D, int64_t I) {
 cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pitch, int64_t E, int64_t I, int64_t D,
                                const void* xp16, int64_t S_rows, const int32_t* counts, const int32_t* offsets,
                                int32_t* tile_base, int bn, void* h16, int* err, cudaStream_t st, int sched,
-                               int h_order, bool table_ready, const void* xsum, const TailSplit* tail) {
+                               int h_order, bool table_ready, const void* xsum, const TailSplit* tail,
+                               const float* xscale) {
   return launch_common(sched, fmt, true, G, U, pitch, E, I, D, xp16, S_rows, counts, offsets, tile_base, bn, 1,
-                       h16, nullptr, I, 0, err, st, h_order, table_ready, xsum, tail);
+                       h16, nullptr, I, 0, err, st, h_order, table_ready, xsum, tail, xscale);
 }
 
 cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
@@ -2047,7 +2184,8 @@ cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, 
                              int bn, int splits, float* out, int* err, cudaStream_t st, int sched,
                              bool table_ready) {
   return launch_common(sched, fmt, false, Dn, Dn, pitch, E, D, I, h16, S_rows, counts, offsets, tile_base, bn,
-                       splits, nullptr, out, D, S_rows * D, err, st, kOrderTc, table_ready, nullptr, nullptr);
+                       splits, nullptr, out, D, S_rows * D, err, st, kOrderTc, table_ready, nullptr, nullptr,
+                       nullptr);
 }
 
 namespace {

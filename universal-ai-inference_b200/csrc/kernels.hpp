@@ -92,6 +92,8 @@ struct TileTables {
   // Quad schedule with Q4_K weights: the activations' 32-element sub-block sums (xsum_kpos order,
   // see launch_gateup_umma), or null.
   void* xsum = nullptr;
+  // kOrderQ4KI8: the per (slot, quad) dequant scales of the integer activations [S][D / 256] f32.
+  float* xscale = nullptr;
 };
 cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E, int k,
                                 const RouteBuffers& rb, float* xp_f32, void* xp_f16,
@@ -167,6 +169,10 @@ inline bool quad_mma_format(int fmt) { return fmt == 14 || fmt == 16; }
 // quad, the f32 sums of the eight 32-element sub-blocks of the f16 activations as 8 f16 values
 // then their 8 f16 remainders ([S_rows][kquads][16] f16, route_gather writes them), so the Q4_K
 // minima take two MMAs per quad instead of one per k-step.
+// xscale (quad schedule, Q4_K gate/up, 8-slot tiles): x holds 16-bit integer activations as
+// int8 hi / lo planes per 256-element quad (route_gather's kOrderQ4KI8: [S_rows][kquads][512]
+// bytes in the xp16 buffer), xscale their per (slot, quad) dequant scales [S_rows][kquads] f32,
+// and xsum the planes' integer sub-block sums / 1024; the products run on integer mma.sync.
 // Tail split of the quad schedule's gate/up launch (see the kernel): part holds
 // kTailMaxUnits x 128 x kTailMaxBn f32, cnt kTailMaxUnits ints, zero before the first launch
 // (every launch leaves them zero).  A null or absent TailSplit turns the split off.
@@ -180,7 +186,7 @@ cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pi
                                const int32_t* offsets, int32_t* tile_base, int bn, void* h16, int* err,
                                cudaStream_t st, int sched = kSchedTcgen05, int h_order = 0,
                                bool table_ready = false, const void* xsum = nullptr,
-                               const TailSplit* tail = nullptr);
+                               const TailSplit* tail = nullptr, const float* xscale = nullptr);
 // out[split][slot, o] = partial of h16[slot] . Dn[e, o] over the split's K range (f32).
 cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
                              int64_t S_rows, const int32_t* counts, const int32_t* offsets,

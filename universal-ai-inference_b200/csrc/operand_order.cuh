@@ -46,7 +46,9 @@ __host__ __device__ __forceinline__ int64_t q6k_kpos(int64_t i) {
 }
 
 // Which order an operand row is stored in.
-enum OperandOrder : int { kOrderTc = 0, kOrderWm = 1, kOrderQ4K = 2, kOrderQ6K = 3 };
+enum OperandOrder : int { kOrderTc = 0, kOrderWm = 1, kOrderQ4K = 2, kOrderQ6K = 3, kOrderQ4KI8 = 4 };
+// kOrderQ4KI8 is not an f16 order: route_gather writes 16-bit integer activations as int8 planes
+// (see launch_gateup_umma); operand_pos does not apply to it.
 __host__ __device__ __forceinline__ int64_t operand_pos(int order, int64_t i) {
   switch (order) {
     case kOrderWm: return wm_kpos(i);

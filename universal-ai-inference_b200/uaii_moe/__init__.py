@@ -244,11 +244,11 @@ class Backend:
 
     def last_plan(self) -> dict:
         """Schedule of the most recent expert-product call: tensor cores or not,
-        which tensor-core schedule ("tcgen05", "warp_mma", "quad_mma" or None), slot
+        which tensor-core schedule ("tcgen05", "warp_mma", "quad_mma", "quad_mma_i8" or None), slot
         tile width and down-projection K splits."""
         tc, bn, sp = c_int(), c_int(), c_int()
         _check(lib.uaii_moe_last_plan(self._h, byref(tc), byref(bn), byref(sp)))
-        sched = {1: "tcgen05", 2: "warp_mma", 3: "quad_mma"}.get(tc.value)
+        sched = {1: "tcgen05", 2: "warp_mma", 3: "quad_mma", 4: "quad_mma_i8"}.get(tc.value)
         return {"tensor_cores": bool(tc.value), "schedule": sched, "slot_tile": bn.value, "down_splits": sp.value}
 
     PHASES = ("router", "route", "gateup", "down", "shared", "combine")
