@@ -1051,7 +1051,8 @@ struct WmCfg {
   static constexpr int kBQuad = 4 * kBAtom;
   static constexpr int kOffB = 0;
   static constexpr int kOffP = kOffB + ST * kBQuad;
-  static constexpr int kRedBytes = 8 * 32 * 4 * NT * 4;  // [8 row blocks][32 lanes][4 NT] f32
+  // warp-MMA schedule: [8 row blocks][32 lanes][4 NT] f32; quad schedule: [2 halves][128 rows][BN] f32
+  static constexpr int kRedBytes = 2 * 128 * BN * 4;
   static constexpr int kOffR = kOffP + ST * kPStage;
   static constexpr int kOffBar = kOffR + kRedBytes;
   static constexpr int kNumBars = 2 * ST;
@@ -1551,7 +1552,6 @@ __global__ void __launch_bounds__(kWmThreads, 1)
         i8off[j] = plane * 2u * (uint32_t)C::kBAtom + r8 * 128u + ((((uint32_t)(2 * j) + half) ^ r8) << 4);
     }
     const uint32_t sB0 = smem_u32(sB);
-    float* red = sR + (mw * 32 + lane) * 4 * NT;
     uint32_t pi = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
@@ -1740,80 +1740,75 @@ __global__ void __launch_bounds__(kWmThreads, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[0][i] += acc2[0][i];
       }
-      // every compute warp reaches this barrier once per tile; a wait that gave up stops all of them
+      // every compute warp reaches this barrier once per tile; a wait that gave up stops all of them.
+      // It also puts every thread's reads of the previous tile's sums before this tile's writes.
       if (bar_any(1, kCompute, !ok)) break;
-      if (h == 1) {  // the odd quads' sums go to the even half
+      {  // both halves' sums: sR[h][slot][row], row 16 mw + g + 8 (i / 2), slot 8 n + 2 tq + i % 2
+        float* rs = sR + h * (128 * BN);
 #pragma unroll
         for (int n = 0; n < NT; ++n)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) red[4 * n + i] = acc[n][i];
+          for (int i = 0; i < 4; ++i) rs[(8 * n + 2 * tq + (i & 1)) * 128 + 16 * mw + g + 8 * (i >> 1)] = acc[n][i];
       }
       bar_sync(1, kCompute);
-      if (h == 1) continue;
-#pragma unroll
-      for (int n = 0; n < NT; ++n)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[n][i] += red[4 * n + i];
-      if (tail >= 0) {  // a tail unit: publish this range's sums; the tile's last unit adds them all
-        float* part = args.tail_part + (int64_t)tail * ts * (128 * BN);
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            part[(int64_t)tsp * (128 * BN) + (16 * mw + g + 8 * (i >> 1)) * BN + 8 * n + 2 * tq + (i & 1)] =
-                acc[n][i];
-        __threadfence();
-        bar_sync(2, kCompute / 2);
-        const bool last = bar_any(2, kCompute / 2, threadIdx.x == 0 && atomicAdd(args.tail_cnt + tail, 1) == ts - 1);
-        if (!last) continue;
-        __threadfence();
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float* src = part + (16 * mw + g + 8 * (i >> 1)) * BN + 8 * n + 2 * tq + (i & 1);
-            float v = 0.f;
-            for (int r = 0; r < ts; ++r) v += __ldcg(src + (int64_t)r * (128 * BN));
-            acc[n][i] = v;
-          }
-        if (threadIdx.x == 0) args.tail_cnt[tail] = 0;  // zero again for the next launch
-      }
-      // accumulator (n, i): row g + 8(i / 2) of the block, slot 8n + 2tq + i % 2
+      // The tile's outputs, spread over all compute threads with the row fastest (coalesced
+      // stores): each the even half's sum plus the odd half's.
+      const int ct = threadIdx.x;
       const int n_valid = min(BN, __ldg(args.counts + t.e) - t.n_tile * BN);
       const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
-      if (args.gateup) {  // up rows (blocks 4-7) meet the gate rows (blocks 0-3) of the same features
-        if (mw >= 4) {
+      if (args.gateup) {  // feature f: gate row f and up row 64 + f
+        constexpr int kPer = 64 * BN / kCompute;
+        float gv[kPer], uv[kPer];
 #pragma unroll
-          for (int n = 0; n < NT; ++n)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) red[4 * n + i] = acc[n][i];
+        for (int r = 0; r < kPer; ++r) {
+          const int o = ct + r * kCompute, f = o % 64, sl = o / 64;
+          gv[r] = sR[sl * 128 + f] + sR[128 * BN + sl * 128 + f];
+          uv[r] = sR[sl * 128 + 64 + f] + sR[128 * BN + sl * 128 + 64 + f];
         }
-        bar_sync(2, kCompute / 2);
-        if (mw < 4) {
-          const float* up = sR + ((mw + 4) * 32 + lane) * 4 * NT;
+        if (tail >= 0) {  // a tail unit: publish this range's sums; the tile's last unit adds them all
+          float* part = args.tail_part + (int64_t)tail * ts * (128 * BN);
 #pragma unroll
-          for (int n = 0; n < NT; ++n)
+          for (int r = 0; r < kPer; ++r) {
+            const int o = ct + r * kCompute, f = o % 64, sl = o / 64;
+            part[(int64_t)tsp * (128 * BN) + sl * 128 + f] = gv[r];
+            part[(int64_t)tsp * (128 * BN) + sl * 128 + 64 + f] = uv[r];
+          }
+          __threadfence();
+          bar_sync(1, kCompute);
+          const bool last = bar_any(1, kCompute, ct == 0 && atomicAdd(args.tail_cnt + tail, 1) == ts - 1);
+          if (!last) continue;
+          __threadfence();
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int feat = t.m_tile * 64 + 16 * mw + g + 8 * (i >> 1);
-              const int sl = 8 * n + 2 * tq + (i & 1);
-              const float gv = acc[n][i], uv = up[4 * n + i];
-              const float sig = 1.0f / (1.0f + __expf(-gv));
-              if (sl < n_valid)
-                args.h_out[(int64_t)(slot0 + sl) * args.out_ld + operand_pos(args.h_order, feat)] =
-                    __float2half_rn((gv * sig) * uv);
+          for (int r = 0; r < kPer; ++r) {
+            const int o = ct + r * kCompute, f = o % 64, sl = o / 64;
+            float a = 0.f, b = 0.f;
+            for (int u = 0; u < ts; ++u) {
+              a += __ldcg(part + (int64_t)u * (128 * BN) + sl * 128 + f);
+              b += __ldcg(part + (int64_t)u * (128 * BN) + sl * 128 + 64 + f);
             }
+            gv[r] = a;
+            uv[r] = b;
+          }
+          if (ct == 0) args.tail_cnt[tail] = 0;  // zero again for the next launch
+        }
+#pragma unroll
+        for (int r = 0; r < kPer; ++r) {
+          const int o = ct + r * kCompute, f = o % 64, sl = o / 64;
+          const float sig = 1.0f / (1.0f + __expf(-gv[r]));
+          if (sl < n_valid)
+            args.h_out[(int64_t)(slot0 + sl) * args.out_ld + operand_pos(args.h_order, t.m_tile * 64 + f)] =
+                __float2half_rn((gv[r] * sig) * uv[r]);
         }
       } else {
+        constexpr int kPer = 128 * BN / kCompute;
         float* out = args.out + (int64_t)t.split * args.split_stride;
 #pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int o = t.m_tile * 128 + 16 * mw + g + 8 * (i >> 1);
-            const int sl = 8 * n + 2 * tq + (i & 1);
-            if (sl < n_valid) out[(int64_t)(slot0 + sl) * args.out_ld + o] = acc[n][i];
-          }
+        for (int r = 0; r < kPer; ++r) {
+          const int o = ct + r * kCompute, row = o % 128, sl = o / 128;
+          if (sl < n_valid)
+            out[(int64_t)(slot0 + sl) * args.out_ld + t.m_tile * 128 + row] =
+                sR[sl * 128 + row] + sR[128 * BN + sl * 128 + row];
+        }
       }
     }
   }
@@ -1960,7 +1955,7 @@ template <int F, int NT>
 struct WmStages {
   static constexpr int kBudget = 220 * 1024;
   static constexpr int kPair = Fmt<F>::kBoxes * 128 * Fmt<F>::kBoxBytes + 4 * 8 * NT * 128;
-  static constexpr int kFit = (kBudget - 8 * 32 * 4 * NT * 4) / kPair;
+  static constexpr int kFit = (kBudget - 2 * 128 * 8 * NT * 4) / kPair;
   static constexpr int ST = kFit > 8 ? 8 : kFit;
   static_assert(ST >= 2, "shared-memory budget");
 };
