@@ -347,9 +347,17 @@ __device__ __forceinline__ Tile decode_tile(const Args& a, int tile, int bn) {
   Tile t;
   t.e = lo;
   int local = tile - __ldg(a.tile_base + lo);
-  t.split = local % a.splits;
-  local /= a.splits;
+  t.split = 0;
+  if (a.splits > 1) {
+    t.split = local % a.splits;
+    local /= a.splits;
+  }
   const int nt = (__ldg(a.counts + lo) + bn - 1) / bn;
+  if (nt == 1) {  // one slot tile (decode): the band order is the row-tile order
+    t.n_tile = 0;
+    t.m_tile = local;
+    return t;
+  }
   const int band = local / (a.band_m * nt);
   const int m0 = band * a.band_m;
   const int bm = min(a.band_m, a.m_tiles - m0);  // the last band may be narrower
