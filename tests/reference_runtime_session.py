@@ -2,7 +2,7 @@
 built from the unmodified reference sources) and prints one JSON line.
 
     python tests/reference_runtime_session.py OUT_DIR [--plugin] [--backend cpu|cuda]
-        [--const-weights] [--demo] [--T 64]
+        [--const-weights] [--demo] [--T 64] [--runtime stub|cuda]
 
 The graph is a .uaii.json IR file (the reference's own format, include/uaii/ir/serialize.hpp)
 with MoERouter -> MoEExpertsSwiGLU; its weights live in a GGUF file next to it and are
@@ -36,6 +36,8 @@ from gguf_writer import F32 as KV_F32, U32, GGML_F32, GGML_Q4_K, GGML_Q6_K, writ
 from oracle import synth  # noqa: E402
 
 RUNTIME_SO = os.path.join(REPO, "oracle", "_ref", "libuaii_ref_runtime.so")
+# the same runtime built with UAII_WITH_CUDA, its CUDA native layer from plugin/uaii_cuda_native.cpp
+RUNTIME_CUDA_SO = os.path.join(REPO, "oracle", "_ref", "libuaii_ref_cuda.so")
 PLUGIN_SO = os.path.join(REPO, "universal-ai-inference_b200", "libuaii_moe_plugin.so")
 Q4_K, Q6_K = 14, 16
 D, E, I, K = 512, 8, 1024, 2
@@ -98,13 +100,16 @@ def main() -> None:
     ap.add_argument("--demo", action="store_true", help="also run the reference's MoE smoke demo")
     ap.add_argument("--T", type=int, default=64)
     ap.add_argument("--runs", type=int, default=2)
+    ap.add_argument("--runtime", default="stub", choices=["stub", "cuda"],
+                    help="stub: the reference's CUDA native layer stubbed out (its default build); cuda: the "
+                         "runtime with the repository's native layer linked in")
     ap.add_argument("--keep-quantized", type=int, default=1,
                     help="1: experts stay packed (the reference's own MoEExpertsSwiGLU reads f32 experts "
                          "only, so without the plugin use 0: dequantized to f32 at load)")
     a = ap.parse_args()
     if a.const_weights:
         os.environ["UAII_MOE_CONST_WEIGHTS"] = "1"
-    rt = ctypes.CDLL(RUNTIME_SO, mode=ctypes.RTLD_GLOBAL)
+    rt = ctypes.CDLL(RUNTIME_CUDA_SO if a.runtime == "cuda" else RUNTIME_SO, mode=ctypes.RTLD_GLOBAL)
     vp, cp, i32, sz = ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_size_t
     for name, res, args in (("urt_last_error", cp, []), ("urt_plugin_load", i32, [cp]),
                             ("urt_operator_registered", i32, [cp]), ("urt_moe_smoke_demo", i32, [vp]),
@@ -114,7 +119,7 @@ def main() -> None:
                             ("urt_session_backend_details", cp, [vp])):
         f = getattr(rt, name)
         f.restype, f.argtypes = res, args
-    out = {"plugin": a.plugin, "backend": a.backend, "keep_quantized": a.keep_quantized}
+    out = {"plugin": a.plugin, "backend": a.backend, "keep_quantized": a.keep_quantized, "runtime": a.runtime}
     if a.plugin:
         st = rt.urt_plugin_load(PLUGIN_SO.encode())
         out["plugin_load"] = [st, rt.urt_last_error().decode()]

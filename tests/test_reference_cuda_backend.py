@@ -92,3 +92,33 @@ def test_reference_cuda_backend_runs_moe_ops_natively():
     assert _rel(r["c"], c) <= 2e-3
     e = np.exp(x.astype(np.float64) - x.max(axis=1, keepdims=True))
     assert np.abs(np.asarray(r["softmax_y"]) - e / e.sum(axis=1, keepdims=True)).max() <= 1e-6
+
+
+def _session(tmp_path, *args):
+    d = tmp_path / ("s_" + "_".join(a.strip("-") for a in args))
+    d.mkdir()
+    p = subprocess.run([sys.executable, os.path.join(HERE, "reference_runtime_session.py"), str(d), *args],
+                       capture_output=True, text=True, timeout=600)
+    lines = [ln for ln in p.stdout.splitlines() if ln.startswith("{")]
+    assert p.returncode == 0 and lines, (p.returncode, p.stdout[-2000:], p.stderr[-2000:])
+    return json.loads(lines[-1])
+
+
+@pytest.mark.gpu
+@needs_build
+def test_reference_cuda_session_with_native_layer_and_plugin(tmp_path):
+    """A Session with backend "cuda" in the runtime built with the native layer: the backend
+    reports native, the Session's host-resident tensors run through host dispatch
+    (cuda_backend.cpp:189-192), where the operator plugin puts both MoE operators on the GPU.
+    Against the stock CPU Session (f32 experts): probabilities within 1e-6, outputs within 2e-3."""
+    plugin = os.path.join(REPO, "universal-ai-inference_b200", "libuaii_moe_plugin.so")
+    if not os.path.exists(plugin):
+        pytest.skip("plugin not built")
+    ref = _session(tmp_path, "--keep-quantized", "0")
+    got = _session(tmp_path, "--runtime", "cuda", "--backend", "cuda", "--plugin", "--const-weights")
+    assert "CUDA backend (native)" in got["details"], got["details"]
+    assert got["plugin_load"][0] == 0 and got["registered"] == [1, 1, 1]
+    assert got["plugin_calls"] == [4, 0]
+    assert np.abs(np.asarray(got["probs"]) - np.asarray(ref["probs"])).max() <= 1e-6
+    y, r = np.asarray(got["y"], np.float64), np.asarray(ref["y"], np.float64)
+    assert np.abs(y - r).max() / np.abs(r).max() <= 2e-3
