@@ -1927,8 +1927,8 @@ struct Stages {
   static constexpr int kBudget = 224 * 1024;  // stage bytes; barriers and alignment slack come on top
   static constexpr int A = BN <= 32 ? 3 : 2;
   static constexpr int kPStage = Fmt<F>::kBoxes * 128 * Fmt<F>::kBoxBytes;
-  // 256-slot tiles: 2-3 packed stages, the rest for 32 KB activation atoms
-  static constexpr int P_wide = kPStage <= 20 * 1024 ? 3 : 2;
+  // 256-slot tiles: 3 packed stages (2 above 30 KB), the rest for 32 KB activation atoms
+  static constexpr int P_wide = kPStage <= 30 * 1024 ? 3 : 2;
   static constexpr int B_wide_fit = (kBudget - P_wide * kPStage) / (256 * 128);
   static constexpr int B = BN == 256 ? (B_wide_fit > 6 ? 6 : B_wide_fit) : BN <= 32 ? 4 : (BN == 64 ? 3 : 2);
   static constexpr int kBBytes = BN == 256 ? B * 256 * 128 : B * BN * 512;
