@@ -568,12 +568,15 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t s
     if (p.warp_mma) p.bn = warp_bn(tpe);
     // K-quant layers run the warp schedule over whole super-blocks (path 4 keeps the per-unit one)
     p.quad_mma = p.warp_mma && path_ != 4 && quad_mma_format(L.gate.fmt) && quad_mma_format(L.down.fmt);
-    // Q4_K gate/up at 8-slot tiles: integer activations (path 5 keeps the f16 ones)
+    // Q4_K gate/up at 8-slot tiles: integer activations (path 5 keeps the f16 ones).  With 16-slot
+    // tiles the integer variant measured slower than tcgen05 (Mixtral-shaped, 32 tokens: 0.218 vs
+    // 0.183 ms; two slot octets of int32 sums spill under the 96-register cap).
     p.quad_i8 = p.quad_mma && !f16_quad_ && L.gate.fmt == kQ4_K && L.up.fmt == kQ4_K && p.bn == 8;
     // 16-slot tiles: the down projection is faster on the quad schedule, gate/up on tcgen05
     // (Mixtral-shaped layer, 32 tokens: down 0.160 -> 0.121 ms; gate/up 0.191 vs 0.247 ms)
     p.down_quad = !p.warp_mma && path_ == 0 && warp_ok && p.bn == 16 && quad_mma_format(L.gate.fmt) &&
                   quad_mma_format(L.down.fmt);
+
     const int64_t n_tiles = (int64_t)((tpe + p.bn - 1) / p.bn);
     p.splits = pick_splits(active * n_tiles * (L.D / 128), umma_kchunks(L.down.fmt, L.I));
   }

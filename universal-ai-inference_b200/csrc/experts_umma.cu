@@ -1444,7 +1444,7 @@ __global__ void __launch_bounds__(kWmThreads, 1)
                            const __grid_constant__ CUtensorMap tm_x, const Args args) {
   static_assert(F == kQ4_K || F == kQ6_K, "quad schedule: K-quants only");
   static_assert(!kXSum || F == kQ4_K, "activation sub-block sums serve the Q4_K minima");
-  static_assert(!kI8 || (F == kQ4_K && kXSum && NT == 1), "integer activations: Q4_K, 8-slot tiles");
+  static_assert(!kI8 || (F == kQ4_K && kXSum), "integer activations: Q4_K gate/up");  // launched with NT == 1
   using C = WmCfg<F, NT, ST>;
   using Fm = Fmt<F>;
   constexpr int BN = C::BN;
@@ -1574,17 +1574,19 @@ __global__ void __launch_bounds__(kWmThreads, 1)
       // per-tile bases of the slot-side records: sub-block sums of slots g (+ 8n), read as
       // (S[2tq], S[2tq+1]) words, and (integer variant) the scales of accumulator columns 2tq, 2tq+1
       const uint32_t* xs_row[NT];
-      const float *xsc_row0 = nullptr, *xsc_row1 = nullptr;
+      const float* xsc_row[NT][2];
       if constexpr (kXSum) {
         const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
           const int64_t slot = min((int64_t)(slot0 + 8 * n + g), args.S_rows - 1);
           xs_row[n] = reinterpret_cast<const uint32_t*>(args.xsum + slot * args.kquads * 16) + tq;
-        }
-        if constexpr (kI8) {
-          xsc_row0 = args.xscale + min((int64_t)(slot0 + 2 * tq), args.S_rows - 1) * args.kquads;
-          xsc_row1 = args.xscale + min((int64_t)(slot0 + 2 * tq + 1), args.S_rows - 1) * args.kquads;
+          if constexpr (kI8) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+              xsc_row[n][c] =
+                  args.xscale + min((int64_t)(slot0 + 8 * n + 2 * tq + c), args.S_rows - 1) * args.kquads;
+          }
         }
       }
       // this half's quads q0 + h, q0 + h + 2, ...; quad q sits in stage (pi + q - q0) % ST
@@ -1605,16 +1607,20 @@ __global__ void __launch_bounds__(kWmThreads, 1)
           }
         }
         if constexpr (kI8) {
-          const float xsc0 = __ldg(xsc_row0 + q);  // dequant scales of columns 2tq, 2tq+1
-          const float xsc1 = __ldg(xsc_row1 + q);
+          float xsc[NT][2];  // dequant scales of accumulator columns 8n + 2tq, 8n + 2tq + 1
+#pragma unroll
+          for (int n = 0; n < NT; ++n) {
+            xsc[n][0] = __ldg(xsc_row[n][0] + q);
+            xsc[n][1] = __ldg(xsc_row[n][1] + q);
+          }
           const uint8_t* row0 = stage + r0 * C::kWB;
           const uint8_t* row1 = stage + r1 * C::kWB;
           QuadI8 v0, v1;
           v0.load(row0, tq);
           v1.load(row1, tq);
           const uint32_t bq = sB0 + (ps % ST) * C::kBQuad;
-          int ah[4], al[4];  // per accumulator: 16 x sum_j sc_j sum_k q_k (hi and lo plane bytes)
-          __syncwarp();            // ldmatrix / mma.sync below need the whole warp converged
+          int ah[NT][4], al[NT][4];  // per accumulator: 16 x sum_j sc_j sum_k q_k (hi and lo plane bytes)
+          __syncwarp();              // ldmatrix / mma.sync below need the whole warp converged
           uint2 w0 = QuadI8::words(row0, 0, tq), w1 = QuadI8::words(row1, 0, tq);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -1625,32 +1631,38 @@ __global__ void __launch_bounds__(kWmThreads, 1)
               w1 = QuadI8::words(row1, j >> 1, tq);
             }
             const uint32_t a[4] = {w0.x & M, w1.x & M, w0.y & M, w1.y & M};
-            uint32_t b[4];
-            asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
-                         : "r"(bq + i8off[j & 3] + (uint32_t)((j >> 2) * C::kBAtom)));
-            int ph[4], pl[4];
-            mma_u8s8(ph, a, b[0], b[1]);
-            mma_u8u8(pl, a, b[2], b[3]);
             // scales of rows g (accumulators 0, 1) and g + 8 (2, 3); x16 where the operand is q, not 16 q
             const int s0 = v0.scale(j) << (nb ? 0 : 4), s1 = v1.scale(j) << (nb ? 0 : 4);
-            if (j == 0) {
-              ah[0] = s0 * ph[0]; ah[1] = s0 * ph[1]; ah[2] = s1 * ph[2]; ah[3] = s1 * ph[3];
-              al[0] = s0 * pl[0]; al[1] = s0 * pl[1]; al[2] = s1 * pl[2]; al[3] = s1 * pl[3];
-            } else {
-              ah[0] += s0 * ph[0]; ah[1] += s0 * ph[1]; ah[2] += s1 * ph[2]; ah[3] += s1 * ph[3];
-              al[0] += s0 * pl[0]; al[1] += s0 * pl[1]; al[2] += s1 * pl[2]; al[3] += s1 * pl[3];
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {  // slot octet n: activation rows 8n .. 8n + 7 of the atoms
+              uint32_t b[4];
+              asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
+                           : "r"(bq + i8off[j & 3] + (uint32_t)((j >> 2) * C::kBAtom + n * 1024)));
+              int ph[4], pl[4];
+              mma_u8s8(ph, a, b[0], b[1]);
+              mma_u8u8(pl, a, b[2], b[3]);
+              if (j == 0) {
+                ah[n][0] = s0 * ph[0]; ah[n][1] = s0 * ph[1]; ah[n][2] = s1 * ph[2]; ah[n][3] = s1 * ph[3];
+                al[n][0] = s0 * pl[0]; al[n][1] = s0 * pl[1]; al[n][2] = s1 * pl[2]; al[n][3] = s1 * pl[3];
+              } else {
+                ah[n][0] += s0 * ph[0]; ah[n][1] += s0 * ph[1]; ah[n][2] += s1 * ph[2]; ah[n][3] += s1 * ph[3];
+                al[n][0] += s0 * pl[0]; al[n][1] += s0 * pl[1]; al[n][2] += s1 * pl[2]; al[n][3] += s1 * pl[3];
+              }
             }
           }
-          float m2[4] = {0.f, 0.f, 0.f, 0.f};  // sum_k m(row, k) S(slot, k) / 1024
           const uint32_t amf[4] = {v0.mf, v1.mf, 0u, 0u};
-          mma_16816(m2, amf, xs[0][0], 0u);
-          mma_16816(m2, amf, xs[0][1], 0u);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float d16 = i < 2 ? v0.d16 : v1.d16, dm = i < 2 ? v0.dm1024 : v1.dm1024;
-            const float main = fmaf(256.f, (float)ah[i], (float)al[i]);  // 16 x sum_j sc_j sum_k q_k a_k
-            acc[0][i] = fmaf((i & 1) ? xsc1 : xsc0, fmaf(d16, main, -dm * m2[i]), acc[0][i]);
+          for (int n = 0; n < NT; ++n) {
+            float m2[4] = {0.f, 0.f, 0.f, 0.f};  // sum_k m(row, k) S(slot, k) / 1024
+            mma_16816(m2, amf, xs[n][0], 0u);
+            mma_16816(m2, amf, xs[n][1], 0u);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float d16 = i < 2 ? v0.d16 : v1.d16, dm = i < 2 ? v0.dm1024 : v1.dm1024;
+              const float main = fmaf(256.f, (float)ah[n][i], (float)al[n][i]);  // 16 x sum_j sc_j sum_k q_k a_k
+              acc[n][i] = fmaf(xsc[n][i & 1], fmaf(d16, main, -dm * m2[i]), acc[n][i]);
+            }
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(empty + ps % ST);
