@@ -564,6 +564,47 @@ def test_quad_integer_activations_vs_oracle(backend, oracle, um, T, D, I, case):
     assert e_i8 <= 2 * e_f16 + 1e-5, (e_i8, e_f16)
 
 
+@pytest.mark.parametrize("T,D,I,mode", [(1, 1024, 2048, "1"), (1, 4096, 2048, "1"), (8, 4096, 2048, ""),
+                                        (12, 4096, 3072, ""), (32, 4096, 2048, "")])
+def test_quad_down_balanced_ranges(oracle, um, monkeypatch, T, D, I, mode):
+    """The quad-schedule down projection in balanced ranges (every CTA an equal share of the
+    tile-major quad sequence; tiles cut between CTAs finished by the CTA that completes the last
+    piece): against the oracle, against whole-unit K splits (UAII_MOE_DOWN_RANGES=0, the same
+    partials grouped differently: 1e-5), and bit-identical over repeated calls (the per-CTA
+    counters are left at zero).  Automatic mode takes ranges from one tile per SM up (8, 12 and
+    32 tokens here; 32 tokens on 16-slot tiles); forced ranges ("1") at 1 token run more CTAs
+    than quads, one-quad pieces of a tile spread over several CTAs."""
+    gf, df, E, k = 14, 16, 8, 2
+    x, w, G, U, Dn = layer_case(um, gf, df, T, D, E, I, k, 2600 + T + D)
+    _, pr, _ = oracle.router(x, w)
+    y_ref, _, _ = oracle.experts_packed(x, G, gf, U, gf, Dn, df, pr, E, I, k, 1)
+    L = um.make_layer(D, E, I, k, 1, w, G, gf, U, gf, Dn, df)
+
+    def run(env, calls):
+        if env:
+            monkeypatch.setenv("UAII_MOE_DOWN_RANGES", env)
+        else:
+            monkeypatch.delenv("UAII_MOE_DOWN_RANGES", raising=False)
+        b = um.Backend(0)
+        try:
+            b.set_graphs(False)
+            out = []
+            for _ in range(calls):
+                y = np.empty_like(x)
+                b.ffn(L, x, T, y)
+                out.append(y)
+            return out, b.last_plan()
+        finally:
+            b.close()
+
+    ys, plan = run(mode, 2)
+    assert plan["down_splits"] == 1, plan
+    (y2,), plan2 = run("0", 1)
+    assert rel_err(ys[0], y_ref) <= REL_TOL
+    assert bits_equal(ys[0], ys[1])
+    assert rel_err(ys[0], y2) <= 1e-5
+
+
 @pytest.mark.parametrize("T,D,E,k", [(1, 4096, 8, 2), (7, 2048, 60, 4), (16, 2048, 128, 8), (3, 1024, 5, 5), (32, 4096, 8, 2)])
 def test_decode_routing_launch_matches_separate_kernels(backend, oracle, um, T, D, E, k):
     """At decode widths the layer routes in one launch (router, softmax, top-k, slot numbering):

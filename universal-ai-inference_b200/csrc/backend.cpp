@@ -13,6 +13,7 @@
 #include "backend.hpp"
 
 #include <cmath>
+#include <cstdlib>
 
 #include <cstring>
 #include <string>
@@ -79,6 +80,9 @@ Error MoeCudaBackend::initialize(int device, cudaStream_t stream) {
     return Error::make(ErrorCode::NotImplemented,
                        std::string("device ") + prop.name + " is not sm_100 (this build targets B200 only)");
   device_ = device;
+  // quad down in balanced ranges: "0" never, "1" always (where the buffers allow), unset: automatic
+  const char* rg = std::getenv("UAII_MOE_DOWN_RANGES");
+  ranges_mode_ = rg && rg[0] == '0' ? 0 : rg && rg[0] == '1' ? 1 : -1;
   UAII_CUDA(cudaMalloc(&dev_err_, sizeof(int)), "Malloc(error flag)");
   UAII_CUDA(cudaMemset(dev_err_, 0, sizeof(int)), "Memset(error flag)");
   // the quad schedule's tail-split partials and counters (the counters stay zero between launches)
@@ -97,17 +101,24 @@ Error MoeCudaBackend::initialize(int device, cudaStream_t stream) {
 }
 
 Error MoeCudaBackend::attach_external(int device, cudaStream_t stream, void* scratch, size_t bytes) {
-  if (scratch == nullptr || bytes < 2 * kAlign)
+  const size_t fixed = kAlign + align_up(tail_bytes());
+  if (scratch == nullptr || bytes < fixed + kAlign)
     return Error::make(ErrorCode::InvalidArgument, "external scratch too small");
   UAII_CUDA(cudaSetDevice(device), "SetDevice");
   device_ = device;
   stream_ = stream;
   own_stream_ = false;
   external_ = true;
-  dev_err_ = static_cast<int*>(scratch);  // first 256 bytes: the error flag
-  ws_ = static_cast<char*>(scratch) + kAlign;
-  ws_cap_ = bytes - kAlign;
+  // first 256 bytes: the error flag; then the tail-split buffers and counters (the same plans as
+  // the owning mode); the rest is the workspace.  The flag and the counters start at zero.
+  dev_err_ = static_cast<int*>(scratch);
+  tail_.part = reinterpret_cast<float*>(static_cast<char*>(scratch) + kAlign);
+  tail_.cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(tail_.part) + tail_part_bytes());
+  route_done_ = tail_.cnt + kTailMaxUnits;
+  ws_ = static_cast<char*>(scratch) + fixed;
+  ws_cap_ = bytes - fixed;
   ws_used_ = 0;
+  UAII_CUDA(cudaMemsetAsync(tail_.cnt, 0, sizeof(int) * (kTailMaxUnits + 16), stream_), "MemsetAsync(counters)");
   return cuda_status(cudaMemsetAsync(dev_err_, 0, sizeof(int), stream_), "MemsetAsync(error flag)");
 }
 
@@ -117,6 +128,8 @@ void MoeCudaBackend::shutdown() noexcept {
     if (stream_) (void)cudaStreamSynchronize(stream_);
     ws_ = nullptr;
     dev_err_ = nullptr;
+    tail_ = TailSplit{};
+    route_done_ = nullptr;
     ws_cap_ = ws_used_ = 0;
     stream_ = nullptr;
     device_ = -1;
@@ -579,6 +592,17 @@ ExpertPlan MoeCudaBackend::plan_experts(const LayerArgs& L, int64_t T, int64_t s
 
     const int64_t n_tiles = (int64_t)((tpe + p.bn - 1) / p.bn);
     p.splits = pick_splits(active * n_tiles * (L.D / 128), umma_kchunks(L.down.fmt, L.I));
+    // A quad down with at least one tile per SM spreads its quads evenly over the SMs instead
+    // (needs the tail-split buffers).  With fewer tiles most pieces would be partial and pay the
+    // fix-up: Mixtral-shaped, 1 token (64 tiles): 41 us in ranges against 38 us in K splits;
+    // 8 tokens (224 tiles): 97 against 110 us.
+    const int64_t dn_tiles = active * n_tiles * (L.D / 128);
+    const bool ranges_ok = (p.quad_mma || p.down_quad) && tail_.part != nullptr &&
+                           2 * kSms * p.bn <= kTailMaxUnits * kTailMaxBn;
+    if (ranges_ok && (ranges_mode_ == 1 || (ranges_mode_ < 0 && dn_tiles >= kSms))) {
+      p.down_ranges = true;
+      p.splits = 1;
+    }
   }
   if (L.I_sh > 0) {
     p.sh_umma = p.umma && umma_shapes_supported(L.gate_sh.fmt, L.down_sh.fmt, L.D, L.I_sh);
@@ -733,7 +757,7 @@ Error MoeCudaBackend::run_experts(const float* xd, const float* scores, const fl
     phase_begin(kDown);
     UAII_CUDA(launch_down_umma(L.down.fmt, dd, dpitch, E, D, I, h16, S, rb.counts, rb.offsets,
                                tables ? tile_base_dn : tile_base, P.bn, splits, out, dev_err_, stream_, dn_sched,
-                               tables),
+                               tables, P.down_ranges ? &tail_ : nullptr),
               "down(tensor cores)");
     phase_end();
     count_launches(tables ? 2 : 4);

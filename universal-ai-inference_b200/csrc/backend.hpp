@@ -89,6 +89,7 @@ struct ExpertPlan {
   bool quad_mma = false;      // ... the mma.sync schedule over whole K-quant super-blocks
   bool down_quad = false;     // the down projection alone on the quad schedule (16-slot tiles, gate/up on tcgen05)
   bool quad_i8 = false;       // quad gate/up (Q4_K, 8-slot tiles) on 16-bit integer activations, int8 mma.sync
+  bool down_ranges = false;   // quad down in balanced ranges of the tile-major quad sequence (splits == 1)
   bool umma_refused = false;  // tensor cores forced but the layer does not qualify
   int bn = 16;         // slots per tile (MMA N)
   int splits = 1;      // K splits of the down projection
@@ -238,9 +239,10 @@ class MoeCudaBackend {
   bool own_stream_ = false;
   int path_ = 0;
   bool f16_quad_ = false;
+  int ranges_mode_ = -1;  // UAII_MOE_DOWN_RANGES: 0 off, 1 forced, -1 automatic (quad down balanced ranges)
   ExpertPlan last_plan_{};
   int* dev_err_ = nullptr;
-  TailSplit tail_{};  // quad schedule tail split (null in external mode: no split)
+  TailSplit tail_{};  // quad schedule tail split and balanced down ranges (in external mode: carved from the scratch)
   static size_t tail_part_bytes() { return sizeof(float) * (size_t)kTailMaxUnits * 128 * kTailMaxBn; }
   static size_t tail_bytes() { return tail_part_bytes() + sizeof(int) * (size_t)(kTailMaxUnits + 16); }
   int* route_done_ = nullptr;  // launch_route_decode's counter (after the tail-split counters)

@@ -97,6 +97,9 @@ struct Args {
   // Null: no tail split.
   float* tail_part;
   int* tail_cnt;
+  // Quad schedule, down: balanced ranges over the tile-major quad sequence (tail_part holds two
+  // pieces per CTA, tail_cnt one counter per CTA); 0: whole units
+  int ranges;
 };
 
 __device__ __forceinline__ __half2 as_h2(uint32_t v) {
@@ -1487,6 +1490,20 @@ __global__ void __launch_bounds__(kWmThreads, 1)
     }
   }
   const int total = tail_base + (tiles - tail_base) * ts;
+  // Balanced ranges (down): CTA c takes quads [W c / G, W (c + 1) / G) of the tile-major sequence
+  // of all W = tiles x kquads quads, so every CTA streams the same number of weight bytes; a tile
+  // cut between CTAs is finished by whichever CTA completes its last piece.
+  // With fewer quads than CTAs only the first W CTAs take ranges (one quad or more each), so every
+  // CTA between a cut tile's first and last holds a piece of it.
+  const bool ranges = args.ranges != 0 && !args.gateup && args.tail_part != nullptr;
+  const int64_t wq = (int64_t)tiles * args.kquads;
+  const int64_t gr = min((int64_t)gridDim.x, wq);
+  const bool has_range = ranges && (int64_t)blockIdx.x < gr;
+  const int64_t rw0 = has_range ? wq * blockIdx.x / gr : 0;
+  const int64_t rw1 = has_range ? wq * (blockIdx.x + 1) / gr : 0;
+  const int rt0 = ranges ? (int)(rw0 / args.kquads) : 0;
+  // the CTA whose range holds quad x of the sequence
+  auto cta_of = [&](int64_t x) { return (int)(((x + 1) * gr + wq - 1) / wq) - 1; };
   // unit -> tile, quad range, and (tail units) the tail tile index and the unit's rank in it
   auto unit_tile = [&](int unit, Tile& t, int& q0, int& q1, int& tail, int& tsp) {
     int tile = unit;
@@ -1507,15 +1524,33 @@ __global__ void __launch_bounds__(kWmThreads, 1)
       q1 = a0 + (tsp + 1) * nq / ts;
     }
   };
+  // this CTA's u-th unit (false past the last); rt: its tile index (ranges)
+  auto unit_at = [&](int u, Tile& t, int& q0, int& q1, int& tail, int& tsp, int& rt) -> bool {
+    if (ranges) {
+      rt = rt0 + u;
+      const int64_t base = (int64_t)rt * args.kquads;
+      if (rw0 >= rw1 || base >= rw1) return false;
+      t = decode_tile(args, rt, BN);  // splits == 1
+      q0 = (int)(max(rw0, base) - base);
+      q1 = (int)(min(rw1, base + args.kquads) - base);
+      tail = -1;
+      tsp = 0;
+      return true;
+    }
+    const int unit = (int)blockIdx.x + u * (int)gridDim.x;
+    if (unit >= total) return false;
+    rt = unit;
+    unit_tile(unit, t, q0, q1, tail, tsp);
+    return true;
+  };
 
   if (warp == kWmWarps) {
     // ------------------------------------------------------------ TMA producer
     uint32_t n = 0;  // stages issued
     bool ok = true;
-    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-      Tile t;
-      int q0, q1, tail, tsp;
-      unit_tile(tile, t, q0, q1, tail, tsp);
+    Tile t;
+    int q0, q1, tail, tsp, rt;
+    for (int u = 0; ok && unit_at(u, t, q0, q1, tail, tsp, rt); ++u) {
       const int row0 = t.e * args.rows_per_expert + t.m_tile * (args.gateup ? 64 : 128);
       const int slot0 = __ldg(args.offsets + t.e) + t.n_tile * BN;
       for (int q = q0; q < q1; ++q) {
@@ -1562,10 +1597,9 @@ __global__ void __launch_bounds__(kWmThreads, 1)
     const uint32_t sB0 = smem_u32(sB);
     uint32_t pi = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
-      Tile t;
-      int q0, q1, tail, tsp;
-      unit_tile(tile, t, q0, q1, tail, tsp);
+    Tile t;
+    int q0, q1, tail, tsp, rt;
+    for (int u = 0; unit_at(u, t, q0, q1, tail, tsp, rt); ++u) {
       float acc[NT][4], acc2[NT][4];  // acc2: Q6_K odd k-steps with one slot octet
 #pragma unroll
       for (int n = 0; n < NT; ++n)
@@ -1821,13 +1855,41 @@ __global__ void __launch_bounds__(kWmThreads, 1)
         }
       } else {
         constexpr int kPer = 128 * BN / kCompute;
+        float v[kPer];  // output o = ct + r * kCompute: row o % 128, slot o / 128
+#pragma unroll
+        for (int r = 0; r < kPer; ++r) {
+          const int o = ct + r * kCompute;
+          v[r] = sR[o] + sR[128 * BN + o];
+        }
+        if (ranges && (q0 != 0 || q1 != args.kquads)) {
+          // a piece of a tile cut between CTAs cf .. cl: piece p = this CTA - cf goes to slot 1 of
+          // CTA cf (its last piece) or slot 0 of this CTA (its first piece); the CTA that completes
+          // the last piece adds pieces 0 .. np - 1 in order
+          const int cf = cta_of((int64_t)rt * args.kquads), cl = cta_of((int64_t)(rt + 1) * args.kquads - 1);
+          const int np = cl - cf + 1, p = (int)blockIdx.x - cf;
+          float* mine = args.tail_part + (int64_t)(2 * (int)blockIdx.x + (p == 0 ? 1 : 0)) * (128 * BN);
+#pragma unroll
+          for (int r = 0; r < kPer; ++r) mine[ct + r * kCompute] = v[r];
+          __threadfence();
+          bar_sync(1, kCompute);
+          const bool last = bar_any(1, kCompute, ct == 0 && atomicAdd(args.tail_cnt + cf, 1) == np - 1);
+          if (!last) continue;
+          __threadfence();
+#pragma unroll
+          for (int r = 0; r < kPer; ++r) {
+            float a = 0.f;
+            for (int u2 = 0; u2 < np; ++u2)
+              a += __ldcg(args.tail_part + (int64_t)(2 * (cf + u2) + (u2 == 0 ? 1 : 0)) * (128 * BN) + ct +
+                          r * kCompute);
+            v[r] = a;
+          }
+          if (ct == 0) args.tail_cnt[cf] = 0;  // zero again for the next launch
+        }
         float* out = args.out + (int64_t)t.split * args.split_stride;
 #pragma unroll
         for (int r = 0; r < kPer; ++r) {
           const int o = ct + r * kCompute, row = o % 128, sl = o / 128;
-          if (sl < n_valid)
-            out[(int64_t)(slot0 + sl) * args.out_ld + t.m_tile * 128 + row] =
-                sR[sl * 128 + row] + sR[128 * BN + sl * 128 + row];
+          if (sl < n_valid) out[(int64_t)(slot0 + sl) * args.out_ld + t.m_tile * 128 + row] = v[r];
         }
       }
     }
@@ -2124,6 +2186,12 @@ cudaError_t launch_common(int sched, int fmt, bool gateup, const void* W0, const
     a.tail_part = tail->part;
     a.tail_cnt = tail->cnt;
   }
+  if (quad && !gateup && tail != nullptr && tail->part != nullptr && tail->cnt != nullptr && splits == 1 &&
+      bn <= kTailMaxBn && 2 * num_sms() * bn <= kTailMaxUnits * kTailMaxBn && num_sms() <= kTailMaxUnits) {
+    a.tail_part = tail->part;
+    a.tail_cnt = tail->cnt;
+    a.ranges = 1;
+  }
   a.out = out;
   a.out_ld = out_ld;
   a.split_stride = split_stride;
@@ -2197,9 +2265,9 @@ cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pi
 cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
                              int64_t S_rows, const int32_t* counts, const int32_t* offsets, int32_t* tile_base,
                              int bn, int splits, float* out, int* err, cudaStream_t st, int sched,
-                             bool table_ready) {
+                             bool table_ready, const TailSplit* ranges) {
   return launch_common(sched, fmt, false, Dn, Dn, pitch, E, D, I, h16, S_rows, counts, offsets, tile_base, bn,
-                       splits, nullptr, out, D, S_rows * D, err, st, kOrderTc, table_ready, nullptr, nullptr,
+                       splits, nullptr, out, D, S_rows * D, err, st, kOrderTc, table_ready, nullptr, ranges,
                        nullptr);
 }
 

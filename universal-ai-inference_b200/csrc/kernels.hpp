@@ -176,7 +176,7 @@ inline bool quad_mma_format(int fmt) { return fmt == 14 || fmt == 16; }
 // Tail split of the quad schedule's gate/up launch (see the kernel): part holds
 // kTailMaxUnits x 128 x kTailMaxBn f32, cnt kTailMaxUnits ints, zero before the first launch
 // (every launch leaves them zero).  A null or absent TailSplit turns the split off.
-constexpr int kTailMaxUnits = 256, kTailMaxBn = 16;
+constexpr int kTailMaxUnits = 320, kTailMaxBn = 16;
 struct TailSplit {
   float* part = nullptr;
   int* cnt = nullptr;
@@ -188,10 +188,14 @@ cudaError_t launch_gateup_umma(int fmt, const void* G, const void* U, int64_t pi
                                bool table_ready = false, const void* xsum = nullptr,
                                const TailSplit* tail = nullptr, const float* xscale = nullptr);
 // out[split][slot, o] = partial of h16[slot] . Dn[e, o] over the split's K range (f32).
+// ranges (quad schedule, splits == 1, the same TailSplit buffers as the gate/up tail split, BN x 2
+// x SMs <= kTailMaxUnits x kTailMaxBn): every CTA takes an equal share of the tile-major sequence
+// of all tiles' quads; a tile cut between CTAs is finished by the CTA that completes its last
+// piece, which adds the pieces in order.  Null: whole tiles (or `splits` K ranges) per unit.
 cudaError_t launch_down_umma(int fmt, const void* Dn, int64_t pitch, int64_t E, int64_t D, int64_t I, const void* h16,
                              int64_t S_rows, const int32_t* counts, const int32_t* offsets,
                              int32_t* tile_base, int bn, int splits, float* out, int* err, cudaStream_t st,
-                             int sched = kSchedTcgen05, bool table_ready = false);
+                             int sched = kSchedTcgen05, bool table_ready = false, const TailSplit* ranges = nullptr);
 // Copies `rows` packed rows of row_bytes (even) from src (src_pitch apart) to dst
 // (dst_pitch apart, a multiple of 16), zero-filling each row's padding.
 cudaError_t launch_pad_rows(const void* src, int64_t src_pitch, int64_t rows, int64_t row_bytes, void* dst,
