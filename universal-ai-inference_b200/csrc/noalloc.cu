@@ -22,8 +22,9 @@
 // device that was current when the call began is current again when it returns.
 //
 // Every call shares the array and finds the previous call's leftovers in it:
-// the error flag and the expert routing mask are cleared on each call and
-// every other buffer is fully rewritten before it is read.  Two calls whose GPU
+// the error flag, the split-work counters of the expert kernels and the expert
+// routing mask are cleared on each call and every other buffer is fully
+// rewritten before it is read.  Two calls whose GPU
 // work overlapped would race on the shared array; this entry point prevents
 // that inside one process by serializing calls with a lock and returning only
 // after the call's GPU work has finished.
