@@ -99,57 +99,62 @@ __global__ void route_gather_kernel(const float* __restrict__ x, int64_t T, int6
   const int lane = threadIdx.x & 31;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int64_t npairs = T * k;
+  if (order == kOrderQ4KI8) {
+    // 16-bit integer activations per 256-element quad: a = rint(x * 32767 / max|x|) as an s8 hi
+    // and a u8 lo plane (256 bytes each) in the integer quad kernel's K order -- lane l holds
+    // elements 8l .. 8l+7, sub-block l / 4 at K positions 4 (l % 4) + i and 16 + 4 (l % 4) + i --
+    // with the sub-block sums of a / 1024 (f16 + f16 remainder, exact) and the scale max|x| / 32767.
+    // One warp per (routed pair, quad), so all quads' loads are in flight together.  Non-finite
+    // activations are not carried through (the f16 orders carry them).
+    const int64_t nq = D / 256;
+    const int sb = lane >> 2, u = lane & 3;
+    for (int64_t wi = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; wi < npairs * nq; wi += nw) {
+      const int64_t p = wi / nq, q = wi - p * nq;
+      const int64_t t = p / k;
+      const int slot = offs[rb.topk_ids[p]] + rb.slot_local[p];
+      if (lane == 0 && q == 0) { rb.slot_of[p] = slot; rb.token_of[slot] = (int32_t)t; }
+      uint8_t* row = reinterpret_cast<uint8_t*>(xp16) + (int64_t)slot * 2 * D;
+      const float4* s4 = reinterpret_cast<const float4*>(x + t * D + 256 * q + 8 * lane);
+      const float4 v0 = s4[0], v1 = s4[1];
+      const float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      float m = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(e[i]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float inv = m > 0.f ? 32767.f / m : 0.f;
+      uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+      int sum = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int a = __float2int_rn(e[i] * inv);  // |e * inv| <= 32767 (+ rounding): no clamp
+        sum += a;
+        hw[i >> 2] |= ((uint32_t)(a >> 8) & 0xFFu) << (8 * (i & 3));
+        lw[i >> 2] |= ((uint32_t)a & 0xFFu) << (8 * (i & 3));
+      }
+      uint8_t* qb = row + 512 * q + 32 * sb + 4 * u;
+      *reinterpret_cast<uint32_t*>(qb) = hw[0];
+      *reinterpret_cast<uint32_t*>(qb + 16) = hw[1];
+      *reinterpret_cast<uint32_t*>(qb + 256) = lw[0];
+      *reinterpret_cast<uint32_t*>(qb + 272) = lw[1];
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      if (u == 0) {
+        __half* xs = static_cast<__half*>(tt.xsum) + ((int64_t)slot * nq + q) * 16;
+        const float sf = (float)sum * (1.0f / 1024.0f);  // |sum| < 2^20: exact
+        const __half hs = __float2half_rn(sf);
+        xs[sb] = hs;
+        xs[8 + sb] = __float2half_rn(sf - __half2float(hs));
+      }
+      if (lane == 0) tt.xscale[(int64_t)slot * nq + q] = m * (1.0f / 32767.0f);
+    }
+    return;
+  }
   for (int64_t p = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; p < npairs; p += nw) {
     const int64_t t = p / k;
     const int e = rb.topk_ids[p];
     const int slot = offs[e] + rb.slot_local[p];
     if (lane == 0) { rb.slot_of[p] = slot; rb.token_of[slot] = (int32_t)t; }
-    if (order == kOrderQ4KI8) {
-      // 16-bit integer activations per 256-element quad: a = rint(x * 32767 / max|x|) as an s8 hi
-      // and a u8 lo plane (256 bytes each) in the integer quad kernel's K order -- lane l holds
-      // elements 8l .. 8l+7, sub-block l / 4 at K positions 4 (l % 4) + i and 16 + 4 (l % 4) + i --
-      // with the sub-block sums of a / 1024 (f16 + f16 remainder, exact) and the scale max|x| / 32767.
-      // Non-finite activations are not carried through (the f16 orders carry them).
-      uint8_t* row = reinterpret_cast<uint8_t*>(xp16) + (int64_t)slot * 2 * D;
-      const int64_t nq = D / 256;
-      const int sb = lane >> 2, u = lane & 3;
-      for (int64_t q = 0; q < nq; ++q) {
-        const float4* s4 = reinterpret_cast<const float4*>(x + t * D + 256 * q + 8 * lane);
-        const float4 v0 = s4[0], v1 = s4[1];
-        const float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        float m = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(e[i]));
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const float inv = m > 0.f ? 32767.f / m : 0.f;
-        uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
-        int sum = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int a = __float2int_rn(e[i] * inv);  // |e * inv| <= 32767 (+ rounding): no clamp
-          sum += a;
-          hw[i >> 2] |= ((uint32_t)(a >> 8) & 0xFFu) << (8 * (i & 3));
-          lw[i >> 2] |= ((uint32_t)a & 0xFFu) << (8 * (i & 3));
-        }
-        uint8_t* qb = row + 512 * q + 32 * sb + 4 * u;
-        *reinterpret_cast<uint32_t*>(qb) = hw[0];
-        *reinterpret_cast<uint32_t*>(qb + 16) = hw[1];
-        *reinterpret_cast<uint32_t*>(qb + 256) = lw[0];
-        *reinterpret_cast<uint32_t*>(qb + 272) = lw[1];
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        if (u == 0) {
-          __half* xs = static_cast<__half*>(tt.xsum) + ((int64_t)slot * nq + q) * 16;
-          const float sf = (float)sum * (1.0f / 1024.0f);  // |sum| < 2^20: exact
-          const __half hs = __float2half_rn(sf);
-          xs[sb] = hs;
-          xs[8 + sb] = __float2half_rn(sf - __half2float(hs));
-        }
-        if (lane == 0) tt.xscale[(int64_t)slot * nq + q] = m * (1.0f / 32767.0f);
-      }
-      continue;
-    }
     if (D % 4 != 0) {  // odd widths: element by element
       for (int64_t i = lane; i < D; i += 32) {
         const float v = x[t * D + i];
@@ -399,7 +404,7 @@ cudaError_t launch_route_gather(const float* x, int64_t T, int64_t D, int64_t E,
   const TileTables tt = tables ? *tables : TileTables{};
   if (order == kOrderQ4KI8 && (tt.xsum == nullptr || tt.xscale == nullptr || xp_f16 == nullptr || xp_f32 != nullptr))
     return cudaErrorInvalidValue;
-  int64_t blocks = (T * k + 7) / 8;
+  int64_t blocks = (T * k * (order == kOrderQ4KI8 ? D / 256 : 1) + 7) / 8;  // 8 warps a block, one per work item
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
   const size_t smem = sizeof(int) * (size_t)(E + 1);
