@@ -912,7 +912,23 @@ __device__ __forceinline__ bool bar_any(int id, int n, bool v) {
       : "memory");
   return r != 0;
 }
+
 __device__ __forceinline__ void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+// Split-work arrival of a CTA whose compute threads 0 .. n-1 have stored their partial sums: after
+// the barrier one thread makes the CTA's stores visible device-wide (a fence is cumulative over
+// what the barrier ordered before it), counts the arrival, and on the last of `parts` arrivals
+// fences again so that the whole CTA then reads the other CTAs' partials.  True on the last.
+__device__ __forceinline__ bool arrive_last(int id, int n, int* cnt, int parts) {
+  bar_sync(id, n);
+  bool last = false;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(cnt, 1) == parts - 1;
+    if (last) __threadfence();
+  }
+  return bar_any(id, n, last);
+}
 
 // NW 32-bit words starting at an even byte offset `off` of shared memory row
 // `p` (4-byte aligned): 4-byte loads joined by a funnel shift of 0 or 16 bits.
@@ -1827,11 +1843,7 @@ __global__ void __launch_bounds__(kWmThreads, 1)
             part[(int64_t)tsp * (128 * BN) + sl * 128 + f] = gv[r];
             part[(int64_t)tsp * (128 * BN) + sl * 128 + 64 + f] = uv[r];
           }
-          __threadfence();
-          bar_sync(1, kCompute);
-          const bool last = bar_any(1, kCompute, ct == 0 && atomicAdd(args.tail_cnt + tail, 1) == ts - 1);
-          if (!last) continue;
-          __threadfence();
+          if (!arrive_last(1, kCompute, args.tail_cnt + tail, ts)) continue;
 #pragma unroll
           for (int r = 0; r < kPer; ++r) {
             const int o = ct + r * kCompute, f = o % 64, sl = o / 64;
@@ -1870,11 +1882,7 @@ __global__ void __launch_bounds__(kWmThreads, 1)
           float* mine = args.tail_part + (int64_t)(2 * (int)blockIdx.x + (p == 0 ? 1 : 0)) * (128 * BN);
 #pragma unroll
           for (int r = 0; r < kPer; ++r) mine[ct + r * kCompute] = v[r];
-          __threadfence();
-          bar_sync(1, kCompute);
-          const bool last = bar_any(1, kCompute, ct == 0 && atomicAdd(args.tail_cnt + cf, 1) == np - 1);
-          if (!last) continue;
-          __threadfence();
+          if (!arrive_last(1, kCompute, args.tail_cnt + cf, np)) continue;
 #pragma unroll
           for (int r = 0; r < kPer; ++r) {
             float a = 0.f;
