@@ -48,6 +48,10 @@ WORKLOAD_NOTE = {
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of the same
 # command (dram__bytes_read.sum + dram__bytes_write.sum); absent workloads report null.
 NCU_TRAFFIC = {
+    ("mixtral_T1", "gateup"): 132193536 + 5757184,
+    ("mixtral_T1", "down"): 98642688 + 452608,
+    ("mixtral_T8", "gateup"): 462690304 + 4268544,
+    ("mixtral_T8", "down"): 346857728 + 846592,
     ("mixtral_T32", "gateup"): 529084672 + 5518336,
     ("mixtral_T32", "down"): 398761984 + 4418304,
     ("mixtral_T4096", "gateup"): 601846784 + 218835200,
